@@ -1,0 +1,392 @@
+"""Architecture descriptions for the supported model families.
+
+One dataclass covers the DeepSeek family (MLA attention, DeepSeek MoE with
+shared experts, dense-first layers, optional grouped / biased routing, fp8
+block-scaled weights) and the Qwen3-MoE family (GQA with QK-RMSNorm, routed
+experts only).  ``from_hf_config`` reads a HuggingFace ``config.json`` dict;
+the presets are the shapes the benchmarks name.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, field, replace
+from typing import Any
+
+DEEPSEEK_ARCHS = ("DeepseekForCausalLM", "DeepseekV2ForCausalLM", "DeepseekV3ForCausalLM", "GlmMoeDsaForCausalLM")
+QWEN3_MOE_ARCHS = ("Qwen3MoeForCausalLM",)
+
+
+@dataclass(frozen=True)
+class ModelArchConfig:
+    architecture: str
+    hidden_size: int
+    num_hidden_layers: int
+    vocab_size: int
+    num_attention_heads: int
+    attention_type: str  # "mla" | "gqa"
+    # MLA
+    q_lora_rank: int | None = None
+    kv_lora_rank: int = 0
+    qk_nope_head_dim: int = 0
+    qk_rope_head_dim: int = 0
+    v_head_dim: int = 0
+    # GQA
+    num_key_value_heads: int = 0
+    head_dim: int = 0
+    qk_norm: bool = False
+    # FFN
+    intermediate_size: int = 0
+    first_k_dense_replace: int = 0
+    moe_layer_freq: int = 1
+    n_routed_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    n_shared_experts: int = 0
+    scoring_func: str = "softmax"  # "softmax" | "sigmoid"
+    topk_method: str = "greedy"  # "greedy" | "group_limited_greedy" | "noaux_tc"
+    n_group: int = 1
+    topk_group: int = 1
+    norm_topk_prob: bool = False
+    routed_scaling_factor: float = 1.0
+    # misc
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    rope_scaling: dict | None = None
+    max_position_embeddings: int = 4096
+    tie_word_embeddings: bool = False
+    # "fp8_block": e4m3 weights with 128x128 scales for experts and dense MLPs.
+    quant: str | None = None
+    weight_block_size: tuple[int, int] = (128, 128)
+    extra: dict = field(default_factory=dict)
+
+    # -------------------------------------------------------------- helpers
+    @property
+    def is_mla(self) -> bool:
+        return self.attention_type == "mla"
+
+    def is_moe_layer(self, layer_idx: int) -> bool:
+        return (
+            self.n_routed_experts > 0
+            and layer_idx >= self.first_k_dense_replace
+            and layer_idx % max(1, self.moe_layer_freq) == 0
+        )
+
+    @property
+    def moe_layer_indices(self) -> tuple[int, ...]:
+        return tuple(i for i in range(self.num_hidden_layers) if self.is_moe_layer(i))
+
+    @property
+    def qk_head_dim(self) -> int:
+        return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+    @property
+    def kv_cache_width(self) -> int:
+        """Elements cached per token per layer (MLA: latent+rope; GQA: K and V)."""
+        if self.is_mla:
+            return self.kv_lora_rank + self.qk_rope_head_dim
+        return 2 * self.num_key_value_heads * self.head_dim
+
+    @property
+    def softmax_scale(self) -> float:
+        if self.is_mla:
+            scale = 1.0 / math.sqrt(self.qk_head_dim)
+            rs = self.rope_scaling or {}
+            if rs.get("type", rs.get("rope_type")) in ("yarn", "deepseek_yarn"):
+                mscale_all = float(rs.get("mscale_all_dim", 0.0) or 0.0)
+                factor = float(rs.get("factor", 1.0))
+                if mscale_all:
+                    m = yarn_get_mscale(factor, mscale_all)
+                    scale = scale * m * m
+            return scale
+        return 1.0 / math.sqrt(self.head_dim)
+
+    @property
+    def shared_intermediate_size(self) -> int:
+        return self.moe_intermediate_size * self.n_shared_experts
+
+    def scaled(self, **overrides: Any) -> "ModelArchConfig":
+        return replace(self, **overrides)
+
+    def to_dict(self) -> dict:
+        d = asdict(self)
+        d["weight_block_size"] = list(self.weight_block_size)
+        return d
+
+    # -------------------------------------------------------------- parsing
+    @classmethod
+    def from_hf_config(cls, hf: dict) -> "ModelArchConfig":
+        archs = hf.get("architectures") or [""]
+        arch = archs[0]
+        if arch.startswith("AFD"):
+            arch = arch[3:]
+        quant = None
+        block = (128, 128)
+        qc = hf.get("quantization_config") or {}
+        if qc.get("quant_method") == "fp8":
+            quant = "fp8_block"
+            block = tuple(qc.get("weight_block_size", [128, 128]))
+        if arch in DEEPSEEK_ARCHS or hf.get("model_type", "").startswith("deepseek"):
+            return cls(
+                architecture=arch or "DeepseekV2ForCausalLM",
+                hidden_size=hf["hidden_size"],
+                num_hidden_layers=hf["num_hidden_layers"],
+                vocab_size=hf["vocab_size"],
+                num_attention_heads=hf["num_attention_heads"],
+                attention_type="mla",
+                q_lora_rank=hf.get("q_lora_rank"),
+                kv_lora_rank=hf["kv_lora_rank"],
+                qk_nope_head_dim=hf["qk_nope_head_dim"],
+                qk_rope_head_dim=hf["qk_rope_head_dim"],
+                v_head_dim=hf["v_head_dim"],
+                intermediate_size=hf["intermediate_size"],
+                first_k_dense_replace=hf.get("first_k_dense_replace", 0),
+                moe_layer_freq=hf.get("moe_layer_freq", 1),
+                n_routed_experts=hf.get("n_routed_experts") or 0,
+                num_experts_per_tok=hf.get("num_experts_per_tok") or 0,
+                moe_intermediate_size=hf.get("moe_intermediate_size", 0),
+                n_shared_experts=hf.get("n_shared_experts") or 0,
+                scoring_func=hf.get("scoring_func", "softmax"),
+                topk_method=hf.get("topk_method", "greedy"),
+                n_group=hf.get("n_group") or 1,
+                topk_group=hf.get("topk_group") or 1,
+                norm_topk_prob=bool(hf.get("norm_topk_prob", False)),
+                routed_scaling_factor=float(hf.get("routed_scaling_factor", 1.0)),
+                rms_norm_eps=hf.get("rms_norm_eps", 1e-6),
+                rope_theta=hf.get("rope_theta", 10000.0),
+                rope_scaling=hf.get("rope_scaling"),
+                max_position_embeddings=hf.get("max_position_embeddings", 4096),
+                tie_word_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                quant=quant,
+                weight_block_size=block,
+            )
+        if arch in QWEN3_MOE_ARCHS or hf.get("model_type") == "qwen3_moe":
+            mlp_only = hf.get("mlp_only_layers") or []
+            if mlp_only:
+                raise ValueError("Qwen3-MoE mlp_only_layers are not supported")
+            return cls(
+                architecture="Qwen3MoeForCausalLM",
+                hidden_size=hf["hidden_size"],
+                num_hidden_layers=hf["num_hidden_layers"],
+                vocab_size=hf["vocab_size"],
+                num_attention_heads=hf["num_attention_heads"],
+                attention_type="gqa",
+                num_key_value_heads=hf["num_key_value_heads"],
+                head_dim=hf.get("head_dim") or hf["hidden_size"] // hf["num_attention_heads"],
+                qk_norm=True,
+                intermediate_size=hf.get("intermediate_size", 0),
+                first_k_dense_replace=0,
+                moe_layer_freq=hf.get("decoder_sparse_step", 1),
+                n_routed_experts=hf["num_experts"],
+                num_experts_per_tok=hf["num_experts_per_tok"],
+                moe_intermediate_size=hf["moe_intermediate_size"],
+                n_shared_experts=0,
+                norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
+                rms_norm_eps=hf.get("rms_norm_eps", 1e-6),
+                rope_theta=hf.get("rope_theta", 1000000.0),
+                rope_scaling=hf.get("rope_scaling"),
+                max_position_embeddings=hf.get("max_position_embeddings", 40960),
+                tie_word_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                quant=quant,
+                weight_block_size=block,
+            )
+        raise ValueError(f"unsupported architecture {arch!r}")
+
+
+def yarn_get_mscale(scale: float, mscale: float = 1.0) -> float:
+    if scale <= 1.0:
+        return 1.0
+    return 0.1 * mscale * math.log(scale) + 1.0
+
+
+# ---------------------------------------------------------------------------
+# Presets named by the benchmark configurations.
+# ---------------------------------------------------------------------------
+
+TINY_DSV2 = ModelArchConfig(
+    architecture="DeepseekV2ForCausalLM",
+    hidden_size=256,
+    num_hidden_layers=2,
+    vocab_size=1024,
+    num_attention_heads=4,
+    attention_type="mla",
+    q_lora_rank=None,
+    kv_lora_rank=64,
+    qk_nope_head_dim=32,
+    qk_rope_head_dim=32,
+    v_head_dim=32,
+    intermediate_size=512,
+    first_k_dense_replace=1,
+    n_routed_experts=8,
+    num_experts_per_tok=2,
+    moe_intermediate_size=128,
+    n_shared_experts=1,
+    scoring_func="softmax",
+    topk_method="greedy",
+    max_position_embeddings=2048,
+)
+
+DSV2_LITE = ModelArchConfig(
+    architecture="DeepseekV2ForCausalLM",
+    hidden_size=2048,
+    num_hidden_layers=27,
+    vocab_size=102400,
+    num_attention_heads=16,
+    attention_type="mla",
+    q_lora_rank=None,
+    kv_lora_rank=512,
+    qk_nope_head_dim=128,
+    qk_rope_head_dim=64,
+    v_head_dim=128,
+    intermediate_size=10944,
+    first_k_dense_replace=1,
+    n_routed_experts=64,
+    num_experts_per_tok=6,
+    moe_intermediate_size=1408,
+    n_shared_experts=2,
+    scoring_func="softmax",
+    topk_method="greedy",
+    norm_topk_prob=False,
+    routed_scaling_factor=1.0,
+    rms_norm_eps=1e-6,
+    rope_theta=10000.0,
+    rope_scaling={
+        "type": "yarn",
+        "factor": 40,
+        "beta_fast": 32,
+        "beta_slow": 1,
+        "mscale": 0.707,
+        "mscale_all_dim": 0.707,
+        "original_max_position_embeddings": 4096,
+    },
+    max_position_embeddings=163840,
+)
+
+QWEN3_30B_A3B = ModelArchConfig(
+    architecture="Qwen3MoeForCausalLM",
+    hidden_size=2048,
+    num_hidden_layers=48,
+    vocab_size=151936,
+    num_attention_heads=32,
+    attention_type="gqa",
+    num_key_value_heads=4,
+    head_dim=128,
+    qk_norm=True,
+    intermediate_size=6144,
+    n_routed_experts=128,
+    num_experts_per_tok=8,
+    moe_intermediate_size=768,
+    n_shared_experts=0,
+    norm_topk_prob=True,
+    rms_norm_eps=1e-6,
+    rope_theta=1000000.0,
+    max_position_embeddings=40960,
+)
+
+DSV3_32L = ModelArchConfig(
+    architecture="DeepseekV3ForCausalLM",
+    hidden_size=7168,
+    num_hidden_layers=32,
+    vocab_size=129280,
+    num_attention_heads=128,
+    attention_type="mla",
+    q_lora_rank=1536,
+    kv_lora_rank=512,
+    qk_nope_head_dim=128,
+    qk_rope_head_dim=64,
+    v_head_dim=128,
+    intermediate_size=18432,
+    first_k_dense_replace=3,
+    n_routed_experts=256,
+    num_experts_per_tok=8,
+    moe_intermediate_size=2048,
+    n_shared_experts=1,
+    scoring_func="sigmoid",
+    topk_method="noaux_tc",
+    n_group=8,
+    topk_group=4,
+    norm_topk_prob=True,
+    routed_scaling_factor=2.5,
+    rms_norm_eps=1e-6,
+    rope_theta=10000.0,
+    rope_scaling={
+        "type": "yarn",
+        "factor": 40,
+        "beta_fast": 32,
+        "beta_slow": 1,
+        "mscale": 1.0,
+        "mscale_all_dim": 1.0,
+        "original_max_position_embeddings": 4096,
+    },
+    max_position_embeddings=163840,
+    quant="fp8_block",
+)
+
+TINY_QWEN3_MOE = ModelArchConfig(
+    architecture="Qwen3MoeForCausalLM",
+    hidden_size=256,
+    num_hidden_layers=2,
+    vocab_size=1024,
+    num_attention_heads=4,
+    attention_type="gqa",
+    num_key_value_heads=2,
+    head_dim=64,
+    qk_norm=True,
+    n_routed_experts=8,
+    num_experts_per_tok=2,
+    moe_intermediate_size=128,
+    norm_topk_prob=True,
+    rope_theta=1000000.0,
+    max_position_embeddings=2048,
+)
+
+TINY_DSV3 = DSV3_32L.scaled(
+    hidden_size=256,
+    num_hidden_layers=3,
+    vocab_size=1024,
+    num_attention_heads=4,
+    q_lora_rank=64,
+    kv_lora_rank=64,
+    qk_nope_head_dim=32,
+    qk_rope_head_dim=32,
+    v_head_dim=32,
+    intermediate_size=512,
+    first_k_dense_replace=1,
+    n_routed_experts=16,
+    num_experts_per_tok=4,
+    moe_intermediate_size=128,
+    n_group=4,
+    topk_group=2,
+    max_position_embeddings=2048,
+    quant=None,
+)
+
+PRESETS: dict[str, ModelArchConfig] = {
+    "tiny-dsv2": TINY_DSV2,
+    "tiny-dsv3": TINY_DSV3,
+    "tiny-qwen3-moe": TINY_QWEN3_MOE,
+    "deepseek-v2-lite": DSV2_LITE,
+    "qwen3-30b-a3b": QWEN3_30B_A3B,
+    "deepseek-v3-32l": DSV3_32L,
+}
+
+
+def get_preset(name: str) -> ModelArchConfig:
+    try:
+        return PRESETS[name]
+    except KeyError:
+        raise ValueError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}") from None
+
+
+__all__ = [
+    "DSV2_LITE",
+    "DSV3_32L",
+    "ModelArchConfig",
+    "PRESETS",
+    "QWEN3_30B_A3B",
+    "TINY_DSV2",
+    "TINY_DSV3",
+    "TINY_QWEN3_MOE",
+    "get_preset",
+    "yarn_get_mscale",
+]

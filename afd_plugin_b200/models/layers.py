@@ -1,0 +1,298 @@
+"""Decoder building blocks with explicit weight tensors.
+
+Each block owns plain tensors (registered as non-trainable parameters) and a
+``forward`` made of :mod:`afd_plugin_b200.ops` calls, so the same code runs the
+fp32 CPU oracle and the bf16 sm_100a path.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+from afd_plugin_b200 import ops
+from afd_plugin_b200.models.configs import ModelArchConfig
+
+
+def _param(shape, dtype, device) -> nn.Parameter:
+    return nn.Parameter(torch.empty(*shape, dtype=dtype, device=device), requires_grad=False)
+
+
+@dataclass
+class AttentionMetadata:
+    """Per-step attention inputs.
+
+    Decode steps: one query token per sequence, ``seq_lens`` includes it.
+    Prefill steps: ``prefill_seqs`` lists ``(token_start, token_end, seq_idx)``
+    over the flattened token dimension.
+    """
+
+    positions: torch.Tensor  # [T] int64
+    slot_mapping: torch.Tensor  # [T] int64
+    block_table: torch.Tensor  # [B, max_blocks] int32
+    seq_lens: torch.Tensor  # [B] int32
+    is_decode: bool = True
+    prefill_seqs: list[tuple[int, int, int]] | None = None
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.positions.shape[0])
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float, dtype, device):
+        super().__init__()
+        self.eps = eps
+        self.weight = _param((dim,), dtype, device)
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None):
+        if residual is None:
+            return ops.rms_norm(x, self.weight, self.eps)
+        return ops.fused_add_rms_norm(x, residual, self.weight, self.eps)
+
+
+class MLAAttention(nn.Module):
+    """DeepSeek multi-head latent attention, absorbed form for cache reads."""
+
+    def __init__(self, arch: ModelArchConfig, dtype, device):
+        super().__init__()
+        self.arch = arch
+        H, nh = arch.hidden_size, arch.num_attention_heads
+        self.num_heads = nh
+        self.qk_nope = arch.qk_nope_head_dim
+        self.qk_rope = arch.qk_rope_head_dim
+        self.v_dim = arch.v_head_dim
+        self.kv_lora = arch.kv_lora_rank
+        self.scale = arch.softmax_scale
+        qk = arch.qk_head_dim
+        if arch.q_lora_rank:
+            self.q_a_proj = _param((arch.q_lora_rank, H), dtype, device)
+            self.q_a_layernorm = RMSNorm(arch.q_lora_rank, arch.rms_norm_eps, dtype, device)
+            self.q_b_proj = _param((nh * qk, arch.q_lora_rank), dtype, device)
+        else:
+            self.q_proj = _param((nh * qk, H), dtype, device)
+        self.kv_a_proj_with_mqa = _param((self.kv_lora + self.qk_rope, H), dtype, device)
+        self.kv_a_layernorm = RMSNorm(self.kv_lora, arch.rms_norm_eps, dtype, device)
+        # Absorbed up-projections derived from kv_b_proj at load time.
+        self.w_uk = _param((nh, self.qk_nope, self.kv_lora), dtype, device)
+        self.w_uv_t = _param((nh, self.kv_lora, self.v_dim), dtype, device)
+        self.o_proj = _param((H, nh * self.v_dim), dtype, device)
+
+    def set_kv_b_proj(self, w: torch.Tensor) -> None:
+        nh = self.num_heads
+        w = w.view(nh, self.qk_nope + self.v_dim, self.kv_lora)
+        self.w_uk.data.copy_(w[:, : self.qk_nope, :])
+        self.w_uv_t.data.copy_(w[:, self.qk_nope :, :].transpose(1, 2))
+
+    def project_q(self, h: torch.Tensor) -> torch.Tensor:
+        if self.arch.q_lora_rank:
+            q = ops.linear(self.q_a_layernorm(ops.linear(h, self.q_a_proj)), self.q_b_proj)
+        else:
+            q = ops.linear(h, self.q_proj)
+        return q.view(h.shape[0], self.num_heads, self.qk_nope + self.qk_rope)
+
+    def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache: torch.Tensor, cos_sin: torch.Tensor):
+        T = h.shape[0]
+        q = self.project_q(h)
+        kv_a = ops.linear(h, self.kv_a_proj_with_mqa)
+        ops.mla_cache_write(
+            kv_cache, kv_a, self.kv_a_layernorm.weight, self.kv_a_layernorm.eps,
+            meta.positions, cos_sin, meta.slot_mapping, self.kv_lora,
+        )
+        q_pe = q[..., self.qk_nope :]
+        ops.rope_(q_pe, meta.positions, cos_sin, interleaved=True)
+        q_nope = q[..., : self.qk_nope]
+        # [H, T, nope] x [H, nope, kv_lora] -> [H, T, kv_lora]
+        q_lat = torch.bmm(q_nope.transpose(0, 1).to(self.w_uk.dtype), self.w_uk) if h.is_cuda else torch.bmm(
+            q_nope.transpose(0, 1).float(), self.w_uk.float()
+        ).to(h.dtype)
+        q_full = torch.cat([q_lat.transpose(0, 1), q_pe], dim=-1).contiguous()  # [T, H, 576]
+        if meta.is_decode:
+            o_lat = ops.mla_decode(q_full, kv_cache, meta.block_table, meta.seq_lens, self.scale, self.kv_lora)
+        else:
+            from afd_plugin_b200.ops import reference as ref
+
+            o_lat = torch.empty(T, self.num_heads, self.kv_lora, dtype=h.dtype, device=h.device)
+            for start, end, seq in meta.prefill_seqs or []:
+                o_lat[start:end] = ref.mla_prefill(
+                    q_full[start:end], kv_cache, meta.block_table[seq], meta.positions[start:end],
+                    self.scale, self.kv_lora,
+                )
+        if h.is_cuda:
+            o = torch.bmm(o_lat.transpose(0, 1), self.w_uv_t)  # [H, T, v]
+        else:
+            o = torch.bmm(o_lat.transpose(0, 1).float(), self.w_uv_t.float()).to(h.dtype)
+        o = o.transpose(0, 1).reshape(T, self.num_heads * self.v_dim)
+        return ops.linear(o, self.o_proj)
+
+
+class GQAAttention(nn.Module):
+    """Grouped-query attention with per-head QK RMSNorm (Qwen3)."""
+
+    def __init__(self, arch: ModelArchConfig, dtype, device):
+        super().__init__()
+        self.arch = arch
+        self.nq = arch.num_attention_heads
+        self.nkv = arch.num_key_value_heads
+        self.d = arch.head_dim
+        self.scale = arch.softmax_scale
+        H = arch.hidden_size
+        self.qkv_proj = _param(((self.nq + 2 * self.nkv) * self.d, H), dtype, device)
+        self.q_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
+        self.k_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
+        self.o_proj = _param((H, self.nq * self.d), dtype, device)
+
+    def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache: tuple[torch.Tensor, torch.Tensor], cos_sin):
+        T = h.shape[0]
+        qkv = ops.linear(h, self.qkv_proj)
+        q, k, v = qkv.split([self.nq * self.d, self.nkv * self.d, self.nkv * self.d], dim=-1)
+        q = self.q_norm(q.reshape(T * self.nq, self.d)).view(T, self.nq, self.d)
+        k = self.k_norm(k.reshape(T * self.nkv, self.d)).view(T, self.nkv, self.d)
+        v = v.reshape(T, self.nkv, self.d)
+        ops.rope_(q, meta.positions, cos_sin, interleaved=False)
+        ops.rope_(k, meta.positions, cos_sin, interleaved=False)
+        k_cache, v_cache = kv_cache
+        ops.gqa_cache_write(k_cache, v_cache, k, v, meta.slot_mapping)
+        if meta.is_decode:
+            o = ops.gqa_decode(q, k_cache, v_cache, meta.block_table, meta.seq_lens, self.scale)
+        else:
+            from afd_plugin_b200.ops import reference as ref
+
+            o = torch.empty_like(q)
+            for start, end, seq in meta.prefill_seqs or []:
+                o[start:end] = ref.gqa_prefill(
+                    q[start:end], k_cache, v_cache, meta.block_table[seq], meta.positions[start:end], self.scale
+                )
+        return ops.linear(o.reshape(T, self.nq * self.d), self.o_proj)
+
+
+class DenseMLP(nn.Module):
+    """SwiGLU MLP with gate and up stacked in ``w13 [2I, H]``."""
+
+    def __init__(self, hidden: int, inter: int, dtype, device, quant: str | None = None):
+        super().__init__()
+        wdtype = torch.float8_e4m3fn if quant == "fp8_block" else dtype
+        self.quant = quant
+        self.w13 = _param((2 * inter, hidden), wdtype, device)
+        self.w2 = _param((hidden, inter), wdtype, device)
+        if quant == "fp8_block":
+            self.w13_scale = _param(((2 * inter + 127) // 128, (hidden + 127) // 128), torch.float32, device)
+            self.w2_scale = _param(((hidden + 127) // 128, (inter + 127) // 128), torch.float32, device)
+        else:
+            self.w13_scale = None
+            self.w2_scale = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.quant == "fp8_block":
+            from afd_plugin_b200.ops import reference as ref
+
+            w13 = ref.dequant_block(self.w13, self.w13_scale).to(x.dtype)
+            w2 = ref.dequant_block(self.w2, self.w2_scale).to(x.dtype)
+            return ops.dense_mlp(x, w13, w2)
+        return ops.dense_mlp(x, self.w13, self.w2)
+
+
+class MoEGate(nn.Module):
+    def __init__(self, arch: ModelArchConfig, dtype, device):
+        super().__init__()
+        self.arch = arch
+        self.weight = _param((arch.n_routed_experts, arch.hidden_size), dtype, device)
+        if arch.topk_method == "noaux_tc":
+            self.e_score_correction_bias = _param((arch.n_routed_experts,), torch.float32, device)
+        else:
+            self.e_score_correction_bias = None
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        return (h.float() @ self.weight.float().t()) if not h.is_cuda else torch.mm(h, self.weight.t()).float()
+
+    def route(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        a = self.arch
+        return ops.topk_route(
+            logits,
+            a.num_experts_per_tok,
+            scoring=a.scoring_func,
+            renormalize=a.norm_topk_prob,
+            bias=self.e_score_correction_bias,
+            n_group=a.n_group if a.topk_method in ("group_limited_greedy", "noaux_tc") else 1,
+            topk_group=a.topk_group if a.topk_method in ("group_limited_greedy", "noaux_tc") else 1,
+            routed_scaling_factor=a.routed_scaling_factor,
+        )
+
+
+class RoutedExperts(nn.Module):
+    """Stacked expert weights for the experts ``[offset, offset + n_local)``."""
+
+    def __init__(self, arch: ModelArchConfig, n_local: int, offset: int, dtype, device):
+        super().__init__()
+        self.n_local = n_local
+        self.offset = offset
+        I, H = arch.moe_intermediate_size, arch.hidden_size
+        self.quant = arch.quant
+        wdtype = torch.float8_e4m3fn if arch.quant == "fp8_block" else dtype
+        self.w13 = _param((n_local, 2 * I, H), wdtype, device)
+        self.w2 = _param((n_local, H, I), wdtype, device)
+        if arch.quant == "fp8_block":
+            self.w13_scale = _param((n_local, (2 * I + 127) // 128, (H + 127) // 128), torch.float32, device)
+            self.w2_scale = _param((n_local, (H + 127) // 128, (I + 127) // 128), torch.float32, device)
+        else:
+            self.w13_scale = None
+            self.w2_scale = None
+
+    def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+        return ops.moe_experts(
+            x, self.w13, self.w2, topk_weights, topk_ids, expert_offset=self.offset,
+            w13_scale=self.w13_scale, w2_scale=self.w2_scale,
+        )
+
+
+class MoEBlock(nn.Module):
+    """Gate + routed experts (+ shared experts).  ``ep_rank/ep_size`` shard the experts."""
+
+    def __init__(self, arch: ModelArchConfig, dtype, device, *, ep_rank: int = 0, ep_size: int = 1, with_gate: bool = True):
+        super().__init__()
+        self.arch = arch
+        E = arch.n_routed_experts
+        if E % ep_size:
+            raise ValueError(f"{E} experts do not split over {ep_size} expert-parallel ranks")
+        n_local = E // ep_size
+        self.gate = MoEGate(arch, dtype, device) if with_gate else None
+        self.experts = RoutedExperts(arch, n_local, ep_rank * n_local, dtype, device)
+        self.shared_experts = (
+            DenseMLP(arch.hidden_size, arch.shared_intermediate_size, dtype, device, arch.quant)
+            if arch.n_shared_experts
+            else None
+        )
+
+    def forward(self, h: torch.Tensor, router_logits: torch.Tensor | None = None) -> torch.Tensor:
+        if router_logits is None:
+            if self.gate is None:
+                raise RuntimeError("MoE block without a gate needs router_logits")
+            router_logits = self.gate.logits(h)
+        if self.gate is None:
+            raise RuntimeError("MoE block needs gate parameters (bias / routing config) to route")
+        w, ids = self.gate.route(router_logits)
+        out = self.experts(h, w, ids)
+        if self.shared_experts is not None:
+            out = out + self.shared_experts(h)
+        return out
+
+    def forward_experts(self, h: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                        include_shared: bool = True) -> torch.Tensor:
+        out = self.experts(h, topk_weights, topk_ids)
+        if include_shared and self.shared_experts is not None:
+            out = out + self.shared_experts(h)
+        return out
+
+
+__all__ = [
+    "AttentionMetadata",
+    "DenseMLP",
+    "GQAAttention",
+    "MLAAttention",
+    "MoEBlock",
+    "MoEGate",
+    "RMSNorm",
+    "RoutedExperts",
+]

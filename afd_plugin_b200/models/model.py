@@ -1,0 +1,408 @@
+"""Role-aware causal LM shared by the DeepSeek and Qwen3-MoE wrappers.
+
+A model instance is built for one of three roles:
+
+* ``colocated`` -- every module (single-process serving, parity oracle);
+* ``attention`` -- embeddings, attention, norms, LM head (plus the MoE gate
+  and dense MLPs when ``compute_gate_on_attention``);
+* ``ffn`` -- dense MLPs and MoE blocks; experts are sharded over the FFN ranks
+  (expert parallelism, ``ep_rank``/``ep_size``).
+
+Behaviour follows the reference wrappers
+(``afd_plugin/model_executor/models/deepseek_v2.py:292-599`` and
+``qwen3_moe.py:102-321``): the Attention side hands post-attention-norm hidden
+states to the FFN side per layer; with ``compute_gate_on_attention`` the MoE
+gate runs on the Attention side and dense layers stay local.
+
+Weights are described by :class:`ParamSpec` entries named like the
+HuggingFace checkpoint, which drives both safetensors loading and the seeded
+random initialisation (per-name seeds, so split roles and the colocated model
+hold bit-identical weights).
+"""
+
+from __future__ import annotations
+
+import zlib
+from collections.abc import Callable, Iterator
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+from afd_plugin_b200 import ops
+from afd_plugin_b200.connectors.metadata import AFDExpertRoutingSpec
+from afd_plugin_b200.models.configs import ModelArchConfig
+from afd_plugin_b200.models.layers import (
+    AttentionMetadata,
+    DenseMLP,
+    GQAAttention,
+    MLAAttention,
+    MoEBlock,
+    RMSNorm,
+    _param,
+)
+from afd_plugin_b200.ops import reference as ref
+
+ROLES = ("colocated", "attention", "ffn")
+_ATTN = frozenset({"attention"})
+_FFN = frozenset({"ffn"})
+_BOTH = frozenset({"attention", "ffn"})
+
+
+@dataclass
+class ParamSpec:
+    name: str  # HF checkpoint name
+    shape: tuple[int, ...]
+    setter: Callable[[torch.Tensor], None]
+    init: str = "normal"  # "normal" | "ones" | "zeros"
+    # fp8-quantised target: random init quantises, checkpoints may carry a scale.
+    fp8_scale_name: str | None = None
+
+
+def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention: bool) -> frozenset[str]:
+    """Which AFD role(s) need checkpoint tensor ``name``.
+
+    Same classification as ``_checkpoint_weight_roles`` of the reference
+    (``deepseek_v2.py:69-92``, ``qwen3_moe.py:51-62``).
+    """
+    parts = name.split(".")
+    for i, p in enumerate(parts[:-2]):
+        if p != "layers":
+            continue
+        try:
+            layer = int(parts[i + 1])
+        except ValueError:
+            continue
+        stage = parts[i + 2]
+        rest = parts[i + 3 :]
+        if stage == "self_attn":
+            return _ATTN
+        if stage != "mlp":
+            return _BOTH
+        if not arch.is_moe_layer(layer):
+            return _ATTN if compute_gate_on_attention else _FFN
+        if rest and rest[0] == "gate" and compute_gate_on_attention:
+            return _BOTH
+        return _FFN
+    return _BOTH
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, arch: ModelArchConfig, idx: int, role: str, dtype, device, *, gate_on_attn: bool,
+                 ep_rank: int, ep_size: int):
+        super().__init__()
+        self.idx = idx
+        self.is_moe = arch.is_moe_layer(idx)
+        eps = arch.rms_norm_eps
+        has_attn = role in ("colocated", "attention")
+        self.input_layernorm = RMSNorm(arch.hidden_size, eps, dtype, device) if has_attn else None
+        self.post_attention_layernorm = RMSNorm(arch.hidden_size, eps, dtype, device) if has_attn else None
+        self.self_attn = None
+        if has_attn:
+            self.self_attn = MLAAttention(arch, dtype, device) if arch.is_mla else GQAAttention(arch, dtype, device)
+        self.mlp: nn.Module | None = None
+        self.gate_only = None
+        if role == "colocated":
+            self.mlp = MoEBlock(arch, dtype, device) if self.is_moe else DenseMLP(
+                arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
+        elif role == "attention":
+            if gate_on_attn:
+                if self.is_moe:
+                    from afd_plugin_b200.models.layers import MoEGate
+
+                    self.gate_only = MoEGate(arch, dtype, device)
+                else:
+                    self.mlp = DenseMLP(arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
+        else:  # ffn
+            if self.is_moe:
+                self.mlp = MoEBlock(arch, dtype, device, ep_rank=ep_rank, ep_size=ep_size)
+            elif not gate_on_attn:
+                self.mlp = DenseMLP(arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
+
+
+class AFDCausalLM(nn.Module):
+    """Decoder-only MoE LM split by AFD role."""
+
+    family = "base"
+
+    def __init__(
+        self,
+        arch: ModelArchConfig,
+        *,
+        role: str = "colocated",
+        dtype: torch.dtype = torch.bfloat16,
+        device: torch.device | str = "cpu",
+        compute_gate_on_attention: bool = False,
+        ep_rank: int = 0,
+        ep_size: int = 1,
+        max_positions: int | None = None,
+    ):
+        super().__init__()
+        if role not in ROLES:
+            raise ValueError(f"role must be one of {ROLES}, got {role!r}")
+        self._validate_arch(arch)
+        self.arch = arch
+        self.role = role
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.compute_gate_on_attention = compute_gate_on_attention
+        self.ep_rank, self.ep_size = ep_rank, ep_size
+        has_attn = role in ("colocated", "attention")
+        self.embed_tokens = _param((arch.vocab_size, arch.hidden_size), dtype, device) if has_attn else None
+        self.layers = nn.ModuleList(
+            DecoderLayer(arch, i, role, dtype, device, gate_on_attn=compute_gate_on_attention,
+                         ep_rank=ep_rank, ep_size=ep_size)
+            for i in range(arch.num_hidden_layers)
+        )
+        self.norm = RMSNorm(arch.hidden_size, arch.rms_norm_eps, dtype, device) if has_attn else None
+        self.lm_head = _param((arch.vocab_size, arch.hidden_size), dtype, device) if has_attn else None
+        self.cos_sin = None
+        if has_attn:
+            rot = arch.qk_rope_head_dim if arch.is_mla else arch.head_dim
+            npos = max_positions or min(arch.max_position_embeddings, 8192)
+            self.cos_sin = ref.rope_cos_sin_cache(rot, npos, arch.rope_theta, arch.rope_scaling, device)
+
+    # ----------------------------------------------------------- checks
+    def _validate_arch(self, arch: ModelArchConfig) -> None:
+        pass
+
+    # ----------------------------------------------------------- forward
+    @property
+    def num_layers(self) -> int:
+        return self.arch.num_hidden_layers
+
+    def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        return self.embed_tokens[input_ids.long()]
+
+    def run_attention(self, layer_idx: int, h: torch.Tensor, residual: torch.Tensor | None,
+                      meta: AttentionMetadata, kv_cache) -> tuple[torch.Tensor, torch.Tensor]:
+        layer = self.layers[layer_idx]
+        if residual is None:
+            residual = h.clone()
+            x = layer.input_layernorm(h)
+        else:
+            x, residual = layer.input_layernorm(h, residual)
+        return layer.self_attn(x, meta, kv_cache, self.cos_sin), residual
+
+    def post_attention_norm(self, layer_idx: int, attn_out: torch.Tensor, residual: torch.Tensor):
+        return self.layers[layer_idx].post_attention_layernorm(attn_out, residual)
+
+    def compute_router_logits(self, layer_idx: int, h: torch.Tensor) -> torch.Tensor:
+        layer = self.layers[layer_idx]
+        gate = layer.gate_only if layer.gate_only is not None else layer.mlp.gate
+        return gate.logits(h)
+
+    def compute_ffn_output(self, hidden_states: torch.Tensor, layer_idx: int, **kwargs) -> torch.Tensor:
+        layer = self.layers[layer_idx]
+        if layer.mlp is None:
+            raise RuntimeError(f"layer {layer_idx} FFN is not owned by role {self.role!r}")
+        if self.role == "ffn" and self.compute_gate_on_attention and layer.is_moe:
+            raise RuntimeError("Attention-side gate: the FFN role must call compute_experts_output")
+        return layer.mlp(hidden_states)
+
+    def compute_experts_output(self, hidden_states: torch.Tensor, layer_idx: int,
+                               router_logits: torch.Tensor) -> torch.Tensor:
+        layer = self.layers[layer_idx]
+        if not (self.compute_gate_on_attention and layer.is_moe):
+            raise RuntimeError("compute_experts_output requires an Attention-side-gate MoE layer")
+        return layer.mlp(hidden_states, router_logits=router_logits)
+
+    def final_logits(self, h: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        x, _ = self.norm(h, residual)
+        return ops.linear(x, self.lm_head)
+
+    def get_experts_layer_indices(self) -> tuple[int, ...]:
+        return self.arch.moe_layer_indices
+
+    def get_experts_routing_spec(self, layer_idx: int) -> AFDExpertRoutingSpec:
+        return AFDExpertRoutingSpec(router_logits_width=self.arch.n_routed_experts,
+                                    router_logits_dtype=torch.float32)
+
+    def ffn_layer_indices(self) -> tuple[int, ...]:
+        """Layers whose FFN runs on the FFN role."""
+        if self.compute_gate_on_attention:
+            return self.arch.moe_layer_indices
+        return tuple(range(self.num_layers))
+
+    # ----------------------------------------------------------- weights
+    def param_specs(self) -> Iterator[ParamSpec]:
+        a = self.arch
+        if self.embed_tokens is not None:
+            yield ParamSpec("model.embed_tokens.weight", tuple(self.embed_tokens.shape), _copy(self.embed_tokens))
+            yield ParamSpec("model.norm.weight", (a.hidden_size,), _copy(self.norm.weight), "ones")
+            yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
+        for i, layer in enumerate(self.layers):
+            p = f"model.layers.{i}."
+            if layer.input_layernorm is not None:
+                yield ParamSpec(p + "input_layernorm.weight", (a.hidden_size,), _copy(layer.input_layernorm.weight), "ones")
+                yield ParamSpec(p + "post_attention_layernorm.weight", (a.hidden_size,),
+                                _copy(layer.post_attention_layernorm.weight), "ones")
+                yield from self._attn_specs(p + "self_attn.", layer.self_attn)
+            if layer.gate_only is not None:
+                yield from _gate_specs(p + "mlp.gate.", layer.gate_only)
+            mlp = layer.mlp
+            if isinstance(mlp, DenseMLP):
+                yield from _mlp_specs(p + "mlp.", mlp, a.intermediate_size)
+            elif isinstance(mlp, MoEBlock):
+                if mlp.gate is not None:
+                    yield from _gate_specs(p + "mlp.gate.", mlp.gate)
+                ex = mlp.experts
+                I = a.moe_intermediate_size
+                for le in range(ex.n_local):
+                    e = ex.offset + le
+                    q = f"{p}mlp.experts.{e}."
+                    s13 = None if ex.w13_scale is None else ex.w13_scale[le]
+                    s2 = None if ex.w2_scale is None else ex.w2_scale[le]
+                    yield from _swiglu_specs(q, ex.w13[le], ex.w2[le], s13, s2, I, a.hidden_size)
+                if mlp.shared_experts is not None:
+                    yield from _mlp_specs(p + "mlp.shared_experts.", mlp.shared_experts, a.shared_intermediate_size)
+
+    def _attn_specs(self, p: str, attn) -> Iterator[ParamSpec]:
+        raise NotImplementedError
+
+    def init_random(self, seed: int = 0, std: float = 0.02) -> None:
+        """Seeded N(0, std) init; each tensor's stream depends only on (seed, name)."""
+        for spec in self.param_specs():
+            gen_dev = self.device if self.device.type == "cuda" else torch.device("cpu")
+            g = torch.Generator(device=gen_dev)
+            g.manual_seed((seed * 1_000_003 + zlib.crc32(spec.name.encode())) & 0x7FFFFFFFFFFFFFFF)
+            if spec.init == "ones":
+                t = torch.ones(spec.shape, dtype=torch.float32, device=gen_dev)
+            elif spec.init == "zeros":
+                t = torch.zeros(spec.shape, dtype=torch.float32, device=gen_dev)
+            else:
+                t = torch.empty(spec.shape, dtype=torch.float32, device=gen_dev).normal_(0.0, std, generator=g)
+            spec.setter(t)
+
+
+def _copy(dst: torch.Tensor) -> Callable[[torch.Tensor], None]:
+    def setter(src: torch.Tensor) -> None:
+        if tuple(src.shape) != tuple(dst.shape):
+            raise ValueError(f"shape mismatch {tuple(src.shape)} vs {tuple(dst.shape)}")
+        dst.data.copy_(src.to(dst.device, dst.dtype))
+
+    return setter
+
+
+def _rows(dst: torch.Tensor, start: int, stop: int) -> Callable[[torch.Tensor], None]:
+    def setter(src: torch.Tensor) -> None:
+        dst.data[start:stop].copy_(src.to(dst.device, dst.dtype))
+
+    return setter
+
+
+def _fp8_rows(dst_w: torch.Tensor, dst_s: torch.Tensor, start: int, stop: int) -> Callable[[torch.Tensor], None]:
+    """Setter for an fp8 block-quantised slice: quantises unless given e4m3 data."""
+
+    def setter(src: torch.Tensor) -> None:
+        if src.dtype == torch.float8_e4m3fn:
+            dst_w.data[start:stop].copy_(src.to(dst_w.device))
+            return
+        q, s = ref.quant_fp8_block_weight(src.float())
+        dst_w.data[start:stop].copy_(q.to(dst_w.device))
+        dst_s.data[start // 128 : (stop + 127) // 128].copy_(s.to(dst_s.device))
+
+    return setter
+
+
+def _swiglu_specs(p: str, w13: torch.Tensor, w2: torch.Tensor, s13, s2, inter: int, hidden: int) -> Iterator[ParamSpec]:
+    if s13 is None:
+        yield ParamSpec(p + "gate_proj.weight", (inter, hidden), _rows(w13, 0, inter))
+        yield ParamSpec(p + "up_proj.weight", (inter, hidden), _rows(w13, inter, 2 * inter))
+        yield ParamSpec(p + "down_proj.weight", (hidden, inter), _copy(w2))
+        return
+    if inter % 128:
+        raise ValueError("fp8 block quantisation needs the intermediate size to be a multiple of 128")
+    yield ParamSpec(p + "gate_proj.weight", (inter, hidden), _fp8_rows(w13, s13, 0, inter),
+                    fp8_scale_name=p + "gate_proj.weight_scale_inv")
+    yield ParamSpec(p + "up_proj.weight", (inter, hidden), _fp8_rows(w13, s13, inter, 2 * inter),
+                    fp8_scale_name=p + "up_proj.weight_scale_inv")
+    yield ParamSpec(p + "down_proj.weight", (hidden, inter), _fp8_rows(w2, s2, 0, hidden),
+                    fp8_scale_name=p + "down_proj.weight_scale_inv")
+
+
+def _mlp_specs(p: str, mlp: DenseMLP, inter: int) -> Iterator[ParamSpec]:
+    hidden = mlp.w13.shape[1]
+    yield from _swiglu_specs(p, mlp.w13, mlp.w2, mlp.w13_scale, mlp.w2_scale, inter, hidden)
+
+
+def _gate_specs(p: str, gate) -> Iterator[ParamSpec]:
+    yield ParamSpec(p + "weight", tuple(gate.weight.shape), _copy(gate.weight))
+    if gate.e_score_correction_bias is not None:
+        yield ParamSpec(p + "e_score_correction_bias", tuple(gate.e_score_correction_bias.shape),
+                        _copy(gate.e_score_correction_bias), "zeros")
+
+
+class AFDDeepseekV2ForCausalLM(AFDCausalLM):
+    """DeepSeek-V2/V3 family (MLA + DeepSeek MoE)."""
+
+    family = "deepseek"
+
+    def _validate_arch(self, arch: ModelArchConfig) -> None:
+        if not arch.is_mla:
+            raise ValueError("DeepSeek wrapper requires MLA attention")
+
+    def _attn_specs(self, p: str, attn: MLAAttention) -> Iterator[ParamSpec]:
+        a = self.arch
+        if a.q_lora_rank:
+            yield ParamSpec(p + "q_a_proj.weight", tuple(attn.q_a_proj.shape), _copy(attn.q_a_proj))
+            yield ParamSpec(p + "q_a_layernorm.weight", (a.q_lora_rank,), _copy(attn.q_a_layernorm.weight), "ones")
+            yield ParamSpec(p + "q_b_proj.weight", tuple(attn.q_b_proj.shape), _copy(attn.q_b_proj))
+        else:
+            yield ParamSpec(p + "q_proj.weight", tuple(attn.q_proj.shape), _copy(attn.q_proj))
+        yield ParamSpec(p + "kv_a_proj_with_mqa.weight", tuple(attn.kv_a_proj_with_mqa.shape),
+                        _copy(attn.kv_a_proj_with_mqa))
+        yield ParamSpec(p + "kv_a_layernorm.weight", (a.kv_lora_rank,), _copy(attn.kv_a_layernorm.weight), "ones")
+        shape = (a.num_attention_heads * (a.qk_nope_head_dim + a.v_head_dim), a.kv_lora_rank)
+        yield ParamSpec(p + "kv_b_proj.weight", shape, lambda t, _a=attn: _a.set_kv_b_proj(t.to(_a.w_uk.device, _a.w_uk.dtype)))
+        yield ParamSpec(p + "o_proj.weight", tuple(attn.o_proj.shape), _copy(attn.o_proj))
+
+
+class AFDDeepseekV3ForCausalLM(AFDDeepseekV2ForCausalLM):
+    pass
+
+
+class AFDDeepseekForCausalLM(AFDDeepseekV2ForCausalLM):
+    pass
+
+
+class AFDGlmMoeDsaForCausalLM(AFDDeepseekV2ForCausalLM):
+    pass
+
+
+class AFDQwen3MoeForCausalLM(AFDCausalLM):
+    """Qwen3-MoE (GQA + QK-norm, routed experts only, gate on the FFN side)."""
+
+    family = "qwen3_moe"
+
+    def __init__(self, arch: ModelArchConfig, **kw):
+        if kw.get("compute_gate_on_attention"):
+            raise ValueError("Qwen3-MoE AFD supports compute_gate_on_attention=false only")
+        super().__init__(arch, **kw)
+
+    def _validate_arch(self, arch: ModelArchConfig) -> None:
+        if arch.is_mla or not arch.qk_norm:
+            raise ValueError("Qwen3-MoE wrapper requires GQA attention with QK-norm")
+
+    def _attn_specs(self, p: str, attn: GQAAttention) -> Iterator[ParamSpec]:
+        d, nq, nkv = attn.d, attn.nq, attn.nkv
+        H = self.arch.hidden_size
+        yield ParamSpec(p + "q_proj.weight", (nq * d, H), _rows(attn.qkv_proj, 0, nq * d))
+        yield ParamSpec(p + "k_proj.weight", (nkv * d, H), _rows(attn.qkv_proj, nq * d, (nq + nkv) * d))
+        yield ParamSpec(p + "v_proj.weight", (nkv * d, H), _rows(attn.qkv_proj, (nq + nkv) * d, (nq + 2 * nkv) * d))
+        yield ParamSpec(p + "q_norm.weight", (d,), _copy(attn.q_norm.weight), "ones")
+        yield ParamSpec(p + "k_norm.weight", (d,), _copy(attn.k_norm.weight), "ones")
+        yield ParamSpec(p + "o_proj.weight", tuple(attn.o_proj.shape), _copy(attn.o_proj))
+
+
+__all__ = [
+    "AFDCausalLM",
+    "AFDDeepseekForCausalLM",
+    "AFDDeepseekV2ForCausalLM",
+    "AFDDeepseekV3ForCausalLM",
+    "AFDGlmMoeDsaForCausalLM",
+    "AFDQwen3MoeForCausalLM",
+    "ParamSpec",
+    "ROLES",
+    "weight_roles",
+]

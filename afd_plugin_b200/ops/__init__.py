@@ -1,0 +1,206 @@
+"""Operator entry points used by the models and the runtime.
+
+Every function takes the same arguments on CPU and CUDA.  CPU tensors run the
+plain PyTorch definitions in :mod:`afd_plugin_b200.ops.reference` (the numeric
+oracle and the path of the gloo multi-rank tests); CUDA tensors run the
+sm_100a kernels of the in-tree extension, which must be built -- a missing
+library raises rather than falling back.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from afd_plugin_b200.ops import reference as ref
+from afd_plugin_b200.ops._ext import ops as _cuda_ops
+
+SCORING_IDS = {"softmax": 0, "sigmoid": 1}
+
+
+def _cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+# ----------------------------------------------------------------- norms
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    if _cuda(x):
+        return _cuda_ops().rms_norm(x, weight, eps)
+    return ref.rms_norm(x, weight, eps)
+
+
+def fused_add_rms_norm(
+    x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Return ``(rms_norm(x + residual), x + residual)``; CUDA updates ``residual`` in place."""
+    if _cuda(x):
+        y = _cuda_ops().fused_add_rms_norm(x, residual, weight, eps)
+        return y, residual
+    return ref.fused_add_rms_norm(x, residual, weight, eps)
+
+
+def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
+    if _cuda(x):
+        return _cuda_ops().silu_and_mul(x)
+    return ref.silu_and_mul(x)
+
+
+# ------------------------------------------------------------------ RoPE
+def rope_(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, *, interleaved: bool) -> torch.Tensor:
+    """Rotate ``x [T, heads, rot]`` in place (last dim contiguous); returns ``x``."""
+    if _cuda(x):
+        _cuda_ops().rope_(x, positions, cos_sin, interleaved)
+        return x
+    x.copy_(ref.apply_rope(x, positions, cos_sin, interleaved=interleaved))
+    return x
+
+
+# --------------------------------------------------------------- routing
+def topk_route(
+    logits: torch.Tensor,
+    top_k: int,
+    *,
+    scoring: str = "softmax",
+    renormalize: bool = False,
+    bias: torch.Tensor | None = None,
+    n_group: int = 1,
+    topk_group: int = 1,
+    routed_scaling_factor: float = 1.0,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    if _cuda(logits):
+        return _cuda_ops().topk_route(
+            logits, top_k, SCORING_IDS[scoring], renormalize, bias, n_group, topk_group, routed_scaling_factor
+        )
+    return ref.topk_route(
+        logits,
+        top_k,
+        scoring=scoring,
+        renormalize=renormalize,
+        bias=bias,
+        n_group=n_group,
+        topk_group=topk_group,
+        routed_scaling_factor=routed_scaling_factor,
+    )
+
+
+# -------------------------------------------------------------- attention
+def mla_decode(
+    q: torch.Tensor,
+    kv_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float,
+    kv_lora_rank: int,
+    *,
+    num_splits: int = 0,
+) -> torch.Tensor:
+    if _cuda(q):
+        return _cuda_ops().mla_decode(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank, num_splits)
+    return ref.mla_decode(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank)
+
+
+def gqa_decode(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float,
+    *,
+    num_splits: int = 0,
+) -> torch.Tensor:
+    if _cuda(q):
+        return _cuda_ops().gqa_decode(q, k_cache, v_cache, block_table, seq_lens, scale, num_splits)
+    return ref.gqa_decode(q, k_cache, v_cache, block_table, seq_lens, scale)
+
+
+def mla_cache_write(
+    kv_cache: torch.Tensor,
+    kv_a: torch.Tensor,
+    norm_weight: torch.Tensor,
+    eps: float,
+    positions: torch.Tensor,
+    cos_sin: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    kv_lora_rank: int,
+) -> None:
+    """Normalise the latent, rotate the shared rope key and store both in the cache.
+
+    ``kv_a [T, kv_lora + rope]`` is the ``kv_a_proj_with_mqa`` output.
+    """
+    if _cuda(kv_a):
+        _cuda_ops().mla_cache_write(kv_cache, kv_a, norm_weight, eps, positions, cos_sin, slot_mapping, kv_lora_rank)
+        return
+    latent = ref.rms_norm(kv_a[:, :kv_lora_rank], norm_weight, eps)
+    k_pe = ref.apply_rope(kv_a[:, None, kv_lora_rank:], positions, cos_sin, interleaved=True)[:, 0]
+    flat = kv_cache.view(-1, kv_cache.shape[-1])
+    flat[slot_mapping.long()] = torch.cat([latent, k_pe], dim=-1).to(kv_cache.dtype)
+
+
+def gqa_cache_write(
+    k_cache: torch.Tensor, v_cache: torch.Tensor, k: torch.Tensor, v: torch.Tensor, slot_mapping: torch.Tensor
+) -> None:
+    if _cuda(k):
+        _cuda_ops().gqa_cache_write(k_cache, v_cache, k, v, slot_mapping)
+        return
+    kf = k_cache.view(-1, *k_cache.shape[2:])
+    vf = v_cache.view(-1, *v_cache.shape[2:])
+    kf[slot_mapping.long()] = k.to(k_cache.dtype)
+    vf[slot_mapping.long()] = v.to(v_cache.dtype)
+
+
+# -------------------------------------------------------------------- MoE
+def moe_experts(
+    x: torch.Tensor,
+    w13: torch.Tensor,
+    w2: torch.Tensor,
+    topk_weights: torch.Tensor,
+    topk_ids: torch.Tensor,
+    *,
+    expert_offset: int = 0,
+    w13_scale: torch.Tensor | None = None,
+    w2_scale: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Routed-expert output ``[T, H]`` (weights applied, summed over k)."""
+    if _cuda(x):
+        from afd_plugin_b200.ops.moe import moe_experts_cuda
+
+        return moe_experts_cuda(
+            x, w13, w2, topk_weights, topk_ids, expert_offset=expert_offset, w13_scale=w13_scale, w2_scale=w2_scale
+        )
+    return ref.moe_experts(
+        x, w13, w2, topk_weights, topk_ids, expert_offset=expert_offset, w13_scale=w13_scale, w2_scale=w2_scale
+    )
+
+
+def dense_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
+    if _cuda(x):
+        return torch.mm(silu_and_mul(torch.mm(x, w13.t())), w2.t())
+    return ref.dense_mlp(x, w13, w2)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Plain ``x @ w.T`` (cuBLAS on CUDA, fp32-accumulating reference on CPU)."""
+    if _cuda(x):
+        return torch.mm(x, w.t())
+    return (x.float() @ w.float().t()).to(x.dtype)
+
+
+def argmax(logits: torch.Tensor) -> torch.Tensor:
+    return torch.argmax(logits.float(), dim=-1).to(torch.int32)
+
+
+__all__ = [
+    "argmax",
+    "dense_mlp",
+    "fused_add_rms_norm",
+    "gqa_cache_write",
+    "gqa_decode",
+    "linear",
+    "mla_cache_write",
+    "mla_decode",
+    "moe_experts",
+    "rms_norm",
+    "rope_",
+    "silu_and_mul",
+    "topk_route",
+]

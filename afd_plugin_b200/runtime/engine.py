@@ -1,0 +1,248 @@
+"""Standalone decode engine: requests, paged KV, greedy sampling, graphs.
+
+Public API (what a user calls)::
+
+    engine = LLMEngine.colocated(engine_config)          # or AFD roles via workers
+    outputs = engine.generate(prompts, max_tokens=16)   # list[list[int]]
+
+    rid = engine.add_request(prompt_ids, max_tokens)
+    while engine.has_unfinished():
+        engine.step()                                   # {req_id: token}
+
+A step is either a prefill of newly admitted requests or a decode of every
+running request.  Decode steps copy their inputs host->device from pinned
+buffers, replay the captured graph of the padded batch size (eager when
+none fits) and read the sampled tokens back.
+
+On AFD Attention ranks several engines (one per rank, data parallel) step in
+lockstep: a per-step exchange over the Attention group agrees on eager vs
+graph mode and the padded size, the same agreement vLLM's DP metadata provides
+in the reference (``attention_model_runner.py:198-283``).
+"""
+
+from __future__ import annotations
+
+import itertools
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from afd_plugin_b200.engine_config import EngineConfig
+from afd_plugin_b200.runtime.cuda_graph import pad_to_capture_size, validate_cuda_graph_mode
+from afd_plugin_b200.runtime.ffn_executor import FFNExecutor, LocalFFNExecutor
+from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache
+from afd_plugin_b200.runtime.model_runner import ModelRunner
+
+
+@dataclass
+class Request:
+    req_id: int
+    prompt: list[int]
+    max_tokens: int
+    output: list[int] = field(default_factory=list)
+    blocks: list[int] = field(default_factory=list)
+
+    @property
+    def num_tokens(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    @property
+    def finished(self) -> bool:
+        return len(self.output) >= self.max_tokens
+
+
+class AttentionCoordinator:
+    """Per-step agreement among Attention (DP) ranks; trivial for one rank."""
+
+    def __init__(self, group=None, size: int = 1, rank: int = 0):
+        self.group, self.size, self.rank = group, size, rank
+
+    def exchange(self, num_tokens: int, is_prefill: bool) -> list[tuple[int, bool]]:
+        if self.group is None or self.size == 1:
+            return [(num_tokens, is_prefill)]
+        mine = torch.tensor([num_tokens, int(is_prefill)], dtype=torch.int64)
+        out = [torch.empty_like(mine) for _ in range(self.size)]
+        dist.all_gather(out, mine, group=self.group)
+        return [(int(t[0]), bool(t[1])) for t in out]
+
+
+class LLMEngine:
+    def __init__(
+        self,
+        engine_config: EngineConfig,
+        model,
+        ffn_executor: FFNExecutor | None = None,
+        *,
+        coordinator: AttentionCoordinator | None = None,
+        num_blocks: int | None = None,
+    ):
+        self.config = engine_config
+        self.model = model
+        self.device = model.device
+        mc, cc = engine_config.model_config, engine_config.cache_config
+        self.block_size = cc.block_size
+        self.max_batch = engine_config.max_num_seqs
+        self.max_blocks_per_seq = math.ceil(mc.max_model_len / self.block_size)
+        if num_blocks is None:
+            num_blocks = cc.num_blocks or (self.max_batch * self.max_blocks_per_seq + 1)
+        self.kv = KVCache(model.arch, num_blocks, self.block_size, model.dtype, self.device)
+        self.ffn = ffn_executor or LocalFFNExecutor(model)
+        num_ub = engine_config.parallel_config.num_ubatches if engine_config.parallel_config.use_ubatching else 1
+        self.runner = ModelRunner(model, self.kv, self.ffn, max_batch=self.max_batch,
+                                  max_blocks_per_seq=self.max_blocks_per_seq, num_ubatches=num_ub)
+        self.coordinator = coordinator or AttentionCoordinator()
+        policy = validate_cuda_graph_mode(engine_config, role="attention")
+        self.use_graphs = policy.enabled and self.device.type == "cuda"
+        self.capture_sizes = sorted(engine_config.compilation_config.cudagraph_capture_sizes) if self.use_graphs else []
+        self._ids = itertools.count()
+        self.waiting: list[Request] = []
+        self.running: list[Request] = []
+        self.finished: dict[int, Request] = {}
+        pin = self.device.type == "cuda"
+        mk = lambda *s, dt: torch.zeros(*s, dtype=dt, pin_memory=pin)  # noqa: E731
+        self._h_ids = mk(self.max_batch, dt=torch.int32)
+        self._h_pos = mk(self.max_batch, dt=torch.int64)
+        self._h_slot = mk(self.max_batch, dt=torch.int64)
+        self._h_table = mk(self.max_batch, self.max_blocks_per_seq, dt=torch.int32)
+        self._h_lens = mk(self.max_batch, dt=torch.int32)
+        self._h_next = mk(self.max_batch, dt=torch.int32)
+        self.last_h2d_bytes = 0
+        self.last_d2h_bytes = 0
+
+    # ------------------------------------------------------------ helpers
+    @classmethod
+    def colocated(cls, engine_config: EngineConfig, *, device="cuda", seed: int | None = None) -> "LLMEngine":
+        from afd_plugin_b200.models import build_model
+
+        mc = engine_config.model_config
+        model = build_model(mc.arch, role="colocated", dtype=mc.dtype, device=device,
+                            seed=mc.seed if seed is None else seed, checkpoint=mc.checkpoint,
+                            max_positions=mc.max_model_len)
+        return cls(engine_config, model)
+
+    def capture_graphs(self) -> None:
+        for size in self.capture_sizes:
+            if size <= self.max_batch:
+                self.runner.capture(size)
+
+    def add_request(self, prompt: list[int], max_tokens: int) -> int:
+        if len(prompt) + max_tokens > self.config.model_config.max_model_len:
+            raise ValueError("prompt + max_tokens exceeds max_model_len")
+        req = Request(next(self._ids), list(prompt), max_tokens)
+        self.waiting.append(req)
+        return req.req_id
+
+    def has_unfinished(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def _ensure_blocks(self, req: Request, upto_tokens: int) -> None:
+        need = math.ceil(upto_tokens / self.block_size) - len(req.blocks)
+        if need > 0:
+            req.blocks.extend(self.kv.allocator.allocate(need))
+
+    def _finish(self, req: Request) -> None:
+        self.kv.allocator.free(req.blocks)
+        req.blocks = []
+        self.finished[req.req_id] = req
+
+    # ---------------------------------------------------------------- step
+    def step(self) -> dict[int, int]:
+        admit = []
+        while self.waiting and len(self.running) + len(admit) < self.max_batch:
+            admit.append(self.waiting.pop(0))
+        is_prefill = bool(admit)
+        ntok = sum(len(r.prompt) for r in admit) if is_prefill else len(self.running)
+        votes = self.coordinator.exchange(ntok, is_prefill)
+        if any(p for _, p in votes):
+            return self._prefill_step(admit, votes)
+        return self._decode_step(votes)
+
+    def _prefill_step(self, admit: list[Request], votes) -> dict[int, int]:
+        if not admit:
+            # Another Attention rank prefills: take part with one placeholder row.
+            admit_tokens, tables, starts = [[0]], [[PAD_BLOCK]], [0]
+        else:
+            for r in admit:
+                self._ensure_blocks(r, len(r.prompt) + 1)
+            admit_tokens = [r.prompt for r in admit]
+            tables = [r.blocks for r in admit]
+            starts = [0] * len(admit)
+        toks = self.runner.prefill(admit_tokens, tables, starts,
+                                   **self._across(votes, sum(len(t) for t in admit_tokens)))
+        toks = toks.cpu().tolist()
+        out = {}
+        for r, t in zip(admit, toks):
+            r.output.append(int(t))
+            out[r.req_id] = int(t)
+            (self._finish(r) if r.finished else self.running.append(r))
+        return out
+
+    def _across(self, votes, mine: int) -> dict:
+        if len(votes) == 1:
+            return {}
+        # Ranks that are not prefilling join with one placeholder row.
+        return {"tokens_across_attn": {0: tuple(max(1, n) if p else 1 for n, p in votes)}}
+
+    def _decode_step(self, votes) -> dict[int, int]:
+        from afd_plugin_b200.runtime.model_runner import ubatch_splits
+
+        reqs = self.running
+        B = len(reqs)
+        top = max(max(n for n, _ in votes), 1)
+        padded = pad_to_capture_size(top, self.capture_sizes) if self.use_graphs else None
+        use_graph = padded is not None and padded in self.runner.graphs
+        # All Attention ranks run the same (padded) batch so FFN stages line up.
+        run_b = padded if use_graph else top
+        bs = self.block_size
+        self._h_table[:run_b].fill_(PAD_BLOCK)
+        for i, r in enumerate(reqs):
+            pos = r.num_tokens - 1
+            self._ensure_blocks(r, pos + 1)
+            self._h_ids[i] = r.output[-1] if r.output else r.prompt[-1]
+            self._h_pos[i] = pos
+            self._h_slot[i] = r.blocks[pos // bs] * bs + pos % bs
+            self._h_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
+            self._h_lens[i] = pos + 1
+        if run_b > B:
+            self._h_ids[B:run_b] = 0
+            self._h_pos[B:run_b] = 0
+            self._h_slot[B:run_b] = PAD_BLOCK * bs
+            self._h_lens[B:run_b] = 1
+        b = self.runner.buf
+        b.input_ids[:run_b].copy_(self._h_ids[:run_b], non_blocking=True)
+        b.positions[:run_b].copy_(self._h_pos[:run_b], non_blocking=True)
+        b.slot_mapping[:run_b].copy_(self._h_slot[:run_b], non_blocking=True)
+        b.block_table[:run_b].copy_(self._h_table[:run_b], non_blocking=True)
+        b.seq_lens[:run_b].copy_(self._h_lens[:run_b], non_blocking=True)
+        self.last_h2d_bytes = run_b * (4 + 8 + 8 + 4 + 4 * self.max_blocks_per_seq)
+        flags = {}
+        if len(votes) > 1:
+            sp = ubatch_splits(run_b, self.runner.num_ubatches)
+            flags["tokens_across_attn"] = {
+                s: tuple(sp[s + 1] - sp[s] for _ in votes) for s in range(len(sp) - 1)
+            }
+        nxt = self.runner.decode_step(run_b, use_graph=use_graph, **flags)
+        self._h_next[:run_b].copy_(nxt, non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+        self.last_d2h_bytes = run_b * 4
+        out = {}
+        still = []
+        for i, r in enumerate(reqs):
+            t = int(self._h_next[i])
+            r.output.append(t)
+            out[r.req_id] = t
+            (self._finish(r) if r.finished else still.append(r))
+        self.running = still
+        return out
+
+    def generate(self, prompts: list[list[int]], max_tokens: int) -> list[list[int]]:
+        ids = [self.add_request(p, max_tokens) for p in prompts]
+        while self.has_unfinished():
+            self.step()
+        return [self.finished[i].output for i in ids]
+
+
+__all__ = ["AttentionCoordinator", "LLMEngine", "Request"]

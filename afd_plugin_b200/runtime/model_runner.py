@@ -1,0 +1,229 @@
+"""Attention-side (or colocated) model runner: prefill, decode, graphs, DBO.
+
+One decode step runs ``embed -> layers -> final norm -> LM head -> argmax``
+over static device buffers.  The FFN of every layer goes through an
+:class:`~afd_plugin_b200.runtime.ffn_executor.FFNExecutor`.
+
+DBO (two ubatches) is a cooperative schedule of two generators: each ubatch
+runs its attention, hands its FFN input to the executor and yields; the other
+ubatch's attention is then issued before the first one collects its FFN
+output.  Every op lands on one CUDA stream in that interleaved order, so a
+decode step -- both ubatches, all layers -- captures as ONE CUDA graph
+(``FULL_DECODE_ONLY``).  This replaces the reference's two Python threads and
+``dbo_yield`` custom op (``afd_plugin/v1/worker/dbo.py:12-73``,
+``ubatch_wrapper.py:70-252``).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from afd_plugin_b200 import ops
+from afd_plugin_b200.models.layers import AttentionMetadata
+from afd_plugin_b200.runtime.ffn_executor import FFNExecutor
+from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache
+
+
+@dataclass
+class DecodeBuffers:
+    """Static device inputs of a decode step (graph-stable addresses)."""
+
+    input_ids: torch.Tensor
+    positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    block_table: torch.Tensor
+    seq_lens: torch.Tensor
+    next_tokens: torch.Tensor
+
+    @classmethod
+    def allocate(cls, max_batch: int, max_blocks: int, device) -> "DecodeBuffers":
+        z = lambda *s, dt: torch.zeros(*s, dtype=dt, device=device)  # noqa: E731
+        return cls(
+            input_ids=z(max_batch, dt=torch.int32),
+            positions=z(max_batch, dt=torch.int64),
+            slot_mapping=z(max_batch, dt=torch.int64),
+            block_table=z(max_batch, max_blocks, dt=torch.int32),
+            seq_lens=torch.ones(max_batch, dtype=torch.int32, device=device),
+            next_tokens=z(max_batch, dt=torch.int32),
+        )
+
+
+@dataclass
+class _Graph:
+    graph: torch.cuda.CUDAGraph
+    batch: int
+    ubatch_splits: tuple[int, ...]
+
+
+def ubatch_splits(batch: int, num_ubatches: int) -> tuple[int, ...]:
+    """Request-boundary split points: ``(0, b0, batch)`` for two ubatches."""
+    if num_ubatches <= 1 or batch < 2:
+        return (0, batch)
+    half = (batch + 1) // 2
+    return (0, half, batch)
+
+
+class ModelRunner:
+    def __init__(
+        self,
+        model,
+        kv_cache: KVCache,
+        ffn_executor: FFNExecutor,
+        *,
+        max_batch: int,
+        max_blocks_per_seq: int,
+        num_ubatches: int = 1,
+    ):
+        self.model = model
+        self.kv = kv_cache
+        self.ffn = ffn_executor
+        self.device = model.device
+        self.max_batch = max_batch
+        self.max_blocks = max_blocks_per_seq
+        self.num_ubatches = num_ubatches
+        self.buf = DecodeBuffers.allocate(max_batch, max_blocks_per_seq, self.device)
+        self.graphs: dict[int, _Graph] = {}
+        self.graph_pool = None
+
+    # ------------------------------------------------------------ forward
+    def _layers(self, h: torch.Tensor, meta: AttentionMetadata, stage: int):
+        """Generator over one ubatch; yields after each layer's FFN send."""
+        model = self.model
+        residual = None
+        for layer in range(model.num_layers):
+            attn_out, residual = model.run_attention(layer, h, residual, meta, self.kv.layer(layer))
+            handle = self.ffn.send(layer, attn_out, residual, stage)
+            yield None
+            h, residual = self.ffn.recv(layer, handle, stage)
+        yield (h, residual)
+
+    def _run_stages(self, embeds: list[torch.Tensor], metas: list[AttentionMetadata]):
+        gens = [self._layers(h, m, s) for s, (h, m) in enumerate(zip(embeds, metas))]
+        results: list = [None] * len(gens)
+        live = list(range(len(gens)))
+        while live:
+            for s in list(live):
+                out = next(gens[s])
+                if out is not None:
+                    results[s] = out
+                    live.remove(s)
+        return results
+
+    def forward(self, input_ids: torch.Tensor, metas: list[AttentionMetadata], splits: tuple[int, ...],
+                **step_flags) -> torch.Tensor:
+        """Logits for the last position of each token row (decode) or all rows (prefill)."""
+        counts = {s: splits[s + 1] - splits[s] for s in range(len(splits) - 1)}
+        self.ffn.begin_step(counts, **step_flags)
+        embeds = [self.model.embed(input_ids[splits[s] : splits[s + 1]]) for s in range(len(splits) - 1)]
+        outs = self._run_stages(embeds, metas)
+        self.ffn.end_step()
+        logits = [self.model.final_logits(h, r) for h, r in outs]
+        return logits[0] if len(logits) == 1 else torch.cat(logits, dim=0)
+
+    # ------------------------------------------------------------- decode
+    def _decode_metas(self, batch: int, splits: tuple[int, ...]) -> list[AttentionMetadata]:
+        b = self.buf
+        metas = []
+        for s in range(len(splits) - 1):
+            lo, hi = splits[s], splits[s + 1]
+            metas.append(AttentionMetadata(
+                positions=b.positions[lo:hi],
+                slot_mapping=b.slot_mapping[lo:hi],
+                block_table=b.block_table[lo:hi],
+                seq_lens=b.seq_lens[lo:hi],
+                is_decode=True,
+            ))
+        return metas
+
+    def _decode_body(self, batch: int, splits: tuple[int, ...], **flags) -> None:
+        b = self.buf
+        logits = self.forward(b.input_ids[:batch], self._decode_metas(batch, splits), splits, **flags)
+        b.next_tokens[:batch].copy_(ops.argmax(logits))
+
+    def decode_step(self, batch: int, *, use_graph: bool = True, **flags) -> torch.Tensor:
+        """Run one decode step on ``buf[:batch]``; returns ``next_tokens[:batch]`` (device)."""
+        g = self.graphs.get(batch) if use_graph else None
+        if g is not None:
+            self.ffn.begin_step({s: g.ubatch_splits[s + 1] - g.ubatch_splits[s]
+                                 for s in range(len(g.ubatch_splits) - 1)}, is_graph_replaying=True, **flags)
+            g.graph.replay()
+        else:
+            self._decode_body(batch, ubatch_splits(batch, self.num_ubatches), **flags)
+        return self.buf.next_tokens[:batch]
+
+    def capture(self, batch: int, *, warmup: int = 2) -> None:
+        """Capture one FULL decode graph for a padded batch size."""
+        splits = ubatch_splits(batch, self.num_ubatches)
+        self._pad_rows(0, batch)
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._decode_body(batch, splits, is_warmup=True)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        if self.graph_pool is None:
+            self.graph_pool = torch.cuda.graph_pool_handle()
+        # Control traffic for the capture pass goes out eagerly, outside the graph.
+        counts = {i: splits[i + 1] - splits[i] for i in range(len(splits) - 1)}
+        self.ffn.begin_step(counts, is_graph_capturing=True)
+        begin = self.ffn.begin_step
+        self.ffn.begin_step = lambda *a, **k: None  # suppressed inside the graph
+        try:
+            with torch.cuda.graph(graph, pool=self.graph_pool):
+                self._decode_body(batch, splits)
+        finally:
+            self.ffn.begin_step = begin
+        torch.cuda.synchronize(self.device)
+        self.graphs[batch] = _Graph(graph, batch, splits)
+
+    def _pad_rows(self, lo: int, hi: int) -> None:
+        """Padding rows read/write only the reserved padding block."""
+        b = self.buf
+        b.input_ids[lo:hi] = 0
+        b.positions[lo:hi] = 0
+        b.slot_mapping[lo:hi] = PAD_BLOCK * self.kv.block_size
+        b.block_table[lo:hi] = PAD_BLOCK
+        b.seq_lens[lo:hi] = 1
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+        self.graph_pool = None
+
+    # ------------------------------------------------------------ prefill
+    def prefill(self, token_lists: list[list[int]], block_tables: list[list[int]], start_positions: list[int],
+                **flags) -> torch.Tensor:
+        """Run prompt tokens (eager, one stage); returns the next token of each sequence."""
+        bs = self.kv.block_size
+        ids, pos, slots, seqs = [], [], [], []
+        t = 0
+        max_blocks = max(len(bt) for bt in block_tables)
+        table = torch.full((len(token_lists), max_blocks), PAD_BLOCK, dtype=torch.int32)
+        for i, (toks, bt, p0) in enumerate(zip(token_lists, block_tables, start_positions)):
+            table[i, : len(bt)] = torch.tensor(bt, dtype=torch.int32)
+            n = len(toks)
+            ids.extend(toks)
+            pp = list(range(p0, p0 + n))
+            pos.extend(pp)
+            slots.extend(bt[p // bs] * bs + p % bs for p in pp)
+            seqs.append((t, t + n, i))
+            t += n
+        dev = self.device
+        meta = AttentionMetadata(
+            positions=torch.tensor(pos, dtype=torch.int64, device=dev),
+            slot_mapping=torch.tensor(slots, dtype=torch.int64, device=dev),
+            block_table=table.to(dev),
+            seq_lens=torch.tensor([p0 + len(x) for x, p0 in zip(token_lists, start_positions)], dtype=torch.int32, device=dev),
+            is_decode=False,
+            prefill_seqs=seqs,
+        )
+        input_ids = torch.tensor(ids, dtype=torch.int32, device=dev)
+        logits = self.forward(input_ids, [meta], (0, t), **flags)
+        last = torch.tensor([e - 1 for _, e, _ in seqs], device=dev)
+        return ops.argmax(logits[last])
+
+
+__all__ = ["DecodeBuffers", "ModelRunner", "ubatch_splits"]
