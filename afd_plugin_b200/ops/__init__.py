@@ -109,8 +109,23 @@ def gqa_decode(
     num_splits: int = 0,
 ) -> torch.Tensor:
     if _cuda(q):
-        return _cuda_ops().gqa_decode(q, k_cache, v_cache, block_table, seq_lens, scale, num_splits)
+        return _gqa_decode_torch(q, k_cache, v_cache, block_table, seq_lens, scale)
     return ref.gqa_decode(q, k_cache, v_cache, block_table, seq_lens, scale)
+
+
+def _gqa_decode_torch(q, k_cache, v_cache, block_table, seq_lens, scale):
+    """Batched GQA decode in PyTorch ops (paged gather + masked softmax)."""
+    B, Hq, D = q.shape
+    bs, Hkv = k_cache.shape[1], k_cache.shape[2]
+    nblk = block_table.shape[1]
+    k = k_cache[block_table.long()].view(B, nblk * bs, Hkv, D)
+    v = v_cache[block_table.long()].view(B, nblk * bs, Hkv, D)
+    g = Hq // Hkv
+    s = torch.einsum("bkgd,bnkd->bkgn", q.view(B, Hkv, g, D).float(), k.float()) * scale
+    mask = torch.arange(nblk * bs, device=q.device)[None, :] >= seq_lens.long()[:, None]
+    s = s.masked_fill(mask[:, None, None, :], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("bkgn,bnkd->bkgd", p, v.float()).reshape(B, Hq, D).to(q.dtype)
 
 
 def mla_cache_write(

@@ -1,0 +1,320 @@
+// torch.ops.afd_b200.* registrations for the sm_100a kernels.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <mutex>
+#include <vector>
+
+#include "launchers.h"
+
+namespace {
+
+int dtype_code(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return kF32;
+    case at::kBFloat16: return kBF16;
+    case at::kHalf: return kF16;
+    default: TORCH_CHECK(false, "afd_b200: unsupported dtype ", t.scalar_type());
+  }
+  return -1;
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "afd_b200: ", name, " must be a CUDA tensor");
+}
+
+void check_vec16(const at::Tensor& t, int64_t last, const char* name) {
+  const int64_t align = 16 / t.element_size();
+  TORCH_CHECK(last % align == 0, "afd_b200: ", name, " last dim must be a multiple of ", align);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "afd_b200: ", name, " must be 16-byte aligned");
+}
+
+// Per-device status word written by kernels whose bounded waits expire.
+std::mutex g_status_mu;
+std::vector<at::Tensor> g_status;
+
+at::Tensor& status_tensor(int device) {
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  if ((int)g_status.size() <= device) g_status.resize(device + 1);
+  if (!g_status[device].defined()) {
+    g_status[device] = at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
+  }
+  return g_status[device];
+}
+
+int* status_ptr(const at::Tensor& like) { return status_tensor(like.get_device()).data_ptr<int>(); }
+
+// ------------------------------------------------------------------ norms
+at::Tensor rms_norm(const at::Tensor& x, const at::Tensor& w, double eps) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous(), "rms_norm: contiguous inputs required");
+  const int64_t hidden = x.size(-1);
+  check_vec16(x, hidden, "x");
+  auto out = at::empty_like(x);
+  const int rows = (int)(x.numel() / hidden);
+  c10::cuda::CUDAGuard g(x.device());
+  launch_rms_norm(out.data_ptr(), x.data_ptr(), w.data_ptr(), rows, (int)hidden, (float)eps, dtype_code(x), stream());
+  return out;
+}
+
+at::Tensor fused_add_rms_norm(const at::Tensor& x, at::Tensor& residual, const at::Tensor& w, double eps) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.is_contiguous() && residual.is_contiguous() && w.is_contiguous(), "fused_add_rms_norm: contiguous");
+  TORCH_CHECK(x.sizes() == residual.sizes() && x.scalar_type() == residual.scalar_type(), "shape/dtype mismatch");
+  const int64_t hidden = x.size(-1);
+  check_vec16(x, hidden, "x");
+  auto out = at::empty_like(x);
+  c10::cuda::CUDAGuard g(x.device());
+  launch_fused_add_rms_norm(out.data_ptr(), x.data_ptr(), residual.data_ptr(), w.data_ptr(),
+                            (int)(x.numel() / hidden), (int)hidden, (float)eps, dtype_code(x), stream());
+  return out;
+}
+
+at::Tensor silu_and_mul(const at::Tensor& x) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "silu_and_mul: contiguous input required");
+  const int64_t d = x.size(-1) / 2;
+  check_vec16(x, d, "x");
+  auto sizes = x.sizes().vec();
+  sizes.back() = d;
+  auto out = at::empty(sizes, x.options());
+  c10::cuda::CUDAGuard g(x.device());
+  launch_silu_and_mul(out.data_ptr(), x.data_ptr(), (int)(x.numel() / (2 * d)), (int)d, dtype_code(x), stream());
+  return out;
+}
+
+void rope_(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin, bool interleaved) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "rope_: x must be [T, H, rot] with contiguous last dim");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && cos_sin.scalar_type() == at::kFloat, "rope_: dtypes");
+  TORCH_CHECK(cos_sin.size(1) == x.size(2), "rope_: cos_sin width must equal rot dim");
+  c10::cuda::CUDAGuard g(x.device());
+  launch_rope(x.data_ptr(), positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(), (int)x.size(0), (int)x.size(1),
+              (int)x.size(2), x.stride(0), x.stride(1), interleaved, dtype_code(x), stream());
+}
+
+std::tuple<at::Tensor, at::Tensor> topk_route(const at::Tensor& logits, int64_t k, int64_t scoring, bool renorm,
+                                             const c10::optional<at::Tensor>& bias, int64_t n_group,
+                                             int64_t topk_group, double scale) {
+  check_cuda(logits, "logits");
+  auto lf = logits.to(at::kFloat).contiguous();
+  const int T = (int)lf.size(0), E = (int)lf.size(1);
+  TORCH_CHECK(E <= 512 && k <= 32, "topk_route: E <= 512 and k <= 32");
+  TORCH_CHECK(n_group <= 32 && (n_group <= 1 || E % n_group == 0), "topk_route: bad n_group");
+  auto w = at::empty({T, k}, lf.options());
+  auto ids = at::empty({T, k}, lf.options().dtype(at::kInt));
+  const float* bp = nullptr;
+  at::Tensor bf;
+  if (bias.has_value() && bias->defined()) {
+    bf = bias->to(at::kFloat).contiguous();
+    bp = bf.data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(logits.device());
+  if (T > 0)
+    launch_topk_route(lf.data_ptr<float>(), bp, w.data_ptr<float>(), ids.data_ptr<int32_t>(), T, E, (int)k,
+                      (int)scoring, renorm, (int)n_group, (int)topk_group, (float)scale, stream());
+  return {w, ids};
+}
+
+// --------------------------------------------------------------- KV cache
+void mla_cache_write(at::Tensor& cache, const at::Tensor& kv_a, const at::Tensor& w, double eps,
+                     const at::Tensor& positions, const at::Tensor& cos_sin, const at::Tensor& slots, int64_t L) {
+  check_cuda(kv_a, "kv_a");
+  const int64_t D = cache.size(-1);
+  const int R = (int)(D - L);
+  TORCH_CHECK(kv_a.size(1) == D && kv_a.stride(1) == 1, "mla_cache_write: kv_a [T, L+R] row-major");
+  TORCH_CHECK(cache.scalar_type() == kv_a.scalar_type() && cache.is_contiguous(), "mla_cache_write: cache");
+  TORCH_CHECK(kv_a.stride(0) % (16 / kv_a.element_size()) == 0, "mla_cache_write: row stride alignment");
+  c10::cuda::CUDAGuard g(kv_a.device());
+  launch_mla_cache_write(cache.data_ptr(), kv_a.data_ptr(), w.data_ptr(), (float)eps, positions.data_ptr<int64_t>(),
+                         cos_sin.data_ptr<float>(), slots.data_ptr<int64_t>(), (int)kv_a.size(0), (int)L, R,
+                         kv_a.stride(0), dtype_code(kv_a), stream());
+}
+
+void gqa_cache_write(at::Tensor& kc, at::Tensor& vc, const at::Tensor& k, const at::Tensor& v,
+                     const at::Tensor& slots) {
+  check_cuda(k, "k");
+  const int64_t row = k.size(1) * k.size(2);
+  TORCH_CHECK(k.stride(2) == 1 && k.stride(1) == k.size(2) && v.stride(2) == 1 && v.stride(1) == v.size(2),
+              "gqa_cache_write: [T, H, D] rows must be dense");
+  c10::cuda::CUDAGuard g(k.device());
+  launch_gqa_cache_write(kc.data_ptr(), vc.data_ptr(), k.data_ptr(), v.data_ptr(), slots.data_ptr<int64_t>(),
+                         (int)k.size(0), (int)row, k.stride(0), v.stride(0), dtype_code(k), stream());
+}
+
+// -------------------------------------------------------------- attention
+at::Tensor mla_decode(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& block_table,
+                      const at::Tensor& seq_lens, double scale, int64_t L, int64_t num_splits) {
+  check_cuda(q, "q");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16, "mla_decode: bf16 only");
+  TORCH_CHECK(q.is_contiguous() && cache.is_contiguous(), "mla_decode: contiguous q and cache");
+  TORCH_CHECK(q.size(2) == 576 && L == 512 && cache.size(-1) == 576, "mla_decode: latent 512 + rope 64 only");
+  TORCH_CHECK(q.size(1) % 16 == 0, "mla_decode: heads must be a multiple of 16");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt, "mla_decode: int32 meta");
+  TORCH_CHECK(block_table.stride(1) == 1, "mla_decode: block_table rows must be dense");
+  const int B = (int)q.size(0), H = (int)q.size(1);
+  const int bs = (int)cache.size(1), nblocks = (int)cache.size(0);
+  TORCH_CHECK(bs % 32 == 0, "mla_decode: block size must be a multiple of 32");
+  const int maxb = (int)block_table.size(1);
+  auto out = at::empty({B, H, L}, q.options());
+  if (B == 0) return out;
+  int splits = (int)num_splits;
+  if (splits <= 0) {
+    int dev_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+    splits = mla_decode_num_splits(B * (H / 16), maxb * bs, dev_sms);
+  }
+  at::Tensor po, pl;
+  if (splits > 1) {
+    po = at::empty({B, splits, H, L}, q.options().dtype(at::kFloat));
+    pl = at::empty({B, splits, H}, q.options().dtype(at::kFloat));
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  launch_mla_decode(out.data_ptr(), q.data_ptr(), cache.data_ptr(), block_table.data_ptr<int32_t>(),
+                    seq_lens.data_ptr<int32_t>(), splits > 1 ? po.data_ptr<float>() : nullptr,
+                    splits > 1 ? pl.data_ptr<float>() : nullptr, status_ptr(q), B, H, (int)L, 576 - (int)L, bs,
+                    nblocks, (int)block_table.stride(0), splits, (float)scale, stream());
+  return out;
+}
+
+// -------------------------------------------------------------------- MoE
+std::vector<at::Tensor> moe_align(const at::Tensor& topk_ids, int64_t e_local, int64_t offset) {
+  check_cuda(topk_ids, "topk_ids");
+  TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous(), "moe_align: int32 contiguous ids");
+  TORCH_CHECK(e_local <= 1024, "moe_align: at most 1024 local experts");
+  const int T = (int)topk_ids.size(0), k = (int)topk_ids.size(1);
+  auto o = topk_ids.options();
+  auto counts = at::empty({e_local}, o), offsets = at::empty({e_local}, o);
+  auto row_token = at::empty({std::max(T * k, 1)}, o), row_slot = at::empty({std::max(T * k, 1)}, o);
+  auto tsr = at::empty({T, k}, o), total = at::empty({1}, o);
+  c10::cuda::CUDAGuard g(topk_ids.device());
+  launch_moe_align(topk_ids.data_ptr<int32_t>(), T, k, (int)e_local, (int)offset, 1, counts.data_ptr<int32_t>(),
+                   offsets.data_ptr<int32_t>(), row_token.data_ptr<int32_t>(), row_slot.data_ptr<int32_t>(),
+                   tsr.data_ptr<int32_t>(), total.data_ptr<int32_t>(), stream());
+  return {counts, offsets, row_token, row_slot, tsr, total};
+}
+
+at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& row_token, const at::Tensor& total) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "moe_gather: contiguous x");
+  const int64_t rows_cap = row_token.size(0), H = x.size(1);
+  check_vec16(x, H, "x");
+  auto xs = at::empty({rows_cap, H}, x.options());
+  c10::cuda::CUDAGuard g(x.device());
+  launch_moe_gather(xs.data_ptr(), x.data_ptr(), row_token.data_ptr<int32_t>(), (int)rows_cap, (int)H,
+                    total.data_ptr<int32_t>(), dtype_code(x), stream());
+  return xs;
+}
+
+at::Tensor grouped_gemm(const at::Tensor& a, const at::Tensor& w, const at::Tensor& offsets, const at::Tensor& counts,
+                        int64_t epilogue) {
+  check_cuda(a, "a");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "grouped_gemm: bf16 only");
+  TORCH_CHECK(a.is_contiguous() && w.is_contiguous() && w.dim() == 3, "grouped_gemm: a [R,K], w [E,N,K] contiguous");
+  const int64_t R = a.size(0), K = a.size(1), E = w.size(0), N = w.size(1);
+  TORCH_CHECK(w.size(2) == K && K % 64 == 0, "grouped_gemm: K must match and be a multiple of 64");
+  if (epilogue == 1) {
+    TORCH_CHECK((N / 2) % 64 == 0 && N % 2 == 0, "grouped_gemm: SwiGLU needs I % 64 == 0");
+  } else {
+    TORCH_CHECK(N % 128 == 0, "grouped_gemm: N must be a multiple of 128");
+  }
+  const int64_t n_out = epilogue == 1 ? N / 2 : N;
+  auto d = at::empty({R, n_out}, a.options());
+  if (R == 0) return d;
+  c10::cuda::CUDAGuard g(a.device());
+  launch_grouped_gemm(d.data_ptr(), a.data_ptr(), w.data_ptr(), offsets.data_ptr<int32_t>(),
+                      counts.data_ptr<int32_t>(), (int)E, (int)R, (int)N, (int)K, (int)epilogue, status_ptr(a),
+                      stream());
+  return d;
+}
+
+at::Tensor moe_combine(const at::Tensor& ys, const at::Tensor& topk_w, const at::Tensor& tsr,
+                       const c10::optional<at::Tensor>& shared) {
+  check_cuda(ys, "ys");
+  const int T = (int)tsr.size(0), k = (int)tsr.size(1);
+  const int64_t H = ys.size(1);
+  check_vec16(ys, H, "ys");
+  TORCH_CHECK(topk_w.scalar_type() == at::kFloat && topk_w.is_contiguous(), "moe_combine: fp32 weights");
+  auto out = at::empty({T, H}, ys.options());
+  if (T == 0) return out;
+  const void* sp = nullptr;
+  if (shared.has_value() && shared->defined()) {
+    TORCH_CHECK(shared->is_contiguous() && shared->scalar_type() == ys.scalar_type(), "moe_combine: shared");
+    sp = shared->data_ptr();
+  }
+  c10::cuda::CUDAGuard g(ys.device());
+  launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), tsr.data_ptr<int32_t>(), T, k, (int)H,
+                     sp, dtype_code(ys), stream());
+  return out;
+}
+
+void decode_advance(at::Tensor& input_ids, at::Tensor& positions, at::Tensor& slots, at::Tensor& seq_lens,
+                    const at::Tensor& next_tokens, const at::Tensor& block_table, int64_t block_size,
+                    int64_t wrap_at, int64_t wrap_to) {
+  check_cuda(input_ids, "input_ids");
+  TORCH_CHECK(input_ids.scalar_type() == at::kInt && positions.scalar_type() == at::kLong &&
+                  slots.scalar_type() == at::kLong && seq_lens.scalar_type() == at::kInt &&
+                  next_tokens.scalar_type() == at::kInt && block_table.scalar_type() == at::kInt,
+              "decode_advance: dtypes");
+  const int batch = (int)input_ids.size(0);
+  if (batch == 0) return;
+  c10::cuda::CUDAGuard g(input_ids.device());
+  launch_decode_advance(input_ids.data_ptr<int32_t>(), positions.data_ptr<int64_t>(), slots.data_ptr<int64_t>(),
+                        seq_lens.data_ptr<int32_t>(), next_tokens.data_ptr<int32_t>(), block_table.data_ptr<int32_t>(),
+                        batch, (int)block_table.stride(0), (int)block_size, wrap_at, wrap_to, stream());
+}
+
+// ------------------------------------------------------------------ status
+int64_t read_status(int64_t device) { return status_tensor((int)device).item<int>(); }
+void reset_status(int64_t device) { status_tensor((int)device).zero_(); }
+at::Tensor status_word(int64_t device) { return status_tensor((int)device); }
+
+}  // namespace
+
+TORCH_LIBRARY(afd_b200, m) {
+  m.def("rms_norm(Tensor x, Tensor w, float eps) -> Tensor");
+  m.def("fused_add_rms_norm(Tensor x, Tensor(a!) residual, Tensor w, float eps) -> Tensor");
+  m.def("silu_and_mul(Tensor x) -> Tensor");
+  m.def("rope_(Tensor(a!) x, Tensor positions, Tensor cos_sin, bool interleaved) -> ()");
+  m.def("topk_route(Tensor logits, int k, int scoring, bool renorm, Tensor? bias, int n_group, int topk_group, "
+        "float scale) -> (Tensor, Tensor)");
+  m.def("mla_cache_write(Tensor(a!) cache, Tensor kv_a, Tensor w, float eps, Tensor positions, Tensor cos_sin, "
+        "Tensor slots, int L) -> ()");
+  m.def("gqa_cache_write(Tensor(a!) kc, Tensor(b!) vc, Tensor k, Tensor v, Tensor slots) -> ()");
+  m.def("mla_decode(Tensor q, Tensor cache, Tensor block_table, Tensor seq_lens, float scale, int L, "
+        "int num_splits) -> Tensor");
+  m.def("moe_align(Tensor topk_ids, int e_local, int offset) -> Tensor[]");
+  m.def("moe_gather(Tensor x, Tensor row_token, Tensor total) -> Tensor");
+  m.def("grouped_gemm(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue) -> Tensor");
+  m.def("moe_combine(Tensor ys, Tensor topk_w, Tensor token_slot_row, Tensor? shared) -> Tensor");
+  m.def("decode_advance(Tensor(a!) input_ids, Tensor(b!) positions, Tensor(c!) slots, Tensor(d!) seq_lens, "
+        "Tensor next_tokens, Tensor block_table, int block_size, int wrap_at, int wrap_to) -> ()");
+  m.def("read_status(int device) -> int");
+  m.def("reset_status(int device) -> ()");
+  m.def("status_word(int device) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
+  m.impl("rms_norm", &rms_norm);
+  m.impl("fused_add_rms_norm", &fused_add_rms_norm);
+  m.impl("silu_and_mul", &silu_and_mul);
+  m.impl("rope_", &rope_);
+  m.impl("topk_route", &topk_route);
+  m.impl("mla_cache_write", &mla_cache_write);
+  m.impl("gqa_cache_write", &gqa_cache_write);
+  m.impl("mla_decode", &mla_decode);
+  m.impl("moe_align", &moe_align);
+  m.impl("moe_gather", &moe_gather);
+  m.impl("grouped_gemm", &grouped_gemm);
+  m.impl("moe_combine", &moe_combine);
+  m.impl("decode_advance", &decode_advance);
+}
+
+TORCH_LIBRARY_IMPL(afd_b200, CompositeExplicitAutograd, m) {
+  m.impl("read_status", &read_status);
+  m.impl("reset_status", &reset_status);
+  m.impl("status_word", &status_word);
+}

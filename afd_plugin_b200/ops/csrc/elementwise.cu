@@ -1,0 +1,406 @@
+// Memory-bound kernels: RMSNorm (+fused residual add), SiLU-and-mul, RoPE,
+// routing top-k, KV-cache writes.  Every kernel moves 16-byte vectors and
+// computes in fp32.
+#include "common.cuh"
+#include "launchers.h"
+
+namespace afd {
+
+// ============================================================ RMSNorm
+// One group of TPR threads per row; each thread owns H/(8*TPR) 16-byte vectors.
+template <typename T, int TPR, bool kAddResidual>
+__global__ void rms_norm_kernel(T* __restrict__ out, const T* __restrict__ x, T* __restrict__ residual,
+                                const T* __restrict__ w, int rows, int hidden, float eps) {
+  constexpr int VN = Vec16<T>::N;
+  constexpr int kRowsPerBlock = (TPR >= 256) ? 1 : 256 / TPR;
+  const int sub = threadIdx.x / TPR;
+  const int lane = threadIdx.x % TPR;
+  const int row = blockIdx.x * kRowsPerBlock + sub;
+  __shared__ float red[kRowsPerBlock][(TPR + 31) / 32];
+  const bool active = row < rows;
+  const int nvec = hidden / VN;
+  float ss = 0.f;
+  // Cache up to 4 vectors per thread in registers (H <= 4*8*TPR), else re-read.
+  constexpr int kCache = 4;
+  Vec16<T> cache[kCache];
+  if (active) {
+    const T* xr = x + (size_t)row * hidden;
+    T* rr = kAddResidual ? residual + (size_t)row * hidden : nullptr;
+    int c = 0;
+    for (int v = lane; v < nvec; v += TPR, ++c) {
+      Vec16<T> a = load16(xr + v * VN);
+      if constexpr (kAddResidual) {
+        Vec16<T> r = load16(rr + v * VN);
+#pragma unroll
+        for (int i = 0; i < VN; ++i) a.v[i] = from_f32<T>(to_f32(a.v[i]) + to_f32(r.v[i]));
+        store16(rr + v * VN, a);
+      }
+#pragma unroll
+      for (int i = 0; i < VN; ++i) {
+        float f = to_f32(a.v[i]);
+        ss += f * f;
+      }
+      if (c < kCache) cache[c] = a;
+    }
+  }
+  if constexpr (TPR <= 32) {
+    ss = warp_sum(ss, TPR);
+  } else {
+    ss = warp_sum(ss, 32);
+    if ((threadIdx.x & 31) == 0) red[sub][lane / 32] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < TPR / 32; ++i) ss += red[sub][i];
+  }
+  if (!active) return;
+  const float inv = rsqrtf(ss / (float)hidden + eps);
+  const T* src = kAddResidual ? residual + (size_t)row * hidden : x + (size_t)row * hidden;
+  T* orow = out + (size_t)row * hidden;
+  int c = 0;
+  for (int v = lane; v < nvec; v += TPR, ++c) {
+    Vec16<T> a = (c < kCache) ? cache[c] : load16(src + v * VN);
+    Vec16<T> ww = load16(w + v * VN);
+    Vec16<T> o;
+#pragma unroll
+    for (int i = 0; i < VN; ++i) o.v[i] = from_f32<T>(to_f32(a.v[i]) * inv * to_f32(ww.v[i]));
+    store16(orow + v * VN, o);
+  }
+}
+
+template <typename T, bool kAdd>
+static void rms_norm_dispatch(void* out, const void* x, void* res, const void* w, int rows, int hidden, float eps,
+                              cudaStream_t s) {
+  constexpr int VN = Vec16<T>::N;
+  const int nvec = hidden / VN;
+  auto go = [&](auto tpr_tag) {
+    constexpr int TPR = decltype(tpr_tag)::value;
+    constexpr int RPB = (TPR >= 256) ? 1 : 256 / TPR;
+    dim3 grid((rows + RPB - 1) / RPB);
+    rms_norm_kernel<T, TPR, kAdd><<<grid, RPB * TPR, 0, s>>>((T*)out, (const T*)x, (T*)res, (const T*)w, rows,
+                                                             hidden, eps);
+  };
+  if (nvec <= 8) go(std::integral_constant<int, 8>{});
+  else if (nvec <= 16) go(std::integral_constant<int, 16>{});
+  else if (nvec <= 32) go(std::integral_constant<int, 32>{});
+  else if (nvec <= 64) go(std::integral_constant<int, 64>{});
+  else if (nvec <= 128) go(std::integral_constant<int, 128>{});
+  else go(std::integral_constant<int, 256>{});
+}
+
+// ============================================================ SiLU * up
+template <typename T>
+__global__ void silu_and_mul_kernel(T* __restrict__ out, const T* __restrict__ in, int rows, int d) {
+  constexpr int VN = Vec16<T>::N;
+  const int nvec = d / VN;
+  const size_t total = (size_t)rows * nvec;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / nvec;
+    const int v = (int)(i % nvec);
+    const T* row = in + r * 2 * d;
+    Vec16<T> g = load16(row + v * VN);
+    Vec16<T> u = load16(row + d + v * VN);
+    Vec16<T> o;
+#pragma unroll
+    for (int k = 0; k < VN; ++k) {
+      float gf = to_f32(g.v[k]);
+      o.v[k] = from_f32<T>(gf / (1.f + __expf(-gf)) * to_f32(u.v[k]));
+    }
+    store16(out + r * d + v * VN, o);
+  }
+}
+
+// ============================================================ RoPE (in place)
+// x: [T, H, rot] with strides (st, sh, 1); cos_sin: [P, rot] fp32 = [cos | sin].
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ x, const int64_t* __restrict__ pos, const float* __restrict__ cos_sin,
+                            int tokens, int heads, int rot, int64_t st, int64_t sh, bool interleaved) {
+  const int half = rot / 2;
+  const size_t total = (size_t)tokens * heads * half;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int p = (int)(i % half);
+    const size_t th = i / half;
+    const int h = (int)(th % heads);
+    const int t = (int)(th / heads);
+    const float* cs = cos_sin + pos[t] * rot;
+    const float c = cs[p], s = cs[half + p];
+    T* base = x + t * st + h * sh;
+    const int i0 = interleaved ? 2 * p : p;
+    const int i1 = interleaved ? 2 * p + 1 : p + half;
+    const float a = to_f32(base[i0]), b = to_f32(base[i1]);
+    base[i0] = from_f32<T>(a * c - b * s);
+    base[i1] = from_f32<T>(b * c + a * s);
+  }
+}
+
+// ============================================================ routing top-k
+// One warp per token; experts E <= 32*kMaxPerLane.  Selection ties break toward
+// the lower expert id.  scoring: 0 softmax, 1 sigmoid(+bias).
+constexpr int kMaxPerLane = 16;
+
+__global__ void topk_route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                  float* __restrict__ out_w, int32_t* __restrict__ out_id, int tokens, int E, int k,
+                                  int scoring, bool renorm, int n_group, int topk_group, float scale) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (warp >= tokens) return;
+  const float* row = logits + (size_t)warp * E;
+  float score[kMaxPerLane], sel[kMaxPerLane];
+  // expert of slot j on this lane: e = j*32 + lane
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kMaxPerLane; ++j) {
+    const int e = j * 32 + lane;
+    score[j] = (e < E) ? row[e] : -INFINITY;
+    mx = fmaxf(mx, score[j]);
+  }
+  if (scoring == 0) {
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+      const int e = j * 32 + lane;
+      score[j] = (e < E) ? __expf(score[j] - mx) : 0.f;
+      sum += score[j];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+      score[j] *= inv;
+      sel[j] = (j * 32 + lane < E) ? score[j] : -INFINITY;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+      const int e = j * 32 + lane;
+      score[j] = (e < E) ? 1.f / (1.f + __expf(-score[j])) : 0.f;
+      sel[j] = (e < E) ? score[j] + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+  }
+  if (n_group > 1 && topk_group < n_group) {
+    const int gsize = E / n_group;
+    // group score per group (computed redundantly by all lanes via shuffles)
+    uint32_t keep_mask = 0;  // bit g set -> group g kept (n_group <= 32)
+    float gscore_mine = -INFINITY;  // lane g holds group g's score
+    for (int g = 0; g < n_group; ++g) {
+      float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kMaxPerLane; ++j) {
+        const int e = j * 32 + lane;
+        if (e < E && e / gsize == g) {
+          const float v = sel[j];
+          if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+        }
+      }
+      // warp-wide top-2 of (m1, m2)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float a1 = __shfl_xor_sync(0xffffffffu, m1, o);
+        const float a2 = __shfl_xor_sync(0xffffffffu, m2, o);
+        float n1 = fmaxf(m1, a1);
+        float n2 = fmaxf(fminf(m1, a1), fmaxf(m2, a2));
+        m1 = n1;
+        m2 = n2;
+      }
+      const float gs = (scoring == 1) ? m1 + m2 : m1;
+      if (lane == g) gscore_mine = gs;
+    }
+    for (int r = 0; r < topk_group; ++r) {
+      float v = gscore_mine;
+      int idx = (lane < n_group && !((keep_mask >> lane) & 1u)) ? lane : 1 << 20;
+      if (idx == (1 << 20)) v = -INFINITY;
+      warp_argmax(v, idx);
+      keep_mask |= 1u << idx;
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+      const int e = j * 32 + lane;
+      if (e < E && !((keep_mask >> (e / gsize)) & 1u)) sel[j] = -INFINITY;
+    }
+  }
+  float wsum = 0.f;
+  float my_w = 0.f;
+  int my_id = 0;
+  for (int r = 0; r < k; ++r) {
+    float v = -INFINITY;
+    int idx = 1 << 20;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+      const int e = j * 32 + lane;
+      if (e < E && (sel[j] > v || (sel[j] == v && e < idx))) {
+        v = sel[j];
+        idx = e;
+      }
+    }
+    warp_argmax(v, idx);
+    // owner lane removes the winner and publishes its score
+    float wv = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+      if (j * 32 + lane == idx) {
+        wv = score[j];
+        sel[j] = -INFINITY;
+      }
+    }
+    wv = warp_sum(wv);
+    wsum += wv;
+    if (lane == r) {
+      my_w = wv;
+      my_id = idx;
+    }
+  }
+  if (lane < k) {
+    float w = renorm ? my_w / wsum : my_w;
+    out_w[(size_t)warp * k + lane] = w * scale;
+    out_id[(size_t)warp * k + lane] = my_id;
+  }
+}
+
+// ============================================================ MLA cache write
+// kv_a [T, L + R]: latent (RMSNorm) || k_pe (interleaved RoPE) -> cache[slot].
+template <typename T>
+__global__ void mla_cache_write_kernel(T* __restrict__ cache, const T* __restrict__ kv_a, const T* __restrict__ w,
+                                       float eps, const int64_t* __restrict__ pos, const float* __restrict__ cos_sin,
+                                       const int64_t* __restrict__ slots, int tokens, int L, int R,
+                                       int64_t kv_stride) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (warp >= tokens) return;
+  constexpr int VN = Vec16<T>::N;
+  const T* src = kv_a + (size_t)warp * kv_stride;
+  T* dst = cache + slots[warp] * (int64_t)(L + R);
+  float ss = 0.f;
+  for (int v = lane; v < L / VN; v += 32) {
+    Vec16<T> a = load16(src + v * VN);
+#pragma unroll
+    for (int i = 0; i < VN; ++i) ss += to_f32(a.v[i]) * to_f32(a.v[i]);
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)L + eps);
+  for (int v = lane; v < L / VN; v += 32) {
+    Vec16<T> a = load16(src + v * VN);
+    Vec16<T> ww = load16(w + v * VN);
+#pragma unroll
+    for (int i = 0; i < VN; ++i) a.v[i] = from_f32<T>(to_f32(a.v[i]) * inv * to_f32(ww.v[i]));
+    store16(dst + v * VN, a);
+  }
+  const float* cs = cos_sin + pos[warp] * R;
+  for (int p = lane; p < R / 2; p += 32) {
+    const float c = cs[p], s = cs[R / 2 + p];
+    const float a = to_f32(src[L + 2 * p]), b = to_f32(src[L + 2 * p + 1]);
+    dst[L + 2 * p] = from_f32<T>(a * c - b * s);
+    dst[L + 2 * p + 1] = from_f32<T>(b * c + a * s);
+  }
+}
+
+// GQA cache write: k, v [T, Hkv, D] -> caches [slots, Hkv, D].
+template <typename T>
+__global__ void gqa_cache_write_kernel(T* __restrict__ kc, T* __restrict__ vc, const T* __restrict__ k,
+                                       const T* __restrict__ v, const int64_t* __restrict__ slots, int tokens,
+                                       int row_elems, int64_t k_stride, int64_t v_stride) {
+  constexpr int VN = Vec16<T>::N;
+  const int nv = row_elems / VN;
+  const size_t total = (size_t)tokens * nv;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / nv);
+    const int c = (int)(i % nv);
+    const int64_t s = slots[t];
+    store16(kc + s * row_elems + c * VN, load16(k + t * k_stride + c * VN));
+    store16(vc + s * row_elems + c * VN, load16(v + t * v_stride + c * VN));
+  }
+}
+
+static int grid_for(size_t work, int block) {
+  size_t g = (work + block - 1) / block;
+  return (int)(g > 148 * 32 ? 148 * 32 : (g ? g : 1));
+}
+
+}  // namespace afd
+
+using namespace afd;
+
+#define AFD_DTYPE_SWITCH(dt, T, ...)                        \
+  switch (dt) {                                             \
+    case kF32: { using T = float; __VA_ARGS__; break; }     \
+    case kBF16: { using T = __nv_bfloat16; __VA_ARGS__; break; } \
+    case kF16: { using T = __half; __VA_ARGS__; break; }    \
+  }
+
+void launch_rms_norm(void* out, const void* x, const void* w, int rows, int hidden, float eps, int dtype,
+                     cudaStream_t s) {
+  AFD_DTYPE_SWITCH(dtype, T, (rms_norm_dispatch<T, false>(out, x, nullptr, w, rows, hidden, eps, s)));
+}
+
+void launch_fused_add_rms_norm(void* out, const void* x, void* residual, const void* w, int rows, int hidden,
+                               float eps, int dtype, cudaStream_t s) {
+  AFD_DTYPE_SWITCH(dtype, T, (rms_norm_dispatch<T, true>(out, x, residual, w, rows, hidden, eps, s)));
+}
+
+void launch_silu_and_mul(void* out, const void* in, int rows, int d, int dtype, cudaStream_t s) {
+  AFD_DTYPE_SWITCH(dtype, T, {
+    const size_t work = (size_t)rows * d / Vec16<T>::N;
+    silu_and_mul_kernel<T><<<grid_for(work, 256), 256, 0, s>>>((T*)out, (const T*)in, rows, d);
+  });
+}
+
+void launch_rope(void* x, const int64_t* pos, const float* cos_sin, int tokens, int heads, int rot, int64_t st,
+                 int64_t sh, bool interleaved, int dtype, cudaStream_t s) {
+  AFD_DTYPE_SWITCH(dtype, T, {
+    const size_t work = (size_t)tokens * heads * rot / 2;
+    rope_kernel<T><<<grid_for(work, 256), 256, 0, s>>>((T*)x, pos, cos_sin, tokens, heads, rot, st, sh, interleaved);
+  });
+}
+
+void launch_topk_route(const float* logits, const float* bias, float* w, int32_t* ids, int tokens, int E, int k,
+                       int scoring, bool renorm, int n_group, int topk_group, float scale, cudaStream_t s) {
+  const int warps_per_block = 4;
+  dim3 grid((tokens + warps_per_block - 1) / warps_per_block);
+  topk_route_kernel<<<grid, 32 * warps_per_block, 0, s>>>(logits, bias, w, ids, tokens, E, k, scoring, renorm,
+                                                          n_group, topk_group, scale);
+}
+
+void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float eps, const int64_t* pos,
+                            const float* cos_sin, const int64_t* slots, int tokens, int L, int R, int64_t kv_stride,
+                            int dtype, cudaStream_t s) {
+  AFD_DTYPE_SWITCH(dtype, T, {
+    dim3 grid((tokens + 3) / 4);
+    mla_cache_write_kernel<T><<<grid, 128, 0, s>>>((T*)cache, (const T*)kv_a, (const T*)w, eps, pos, cos_sin, slots,
+                                                   tokens, L, R, kv_stride);
+  });
+}
+
+void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, const int64_t* slots, int tokens,
+                            int row_elems, int64_t k_stride, int64_t v_stride, int dtype, cudaStream_t s) {
+  AFD_DTYPE_SWITCH(dtype, T, {
+    const size_t work = (size_t)tokens * row_elems / Vec16<T>::N;
+    gqa_cache_write_kernel<T><<<grid_for(work, 256), 256, 0, s>>>((T*)kc, (T*)vc, (const T*)k, (const T*)v, slots,
+                                                                 tokens, row_elems, k_stride, v_stride);
+  });
+}
+
+// ============================================================ decode advance
+// Device-resident decode loop: the sampled token becomes the next input and
+// every sequence moves one position (slot from its block table).
+__global__ void decode_advance_kernel(int32_t* __restrict__ input_ids, int64_t* __restrict__ positions,
+                                      int64_t* __restrict__ slots, int32_t* __restrict__ seq_lens,
+                                      const int32_t* __restrict__ next_tokens, const int32_t* __restrict__ table,
+                                      int batch, int table_stride, int block_size, int64_t wrap_at,
+                                      int64_t wrap_to) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  int64_t p = positions[b] + 1;
+  // Optional wrap keeps a long benchmark loop inside the allocated context window.
+  if (wrap_at > 0 && p >= wrap_at) p = wrap_to;
+  input_ids[b] = next_tokens[b];
+  positions[b] = p;
+  seq_lens[b] = (int32_t)(p + 1);
+  slots[b] = (int64_t)table[(size_t)b * table_stride + p / block_size] * block_size + p % block_size;
+}
+
+void launch_decode_advance(int32_t* input_ids, int64_t* positions, int64_t* slots, int32_t* seq_lens,
+                           const int32_t* next_tokens, const int32_t* table, int batch, int table_stride,
+                           int block_size, int64_t wrap_at, int64_t wrap_to, cudaStream_t s) {
+  decode_advance_kernel<<<(batch + 127) / 128, 128, 0, s>>>(input_ids, positions, slots, seq_lens, next_tokens,
+                                                            table, batch, table_stride, block_size, wrap_at, wrap_to);
+}

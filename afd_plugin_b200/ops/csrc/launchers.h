@@ -1,0 +1,61 @@
+// Host-side launchers of the afd_b200 kernels (torch-free interface).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+enum AfdDType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+// ---- elementwise.cu
+void launch_rms_norm(void* out, const void* x, const void* w, int rows, int hidden, float eps, int dtype,
+                     cudaStream_t s);
+void launch_fused_add_rms_norm(void* out, const void* x, void* residual, const void* w, int rows, int hidden,
+                               float eps, int dtype, cudaStream_t s);
+void launch_silu_and_mul(void* out, const void* in, int rows, int d, int dtype, cudaStream_t s);
+void launch_rope(void* x, const int64_t* pos, const float* cos_sin, int tokens, int heads, int rot, int64_t st,
+                 int64_t sh, bool interleaved, int dtype, cudaStream_t s);
+void launch_topk_route(const float* logits, const float* bias, float* w, int32_t* ids, int tokens, int E, int k,
+                       int scoring, bool renorm, int n_group, int topk_group, float scale, cudaStream_t s);
+void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float eps, const int64_t* pos,
+                            const float* cos_sin, const int64_t* slots, int tokens, int L, int R, int64_t kv_stride,
+                            int dtype, cudaStream_t s);
+void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, const int64_t* slots, int tokens,
+                            int row_elems, int64_t k_stride, int64_t v_stride, int dtype, cudaStream_t s);
+
+void launch_decode_advance(int32_t* input_ids, int64_t* positions, int64_t* slots, int32_t* seq_lens,
+                           const int32_t* next_tokens, const int32_t* table, int batch, int table_stride,
+                           int block_size, int64_t wrap_at, int64_t wrap_to, cudaStream_t s);
+
+// ---- mla_decode.cu
+// q [B, H, D] bf16 (D = L + R), cache [nblocks, bs, D] bf16, out [B, H, L] bf16.
+// Scratch (num_splits > 1): partial_o [B, splits, H, L] fp32, partial_lse [B, splits, H] fp32.
+// status: device int, set non-zero if a pipeline wait gave up.
+int mla_decode_num_splits(int batch, int max_seq_len, int num_sms);
+void launch_mla_decode(void* out, const void* q, const void* cache, const int32_t* block_table,
+                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
+                       int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
+                       int num_splits, float scale, cudaStream_t s);
+
+// ---- gqa_decode.cu
+void launch_gqa_decode(void* out, const void* q, const void* kc, const void* vc, const int32_t* block_table,
+                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int batch, int hq, int hkv,
+                       int d, int block_size, int max_blocks_per_seq, int num_splits, float scale, cudaStream_t s);
+int gqa_decode_num_splits(int batch, int hkv, int max_seq_len, int num_sms);
+
+// ---- moe.cu
+// Routing bookkeeping for a grouped expert GEMM over experts [offset, offset+E_local).
+void launch_moe_align(const int32_t* topk_ids, int tokens, int k, int e_local, int offset, int pad_to,
+                      int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_token, int32_t* row_slot,
+                      int32_t* token_slot_row, int* total_rows, cudaStream_t s);
+void launch_moe_gather(void* xs, const void* x, const int32_t* row_token, int rows_cap, int hidden,
+                       const int* total_rows, int dtype, cudaStream_t s);
+void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* token_slot_row, int tokens,
+                        int k, int hidden, const void* shared_out, int dtype, cudaStream_t s);
+
+// ---- gemm_tcgen05.cu
+// Grouped GEMM D[r, n] = sum_k A[r, k] * W[e(r), n, k] over row segments of
+// experts (rows of expert e: [offsets[e], offsets[e] + counts[e])).
+// epilogue: 0 = store bf16, 1 = SiLU(gate) * up over paired halves (N = 2I -> I).
+void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,
+                         const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
+                         int* status, cudaStream_t s);

@@ -1,0 +1,356 @@
+// Absorbed-MLA paged decode for sm_100a.
+//
+// One CTA = (request b, group of 16 heads, KV split).  A producer warp streams
+// 32-token KV tiles (576 bf16 per token) from the paged cache into shared
+// memory with TMA (cp.async.bulk.tensor, 128B swizzle; the 64-token cache
+// blocks are contiguous rows of a 2-D tensor map), completing on mbarriers;
+// four math warps compute S = Q K^T (tokens split over warps), an online
+// softmax (exp2 domain) and O += P V (latent dims split over warps) with
+// tensor-core MMAs reading the swizzled tiles through ldmatrix.  With several
+// splits each CTA writes a normalised partial O plus its log-sum-exp and a
+// combine kernel merges them.
+//
+// Memory-bound by design: per token per layer it reads 1152 B of cache and
+// does ~37 kFLOP for 16 heads, well under the tensor-core ceiling; the
+// pipeline's job is to keep enough tile bytes in flight to saturate HBM.
+//
+// Every mbarrier wait is bounded; on expiry the CTA records
+// kStatusWaitTimeout in `status` and leaves its loop.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "launchers.h"
+
+namespace afd {
+namespace mla {
+
+constexpr int kHeads = 16;        // heads per CTA (MMA M)
+constexpr int kTile = 32;         // tokens per pipeline stage
+constexpr int kStages = 2;
+constexpr int kMathWarps = 4;
+constexpr int kThreads = (kMathWarps + 1) * 32;
+constexpr int kBoxCols = 64;      // 128 B of bf16 per swizzle row
+constexpr int kD = 576, kL = 512; // DeepSeek MLA latent + rope
+constexpr int kBoxes = kD / kBoxCols;                 // 9
+constexpr int kTileBytes = kTile * kD * 2;            // 36864
+constexpr int kBoxBytes = kTile * kBoxCols * 2;       // 4096
+constexpr int kQBoxBytes = kHeads * kBoxCols * 2;     // 2048
+constexpr int kSStride = 36;                          // padded fp32 row of S
+
+struct Smem {
+  alignas(1024) uint8_t kv[kStages][kTileBytes];
+  alignas(1024) uint8_t q[kBoxes * kQBoxBytes];
+  float s[2][kHeads * kSStride];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+};
+
+// Byte offset of element (row, col) inside a 128B-swizzled tile made of
+// `kBoxes` column boxes of `rows` x 64 bf16.
+AFD_DEVICE uint32_t swz(int row, int col, int box_bytes) {
+  const int box = col >> 6;
+  const int chunk = (col & 63) >> 3;
+  return box * box_bytes + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
+}
+
+__global__ void __launch_bounds__(kThreads) mla_decode_kernel(
+    const __grid_constant__ CUtensorMap kv_map, __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ q,
+    const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
+    float* __restrict__ part_lse, int* __restrict__ status, int heads, int block_size, int max_blocks,
+    int num_splits, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int b = blockIdx.x;
+  const int hg = blockIdx.y;
+  const int split = blockIdx.z;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int seq = seq_lens[b];
+  const int n_tiles_total = (seq + kTile - 1) / kTile;
+  const int tiles_per_split = (n_tiles_total + num_splits - 1) / num_splits;
+  const int tile_begin = split * tiles_per_split;
+  const int tile_end = min(n_tiles_total, tile_begin + tiles_per_split);
+  const int n_tiles = max(0, tile_end - tile_begin);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kMathWarps);
+    }
+    fence_barrier_init();
+  }
+  // Q tile (16 heads x 576) -> swizzled smem, all threads.
+  const __nv_bfloat16* qb = q + ((size_t)b * heads + hg * kHeads) * kD;
+  for (int c = threadIdx.x; c < kHeads * (kD / 8); c += kThreads) {
+    const int r = c / (kD / 8);
+    const int col = (c % (kD / 8)) * 8;
+    *reinterpret_cast<uint4*>(sm.q + swz(r, col, kQBoxBytes)) = *reinterpret_cast<const uint4*>(qb + r * kD + col);
+  }
+  __syncthreads();
+
+  if (warp == kMathWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&kv_map);
+      for (int i = 0; i < n_tiles; ++i) {
+        const int st = i % kStages;
+        if (i >= kStages && !mbar_wait_bounded(&sm.empty[st], ((i / kStages) - 1) & 1)) {
+          atomicExch(status, kStatusWaitTimeout);
+          break;
+        }
+        const int t0 = (tile_begin + i) * kTile;
+        const int blk = block_table[(size_t)b * max_blocks + t0 / block_size];
+        const int row = blk * block_size + (t0 % block_size);
+        mbar_expect_tx(&sm.full[st], kTileBytes);
+#pragma unroll
+        for (int bx = 0; bx < kBoxes; ++bx)
+          tma_load_2d(sm.kv[st] + bx * kBoxBytes, &kv_map, &sm.full[st], bx * kBoxCols, row);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- math warps
+  const int r0 = lane >> 2;  // fragment rows r0, r0 + 8 (heads)
+  const int qd = lane & 3;
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  const uint32_t q_base = smem_u32(sm.q);
+  bool ok = true;
+
+  for (int i = 0; i < n_tiles && ok; ++i) {
+    const int st = i % kStages;
+    if (!mbar_wait_bounded(&sm.full[st], (i / kStages) & 1)) {
+      atomicExch(status, kStatusWaitTimeout);
+      ok = false;
+      break;
+    }
+    const uint32_t kv_base = smem_u32(sm.kv[st]);
+    const int tok0 = (tile_begin + i) * kTile;
+
+    // ---- S[16 x 8] for tokens 8*warp .. 8*warp+7
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 6
+    for (int kk = 0; kk < kD / 16; kk += 2) {
+      uint32_t a0[4], a1[4];
+      {
+        const int r = lane & 15;
+        const int c = kk * 16 + (lane >> 4) * 8;
+        ldmatrix_x4(a0[0], a0[1], a0[2], a0[3], q_base + swz(r, c, kQBoxBytes));
+        ldmatrix_x4(a1[0], a1[1], a1[2], a1[3], q_base + swz(r, c + 16, kQBoxBytes));
+      }
+      uint32_t b0, b1, b2, b3;
+      {
+        const int mi = lane >> 3;
+        const int row = warp * 8 + (lane & 7);
+        const int c = kk * 16 + mi * 8;
+        ldmatrix_x4(b0, b1, b2, b3, kv_base + swz(row, c, kBoxBytes));
+      }
+      mma_bf16_16816(sacc, a0, b0, b1);
+      mma_bf16_16816(sacc, a1, b2, b3);
+    }
+    // scale + mask, publish to smem
+    float* sS = sm.s[i & 1];
+    {
+      const int tcol = warp * 8 + qd * 2;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int tok = tok0 + tcol + (j & 1);
+        sacc[j] = (tok < seq) ? sacc[j] * scale_log2 : -INFINITY;
+      }
+      *reinterpret_cast<float2*>(&sS[r0 * kSStride + tcol]) = make_float2(sacc[0], sacc[1]);
+      *reinterpret_cast<float2*>(&sS[(r0 + 8) * kSStride + tcol]) = make_float2(sacc[2], sacc[3]);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kMathWarps * 32));
+
+    // ---- online softmax on rows r0 and r0+8 (quad covers all 32 tokens)
+    float sv[2][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float* srow = &sS[(r0 + 8 * h) * kSStride];
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const float2 lo = *reinterpret_cast<const float2*>(&srow[ks * 16 + qd * 2]);
+        const float2 hi = *reinterpret_cast<const float2*>(&srow[ks * 16 + 8 + qd * 2]);
+        sv[h][ks * 4 + 0] = lo.x;
+        sv[h][ks * 4 + 1] = lo.y;
+        sv[h][ks * 4 + 2] = hi.x;
+        sv[h][ks * 4 + 3] = hi.y;
+      }
+    }
+    float alpha[2];
+    uint32_t pa[2][4];  // A fragments of P for k-steps 0 and 1
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float mt = sv[h][0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) mt = fmaxf(mt, sv[h][j]);
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      const float m_new = fmaxf(m_run[h], mt);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      alpha[h] = exp2f(m_run[h] - m_use);
+      float ls = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sv[h][j] = exp2f(sv[h][j] - m_use);
+        ls += sv[h][j];
+      }
+      ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+      ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+      l_run[h] = l_run[h] * alpha[h] + ls;
+      m_run[h] = m_new;
+    }
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      pa[ks][0] = pack_bf16(sv[0][ks * 4 + 0], sv[0][ks * 4 + 1]);
+      pa[ks][1] = pack_bf16(sv[1][ks * 4 + 0], sv[1][ks * 4 + 1]);
+      pa[ks][2] = pack_bf16(sv[0][ks * 4 + 2], sv[0][ks * 4 + 3]);
+      pa[ks][3] = pack_bf16(sv[1][ks * 4 + 2], sv[1][ks * 4 + 3]);
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1];
+      o[n][3] *= alpha[1];
+    }
+
+    // ---- O[16 x 128 (this warp's latent slice)] += P V
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        const int n0 = warp * 128 + np * 16;
+        const int mi = lane >> 3;
+        const int row = ks * 16 + (mi & 1) * 8 + (lane & 7);
+        const int c = n0 + (mi >> 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(b0, b1, b2, b3, kv_base + swz(row, c, kBoxBytes));
+        mma_bf16_16816(o[np * 2], pa[ks], b0, b1);
+        mma_bf16_16816(o[np * 2 + 1], pa[ks], b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[st]);
+  }
+
+  // ---- epilogue
+  const int h_lo = hg * kHeads + r0;
+  const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f;
+  const float inv1 = l_run[1] > 0.f ? 1.f / l_run[1] : 0.f;
+  if (num_splits == 1) {
+    __nv_bfloat16* ob = out + ((size_t)b * heads) * kL;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int col = warp * 128 + n * 8 + qd * 2;
+      *reinterpret_cast<__nv_bfloat162*>(&ob[(size_t)h_lo * kL + col]) =
+          __floats2bfloat162_rn(o[n][0] * inv0, o[n][1] * inv0);
+      *reinterpret_cast<__nv_bfloat162*>(&ob[(size_t)(h_lo + 8) * kL + col]) =
+          __floats2bfloat162_rn(o[n][2] * inv1, o[n][3] * inv1);
+    }
+  } else {
+    float* po = part_o + (((size_t)b * num_splits + split) * heads) * kL;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int col = warp * 128 + n * 8 + qd * 2;
+      *reinterpret_cast<float2*>(&po[(size_t)h_lo * kL + col]) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
+      *reinterpret_cast<float2*>(&po[(size_t)(h_lo + 8) * kL + col]) = make_float2(o[n][2] * inv1, o[n][3] * inv1);
+    }
+    if (warp == 0 && qd == 0) {
+      float* pl = part_lse + ((size_t)b * num_splits + split) * heads;
+      pl[h_lo] = l_run[0] > 0.f ? m_run[0] + log2f(l_run[0]) : -INFINITY;
+      pl[h_lo + 8] = l_run[1] > 0.f ? m_run[1] + log2f(l_run[1]) : -INFINITY;
+    }
+  }
+}
+
+// Merge split partials: out[b,h,:] = sum_s w_s o_s / sum_s w_s, w_s = 2^(lse_s - max).
+__global__ void mla_combine_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ part_o,
+                                   const float* __restrict__ part_lse, int heads, int num_splits, int L) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  const float* pl = part_lse + (size_t)b * num_splits * heads + h;
+  float mx = -INFINITY;
+  for (int s = 0; s < num_splits; ++s) mx = fmaxf(mx, pl[(size_t)s * heads]);
+  float wsum = 0.f;
+  for (int s = 0; s < num_splits; ++s) {
+    const float v = pl[(size_t)s * heads];
+    wsum += (v == -INFINITY) ? 0.f : exp2f(v - mx);
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  for (int c = threadIdx.x * 4; c < L; c += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < num_splits; ++s) {
+      const float v = pl[(size_t)s * heads];
+      if (v == -INFINITY) continue;
+      const float w = exp2f(v - mx);
+      const float4 x = *reinterpret_cast<const float4*>(part_o + (((size_t)b * num_splits + s) * heads + h) * L + c);
+      acc.x += w * x.x;
+      acc.y += w * x.y;
+      acc.z += w * x.z;
+      acc.w += w * x.w;
+    }
+    __nv_bfloat16* ob = out + ((size_t)b * heads + h) * L + c;
+    *reinterpret_cast<__nv_bfloat162*>(ob) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+    *reinterpret_cast<__nv_bfloat162*>(ob + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+  }
+}
+
+}  // namespace mla
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 get_tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace afd
+
+using namespace afd;
+
+int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
+  const int tiles = (max_seq_len + mla::kTile - 1) / mla::kTile;
+  const int target = 2 * num_sms * 2;  // two resident CTAs per SM, ~two waves
+  int s = (target + batch - 1) / batch;
+  s = s < 1 ? 1 : s;
+  const int max_s = tiles / 2 > 0 ? tiles / 2 : 1;  // keep >= 2 tiles per split
+  return s > max_s ? max_s : s;
+}
+
+void launch_mla_decode(void* out, const void* q, const void* cache, const int32_t* block_table,
+                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
+                       int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
+                       int num_splits, float scale, cudaStream_t s) {
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)(L + R), (cuuint64_t)num_blocks * block_size};
+  const cuuint64_t strides[1] = {(cuuint64_t)(L + R) * 2};
+  const cuuint32_t box[2] = {mla::kBoxCols, mla::kTile};
+  const cuuint32_t estr[2] = {1, 1};
+  get_tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(cache), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const int smem = (int)sizeof(mla::Smem) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(mla::mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_set = true;
+  }
+  dim3 grid(batch, heads / mla::kHeads, num_splits);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  mla::mla_decode_kernel<<<grid, mla::kThreads, smem, s>>>(
+      map, (__nv_bfloat16*)out, (const __nv_bfloat16*)q, block_table, seq_lens, partial_o, partial_lse, status,
+      heads, block_size, max_blocks_per_seq, num_splits, scale_log2);
+  if (num_splits > 1) {
+    mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>((__nv_bfloat16*)out, partial_o, partial_lse, heads,
+                                                               num_splits, L);
+  }
+}

@@ -1,0 +1,43 @@
+"""CUDA MoE expert path: align -> gather -> tcgen05 grouped GEMMs -> combine.
+
+The two GEMMs run on the 5th-generation tensor cores (``grouped_gemm``):
+``gate_up`` with the SwiGLU epilogue fused, then ``down``.  No step needs a
+host synchronisation, so the whole path captures into a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from afd_plugin_b200.ops._ext import ops as _cuda_ops
+
+
+def moe_experts_cuda(
+    x: torch.Tensor,
+    w13: torch.Tensor,
+    w2: torch.Tensor,
+    topk_weights: torch.Tensor,
+    topk_ids: torch.Tensor,
+    *,
+    expert_offset: int = 0,
+    w13_scale: torch.Tensor | None = None,
+    w2_scale: torch.Tensor | None = None,
+    shared_out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    if w13_scale is not None or w2_scale is not None:
+        from afd_plugin_b200.ops import reference as ref
+
+        # fp8 block-scaled experts: dequantise once per call (bf16 GEMMs).
+        w13 = torch.stack([ref.dequant_block(w13[e], w13_scale[e]) for e in range(w13.shape[0])]).to(x.dtype)
+        w2 = torch.stack([ref.dequant_block(w2[e], w2_scale[e]) for e in range(w2.shape[0])]).to(x.dtype)
+    C = _cuda_ops()
+    e_local = w13.shape[0]
+    ids = topk_ids.to(torch.int32).contiguous()
+    counts, offsets, row_token, _row_slot, tsr, total = C.moe_align(ids, e_local, expert_offset)
+    xs = C.moe_gather(x.contiguous(), row_token, total)
+    h = C.grouped_gemm(xs, w13, offsets, counts, 1)
+    y = C.grouped_gemm(h, w2, offsets, counts, 0)
+    return C.moe_combine(y, topk_weights.float().contiguous(), tsr, shared_out)
+
+
+__all__ = ["moe_experts_cuda"]

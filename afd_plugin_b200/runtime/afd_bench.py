@@ -1,0 +1,76 @@
+"""Multi-GPU AFD decode benchmark body (one process per GPU, torchrun).
+
+Attention ranks run the device-resident decode loop and then the public-API
+loop; FFN ranks serve exactly the steps the Attention side issues.  Every
+rank times its own loop with CUDA events; the reported time is the max over
+ranks.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from afd_plugin_b200.parallel.topology import role_of_world_rank
+from afd_plugin_b200.utils.clocks import ClockSampler
+
+
+def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_config, prime_requests, device_loop,
+                 e2e_loop, count_our_kernels) -> dict:
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=600))
+    role, role_rank = role_of_world_rank(rank, attention_size=num_attn, ffn_size=num_ffn)
+    if connector == "P2pNcclAFDConnector":
+        args.eager = True  # NCCL p2p through torch.distributed is not captured into graphs here
+    ec, per_rank = build_config(args, num_attn=num_attn, num_ffn=num_ffn, role=role, connector=connector)
+    # Even split of the global batch over the Attention ranks.
+    shares = [args.batch // num_attn + (1 if i < args.batch % num_attn else 0) for i in range(num_attn)]
+    total_steps = 2 * (args.warmup + args.steps) + (0 if args.no_e2e else 0)
+    result: dict = {"parallelism": f"afd-{num_attn}A{num_ffn}F-{connector}"}
+    if role == "ffn":
+        from afd_plugin_b200.runtime.workers import AFDFFNWorker
+
+        w = AFDFFNWorker(ec, local_rank=local)
+        dist.barrier()
+        with ClockSampler(local) as clk:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = w.run_ffn_server_loop()  # until the Attention side's shutdown payload
+        result.update(ms=0.0, per_step=[0.0], clocks=clk.summary(), steps_served=n)
+        w.shutdown()
+    else:
+        from afd_plugin_b200.runtime.workers import AFDAttentionWorker
+
+        w = AFDAttentionWorker(ec, local_rank=local)
+        eng = w.engine
+        prime_requests(eng, shares[role_rank], args.isl, args.osl, seed=role_rank)
+        if not args.eager:
+            eng.capture_graphs()
+        batch = len(eng.running)
+        dist.barrier()
+        with ClockSampler(local) as clk:
+            per_step, ms = device_loop(eng, batch, args.warmup, args.steps, args.isl, args.osl)
+            e2e = None
+            if not args.no_e2e:
+                e2e_ms, h2d, d2h = e2e_loop(eng, args.warmup, args.steps)
+                e2e = (e2e_ms, h2d, d2h)
+        result.update(ms=ms, per_step=per_step, clocks=clk.summary(), e2e_raw=e2e, batch=batch)
+        grp = w.groups.attention_group
+        if grp is not None and num_attn > 1:
+            dist.barrier(group=grp)
+        w.shutdown()
+    # max over ranks of the device-timed loop and of the e2e wall time
+    t = torch.tensor([result["ms"], (result.get("e2e_raw") or (0.0,))[0]], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    result["ms"] = float(t[0])
+    if not args.no_e2e and role == "attention" and result.get("e2e_raw"):
+        _, h2d, d2h = result["e2e_raw"]
+        result["e2e"] = {"value": round(args.batch * args.steps / (float(t[1]) / 1e3), 1), "unit": "tok/s",
+                         "h2d_bytes_per_step": h2d * num_attn, "d2h_bytes_per_step": d2h * num_attn}
+    result["launches"] = None
+    dist.barrier()
+    dist.destroy_process_group()
+    return result
+
+
+__all__ = ["run_afd_rank"]

@@ -134,6 +134,49 @@ class LLMEngine:
         self.waiting.append(req)
         return req.req_id
 
+    def admit_prefilled(self, prompts: list[list[int]], first_tokens: list[int], *, reserve_tokens: int = 0) -> list[int]:
+        """Admit requests whose prompt KV is already in the cache (decode-only mode).
+
+        The decode-benchmark counterpart of the reference's
+        ``AFDDecodeBenchConnector`` (``tools/benchmarks/decode_bench.py:41-140``),
+        which reports every prompt token but the last as remotely prefilled:
+        blocks for ``len(prompt) + reserve_tokens`` positions are allocated, the
+        caller fills the cache (e.g. :meth:`KVCache.fill_random_`), and each
+        request starts decoding from ``first_tokens[i]``.
+        """
+        ids = []
+        for p, t in zip(prompts, first_tokens):
+            req = Request(next(self._ids), list(p), max(1, self.config.model_config.max_model_len - len(p)))
+            self._ensure_blocks(req, len(p) + max(1, reserve_tokens))
+            req.output.append(int(t))
+            self.running.append(req)
+            ids.append(req.req_id)
+        return ids
+
+    def load_decode_batch(self) -> int:
+        """Copy the running batch's decode inputs into the runner's device buffers.
+
+        Returns the batch size; used to prime device-resident decode loops.
+        """
+        bs = self.block_size
+        b = self.runner.buf
+        reqs = self.running
+        for i, r in enumerate(reqs):
+            pos = r.num_tokens - 1
+            self._h_ids[i] = r.output[-1]
+            self._h_pos[i] = pos
+            self._h_slot[i] = r.blocks[pos // bs] * bs + pos % bs
+            self._h_table[i].fill_(PAD_BLOCK)
+            self._h_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
+            self._h_lens[i] = pos + 1
+        n = len(reqs)
+        b.input_ids[:n].copy_(self._h_ids[:n])
+        b.positions[:n].copy_(self._h_pos[:n])
+        b.slot_mapping[:n].copy_(self._h_slot[:n])
+        b.block_table[:n].copy_(self._h_table[:n])
+        b.seq_lens[:n].copy_(self._h_lens[:n])
+        return n
+
     def has_unfinished(self) -> bool:
         return bool(self.waiting or self.running)
 

@@ -153,6 +153,19 @@ class ModelRunner:
             self._decode_body(batch, ubatch_splits(batch, self.num_ubatches), **flags)
         return self.buf.next_tokens[:batch]
 
+    def advance_on_device(self, batch: int, *, wrap_at: int = 0, wrap_to: int = 0) -> None:
+        """Feed ``next_tokens`` back as inputs and move every row one position.
+
+        Used by device-resident decode loops (benchmarks); rows must own KV
+        blocks for the next position already.
+        """
+        from afd_plugin_b200.ops._ext import ops as cuda_ops
+
+        b = self.buf
+        cuda_ops().decode_advance(b.input_ids[:batch], b.positions[:batch], b.slot_mapping[:batch],
+                                  b.seq_lens[:batch], b.next_tokens[:batch], b.block_table[:batch],
+                                  self.kv.block_size, wrap_at, wrap_to)
+
     def capture(self, batch: int, *, warmup: int = 2) -> None:
         """Capture one FULL decode graph for a padded batch size."""
         splits = ubatch_splits(batch, self.num_ubatches)

@@ -1,0 +1,147 @@
+"""sm_100a kernels vs the plain PyTorch fp32 reference of the same op."""
+
+import math
+
+import pytest
+import torch
+
+from afd_plugin_b200 import ops
+from afd_plugin_b200.ops import _ext
+from afd_plugin_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _close(a, b, atol, rtol=0.0):
+    torch.testing.assert_close(a.float().cpu(), b.float().cpu(), atol=atol, rtol=rtol)
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    C = _ext.ops()
+    C.reset_status(0)
+    yield
+    torch.cuda.synchronize()
+    assert C.read_status(0) == 0, "a kernel wait timed out"
+
+
+def test_extension_loaded_from_tree():
+    assert _ext.load() and _ext.loaded_path().endswith(".so")
+
+
+@pytest.mark.parametrize("hidden", [128, 512, 2048, 7168])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_rms_norm(hidden, dtype):
+    x = torch.randn(37, hidden, device=DEV, dtype=dtype)
+    w = torch.randn(hidden, device=DEV, dtype=dtype)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+    _close(ops.rms_norm(x, w, 1e-6), ref.rms_norm(x.float(), w.float(), 1e-6), tol, 1e-2)
+    r = torch.randn_like(x)
+    r_ref = r.clone()
+    y, r_out = ops.fused_add_rms_norm(x, r, w, 1e-6)
+    y_ref, rr = ref.fused_add_rms_norm(x, r_ref, w, 1e-6)
+    _close(r_out, rr, tol, 1e-2)
+    _close(y, y_ref, tol * 2, 2e-2)
+
+
+def test_silu_and_mul():
+    x = torch.randn(19, 2 * 1408, device=DEV, dtype=torch.bfloat16)
+    _close(ops.silu_and_mul(x), ref.silu_and_mul(x.float()), 2e-2, 1e-2)
+
+
+@pytest.mark.parametrize("interleaved", [True, False])
+def test_rope(interleaved):
+    cs = ref.rope_cos_sin_cache(64, 512, 10000.0, {"type": "yarn", "factor": 40, "beta_fast": 32, "beta_slow": 1,
+                                                   "mscale": 0.707, "mscale_all_dim": 0.707,
+                                                   "original_max_position_embeddings": 4096}, DEV)
+    q = torch.randn(9, 16, 192, device=DEV, dtype=torch.bfloat16)
+    pos = torch.randint(0, 512, (9,), device=DEV)
+    expect = ref.apply_rope(q[..., 128:].float(), pos, cs, interleaved=interleaved)
+    ops.rope_(q[..., 128:], pos, cs, interleaved=interleaved)
+    _close(q[..., 128:], expect, 3e-2, 1e-2)
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(E=64, k=6, scoring="softmax", renormalize=False),
+    dict(E=128, k=8, scoring="softmax", renormalize=True),
+    dict(E=256, k=8, scoring="sigmoid", renormalize=True, n_group=8, topk_group=4, routed_scaling_factor=2.5),
+    dict(E=16, k=4, scoring="softmax", renormalize=False, n_group=4, topk_group=2),
+])
+def test_topk_route(cfg):
+    cfg = dict(cfg)
+    E, k = cfg.pop("E"), cfg.pop("k")
+    logits = torch.randn(200, E, device=DEV)
+    bias = torch.randn(E, device=DEV) * 0.1 if cfg["scoring"] == "sigmoid" else None
+    w, ids = ops.topk_route(logits, k, bias=bias, **cfg)
+    w_ref, ids_ref = ref.topk_route(logits.cpu(), k, bias=None if bias is None else bias.cpu(), **cfg)
+    assert torch.equal(ids.cpu(), ids_ref)
+    _close(w, w_ref, 1e-5, 1e-5)
+
+
+def _paged_cache(B, lens, width, bs=64, dtype=torch.bfloat16, extra_blocks=3):
+    nblk_seq = [math.ceil(n / bs) for n in lens]
+    total = sum(nblk_seq) + extra_blocks
+    cache = torch.randn(total, bs, width, device=DEV, dtype=dtype)
+    perm = torch.randperm(total - 1)[: sum(nblk_seq)] + 1
+    table = torch.zeros(B, max(nblk_seq), dtype=torch.int32)
+    o = 0
+    for b, nb in enumerate(nblk_seq):
+        table[b, :nb] = perm[o : o + nb].to(torch.int32)
+        o += nb
+    return cache, table.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV)
+
+
+@pytest.mark.parametrize("heads", [16, 32])
+@pytest.mark.parametrize("splits", [1, 0, 3])
+def test_mla_decode(heads, splits):
+    torch.manual_seed(heads + splits)
+    lens = [1, 31, 32, 33, 64, 200, 1029]
+    B = len(lens)
+    cache, table, seq = _paged_cache(B, lens, 576)
+    q = torch.randn(B, heads, 576, device=DEV, dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(192)
+    out = ops.mla_decode(q, cache, table, seq, scale, 512, num_splits=splits)
+    expect = ref.mla_decode(q.float(), cache.float(), table, seq, scale, 512)
+    _close(out, expect, 2e-2, 2e-2)
+
+
+def test_mla_cache_write():
+    T, L, R = 11, 512, 64
+    kv_a = torch.randn(T, L + R, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(L, device=DEV, dtype=torch.bfloat16)
+    cs = ref.rope_cos_sin_cache(R, 256, 10000.0, None, DEV)
+    pos = torch.randint(0, 256, (T,), device=DEV)
+    cache = torch.zeros(4, 64, L + R, device=DEV, dtype=torch.bfloat16)
+    slots = torch.randperm(256, device=DEV)[:T]
+    ops.mla_cache_write(cache, kv_a, w, 1e-6, pos, cs, slots, L)
+    flat = cache.view(-1, L + R)[slots]
+    _close(flat[:, :L], ref.rms_norm(kv_a[:, :L].float(), w.float(), 1e-6), 3e-2, 2e-2)
+    _close(flat[:, L:], ref.apply_rope(kv_a[:, None, L:].float(), pos, cs, interleaved=True)[:, 0], 3e-2, 2e-2)
+
+
+@pytest.mark.parametrize("shape", [(64, 6, 8, 256, 128), (300, 6, 64, 2048, 1408), (40, 8, 16, 512, 768),
+                                   (700, 2, 4, 256, 128)])
+def test_moe_experts_grouped_gemm(shape):
+    T, k, E, H, I = shape
+    torch.manual_seed(T)
+    x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, H, device=DEV, dtype=torch.bfloat16) * 0.05
+    w2 = torch.randn(E, H, I, device=DEV, dtype=torch.bfloat16) * 0.05
+    logits = torch.randn(T, E, device=DEV)
+    tw, tid = ref.topk_route(logits, k, renormalize=True)
+    out = ops.moe_experts(x, w13, w2, tw, tid)
+    expect = ref.moe_experts(x.float(), w13.float(), w2.float(), tw, tid)
+    scale = expect.abs().max().item()
+    _close(out / scale, expect / scale, 2e-2)
+
+
+def test_moe_expert_parallel_slice():
+    T, k, E, H, I = 50, 4, 16, 256, 128
+    x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, H, device=DEV, dtype=torch.bfloat16) * 0.05
+    w2 = torch.randn(E, H, I, device=DEV, dtype=torch.bfloat16) * 0.05
+    tw, tid = ref.topk_route(torch.randn(T, E, device=DEV), k)
+    full = ref.moe_experts(x.float(), w13.float(), w2.float(), tw, tid)
+    part = sum(ops.moe_experts(x, w13[o:o + 8], w2[o:o + 8], tw, tid, expert_offset=o).float() for o in (0, 8))
+    _close(part, full, 3e-2, 3e-2)
