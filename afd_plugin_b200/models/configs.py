@@ -361,7 +361,14 @@ TINY_DSV3 = DSV3_32L.scaled(
     quant=None,
 )
 
+# Tiny DeepSeek with the production MLA shapes (latent 512 + rope 64, 16
+# heads), so GPU tests exercise the specialised decode kernel.
+TINY_DSV2_MLA512 = TINY_DSV2.scaled(
+    kv_lora_rank=512, qk_rope_head_dim=64, qk_nope_head_dim=128, v_head_dim=128, num_attention_heads=16
+)
+
 PRESETS: dict[str, ModelArchConfig] = {
+    "tiny-dsv2-mla512": TINY_DSV2_MLA512,
     "tiny-dsv2": TINY_DSV2,
     "tiny-dsv3": TINY_DSV3,
     "tiny-qwen3-moe": TINY_QWEN3_MOE,

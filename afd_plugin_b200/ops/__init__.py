@@ -94,8 +94,23 @@ def mla_decode(
     num_splits: int = 0,
 ) -> torch.Tensor:
     if _cuda(q):
-        return _cuda_ops().mla_decode(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank, num_splits)
+        if q.shape[-1] == 576 and kv_lora_rank == 512 and q.shape[1] % 16 == 0:
+            return _cuda_ops().mla_decode(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank, num_splits)
+        # The kernel is specialised to DeepSeek's 512 + 64 latent; other
+        # (test-sized) shapes run the batched PyTorch form.
+        return _mla_decode_torch(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank)
     return ref.mla_decode(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank)
+
+
+def _mla_decode_torch(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank):
+    B, Hh, D = q.shape
+    bs = kv_cache.shape[1]
+    nblk = block_table.shape[1]
+    kv = kv_cache[block_table.long()].view(B, nblk * bs, D).float()
+    s = torch.einsum("bhd,bnd->bhn", q.float(), kv) * scale
+    mask = torch.arange(nblk * bs, device=q.device)[None, :] >= seq_lens.long()[:, None]
+    s = s.masked_fill(mask[:, None, :], float("-inf"))
+    return torch.einsum("bhn,bnd->bhd", torch.softmax(s, dim=-1), kv[..., :kv_lora_rank]).to(q.dtype)
 
 
 def gqa_decode(

@@ -150,12 +150,17 @@ def device_loop(engine, batch: int, warmup: int, steps: int, isl: int, osl: int)
     for _ in range(warmup):
         one()
     torch.cuda.synchronize()
+    nvtx = os.environ.get("AFD_BENCH_NVTX") == "1"
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    if nvtx:
+        torch.cuda.nvtx.range_push("timed")
     ev[0].record()
     for i in range(steps):
         one()
         ev[i + 1].record()
     torch.cuda.synchronize()
+    if nvtx:
+        torch.cuda.nvtx.range_pop()
     return [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)], ev[0].elapsed_time(ev[-1])
 
 
@@ -210,7 +215,8 @@ def main(argv=None) -> int:
             engine.capture_graphs()
         batch = len(engine.running)
         engine.load_decode_batch()
-        launches_per_step = count_our_kernels(lambda: one_eager_step(engine, batch))
+        launches_per_step = (0 if os.environ.get("AFD_BENCH_NO_COUNT") == "1"
+                             else count_our_kernels(lambda: one_eager_step(engine, batch)))
         with ClockSampler(local) as clk:
             per_step, total_ms = device_loop(engine, batch, args.warmup, args.steps, args.isl, args.osl)
             e2e = None
