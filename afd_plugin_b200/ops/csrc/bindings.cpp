@@ -267,6 +267,142 @@ void decode_advance(at::Tensor& input_ids, at::Tensor& positions, at::Tensor& sl
                         batch, (int)block_table.stride(0), (int)block_size, wrap_at, wrap_to, stream());
 }
 
+// ------------------------------------------------------- fused AFD transfer
+int64_t iptr(const at::Tensor& t) { return reinterpret_cast<int64_t>(t.data_ptr()); }
+
+void afd_epoch(at::Tensor& epoch) {
+  c10::cuda::CUDAGuard g(epoch.device());
+  launch_afd_epoch(reinterpret_cast<uint64_t*>(epoch.data_ptr()), stream());
+}
+
+void afd_wait(const at::Tensor& flag, int64_t index, const at::Tensor& epoch, int64_t arrivals, int64_t timeout_ns) {
+  c10::cuda::CUDAGuard g(flag.device());
+  launch_afd_wait(reinterpret_cast<const uint64_t*>(flag.data_ptr()) + index,
+                  reinterpret_cast<const uint64_t*>(epoch.data_ptr()), (uint64_t)arrivals, timeout_ns,
+                  status_ptr(flag), stream());
+}
+
+// cfg (int64): [E, k, scoring, renorm, n_group, topk_group, moe, has_shared, num_ffn, e_local, cap, t_cap,
+//               src_local, home_f, attn_rank, layer]
+void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Tensor& norm_w, double eps,
+                  const at::Tensor& gate_w, const c10::optional<at::Tensor>& gate_bias, double scale,
+                  const at::Tensor& ptrs, at::Tensor& done_ctr, std::vector<int64_t> cfg) {
+  check_cuda(attn_out, "attn_out");
+  TORCH_CHECK(attn_out.scalar_type() == at::kBFloat16 && residual.scalar_type() == at::kBFloat16,
+              "afd_dispatch: bf16 activations");
+  TORCH_CHECK(attn_out.is_contiguous() && residual.is_contiguous() && gate_w.is_contiguous(), "afd_dispatch: layout");
+  TORCH_CHECK(cfg.size() == 16, "afd_dispatch: cfg has 16 entries");
+  TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.dim() == 2 && ptrs.size(0) == 5, "afd_dispatch: ptrs [5, F]");
+  DispatchParams p{};
+  p.attn_out = attn_out.data_ptr();
+  p.residual = residual.data_ptr();
+  p.norm_w = norm_w.data_ptr();
+  p.eps = (float)eps;
+  p.gate_w = gate_w.data_ptr();
+  at::Tensor gb;
+  if (gate_bias.has_value() && gate_bias->defined()) {
+    gb = gate_bias->to(at::kFloat).contiguous();
+    p.gate_bias = gb.data_ptr<float>();
+  }
+  p.E = (int)cfg[0];
+  p.k = (int)cfg[1];
+  p.scoring = (int)cfg[2];
+  p.renorm = cfg[3] != 0;
+  p.n_group = (int)cfg[4];
+  p.topk_group = (int)cfg[5];
+  p.scale = (float)scale;
+  p.T = (int)attn_out.size(0);
+  p.H = (int)attn_out.size(1);
+  p.moe = (int)cfg[6];
+  p.has_shared = (int)cfg[7];
+  p.num_ffn = (int)cfg[8];
+  p.e_local = (int)cfg[9];
+  p.cap = (int)cfg[10];
+  p.t_cap = (int)cfg[11];
+  p.src_local = (int)cfg[12];
+  p.home_f = (int)cfg[13];
+  p.attn_rank = (int)cfg[14];
+  p.layer = (int)cfg[15];
+  TORCH_CHECK(p.k <= 16 && p.H % 8 == 0 && p.T <= p.t_cap, "afd_dispatch: k <= 16, H % 8 == 0, T <= t_cap");
+  const int64_t* pt = ptrs.data_ptr<int64_t>();
+  const int64_t F = ptrs.size(1);
+  p.x_ptrs = pt;
+  p.meta_ptrs = pt + F;
+  p.w_ptrs = pt + 2 * F;
+  p.cnt_ptrs = pt + 3 * F;
+  p.flag_ptrs = pt + 4 * F;
+  p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  p.status = status_ptr(attn_out);
+  c10::cuda::CUDAGuard g(attn_out.device());
+  launch_afd_dispatch(p, stream());
+}
+
+at::Tensor afd_combine(const at::Tensor& comb, int64_t T, int64_t n_routed, int64_t shared_slot, const at::Tensor& flags,
+                       int64_t layer, const at::Tensor& epoch, int64_t arrivals, int64_t timeout_ns) {
+  check_cuda(comb, "comb");
+  TORCH_CHECK(comb.dim() == 3 && comb.is_contiguous() && comb.scalar_type() == at::kBFloat16, "afd_combine: comb");
+  auto out = at::empty({T, comb.size(2)}, comb.options());
+  CombineParams p{};
+  p.out = out.data_ptr();
+  p.comb = comb.data_ptr();
+  p.T = (int)T;
+  p.H = (int)comb.size(2);
+  p.J = (int)comb.size(1);
+  p.n_routed = (int)n_routed;
+  p.shared_slot = (int)shared_slot;
+  p.flag = reinterpret_cast<const uint64_t*>(flags.data_ptr());
+  p.layer = (int)layer;
+  p.epoch = reinterpret_cast<const uint64_t*>(epoch.data_ptr());
+  p.arrivals = (uint64_t)arrivals;
+  p.timeout_ns = timeout_ns;
+  p.status = status_ptr(comb);
+  c10::cuda::CUDAGuard g(comb.device());
+  launch_afd_combine(p, stream());
+  return out;
+}
+
+// Grouped GEMM whose epilogue scatters rows into peer combine buffers.
+// sp_ptrs (int64 [4]): meta, rw, dst_ptr_table, flag_ptr_table; sp_cfg: [J, H, total_ctas, num_dst, layer, n_reset]
+void grouped_gemm_scatter(const at::Tensor& a, const at::Tensor& w, const at::Tensor& offsets, const at::Tensor& counts,
+                          int64_t w_experts, const at::Tensor& meta, const at::Tensor& rw, const at::Tensor& dst_ptrs,
+                          const at::Tensor& flag_ptrs, at::Tensor& done_ctr, at::Tensor& counts_reset,
+                          std::vector<int64_t> cfg) {
+  check_cuda(a, "a");
+  TORCH_CHECK(cfg.size() == 5, "grouped_gemm_scatter: cfg [J, H, total_ctas, num_dst, layer]");
+  const int64_t R = a.size(0), K = a.size(1), N = w.size(1);
+  TORCH_CHECK(N % 128 == 0 && K % 64 == 0 && w.size(2) == K, "grouped_gemm_scatter: shapes");
+  ScatterParams sp{};
+  sp.meta = meta.data_ptr<int32_t>();
+  sp.rw = rw.data_ptr<float>();
+  sp.dst_ptrs = dst_ptrs.data_ptr<int64_t>();
+  sp.J = (int)cfg[0];
+  sp.H = (int)cfg[1];
+  sp.total_ctas = (int)cfg[2];
+  sp.num_dst = (int)cfg[3];
+  sp.layer = (int)cfg[4];
+  sp.flag_ptrs = flag_ptrs.data_ptr<int64_t>();
+  sp.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  sp.counts_reset = counts_reset.data_ptr<int32_t>();
+  sp.n_reset = (int)counts_reset.numel();
+  c10::cuda::CUDAGuard g(a.device());
+  launch_grouped_gemm(nullptr, a.data_ptr(), w.data_ptr(), offsets.data_ptr<int32_t>(), counts.data_ptr<int32_t>(),
+                      (int)counts.numel(), (int)R, (int)N, (int)K, 2, status_ptr(a), stream(), (int)w_experts, &sp);
+}
+
+at::Tensor grouped_gemm_ex(const at::Tensor& a, const at::Tensor& w, const at::Tensor& offsets,
+                           const at::Tensor& counts, int64_t epilogue, int64_t w_experts) {
+  check_cuda(a, "a");
+  const int64_t R = a.size(0), K = a.size(1), N = w.size(-2);
+  const int64_t n_out = epilogue == 1 ? N / 2 : N;
+  TORCH_CHECK(K % 64 == 0 && w.size(-1) == K, "grouped_gemm_ex: K");
+  auto d = at::empty({R, n_out}, a.options());
+  c10::cuda::CUDAGuard g(a.device());
+  launch_grouped_gemm(d.data_ptr(), a.data_ptr(), w.data_ptr(), offsets.data_ptr<int32_t>(),
+                      counts.data_ptr<int32_t>(), (int)counts.numel(), (int)R, (int)N, (int)K, (int)epilogue,
+                      status_ptr(a), stream(), (int)w_experts, nullptr);
+  return d;
+}
+
 // ------------------------------------------------------------------ status
 int64_t read_status(int64_t device) { return status_tensor((int)device).item<int>(); }
 void reset_status(int64_t device) { status_tensor((int)device).zero_(); }
@@ -292,6 +428,15 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("moe_combine(Tensor ys, Tensor topk_w, Tensor token_slot_row, Tensor? shared) -> Tensor");
   m.def("decode_advance(Tensor(a!) input_ids, Tensor(b!) positions, Tensor(c!) slots, Tensor(d!) seq_lens, "
         "Tensor next_tokens, Tensor block_table, int block_size, int wrap_at, int wrap_to) -> ()");
+  m.def("afd_epoch(Tensor(a!) epoch) -> ()");
+  m.def("afd_wait(Tensor flag, int index, Tensor epoch, int arrivals, int timeout_ns) -> ()");
+  m.def("afd_dispatch(Tensor attn_out, Tensor(a!) residual, Tensor norm_w, float eps, Tensor gate_w, Tensor? gate_bias, "
+        "float scale, Tensor ptrs, Tensor(b!) done_ctr, int[] cfg) -> ()");
+  m.def("afd_combine(Tensor comb, int T, int n_routed, int shared_slot, Tensor flags, int layer, Tensor epoch, "
+        "int arrivals, int timeout_ns) -> Tensor");
+  m.def("grouped_gemm_scatter(Tensor a, Tensor w, Tensor offsets, Tensor counts, int w_experts, Tensor meta, Tensor rw, "
+        "Tensor dst_ptrs, Tensor flag_ptrs, Tensor(a!) done_ctr, Tensor(b!) counts_reset, int[] cfg) -> ()");
+  m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
   m.def("read_status(int device) -> int");
   m.def("reset_status(int device) -> ()");
   m.def("status_word(int device) -> Tensor");
@@ -311,6 +456,12 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("grouped_gemm", &grouped_gemm);
   m.impl("moe_combine", &moe_combine);
   m.impl("decode_advance", &decode_advance);
+  m.impl("afd_epoch", &afd_epoch);
+  m.impl("afd_wait", &afd_wait);
+  m.impl("afd_dispatch", &afd_dispatch);
+  m.impl("afd_combine", &afd_combine);
+  m.impl("grouped_gemm_scatter", &grouped_gemm_scatter);
+  m.impl("grouped_gemm_ex", &grouped_gemm_ex);
 }
 
 TORCH_LIBRARY_IMPL(afd_b200, CompositeExplicitAutograd, m) {

@@ -3,6 +3,7 @@
 // computes in fp32.
 #include "common.cuh"
 #include "launchers.h"
+#include "routing.cuh"
 
 namespace afd {
 
@@ -134,126 +135,19 @@ __global__ void rope_kernel(T* __restrict__ x, const int64_t* __restrict__ pos, 
 }
 
 // ============================================================ routing top-k
-// One warp per token; experts E <= 32*kMaxPerLane.  Selection ties break toward
-// the lower expert id.  scoring: 0 softmax, 1 sigmoid(+bias).
-constexpr int kMaxPerLane = 16;
-
+// One warp per token (see routing.cuh for the selection rules).
 __global__ void topk_route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
                                   float* __restrict__ out_w, int32_t* __restrict__ out_id, int tokens, int E, int k,
                                   int scoring, bool renorm, int n_group, int topk_group, float scale) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (warp >= tokens) return;
-  const float* row = logits + (size_t)warp * E;
-  float score[kMaxPerLane], sel[kMaxPerLane];
-  // expert of slot j on this lane: e = j*32 + lane
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < kMaxPerLane; ++j) {
-    const int e = j * 32 + lane;
-    score[j] = (e < E) ? row[e] : -INFINITY;
-    mx = fmaxf(mx, score[j]);
-  }
-  if (scoring == 0) {
-    mx = warp_max(mx);
-    float sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
-      const int e = j * 32 + lane;
-      score[j] = (e < E) ? __expf(score[j] - mx) : 0.f;
-      sum += score[j];
-    }
-    sum = warp_sum(sum);
-    const float inv = 1.f / sum;
-#pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
-      score[j] *= inv;
-      sel[j] = (j * 32 + lane < E) ? score[j] : -INFINITY;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
-      const int e = j * 32 + lane;
-      score[j] = (e < E) ? 1.f / (1.f + __expf(-score[j])) : 0.f;
-      sel[j] = (e < E) ? score[j] + (bias ? bias[e] : 0.f) : -INFINITY;
-    }
-  }
-  if (n_group > 1 && topk_group < n_group) {
-    const int gsize = E / n_group;
-    // group score per group (computed redundantly by all lanes via shuffles)
-    uint32_t keep_mask = 0;  // bit g set -> group g kept (n_group <= 32)
-    float gscore_mine = -INFINITY;  // lane g holds group g's score
-    for (int g = 0; g < n_group; ++g) {
-      float m1 = -INFINITY, m2 = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < kMaxPerLane; ++j) {
-        const int e = j * 32 + lane;
-        if (e < E && e / gsize == g) {
-          const float v = sel[j];
-          if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
-        }
-      }
-      // warp-wide top-2 of (m1, m2)
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float a1 = __shfl_xor_sync(0xffffffffu, m1, o);
-        const float a2 = __shfl_xor_sync(0xffffffffu, m2, o);
-        float n1 = fmaxf(m1, a1);
-        float n2 = fmaxf(fminf(m1, a1), fmaxf(m2, a2));
-        m1 = n1;
-        m2 = n2;
-      }
-      const float gs = (scoring == 1) ? m1 + m2 : m1;
-      if (lane == g) gscore_mine = gs;
-    }
-    for (int r = 0; r < topk_group; ++r) {
-      float v = gscore_mine;
-      int idx = (lane < n_group && !((keep_mask >> lane) & 1u)) ? lane : 1 << 20;
-      if (idx == (1 << 20)) v = -INFINITY;
-      warp_argmax(v, idx);
-      keep_mask |= 1u << idx;
-    }
-#pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
-      const int e = j * 32 + lane;
-      if (e < E && !((keep_mask >> (e / gsize)) & 1u)) sel[j] = -INFINITY;
-    }
-  }
-  float wsum = 0.f;
-  float my_w = 0.f;
-  int my_id = 0;
-  for (int r = 0; r < k; ++r) {
-    float v = -INFINITY;
-    int idx = 1 << 20;
-#pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
-      const int e = j * 32 + lane;
-      if (e < E && (sel[j] > v || (sel[j] == v && e < idx))) {
-        v = sel[j];
-        idx = e;
-      }
-    }
-    warp_argmax(v, idx);
-    // owner lane removes the winner and publishes its score
-    float wv = 0.f;
-#pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
-      if (j * 32 + lane == idx) {
-        wv = score[j];
-        sel[j] = -INFINITY;
-      }
-    }
-    wv = warp_sum(wv);
-    wsum += wv;
-    if (lane == r) {
-      my_w = wv;
-      my_id = idx;
-    }
-  }
+  float w;
+  int id;
+  warp_route(logits + (size_t)warp * E, bias, E, k, scoring, renorm, n_group, topk_group, scale, w, id);
   if (lane < k) {
-    float w = renorm ? my_w / wsum : my_w;
-    out_w[(size_t)warp * k + lane] = w * scale;
-    out_id[(size_t)warp * k + lane] = my_id;
+    out_w[(size_t)warp * k + lane] = w;
+    out_id[(size_t)warp * k + lane] = id;
   }
 }
 

@@ -20,6 +20,8 @@
 // winds down (TMEM is always released).
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "launchers.h"
 
@@ -94,14 +96,39 @@ AFD_DEVICE void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+AFD_DEVICE uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Scatter epilogue bookkeeping: every CTA of the layer arrives once; the last
+// one clears the local expert counters and signals every Attention rank.
+AFD_DEVICE void scatter_arrive(const ScatterParams& sp) {
+  __threadfence_system();
+  if (atomicAdd(sp.done_ctr, 1u) == (unsigned)sp.total_ctas - 1) {
+    for (int i = 0; i < sp.n_reset; ++i) sp.counts_reset[i] = 0;
+    *sp.done_ctr = 0u;
+    __threadfence_system();
+    for (int a = 0; a < sp.num_dst; ++a)
+      asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(reinterpret_cast<uint64_t*>(sp.flag_ptrs[a]) +
+                                                                     sp.layer),
+                   "l"(1ull)
+                   : "memory");
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap a_map,
     __nv_bfloat16* __restrict__ d, const int32_t* __restrict__ offsets, const int32_t* __restrict__ counts, int n_w,
-    int k_dim, int ld_d, int* __restrict__ status) {
+    int w_stride_rows, int k_dim, int ld_d, int* __restrict__ status, const ScatterParams sp) {
   const int e = blockIdx.y;
   const int cnt = counts[e];
-  if (cnt == 0) return;
+  if (cnt == 0) {
+    if (EPI == 2 && threadIdx.x == 0) scatter_arrive(sp);
+    return;
+  }
   const int seg = offsets[e];
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -114,10 +141,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   int w_row0, w_row1;
   if (EPI == 1) {
     const int inter = n_w / 2;
-    w_row0 = e * n_w + nt * 64;
-    w_row1 = e * n_w + inter + nt * 64;
+    w_row0 = e * w_stride_rows + nt * 64;
+    w_row1 = e * w_stride_rows + inter + nt * 64;
   } else {
-    w_row0 = e * n_w + nt * kBM;
+    w_row0 = e * w_stride_rows + nt * kBM;
     w_row1 = w_row0 + 64;
   }
 
@@ -219,6 +246,19 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (c0 + j < n_cols) d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(v[j]);
+        } else if (EPI == 2) {
+          // routing weight applied, row stored into the source rank's slot (peer memory)
+          const int col = nt * kBM + row;
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            if (c0 + j < n_cols) {
+              const int r = r_base + c0 + j;
+              const int m = sp.meta[r];
+              const int src = (m >> 24) & 0xFF, tok = (m >> 8) & 0xFFFF, slot = m & 0xFF;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sp.dst_ptrs[src]);
+              dst[((size_t)tok * sp.J + slot) * sp.H + col] = __float2bfloat16_rn(sp.rw[r] * v[j]);
+            }
+          }
         } else {
           if (quarter >= 2) {
 #pragma unroll
@@ -241,6 +281,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       }
       tc_fence_before();
       if (lane == 0) mbar_arrive(&sm.acc_empty);
+    }
+    if (EPI == 2) {
+      __threadfence_system();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0) scatter_arrive(sp);
     }
   }
   tc_fence_before();
@@ -268,28 +313,30 @@ using namespace afd;
 
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,
                          const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
-                         int* status, cudaStream_t s) {
+                         int* status, cudaStream_t s, int w_experts, const ScatterParams* sp) {
+  if (w_experts < 0) w_experts = e_local;
   CUtensorMap wmap, amap;
-  gg::encode_2d(&wmap, w, (uint64_t)e_local * n, k, 64);
+  gg::encode_2d(&wmap, w, (uint64_t)w_experts * n, k, 64);
   gg::encode_2d(&amap, a, rows_cap, k, gg::kSub);
   const int smem = (int)sizeof(gg::Smem) + 1024;
+  const int w_stride = (w_experts == 1) ? 0 : n;
+  ScatterParams none{};
+  const ScatterParams& spv = sp ? *sp : none;
+  auto go = [&](auto epi_tag, dim3 grid, int ld) {
+    constexpr int EPI = decltype(epi_tag)::value;
+    static bool set = false;
+    if (!set) {
+      cudaFuncSetAttribute(gg::grouped_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      set = true;
+    }
+    gg::grouped_gemm_kernel<EPI><<<grid, gg::kThreads, smem, s>>>(wmap, amap, (__nv_bfloat16*)d, expert_offsets,
+                                                                    expert_counts, n, w_stride, k, ld, status, spv);
+  };
   if (epilogue == 1) {
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(gg::grouped_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      set = true;
-    }
-    dim3 grid((n / 2) / 64, e_local);
-    gg::grouped_gemm_kernel<1><<<grid, gg::kThreads, smem, s>>>(wmap, amap, (__nv_bfloat16*)d, expert_offsets,
-                                                                  expert_counts, n, k, n / 2, status);
+    go(std::integral_constant<int, 1>{}, dim3((n / 2) / 64, e_local), n / 2);
+  } else if (epilogue == 2) {
+    go(std::integral_constant<int, 2>{}, dim3(n / gg::kBM, e_local), n);
   } else {
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(gg::grouped_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      set = true;
-    }
-    dim3 grid(n / gg::kBM, e_local);
-    gg::grouped_gemm_kernel<0><<<grid, gg::kThreads, smem, s>>>(wmap, amap, (__nv_bfloat16*)d, expert_offsets,
-                                                                  expert_counts, n, k, n, status);
+    go(std::integral_constant<int, 0>{}, dim3(n / gg::kBM, e_local), n);
   }
 }

@@ -52,10 +52,67 @@ void launch_moe_gather(void* xs, const void* x, const int32_t* row_token, int ro
 void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* token_slot_row, int tokens,
                         int k, int hidden, const void* shared_out, int dtype, cudaStream_t s);
 
+// ---- afd_fused.cu
+struct DispatchParams {
+  const void* attn_out;   // [T, H] bf16
+  void* residual;         // [T, H] bf16, updated in place
+  const void* norm_w;     // [H] bf16 (post-attention RMSNorm)
+  float eps;
+  const void* gate_w;     // [E, H] bf16
+  const float* gate_bias; // [E] or null
+  int E, k, scoring, n_group, topk_group;
+  bool renorm;
+  float scale;
+  int T, H;
+  int moe;         // route to experts (0 for dense layers)
+  int has_shared;  // also send to the home FFN rank's shared/dense segment
+  int num_ffn, e_local, cap, t_cap, src_local, home_f, attn_rank, layer;
+  const int64_t* x_ptrs;     // [F] receive rows (stage base) on each FFN rank
+  const int64_t* meta_ptrs;  // [F] int32 row metadata
+  const int64_t* w_ptrs;     // [F] fp32 row routing weights
+  const int64_t* cnt_ptrs;   // [F] int32 counters [e_local + ratio]
+  const int64_t* flag_ptrs;  // [F] uint64 arrival counters [layers]
+  unsigned* done_ctr;        // local CTA-completion counter
+  int* status;
+};
+struct CombineParams {
+  void* out;          // [T, H] bf16
+  const void* comb;   // [T_cap, J, H] bf16 (stage base, local)
+  int T, H, J, n_routed, shared_slot;
+  const uint64_t* flag;  // [layers] (stage base, local)
+  int layer;
+  const uint64_t* epoch;
+  uint64_t arrivals;
+  int64_t timeout_ns;
+  int* status;
+};
+void launch_afd_epoch(uint64_t* epoch, cudaStream_t s);
+void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns, int* status,
+                     cudaStream_t s);
+void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s);
+void launch_afd_combine(const CombineParams& p, cudaStream_t s);
+
 // ---- gemm_tcgen05.cu
+// Epilogue 2 ("scatter") stores routing-weighted rows straight into the
+// originating Attention ranks' combine buffers and signals them when the last
+// CTA of the layer is done.
+struct ScatterParams {
+  const int32_t* meta;      // [rows] (src << 24 | token << 8 | slot)
+  const float* rw;          // [rows] routing weight
+  const int64_t* dst_ptrs;  // [A] combine buffer (stage base) on each Attention rank
+  int J, H;                 // slots per token, hidden size
+  unsigned* done_ctr;       // local, counts CTAs of the layer's scatter launches
+  int total_ctas;           // CTAs across all scatter launches of the layer
+  const int64_t* flag_ptrs; // [A] uint64 combine counters (stage base)
+  int num_dst, layer;
+  int32_t* counts_reset;    // local counters cleared before signalling
+  int n_reset;
+};
 // Grouped GEMM D[r, n] = sum_k A[r, k] * W[e(r), n, k] over row segments of
 // experts (rows of expert e: [offsets[e], offsets[e] + counts[e])).
 // epilogue: 0 = store bf16, 1 = SiLU(gate) * up over paired halves (N = 2I -> I).
+// w_expert_rows: rows between consecutive experts in W (0 = one weight set
+// shared by every segment, e.g. shared experts / dense MLP over per-source segments).
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,
                          const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
-                         int* status, cudaStream_t s);
+                         int* status, cudaStream_t s, int w_experts = -1, const ScatterParams* sp = nullptr);
