@@ -1,0 +1,462 @@
+"""B200 fused AFD connector: dispatch and combine inside the kernels, over NVLink.
+
+Data path (no library call, no host hop):
+
+* Attention rank, per layer and ubatch -- ``afd_dispatch``: residual add +
+  post-attention RMSNorm + router GEMV + top-k, then each routed copy of the
+  token is stored straight into the owning FFN rank's per-expert receive
+  segment (slot claimed with a system-scope atomic on that rank's counter),
+  plus one copy into the home FFN rank's shared-expert / dense segment.  The
+  last CTA bumps every FFN rank's arrival counter.
+* FFN rank -- ``afd_wait`` for all Attention ranks, tcgen05 grouped
+  ``gate_up`` GEMM (SwiGLU fused) over the receive segments, then the grouped
+  ``down`` GEMM whose epilogue multiplies by the routing weight and stores the
+  row into the originating Attention rank's combine slot (peer memory); the
+  last CTA bumps every Attention rank's combine counter.
+* Attention rank -- ``afd_combine`` waits for every FFN rank and sums each
+  token's slots.
+
+Routing always runs on the Attention side here (the Attention role loads the
+MoE gate), so expert parallelism across FFN ranks needs no FFN-side
+all-to-all; with several FFN ranks each holds ``E / F`` routed experts and a
+replica of the shared experts / dense MLPs.
+
+The control plane (per-step payload Attention -> FFN over gloo) only tells the
+FFN host loop to replay its captured step; token counts stay on the device, so
+one FFN graph serves every routing (key: stages and capacity).
+
+Counters only grow and are compared with ``epoch * arrivals`` (a per-step
+device epoch bumped inside every captured step), so graphs replay without
+resets.  Every wait is bounded (``wait_timeout_ms``) and reports through the
+device status word instead of hanging.
+
+Semantics follow the reference connector contract
+(``afd_plugin/connectors/base.py:37-307``); the transfer mechanism follows the
+shape of the reference's Ascend ``a2e``/``e2a`` kernels (device-initiated
+peer copies with epoch-tagged flags, ``csrc/npu/a2e/op_kernel/a2e.h:26-382``)
+re-designed for NVLink: push instead of pull, per-expert slots, and the FFN
+GEMM epilogue as the sender.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Mapping
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from afd_plugin_b200.config import AFDConfig
+from afd_plugin_b200.config_utils import coerce_extra_bool, coerce_extra_positive_int
+from afd_plugin_b200.connectors.base import AFDConnectorBase, ConnectorExtraInfo
+from afd_plugin_b200.connectors.metadata import AFDA2FTransferPayload, AFDTransferContext
+from afd_plugin_b200.connectors.p2p_nccl import P2pNcclAFDControlPlane
+from afd_plugin_b200.parallel.symm_heap import HeapLayout
+from afd_plugin_b200.parallel.topology import build_rank_mapping
+from afd_plugin_b200.runtime.ffn_executor import FFNExecutor
+
+_EXTRA_KEYS = {"max_tokens_per_rank", "wait_timeout_ms", "fp8_dispatch"}
+
+
+@dataclass(frozen=True)
+class B200FusedExtraInfo(ConnectorExtraInfo):
+    max_tokens_per_rank: int | None = None  # per Attention rank and ubatch; default: max_num_seqs
+    wait_timeout_ms: int = 5000
+    fp8_dispatch: bool = False
+
+    @classmethod
+    def from_mapping(cls, raw: Mapping[str, Any] | None) -> "B200FusedExtraInfo":
+        raw = dict(raw or {})
+        unknown = set(raw) - _EXTRA_KEYS
+        if unknown:
+            raise ValueError(f"B200FusedAFDConnector: unknown connector_extra_config keys {sorted(unknown)}")
+        out = cls(
+            max_tokens_per_rank=(coerce_extra_positive_int(raw["max_tokens_per_rank"], field_name="max_tokens_per_rank")
+                                 if "max_tokens_per_rank" in raw else None),
+            wait_timeout_ms=coerce_extra_positive_int(raw.get("wait_timeout_ms", 5000), field_name="wait_timeout_ms"),
+            fp8_dispatch=coerce_extra_bool(raw.get("fp8_dispatch", False), field_name="fp8_dispatch"),
+        )
+        if out.fp8_dispatch:
+            raise ValueError("B200FusedAFDConnector: fp8_dispatch is not available yet (bf16 rows are sent)")
+        return out
+
+    def to_mapping(self) -> dict[str, Any]:
+        return {"max_tokens_per_rank": self.max_tokens_per_rank, "wait_timeout_ms": self.wait_timeout_ms,
+                "fp8_dispatch": self.fp8_dispatch}
+
+
+@dataclass(frozen=True)
+class FusedLayout:
+    """Dimensions shared by every rank (pure arithmetic, CPU-testable)."""
+
+    num_attn: int
+    num_ffn: int
+    stages: int
+    layers: int
+    hidden: int
+    experts: int
+    top_k: int
+    t_cap: int  # tokens per Attention rank per stage
+
+    @property
+    def ratio(self) -> int:
+        return self.num_attn // self.num_ffn
+
+    @property
+    def e_local(self) -> int:
+        return self.experts // self.num_ffn
+
+    @property
+    def cap(self) -> int:
+        """Receive rows per routed expert (every token of every Attention rank)."""
+        return self.num_attn * self.t_cap
+
+    @property
+    def shared_row0(self) -> int:
+        return self.e_local * self.cap
+
+    @property
+    def rows(self) -> int:
+        return self.e_local * self.cap + self.ratio * self.t_cap
+
+    @property
+    def slots(self) -> int:
+        """Combine slots per token: top-k routed + one shared/dense."""
+        return self.top_k + 1
+
+    def heap_layout(self) -> HeapLayout:
+        L = HeapLayout()
+        S = self.stages
+        L.add("x_recv", (S, self.rows, self.hidden), torch.bfloat16)
+        L.add("meta", (S, self.rows), torch.int32)
+        L.add("rw", (S, self.rows), torch.float32)
+        L.add("counts", (S, self.e_local + self.ratio), torch.int32)
+        L.add("arrive", (S, self.layers), torch.int64)
+        L.add("comb", (S, self.t_cap, self.slots, self.hidden), torch.bfloat16)
+        L.add("comb_flag", (S, self.layers), torch.int64)
+        L.add("epoch", (1,), torch.int64)
+        L.add("done", (S, 2), torch.int32)
+        return L
+
+    def stage_bytes(self, layout: HeapLayout, name: str) -> int:
+        reg = layout[name]
+        return reg.nbytes // self.stages
+
+
+class B200FusedAFDConnector(AFDConnectorBase):
+    supports_graph_capture = True
+
+    @classmethod
+    def parse_extra_config(cls, raw: Mapping[str, Any] | None) -> ConnectorExtraInfo:
+        if raw is not None and not isinstance(raw, Mapping):
+            raise TypeError("B200FusedAFDConnector connector_extra_config must be a mapping")
+        return B200FusedExtraInfo.from_mapping(raw)
+
+    def __init__(self, rank: int, local_rank: int, engine_config: Any, afd_config: AFDConfig, role_rank: int) -> None:
+        super().__init__(rank, local_rank, engine_config, afd_config, role_rank)
+        self.mapping = build_rank_mapping(afd_config, role_rank)
+        self.world_rank = self.mapping.world_rank
+        self.attn_size = self.mapping.attention_size
+        self.ffn_size = self.mapping.ffn_size
+        self.min_size = self.mapping.min_size
+        self.ratio = self.mapping.ratio
+        self.dst_list = list(self.mapping.dp_metadata_destinations)
+        self.p2p_rank = self.mapping.p2p_rank
+        arch = engine_config.model_config.hf_config
+        self.arch = arch
+        par = engine_config.parallel_config
+        stages = 2 if getattr(par, "use_ubatching", False) else 1
+        t_cap = self.extra_info.max_tokens_per_rank or engine_config.max_num_seqs
+        if stages == 2:
+            t_cap = (t_cap + 1) // 2
+        if arch.n_routed_experts and arch.n_routed_experts % self.ffn_size:
+            raise ValueError(f"{arch.n_routed_experts} experts do not split over {self.ffn_size} FFN ranks")
+        self.dims = FusedLayout(
+            num_attn=self.attn_size, num_ffn=self.ffn_size, stages=stages, layers=arch.num_hidden_layers,
+            hidden=arch.hidden_size, experts=max(arch.n_routed_experts, self.ffn_size),
+            top_k=max(arch.num_experts_per_tok, 1), t_cap=t_cap)
+        self.timeout_ns = int(self.extra_info.wait_timeout_ms) * 1_000_000
+        self.heap = None
+        self.control_group = None
+        self._initialized = False
+        # P2P control plane semantics (payload per step, first min(A,F) Attention ranks send).
+        self.control_plane = P2pNcclAFDControlPlane(self)
+        self.dp_metadata_list: dict = {}
+        self.tensor_metadata_list: dict = {}
+        self._peer_specs: dict = {}
+        self._recv_buffers: dict = {}
+        self._ids_buffers: dict = {}
+        self.group_size = len(self.mapping.subgroup_ranks)
+        self.hidden_size = arch.hidden_size
+        self.dtype = engine_config.model_config.dtype
+        self.device = torch.device("cuda", local_rank)
+
+    # --------------------------------------------------------- lifecycle
+    def init_afd_connector(self) -> None:
+        if self._initialized:
+            return
+        from afd_plugin_b200.parallel.symm_heap import SymmetricHeap
+
+        if not dist.is_initialized() or dist.get_world_size() != self.attn_size + self.ffn_size:
+            raise RuntimeError("B200FusedAFDConnector needs the AFD world initialised with A + F ranks")
+        if dist.get_rank() != self.world_rank:
+            raise RuntimeError(f"process has world rank {dist.get_rank()}, AFD topology expects {self.world_rank}")
+        group = dist.new_group(list(range(self.ffn_size + self.min_size)), backend="gloo")
+        self.control_group = group if self.mapping.participates_in_dp_metadata_group else None
+        self.layout = self.dims.heap_layout()
+        self.heap = SymmetricHeap(self.layout, device=self.local_rank)
+        self._build_views()
+        self._initialized = True
+
+    def _build_views(self) -> None:
+        d, h = self.dims, self.heap
+        self.x_recv = h.view("x_recv")
+        self.meta = h.view("meta")
+        self.rw = h.view("rw")
+        self.counts = h.view("counts")
+        self.arrive = h.view("arrive")
+        self.comb = h.view("comb")
+        self.comb_flag = h.view("comb_flag")
+        self.epoch = h.view("epoch")
+        self.done = h.view("done")
+        F, A = d.num_ffn, d.num_attn
+        ffn_world = list(range(F))
+        attn_world = list(range(F, F + A))
+        sb = lambda name: d.stage_bytes(self.layout, name)  # noqa: E731
+        # Attention side: [5, F] per stage -> x, meta, rw, counts, arrive on each FFN rank.
+        self.dispatch_ptrs = []
+        self.scatter_dst = []
+        self.scatter_flags = []
+        for s in range(d.stages):
+            rows = [h.ptr_table(ffn_world, n, s * sb(n)) for n in ("x_recv", "meta", "rw", "counts", "arrive")]
+            self.dispatch_ptrs.append(torch.stack(rows))
+            self.scatter_dst.append(h.ptr_table(attn_world, "comb", s * sb("comb")))
+            self.scatter_flags.append(h.ptr_table(attn_world, "comb_flag", s * sb("comb_flag")))
+
+    def close(self) -> None:
+        if self.heap is not None:
+            self.heap.close()
+        self.heap = None
+        self.control_group = None
+        self._initialized = False
+
+    @property
+    def is_initialized(self) -> bool:
+        return self._initialized
+
+    def flush(self) -> None:
+        return None
+
+    def read_status(self) -> int:
+        return int(torch.ops.afd_b200.read_status(self.local_rank))
+
+    # ---------------------------------------------- role-specific engines
+    def make_executor(self, model) -> "FusedAttentionExecutor":
+        return FusedAttentionExecutor(model, self)
+
+    def make_ffn_runner(self, model) -> "FusedFFNRunner":
+        return FusedFFNRunner(model, self, self.engine_config)
+
+    # ------------------------------------------- reference data-path API
+    def send_attn_output(self, hidden_states: torch.Tensor, context: AFDTransferContext, **kwargs: Any) -> None:
+        raise NotImplementedError(
+            "B200FusedAFDConnector sends from the fused dispatch kernel; use make_executor(model)")
+
+    def recv_ffn_output(self, ref_tensor: torch.Tensor, ubatch_idx: int = 0, **kwargs: Any) -> torch.Tensor:
+        raise NotImplementedError("B200FusedAFDConnector combines in afd_combine; use make_executor(model)")
+
+    def recv_attn_output(self, ubatch_idx: int = 0, **kwargs: Any) -> AFDA2FTransferPayload:
+        raise NotImplementedError("B200FusedAFDConnector FFN side is driven by make_ffn_runner(model)")
+
+    def send_ffn_output(self, ffn_output: torch.Tensor, context: AFDTransferContext, **kwargs: Any) -> None:
+        raise NotImplementedError("B200FusedAFDConnector FFN side is driven by make_ffn_runner(model)")
+
+
+def _routing_cfg(arch) -> tuple[int, int, int, int, int]:
+    grouped = arch.topk_method in ("group_limited_greedy", "noaux_tc")
+    scoring = 0 if arch.scoring_func == "softmax" else 1
+    return (scoring, int(arch.norm_topk_prob), arch.n_group if grouped else 1, arch.topk_group if grouped else 1,
+            arch.num_experts_per_tok)
+
+
+class FusedAttentionExecutor(FFNExecutor):
+    """Attention-side FFN boundary on the fused kernels."""
+
+    def __init__(self, model, connector: B200FusedAFDConnector):
+        if model.compute_gate_on_attention:
+            raise ValueError("B200FusedAFDConnector keeps dense MLPs on the FFN side; use compute_gate_on_attention=false")
+        self.model = model
+        self.c = connector
+        self.arch = model.arch
+
+    def begin_step(self, stage_tokens, **flags) -> None:
+        from afd_plugin_b200.connectors.metadata import AFDControlPayload, AFDDPMetadata
+
+        across = flags.get("tokens_across_attn")
+        stages = sorted(stage_tokens)
+        dpl = {}
+        for s in stages:
+            counts = list(across[s]) if across is not None else [stage_tokens[s]] * self.c.attn_size
+            dpl[s] = AFDDPMetadata(num_tokens_across_dp_cpu=counts)
+        payload = AFDControlPayload(
+            dp_metadata_list=dpl,
+            is_graph_capturing=bool(flags.get("is_graph_capturing", False)),
+            is_warmup=bool(flags.get("is_warmup", False)),
+            is_graph_replaying=bool(flags.get("is_graph_replaying", False)),
+        )
+        self.c.control_plane.send_dp_metadata_list(payload)
+
+    def step_prologue(self) -> None:
+        torch.ops.afd_b200.afd_epoch(self.c.epoch)
+
+    def check_device_status(self) -> None:
+        st = self.c.read_status()
+        if st:
+            raise RuntimeError(f"Attention step failed on the device (status {st}: a peer wait timed out)")
+
+    def send(self, layer_idx, attn_out, residual, stage_idx):
+        c, d, a = self.c, self.c.dims, self.arch
+        is_moe = a.is_moe_layer(layer_idx)
+        layer = self.model.layers[layer_idx]
+        T = int(attn_out.shape[0])
+        if T > d.t_cap:
+            raise ValueError(f"{T} tokens exceed the connector capacity {d.t_cap} per rank and ubatch")
+        gate = layer.gate_only
+        if is_moe and gate is None:
+            raise RuntimeError("fused dispatch needs the MoE gate on the Attention role")
+        scoring, renorm, n_group, topk_group, k = _routing_cfg(a)
+        has_shared = (not is_moe) or a.n_shared_experts > 0
+        cfg = [a.n_routed_experts if is_moe else 1, k, scoring, renorm, n_group, topk_group, int(is_moe),
+               int(has_shared), d.num_ffn, d.e_local, d.cap, d.t_cap, c.role_rank % d.ratio, c.role_rank // d.ratio,
+               c.role_rank, layer_idx]
+        gate_w = gate.weight if is_moe else layer.post_attention_layernorm.weight
+        bias = gate.e_score_correction_bias if is_moe else None
+        torch.ops.afd_b200.afd_dispatch(
+            attn_out.contiguous(), residual, layer.post_attention_layernorm.weight, layer.post_attention_layernorm.eps,
+            gate_w, bias, float(a.routed_scaling_factor), c.dispatch_ptrs[stage_idx], c.done[stage_idx, 0:1], cfg)
+        return (T, residual, is_moe, has_shared)
+
+    def recv(self, layer_idx, handle, stage_idx):
+        T, residual, is_moe, has_shared = handle
+        c, d = self.c, self.c.dims
+        out = torch.ops.afd_b200.afd_combine(
+            c.comb[stage_idx], T, d.top_k if is_moe else 0, d.top_k if has_shared else -1, c.comb_flag[stage_idx],
+            layer_idx, c.epoch, d.num_ffn, c.timeout_ns)
+        return out, residual
+
+    def shutdown_remote(self) -> None:
+        from afd_plugin_b200.connectors.metadata import AFDControlPayload, AFDDPMetadata
+
+        payload = AFDControlPayload(dp_metadata_list={0: AFDDPMetadata(num_tokens_across_dp_cpu=[1])},
+                                    is_graph_capturing=False, is_warmup=False, is_shutdown=True)
+        self.c.control_plane.send_dp_metadata_list(payload)
+
+
+class FusedFFNRunner:
+    """FFN-side step: wait, tcgen05 grouped GEMMs, scatter to Attention ranks."""
+
+    def __init__(self, model, connector: B200FusedAFDConnector, engine_config):
+        from afd_plugin_b200.runtime.cuda_graph import validate_cuda_graph_mode
+
+        self.model = model
+        self.c = connector
+        self.config = engine_config
+        self.device = model.device
+        self.use_cuda_graph = validate_cuda_graph_mode(engine_config, role="ffn").enabled
+        d = connector.dims
+        dev = self.device
+        self.off_routed = torch.arange(d.e_local, dtype=torch.int32, device=dev) * d.cap
+        self.off_shared = d.shared_row0 + torch.arange(d.ratio, dtype=torch.int32, device=dev) * d.t_cap
+        self._graphs: dict = {}
+        self._pool = None
+        self._prepare_weights()
+        self.steps = 0
+
+    def _prepare_weights(self) -> None:
+        """Per layer: routed (w13, w2) and the 'shared segment' weights (shared experts or dense MLP)."""
+        a = self.model.arch
+        self.layer_w = []
+        for i, layer in enumerate(self.model.layers):
+            mlp = layer.mlp
+            if a.is_moe_layer(i):
+                ex = mlp.experts
+                if ex.w13_scale is not None:
+                    raise NotImplementedError("fused FFN path: fp8 block-scaled experts not wired yet")
+                shared = mlp.shared_experts
+                sw13 = shared.w13.unsqueeze(0) if shared is not None else None
+                sw2 = shared.w2.unsqueeze(0) if shared is not None else None
+                self.layer_w.append((ex.w13, ex.w2, sw13, sw2))
+            else:
+                self.layer_w.append((None, None, mlp.w13.unsqueeze(0), mlp.w2.unsqueeze(0)))
+
+    def _layer(self, layer_idx: int, s: int) -> None:
+        c, d = self.c, self.c.dims
+        C = torch.ops.afd_b200
+        C.afd_wait(c.arrive[s], layer_idx, c.epoch, d.num_attn, c.timeout_ns)
+        x = c.x_recv[s]
+        counts = c.counts[s]
+        w13, w2, sw13, sw2 = self.layer_w[layer_idx]
+        H = d.hidden
+        launches = []
+        if w13 is not None:
+            h_r = C.grouped_gemm_ex(x, w13, self.off_routed, counts[: d.e_local], 1, d.e_local)
+            launches.append((h_r, w2, self.off_routed, counts[: d.e_local], d.e_local))
+        if sw13 is not None:
+            h_s = C.grouped_gemm_ex(x, sw13, self.off_shared, counts[d.e_local :], 1, 1)
+            launches.append((h_s, sw2, self.off_shared, counts[d.e_local :], 1))
+        total = sum((H // 128) * int(cnt.numel()) for _, _, _, cnt, _ in launches)
+        for h, w, off, cnt, wexp in launches:
+            C.grouped_gemm_scatter(h, w, off, cnt, wexp, c.meta[s], c.rw[s], c.scatter_dst[s], c.scatter_flags[s],
+                                   c.done[s, 1:2], counts, [d.slots, H, total, d.num_attn, layer_idx])
+
+    def _step(self, stages) -> None:
+        torch.ops.afd_b200.afd_epoch(self.c.epoch)
+        for layer in range(self.model.num_layers):
+            for s in stages:
+                self._layer(layer, s)
+
+    def execute_model(self, payload) -> None:
+        from afd_plugin_b200.runtime.cuda_graph import AFDGraphRunMode, graph_run_mode, make_capacity_graph_key
+
+        stages = tuple(sorted(payload.dp_metadata_list))
+        key = make_capacity_graph_key(stages, self.c.dims.t_cap)
+        entry = self._graphs.get(key)
+        mode = graph_run_mode(is_warmup=payload.is_warmup, is_graph_capturing=payload.is_graph_capturing,
+                              is_graph_replaying=payload.is_graph_replaying, graph_enabled=self.use_cuda_graph,
+                              graph_exists=entry is not None)
+        self.steps += 1
+        if mode is AFDGraphRunMode.REPLAY:
+            entry.replay()
+            return
+        if mode is AFDGraphRunMode.CAPTURE and self.use_cuda_graph:
+            g = torch.cuda.CUDAGraph()
+            if self._pool is None:
+                self._pool = torch.cuda.graph_pool_handle()
+            with torch.cuda.graph(g, pool=self._pool):
+                self._step(stages)
+            self._graphs[key] = g
+            return
+        self._step(stages)
+
+    def serve(self, *, max_steps: int | None = None, stop=None) -> int:
+        cp = self.c.control_plane
+        n = 0
+        while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
+            payload = cp.recv_dp_metadata_list()
+            if payload.is_shutdown:
+                break
+            self.execute_model(payload)
+            torch.cuda.synchronize(self.device)
+            st = self.c.read_status()
+            if st:
+                raise RuntimeError(f"FFN step failed on the device (status {st}: a peer wait timed out)")
+            n += 1
+        return n
+
+    def release_graphs(self) -> None:
+        self._graphs.clear()
+        self._pool = None
+
+
+__all__ = ["B200FusedAFDConnector", "B200FusedExtraInfo", "FusedAttentionExecutor", "FusedFFNRunner", "FusedLayout"]

@@ -51,6 +51,7 @@ def build_model(
     seed: int = 0,
     checkpoint: str | None = None,
     max_positions: int | None = None,
+    route_on_attention: bool = False,
 ) -> AFDCausalLM:
     cls = model_class_for(arch)
     model = cls(
@@ -62,6 +63,7 @@ def build_model(
         ep_rank=ep_rank,
         ep_size=ep_size,
         max_positions=max_positions,
+        route_on_attention=route_on_attention,
     )
     if checkpoint is None:
         model.init_random(seed)

@@ -38,10 +38,12 @@ def iter_safetensors(path: str) -> Iterator[tuple[str, torch.Tensor]]:
 
 
 def iter_role_weights(
-    weights: Iterable[tuple[str, torch.Tensor]], *, role: str, arch: ModelArchConfig, compute_gate_on_attention: bool
+    weights: Iterable[tuple[str, torch.Tensor]], *, role: str, arch: ModelArchConfig, compute_gate_on_attention: bool,
+    route_on_attention: bool = False,
 ) -> Iterator[tuple[str, torch.Tensor]]:
     for name, t in weights:
-        if role == "colocated" or role in weight_roles(name, arch, compute_gate_on_attention=compute_gate_on_attention):
+        if role == "colocated" or role in weight_roles(name, arch, compute_gate_on_attention=compute_gate_on_attention,
+                                                       route_on_attention=route_on_attention):
             yield name, t
 
 
@@ -55,7 +57,8 @@ def load_weights(model: AFDCausalLM, weights: Iterable[tuple[str, torch.Tensor]]
     pending_scales: dict[str, torch.Tensor] = {}
     loaded: set[str] = set()
     stream = iter_role_weights(
-        weights, role=model.role, arch=model.arch, compute_gate_on_attention=model.compute_gate_on_attention
+        weights, role=model.role, arch=model.arch, compute_gate_on_attention=model.compute_gate_on_attention,
+        route_on_attention=getattr(model, "route_on_attention", False),
     )
     for name, t in stream:
         if name in specs:

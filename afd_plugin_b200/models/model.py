@@ -59,7 +59,8 @@ class ParamSpec:
     fp8_scale_name: str | None = None
 
 
-def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention: bool) -> frozenset[str]:
+def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention: bool,
+                 route_on_attention: bool = False) -> frozenset[str]:
     """Which AFD role(s) need checkpoint tensor ``name``.
 
     Same classification as ``_checkpoint_weight_roles`` of the reference
@@ -81,7 +82,7 @@ def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention:
             return _BOTH
         if not arch.is_moe_layer(layer):
             return _ATTN if compute_gate_on_attention else _FFN
-        if rest and rest[0] == "gate" and compute_gate_on_attention:
+        if rest and rest[0] == "gate" and (compute_gate_on_attention or route_on_attention):
             return _BOTH
         return _FFN
     return _BOTH
@@ -89,7 +90,7 @@ def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention:
 
 class DecoderLayer(nn.Module):
     def __init__(self, arch: ModelArchConfig, idx: int, role: str, dtype, device, *, gate_on_attn: bool,
-                 ep_rank: int, ep_size: int):
+                 ep_rank: int, ep_size: int, route_on_attn: bool = False):
         super().__init__()
         self.idx = idx
         self.is_moe = arch.is_moe_layer(idx)
@@ -106,13 +107,12 @@ class DecoderLayer(nn.Module):
             self.mlp = MoEBlock(arch, dtype, device) if self.is_moe else DenseMLP(
                 arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
         elif role == "attention":
-            if gate_on_attn:
-                if self.is_moe:
-                    from afd_plugin_b200.models.layers import MoEGate
+            if self.is_moe and (gate_on_attn or route_on_attn):
+                from afd_plugin_b200.models.layers import MoEGate
 
-                    self.gate_only = MoEGate(arch, dtype, device)
-                else:
-                    self.mlp = DenseMLP(arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
+                self.gate_only = MoEGate(arch, dtype, device)
+            elif gate_on_attn:
+                self.mlp = DenseMLP(arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
         else:  # ffn
             if self.is_moe:
                 self.mlp = MoEBlock(arch, dtype, device, ep_rank=ep_rank, ep_size=ep_size)
@@ -136,6 +136,7 @@ class AFDCausalLM(nn.Module):
         ep_rank: int = 0,
         ep_size: int = 1,
         max_positions: int | None = None,
+        route_on_attention: bool = False,
     ):
         super().__init__()
         if role not in ROLES:
@@ -146,12 +147,14 @@ class AFDCausalLM(nn.Module):
         self.dtype = dtype
         self.device = torch.device(device)
         self.compute_gate_on_attention = compute_gate_on_attention
+        # Routing on the Attention side without moving dense MLPs there (fused connector).
+        self.route_on_attention = route_on_attention
         self.ep_rank, self.ep_size = ep_rank, ep_size
         has_attn = role in ("colocated", "attention")
         self.embed_tokens = _param((arch.vocab_size, arch.hidden_size), dtype, device) if has_attn else None
         self.layers = nn.ModuleList(
             DecoderLayer(arch, i, role, dtype, device, gate_on_attn=compute_gate_on_attention,
-                         ep_rank=ep_rank, ep_size=ep_size)
+                         ep_rank=ep_rank, ep_size=ep_size, route_on_attn=route_on_attention)
             for i in range(arch.num_hidden_layers)
         )
         self.norm = RMSNorm(arch.hidden_size, arch.rms_norm_eps, dtype, device) if has_attn else None

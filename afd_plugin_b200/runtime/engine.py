@@ -270,6 +270,9 @@ class LLMEngine:
         self._h_next[:run_b].copy_(nxt, non_blocking=True)
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
+            check = getattr(self.ffn, "check_device_status", None)
+            if check is not None:
+                check()
         self.last_d2h_bytes = run_b * 4
         out = {}
         still = []

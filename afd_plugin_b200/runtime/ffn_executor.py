@@ -36,6 +36,10 @@ class FFNExecutor:
         """``flags``: is_warmup / is_graph_capturing / is_graph_replaying / tokens_across_attn."""
         return None
 
+    def step_prologue(self) -> None:
+        """Device work issued at the start of every forward (inside captured graphs)."""
+        return None
+
     def send(self, layer_idx: int, attn_out: torch.Tensor, residual: torch.Tensor, stage_idx: int) -> Any:
         raise NotImplementedError
 

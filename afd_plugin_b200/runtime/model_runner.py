@@ -116,6 +116,7 @@ class ModelRunner:
         """Logits for the last position of each token row (decode) or all rows (prefill)."""
         counts = {s: splits[s + 1] - splits[s] for s in range(len(splits) - 1)}
         self.ffn.begin_step(counts, **step_flags)
+        self.ffn.step_prologue()
         embeds = [self.model.embed(input_ids[splits[s] : splits[s + 1]]) for s in range(len(splits) - 1)]
         outs = self._run_stages(embeds, metas)
         self.ffn.end_step()

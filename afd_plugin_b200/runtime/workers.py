@@ -86,6 +86,7 @@ class AFDAttentionWorker(_WorkerBase):
         self.model = build_model(
             mc.arch, role="attention", dtype=mc.dtype, device=self.device,
             compute_gate_on_attention=self.afd.compute_gate_on_attention,
+            route_on_attention=self.afd.connector == B200_FUSED_CONNECTOR,
             seed=mc.seed if seed is None else seed, checkpoint=mc.checkpoint, max_positions=mc.max_model_len)
         A = self.afd.num_attention_ranks
         if self.afd.connector == B200_FUSED_CONNECTOR:

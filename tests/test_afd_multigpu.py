@@ -1,0 +1,72 @@
+"""AFD across two GPUs (one process per GPU): NCCL baseline and fused B200 connector.
+
+The NCCL connector runs the same FFN ops as the colocated model, so its tokens
+must match exactly.  The fused connector normalises, routes and sums in its own
+kernels (different bf16 rounding points), so it is held to near-agreement.
+"""
+
+import pytest
+import torch
+
+from afd_plugin_b200.engine_config import CompilationConfig, EngineConfig, ModelConfig
+from afd_plugin_b200.models import build_model, get_preset
+from afd_plugin_b200.runtime.engine import LLMEngine
+from afd_plugin_b200.runtime.launcher import LocalAFDSpec, launch_local
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+PRESET = "tiny-dsv2-mla512"
+
+
+def _need(n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+def _prompts(n, length, vocab=1024, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, vocab, (n, length), generator=g).tolist()
+
+
+def _colocated(prompts, max_tokens):
+    arch = get_preset(PRESET)
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.bfloat16, enforce_eager=True, max_model_len=128), max_num_seqs=8)
+    m = build_model(arch, role="colocated", dtype=torch.bfloat16, device="cuda", seed=0, max_positions=128)
+    return LLMEngine(ec, m).generate(prompts, max_tokens)
+
+
+def _run(afd, prompts, max_tokens, **kw):
+    spec = LocalAFDSpec(preset=PRESET, afd=afd, prompts=prompts, max_tokens=max_tokens, dtype="bfloat16",
+                        backend="nccl", **kw)
+    res = launch_local(spec, join_timeout_s=240)
+    errs = {r: v for r, v in res.items() if "error" in v}
+    assert not errs, errs
+    outs = []
+    for r in sorted(res):
+        outs += res[r].get("outputs", [])
+    return outs
+
+
+def _agreement(a, b):
+    flat_a = [t for o in a for t in o]
+    flat_b = [t for o in b for t in o]
+    return sum(x == y for x, y in zip(flat_a, flat_b)) / max(1, len(flat_a))
+
+
+def test_nccl_connector_1a1f_exact():
+    _need(2)
+    prompts = _prompts(4, 16)
+    ref = _colocated(prompts, 6)
+    outs = _run({"num_attention_ranks": 1, "num_ffn_ranks": 1}, prompts, 6)
+    assert outs == ref
+
+
+@pytest.mark.parametrize("eager,dbo", [(True, False), (False, False), (False, True)])
+def test_fused_connector_1a1f(eager, dbo):
+    _need(2)
+    prompts = _prompts(4, 16)
+    ref = _colocated(prompts, 6)
+    afd = {"num_attention_ranks": 1, "num_ffn_ranks": 1, "connector": "B200FusedAFDConnector",
+           "connector_extra_config": {"max_tokens_per_rank": 128, "wait_timeout_ms": 20000}}
+    outs = _run(afd, prompts, 6, enforce_eager=eager, use_ubatching=dbo, capture_sizes=[4])
+    assert [o[0] for o in outs] == [o[0] for o in ref]
+    assert _agreement(outs, ref) >= 0.75
