@@ -25,9 +25,10 @@ The control plane (per-step payload Attention -> FFN over gloo) only tells the
 FFN host loop to replay its captured step; token counts stay on the device, so
 one FFN graph serves every routing (key: stages and capacity).
 
-Counters only grow and are compared with ``epoch * arrivals`` (a per-step
-device epoch bumped inside every captured step), so graphs replay without
-resets.  Every wait is bounded (``wait_timeout_ms``) and reports through the
+Counters only grow and are compared with ``epoch[stage] * arrivals`` (a
+per-stage device epoch bumped inside every captured step that uses the
+stage; prefill steps use one stage, DBO decode steps two), so graphs replay
+without resets.  Every wait is bounded (``wait_timeout_ms``) and reports through the
 device status word instead of hanging.
 
 Semantics follow the reference connector contract
@@ -135,7 +136,7 @@ class FusedLayout:
         L.add("arrive", (S, self.layers), torch.int64)
         L.add("comb", (S, self.t_cap, self.slots, self.hidden), torch.bfloat16)
         L.add("comb_flag", (S, self.layers), torch.int64)
-        L.add("epoch", (1,), torch.int64)
+        L.add("epoch", (S,), torch.int64)  # per stage: steps that used the stage
         L.add("done", (S, 2), torch.int32)
         return L
 
@@ -295,6 +296,7 @@ class FusedAttentionExecutor(FFNExecutor):
 
         across = flags.get("tokens_across_attn")
         stages = sorted(stage_tokens)
+        self._stages = tuple(stages)
         dpl = {}
         for s in stages:
             counts = list(across[s]) if across is not None else [stage_tokens[s]] * self.c.attn_size
@@ -308,7 +310,8 @@ class FusedAttentionExecutor(FFNExecutor):
         self.c.control_plane.send_dp_metadata_list(payload)
 
     def step_prologue(self) -> None:
-        torch.ops.afd_b200.afd_epoch(self.c.epoch)
+        for s in getattr(self, "_stages", (0,)):
+            torch.ops.afd_b200.afd_epoch(self.c.epoch[s : s + 1])
 
     def check_device_status(self) -> None:
         st = self.c.read_status()
@@ -342,7 +345,7 @@ class FusedAttentionExecutor(FFNExecutor):
         c, d = self.c, self.c.dims
         out = torch.ops.afd_b200.afd_combine(
             c.comb[stage_idx], T, d.top_k if is_moe else 0, d.top_k if has_shared else -1, c.comb_flag[stage_idx],
-            layer_idx, c.epoch, d.num_ffn, c.timeout_ns)
+            layer_idx, c.epoch[stage_idx : stage_idx + 1], d.num_ffn, c.timeout_ns)
         return out, residual
 
     def shutdown_remote(self) -> None:
@@ -393,7 +396,7 @@ class FusedFFNRunner:
     def _layer(self, layer_idx: int, s: int) -> None:
         c, d = self.c, self.c.dims
         C = torch.ops.afd_b200
-        C.afd_wait(c.arrive[s], layer_idx, c.epoch, d.num_attn, c.timeout_ns)
+        C.afd_wait(c.arrive[s], layer_idx, c.epoch[s : s + 1], d.num_attn, c.timeout_ns)
         x = c.x_recv[s]
         counts = c.counts[s]
         w13, w2, sw13, sw2 = self.layer_w[layer_idx]
@@ -405,13 +408,14 @@ class FusedFFNRunner:
         if sw13 is not None:
             h_s = C.grouped_gemm_ex(x, sw13, self.off_shared, counts[d.e_local :], 1, 1)
             launches.append((h_s, sw2, self.off_shared, counts[d.e_local :], 1))
-        total = sum((H // 128) * int(cnt.numel()) for _, _, _, cnt, _ in launches)
+        total = sum(int(C.grouped_gemm_grid((H // 128) * int(cnt.numel()))) for _, _, _, cnt, _ in launches)
         for h, w, off, cnt, wexp in launches:
             C.grouped_gemm_scatter(h, w, off, cnt, wexp, c.meta[s], c.rw[s], c.scatter_dst[s], c.scatter_flags[s],
                                    c.done[s, 1:2], counts, [d.slots, H, total, d.num_attn, layer_idx])
 
     def _step(self, stages) -> None:
-        torch.ops.afd_b200.afd_epoch(self.c.epoch)
+        for s in stages:
+            torch.ops.afd_b200.afd_epoch(self.c.epoch[s : s + 1])
         for layer in range(self.model.num_layers):
             for s in stages:
                 self._layer(layer, s)
@@ -439,20 +443,34 @@ class FusedFFNRunner:
             return
         self._step(stages)
 
-    def serve(self, *, max_steps: int | None = None, stop=None) -> int:
+    def serve(self, *, max_steps: int | None = None, stop=None, check_every: int = 16) -> int:
+        """Replay one step per control payload.
+
+        Steps are launched without waiting for the previous one: the captured
+        step itself waits (bounded) for the Attention side's arrivals, so the
+        host can queue the next step while the device runs.  The device status
+        is checked every ``check_every`` steps and at the end.
+        """
         cp = self.c.control_plane
         n = 0
-        while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
-            payload = cp.recv_dp_metadata_list()
-            if payload.is_shutdown:
-                break
-            self.execute_model(payload)
+        try:
+            while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
+                payload = cp.recv_dp_metadata_list()
+                if payload.is_shutdown:
+                    break
+                self.execute_model(payload)
+                n += 1
+                if n % check_every == 0:
+                    self._check()
+        finally:
             torch.cuda.synchronize(self.device)
-            st = self.c.read_status()
-            if st:
-                raise RuntimeError(f"FFN step failed on the device (status {st}: a peer wait timed out)")
-            n += 1
+        self._check()
         return n
+
+    def _check(self) -> None:
+        st = self.c.read_status()
+        if st:
+            raise RuntimeError(f"FFN step failed on the device (status {st}: a peer wait timed out)")
 
     def release_graphs(self) -> None:
         self._graphs.clear()

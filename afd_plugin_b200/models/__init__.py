@@ -52,6 +52,7 @@ def build_model(
     checkpoint: str | None = None,
     max_positions: int | None = None,
     route_on_attention: bool = False,
+    init_on: str | None = None,
 ) -> AFDCausalLM:
     cls = model_class_for(arch)
     model = cls(
@@ -66,11 +67,12 @@ def build_model(
         route_on_attention=route_on_attention,
     )
     if checkpoint is None:
-        model.init_random(seed)
+        model.init_random(seed, generate_on=init_on)
     else:
         from afd_plugin_b200.models.loader import load_checkpoint
 
         load_checkpoint(model, checkpoint)
+    model.finalize_weights()
     return model
 
 

@@ -104,10 +104,18 @@ class MLAAttention(nn.Module):
         q_pe = q[..., self.qk_nope :]
         ops.rope_(q_pe, meta.positions, cos_sin, interleaved=True)
         q_nope = q[..., : self.qk_nope]
+        if h.is_cuda and meta.is_decode and self.kv_lora == 512 and self.qk_rope == 64 and self.num_heads % 16 == 0:
+            # Head-major end to end: [H,T,128]x[H,128,512] -> kernel -> [H,T,512]x[H,512,v].
+            q_lat = torch.bmm(q_nope.transpose(0, 1), self.w_uk)
+            o_lat = ops.mla_decode_split(q_lat.transpose(0, 1), q_pe, kv_cache, meta.block_table, meta.seq_lens,
+                                         self.scale, head_major_out=True)
+            o = torch.bmm(o_lat, self.w_uv_t).transpose(0, 1).reshape(T, self.num_heads * self.v_dim)
+            return ops.linear(o, self.o_proj)
         # [H, T, nope] x [H, nope, kv_lora] -> [H, T, kv_lora]
-        q_lat = torch.bmm(q_nope.transpose(0, 1).to(self.w_uk.dtype), self.w_uk) if h.is_cuda else torch.bmm(
-            q_nope.transpose(0, 1).float(), self.w_uk.float()
-        ).to(h.dtype)
+        if h.is_cuda:
+            q_lat = torch.bmm(q_nope.transpose(0, 1), self.w_uk)
+        else:
+            q_lat = torch.bmm(q_nope.transpose(0, 1).float(), self.w_uk.float()).to(h.dtype)
         q_full = torch.cat([q_lat.transpose(0, 1), q_pe], dim=-1).contiguous()  # [T, H, 576]
         if meta.is_decode:
             o_lat = ops.mla_decode(q_full, kv_cache, meta.block_table, meta.seq_lens, self.scale, self.kv_lora)
@@ -222,23 +230,49 @@ class MoEGate(nn.Module):
 
 
 class RoutedExperts(nn.Module):
-    """Stacked expert weights for the experts ``[offset, offset + n_local)``."""
+    """Stacked expert weights for the experts ``[offset, offset + n_local)``.
 
-    def __init__(self, arch: ModelArchConfig, n_local: int, offset: int, dtype, device):
+    ``n_extra`` additional slots after the routed experts hold the shared
+    experts split into chunks of the routed intermediate size, so the CUDA path
+    runs routed and shared experts in one grouped GEMM ("virtual experts").
+    """
+
+    def __init__(self, arch: ModelArchConfig, n_local: int, offset: int, dtype, device, n_extra: int = 0):
         super().__init__()
         self.n_local = n_local
+        self.n_extra = n_extra
         self.offset = offset
         I, H = arch.moe_intermediate_size, arch.hidden_size
         self.quant = arch.quant
         wdtype = torch.float8_e4m3fn if arch.quant == "fp8_block" else dtype
-        self.w13 = _param((n_local, 2 * I, H), wdtype, device)
-        self.w2 = _param((n_local, H, I), wdtype, device)
+        self.w13_all = _param((n_local + n_extra, 2 * I, H), wdtype, device)
+        self.w2_all = _param((n_local + n_extra, H, I), wdtype, device)
         if arch.quant == "fp8_block":
             self.w13_scale = _param((n_local, (2 * I + 127) // 128, (H + 127) // 128), torch.float32, device)
             self.w2_scale = _param((n_local, (H + 127) // 128, (I + 127) // 128), torch.float32, device)
         else:
             self.w13_scale = None
             self.w2_scale = None
+
+    @property
+    def w13(self) -> torch.Tensor:
+        return self.w13_all[: self.n_local]
+
+    @property
+    def w2(self) -> torch.Tensor:
+        return self.w2_all[: self.n_local]
+
+    def pack_shared(self, shared: "DenseMLP") -> None:
+        """Copy the shared expert into the extra slots, chunked by the routed width."""
+        if not self.n_extra:
+            return
+        I = self.w2_all.shape[2]
+        Is = shared.w2.shape[1]
+        for c in range(self.n_extra):
+            e = self.n_local + c
+            self.w13_all.data[e, :I].copy_(shared.w13[c * I : (c + 1) * I])
+            self.w13_all.data[e, I:].copy_(shared.w13[Is + c * I : Is + (c + 1) * I])
+            self.w2_all.data[e].copy_(shared.w2[:, c * I : (c + 1) * I])
 
     def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
         return ops.moe_experts(
@@ -258,12 +292,18 @@ class MoEBlock(nn.Module):
             raise ValueError(f"{E} experts do not split over {ep_size} expert-parallel ranks")
         n_local = E // ep_size
         self.gate = MoEGate(arch, dtype, device) if with_gate else None
-        self.experts = RoutedExperts(arch, n_local, ep_rank * n_local, dtype, device)
+        chunked = (arch.n_shared_experts > 0 and arch.quant is None and arch.moe_intermediate_size % 64 == 0)
+        self.n_shared_chunks = arch.n_shared_experts if chunked else 0
+        self.experts = RoutedExperts(arch, n_local, ep_rank * n_local, dtype, device, n_extra=self.n_shared_chunks)
         self.shared_experts = (
             DenseMLP(arch.hidden_size, arch.shared_intermediate_size, dtype, device, arch.quant)
             if arch.n_shared_experts
             else None
         )
+
+    def finalize(self) -> None:
+        if self.shared_experts is not None:
+            self.experts.pack_shared(self.shared_experts)
 
     def forward(self, h: torch.Tensor, router_logits: torch.Tensor | None = None) -> torch.Tensor:
         if router_logits is None:
@@ -273,14 +313,16 @@ class MoEBlock(nn.Module):
         if self.gate is None:
             raise RuntimeError("MoE block needs gate parameters (bias / routing config) to route")
         w, ids = self.gate.route(router_logits)
-        out = self.experts(h, w, ids)
-        if self.shared_experts is not None:
-            out = out + self.shared_experts(h)
-        return out
+        return self.forward_experts(h, w, ids)
 
     def forward_experts(self, h: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
                         include_shared: bool = True) -> torch.Tensor:
-        out = self.experts(h, topk_weights, topk_ids)
+        ex = self.experts
+        if h.is_cuda and include_shared and self.n_shared_chunks:
+            # Routed and shared experts in the same grouped GEMMs.
+            return ops.moe_experts(h, ex.w13_all, ex.w2_all, topk_weights, topk_ids, expert_offset=ex.offset,
+                                   n_shared=self.n_shared_chunks)
+        out = ex(h, topk_weights, topk_ids)
         if include_shared and self.shared_experts is not None:
             out = out + self.shared_experts(h)
         return out

@@ -263,10 +263,22 @@ class AFDCausalLM(nn.Module):
     def _attn_specs(self, p: str, attn) -> Iterator[ParamSpec]:
         raise NotImplementedError
 
-    def init_random(self, seed: int = 0, std: float = 0.02) -> None:
-        """Seeded N(0, std) init; each tensor's stream depends only on (seed, name)."""
+    def finalize_weights(self) -> None:
+        """Derived layouts after loading (shared experts packed as virtual experts)."""
+        for layer in self.layers:
+            if isinstance(layer.mlp, MoEBlock):
+                layer.mlp.finalize()
+
+    def init_random(self, seed: int = 0, std: float = 0.02, *, generate_on: str | None = None) -> None:
+        """Seeded N(0, std) init; each tensor's stream depends only on (seed, name).
+
+        Values are drawn on the model's device unless ``generate_on="cpu"``
+        (CPU and CUDA generators produce different streams; generate on CPU to
+        compare a GPU model with a CPU one).
+        """
         for spec in self.param_specs():
-            gen_dev = self.device if self.device.type == "cuda" else torch.device("cpu")
+            gen_dev = torch.device(generate_on) if generate_on else (
+                self.device if self.device.type == "cuda" else torch.device("cpu"))
             g = torch.Generator(device=gen_dev)
             g.manual_seed((seed * 1_000_003 + zlib.crc32(spec.name.encode())) & 0x7FFFFFFFFFFFFFFF)
             if spec.init == "ones":

@@ -95,7 +95,8 @@ def mla_decode(
 ) -> torch.Tensor:
     if _cuda(q):
         if q.shape[-1] == 576 and kv_lora_rank == 512 and q.shape[1] % 16 == 0:
-            return _cuda_ops().mla_decode(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank, num_splits)
+            return _cuda_ops().mla_decode(q[..., :512], q[..., 512:], kv_cache, block_table, seq_lens, scale,
+                                          num_splits, False)
         # The kernel is specialised to DeepSeek's 512 + 64 latent; other
         # (test-sized) shapes run the batched PyTorch form.
         return _mla_decode_torch(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank)
@@ -111,6 +112,25 @@ def _mla_decode_torch(q, kv_cache, block_table, seq_lens, scale, kv_lora_rank):
     mask = torch.arange(nblk * bs, device=q.device)[None, :] >= seq_lens.long()[:, None]
     s = s.masked_fill(mask[:, None, :], float("-inf"))
     return torch.einsum("bhn,bnd->bhd", torch.softmax(s, dim=-1), kv[..., :kv_lora_rank]).to(q.dtype)
+
+
+def mla_decode_split(
+    q_lat: torch.Tensor,
+    q_pe: torch.Tensor,
+    kv_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float,
+    *,
+    head_major_out: bool = True,
+    num_splits: int = 0,
+) -> torch.Tensor:
+    """MLA decode with the query as two strided views ``[B, H, 512]`` / ``[B, H, 64]``.
+
+    Returns ``[H, B, 512]`` (head-major, ready for the per-head V up-projection)
+    or ``[B, H, 512]``.  CUDA only (the kernel's native interface).
+    """
+    return _cuda_ops().mla_decode(q_lat, q_pe, kv_cache, block_table, seq_lens, scale, num_splits, head_major_out)
 
 
 def gqa_decode(
@@ -189,14 +209,22 @@ def moe_experts(
     expert_offset: int = 0,
     w13_scale: torch.Tensor | None = None,
     w2_scale: torch.Tensor | None = None,
+    n_shared: int = 0,
 ) -> torch.Tensor:
-    """Routed-expert output ``[T, H]`` (weights applied, summed over k)."""
+    """Routed-expert output ``[T, H]`` (weights applied, summed over k).
+
+    With ``n_shared`` the last ``n_shared`` experts of ``w13``/``w2`` are shared
+    chunks applied to every token with weight 1 (CUDA path).
+    """
     if _cuda(x):
         from afd_plugin_b200.ops.moe import moe_experts_cuda
 
         return moe_experts_cuda(
-            x, w13, w2, topk_weights, topk_ids, expert_offset=expert_offset, w13_scale=w13_scale, w2_scale=w2_scale
+            x, w13, w2, topk_weights, topk_ids, expert_offset=expert_offset, w13_scale=w13_scale, w2_scale=w2_scale,
+            n_shared=n_shared,
         )
+    if n_shared:
+        raise ValueError("virtual shared experts are a CUDA-path layout")
     return ref.moe_experts(
         x, w13, w2, topk_weights, topk_ids, expert_offset=expert_offset, w13_scale=w13_scale, w2_scale=w2_scale
     )

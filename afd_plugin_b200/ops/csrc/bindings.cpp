@@ -147,20 +147,29 @@ void gqa_cache_write(at::Tensor& kc, at::Tensor& vc, const at::Tensor& k, const 
 }
 
 // -------------------------------------------------------------- attention
-at::Tensor mla_decode(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& block_table,
-                      const at::Tensor& seq_lens, double scale, int64_t L, int64_t num_splits) {
-  check_cuda(q, "q");
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16, "mla_decode: bf16 only");
-  TORCH_CHECK(q.is_contiguous() && cache.is_contiguous(), "mla_decode: contiguous q and cache");
-  TORCH_CHECK(q.size(2) == 576 && L == 512 && cache.size(-1) == 576, "mla_decode: latent 512 + rope 64 only");
-  TORCH_CHECK(q.size(1) % 16 == 0, "mla_decode: heads must be a multiple of 16");
+// q_lat [B, H, 512] and q_pe [B, H, 64] may be any strided views (last dim
+// contiguous); the output is [B, H, 512], or [H, B, 512] when head_major.
+at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& cache,
+                      const at::Tensor& block_table, const at::Tensor& seq_lens, double scale, int64_t num_splits,
+                      bool head_major) {
+  check_cuda(q_lat, "q_lat");
+  TORCH_CHECK(q_lat.scalar_type() == at::kBFloat16 && q_pe.scalar_type() == at::kBFloat16 &&
+                  cache.scalar_type() == at::kBFloat16, "mla_decode: bf16 only");
+  TORCH_CHECK(q_lat.dim() == 3 && q_pe.dim() == 3 && q_lat.size(2) == 512 && q_pe.size(2) == 64 &&
+                  q_lat.stride(2) == 1 && q_pe.stride(2) == 1, "mla_decode: q_lat [B,H,512], q_pe [B,H,64]");
+  TORCH_CHECK(q_lat.size(0) == q_pe.size(0) && q_lat.size(1) == q_pe.size(1), "mla_decode: q halves disagree");
+  TORCH_CHECK(q_lat.stride(0) % 8 == 0 && q_lat.stride(1) % 8 == 0 && q_pe.stride(0) % 8 == 0 && q_pe.stride(1) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(q_lat.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(q_pe.data_ptr()) % 16 == 0, "mla_decode: 16-byte aligned rows");
+  TORCH_CHECK(cache.is_contiguous() && cache.size(-1) == 576, "mla_decode: cache [blocks, bs, 576] contiguous");
+  TORCH_CHECK(q_lat.size(1) % 16 == 0, "mla_decode: heads must be a multiple of 16");
   TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt, "mla_decode: int32 meta");
   TORCH_CHECK(block_table.stride(1) == 1, "mla_decode: block_table rows must be dense");
-  const int B = (int)q.size(0), H = (int)q.size(1);
+  const int B = (int)q_lat.size(0), H = (int)q_lat.size(1);
   const int bs = (int)cache.size(1), nblocks = (int)cache.size(0);
   TORCH_CHECK(bs % 32 == 0, "mla_decode: block size must be a multiple of 32");
   const int maxb = (int)block_table.size(1);
-  auto out = at::empty({B, H, L}, q.options());
+  at::Tensor out = head_major ? at::empty({H, B, 512}, q_lat.options()) : at::empty({B, H, 512}, q_lat.options());
   if (B == 0) return out;
   int splits = (int)num_splits;
   if (splits <= 0) {
@@ -169,29 +178,41 @@ at::Tensor mla_decode(const at::Tensor& q, const at::Tensor& cache, const at::Te
   }
   at::Tensor po, pl;
   if (splits > 1) {
-    po = at::empty({B, splits, H, L}, q.options().dtype(at::kFloat));
-    pl = at::empty({B, splits, H}, q.options().dtype(at::kFloat));
+    po = at::empty({B, splits, H, 512}, q_lat.options().dtype(at::kFloat));
+    pl = at::empty({B, splits, H}, q_lat.options().dtype(at::kFloat));
   }
-  c10::cuda::CUDAGuard g(q.device());
-  launch_mla_decode(out.data_ptr(), q.data_ptr(), cache.data_ptr(), block_table.data_ptr<int32_t>(),
-                    seq_lens.data_ptr<int32_t>(), splits > 1 ? po.data_ptr<float>() : nullptr,
-                    splits > 1 ? pl.data_ptr<float>() : nullptr, status_ptr(q), B, H, (int)L, 576 - (int)L, bs,
-                    nblocks, (int)block_table.stride(0), splits, (float)scale, stream());
+  MlaQO qo{};
+  qo.q_lat = reinterpret_cast<const __nv_bfloat16*>(q_lat.data_ptr());
+  qo.lat_sb = q_lat.stride(0);
+  qo.lat_sh = q_lat.stride(1);
+  qo.q_pe = reinterpret_cast<const __nv_bfloat16*>(q_pe.data_ptr());
+  qo.pe_sb = q_pe.stride(0);
+  qo.pe_sh = q_pe.stride(1);
+  qo.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  qo.out_sb = head_major ? 512 : (int64_t)H * 512;
+  qo.out_sh = head_major ? (int64_t)B * 512 : 512;
+  c10::cuda::CUDAGuard g(q_lat.device());
+  launch_mla_decode(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                    splits > 1 ? po.data_ptr<float>() : nullptr, splits > 1 ? pl.data_ptr<float>() : nullptr,
+                    status_ptr(q_lat), B, H, 512, 64, bs, nblocks, (int)block_table.stride(0), splits, (float)scale,
+                    stream());
   return out;
 }
 
 // -------------------------------------------------------------------- MoE
-std::vector<at::Tensor> moe_align(const at::Tensor& topk_ids, int64_t e_local, int64_t offset) {
+std::vector<at::Tensor> moe_align(const at::Tensor& topk_ids, int64_t e_local, int64_t offset, int64_t n_shared) {
   check_cuda(topk_ids, "topk_ids");
   TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous(), "moe_align: int32 contiguous ids");
-  TORCH_CHECK(e_local <= 1024, "moe_align: at most 1024 local experts");
+  TORCH_CHECK(e_local + n_shared <= 1024, "moe_align: at most 1024 local experts");
   const int T = (int)topk_ids.size(0), k = (int)topk_ids.size(1);
+  const int ks = k + (int)n_shared;
   auto o = topk_ids.options();
-  auto counts = at::empty({e_local}, o), offsets = at::empty({e_local}, o);
-  auto row_token = at::empty({std::max(T * k, 1)}, o), row_slot = at::empty({std::max(T * k, 1)}, o);
-  auto tsr = at::empty({T, k}, o), total = at::empty({1}, o);
+  auto counts = at::empty({e_local + n_shared}, o), offsets = at::empty({e_local + n_shared}, o);
+  auto row_token = at::empty({std::max(T * ks, 1)}, o), row_slot = at::empty({std::max(T * ks, 1)}, o);
+  auto tsr = at::empty({T, ks}, o), total = at::empty({1}, o);
   c10::cuda::CUDAGuard g(topk_ids.device());
-  launch_moe_align(topk_ids.data_ptr<int32_t>(), T, k, (int)e_local, (int)offset, 1, counts.data_ptr<int32_t>(),
+  launch_moe_align(topk_ids.data_ptr<int32_t>(), T, k, (int)n_shared, (int)e_local, (int)offset,
+                   counts.data_ptr<int32_t>(),
                    offsets.data_ptr<int32_t>(), row_token.data_ptr<int32_t>(), row_slot.data_ptr<int32_t>(),
                    tsr.data_ptr<int32_t>(), total.data_ptr<int32_t>(), stream());
   return {counts, offsets, row_token, row_slot, tsr, total};
@@ -233,6 +254,7 @@ at::Tensor grouped_gemm(const at::Tensor& a, const at::Tensor& w, const at::Tens
 
 at::Tensor moe_combine(const at::Tensor& ys, const at::Tensor& topk_w, const at::Tensor& tsr,
                        const c10::optional<at::Tensor>& shared) {
+  const int k_routed = (int)topk_w.size(1);
   check_cuda(ys, "ys");
   const int T = (int)tsr.size(0), k = (int)tsr.size(1);
   const int64_t H = ys.size(1);
@@ -246,8 +268,8 @@ at::Tensor moe_combine(const at::Tensor& ys, const at::Tensor& topk_w, const at:
     sp = shared->data_ptr();
   }
   c10::cuda::CUDAGuard g(ys.device());
-  launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), tsr.data_ptr<int32_t>(), T, k, (int)H,
-                     sp, dtype_code(ys), stream());
+  launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), tsr.data_ptr<int32_t>(), T, k, k_routed,
+                     (int)H, sp, dtype_code(ys), stream());
   return out;
 }
 
@@ -404,6 +426,8 @@ at::Tensor grouped_gemm_ex(const at::Tensor& a, const at::Tensor& w, const at::T
 }
 
 // ------------------------------------------------------------------ status
+int64_t gg_grid(int64_t n_items) { return grouped_gemm_grid((int)n_items); }
+
 int64_t read_status(int64_t device) { return status_tensor((int)device).item<int>(); }
 void reset_status(int64_t device) { status_tensor((int)device).zero_(); }
 at::Tensor status_word(int64_t device) { return status_tensor((int)device); }
@@ -420,9 +444,9 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("mla_cache_write(Tensor(a!) cache, Tensor kv_a, Tensor w, float eps, Tensor positions, Tensor cos_sin, "
         "Tensor slots, int L) -> ()");
   m.def("gqa_cache_write(Tensor(a!) kc, Tensor(b!) vc, Tensor k, Tensor v, Tensor slots) -> ()");
-  m.def("mla_decode(Tensor q, Tensor cache, Tensor block_table, Tensor seq_lens, float scale, int L, "
-        "int num_splits) -> Tensor");
-  m.def("moe_align(Tensor topk_ids, int e_local, int offset) -> Tensor[]");
+  m.def("mla_decode(Tensor q_lat, Tensor q_pe, Tensor cache, Tensor block_table, Tensor seq_lens, float scale, "
+        "int num_splits, bool head_major) -> Tensor");
+  m.def("moe_align(Tensor topk_ids, int e_local, int offset, int n_shared) -> Tensor[]");
   m.def("moe_gather(Tensor x, Tensor row_token, Tensor total) -> Tensor");
   m.def("grouped_gemm(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue) -> Tensor");
   m.def("moe_combine(Tensor ys, Tensor topk_w, Tensor token_slot_row, Tensor? shared) -> Tensor");
@@ -437,6 +461,7 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("grouped_gemm_scatter(Tensor a, Tensor w, Tensor offsets, Tensor counts, int w_experts, Tensor meta, Tensor rw, "
         "Tensor dst_ptrs, Tensor flag_ptrs, Tensor(a!) done_ctr, Tensor(b!) counts_reset, int[] cfg) -> ()");
   m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
+  m.def("grouped_gemm_grid(int n_items) -> int");
   m.def("read_status(int device) -> int");
   m.def("reset_status(int device) -> ()");
   m.def("status_word(int device) -> Tensor");
@@ -468,4 +493,5 @@ TORCH_LIBRARY_IMPL(afd_b200, CompositeExplicitAutograd, m) {
   m.impl("read_status", &read_status);
   m.impl("reset_status", &reset_status);
   m.impl("status_word", &status_word);
+  m.impl("grouped_gemm_grid", &gg_grid);
 }

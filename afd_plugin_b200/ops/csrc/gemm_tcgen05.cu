@@ -39,7 +39,8 @@ constexpr int kThreads = 6 * 32;
 constexpr int kWBytes = kBM * kBK * 2;          // 16 KB
 constexpr int kSubBytes = kSub * kBK * 2;       // 8 KB
 constexpr int kABytes = kMaxSub * kSubBytes;    // 32 KB
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kAccCols = 256;   // one accumulator: 128 lanes x 256 fp32 columns
+constexpr uint32_t kTmemCols = 512;  // two accumulators
 
 struct Smem {
   alignas(1024) uint8_t w[kStages][kWBytes];
@@ -47,8 +48,8 @@ struct Smem {
   float xchg[32 * 64];  // SwiGLU exchange: [col][row] for the 64 up rows
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t acc_full;
-  uint64_t acc_empty;
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
   uint32_t tmem_base;
 };
 
@@ -118,43 +119,56 @@ AFD_DEVICE void scatter_arrive(const ScatterParams& sp) {
   }
 }
 
+// Work item = (expert e, weight tile nt); items are ordered expert-major so the
+// CTAs working on one expert at the same time share its activation tiles in L2.
+struct Item {
+  int e, nt, cnt, seg;
+};
+
+AFD_DEVICE bool next_item(int& idx, int n_items, int n_tiles, const int32_t* counts, const int32_t* offsets,
+                          Item& it) {
+  for (; idx < n_items; idx += gridDim.x) {
+    const int e = idx / n_tiles;
+    const int c = counts[e];
+    if (c > 0) {
+      it.e = e;
+      it.nt = idx % n_tiles;
+      it.cnt = c;
+      it.seg = offsets[e];
+      idx += gridDim.x;
+      return true;
+    }
+  }
+  return false;
+}
+
+// Persistent grouped GEMM: one CTA per SM walks its work items; the TMA
+// producer runs ahead across item boundaries, the accumulator is double
+// buffered in TMEM (2 x 256 columns) so the epilogue of one item overlaps the
+// MMAs of the next.
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap a_map,
     __nv_bfloat16* __restrict__ d, const int32_t* __restrict__ offsets, const int32_t* __restrict__ counts, int n_w,
-    int w_stride_rows, int k_dim, int ld_d, int* __restrict__ status, const ScatterParams sp) {
-  const int e = blockIdx.y;
-  const int cnt = counts[e];
-  if (cnt == 0) {
-    if (EPI == 2 && threadIdx.x == 0) scatter_arrive(sp);
-    return;
-  }
-  const int seg = offsets[e];
+    int w_stride_rows, int k_dim, int ld_d, int n_tiles, int n_experts, int* __restrict__ status,
+    const ScatterParams sp) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const int nt = blockIdx.x;
   const int kb_total = k_dim / kBK;
-  const int n_pass = (cnt + kMaxSub * kSub - 1) / (kMaxSub * kSub);
-  // Weight rows of this tile (two 64-row halves).
-  int w_row0, w_row1;
-  if (EPI == 1) {
-    const int inter = n_w / 2;
-    w_row0 = e * w_stride_rows + nt * 64;
-    w_row1 = e * w_stride_rows + inter + nt * 64;
-  } else {
-    w_row0 = e * w_stride_rows + nt * kBM;
-    w_row1 = w_row0 + 64;
-  }
+  const int n_items = n_tiles * n_experts;
+  constexpr int kPassRows = kMaxSub * kSub;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    mbar_init(&sm.acc_full, 1);
-    mbar_init(&sm.acc_empty, 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -166,121 +180,149 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  bool ok = true;
+
+  auto w_rows = [&](const Item& it, int& r0, int& r1) {
+    if (EPI == 1) {
+      r0 = it.e * w_stride_rows + it.nt * 64;
+      r1 = it.e * w_stride_rows + n_w / 2 + it.nt * 64;
+    } else {
+      r0 = it.e * w_stride_rows + it.nt * kBM;
+      r1 = r0 + 64;
+    }
+  };
 
   if (warp == 0) {
     // ----------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tensormap(&w_map);
       prefetch_tensormap(&a_map);
-      int it = 0;
-      for (int p = 0; p < n_pass && ok; ++p) {
-        const int rows_left = cnt - p * kMaxSub * kSub;
-        const int n_sub = min(kMaxSub, (rows_left + kSub - 1) / kSub);
-        for (int kb = 0; kb < kb_total; ++kb, ++it) {
-          const int st = it % kStages;
-          if (it >= kStages && !mbar_wait_bounded(&sm.empty[st], ((it / kStages) - 1) & 1)) {
-            atomicExch(status, kStatusWaitTimeout);
-            ok = false;
-            break;
+      int it_count = 0, idx = blockIdx.x;
+      Item it;
+      bool ok = true;
+      while (ok && next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+        int r0, r1;
+        w_rows(it, r0, r1);
+        const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+        for (int p = 0; p < n_pass && ok; ++p) {
+          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
+            const int st = it_count % kStages;
+            if (!mbar_wait_bounded(&sm.empty[st], ((it_count / kStages) & 1) ^ 1)) {
+              atomicExch(status, kStatusWaitTimeout);
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&sm.full[st], kWBytes + n_sub * kSubBytes);
+            tma_load_2d(sm.w[st], &w_map, &sm.full[st], kb * kBK, r0);
+            tma_load_2d(sm.w[st] + kWBytes / 2, &w_map, &sm.full[st], kb * kBK, r1);
+            for (int s2 = 0; s2 < n_sub; ++s2)
+              tma_load_2d(sm.a[st] + s2 * kSubBytes, &a_map, &sm.full[st], kb * kBK, it.seg + p * kPassRows + s2 * kSub);
           }
-          mbar_expect_tx(&sm.full[st], kWBytes + n_sub * kSubBytes);
-          tma_load_2d(sm.w[st], &w_map, &sm.full[st], kb * kBK, w_row0);
-          tma_load_2d(sm.w[st] + kWBytes / 2, &w_map, &sm.full[st], kb * kBK, w_row1);
-          for (int s = 0; s < n_sub; ++s)
-            tma_load_2d(sm.a[st] + s * kSubBytes, &a_map, &sm.full[st], kb * kBK,
-                        seg + p * kMaxSub * kSub + s * kSub);
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      int it = 0;
-      for (int p = 0; p < n_pass && ok; ++p) {
-        const int rows_left = cnt - p * kMaxSub * kSub;
-        const int n_sub = min(kMaxSub, (rows_left + kSub - 1) / kSub);
-        const uint32_t idesc = make_idesc(kBM, n_sub * kSub);
-        if (p > 0 && !mbar_wait_bounded(&sm.acc_empty, (p - 1) & 1)) {
-          atomicExch(status, kStatusWaitTimeout);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        for (int kb = 0; kb < kb_total; ++kb, ++it) {
-          const int st = it % kStages;
-          if (!mbar_wait_bounded(&sm.full[st], (it / kStages) & 1)) {
+      int it_count = 0, acc_count = 0, idx = blockIdx.x;
+      Item it;
+      bool ok = true;
+      while (ok && next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+        const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+        for (int p = 0; p < n_pass && ok; ++p, ++acc_count) {
+          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          const uint32_t idesc = make_idesc(kBM, n_sub * kSub);
+          const int ab = acc_count & 1;
+          if (!mbar_wait_bounded(&sm.acc_empty[ab], ((acc_count >> 1) & 1) ^ 1)) {
             atomicExch(status, kStatusWaitTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t wa = smem_u32(sm.w[st]);
-          const uint32_t aa = smem_u32(sm.a[st]);
+          const uint32_t tacc = tmem + ab * kAccCols;
+          for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
+            const int st = it_count % kStages;
+            if (!mbar_wait_bounded(&sm.full[st], (it_count / kStages) & 1)) {
+              atomicExch(status, kStatusWaitTimeout);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t wa = smem_u32(sm.w[st]);
+            const uint32_t aa = smem_u32(sm.a[st]);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma(tmem, make_desc(wa + kk * 32), make_desc(aa + kk * 32), idesc, (kb | kk) != 0);
-          umma_commit(&sm.empty[st]);
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma(tacc, make_desc(wa + kk * 32), make_desc(aa + kk * 32), idesc, (kb | kk) != 0);
+            umma_commit(&sm.empty[st]);
+          }
+          if (ok) umma_commit(&sm.acc_full[ab]);
         }
-        if (ok) umma_commit(&sm.acc_full);
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;           // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;    // weight row within the tile
-    for (int p = 0; p < n_pass; ++p) {
-      if (!mbar_wait_bounded(&sm.acc_full, p & 1)) {
-        atomicExch(status, kStatusWaitTimeout);
-        break;
-      }
-      tc_fence_after();
-      const int rows_left = cnt - p * kMaxSub * kSub;
-      const int n_cols = min(kMaxSub * kSub, rows_left);
-      const int r_base = seg + p * kMaxSub * kSub;
-      for (int c0 = 0; c0 < n_cols; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, v);
-        if (EPI == 0) {
-          const int col = nt * kBM + row;
+    int acc_count = 0, idx = blockIdx.x;
+    Item it;
+    bool ok = true;
+    while (ok && next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+      const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+      for (int p = 0; p < n_pass; ++p, ++acc_count) {
+        const int ab = acc_count & 1;
+        if (!mbar_wait_bounded(&sm.acc_full[ab], (acc_count >> 1) & 1)) {
+          atomicExch(status, kStatusWaitTimeout);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int n_cols = min(kPassRows, it.cnt - p * kPassRows);
+        const int r_base = it.seg + p * kPassRows;
+        const uint32_t tacc = tmem + ab * kAccCols + ((uint32_t)(quarter * 32) << 16);
+        for (int c0 = 0; c0 < n_cols; c0 += 32) {
+          float v[32];
+          tmem_ld32(tacc + c0, v);
+          if (EPI == 0) {
+            const int col = it.nt * kBM + row;
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (c0 + j < n_cols) d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(v[j]);
-        } else if (EPI == 2) {
-          // routing weight applied, row stored into the source rank's slot (peer memory)
-          const int col = nt * kBM + row;
+            for (int j = 0; j < 32; ++j)
+              if (c0 + j < n_cols) d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(v[j]);
+          } else if (EPI == 2) {
+            // routing weight applied, row stored into the source rank's slot (peer memory)
+            const int col = it.nt * kBM + row;
 #pragma unroll 4
-          for (int j = 0; j < 32; ++j) {
-            if (c0 + j < n_cols) {
-              const int r = r_base + c0 + j;
-              const int m = sp.meta[r];
-              const int src = (m >> 24) & 0xFF, tok = (m >> 8) & 0xFFFF, slot = m & 0xFF;
-              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sp.dst_ptrs[src]);
-              dst[((size_t)tok * sp.J + slot) * sp.H + col] = __float2bfloat16_rn(sp.rw[r] * v[j]);
-            }
-          }
-        } else {
-          if (quarter >= 2) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) sm.xchg[j * 64 + (row - 64)] = v[j];
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (quarter < 2) {
-            const int col = nt * 64 + row;
-#pragma unroll
             for (int j = 0; j < 32; ++j) {
               if (c0 + j < n_cols) {
-                const float g = v[j];
-                const float u = sm.xchg[j * 64 + row];
-                d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
+                const int r = r_base + c0 + j;
+                const int m = sp.meta[r];
+                const int src = (m >> 24) & 0xFF, tok = (m >> 8) & 0xFFFF, slot = m & 0xFF;
+                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sp.dst_ptrs[src]);
+                dst[((size_t)tok * sp.J + slot) * sp.H + col] = __float2bfloat16_rn(sp.rw[r] * v[j]);
               }
             }
+          } else {
+            if (quarter >= 2) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sm.xchg[j * 64 + (row - 64)] = v[j];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (quarter < 2) {
+              const int col = it.nt * 64 + row;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (c0 + j < n_cols) {
+                  const float g = v[j];
+                  const float u = sm.xchg[j * 64 + row];
+                  d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
+                }
+              }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
         }
+        tc_fence_before();
+        if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
       }
-      tc_fence_before();
-      if (lane == 0) mbar_arrive(&sm.acc_empty);
     }
     if (EPI == 2) {
       __threadfence_system();
@@ -311,6 +353,16 @@ static void encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 
 using namespace afd;
 
+int grouped_gemm_grid(int n_items) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n_items < sms ? (n_items > 0 ? n_items : 1) : sms;
+}
+
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,
                          const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
                          int* status, cudaStream_t s, int w_experts, const ScatterParams* sp) {
@@ -322,21 +374,23 @@ void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* e
   const int w_stride = (w_experts == 1) ? 0 : n;
   ScatterParams none{};
   const ScatterParams& spv = sp ? *sp : none;
-  auto go = [&](auto epi_tag, dim3 grid, int ld) {
+  auto go = [&](auto epi_tag, int n_tiles, int ld) {
     constexpr int EPI = decltype(epi_tag)::value;
     static bool set = false;
     if (!set) {
       cudaFuncSetAttribute(gg::grouped_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       set = true;
     }
+    const int grid = grouped_gemm_grid(n_tiles * e_local);
     gg::grouped_gemm_kernel<EPI><<<grid, gg::kThreads, smem, s>>>(wmap, amap, (__nv_bfloat16*)d, expert_offsets,
-                                                                    expert_counts, n, w_stride, k, ld, status, spv);
+                                                                    expert_counts, n, w_stride, k, ld, n_tiles,
+                                                                    e_local, status, spv);
   };
   if (epilogue == 1) {
-    go(std::integral_constant<int, 1>{}, dim3((n / 2) / 64, e_local), n / 2);
+    go(std::integral_constant<int, 1>{}, (n / 2) / 64, n / 2);
   } else if (epilogue == 2) {
-    go(std::integral_constant<int, 2>{}, dim3(n / gg::kBM, e_local), n);
+    go(std::integral_constant<int, 2>{}, n / gg::kBM, n);
   } else {
-    go(std::integral_constant<int, 0>{}, dim3(n / gg::kBM, e_local), n);
+    go(std::integral_constant<int, 0>{}, n / gg::kBM, n);
   }
 }

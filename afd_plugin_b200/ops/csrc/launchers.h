@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stdint.h>
 
 enum AfdDType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
@@ -30,8 +31,19 @@ void launch_decode_advance(int32_t* input_ids, int64_t* positions, int64_t* slot
 // q [B, H, D] bf16 (D = L + R), cache [nblocks, bs, D] bf16, out [B, H, L] bf16.
 // Scratch (num_splits > 1): partial_o [B, splits, H, L] fp32, partial_lse [B, splits, H] fp32.
 // status: device int, set non-zero if a pipeline wait gave up.
+// Query halves and output addressed through element strides (batch, head):
+// the latent query and output may be head-major ([H, B, 512]) so the
+// absorbed up-projections run as plain batched GEMMs without copies.
+struct MlaQO {
+  const __nv_bfloat16* q_lat;
+  int64_t lat_sb, lat_sh;
+  const __nv_bfloat16* q_pe;
+  int64_t pe_sb, pe_sh;
+  __nv_bfloat16* out;
+  int64_t out_sb, out_sh;
+};
 int mla_decode_num_splits(int batch, int max_seq_len, int num_sms);
-void launch_mla_decode(void* out, const void* q, const void* cache, const int32_t* block_table,
+void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
                        const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                        int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
                        int num_splits, float scale, cudaStream_t s);
@@ -44,13 +56,13 @@ int gqa_decode_num_splits(int batch, int hkv, int max_seq_len, int num_sms);
 
 // ---- moe.cu
 // Routing bookkeeping for a grouped expert GEMM over experts [offset, offset+E_local).
-void launch_moe_align(const int32_t* topk_ids, int tokens, int k, int e_local, int offset, int pad_to,
+void launch_moe_align(const int32_t* topk_ids, int tokens, int k, int n_shared, int e_local, int offset,
                       int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_token, int32_t* row_slot,
                       int32_t* token_slot_row, int* total_rows, cudaStream_t s);
 void launch_moe_gather(void* xs, const void* x, const int32_t* row_token, int rows_cap, int hidden,
                        const int* total_rows, int dtype, cudaStream_t s);
 void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* token_slot_row, int tokens,
-                        int k, int hidden, const void* shared_out, int dtype, cudaStream_t s);
+                        int k, int k_routed, int hidden, const void* shared_out, int dtype, cudaStream_t s);
 
 // ---- afd_fused.cu
 struct DispatchParams {
@@ -111,6 +123,8 @@ struct ScatterParams {
 // Grouped GEMM D[r, n] = sum_k A[r, k] * W[e(r), n, k] over row segments of
 // experts (rows of expert e: [offsets[e], offsets[e] + counts[e])).
 // epilogue: 0 = store bf16, 1 = SiLU(gate) * up over paired halves (N = 2I -> I).
+// CTAs of a persistent grouped-GEMM launch over n_items (expert, tile) items.
+int grouped_gemm_grid(int n_items);
 // w_expert_rows: rows between consecutive experts in W (0 = one weight set
 // shared by every segment, e.g. shared experts / dense MLP over per-source segments).
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,

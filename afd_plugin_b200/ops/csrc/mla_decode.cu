@@ -54,8 +54,7 @@ AFD_DEVICE uint32_t swz(int row, int col, int box_bytes) {
 }
 
 __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
-    const __grid_constant__ CUtensorMap kv_map, __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ q,
-    const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
+    const __grid_constant__ CUtensorMap kv_map, const MlaQO qo, const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
     float* __restrict__ part_lse, int* __restrict__ status, int heads, int block_size, int max_blocks,
     int num_splits, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
@@ -79,12 +78,16 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
     }
     fence_barrier_init();
   }
-  // Q tile (16 heads x 576) -> swizzled smem, all threads.
-  const __nv_bfloat16* qb = q + ((size_t)b * heads + hg * kHeads) * kD;
+  // Q tile (16 heads x 576) -> swizzled smem, all threads.  The latent part
+  // and the rope part come from separate (strided) tensors.
   for (int c = threadIdx.x; c < kHeads * (kD / 8); c += kThreads) {
     const int r = c / (kD / 8);
     const int col = (c % (kD / 8)) * 8;
-    *reinterpret_cast<uint4*>(sm.q + swz(r, col, kQBoxBytes)) = *reinterpret_cast<const uint4*>(qb + r * kD + col);
+    const int h = hg * kHeads + r;
+    const __nv_bfloat16* src =
+        (col < kL) ? qo.q_lat + (size_t)b * qo.lat_sb + (size_t)h * qo.lat_sh + col
+                   : qo.q_pe + (size_t)b * qo.pe_sb + (size_t)h * qo.pe_sh + (col - kL);
+    *reinterpret_cast<uint4*>(sm.q + swz(r, col, kQBoxBytes)) = *reinterpret_cast<const uint4*>(src);
   }
   __syncthreads();
 
@@ -243,14 +246,13 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
   const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f;
   const float inv1 = l_run[1] > 0.f ? 1.f / l_run[1] : 0.f;
   if (num_splits == 1) {
-    __nv_bfloat16* ob = out + ((size_t)b * heads) * kL;
+    __nv_bfloat16* o0 = qo.out + (size_t)b * qo.out_sb + (size_t)h_lo * qo.out_sh;
+    __nv_bfloat16* o1 = qo.out + (size_t)b * qo.out_sb + (size_t)(h_lo + 8) * qo.out_sh;
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
       const int col = warp * 128 + n * 8 + qd * 2;
-      *reinterpret_cast<__nv_bfloat162*>(&ob[(size_t)h_lo * kL + col]) =
-          __floats2bfloat162_rn(o[n][0] * inv0, o[n][1] * inv0);
-      *reinterpret_cast<__nv_bfloat162*>(&ob[(size_t)(h_lo + 8) * kL + col]) =
-          __floats2bfloat162_rn(o[n][2] * inv1, o[n][3] * inv1);
+      *reinterpret_cast<__nv_bfloat162*>(&o0[col]) = __floats2bfloat162_rn(o[n][0] * inv0, o[n][1] * inv0);
+      *reinterpret_cast<__nv_bfloat162*>(&o1[col]) = __floats2bfloat162_rn(o[n][2] * inv1, o[n][3] * inv1);
     }
   } else {
     float* po = part_o + (((size_t)b * num_splits + split) * heads) * kL;
@@ -269,7 +271,7 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
 }
 
 // Merge split partials: out[b,h,:] = sum_s w_s o_s / sum_s w_s, w_s = 2^(lse_s - max).
-__global__ void mla_combine_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ part_o,
+__global__ void mla_combine_kernel(const MlaQO qo, const float* __restrict__ part_o,
                                    const float* __restrict__ part_lse, int heads, int num_splits, int L) {
   const int b = blockIdx.x, h = blockIdx.y;
   const float* pl = part_lse + (size_t)b * num_splits * heads + h;
@@ -293,7 +295,7 @@ __global__ void mla_combine_kernel(__nv_bfloat16* __restrict__ out, const float*
       acc.z += w * x.z;
       acc.w += w * x.w;
     }
-    __nv_bfloat16* ob = out + ((size_t)b * heads + h) * L + c;
+    __nv_bfloat16* ob = qo.out + (size_t)b * qo.out_sb + (size_t)h * qo.out_sh + c;
     *reinterpret_cast<__nv_bfloat162*>(ob) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
     *reinterpret_cast<__nv_bfloat162*>(ob + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
   }
@@ -326,7 +328,7 @@ int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
   return s > max_s ? max_s : s;
 }
 
-void launch_mla_decode(void* out, const void* q, const void* cache, const int32_t* block_table,
+void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
                        const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                        int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
                        int num_splits, float scale, cudaStream_t s) {
@@ -346,11 +348,10 @@ void launch_mla_decode(void* out, const void* q, const void* cache, const int32_
   }
   dim3 grid(batch, heads / mla::kHeads, num_splits);
   const float scale_log2 = scale * 1.4426950408889634f;
-  mla::mla_decode_kernel<<<grid, mla::kThreads, smem, s>>>(
-      map, (__nv_bfloat16*)out, (const __nv_bfloat16*)q, block_table, seq_lens, partial_o, partial_lse, status,
-      heads, block_size, max_blocks_per_seq, num_splits, scale_log2);
+  mla::mla_decode_kernel<<<grid, mla::kThreads, smem, s>>>(map, qo, block_table, seq_lens, partial_o, partial_lse,
+                                                            status, heads, block_size, max_blocks_per_seq, num_splits,
+                                                            scale_log2);
   if (num_splits > 1) {
-    mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>((__nv_bfloat16*)out, partial_o, partial_lse, heads,
-                                                               num_splits, L);
+    mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
   }
 }

@@ -12,22 +12,33 @@ namespace afd {
 
 constexpr int kMaxLocalExperts = 1024;
 
-__global__ void moe_align_kernel(const int32_t* __restrict__ ids, int n, int k, int e_local, int offset,
-                                 int32_t* __restrict__ counts_out, int32_t* __restrict__ offsets_out,
+// Entries are (token, slot) pairs: the routed ones (slot < k, expert from
+// `ids`) and, with n_shared > 0, every token's shared-expert chunks (slot
+// k + c, virtual expert e_local + c, weight 1).  Segments of the virtual
+// experts follow the routed ones.
+__global__ void moe_align_kernel(const int32_t* __restrict__ ids, int tokens, int k, int n_shared, int e_local,
+                                 int offset, int32_t* __restrict__ counts_out, int32_t* __restrict__ offsets_out,
                                  int32_t* __restrict__ row_token, int32_t* __restrict__ row_slot,
                                  int32_t* __restrict__ token_slot_row, int* __restrict__ total_rows) {
   __shared__ int cnt[kMaxLocalExperts];
   __shared__ int cur[kMaxLocalExperts];
-  for (int e = threadIdx.x; e < e_local; e += blockDim.x) cnt[e] = 0;
+  const int ks = k + n_shared;
+  const int e_all = e_local + n_shared;
+  const int n = tokens * ks;
+  auto expert_of = [&](int i) {
+    const int t = i / ks, j = i % ks;
+    return j < k ? ids[t * k + j] - offset : e_local + (j - k);
+  };
+  for (int e = threadIdx.x; e < e_all; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = ids[i] - offset;
-    if (e >= 0 && e < e_local) atomicAdd(&cnt[e], 1);
+    const int e = expert_of(i);
+    if (e >= 0 && e < e_all) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     int run = 0;
-    for (int e = 0; e < e_local; ++e) {
+    for (int e = 0; e < e_all; ++e) {
       cur[e] = run;
       offsets_out[e] = run;
       counts_out[e] = cnt[e];
@@ -37,11 +48,11 @@ __global__ void moe_align_kernel(const int32_t* __restrict__ ids, int n, int k, 
   }
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = ids[i] - offset;
-    if (e >= 0 && e < e_local) {
+    const int e = expert_of(i);
+    if (e >= 0 && e < e_all) {
       const int r = atomicAdd(&cur[e], 1);
-      row_token[r] = i / k;
-      row_slot[r] = i % k;
+      row_token[r] = i / ks;
+      row_slot[r] = i % ks;
       token_slot_row[i] = r;
     } else {
       token_slot_row[i] = -1;
@@ -64,9 +75,12 @@ __global__ void moe_gather_kernel(T* __restrict__ xs, const T* __restrict__ x, c
   }
 }
 
+// Slots j < k_routed carry routing weight w[t, j]; the remaining slots (shared
+// chunks) have weight 1.
 template <typename T>
 __global__ void moe_combine_kernel(T* __restrict__ out, const T* __restrict__ ys, const float* __restrict__ w,
-                                   const int32_t* __restrict__ tsr, int k, int hidden, const T* __restrict__ shared) {
+                                   const int32_t* __restrict__ tsr, int k, int k_routed, int hidden,
+                                   const T* __restrict__ shared) {
   constexpr int VN = Vec16<T>::N;
   const int t = blockIdx.x;
   for (int c = threadIdx.x; c < hidden / VN; c += blockDim.x) {
@@ -76,7 +90,7 @@ __global__ void moe_combine_kernel(T* __restrict__ out, const T* __restrict__ ys
     for (int j = 0; j < k; ++j) {
       const int r = tsr[t * k + j];
       if (r < 0) continue;
-      const float wj = w[t * k + j];
+      const float wj = j < k_routed ? w[t * k_routed + j] : 1.f;
       Vec16<T> y = load16(ys + (size_t)r * hidden + c * VN);
 #pragma unroll
       for (int i = 0; i < VN; ++i) acc[i] += wj * to_f32(y.v[i]);
@@ -104,10 +118,10 @@ using namespace afd;
     case kF16: { using T = __half; __VA_ARGS__; break; }            \
   }
 
-void launch_moe_align(const int32_t* topk_ids, int tokens, int k, int e_local, int offset, int /*pad_to*/,
+void launch_moe_align(const int32_t* topk_ids, int tokens, int k, int n_shared, int e_local, int offset,
                       int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_token, int32_t* row_slot,
                       int32_t* token_slot_row, int* total_rows, cudaStream_t s) {
-  moe_align_kernel<<<1, 1024, 0, s>>>(topk_ids, tokens * k, k, e_local, offset, expert_counts, expert_offsets,
+  moe_align_kernel<<<1, 1024, 0, s>>>(topk_ids, tokens, k, n_shared, e_local, offset, expert_counts, expert_offsets,
                                       row_token, row_slot, token_slot_row, total_rows);
 }
 
@@ -122,10 +136,10 @@ void launch_moe_gather(void* xs, const void* x, const int32_t* row_token, int ro
 }
 
 void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* token_slot_row, int tokens,
-                        int k, int hidden, const void* shared_out, int dtype, cudaStream_t s) {
+                        int k, int k_routed, int hidden, const void* shared_out, int dtype, cudaStream_t s) {
   AFD_DTYPE_SWITCH(dtype, T, {
     const int threads = hidden / Vec16<T>::N < 256 ? hidden / Vec16<T>::N : 256;
-    moe_combine_kernel<T><<<tokens, threads, 0, s>>>((T*)out, (const T*)ys, topk_w, token_slot_row, k, hidden,
-                                                     (const T*)shared_out);
+    moe_combine_kernel<T><<<tokens, threads, 0, s>>>((T*)out, (const T*)ys, topk_w, token_slot_row, k, k_routed,
+                                                     hidden, (const T*)shared_out);
   });
 }

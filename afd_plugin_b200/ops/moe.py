@@ -23,6 +23,7 @@ def moe_experts_cuda(
     w13_scale: torch.Tensor | None = None,
     w2_scale: torch.Tensor | None = None,
     shared_out: torch.Tensor | None = None,
+    n_shared: int = 0,
 ) -> torch.Tensor:
     if w13_scale is not None or w2_scale is not None:
         from afd_plugin_b200.ops import reference as ref
@@ -31,9 +32,9 @@ def moe_experts_cuda(
         w13 = torch.stack([ref.dequant_block(w13[e], w13_scale[e]) for e in range(w13.shape[0])]).to(x.dtype)
         w2 = torch.stack([ref.dequant_block(w2[e], w2_scale[e]) for e in range(w2.shape[0])]).to(x.dtype)
     C = _cuda_ops()
-    e_local = w13.shape[0]
+    e_local = w13.shape[0] - n_shared
     ids = topk_ids.to(torch.int32).contiguous()
-    counts, offsets, row_token, _row_slot, tsr, total = C.moe_align(ids, e_local, expert_offset)
+    counts, offsets, row_token, _row_slot, tsr, total = C.moe_align(ids, e_local, expert_offset, n_shared)
     xs = C.moe_gather(x.contiguous(), row_token, total)
     h = C.grouped_gemm(xs, w13, offsets, counts, 1)
     y = C.grouped_gemm(h, w2, offsets, counts, 0)

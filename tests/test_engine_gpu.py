@@ -10,11 +10,12 @@ from afd_plugin_b200.runtime.engine import LLMEngine
 pytestmark = pytest.mark.gpu
 
 
-def _engine(preset, *, eager, sizes=(8,), device="cuda", dtype=torch.bfloat16, max_len=256, seqs=8):
+def _engine(preset, *, eager, sizes=(8,), device="cuda", dtype=torch.bfloat16, max_len=256, seqs=8, init_on=None):
     arch = get_preset(preset)
     ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=eager, max_model_len=max_len),
                       compilation_config=CompilationConfig(cudagraph_capture_sizes=list(sizes)), max_num_seqs=seqs)
-    m = build_model(arch, role="colocated", dtype=dtype, device=device, seed=0, max_positions=max_len)
+    m = build_model(arch, role="colocated", dtype=dtype, device=device, seed=0, max_positions=max_len,
+                    init_on=init_on)
     return LLMEngine(ec, m)
 
 
@@ -42,7 +43,7 @@ def test_gpu_prefill_logits_track_fp32_reference():
     res = {}
     first_cpu = None
     for dev, dt in (("cpu", torch.float32), ("cuda", torch.bfloat16)):
-        e = _engine("tiny-dsv2-mla512", eager=True, device=dev, dtype=dt)
+        e = _engine("tiny-dsv2-mla512", eager=True, device=dev, dtype=dt, init_on="cpu")
         reqs = [Request(i, p, 1) for i, p in enumerate(prompts)]
         for r in reqs:
             e._ensure_blocks(r, len(r.prompt) + 2)
