@@ -1,0 +1,206 @@
+"""Connector microbenchmark: dispatch + combine round trip, fused vs NCCL.
+
+    torchrun --nproc-per-node A+F -m afd_plugin_b200.bench.connector_bench \
+        --attn A --ffn F [--tokens 1,2,4,...,1024] [--hidden 7168 --experts 256 --topk 8]
+
+Payload (BASELINE config #4): hidden-7168 bf16 rows, top-8 routing over 256
+experts from N(0, 1) logits with softmax weights.
+
+* ``fused``: Attention ranks run the fused dispatch kernel (norm, router,
+  top-k, per-expert peer stores); FFN ranks run a transport-only stand-in for
+  the expert GEMM (``afd_echo``: weight and store each row back into its
+  source slot) and the Attention ranks run ``afd_combine``.  Bytes over NVLink
+  per token: top-k rows each way.
+* ``nccl``: the reference wire protocol -- each Attention rank sends its
+  ``[T, H]`` hidden states to its FFN rank and receives ``[T, H]`` back
+  (NCCL send/recv).  Bytes per token: one row each way.
+
+Every number is CUDA-event timed per rank; the max over ranks is reported,
+with the achieved GB/s (bytes one Attention rank moves out and in) and the
+fraction of the NVLink roofline (measured 770 GB/s per direction per GPU).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+NVLINK_GBPS = 770.0
+
+
+def _args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--attn", type=int, default=1)
+    ap.add_argument("--ffn", type=int, default=1)
+    ap.add_argument("--tokens", default="1,2,4,8,16,32,64,128,256,512,1024")
+    ap.add_argument("--hidden", type=int, default=7168)
+    ap.add_argument("--experts", type=int, default=256)
+    ap.add_argument("--topk", type=int, default=8)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--paths", default="fused,nccl")
+    ap.add_argument("--out", default="")
+    return ap.parse_args(argv)
+
+
+def _max_over_ranks(x: float) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
+    from afd_plugin_b200.config import afd_config_from_mapping
+    from afd_plugin_b200.connectors.b200_fused import B200FusedAFDConnector
+    from afd_plugin_b200.engine_config import EngineConfig, ModelConfig
+    from afd_plugin_b200.models.configs import DSV3_32L
+    from afd_plugin_b200.parallel.topology import role_of_world_rank
+
+    A, F = args.attn, args.ffn
+    role, role_rank = role_of_world_rank(rank, attention_size=A, ffn_size=F)
+    arch = DSV3_32L.scaled(hidden_size=args.hidden, n_routed_experts=args.experts, num_experts_per_tok=args.topk,
+                           num_hidden_layers=1, quant=None, scoring_func="softmax", topk_method="greedy",
+                           n_shared_experts=0, routed_scaling_factor=1.0, norm_topk_prob=False)
+    t_cap = max(tokens)
+    afd = afd_config_from_mapping({
+        "role": role, "connector": "B200FusedAFDConnector", "num_attention_ranks": A, "num_ffn_ranks": F,
+        "connector_extra_config": {"max_tokens_per_rank": t_cap, "expert_capacity_factor": 4.0,
+                                   "wait_timeout_ms": 20000}})
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.bfloat16), additional_config={"afd": {}}, max_num_seqs=t_cap)
+    conn = B200FusedAFDConnector(rank, rank, ec, afd, role_rank)
+    conn.init_afd_connector()
+    C = torch.ops.afd_b200
+    d = conn.dims
+    H = args.hidden
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    gate_w = (torch.randn(args.experts, H, device="cuda", generator=g) / H ** 0.5).to(torch.bfloat16)
+    norm_w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+    results = []
+    for T in tokens:
+        x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+        res = torch.zeros_like(x)
+
+        def step_attn():
+            C.afd_epoch(conn.epoch[0:1])
+            r = res.clone()
+            cfg = [args.experts, args.topk, 0, 0, 1, 1, 1, 0, F, d.e_local, d.cap, d.t_cap, role_rank % d.ratio,
+                   role_rank // d.ratio, role_rank, 0]
+            C.afd_dispatch(x, r, norm_w, 1e-6, gate_w, None, 1.0, conn.dispatch_ptrs[0], conn.done[0, 0:1], cfg)
+            return C.afd_combine(conn.comb[0], T, args.topk, -1, conn.comb_flag[0], 0, conn.epoch[0:1], F,
+                                 conn.timeout_ns)
+
+        def step_ffn():
+            C.afd_epoch(conn.epoch[0:1])
+            C.afd_wait(conn.arrive[0], 0, conn.epoch[0:1], A, conn.timeout_ns)
+            C.afd_echo(conn.x_recv[0], conn.counts[0], conn.meta[0], conn.rw[0], conn.scatter_dst[0],
+                       conn.scatter_flags[0], conn.done[0, 1:2],
+                       [d.e_local, d.cap, d.ratio, d.t_cap, d.slots, A, 0])
+
+        fn = step_attn if role == "attention" else step_ffn
+        dist.barrier()
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / args.iters)
+        status = int(C.read_status(torch.cuda.current_device()))
+        bytes_per_attn = 2 * T * args.topk * H * 2  # out + back, per Attention rank
+        gbps = bytes_per_attn / (us * 1e-6) / 1e9
+        # roofline: each direction limited by one GPU's NVLink at NVLINK_GBPS
+        ideal_us = (T * args.topk * H * 2) / (NVLINK_GBPS * 1e9) * 1e6 * 2
+        results.append({"path": "fused", "tokens": T, "us": round(us, 2), "GBps": round(gbps, 1),
+                        "roofline_frac": round(ideal_us / us, 3), "status": status})
+    conn.close()
+    return results
+
+
+def bench_nccl(args, rank: int, tokens: list[int]) -> list[dict]:
+    from afd_plugin_b200.config import afd_config_from_mapping
+    from afd_plugin_b200.parallel.topology import build_rank_mapping, role_of_world_rank
+
+    A, F = args.attn, args.ffn
+    role, role_rank = role_of_world_rank(rank, attention_size=A, ffn_size=F)
+    m = build_rank_mapping(afd_config_from_mapping({"role": role, "num_attention_ranks": A, "num_ffn_ranks": F}),
+                           role_rank)
+    H = args.hidden
+    results = []
+    for T in tokens:
+        if role == "attention":
+            x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+            y = torch.empty_like(x)
+
+            def fn():
+                dist.send(x, dst=m.subgroup_ranks[0])
+                dist.recv(y, src=m.subgroup_ranks[0])
+        else:
+            peers = list(m.subgroup_ranks[1:])
+            bufs = [torch.empty(T, H, device="cuda", dtype=torch.bfloat16) for _ in peers]
+
+            def fn():
+                for p, b in zip(peers, bufs):
+                    dist.recv(b, src=p)
+                cat = torch.cat(bufs) if len(bufs) > 1 else bufs[0]
+                for i, p in enumerate(peers):
+                    dist.send(cat[i * T : (i + 1) * T].contiguous(), dst=p)
+
+        dist.barrier()
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / args.iters)
+        bytes_per_attn = 2 * T * H * 2
+        gbps = bytes_per_attn / (us * 1e-6) / 1e9
+        ideal_us = (T * H * 2 * (A // F)) / (NVLINK_GBPS * 1e9) * 1e6 * 2  # the FFN rank serves A/F peers
+        results.append({"path": "nccl", "tokens": T, "us": round(us, 2), "GBps": round(gbps, 1),
+                        "roofline_frac": round(ideal_us / us, 3)})
+    return results
+
+
+def main(argv=None) -> int:
+    args = _args(argv)
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
+    if dist.get_world_size() != args.attn + args.ffn:
+        raise SystemExit("world size must equal --attn + --ffn")
+    tokens = [int(t) for t in args.tokens.split(",")]
+    rows = []
+    for path in args.paths.split(","):
+        rows += bench_fused(args, rank, tokens) if path == "fused" else bench_nccl(args, rank, tokens)
+    if rank == 0:
+        topo = f"{args.attn}A{args.ffn}F"
+        for r in rows:
+            r["topology"] = topo
+            print(json.dumps(r))
+        if args.out:
+            with open(args.out, "a") as fh:
+                for r in rows:
+                    fh.write(json.dumps(r) + "\n")
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

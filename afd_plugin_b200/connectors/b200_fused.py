@@ -57,7 +57,7 @@ from afd_plugin_b200.parallel.symm_heap import HeapLayout
 from afd_plugin_b200.parallel.topology import build_rank_mapping
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor
 
-_EXTRA_KEYS = {"max_tokens_per_rank", "wait_timeout_ms", "fp8_dispatch"}
+_EXTRA_KEYS = {"max_tokens_per_rank", "wait_timeout_ms", "fp8_dispatch", "expert_capacity_factor"}
 
 
 @dataclass(frozen=True)
@@ -65,6 +65,10 @@ class B200FusedExtraInfo(ConnectorExtraInfo):
     max_tokens_per_rank: int | None = None  # per Attention rank and ubatch; default: max_num_seqs
     wait_timeout_ms: int = 5000
     fp8_dispatch: bool = False
+    # Receive rows per expert as a multiple of the mean load (None: worst case,
+    # every token of every Attention rank).  Overflowing rows are dropped and
+    # reported through the device status word.
+    expert_capacity_factor: float | None = None
 
     @classmethod
     def from_mapping(cls, raw: Mapping[str, Any] | None) -> "B200FusedExtraInfo":
@@ -77,6 +81,7 @@ class B200FusedExtraInfo(ConnectorExtraInfo):
                                  if "max_tokens_per_rank" in raw else None),
             wait_timeout_ms=coerce_extra_positive_int(raw.get("wait_timeout_ms", 5000), field_name="wait_timeout_ms"),
             fp8_dispatch=coerce_extra_bool(raw.get("fp8_dispatch", False), field_name="fp8_dispatch"),
+            expert_capacity_factor=_positive_float(raw.get("expert_capacity_factor")),
         )
         if out.fp8_dispatch:
             raise ValueError("B200FusedAFDConnector: fp8_dispatch is not available yet (bf16 rows are sent)")
@@ -84,7 +89,18 @@ class B200FusedExtraInfo(ConnectorExtraInfo):
 
     def to_mapping(self) -> dict[str, Any]:
         return {"max_tokens_per_rank": self.max_tokens_per_rank, "wait_timeout_ms": self.wait_timeout_ms,
-                "fp8_dispatch": self.fp8_dispatch}
+                "fp8_dispatch": self.fp8_dispatch, "expert_capacity_factor": self.expert_capacity_factor}
+
+
+def _positive_float(v) -> float | None:
+    if v is None or v == "":
+        return None
+    if isinstance(v, bool):
+        raise TypeError("expert_capacity_factor must be a number")
+    f = float(v)
+    if f <= 0:
+        raise ValueError(f"expert_capacity_factor must be positive, got {f}")
+    return f
 
 
 @dataclass(frozen=True)
@@ -99,6 +115,7 @@ class FusedLayout:
     experts: int
     top_k: int
     t_cap: int  # tokens per Attention rank per stage
+    capacity_factor: float | None = None
 
     @property
     def ratio(self) -> int:
@@ -110,8 +127,12 @@ class FusedLayout:
 
     @property
     def cap(self) -> int:
-        """Receive rows per routed expert (every token of every Attention rank)."""
-        return self.num_attn * self.t_cap
+        """Receive rows per routed expert (worst case: every token of every Attention rank)."""
+        worst = self.num_attn * self.t_cap
+        if self.capacity_factor is None:
+            return worst
+        mean = worst * self.top_k / max(1, self.experts)
+        return min(worst, int(self.capacity_factor * mean) + 64)
 
     @property
     def shared_row0(self) -> int:
@@ -176,7 +197,8 @@ class B200FusedAFDConnector(AFDConnectorBase):
         self.dims = FusedLayout(
             num_attn=self.attn_size, num_ffn=self.ffn_size, stages=stages, layers=arch.num_hidden_layers,
             hidden=arch.hidden_size, experts=max(arch.n_routed_experts, self.ffn_size),
-            top_k=max(arch.num_experts_per_tok, 1), t_cap=t_cap)
+            top_k=max(arch.num_experts_per_tok, 1), t_cap=t_cap,
+            capacity_factor=self.extra_info.expert_capacity_factor)
         self.timeout_ns = int(self.extra_info.wait_timeout_ms) * 1_000_000
         self.heap = None
         self.control_group = None

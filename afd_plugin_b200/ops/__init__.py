@@ -144,6 +144,8 @@ def gqa_decode(
     num_splits: int = 0,
 ) -> torch.Tensor:
     if _cuda(q):
+        if q.shape[-1] == 128 and q.shape[1] // k_cache.shape[2] <= 16 and k_cache.shape[1] % 32 == 0:
+            return _cuda_ops().gqa_decode(q.contiguous(), k_cache, v_cache, block_table, seq_lens, scale, num_splits)
         return _gqa_decode_torch(q, k_cache, v_cache, block_table, seq_lens, scale)
     return ref.gqa_decode(q, k_cache, v_cache, block_table, seq_lens, scale)
 

@@ -229,10 +229,53 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineParams p) {
   }
 }
 
+// Transport-only FFN stand-in for connector benchmarks: every received row is
+// weighted and stored back into its source rank's combine slot, exactly like
+// the scatter epilogue of the expert GEMM but without the math.
+__global__ void __launch_bounds__(kThreads) echo_kernel(EchoParams p) {
+  __shared__ int s_last;
+  const int VN = 8;
+  const int nv = p.H / VN;
+  const int n_seg = p.e_local + p.ratio;
+  for (int seg = blockIdx.y; seg < n_seg; seg += gridDim.y) {
+    const int cnt = p.counts[seg];
+    const int row0 = seg < p.e_local ? seg * p.cap : p.e_local * p.cap + (seg - p.e_local) * p.t_cap;
+    for (int i = blockIdx.x; i < cnt; i += gridDim.x) {
+      const int r = row0 + i;
+      const int m = p.meta[r];
+      const int src = (m >> 24) & 0xFF, tok = (m >> 8) & 0xFFFF, slot = m & 0xFF;
+      const float w = p.rw[r];
+      const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x) + (size_t)r * p.H;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.dst_ptrs[src]) + ((size_t)tok * p.J + slot) * p.H;
+      for (int v = threadIdx.x; v < nv; v += kThreads) {
+        Vec16<__nv_bfloat16> a = load16(x + v * VN);
+#pragma unroll
+        for (int j = 0; j < VN; ++j) a.v[j] = __float2bfloat16_rn(__bfloat162float(a.v[j]) * w);
+        store16(dst + v * VN, a);
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(p.done_ctr, 1u) == gridDim.x * gridDim.y - 1);
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    for (int i = 0; i < n_seg; ++i) p.counts[i] = 0;
+    *p.done_ctr = 0u;
+    __threadfence_system();
+    for (int a = 0; a < p.num_dst; ++a)
+      red_release_sys_add(reinterpret_cast<uint64_t*>(p.flag_ptrs[a]) + p.layer, 1ull);
+  }
+}
+
 }  // namespace fused
 }  // namespace afd
 
 using namespace afd;
+
+void launch_afd_echo(const EchoParams& p, cudaStream_t s) {
+  fused::echo_kernel<<<dim3(16, 148), fused::kThreads, 0, s>>>(p);
+}
 
 void launch_afd_epoch(uint64_t* epoch, cudaStream_t s) { fused::epoch_kernel<<<1, 1, 0, s>>>(epoch); }
 

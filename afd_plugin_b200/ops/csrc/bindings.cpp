@@ -199,6 +199,37 @@ at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at:
   return out;
 }
 
+at::Tensor gqa_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& block_table,
+                      const at::Tensor& seq_lens, double scale, int64_t num_splits) {
+  check_cuda(q, "q");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && kc.scalar_type() == at::kBFloat16 && vc.scalar_type() == at::kBFloat16,
+              "gqa_decode: bf16 only");
+  TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "gqa_decode: contiguous tensors");
+  TORCH_CHECK(q.size(2) == 128 && kc.size(3) == 128, "gqa_decode: head_dim 128 only");
+  const int B = (int)q.size(0), hq = (int)q.size(1), hkv = (int)kc.size(2);
+  TORCH_CHECK(hq % hkv == 0 && hq / hkv <= 16, "gqa_decode: query group of at most 16 heads");
+  const int bs = (int)kc.size(1), nblocks = (int)kc.size(0), maxb = (int)block_table.size(1);
+  TORCH_CHECK(bs % 32 == 0 && block_table.stride(1) == 1, "gqa_decode: block size % 32, dense table rows");
+  auto out = at::empty_like(q);
+  if (B == 0) return out;
+  int splits = (int)num_splits;
+  if (splits <= 0) {
+    int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+    splits = gqa_decode_num_splits(B, hkv, maxb * bs, sms);
+  }
+  at::Tensor po, pl;
+  if (splits > 1) {
+    po = at::empty({B, splits, hq, 128}, q.options().dtype(at::kFloat));
+    pl = at::empty({B, splits, hq}, q.options().dtype(at::kFloat));
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  launch_gqa_decode(out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), block_table.data_ptr<int32_t>(),
+                    seq_lens.data_ptr<int32_t>(), splits > 1 ? po.data_ptr<float>() : nullptr,
+                    splits > 1 ? pl.data_ptr<float>() : nullptr, status_ptr(q), B, hq, hkv, 128, bs, nblocks,
+                    (int)block_table.stride(0), splits, (float)scale, stream());
+  return out;
+}
+
 // -------------------------------------------------------------------- MoE
 std::vector<at::Tensor> moe_align(const at::Tensor& topk_ids, int64_t e_local, int64_t offset, int64_t n_shared) {
   check_cuda(topk_ids, "topk_ids");
@@ -383,6 +414,31 @@ at::Tensor afd_combine(const at::Tensor& comb, int64_t T, int64_t n_routed, int6
   return out;
 }
 
+// cfg: [e_local, cap, ratio, t_cap, J, num_dst, layer]
+void afd_echo(const at::Tensor& x, at::Tensor& counts, const at::Tensor& meta, const at::Tensor& rw,
+              const at::Tensor& dst_ptrs, const at::Tensor& flag_ptrs, at::Tensor& done_ctr, std::vector<int64_t> cfg) {
+  check_cuda(x, "x");
+  TORCH_CHECK(cfg.size() == 7, "afd_echo: cfg has 7 entries");
+  EchoParams p{};
+  p.x = x.data_ptr();
+  p.counts = counts.data_ptr<int32_t>();
+  p.meta = meta.data_ptr<int32_t>();
+  p.rw = rw.data_ptr<float>();
+  p.dst_ptrs = dst_ptrs.data_ptr<int64_t>();
+  p.flag_ptrs = flag_ptrs.data_ptr<int64_t>();
+  p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  p.e_local = (int)cfg[0];
+  p.cap = (int)cfg[1];
+  p.ratio = (int)cfg[2];
+  p.t_cap = (int)cfg[3];
+  p.H = (int)x.size(-1);
+  p.J = (int)cfg[4];
+  p.num_dst = (int)cfg[5];
+  p.layer = (int)cfg[6];
+  c10::cuda::CUDAGuard g(x.device());
+  launch_afd_echo(p, stream());
+}
+
 // Grouped GEMM whose epilogue scatters rows into peer combine buffers.
 // sp_ptrs (int64 [4]): meta, rw, dst_ptr_table, flag_ptr_table; sp_cfg: [J, H, total_ctas, num_dst, layer, n_reset]
 void grouped_gemm_scatter(const at::Tensor& a, const at::Tensor& w, const at::Tensor& offsets, const at::Tensor& counts,
@@ -446,6 +502,8 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("gqa_cache_write(Tensor(a!) kc, Tensor(b!) vc, Tensor k, Tensor v, Tensor slots) -> ()");
   m.def("mla_decode(Tensor q_lat, Tensor q_pe, Tensor cache, Tensor block_table, Tensor seq_lens, float scale, "
         "int num_splits, bool head_major) -> Tensor");
+  m.def("gqa_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor seq_lens, float scale, "
+        "int num_splits) -> Tensor");
   m.def("moe_align(Tensor topk_ids, int e_local, int offset, int n_shared) -> Tensor[]");
   m.def("moe_gather(Tensor x, Tensor row_token, Tensor total) -> Tensor");
   m.def("grouped_gemm(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue) -> Tensor");
@@ -462,6 +520,8 @@ TORCH_LIBRARY(afd_b200, m) {
         "Tensor dst_ptrs, Tensor flag_ptrs, Tensor(a!) done_ctr, Tensor(b!) counts_reset, int[] cfg) -> ()");
   m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
   m.def("grouped_gemm_grid(int n_items) -> int");
+  m.def("afd_echo(Tensor x, Tensor(a!) counts, Tensor meta, Tensor rw, Tensor dst_ptrs, Tensor flag_ptrs, "
+        "Tensor(b!) done_ctr, int[] cfg) -> ()");
   m.def("read_status(int device) -> int");
   m.def("reset_status(int device) -> ()");
   m.def("status_word(int device) -> Tensor");
@@ -476,6 +536,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("mla_cache_write", &mla_cache_write);
   m.impl("gqa_cache_write", &gqa_cache_write);
   m.impl("mla_decode", &mla_decode);
+  m.impl("gqa_decode", &gqa_decode);
   m.impl("moe_align", &moe_align);
   m.impl("moe_gather", &moe_gather);
   m.impl("grouped_gemm", &grouped_gemm);
@@ -487,6 +548,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("afd_combine", &afd_combine);
   m.impl("grouped_gemm_scatter", &grouped_gemm_scatter);
   m.impl("grouped_gemm_ex", &grouped_gemm_ex);
+  m.impl("afd_echo", &afd_echo);
 }
 
 TORCH_LIBRARY_IMPL(afd_b200, CompositeExplicitAutograd, m) {

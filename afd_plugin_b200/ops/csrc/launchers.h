@@ -49,9 +49,11 @@ void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_
                        int num_splits, float scale, cudaStream_t s);
 
 // ---- gqa_decode.cu
+// q [B, hq, 128], caches [blocks, bs, hkv, 128], out [B, hq, 128] (bf16).
 void launch_gqa_decode(void* out, const void* q, const void* kc, const void* vc, const int32_t* block_table,
-                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int batch, int hq, int hkv,
-                       int d, int block_size, int max_blocks_per_seq, int num_splits, float scale, cudaStream_t s);
+                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch, int hq,
+                       int hkv, int d, int block_size, int num_blocks, int max_blocks_per_seq, int num_splits,
+                       float scale, cudaStream_t s);
 int gqa_decode_num_splits(int batch, int hkv, int max_seq_len, int num_sms);
 
 // ---- moe.cu
@@ -98,6 +100,17 @@ struct CombineParams {
   int64_t timeout_ns;
   int* status;
 };
+struct EchoParams {
+  const void* x;             // received rows (stage base, local)
+  int32_t* counts;           // [e_local + ratio] (reset by the last CTA)
+  const int32_t* meta;
+  const float* rw;
+  const int64_t* dst_ptrs;   // [A] combine buffers (stage base)
+  const int64_t* flag_ptrs;  // [A] combine counters (stage base)
+  unsigned* done_ctr;
+  int e_local, cap, ratio, t_cap, H, J, num_dst, layer;
+};
+void launch_afd_echo(const EchoParams& p, cudaStream_t s);
 void launch_afd_epoch(uint64_t* epoch, cudaStream_t s);
 void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns, int* status,
                      cudaStream_t s);

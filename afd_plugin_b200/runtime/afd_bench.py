@@ -19,7 +19,7 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
                  e2e_loop, count_our_kernels) -> dict:
     from datetime import timedelta
 
-    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=600))
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=180))
     role, role_rank = role_of_world_rank(rank, attention_size=num_attn, ffn_size=num_ffn)
     if connector == "P2pNcclAFDConnector":
         args.eager = True  # NCCL p2p through torch.distributed is not captured into graphs here
@@ -32,10 +32,10 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         from afd_plugin_b200.runtime.workers import AFDFFNWorker
 
         w = AFDFFNWorker(ec, local_rank=local)
-        dist.barrier()
+        # Serve right away: the Attention side's warmup and graph capture already
+        # send control payloads.  The loop ends on the shutdown payload.
         with ClockSampler(local) as clk:
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            n = w.run_ffn_server_loop()  # until the Attention side's shutdown payload
+            n = w.run_ffn_server_loop()
         result.update(ms=0.0, per_step=[0.0], clocks=clk.summary(), steps_served=n)
         w.shutdown()
     else:
@@ -47,17 +47,17 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         if not args.eager:
             eng.capture_graphs()
         batch = len(eng.running)
-        dist.barrier()
+        grp = w.groups.attention_group
+        barrier = (lambda: dist.barrier(group=grp)) if num_attn > 1 else None
         with ClockSampler(local) as clk:
-            per_step, ms = device_loop(eng, batch, args.warmup, args.steps, args.isl, args.osl)
+            per_step, ms = device_loop(eng, batch, args.warmup, args.steps, args.isl, args.osl, barrier=barrier)
             e2e = None
             if not args.no_e2e:
                 e2e_ms, h2d, d2h = e2e_loop(eng, args.warmup, args.steps)
                 e2e = (e2e_ms, h2d, d2h)
         result.update(ms=ms, per_step=per_step, clocks=clk.summary(), e2e_raw=e2e, batch=batch)
-        grp = w.groups.attention_group
-        if grp is not None and num_attn > 1:
-            dist.barrier(group=grp)
+        if barrier is not None:
+            barrier()
         w.shutdown()
     # max over ranks of the device-timed loop and of the e2e wall time
     t = torch.tensor([result["ms"], (result.get("e2e_raw") or (0.0,))[0]], dtype=torch.float64, device="cuda")

@@ -38,6 +38,11 @@ sys.path.insert(0, ROOT)
 METRIC = "decode output tok/s (8xB200, max over ranks) + p50 TPOT, AFD vs NCCL connector"
 BASELINE_VALUE = None  # BASELINE.md publishes no GPU number for this metric
 TOPOLOGY = {1: (0, 0), 2: (1, 1), 4: (3, 1), 8: (6, 2)}
+MODEL_DESC = {
+    "deepseek-v2-lite": "DeepSeek-V2-Lite (27 layers, 64 experts top-6, MLA 16 heads)",
+    "qwen3-30b-a3b": "Qwen3-30B-A3B (48 layers, 128 experts top-8, GQA 32q/4kv)",
+    "deepseek-v3-32l": "DeepSeek-V3 shapes truncated to 32 layers (fp8 block-scaled experts)",
+}
 
 
 def parse_args(argv=None):
@@ -55,6 +60,7 @@ def parse_args(argv=None):
     ap.add_argument("--dbo", action="store_true", help="two-ubatch dual-batch overlap")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate layers (invalid as a bench)")
+    ap.add_argument("--topology", default="", help="override A,F split for N>1, e.g. 4,4 or 2,2")
     return ap.parse_args(argv)
 
 
@@ -136,8 +142,12 @@ def prime_requests(engine, n: int, isl: int, osl: int, seed: int = 0):
     engine.kv.fill_random_(seed=seed, std=1.0)
 
 
-def device_loop(engine, batch: int, warmup: int, steps: int, isl: int, osl: int):
-    """Graph replay + on-device advance; returns per-step ms list (events)."""
+def device_loop(engine, batch: int, warmup: int, steps: int, isl: int, osl: int, barrier=None):
+    """Graph replay + on-device advance; returns per-step ms list (events).
+
+    ``barrier`` (multi-rank) brackets the timed region together with a device
+    synchronize on both sides.
+    """
     runner = engine.runner
     use_graph = batch in runner.graphs
     wrap_at, wrap_to = isl + osl - 1, isl
@@ -150,6 +160,8 @@ def device_loop(engine, batch: int, warmup: int, steps: int, isl: int, osl: int)
     for _ in range(warmup):
         one()
     torch.cuda.synchronize()
+    if barrier is not None:
+        barrier()
     nvtx = os.environ.get("AFD_BENCH_NVTX") == "1"
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     if nvtx:
@@ -159,6 +171,8 @@ def device_loop(engine, batch: int, warmup: int, steps: int, isl: int, osl: int)
         one()
         ev[i + 1].record()
     torch.cuda.synchronize()
+    if barrier is not None:
+        barrier()
     if nvtx:
         torch.cuda.nvtx.range_pop()
     return [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)], ev[0].elapsed_time(ev[-1])
@@ -192,6 +206,10 @@ def main(argv=None) -> int:
     if args.gpus not in TOPOLOGY:
         raise SystemExit(f"unsupported --gpus {args.gpus}; use 1, 2, 4 or 8")
     num_attn, num_ffn = TOPOLOGY[args.gpus]
+    if args.topology:
+        num_attn, num_ffn = (int(x) for x in args.topology.split(","))
+        if num_attn + num_ffn != args.gpus:
+            raise SystemExit("--topology A,F must add up to --gpus")
     connector = {"auto": "P2pNcclAFDConnector", "nccl": "P2pNcclAFDConnector",
                  "b200": "B200FusedAFDConnector"}[args.connector]
     if args.connector == "auto":
@@ -256,7 +274,7 @@ def main(argv=None) -> int:
             "dtype": "bf16",
             "data": "synthetic (random-init weights; random prompt ids with synthetic prompt KV, decode only)",
             "config": {
-                "model": "DeepSeek-V2-Lite (27 layers, 64 experts top-6, MLA 16 heads)",
+                "model": MODEL_DESC.get(args.model, args.model),
                 "global_batch": args.batch,
                 "seq_len": args.isl + args.osl,
                 "input_len": args.isl,

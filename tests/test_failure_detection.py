@@ -1,0 +1,89 @@
+"""Failure detection without any GPU fault: host-side injected failures on gloo ranks."""
+
+import os
+import time
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from afd_plugin_b200.runtime.launcher import LocalAFDSpec, free_port, launch_local
+from afd_plugin_b200.runtime.watchdog import HeartbeatWatchdog
+
+
+def _prompts(n=3, length=12):
+    g = torch.Generator().manual_seed(0)
+    return torch.randint(0, 1024, (n, length), generator=g).tolist()
+
+
+def test_attention_rank_exception_surfaces_everywhere():
+    spec = LocalAFDSpec(afd={"num_attention_ranks": 1, "num_ffn_ranks": 1}, prompts=_prompts(), max_tokens=8,
+                        timeout_s=8, fault={"rank": 1, "kind": "raise", "at_step": 2})
+    t0 = time.time()
+    res = launch_local(spec, join_timeout_s=60)
+    assert time.time() - t0 < 60
+    assert "injected fault" in res[1]["error"]
+    assert "error" in res[0]  # the FFN rank learns of it (timeout / closed peer), it does not hang
+
+
+def test_ffn_rank_exit_surfaces_on_attention_side():
+    spec = LocalAFDSpec(afd={"num_attention_ranks": 1, "num_ffn_ranks": 1}, prompts=_prompts(), max_tokens=4,
+                        timeout_s=8, fault={"rank": 0, "kind": "exit_before_serve"})
+    res = launch_local(spec, join_timeout_s=60)
+    assert "error" in res[1]
+    assert "error" in res[0]
+
+
+def test_ffn_loop_error_reraised():
+    from afd_plugin_b200.runtime.workers import AFDFFNWorker
+
+    class Runner:
+        def serve(self, stop=None, max_steps=None):
+            raise ValueError("boom")
+
+    w = AFDFFNWorker.__new__(AFDFFNWorker)
+    w.device = torch.device("cpu")
+    w.model_runner = Runner()
+    w._thread = None
+    w._stop = None
+    w._error = None
+    w.start_ffn_server_loop()
+    w._thread.join(5)
+    with pytest.raises(RuntimeError, match="FFN worker loop failed"):
+        w.raise_ffn_loop_error_if_any()
+    w.raise_ffn_loop_error_if_any()  # cleared after raising
+    with pytest.raises(RuntimeError):
+        w.execute_model()
+
+
+def _hb_rank(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=20))
+    wd = HeartbeatWatchdog(store, rank, world, period_s=0.05, timeout_s=0.5).start()
+    if rank == 1:
+        time.sleep(0.3)
+        wd.stop()  # rank 1 "dies": stops beating but keeps the process alive for the store
+        time.sleep(2.0)
+        q.put((rank, []))
+        return
+    time.sleep(1.5)
+    dead = sorted(wd.dead_peers())
+    wd.stop()
+    q.put((rank, dead))
+    time.sleep(0.8)
+
+
+def test_heartbeat_watchdog_detects_silent_peer():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_hb_rank, args=(r, 3, port, q)) for r in range(3)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(30)
+    got = dict(q.get(timeout=5) for _ in range(3))
+    assert got[0] == [1] and got[2] == [1]

@@ -106,6 +106,21 @@ def test_mla_decode(heads, splits):
     _close(out, expect, 2e-2, 2e-2)
 
 
+@pytest.mark.parametrize("hq,hkv", [(32, 4), (8, 8), (16, 2)])
+@pytest.mark.parametrize("splits", [1, 0])
+def test_gqa_decode(hq, hkv, splits):
+    torch.manual_seed(hq + hkv + splits)
+    lens = [1, 30, 64, 65, 333]
+    B = len(lens)
+    kc, table, seq = _paged_cache(B, lens, hkv * 128)
+    kc = kc.view(kc.shape[0], kc.shape[1], hkv, 128)
+    vc = torch.randn_like(kc)
+    q = torch.randn(B, hq, 128, device=DEV, dtype=torch.bfloat16)
+    out = ops.gqa_decode(q, kc, vc, table, seq, 0.088, num_splits=splits)
+    expect = ref.gqa_decode(q.float(), kc.float(), vc.float(), table, seq, 0.088)
+    _close(out, expect, 2e-2, 2e-2)
+
+
 def test_mla_cache_write():
     T, L, R = 11, 512, 64
     kv_a = torch.randn(T, L + R, device=DEV, dtype=torch.bfloat16)
