@@ -67,18 +67,28 @@ class MLAAttention(nn.Module):
         self.kv_lora = arch.kv_lora_rank
         self.scale = arch.softmax_scale
         qk = arch.qk_head_dim
+        # The two projections that read the layer input (q or q_a, and
+        # kv_a_proj_with_mqa) share one weight so they run as one GEMM.
+        self.n_q_in = arch.q_lora_rank if arch.q_lora_rank else nh * qk
+        self.in_proj = _param((self.n_q_in + self.kv_lora + self.qk_rope, H), dtype, device)
         if arch.q_lora_rank:
-            self.q_a_proj = _param((arch.q_lora_rank, H), dtype, device)
             self.q_a_layernorm = RMSNorm(arch.q_lora_rank, arch.rms_norm_eps, dtype, device)
             self.q_b_proj = _param((nh * qk, arch.q_lora_rank), dtype, device)
-        else:
-            self.q_proj = _param((nh * qk, H), dtype, device)
-        self.kv_a_proj_with_mqa = _param((self.kv_lora + self.qk_rope, H), dtype, device)
         self.kv_a_layernorm = RMSNorm(self.kv_lora, arch.rms_norm_eps, dtype, device)
         # Absorbed up-projections derived from kv_b_proj at load time.
         self.w_uk = _param((nh, self.qk_nope, self.kv_lora), dtype, device)
         self.w_uv_t = _param((nh, self.kv_lora, self.v_dim), dtype, device)
         self.o_proj = _param((H, nh * self.v_dim), dtype, device)
+
+    @property
+    def q_proj(self) -> torch.Tensor:
+        return self.in_proj[: self.n_q_in]
+
+    q_a_proj = q_proj
+
+    @property
+    def kv_a_proj_with_mqa(self) -> torch.Tensor:
+        return self.in_proj[self.n_q_in :]
 
     def set_kv_b_proj(self, w: torch.Tensor) -> None:
         nh = self.num_heads
@@ -86,17 +96,19 @@ class MLAAttention(nn.Module):
         self.w_uk.data.copy_(w[:, : self.qk_nope, :])
         self.w_uv_t.data.copy_(w[:, self.qk_nope :, :].transpose(1, 2))
 
-    def project_q(self, h: torch.Tensor) -> torch.Tensor:
+    def project(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(q [T, H, qk], kv_a [T, kv_lora + rope])``; both may be strided views."""
+        y = ops.linear(h, self.in_proj)
+        kv_a = y[:, self.n_q_in :]
         if self.arch.q_lora_rank:
-            q = ops.linear(self.q_a_layernorm(ops.linear(h, self.q_a_proj)), self.q_b_proj)
+            q = ops.linear(self.q_a_layernorm(y[:, : self.n_q_in].contiguous()), self.q_b_proj)
         else:
-            q = ops.linear(h, self.q_proj)
-        return q.view(h.shape[0], self.num_heads, self.qk_nope + self.qk_rope)
+            q = y[:, : self.n_q_in]
+        return q.view(h.shape[0], self.num_heads, self.qk_nope + self.qk_rope), kv_a
 
     def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache: torch.Tensor, cos_sin: torch.Tensor):
         T = h.shape[0]
-        q = self.project_q(h)
-        kv_a = ops.linear(h, self.kv_a_proj_with_mqa)
+        q, kv_a = self.project(h)
         ops.mla_cache_write(
             kv_cache, kv_a, self.kv_a_layernorm.weight, self.kv_a_layernorm.eps,
             meta.positions, cos_sin, meta.slot_mapping, self.kv_lora,
@@ -217,6 +229,10 @@ class MoEGate(nn.Module):
 
     def route(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         a = self.arch
+        from afd_plugin_b200.models.routing_simulator import balanced_routing_enabled, balanced_topk
+
+        if balanced_routing_enabled():
+            return balanced_topk(logits.shape[0], a.n_routed_experts, a.num_experts_per_tok, device=logits.device)
         return ops.topk_route(
             logits,
             a.num_experts_per_tok,

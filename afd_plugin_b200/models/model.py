@@ -359,14 +359,15 @@ class AFDDeepseekV2ForCausalLM(AFDCausalLM):
 
     def _attn_specs(self, p: str, attn: MLAAttention) -> Iterator[ParamSpec]:
         a = self.arch
+        nq = attn.n_q_in
+        nkv = a.kv_lora_rank + a.qk_rope_head_dim
         if a.q_lora_rank:
-            yield ParamSpec(p + "q_a_proj.weight", tuple(attn.q_a_proj.shape), _copy(attn.q_a_proj))
+            yield ParamSpec(p + "q_a_proj.weight", (nq, a.hidden_size), _rows(attn.in_proj, 0, nq))
             yield ParamSpec(p + "q_a_layernorm.weight", (a.q_lora_rank,), _copy(attn.q_a_layernorm.weight), "ones")
             yield ParamSpec(p + "q_b_proj.weight", tuple(attn.q_b_proj.shape), _copy(attn.q_b_proj))
         else:
-            yield ParamSpec(p + "q_proj.weight", tuple(attn.q_proj.shape), _copy(attn.q_proj))
-        yield ParamSpec(p + "kv_a_proj_with_mqa.weight", tuple(attn.kv_a_proj_with_mqa.shape),
-                        _copy(attn.kv_a_proj_with_mqa))
+            yield ParamSpec(p + "q_proj.weight", (nq, a.hidden_size), _rows(attn.in_proj, 0, nq))
+        yield ParamSpec(p + "kv_a_proj_with_mqa.weight", (nkv, a.hidden_size), _rows(attn.in_proj, nq, nq + nkv))
         yield ParamSpec(p + "kv_a_layernorm.weight", (a.kv_lora_rank,), _copy(attn.kv_a_layernorm.weight), "ones")
         shape = (a.num_attention_heads * (a.qk_nope_head_dim + a.v_head_dim), a.kv_lora_rank)
         yield ParamSpec(p + "kv_b_proj.weight", shape, lambda t, _a=attn: _a.set_kv_b_proj(t.to(_a.w_uk.device, _a.w_uk.dtype)))

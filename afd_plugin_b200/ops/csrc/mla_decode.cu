@@ -134,9 +134,12 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
     const uint32_t kv_base = smem_u32(sm.kv[st]);
     const int tok0 = (tile_begin + i) * kTile;
 
-    // ---- S[16 x 8] for tokens 8*warp .. 8*warp+7
-    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 6
+    // ---- S[16 x 8] for tokens 8*warp .. 8*warp+7; four independent
+    // accumulators keep four MMA chains in flight instead of one.
+    float sacc4[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) sacc4[a][0] = sacc4[a][1] = sacc4[a][2] = sacc4[a][3] = 0.f;
+#pragma unroll
     for (int kk = 0; kk < kD / 16; kk += 2) {
       uint32_t a0[4], a1[4];
       {
@@ -152,9 +155,12 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
         const int c = kk * 16 + mi * 8;
         ldmatrix_x4(b0, b1, b2, b3, kv_base + swz(row, c, kBoxBytes));
       }
-      mma_bf16_16816(sacc, a0, b0, b1);
-      mma_bf16_16816(sacc, a1, b2, b3);
+      mma_bf16_16816(sacc4[(kk >> 1) & 3], a0, b0, b1);
+      mma_bf16_16816(sacc4[((kk >> 1) + 2) & 3], a1, b2, b3);
     }
+    float sacc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sacc[j] = (sacc4[0][j] + sacc4[1][j]) + (sacc4[2][j] + sacc4[3][j]);
     // scale + mask, publish to smem
     float* sS = sm.s[i & 1];
     {
@@ -321,6 +327,9 @@ using namespace afd;
 
 int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
   const int tiles = (max_seq_len + mla::kTile - 1) / mla::kTile;
+  // Splitting costs a partial-O round trip through HBM (and a combine launch),
+  // so split only when the batch alone leaves SMs idle.
+  if (batch * 2 >= 3 * num_sms) return 1;
   const int target = 2 * num_sms * 2;  // two resident CTAs per SM, ~two waves
   int s = (target + batch - 1) / batch;
   s = s < 1 ? 1 : s;

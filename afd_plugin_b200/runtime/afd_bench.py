@@ -16,10 +16,11 @@ from afd_plugin_b200.utils.clocks import ClockSampler
 
 
 def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_config, prime_requests, device_loop,
-                 e2e_loop, count_our_kernels) -> dict:
+                 e2e_loop, count_our_kernels, log=lambda msg: None) -> dict:
     from datetime import timedelta
 
     dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=180))
+    log("process group up")
     role, role_rank = role_of_world_rank(rank, attention_size=num_attn, ffn_size=num_ffn)
     if connector == "P2pNcclAFDConnector":
         args.eager = True  # NCCL p2p through torch.distributed is not captured into graphs here
@@ -32,6 +33,7 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         from afd_plugin_b200.runtime.workers import AFDFFNWorker
 
         w = AFDFFNWorker(ec, local_rank=local)
+        log("ffn worker ready, serving")
         # Serve right away: the Attention side's warmup and graph capture already
         # send control payloads.  The loop ends on the shutdown payload.
         with ClockSampler(local) as clk:
@@ -42,10 +44,13 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         from afd_plugin_b200.runtime.workers import AFDAttentionWorker
 
         w = AFDAttentionWorker(ec, local_rank=local)
+        log("attention worker ready")
         eng = w.engine
         prime_requests(eng, shares[role_rank], args.isl, args.osl, seed=role_rank)
+        log("requests primed")
         if not args.eager:
             eng.capture_graphs()
+            log("graphs captured")
         batch = len(eng.running)
         grp = w.groups.attention_group
         barrier = (lambda: dist.barrier(group=grp)) if num_attn > 1 else None
@@ -56,6 +61,7 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
                 e2e_ms, h2d, d2h = e2e_loop(eng, args.warmup, args.steps)
                 e2e = (e2e_ms, h2d, d2h)
         result.update(ms=ms, per_step=per_step, clocks=clk.summary(), e2e_raw=e2e, batch=batch)
+        log("timed loops done")
         if barrier is not None:
             barrier()
         w.shutdown()

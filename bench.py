@@ -190,8 +190,18 @@ def e2e_loop(engine, warmup: int, steps: int):
     return (time.perf_counter() - t0) * 1e3, engine.last_h2d_bytes, engine.last_d2h_bytes
 
 
+def _log(msg: str) -> None:
+    if os.environ.get("AFD_BENCH_VERBOSE") == "1":
+        print(f"[rank {os.environ.get('RANK', '0')}] {msg}", file=sys.stderr, flush=True)
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
+    trace_after = os.environ.get("AFD_BENCH_TRACE_AFTER")
+    if trace_after:
+        import faulthandler
+
+        faulthandler.dump_traceback_later(float(trace_after), exit=False)
     if args.impl == "reference":
         reference_arm(args)
         return 0
@@ -253,7 +263,7 @@ def main(argv=None) -> int:
 
         result = run_afd_rank(args, rank=rank, local=local, num_attn=num_attn, num_ffn=num_ffn, connector=connector,
                               build_config=build_config, prime_requests=prime_requests, device_loop=device_loop,
-                              e2e_loop=e2e_loop, count_our_kernels=count_our_kernels)
+                              e2e_loop=e2e_loop, count_our_kernels=count_our_kernels, log=_log)
     if rank == 0:
         ms = result["ms"]
         tokens_per_step = args.batch
