@@ -19,7 +19,9 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
                  e2e_loop, count_our_kernels, log=lambda msg: None) -> dict:
     from datetime import timedelta
 
-    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=180))
+    # Lazy NCCL init: with an eagerly bound device, new_group() becomes a
+    # communicator split that every rank must enter before any other traffic.
+    dist.init_process_group("nccl", timeout=timedelta(seconds=180))
     log("process group up")
     role, role_rank = role_of_world_rank(rank, attention_size=num_attn, ffn_size=num_ffn)
     if connector == "P2pNcclAFDConnector":
