@@ -7,10 +7,12 @@ Payload (BASELINE config #4): hidden-7168 bf16 rows, top-8 routing over 256
 experts from N(0, 1) logits with softmax weights.
 
 * ``fused``: Attention ranks run the fused dispatch kernel (norm, router,
-  top-k, per-expert peer stores); FFN ranks run a transport-only stand-in for
-  the expert GEMM (``afd_echo``: weight and store each row back into its
-  source slot) and the Attention ranks run ``afd_combine``.  Bytes over NVLink
-  per token: top-k rows each way.
+  top-k, one row per destination FFN rank + routing); FFN ranks run the
+  combine-send kernel in transport-only mode (each received row scaled by its
+  local routing weights and stored back into the source's slot, i.e. the
+  expert GEMMs replaced by identity) and the Attention ranks run
+  ``afd_combine``.  Bytes over NVLink per token: one row per destination FFN
+  rank each way (+ 8 bytes per routed expert of routing metadata).
 * ``nccl``: the reference wire protocol -- each Attention rank sends its
   ``[T, H]`` hidden states to its FFN rank and receives ``[T, H]`` back
   (NCCL send/recv).  Bytes per token: one row each way.
@@ -88,18 +90,20 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
         def step_attn():
             C.afd_epoch(conn.epoch[0:1])
             r = res.clone()
-            cfg = [args.experts, args.topk, 0, 0, 1, 1, 1, 0, F, d.e_local, d.cap, d.t_cap, role_rank % d.ratio,
-                   role_rank // d.ratio, role_rank, 0]
-            C.afd_dispatch(x, r, norm_w, 1e-6, gate_w, None, 1.0, conn.dispatch_ptrs[0], conn.done[0, 0:1], cfg)
-            return C.afd_combine(conn.comb[0], T, args.topk, -1, conn.comb_flag[0], 0, conn.epoch[0:1], F,
+            cfg = [args.experts, args.topk, 0, 0, 1, 1, 1, 0, F, d.e_local, d.t_cap, role_rank,
+                   role_rank // d.ratio, 0]
+            C.afd_dispatch(x, r, norm_w, 1e-6, gate_w, None, 1.0, conn.dispatch_ptrs[0], conn.fmask[0],
+                           conn.done[0, 0:1], cfg)
+            return C.afd_combine(conn.comb[0], conn.fmask[0], T, conn.comb_flag[0], 0, conn.epoch[0:1], F,
                                  conn.timeout_ns)
 
         def step_ffn():
             C.afd_epoch(conn.epoch[0:1])
             C.afd_wait(conn.arrive[0], 0, conn.epoch[0:1], A, conn.timeout_ns)
-            C.afd_echo(conn.x_recv[0], conn.counts[0], conn.meta[0], conn.rw[0], conn.scatter_dst[0],
-                       conn.scatter_flags[0], conn.done[0, 1:2],
-                       [d.e_local, d.cap, d.ratio, d.t_cap, d.slots, A, 0])
+            C.afd_combine_send(conn.tok[0], conn.rid[0], conn.rwt[0], conn.tcount[0], conn.comb_ptrs[0],
+                               conn.comb_flag_ptrs[0], conn.done[0, 2:3], H,
+                               [A, d.t_cap, args.topk, d.slots, d.e_local, role_rank * d.e_local, d.ratio,
+                                role_rank * d.ratio, 1, 0, role_rank, F, 0, 1])
 
         fn = step_attn if role == "attention" else step_ffn
         dist.barrier()
@@ -116,11 +120,21 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
         dist.barrier()
         us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / args.iters)
         status = int(C.read_status(torch.cuda.current_device()))
-        bytes_per_attn = 2 * T * args.topk * H * 2  # out + back, per Attention rank
+        # Rows this rank moved: one per (token, destination FFN rank) each way.
+        if role == "attention":
+            masks = conn.fmask[0, :T].cpu()
+            dest = sum(bin(int(m)).count("1") for m in masks)
+        else:
+            dest = 0
+        dest = int(_max_over_ranks(float(dest)))
+        bytes_per_attn = 2 * dest * H * 2 + 2 * T * args.topk * 8 * F  # rows out + back, routing metadata
         gbps = bytes_per_attn / (us * 1e-6) / 1e9
-        # roofline: each direction limited by one GPU's NVLink at NVLINK_GBPS
-        ideal_us = (T * args.topk * H * 2) / (NVLINK_GBPS * 1e9) * 1e6 * 2
+        # roofline: each direction limited by one GPU's NVLink; the busiest GPU is an FFN rank
+        # receiving from its share of the Attention ranks.
+        ffn_rows = dest * A / F
+        ideal_us = max(dest, ffn_rows) * H * 2 / (NVLINK_GBPS * 1e9) * 1e6
         results.append({"path": "fused", "tokens": T, "us": round(us, 2), "GBps": round(gbps, 1),
+                        "rows_per_token": round(dest / max(1, T), 2),
                         "roofline_frac": round(ideal_us / us, 3), "status": status})
     conn.close()
     return results
@@ -170,7 +184,7 @@ def bench_nccl(args, rank: int, tokens: list[int]) -> list[dict]:
         us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / args.iters)
         bytes_per_attn = 2 * T * H * 2
         gbps = bytes_per_attn / (us * 1e-6) / 1e9
-        ideal_us = (T * H * 2 * (A // F)) / (NVLINK_GBPS * 1e9) * 1e6 * 2  # the FFN rank serves A/F peers
+        ideal_us = (T * H * 2 * (A // F)) / (NVLINK_GBPS * 1e9) * 1e6  # the FFN rank serves A/F peers
         results.append({"path": "nccl", "tokens": T, "us": round(us, 2), "GBps": round(gbps, 1),
                         "roofline_frac": round(ideal_us / us, 3)})
     return results

@@ -1,20 +1,23 @@
 """B200 fused AFD connector: dispatch and combine inside the kernels, over NVLink.
 
-Data path (no library call, no host hop):
+Data path (no library call, no host hop), one token row over NVLink per
+FFN rank that needs it:
 
 * Attention rank, per layer and ubatch -- ``afd_dispatch``: residual add +
-  post-attention RMSNorm + router GEMV + top-k, then each routed copy of the
-  token is stored straight into the owning FFN rank's per-expert receive
-  segment (slot claimed with a system-scope atomic on that rank's counter),
-  plus one copy into the home FFN rank's shared-expert / dense segment.  The
-  last CTA bumps every FFN rank's arrival counter.
-* FFN rank -- ``afd_wait`` for all Attention ranks, tcgen05 grouped
-  ``gate_up`` GEMM (SwiGLU fused) over the receive segments, then the grouped
-  ``down`` GEMM whose epilogue multiplies by the routing weight and stores the
-  row into the originating Attention rank's combine slot (peer memory); the
-  last CTA bumps every Attention rank's combine counter.
-* Attention rank -- ``afd_combine`` waits for every FFN rank and sums each
-  token's slots.
+  post-attention RMSNorm + router GEMV + top-k; the normalised row is stored
+  once into each destination FFN rank's token buffer (ranks owning one of the
+  token's experts, plus the home rank for the shared expert / dense MLP), and
+  the routing (ids, weights) into every FFN rank.  The last CTA publishes the
+  token count and bumps every FFN rank's arrival counter.
+* FFN rank -- ``afd_wait`` for all Attention ranks; ``afd_expand`` copies
+  rows into per-expert segments (local HBM); tcgen05 grouped ``gate_up``
+  (SwiGLU fused) and ``down`` GEMMs, whose epilogue writes routing-weighted
+  rows into a local staging slot per (source, token, expert slot);
+  ``afd_combine_send`` sums each token's slots and stores ONE row into the
+  source Attention rank's combine slot for this FFN rank (peer memory), then
+  bumps every Attention rank's combine counter.
+* Attention rank -- ``afd_combine`` waits for every FFN rank and sums the
+  token's FFN slots.
 
 Routing always runs on the Attention side here (the Attention role loads the
 MoE gate), so expert parallelism across FFN ranks needs no FFN-side
@@ -135,12 +138,9 @@ class FusedLayout:
         return min(worst, int(self.capacity_factor * mean) + 64)
 
     @property
-    def shared_row0(self) -> int:
-        return self.e_local * self.cap
-
-    @property
     def rows(self) -> int:
-        return self.e_local * self.cap + self.ratio * self.t_cap
+        """Rows of the FFN-side per-expert segments."""
+        return self.e_local * self.cap
 
     @property
     def slots(self) -> int:
@@ -148,17 +148,18 @@ class FusedLayout:
         return self.top_k + 1
 
     def heap_layout(self) -> HeapLayout:
+        """Regions every rank maps (peers write into them)."""
         L = HeapLayout()
-        S = self.stages
-        L.add("x_recv", (S, self.rows, self.hidden), torch.bfloat16)
-        L.add("meta", (S, self.rows), torch.int32)
-        L.add("rw", (S, self.rows), torch.float32)
-        L.add("counts", (S, self.e_local + self.ratio), torch.int32)
-        L.add("arrive", (S, self.layers), torch.int64)
-        L.add("comb", (S, self.t_cap, self.slots, self.hidden), torch.bfloat16)
-        L.add("comb_flag", (S, self.layers), torch.int64)
-        L.add("epoch", (S,), torch.int64)  # per stage: steps that used the stage
-        L.add("done", (S, 2), torch.int32)
+        S, A, F = self.stages, self.num_attn, self.num_ffn
+        L.add("tok", (S, A, self.t_cap, self.hidden), torch.bfloat16)      # FFN side: token rows per source
+        L.add("rid", (S, A, self.t_cap, self.top_k), torch.int32)          # FFN side: routed expert ids
+        L.add("rwt", (S, A, self.t_cap, self.top_k), torch.float32)        # FFN side: routing weights
+        L.add("tcount", (S, A), torch.int32)                               # FFN side: tokens per source
+        L.add("arrive", (S, self.layers), torch.int64)                     # FFN side: dispatch arrivals
+        L.add("comb", (S, self.t_cap, F, self.hidden), torch.bfloat16)     # Attention side: one row per FFN rank
+        L.add("comb_flag", (S, self.layers), torch.int64)                  # Attention side: combine arrivals
+        L.add("epoch", (S,), torch.int64)
+        L.add("done", (S, 4), torch.int32)
         return L
 
     def stage_bytes(self, layout: HeapLayout, name: str) -> int:
@@ -234,28 +235,21 @@ class B200FusedAFDConnector(AFDConnectorBase):
 
     def _build_views(self) -> None:
         d, h = self.dims, self.heap
-        self.x_recv = h.view("x_recv")
-        self.meta = h.view("meta")
-        self.rw = h.view("rw")
-        self.counts = h.view("counts")
-        self.arrive = h.view("arrive")
-        self.comb = h.view("comb")
-        self.comb_flag = h.view("comb_flag")
-        self.epoch = h.view("epoch")
-        self.done = h.view("done")
+        for name in ("tok", "rid", "rwt", "tcount", "arrive", "comb", "comb_flag", "epoch", "done"):
+            setattr(self, name, h.view(name))
+        self.fmask = torch.zeros(d.stages, d.t_cap, dtype=torch.int32, device=self.device)
         F, A = d.num_ffn, d.num_attn
         ffn_world = list(range(F))
         attn_world = list(range(F, F + A))
         sb = lambda name: d.stage_bytes(self.layout, name)  # noqa: E731
-        # Attention side: [5, F] per stage -> x, meta, rw, counts, arrive on each FFN rank.
-        self.dispatch_ptrs = []
-        self.scatter_dst = []
-        self.scatter_flags = []
+        # Attention side, per stage: [5, F] -> tok, rid, rwt, tcount, arrive on each FFN rank.
+        # FFN side, per stage: comb / comb_flag on each Attention rank.
+        self.dispatch_ptrs, self.comb_ptrs, self.comb_flag_ptrs = [], [], []
         for s in range(d.stages):
-            rows = [h.ptr_table(ffn_world, n, s * sb(n)) for n in ("x_recv", "meta", "rw", "counts", "arrive")]
+            rows = [h.ptr_table(ffn_world, n, s * sb(n)) for n in ("tok", "rid", "rwt", "tcount", "arrive")]
             self.dispatch_ptrs.append(torch.stack(rows))
-            self.scatter_dst.append(h.ptr_table(attn_world, "comb", s * sb("comb")))
-            self.scatter_flags.append(h.ptr_table(attn_world, "comb_flag", s * sb("comb_flag")))
+            self.comb_ptrs.append(h.ptr_table(attn_world, "comb", s * sb("comb")))
+            self.comb_flag_ptrs.append(h.ptr_table(attn_world, "comb_flag", s * sb("comb_flag")))
 
     def close(self) -> None:
         if self.heap is not None:
@@ -352,22 +346,22 @@ class FusedAttentionExecutor(FFNExecutor):
             raise RuntimeError("fused dispatch needs the MoE gate on the Attention role")
         scoring, renorm, n_group, topk_group, k = _routing_cfg(a)
         has_shared = (not is_moe) or a.n_shared_experts > 0
-        cfg = [a.n_routed_experts if is_moe else 1, k, scoring, renorm, n_group, topk_group, int(is_moe),
-               int(has_shared), d.num_ffn, d.e_local, d.cap, d.t_cap, c.role_rank % d.ratio, c.role_rank // d.ratio,
-               c.role_rank, layer_idx]
+        cfg = [a.n_routed_experts if is_moe else 1, d.top_k, scoring, renorm, n_group, topk_group, int(is_moe),
+               int(has_shared), d.num_ffn, d.e_local, d.t_cap, c.role_rank, c.role_rank // d.ratio, layer_idx]
         gate_w = gate.weight if is_moe else layer.post_attention_layernorm.weight
         bias = gate.e_score_correction_bias if is_moe else None
         torch.ops.afd_b200.afd_dispatch(
             attn_out.contiguous(), residual, layer.post_attention_layernorm.weight, layer.post_attention_layernorm.eps,
-            gate_w, bias, float(a.routed_scaling_factor), c.dispatch_ptrs[stage_idx], c.done[stage_idx, 0:1], cfg)
-        return (T, residual, is_moe, has_shared)
+            gate_w, bias, float(a.routed_scaling_factor), c.dispatch_ptrs[stage_idx], c.fmask[stage_idx],
+            c.done[stage_idx, 0:1], cfg)
+        return (T, residual)
 
     def recv(self, layer_idx, handle, stage_idx):
-        T, residual, is_moe, has_shared = handle
+        T, residual = handle
         c, d = self.c, self.c.dims
         out = torch.ops.afd_b200.afd_combine(
-            c.comb[stage_idx], T, d.top_k if is_moe else 0, d.top_k if has_shared else -1, c.comb_flag[stage_idx],
-            layer_idx, c.epoch[stage_idx : stage_idx + 1], d.num_ffn, c.timeout_ns)
+            c.comb[stage_idx], c.fmask[stage_idx], T, c.comb_flag[stage_idx], layer_idx,
+            c.epoch[stage_idx : stage_idx + 1], d.num_ffn, c.timeout_ns)
         return out, residual
 
     def shutdown_remote(self) -> None:
@@ -379,7 +373,7 @@ class FusedAttentionExecutor(FFNExecutor):
 
 
 class FusedFFNRunner:
-    """FFN-side step: wait, tcgen05 grouped GEMMs, scatter to Attention ranks."""
+    """FFN-side step: wait, expand, tcgen05 grouped GEMMs, combine-send."""
 
     def __init__(self, model, connector: B200FusedAFDConnector, engine_config):
         from afd_plugin_b200.runtime.cuda_graph import validate_cuda_graph_mode
@@ -391,15 +385,34 @@ class FusedFFNRunner:
         self.use_cuda_graph = validate_cuda_graph_mode(engine_config, role="ffn").enabled
         d = connector.dims
         dev = self.device
+        S, A, H = d.stages, d.num_attn, d.hidden
+        self.f_rank = connector.role_rank
+        self.home_a0 = self.f_rank * d.ratio
+        self.e_offset = self.f_rank * d.e_local
+        # Local buffers (never touched by peers).
+        self.x = torch.empty(S, max(1, d.rows), H, dtype=torch.bfloat16, device=dev)
+        self.meta = torch.zeros(S, max(1, d.rows), dtype=torch.int32, device=dev)
+        self.rw = torch.zeros(S, max(1, d.rows), dtype=torch.float32, device=dev)
+        self.counts = torch.zeros(S, d.e_local + d.ratio, dtype=torch.int32, device=dev)
+        self.staging = torch.empty(S, A, d.t_cap, d.slots, H, dtype=torch.bfloat16, device=dev)
+        stage_stride = self.staging[0, 0].numel() * self.staging.element_size()
+        self.staging_ptrs = [
+            torch.tensor([self.staging[s].data_ptr() + a * stage_stride for a in range(A)], dtype=torch.int64,
+                         device=dev) for s in range(S)]
         self.off_routed = torch.arange(d.e_local, dtype=torch.int32, device=dev) * d.cap
-        self.off_shared = d.shared_row0 + torch.arange(d.ratio, dtype=torch.int32, device=dev) * d.t_cap
+        self.off_shared = torch.arange(d.ratio, dtype=torch.int32, device=dev) * d.t_cap
+        # Shared / dense rows are the home sources' token rows; their (source, token, slot) map is static.
+        t = torch.arange(d.t_cap, dtype=torch.int32)
+        self.meta_shared = torch.cat([((self.home_a0 + i) << 24) | (t << 8) | d.top_k for i in range(d.ratio)]).to(dev)
+        self.rw_shared = torch.ones(d.ratio * d.t_cap, dtype=torch.float32, device=dev)
+        self.no_flags = torch.zeros(1, dtype=torch.int64, device=dev)
         self._graphs: dict = {}
         self._pool = None
         self._prepare_weights()
         self.steps = 0
 
     def _prepare_weights(self) -> None:
-        """Per layer: routed (w13, w2) and the 'shared segment' weights (shared experts or dense MLP)."""
+        """Per layer: routed (w13, w2) and the home-token weights (shared experts or dense MLP)."""
         a = self.model.arch
         self.layer_w = []
         for i, layer in enumerate(self.model.layers):
@@ -418,22 +431,30 @@ class FusedFFNRunner:
     def _layer(self, layer_idx: int, s: int) -> None:
         c, d = self.c, self.c.dims
         C = torch.ops.afd_b200
-        C.afd_wait(c.arrive[s], layer_idx, c.epoch[s : s + 1], d.num_attn, c.timeout_ns)
-        x = c.x_recv[s]
-        counts = c.counts[s]
+        A, H = d.num_attn, d.hidden
+        C.afd_wait(c.arrive[s], layer_idx, c.epoch[s : s + 1], A, c.timeout_ns)
         w13, w2, sw13, sw2 = self.layer_w[layer_idx]
-        H = d.hidden
+        is_moe = w13 is not None
+        counts = self.counts[s]
+        C.afd_expand(c.tok[s], c.rid[s], c.rwt[s], c.tcount[s], self.x[s], self.meta[s], self.rw[s], counts,
+                     [A, d.t_cap, d.top_k, d.e_local, self.e_offset, d.cap, d.ratio, self.home_a0, int(is_moe)])
+        home_rows = c.tok[s][self.home_a0 : self.home_a0 + d.ratio].reshape(d.ratio * d.t_cap, H)
         launches = []
-        if w13 is not None:
-            h_r = C.grouped_gemm_ex(x, w13, self.off_routed, counts[: d.e_local], 1, d.e_local)
-            launches.append((h_r, w2, self.off_routed, counts[: d.e_local], d.e_local))
+        if is_moe:
+            h_r = C.grouped_gemm_ex(self.x[s], w13, self.off_routed, counts[: d.e_local], 1, d.e_local)
+            launches.append((h_r, w2, self.off_routed, counts[: d.e_local], d.e_local, self.meta[s], self.rw[s]))
         if sw13 is not None:
-            h_s = C.grouped_gemm_ex(x, sw13, self.off_shared, counts[d.e_local :], 1, 1)
-            launches.append((h_s, sw2, self.off_shared, counts[d.e_local :], 1))
-        total = sum(int(C.grouped_gemm_grid((H // 128) * int(cnt.numel()))) for _, _, _, cnt, _ in launches)
-        for h, w, off, cnt, wexp in launches:
-            C.grouped_gemm_scatter(h, w, off, cnt, wexp, c.meta[s], c.rw[s], c.scatter_dst[s], c.scatter_flags[s],
-                                   c.done[s, 1:2], counts, [d.slots, H, total, d.num_attn, layer_idx])
+            h_s = C.grouped_gemm_ex(home_rows, sw13, self.off_shared, counts[d.e_local :], 1, 1)
+            launches.append((h_s, sw2, self.off_shared, counts[d.e_local :], 1, self.meta_shared, self.rw_shared))
+        total = sum(int(C.grouped_gemm_grid((H // 128) * int(cnt.numel()))) for _, _, _, cnt, _, _, _ in launches)
+        for h, w, off, cnt, wexp, meta, rw in launches:
+            # Expert outputs land in local staging slots; the last CTA clears the counters.
+            C.grouped_gemm_scatter(h, w, off, cnt, wexp, meta, rw, self.staging_ptrs[s], self.no_flags,
+                                   c.done[s, 1:2], counts, [d.slots, H, total, 0, layer_idx])
+        C.afd_combine_send(self.staging[s], c.rid[s], c.rwt[s], c.tcount[s], c.comb_ptrs[s], c.comb_flag_ptrs[s],
+                           c.done[s, 2:3], H,
+                           [A, d.t_cap, d.top_k, d.slots, d.e_local, self.e_offset, d.ratio, self.home_a0,
+                            int(is_moe), int(sw13 is not None), self.f_rank, d.num_ffn, layer_idx, 0])
 
     def _step(self, stages) -> None:
         for s in stages:

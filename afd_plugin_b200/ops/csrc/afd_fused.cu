@@ -1,24 +1,30 @@
 // Fused Attention<->FFN transfer kernels over NVLink peer memory.
 //
-// afd_dispatch  (Attention side, one kernel per layer and ubatch)
+// Per-rank protocol: a token row crosses NVLink once per FFN rank that owns
+// one of its experts (or is its home rank for the shared expert / dense MLP)
+// and comes back as one pre-reduced row per such rank.
+//
+// afd_dispatch      (Attention side, per layer and ubatch)
 //   residual += attn_out; h = RMSNorm(residual) * w           (post-attn norm)
 //   logits = h . gate^T; (weight, expert) = top-k routing      (router)
-//   for every routed (token, k): claim a row of the owning FFN rank's
-//   per-expert receive segment with a system-scope atomic on that rank's
-//   counter, then store h (bf16, 16-byte stores) plus (source, token, slot)
-//   metadata and the routing weight straight into the peer's memory.  The
-//   token is also stored once into its home FFN rank's shared-expert /
-//   dense-MLP segment.  The last CTA publishes the shared-segment count and
-//   bumps every FFN rank's arrival counter (release, system scope).
-// afd_wait      one thread spins (bounded by globaltimer) until a counter
-//               reaches epoch * arrivals (acquire, system scope).
-// afd_combine   (Attention side) waits for every FFN rank's arrival and sums
-//               the k routed slots + the shared slot of each token.
-// afd_epoch     bumps the per-step epoch that all counters are compared to.
+//   h is stored (16-byte stores) into each destination FFN rank's token
+//   buffer; the token's routing (k ids + weights) goes to every FFN rank.  The
+//   last CTA publishes the token count and bumps every FFN rank's arrival
+//   counter (release, system scope).
+// afd_expand        (FFN side) copies each received row into the contiguous
+//   segment of every local expert it routes to (local HBM), building the
+//   grouped GEMM's row -> (source, token, slot) map.
+// afd_combine_send  (FFN side, after the expert GEMMs) sums a token's local
+//   expert outputs (+ shared expert) and stores one row into the source
+//   Attention rank's combine slot; the last CTA bumps every Attention rank's
+//   counter.
+// afd_combine       (Attention side) waits for every FFN rank and sums the
+//   token's FFN slots.
+// afd_wait / afd_epoch: bounded arrival wait and per-stage epoch bump.
 //
-// Counters only grow: the n-th step expects epoch n times the number of
-// arriving ranks, so graphs replay without resetting them.  No wait is
-// unbounded: on expiry the kernel records kStatusWaitTimeout and returns.
+// Counters only grow: the n-th use of a stage expects epoch[stage] * arrivals,
+// so captured graphs replay without resets.  No wait is unbounded: on expiry
+// a kernel records kStatusWaitTimeout and returns.
 #include "common.cuh"
 #include "launchers.h"
 #include "routing.cuh"
@@ -28,7 +34,7 @@ namespace fused {
 
 constexpr int kTPC = 4;         // tokens per dispatch CTA
 constexpr int kThreads = 256;
-constexpr int kMaxSlots = 17;   // top-k (<= 16) + one shared/dense slot
+constexpr int kMaxK = 16;
 
 AFD_DEVICE uint64_t ld_acquire_sys(const uint64_t* p) {
   uint64_t v;
@@ -49,6 +55,11 @@ AFD_DEVICE bool wait_flag(const uint64_t* flag, uint64_t target, int64_t timeout
   return true;
 }
 
+// CTA-wide 16-byte row copy of H bf16 elements.
+AFD_DEVICE void copy_row(__nv_bfloat16* dst, const __nv_bfloat16* src, int H) {
+  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) store16(dst + v * 8, load16(src + v * 8));
+}
+
 __global__ void epoch_kernel(uint64_t* epoch) { *epoch += 1; }
 
 __global__ void wait_kernel(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns,
@@ -61,9 +72,9 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(DispatchParams p) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(dsm);                      // [kTPC][H]
   float* logits = reinterpret_cast<float*>(dsm + (size_t)kTPC * p.H * 2);            // [kTPC][E]
-  __shared__ int s_row[kTPC][kMaxSlots];
-  __shared__ int s_dst[kTPC][kMaxSlots];
-  __shared__ float s_w[kTPC][kMaxSlots];
+  __shared__ int s_id[kTPC][kMaxK];
+  __shared__ float s_w[kTPC][kMaxK];
+  __shared__ unsigned s_mask[kTPC];
   __shared__ float s_red[kThreads / 32];
   __shared__ int s_last;
 
@@ -112,6 +123,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(DispatchParams p) {
   }
 
   // ---- router logits (gate rows read once per CTA for all its tokens)
+  if (threadIdx.x < kTPC) s_mask[threadIdx.x] = p.has_shared ? (1u << p.home_f) : 0u;
+  __syncthreads();
   if (p.moe && nt > 0) {
     for (int e = warp; e < p.E; e += kThreads / 32) {
       float acc[kTPC] = {0.f, 0.f, 0.f, 0.f};
@@ -134,49 +147,34 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(DispatchParams p) {
       }
     }
     __syncthreads();
-    // ---- top-k per token, one warp each
-    if (warp < nt) {
+    if (warp < nt) {  // top-k, one warp per token
       float w;
       int id;
       warp_route(logits + warp * p.E, p.gate_bias, p.E, p.k, p.scoring, p.renorm, p.n_group, p.topk_group, p.scale,
                  w, id);
       if (lane < p.k) {
-        const int f = id / p.e_local, le = id % p.e_local;
-        // claim a row in the owner's segment for expert `le`
-        int* cnt = reinterpret_cast<int*>(p.cnt_ptrs[f]);
-        const int slot = atomicAdd_system(cnt + le, 1);
-        s_row[warp][lane] = (slot < p.cap) ? le * p.cap + slot : -1;
-        s_dst[warp][lane] = f;
+        s_id[warp][lane] = id;
         s_w[warp][lane] = w;
-        if (slot >= p.cap) atomicExch(p.status, kStatusBadIndex);
+        atomicOr(&s_mask[warp], 1u << (id / p.e_local));
       }
     }
+    __syncthreads();
   }
-  const int n_route = p.moe ? p.k : 0;
-  const int n_slots = n_route + (p.has_shared ? 1 : 0);
-  if (threadIdx.x < nt && p.has_shared) {
-    const int i = threadIdx.x;
-    s_row[i][n_route] = p.e_local * p.cap + p.src_local * p.t_cap + (t0 + i);
-    s_dst[i][n_route] = p.home_f;
-    s_w[i][n_route] = 1.f;
-  }
-  __syncthreads();
 
-  // ---- stores into the FFN ranks' receive segments (peer memory)
+  // ---- stores into the FFN ranks (peer memory)
   for (int i = 0; i < nt; ++i) {
-    for (int j = 0; j < n_slots; ++j) {
-      const int row = s_row[i][j];
-      if (row < 0) continue;
-      const int f = s_dst[i][j];
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.x_ptrs[f]) + (size_t)row * p.H;
-      for (int v = threadIdx.x; v < nv; v += kThreads) store16(dst + v * VN, load16(hbuf + (size_t)i * p.H + v * VN));
-      if (threadIdx.x == 0) {
-        const int slot_id = (j == n_route) ? p.k : j;  // shared/dense output lands in slot k
-        reinterpret_cast<int32_t*>(p.meta_ptrs[f])[row] =
-            ((p.attn_rank & 0xFF) << 24) | (((t0 + i) & 0xFFFF) << 8) | (slot_id & 0xFF);
-        reinterpret_cast<float*>(p.w_ptrs[f])[row] = s_w[i][j];
+    const int t = t0 + i;
+    const unsigned mask = s_mask[i];
+    const size_t tok_off = (size_t)p.attn_rank * p.t_cap + t;
+    for (int f = 0; f < p.num_ffn; ++f) {
+      if (mask & (1u << f))
+        copy_row(reinterpret_cast<__nv_bfloat16*>(p.tok_ptrs[f]) + tok_off * p.H, hbuf + (size_t)i * p.H, p.H);
+      if (p.moe && threadIdx.x < p.k) {
+        reinterpret_cast<int32_t*>(p.rid_ptrs[f])[tok_off * p.k + threadIdx.x] = s_id[i][threadIdx.x];
+        reinterpret_cast<float*>(p.rwt_ptrs[f])[tok_off * p.k + threadIdx.x] = s_w[i][threadIdx.x];
       }
     }
+    if (threadIdx.x == 0) p.fmask[t] = (int32_t)mask;
   }
 
   // ---- completion: the last CTA publishes counts and arrives at every FFN rank
@@ -185,10 +183,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(DispatchParams p) {
   if (threadIdx.x == 0) s_last = (atomicAdd(p.done_ctr, 1u) == gridDim.x - 1);
   __syncthreads();
   if (s_last && threadIdx.x == 0) {
-    if (p.has_shared) {
-      int* cnt = reinterpret_cast<int*>(p.cnt_ptrs[p.home_f]);
-      atomicExch_system(cnt + p.e_local + p.src_local, p.T);
-    }
+    for (int f = 0; f < p.num_ffn; ++f) atomicExch_system(reinterpret_cast<int*>(p.tcount_ptrs[f]) + p.attn_rank, p.T);
     *p.done_ctr = 0u;
     __threadfence_system();
     for (int f = 0; f < p.num_ffn; ++f)
@@ -196,7 +191,114 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(DispatchParams p) {
   }
 }
 
-// out[t] = sum of the token's routed slots and its shared slot.
+// One CTA per (source, token): copy the row into every local expert segment it
+// routes to.  Counters start at zero (cleared after the previous use).
+__global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
+  __shared__ int s_row[kMaxK];
+  if (blockIdx.x == 0 && threadIdx.x < p.ratio) p.counts[p.e_local + threadIdx.x] = p.tcount[p.home_a0 + threadIdx.x];
+  if (!p.moe) return;
+  const __nv_bfloat16* tok = static_cast<const __nv_bfloat16*>(p.tok);
+  __nv_bfloat16* x = static_cast<__nv_bfloat16*>(p.x);
+  for (int pair = blockIdx.x; pair < p.A * p.t_cap; pair += gridDim.x) {
+    const int a = pair / p.t_cap, t = pair % p.t_cap;
+    if (t >= p.tcount[a]) continue;
+    const size_t base = (size_t)pair * p.k;
+    if (threadIdx.x < p.k) {
+      const int le = p.rid[base + threadIdx.x] - p.e_offset;
+      int row = -1;
+      if (le >= 0 && le < p.e_local) {
+        const int slot = atomicAdd(&p.counts[le], 1);
+        if (slot < p.cap) {
+          row = le * p.cap + slot;
+          p.meta[row] = (a << 24) | (t << 8) | threadIdx.x;
+          p.rw[row] = p.rwt[base + threadIdx.x];
+        } else {
+          atomicExch(p.status, kStatusBadIndex);
+        }
+      }
+      s_row[threadIdx.x] = row;
+    }
+    __syncthreads();
+    for (int j = 0; j < p.k; ++j)
+      if (s_row[j] >= 0) copy_row(x + (size_t)s_row[j] * p.H, tok + (size_t)pair * p.H, p.H);
+    __syncthreads();
+  }
+}
+
+// One CTA per (source, token): sum this rank's slots for the token and store
+// the row into the source's combine slot [t][f_rank].
+__global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParams p) {
+  __shared__ float s_w[kMaxK + 1];
+  __shared__ int s_any;
+  __shared__ int s_last;
+  const int VN = 8;
+  const int nv = p.H / VN;
+  for (int pair = blockIdx.x; pair < p.A * p.t_cap; pair += gridDim.x) {
+    const int a = pair / p.t_cap, t = pair % p.t_cap;
+    if (t >= p.tcount[a]) continue;
+    const bool home = p.has_shared && a >= p.home_a0 && a < p.home_a0 + p.ratio;
+    if (threadIdx.x == 0) s_any = home ? 1 : 0;
+    __syncthreads();
+    if (threadIdx.x <= p.k) {
+      float w = 0.f;  // weight of a slot this rank filled (1, or the routing weight in echo mode)
+      if (threadIdx.x < p.k) {
+        if (p.moe) {
+          const int le = p.rid[(size_t)pair * p.k + threadIdx.x] - p.e_offset;
+          if (le >= 0 && le < p.e_local) {
+            w = p.echo ? p.rwt[(size_t)pair * p.k + threadIdx.x] : 1.f;
+            atomicOr(&s_any, 1);
+          }
+        }
+      } else {
+        w = home ? 1.f : 0.f;
+      }
+      s_w[threadIdx.x] = w;
+    }
+    __syncthreads();
+    if (s_any) {
+      __nv_bfloat16* dst =
+          reinterpret_cast<__nv_bfloat16*>(p.dst_ptrs[a]) + ((size_t)t * p.num_ffn + p.f_rank) * p.H;
+      if (p.echo) {
+        float wsum = 0.f;
+        for (int j = 0; j <= p.k; ++j) wsum += s_w[j];
+        const __nv_bfloat16* row = static_cast<const __nv_bfloat16*>(p.staging) + (size_t)pair * p.H;
+        for (int v = threadIdx.x; v < nv; v += kThreads) {
+          Vec16<__nv_bfloat16> x = load16(row + v * VN);
+#pragma unroll
+          for (int q = 0; q < VN; ++q) x.v[q] = __float2bfloat16_rn(__bfloat162float(x.v[q]) * wsum);
+          store16(dst + v * VN, x);
+        }
+      } else {
+        const __nv_bfloat16* st = static_cast<const __nv_bfloat16*>(p.staging) + (size_t)pair * p.J * p.H;
+        for (int v = threadIdx.x; v < nv; v += kThreads) {
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int j = 0; j < p.J; ++j) {
+            if (s_w[j] == 0.f) continue;
+            Vec16<__nv_bfloat16> x = load16(st + (size_t)j * p.H + v * VN);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(x.v[q]);
+          }
+          Vec16<__nv_bfloat16> o;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) o.v[q] = __float2bfloat16_rn(acc[q]);
+          store16(dst + v * VN, o);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(p.done_ctr, 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    *p.done_ctr = 0u;
+    __threadfence_system();
+    for (int a = 0; a < p.A; ++a) red_release_sys_add(reinterpret_cast<uint64_t*>(p.flag_ptrs[a]) + p.layer, 1ull);
+  }
+}
+
+// out[t] = sum of the FFN slots that answer token t.
 __global__ void __launch_bounds__(kThreads) combine_kernel(CombineParams p) {
   __shared__ bool ok;
   if (threadIdx.x == 0) ok = wait_flag(p.flag + p.layer, (*p.epoch) * p.arrivals, p.timeout_ns);
@@ -208,16 +310,13 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineParams p) {
   const int VN = 8;
   const int nv = p.H / VN;
   for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
-    const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(p.comb) + (size_t)t * p.J * p.H;
+    const unsigned mask = (unsigned)p.fmask[t];
+    const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(p.comb) + (size_t)t * p.F * p.H;
     for (int v = threadIdx.x; v < nv; v += kThreads) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int j = 0; j < p.n_routed; ++j) {
-        Vec16<__nv_bfloat16> x = load16(base + (size_t)j * p.H + v * VN);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(x.v[q]);
-      }
-      if (p.shared_slot >= 0) {
-        Vec16<__nv_bfloat16> x = load16(base + (size_t)p.shared_slot * p.H + v * VN);
+      for (int f = 0; f < p.F; ++f) {
+        if (!(mask & (1u << f))) continue;
+        Vec16<__nv_bfloat16> x = load16(base + (size_t)f * p.H + v * VN);
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(x.v[q]);
       }
@@ -229,53 +328,10 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineParams p) {
   }
 }
 
-// Transport-only FFN stand-in for connector benchmarks: every received row is
-// weighted and stored back into its source rank's combine slot, exactly like
-// the scatter epilogue of the expert GEMM but without the math.
-__global__ void __launch_bounds__(kThreads) echo_kernel(EchoParams p) {
-  __shared__ int s_last;
-  const int VN = 8;
-  const int nv = p.H / VN;
-  const int n_seg = p.e_local + p.ratio;
-  for (int seg = blockIdx.y; seg < n_seg; seg += gridDim.y) {
-    const int cnt = p.counts[seg];
-    const int row0 = seg < p.e_local ? seg * p.cap : p.e_local * p.cap + (seg - p.e_local) * p.t_cap;
-    for (int i = blockIdx.x; i < cnt; i += gridDim.x) {
-      const int r = row0 + i;
-      const int m = p.meta[r];
-      const int src = (m >> 24) & 0xFF, tok = (m >> 8) & 0xFFFF, slot = m & 0xFF;
-      const float w = p.rw[r];
-      const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x) + (size_t)r * p.H;
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.dst_ptrs[src]) + ((size_t)tok * p.J + slot) * p.H;
-      for (int v = threadIdx.x; v < nv; v += kThreads) {
-        Vec16<__nv_bfloat16> a = load16(x + v * VN);
-#pragma unroll
-        for (int j = 0; j < VN; ++j) a.v[j] = __float2bfloat16_rn(__bfloat162float(a.v[j]) * w);
-        store16(dst + v * VN, a);
-      }
-    }
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(p.done_ctr, 1u) == gridDim.x * gridDim.y - 1);
-  __syncthreads();
-  if (s_last && threadIdx.x == 0) {
-    for (int i = 0; i < n_seg; ++i) p.counts[i] = 0;
-    *p.done_ctr = 0u;
-    __threadfence_system();
-    for (int a = 0; a < p.num_dst; ++a)
-      red_release_sys_add(reinterpret_cast<uint64_t*>(p.flag_ptrs[a]) + p.layer, 1ull);
-  }
-}
-
 }  // namespace fused
 }  // namespace afd
 
 using namespace afd;
-
-void launch_afd_echo(const EchoParams& p, cudaStream_t s) {
-  fused::echo_kernel<<<dim3(16, 148), fused::kThreads, 0, s>>>(p);
-}
 
 void launch_afd_epoch(uint64_t* epoch, cudaStream_t s) { fused::epoch_kernel<<<1, 1, 0, s>>>(epoch); }
 
@@ -293,6 +349,16 @@ void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s) {
     attr = smem;
   }
   fused::dispatch_kernel<<<grid, fused::kThreads, smem, s>>>(p);
+}
+
+static int pair_grid(int pairs) { return std::max(1, std::min(pairs, 148 * 8)); }
+
+void launch_afd_expand(const ExpandParams& p, cudaStream_t s) {
+  fused::expand_kernel<<<pair_grid(p.A * p.t_cap), fused::kThreads, 0, s>>>(p);
+}
+
+void launch_afd_combine_send(const CombineSendParams& p, cudaStream_t s) {
+  fused::combine_send_kernel<<<pair_grid(p.A * p.t_cap), fused::kThreads, 0, s>>>(p);
 }
 
 void launch_afd_combine(const CombineParams& p, cudaStream_t s) {

@@ -335,16 +335,16 @@ void afd_wait(const at::Tensor& flag, int64_t index, const at::Tensor& epoch, in
                   status_ptr(flag), stream());
 }
 
-// cfg (int64): [E, k, scoring, renorm, n_group, topk_group, moe, has_shared, num_ffn, e_local, cap, t_cap,
-//               src_local, home_f, attn_rank, layer]
+// cfg (int64): [E, k, scoring, renorm, n_group, topk_group, moe, has_shared, num_ffn, e_local, t_cap,
+//               attn_rank, home_f, layer]; ptrs [5, F]: tok, rid, rwt, tcount, arrive flags on each FFN rank.
 void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Tensor& norm_w, double eps,
                   const at::Tensor& gate_w, const c10::optional<at::Tensor>& gate_bias, double scale,
-                  const at::Tensor& ptrs, at::Tensor& done_ctr, std::vector<int64_t> cfg) {
+                  const at::Tensor& ptrs, at::Tensor& fmask, at::Tensor& done_ctr, std::vector<int64_t> cfg) {
   check_cuda(attn_out, "attn_out");
   TORCH_CHECK(attn_out.scalar_type() == at::kBFloat16 && residual.scalar_type() == at::kBFloat16,
               "afd_dispatch: bf16 activations");
   TORCH_CHECK(attn_out.is_contiguous() && residual.is_contiguous() && gate_w.is_contiguous(), "afd_dispatch: layout");
-  TORCH_CHECK(cfg.size() == 16, "afd_dispatch: cfg has 16 entries");
+  TORCH_CHECK(cfg.size() == 14, "afd_dispatch: cfg has 14 entries");
   TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.dim() == 2 && ptrs.size(0) == 5, "afd_dispatch: ptrs [5, F]");
   DispatchParams p{};
   p.attn_out = attn_out.data_ptr();
@@ -370,27 +370,89 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
   p.has_shared = (int)cfg[7];
   p.num_ffn = (int)cfg[8];
   p.e_local = (int)cfg[9];
-  p.cap = (int)cfg[10];
-  p.t_cap = (int)cfg[11];
-  p.src_local = (int)cfg[12];
-  p.home_f = (int)cfg[13];
-  p.attn_rank = (int)cfg[14];
-  p.layer = (int)cfg[15];
-  TORCH_CHECK(p.k <= 16 && p.H % 8 == 0 && p.T <= p.t_cap, "afd_dispatch: k <= 16, H % 8 == 0, T <= t_cap");
+  p.t_cap = (int)cfg[10];
+  p.attn_rank = (int)cfg[11];
+  p.home_f = (int)cfg[12];
+  p.layer = (int)cfg[13];
+  TORCH_CHECK(p.k <= 16 && p.H % 8 == 0 && p.T <= p.t_cap && p.num_ffn <= 32,
+              "afd_dispatch: k <= 16, H % 8 == 0, T <= t_cap, at most 32 FFN ranks");
   const int64_t* pt = ptrs.data_ptr<int64_t>();
   const int64_t F = ptrs.size(1);
-  p.x_ptrs = pt;
-  p.meta_ptrs = pt + F;
-  p.w_ptrs = pt + 2 * F;
-  p.cnt_ptrs = pt + 3 * F;
+  p.tok_ptrs = pt;
+  p.rid_ptrs = pt + F;
+  p.rwt_ptrs = pt + 2 * F;
+  p.tcount_ptrs = pt + 3 * F;
   p.flag_ptrs = pt + 4 * F;
+  p.fmask = fmask.data_ptr<int32_t>();
   p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
   p.status = status_ptr(attn_out);
   c10::cuda::CUDAGuard g(attn_out.device());
   launch_afd_dispatch(p, stream());
 }
 
-at::Tensor afd_combine(const at::Tensor& comb, int64_t T, int64_t n_routed, int64_t shared_slot, const at::Tensor& flags,
+// cfg: [A, t_cap, k, e_local, e_offset, cap, ratio, home_a0, moe]
+void afd_expand(const at::Tensor& tok, const at::Tensor& rid, const at::Tensor& rwt, const at::Tensor& tcount,
+                at::Tensor& x, at::Tensor& meta, at::Tensor& rw, at::Tensor& counts, std::vector<int64_t> cfg) {
+  check_cuda(tok, "tok");
+  TORCH_CHECK(cfg.size() == 9, "afd_expand: cfg has 9 entries");
+  ExpandParams p{};
+  p.tok = tok.data_ptr();
+  p.rid = rid.data_ptr<int32_t>();
+  p.rwt = rwt.data_ptr<float>();
+  p.tcount = tcount.data_ptr<int32_t>();
+  p.x = x.data_ptr();
+  p.meta = meta.data_ptr<int32_t>();
+  p.rw = rw.data_ptr<float>();
+  p.counts = counts.data_ptr<int32_t>();
+  p.A = (int)cfg[0];
+  p.t_cap = (int)cfg[1];
+  p.k = (int)cfg[2];
+  p.H = (int)tok.size(-1);
+  p.e_local = (int)cfg[3];
+  p.e_offset = (int)cfg[4];
+  p.cap = (int)cfg[5];
+  p.ratio = (int)cfg[6];
+  p.home_a0 = (int)cfg[7];
+  p.moe = (int)cfg[8];
+  p.status = status_ptr(tok);
+  c10::cuda::CUDAGuard g(tok.device());
+  launch_afd_expand(p, stream());
+}
+
+// cfg: [A, t_cap, k, J, e_local, e_offset, ratio, home_a0, moe, has_shared, f_rank, num_ffn, layer, echo]
+void afd_combine_send(const at::Tensor& staging, const at::Tensor& rid, const at::Tensor& rwt,
+                      const at::Tensor& tcount, const at::Tensor& dst_ptrs, const at::Tensor& flag_ptrs,
+                      at::Tensor& done_ctr, int64_t H, std::vector<int64_t> cfg) {
+  check_cuda(staging, "staging");
+  TORCH_CHECK(cfg.size() == 14, "afd_combine_send: cfg has 14 entries");
+  CombineSendParams p{};
+  p.staging = staging.data_ptr();
+  p.rid = rid.data_ptr<int32_t>();
+  p.rwt = rwt.data_ptr<float>();
+  p.tcount = tcount.data_ptr<int32_t>();
+  p.A = (int)cfg[0];
+  p.t_cap = (int)cfg[1];
+  p.k = (int)cfg[2];
+  p.J = (int)cfg[3];
+  p.H = (int)H;
+  p.e_local = (int)cfg[4];
+  p.e_offset = (int)cfg[5];
+  p.ratio = (int)cfg[6];
+  p.home_a0 = (int)cfg[7];
+  p.moe = (int)cfg[8];
+  p.has_shared = (int)cfg[9];
+  p.f_rank = (int)cfg[10];
+  p.num_ffn = (int)cfg[11];
+  p.layer = (int)cfg[12];
+  p.echo = (int)cfg[13];
+  p.dst_ptrs = dst_ptrs.data_ptr<int64_t>();
+  p.flag_ptrs = flag_ptrs.data_ptr<int64_t>();
+  p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  c10::cuda::CUDAGuard g(staging.device());
+  launch_afd_combine_send(p, stream());
+}
+
+at::Tensor afd_combine(const at::Tensor& comb, const at::Tensor& fmask, int64_t T, const at::Tensor& flags,
                        int64_t layer, const at::Tensor& epoch, int64_t arrivals, int64_t timeout_ns) {
   check_cuda(comb, "comb");
   TORCH_CHECK(comb.dim() == 3 && comb.is_contiguous() && comb.scalar_type() == at::kBFloat16, "afd_combine: comb");
@@ -398,11 +460,10 @@ at::Tensor afd_combine(const at::Tensor& comb, int64_t T, int64_t n_routed, int6
   CombineParams p{};
   p.out = out.data_ptr();
   p.comb = comb.data_ptr();
+  p.fmask = fmask.data_ptr<int32_t>();
   p.T = (int)T;
   p.H = (int)comb.size(2);
-  p.J = (int)comb.size(1);
-  p.n_routed = (int)n_routed;
-  p.shared_slot = (int)shared_slot;
+  p.F = (int)comb.size(1);
   p.flag = reinterpret_cast<const uint64_t*>(flags.data_ptr());
   p.layer = (int)layer;
   p.epoch = reinterpret_cast<const uint64_t*>(epoch.data_ptr());
@@ -412,31 +473,6 @@ at::Tensor afd_combine(const at::Tensor& comb, int64_t T, int64_t n_routed, int6
   c10::cuda::CUDAGuard g(comb.device());
   launch_afd_combine(p, stream());
   return out;
-}
-
-// cfg: [e_local, cap, ratio, t_cap, J, num_dst, layer]
-void afd_echo(const at::Tensor& x, at::Tensor& counts, const at::Tensor& meta, const at::Tensor& rw,
-              const at::Tensor& dst_ptrs, const at::Tensor& flag_ptrs, at::Tensor& done_ctr, std::vector<int64_t> cfg) {
-  check_cuda(x, "x");
-  TORCH_CHECK(cfg.size() == 7, "afd_echo: cfg has 7 entries");
-  EchoParams p{};
-  p.x = x.data_ptr();
-  p.counts = counts.data_ptr<int32_t>();
-  p.meta = meta.data_ptr<int32_t>();
-  p.rw = rw.data_ptr<float>();
-  p.dst_ptrs = dst_ptrs.data_ptr<int64_t>();
-  p.flag_ptrs = flag_ptrs.data_ptr<int64_t>();
-  p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
-  p.e_local = (int)cfg[0];
-  p.cap = (int)cfg[1];
-  p.ratio = (int)cfg[2];
-  p.t_cap = (int)cfg[3];
-  p.H = (int)x.size(-1);
-  p.J = (int)cfg[4];
-  p.num_dst = (int)cfg[5];
-  p.layer = (int)cfg[6];
-  c10::cuda::CUDAGuard g(x.device());
-  launch_afd_echo(p, stream());
 }
 
 // Grouped GEMM whose epilogue scatters rows into peer combine buffers.
@@ -513,15 +549,17 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("afd_epoch(Tensor(a!) epoch) -> ()");
   m.def("afd_wait(Tensor flag, int index, Tensor epoch, int arrivals, int timeout_ns) -> ()");
   m.def("afd_dispatch(Tensor attn_out, Tensor(a!) residual, Tensor norm_w, float eps, Tensor gate_w, Tensor? gate_bias, "
-        "float scale, Tensor ptrs, Tensor(b!) done_ctr, int[] cfg) -> ()");
-  m.def("afd_combine(Tensor comb, int T, int n_routed, int shared_slot, Tensor flags, int layer, Tensor epoch, "
-        "int arrivals, int timeout_ns) -> Tensor");
+        "float scale, Tensor ptrs, Tensor(b!) fmask, Tensor(c!) done_ctr, int[] cfg) -> ()");
+  m.def("afd_expand(Tensor tok, Tensor rid, Tensor rwt, Tensor tcount, Tensor(a!) x, Tensor(b!) meta, Tensor(c!) rw, "
+        "Tensor(d!) counts, int[] cfg) -> ()");
+  m.def("afd_combine_send(Tensor staging, Tensor rid, Tensor rwt, Tensor tcount, Tensor dst_ptrs, Tensor flag_ptrs, "
+        "Tensor(a!) done_ctr, int H, int[] cfg) -> ()");
+  m.def("afd_combine(Tensor comb, Tensor fmask, int T, Tensor flags, int layer, Tensor epoch, int arrivals, "
+        "int timeout_ns) -> Tensor");
   m.def("grouped_gemm_scatter(Tensor a, Tensor w, Tensor offsets, Tensor counts, int w_experts, Tensor meta, Tensor rw, "
         "Tensor dst_ptrs, Tensor flag_ptrs, Tensor(a!) done_ctr, Tensor(b!) counts_reset, int[] cfg) -> ()");
   m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
   m.def("grouped_gemm_grid(int n_items) -> int");
-  m.def("afd_echo(Tensor x, Tensor(a!) counts, Tensor meta, Tensor rw, Tensor dst_ptrs, Tensor flag_ptrs, "
-        "Tensor(b!) done_ctr, int[] cfg) -> ()");
   m.def("read_status(int device) -> int");
   m.def("reset_status(int device) -> ()");
   m.def("status_word(int device) -> Tensor");
@@ -548,7 +586,8 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("afd_combine", &afd_combine);
   m.impl("grouped_gemm_scatter", &grouped_gemm_scatter);
   m.impl("grouped_gemm_ex", &grouped_gemm_ex);
-  m.impl("afd_echo", &afd_echo);
+  m.impl("afd_expand", &afd_expand);
+  m.impl("afd_combine_send", &afd_combine_send);
 }
 
 TORCH_LIBRARY_IMPL(afd_b200, CompositeExplicitAutograd, m) {

@@ -67,6 +67,9 @@ void launch_moe_combine(void* out, const void* ys, const float* topk_w, const in
                         int k, int k_routed, int hidden, const void* shared_out, int dtype, cudaStream_t s);
 
 // ---- afd_fused.cu
+// Per-rank protocol: a token crosses NVLink once per FFN rank that owns one of
+// its experts (or is its home rank for the shared expert / dense MLP), and
+// comes back as one pre-reduced row per such FFN rank.
 struct DispatchParams {
   const void* attn_out;   // [T, H] bf16
   void* residual;         // [T, H] bf16, updated in place
@@ -79,42 +82,61 @@ struct DispatchParams {
   float scale;
   int T, H;
   int moe;         // route to experts (0 for dense layers)
-  int has_shared;  // also send to the home FFN rank's shared/dense segment
-  int num_ffn, e_local, cap, t_cap, src_local, home_f, attn_rank, layer;
-  const int64_t* x_ptrs;     // [F] receive rows (stage base) on each FFN rank
-  const int64_t* meta_ptrs;  // [F] int32 row metadata
-  const int64_t* w_ptrs;     // [F] fp32 row routing weights
-  const int64_t* cnt_ptrs;   // [F] int32 counters [e_local + ratio]
-  const int64_t* flag_ptrs;  // [F] uint64 arrival counters [layers]
-  unsigned* done_ctr;        // local CTA-completion counter
+  int has_shared;  // the home FFN rank also applies the shared expert / dense MLP
+  int num_ffn, e_local, t_cap, attn_rank, home_f, layer;
+  const int64_t* tok_ptrs;     // [F] token rows [A, t_cap, H] (stage base) on each FFN rank
+  const int64_t* rid_ptrs;     // [F] int32 [A, t_cap, k] routed expert ids
+  const int64_t* rwt_ptrs;     // [F] fp32 [A, t_cap, k] routing weights
+  const int64_t* tcount_ptrs;  // [F] int32 [A] tokens per source
+  const int64_t* flag_ptrs;    // [F] uint64 arrival counters [layers]
+  int32_t* fmask;              // local [t_cap]: FFN ranks that answer token t
+  unsigned* done_ctr;          // local CTA-completion counter
   int* status;
 };
+// FFN side: received token rows -> per-expert contiguous segments (local copies).
+struct ExpandParams {
+  const void* tok;        // [A, t_cap, H] (stage base, local)
+  const int32_t* rid;     // [A, t_cap, k]
+  const float* rwt;       // [A, t_cap, k]
+  const int32_t* tcount;  // [A]
+  void* x;                // [e_local * cap, H] expert segments
+  int32_t* meta;          // [e_local * cap] (src << 24 | token << 8 | slot)
+  float* rw;              // [e_local * cap]
+  int32_t* counts;        // [e_local + ratio]: routed rows, then home-source token counts
+  int A, t_cap, k, H, e_local, e_offset, cap, ratio, home_a0, moe;
+  int* status;
+};
+// FFN side: per (source, token) sum of this rank's expert outputs (+ shared),
+// one row stored into the source Attention rank's combine slot for this rank.
+struct CombineSendParams {
+  const void* staging;    // [A, t_cap, J, H] weighted expert outputs (local); or token rows in echo mode
+  const int32_t* rid;     // [A, t_cap, k]
+  const float* rwt;       // [A, t_cap, k] (echo mode)
+  const int32_t* tcount;  // [A]
+  int A, t_cap, k, J, H, e_local, e_offset, ratio, home_a0, moe, has_shared, f_rank, num_ffn, layer;
+  int echo;               // 1: transport-only stand-in (scale the token row by its local weights)
+  const int64_t* dst_ptrs;   // [A] combine buffers [t_cap, F, H] (stage base)
+  const int64_t* flag_ptrs;  // [A] combine counters [layers]
+  unsigned* done_ctr;
+};
 struct CombineParams {
-  void* out;          // [T, H] bf16
-  const void* comb;   // [T_cap, J, H] bf16 (stage base, local)
-  int T, H, J, n_routed, shared_slot;
-  const uint64_t* flag;  // [layers] (stage base, local)
+  void* out;              // [T, H] bf16
+  const void* comb;       // [t_cap, F, H] bf16 (stage base, local)
+  const int32_t* fmask;   // [t_cap]
+  int T, H, F;
+  const uint64_t* flag;   // [layers] (stage base, local)
   int layer;
   const uint64_t* epoch;
   uint64_t arrivals;
   int64_t timeout_ns;
   int* status;
 };
-struct EchoParams {
-  const void* x;             // received rows (stage base, local)
-  int32_t* counts;           // [e_local + ratio] (reset by the last CTA)
-  const int32_t* meta;
-  const float* rw;
-  const int64_t* dst_ptrs;   // [A] combine buffers (stage base)
-  const int64_t* flag_ptrs;  // [A] combine counters (stage base)
-  unsigned* done_ctr;
-  int e_local, cap, ratio, t_cap, H, J, num_dst, layer;
-};
-void launch_afd_echo(const EchoParams& p, cudaStream_t s);
 void launch_afd_epoch(uint64_t* epoch, cudaStream_t s);
 void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns, int* status,
                      cudaStream_t s);
 void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s);
+void launch_afd_expand(const ExpandParams& p, cudaStream_t s);
+void launch_afd_combine_send(const CombineSendParams& p, cudaStream_t s);
 void launch_afd_combine(const CombineParams& p, cudaStream_t s);
 
 // ---- gemm_tcgen05.cu

@@ -9,9 +9,9 @@ from afd_plugin_b200.connectors.b200_fused import B200FusedExtraInfo, FusedLayou
 def test_layout_sizes_6a2f():
     d = FusedLayout(num_attn=6, num_ffn=2, stages=1, layers=27, hidden=2048, experts=64, top_k=6, t_cap=43)
     assert d.ratio == 3 and d.e_local == 32 and d.cap == 258
-    assert d.rows == 32 * 258 + 3 * 43 and d.slots == 7
+    assert d.rows == 32 * 258 and d.slots == 7
     lay = d.heap_layout()
-    assert lay["x_recv"].nbytes == d.rows * 2048 * 2
+    assert lay["tok"].nbytes == 6 * 43 * 2048 * 2
     offs = sorted(r.offset for r in lay.regions.values())
     assert all(o % 256 == 0 for o in offs)
     assert lay.size < 64 * 2**20
