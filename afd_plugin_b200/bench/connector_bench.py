@@ -47,6 +47,8 @@ def _args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--paths", default="fused,nccl")
     ap.add_argument("--out", default="")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="time each kernel of single round trips (barrier between trips)")
     return ap.parse_args(argv)
 
 
@@ -106,6 +108,9 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
                                 role_rank * d.ratio, 1, 0, role_rank, F, 0, 1])
 
         fn = step_attn if role == "attention" else step_ffn
+        if args.breakdown:
+            results.append(_breakdown(args, role, T, conn, x, res, norm_w, gate_w, role_rank, d, A, F, H))
+            continue
         dist.barrier()
         for _ in range(args.warmup):
             fn()
@@ -138,6 +143,50 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
                         "roofline_frac": round(ideal_us / us, 3), "status": status})
     conn.close()
     return results
+
+
+def _breakdown(args, role, T, conn, x, res, norm_w, gate_w, role_rank, d, A, F, H) -> dict:
+    """Median per-kernel device time over single round trips (both sides aligned by a barrier)."""
+    import statistics
+
+    C = torch.ops.afd_b200
+    names = ["epoch", "dispatch", "combine"] if role == "attention" else ["epoch", "wait", "combine_send"]
+    rows = {n: [] for n in names}
+    for it in range(args.warmup + args.iters):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev[0].record()
+        C.afd_epoch(conn.epoch[0:1])
+        ev[1].record()
+        if role == "attention":
+            r = res.clone()
+            cfg = [args.experts, args.topk, 0, 0, 1, 1, 1, 0, F, d.e_local, d.t_cap, role_rank, role_rank // d.ratio, 0]
+            C.afd_dispatch(x, r, norm_w, 1e-6, gate_w, None, 1.0, conn.dispatch_ptrs[0], conn.fmask[0],
+                           conn.done[0, 0:1], cfg)
+            ev[2].record()
+            C.afd_combine(conn.comb[0], conn.fmask[0], T, conn.comb_flag[0], 0, conn.epoch[0:1], F, conn.timeout_ns)
+        else:
+            C.afd_wait(conn.arrive[0], 0, conn.epoch[0:1], A, conn.timeout_ns)
+            ev[2].record()
+            C.afd_combine_send(conn.tok[0], conn.rid[0], conn.rwt[0], conn.tcount[0], conn.comb_ptrs[0],
+                               conn.comb_flag_ptrs[0], conn.done[0, 2:3], H,
+                               [A, d.t_cap, args.topk, d.slots, d.e_local, role_rank * d.e_local, d.ratio,
+                                role_rank * d.ratio, 1, 0, role_rank, F, 0, 1])
+        ev[3].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            for i, n in enumerate(names):
+                rows[n].append(ev[i].elapsed_time(ev[i + 1]) * 1e3)
+    out = {"path": "fused-breakdown", "tokens": T}
+    for n in names:
+        out[n + "_us"] = round(statistics.median(rows[n]), 2)
+    gathered = [None] * dist.get_world_size()
+    dist.all_gather_object(gathered, out)
+    merged = {"path": "fused-breakdown", "tokens": T}
+    for g in gathered:
+        merged.update({k: v for k, v in g.items() if k.endswith("_us")})
+    return merged
 
 
 def bench_nccl(args, rank: int, tokens: list[int]) -> list[dict]:

@@ -410,6 +410,9 @@ class FusedFFNRunner:
         self._pool = None
         self._prepare_weights()
         self.steps = 0
+        # Set by benchmarks: count the kernels of the next eager step.
+        self.count_next_eager = False
+        self.kernels_per_step = 0
 
     def _prepare_weights(self) -> None:
         """Per layer: routed (w13, w2) and the home-token weights (shared experts or dense MLP)."""
@@ -483,6 +486,12 @@ class FusedFFNRunner:
             with torch.cuda.graph(g, pool=self._pool):
                 self._step(stages)
             self._graphs[key] = g
+            return
+        if self.count_next_eager and mode is AFDGraphRunMode.EAGER:
+            from afd_plugin_b200.utils.launch_count import count_afd_kernels
+
+            self.count_next_eager = False
+            self.kernels_per_step = count_afd_kernels(lambda: self._step(stages))
             return
         self._step(stages)
 

@@ -35,12 +35,14 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         from afd_plugin_b200.runtime.workers import AFDFFNWorker
 
         w = AFDFFNWorker(ec, local_rank=local)
+        w.model_runner.count_next_eager = True
         log("ffn worker ready, serving")
         # Serve right away: the Attention side's warmup and graph capture already
         # send control payloads.  The loop ends on the shutdown payload.
         with ClockSampler(local) as clk:
             n = w.run_ffn_server_loop()
-        result.update(ms=0.0, per_step=[0.0], clocks=clk.summary(), steps_served=n)
+        result.update(ms=0.0, per_step=[0.0], clocks=clk.summary(), steps_served=n,
+                      launches_local=w.model_runner.kernels_per_step * args.steps)
         w.shutdown()
     else:
         from afd_plugin_b200.runtime.workers import AFDAttentionWorker
@@ -50,6 +52,9 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         eng = w.engine
         prime_requests(eng, shares[role_rank], args.isl, args.osl, seed=role_rank)
         log("requests primed")
+        from bench import one_eager_step  # the same decode step the timed loop runs
+
+        per_step_kernels = count_our_kernels(lambda: one_eager_step(eng, len(eng.running)))
         if not args.eager:
             eng.capture_graphs()
             log("graphs captured")
@@ -62,20 +67,29 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
             if not args.no_e2e:
                 e2e_ms, h2d, d2h = e2e_loop(eng, args.warmup, args.steps)
                 e2e = (e2e_ms, h2d, d2h)
-        result.update(ms=ms, per_step=per_step, clocks=clk.summary(), e2e_raw=e2e, batch=batch)
+        result.update(ms=ms, per_step=per_step, clocks=clk.summary(), e2e_raw=e2e, batch=batch,
+                      launches_local=per_step_kernels * args.steps)
         log("timed loops done")
         if barrier is not None:
             barrier()
         w.shutdown()
-    # max over ranks of the device-timed loop and of the e2e wall time
-    t = torch.tensor([result["ms"], (result.get("e2e_raw") or (0.0,))[0]], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    result["ms"] = float(t[0])
-    if not args.no_e2e and role == "attention" and result.get("e2e_raw"):
-        _, h2d, d2h = result["e2e_raw"]
-        result["e2e"] = {"value": round(args.batch * args.steps / (float(t[1]) / 1e3), 1), "unit": "tok/s",
-                         "h2d_bytes_per_step": h2d * num_attn, "d2h_bytes_per_step": d2h * num_attn}
-    result["launches"] = None
+    # Max over ranks of the device-timed loop, its p50 step and the e2e wall time;
+    # sums of launches and host<->device bytes.
+    import statistics
+
+    p50 = statistics.median(result["per_step"]) if role == "attention" else 0.0
+    e2e_ms, h2d, d2h = result.get("e2e_raw") or (0.0, 0, 0)
+    mx = torch.tensor([result["ms"], e2e_ms, p50], dtype=torch.float64, device="cuda")
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    sm = torch.tensor([float(result.get("launches_local", 0)), float(h2d), float(d2h)], dtype=torch.float64,
+                      device="cuda")
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    result["ms"] = float(mx[0])
+    result["per_step"] = [float(mx[2])]
+    if not args.no_e2e and float(mx[1]) > 0:
+        result["e2e"] = {"value": round(args.batch * args.steps / (float(mx[1]) / 1e3), 1), "unit": "tok/s",
+                         "h2d_bytes_per_step": int(sm[1]), "d2h_bytes_per_step": int(sm[2])}
+    result["launches"] = int(sm[0])
     dist.barrier()
     dist.destroy_process_group()
     return result

@@ -49,6 +49,9 @@ class FFNModelRunner:
         self._pool = None
         self._ffn_counts: dict[int, tuple[int, ...]] = {}
         self.steps = 0
+        # Set by benchmarks: count the kernels of the next eager step.
+        self.count_next_eager = False
+        self.kernels_per_step = 0
 
     def _graph_capable(self) -> bool:
         return bool(getattr(self.connector, "supports_graph_capture", False))
@@ -72,6 +75,12 @@ class FFNModelRunner:
             return
         if mode is AFDGraphRunMode.CAPTURE and self.use_cuda_graph:
             self._capture(payload, key)
+            return
+        if self.count_next_eager and mode is AFDGraphRunMode.EAGER and self.device.type == "cuda":
+            from afd_plugin_b200.utils.launch_count import count_afd_kernels
+
+            self.count_next_eager = False
+            self.kernels_per_step = count_afd_kernels(lambda: self._ffn_forward(payload))
             return
         self._ffn_forward(payload)
 
