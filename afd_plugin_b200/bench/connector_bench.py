@@ -95,7 +95,7 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
             cfg = [args.experts, args.topk, 0, 0, 1, 1, 1, 0, F, d.e_local, d.t_cap, role_rank,
                    role_rank // d.ratio, 0]
             C.afd_dispatch(x, r, norm_w, 1e-6, gate_w, None, 1.0, conn.dispatch_ptrs[0], conn.fmask[0],
-                           conn.done[0, 0:1], cfg)
+                           conn.dctr[0], cfg)
             return C.afd_combine(conn.comb[0], conn.fmask[0], T, conn.comb_flag[0], 0, conn.epoch[0:1], F,
                                  conn.timeout_ns)
 
@@ -163,7 +163,7 @@ def _breakdown(args, role, T, conn, x, res, norm_w, gate_w, role_rank, d, A, F, 
             r = res.clone()
             cfg = [args.experts, args.topk, 0, 0, 1, 1, 1, 0, F, d.e_local, d.t_cap, role_rank, role_rank // d.ratio, 0]
             C.afd_dispatch(x, r, norm_w, 1e-6, gate_w, None, 1.0, conn.dispatch_ptrs[0], conn.fmask[0],
-                           conn.done[0, 0:1], cfg)
+                           conn.dctr[0], cfg)
             ev[2].record()
             C.afd_combine(conn.comb[0], conn.fmask[0], T, conn.comb_flag[0], 0, conn.epoch[0:1], F, conn.timeout_ns)
         else:

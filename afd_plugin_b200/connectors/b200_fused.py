@@ -238,6 +238,8 @@ class B200FusedAFDConnector(AFDConnectorBase):
         for name in ("tok", "rid", "rwt", "tcount", "arrive", "comb", "comb_flag", "epoch", "done"):
             setattr(self, name, h.view(name))
         self.fmask = torch.zeros(d.stages, d.t_cap, dtype=torch.int32, device=self.device)
+        # dispatch completion counters: [0] send kernel, [1:] router token tiles of 16
+        self.dctr = torch.zeros(d.stages, 1 + (d.t_cap + 15) // 16, dtype=torch.int32, device=self.device)
         F, A = d.num_ffn, d.num_attn
         ffn_world = list(range(F))
         attn_world = list(range(F, F + A))
@@ -353,7 +355,7 @@ class FusedAttentionExecutor(FFNExecutor):
         torch.ops.afd_b200.afd_dispatch(
             attn_out.contiguous(), residual, layer.post_attention_layernorm.weight, layer.post_attention_layernorm.eps,
             gate_w, bias, float(a.routed_scaling_factor), c.dispatch_ptrs[stage_idx], c.fmask[stage_idx],
-            c.done[stage_idx, 0:1], cfg)
+            c.dctr[stage_idx], cfg)
         return (T, residual)
 
     def recv(self, layer_idx, handle, stage_idx):

@@ -337,6 +337,8 @@ void afd_wait(const at::Tensor& flag, int64_t index, const at::Tensor& epoch, in
 
 // cfg (int64): [E, k, scoring, renorm, n_group, topk_group, moe, has_shared, num_ffn, e_local, t_cap,
 //               attn_rank, home_f, layer]; ptrs [5, F]: tok, rid, rwt, tcount, arrive flags on each FFN rank.
+// done_ctr: int32 [>= 1 + ceil(T / 16)], zero before the first use and left zero by every call
+// ([0] send-kernel completion, [1:] router token tiles).
 void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Tensor& norm_w, double eps,
                   const at::Tensor& gate_w, const c10::optional<at::Tensor>& gate_bias, double scale,
                   const at::Tensor& ptrs, at::Tensor& fmask, at::Tensor& done_ctr, std::vector<int64_t> cfg) {
@@ -374,8 +376,15 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
   p.attn_rank = (int)cfg[11];
   p.home_f = (int)cfg[12];
   p.layer = (int)cfg[13];
-  TORCH_CHECK(p.k <= 16 && p.H % 8 == 0 && p.T <= p.t_cap && p.num_ffn <= 32,
-              "afd_dispatch: k <= 16, H % 8 == 0, T <= t_cap, at most 32 FFN ranks");
+  TORCH_CHECK(p.k <= 16 && p.H % 16 == 0 && p.H <= 8192 && p.T <= p.t_cap && p.num_ffn <= 32 && p.E <= 512,
+              "afd_dispatch: k <= 16, H % 16 == 0, H <= 8192, T <= t_cap, at most 32 FFN ranks, E <= 512");
+  const int64_t tiles = (p.T + 15) / 16;
+  TORCH_CHECK(done_ctr.scalar_type() == at::kInt && done_ctr.is_contiguous() && done_ctr.numel() >= 1 + tiles,
+              "afd_dispatch: done counters need 1 + ceil(T / 16) int32 entries");
+  at::Tensor h_scratch = at::empty({std::max<int64_t>(p.T, 1), p.H}, attn_out.options());
+  at::Tensor logits = at::empty({std::max<int64_t>(p.T, 1), std::max(p.E, 1)}, attn_out.options().dtype(at::kFloat));
+  p.h = h_scratch.data_ptr();
+  p.logits = logits.data_ptr<float>();
   const int64_t* pt = ptrs.data_ptr<int64_t>();
   const int64_t F = ptrs.size(1);
   p.tok_ptrs = pt;
@@ -385,6 +394,7 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
   p.flag_ptrs = pt + 4 * F;
   p.fmask = fmask.data_ptr<int32_t>();
   p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  p.route_ctr = p.done_ctr + 1;
   p.status = status_ptr(attn_out);
   c10::cuda::CUDAGuard g(attn_out.device());
   launch_afd_dispatch(p, stream());

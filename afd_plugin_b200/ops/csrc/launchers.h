@@ -90,7 +90,10 @@ struct DispatchParams {
   const int64_t* tcount_ptrs;  // [F] int32 [A] tokens per source
   const int64_t* flag_ptrs;    // [F] uint64 arrival counters [layers]
   int32_t* fmask;              // local [t_cap]: FFN ranks that answer token t
-  unsigned* done_ctr;          // local CTA-completion counter
+  unsigned* done_ctr;          // local CTA-completion counter of the send kernel
+  unsigned* route_ctr;         // local [ceil(T / 16)] router completion counters (zero between uses)
+  void* h;                     // local scratch [T, H] bf16: normalised rows
+  float* logits;               // local scratch [T, E] fp32: router logits
   int* status;
 };
 // FFN side: received token rows -> per-expert contiguous segments (local copies).

@@ -57,8 +57,10 @@ def parse_args(argv=None):
     ap.add_argument("--osl", type=int, default=256)
     ap.add_argument("--connector", default="auto", choices=["auto", "b200", "nccl"])
     ap.add_argument("--eager", action="store_true", help="disable CUDA graphs")
-    ap.add_argument("--dbo", action="store_true", help="two-ubatch dual-batch overlap (default for N>1)")
-    ap.add_argument("--no-dbo", action="store_true", help="disable DBO for N>1")
+    ap.add_argument("--dbo", action="store_true",
+                    help="two-ubatch dual-batch overlap (off by default: the FFN step is weight-bandwidth bound, "
+                         "so a second ubatch re-reads every expert weight)")
+    ap.add_argument("--no-dbo", action="store_true", help="force DBO off")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate layers (invalid as a bench)")
     ap.add_argument("--topology", default="", help="override A,F split for N>1, e.g. 4,4 or 2,2")
@@ -217,8 +219,8 @@ def main(argv=None) -> int:
     if args.gpus not in TOPOLOGY:
         raise SystemExit(f"unsupported --gpus {args.gpus}; use 1, 2, 4 or 8")
     num_attn, num_ffn = TOPOLOGY[args.gpus]
-    if args.gpus > 1 and not args.no_dbo:
-        args.dbo = True
+    if args.no_dbo:
+        args.dbo = False
     if args.topology:
         num_attn, num_ffn = (int(x) for x in args.topology.split(","))
         if num_attn + num_ffn != args.gpus:

@@ -1,0 +1,175 @@
+"""Fused AFD transfer kernels on one GPU (loopback) vs a plain PyTorch fp32 reference.
+
+The "FFN ranks" and the "Attention rank" are separate buffers on cuda:0, so the
+whole dispatch -> expand -> combine_send -> combine chain runs in one process
+and one stream.  The only wait (combine) targets a counter that the preceding
+combine_send launches already raised, so nothing spins on a concurrent kernel.
+"""
+
+import pytest
+import torch
+
+from afd_plugin_b200.ops import _ext
+from afd_plugin_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    C = _ext.ops()
+    C.reset_status(0)
+    yield
+    torch.cuda.synchronize()
+    assert C.read_status(0) == 0, "a fused kernel recorded an error status"
+
+
+def _ref_norm(x, res, w, eps):
+    r = (x.float() + res.float()).to(torch.bfloat16)
+    inv = torch.rsqrt(r.float().pow(2).mean(-1, keepdim=True) + eps)
+    return r, (r.float() * inv * w.float()).to(torch.bfloat16)
+
+
+class _Loopback:
+    """A=1 Attention rank and F FFN ranks as local buffers."""
+
+    def __init__(self, F, t_cap, H, E, k, layers=1):
+        self.F, self.t_cap, self.H, self.E, self.k = F, t_cap, H, E, k
+        z = lambda *s, dt: torch.zeros(*s, dtype=dt, device=DEV)  # noqa: E731
+        self.tok = [z(1, t_cap, H, dt=torch.bfloat16) for _ in range(F)]
+        self.rid = [z(1, t_cap, k, dt=torch.int32) for _ in range(F)]
+        self.rwt = [z(1, t_cap, k, dt=torch.float32) for _ in range(F)]
+        self.tcount = [z(1, dt=torch.int32) for _ in range(F)]
+        self.arrive = [z(layers, dt=torch.int64) for _ in range(F)]
+        rows = [[t.data_ptr() for t in grp] for grp in (self.tok, self.rid, self.rwt, self.tcount, self.arrive)]
+        self.ptrs = torch.tensor(rows, dtype=torch.int64, device=DEV)
+        self.fmask = z(t_cap, dt=torch.int32)
+        self.dctr = z(1 + (t_cap + 15) // 16, dt=torch.int32)
+        self.comb = z(t_cap, F, H, dt=torch.bfloat16)
+        self.comb_flag = z(layers, dt=torch.int64)
+        self.comb_ptrs = torch.tensor([self.comb.data_ptr()], dtype=torch.int64, device=DEV)
+        self.comb_flag_ptrs = torch.tensor([self.comb_flag.data_ptr()], dtype=torch.int64, device=DEV)
+
+
+def _dispatch(lb, x, res, norm_w, gate, bias, scale, scoring, renorm, n_group, topk_group, has_shared=1, moe=1):
+    C = _ext.ops()
+    e_local = lb.E // lb.F
+    cfg = [lb.E, lb.k, scoring, renorm, n_group, topk_group, moe, has_shared, lb.F, e_local, lb.t_cap, 0, 0, 0]
+    C.afd_dispatch(x, res, norm_w, 1e-6, gate, bias, scale, lb.ptrs, lb.fmask, lb.dctr, cfg)
+
+
+@pytest.mark.parametrize("T", [1, 37, 600, 1200])
+@pytest.mark.parametrize("routing", ["softmax", "sigmoid_grouped"])
+def test_dispatch_expand_combine_loopback(T, routing):
+    if routing == "sigmoid_grouped" and T not in (37,):
+        pytest.skip("one size is enough for the grouped variant")
+    torch.manual_seed(T)
+    C = _ext.ops()
+    F, H, E, k, t_cap = 2, 256, 64, 6, 1280
+    if routing == "softmax":
+        scoring, renorm, n_group, topk_group, scale, bias = 0, 0, 1, 1, 1.5, None
+    else:
+        scoring, renorm, n_group, topk_group, scale = 1, 1, 8, 3, 2.5
+        bias = (torch.randn(E, device=DEV) * 0.1).float()
+    lb = _Loopback(F, t_cap, H, E, k)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    res0 = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    norm_w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    gate = (torch.randn(E, H, device=DEV) / H**0.5).to(torch.bfloat16)
+    res = res0.clone()
+    _dispatch(lb, x, res, norm_w, gate, bias, scale, scoring, renorm, n_group, topk_group)
+    torch.cuda.synchronize()
+
+    r_ref, h_ref = _ref_norm(x, res0, norm_w, 1e-6)
+    torch.testing.assert_close(res, r_ref, atol=0, rtol=0)
+    h_k = lb.tok[0][0, :T]  # home rank 0 holds every token's normalised row
+    torch.testing.assert_close(h_k.float(), h_ref.float(), atol=2e-2, rtol=1e-2)
+    # logits from the kernel's own rows: only the accumulation order differs
+    logits = h_k.float() @ gate.float().t()
+    w_ref, id_ref = ref.topk_route(logits, k, scoring="softmax" if scoring == 0 else "sigmoid",
+                                   renormalize=bool(renorm), bias=bias, n_group=n_group, topk_group=topk_group,
+                                   routed_scaling_factor=scale)
+    e_local = E // F
+    # routing sent to every FFN rank; compare as sorted (id, weight) pairs
+    for f in range(F):
+        ids = lb.rid[f][0, :T].long()
+        srt, order = ids.sort(dim=-1)
+        rsrt, rorder = id_ref.long().sort(dim=-1)
+        assert torch.equal(srt.cpu(), rsrt.cpu())
+        torch.testing.assert_close(lb.rwt[f][0, :T].gather(1, order), w_ref.gather(1, rorder), atol=1e-4, rtol=1e-3)
+        assert int(lb.tcount[f][0]) == T
+        assert int(lb.arrive[f][0]) == 1
+    mask_ref = torch.ones(T, dtype=torch.int64, device=DEV)  # home rank 0 (shared expert)
+    for f in range(F):
+        mask_ref |= ((id_ref.long() // e_local) == f).any(-1).long() << f
+    assert torch.equal(lb.fmask[:T].long().cpu(), mask_ref.cpu())
+    for f in range(F):
+        sel = ((mask_ref >> f) & 1).bool()
+        torch.testing.assert_close(lb.tok[f][0, :T][sel].float(), h_ref[sel].float(), atol=2e-2, rtol=1e-2)
+    assert int(lb.dctr.abs().sum()) == 0, "dispatch counters must return to zero"
+
+    # FFN side: expand into expert segments, then a stand-in expert output and combine_send
+    J = k + 1
+    staging = torch.randn(1, t_cap, J, H, device=DEV).to(torch.bfloat16)
+    cap = t_cap
+    done = torch.zeros(1, dtype=torch.int32, device=DEV)
+    expected = torch.zeros(T, F, H, device=DEV)
+    for f in range(F):
+        xs = torch.zeros(e_local * cap, H, dtype=torch.bfloat16, device=DEV)
+        meta = torch.full((e_local * cap,), -1, dtype=torch.int32, device=DEV)
+        rw = torch.zeros(e_local * cap, dtype=torch.float32, device=DEV)
+        counts = torch.zeros(e_local + 1, dtype=torch.int32, device=DEV)
+        ratio = 1 if f == 0 else 0
+        C.afd_expand(lb.tok[f], lb.rid[f], lb.rwt[f], lb.tcount[f], xs, meta, rw, counts,
+                     [1, t_cap, k, e_local, f * e_local, cap, ratio, 0, 1])
+        torch.cuda.synchronize()
+        local = (id_ref.long() // e_local) == f
+        for le in range(e_local):
+            n = int(counts[le])
+            assert n == int((id_ref.long() == f * e_local + le).sum())
+            m = meta[le * cap : le * cap + n].long()
+            tt, jj = (m >> 8) & 0xFFFF, m & 0xFF
+            assert torch.equal(lb.rid[f][0, tt, jj].long(), torch.full_like(tt, f * e_local + le))
+            torch.testing.assert_close(xs[le * cap : le * cap + n], lb.tok[f][0, tt], atol=0, rtol=0)
+            torch.testing.assert_close(rw[le * cap : le * cap + n], lb.rwt[f][0, tt, jj], atol=0, rtol=0)
+        if f == 0:
+            assert int(counts[e_local]) == T
+        C.afd_combine_send(staging, lb.rid[f], lb.rwt[f], lb.tcount[f], lb.comb_ptrs, lb.comb_flag_ptrs, done, H,
+                           [1, t_cap, k, J, e_local, f * e_local, 1, f, 1, 1, f, F, 0, 0])
+        used = torch.cat([local, torch.full((T, 1), f == 0, device=DEV)], dim=1)
+        expected[:, f] = (staging[0, :T].float() * used.unsqueeze(-1)).sum(1)
+    torch.cuda.synchronize()
+    assert int(lb.comb_flag[0]) == F
+    for f in range(F):
+        sel = ((mask_ref >> f) & 1).bool()
+        torch.testing.assert_close(lb.comb[:T, f][sel].float(), expected[:, f][sel], atol=3e-2, rtol=1e-2)
+    epoch = torch.ones(1, dtype=torch.int64, device=DEV)
+    out = C.afd_combine(lb.comb, lb.fmask, T, lb.comb_flag, 0, epoch, F, 10**9)
+    torch.cuda.synchronize()
+    want = (lb.comb[:T].float() * ((mask_ref.unsqueeze(-1) >> torch.arange(F, device=DEV)) & 1).unsqueeze(-1)).sum(1)
+    torch.testing.assert_close(out.float(), want, atol=3e-2, rtol=1e-2)
+    assert int(done.abs().sum()) == 0
+
+    # a second dispatch reuses the counters: arrivals grow by one, counters stay zero
+    _dispatch(lb, x, res, norm_w, gate, bias, scale, scoring, renorm, n_group, topk_group)
+    torch.cuda.synchronize()
+    assert all(int(a[0]) == 2 for a in lb.arrive)
+    assert int(lb.dctr.abs().sum()) == 0
+
+
+def test_dispatch_dense_layer_goes_home_only():
+    torch.manual_seed(0)
+    F, H, t_cap, T = 2, 512, 64, 19
+    lb = _Loopback(F, t_cap, H, 1, 1)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    res0 = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    norm_w = torch.ones(H, device=DEV, dtype=torch.bfloat16)
+    res = res0.clone()
+    _dispatch(lb, x, res, norm_w, norm_w, None, 1.0, 0, 0, 1, 1, has_shared=1, moe=0)
+    torch.cuda.synchronize()
+    _, h_ref = _ref_norm(x, res0, norm_w, 1e-6)
+    assert torch.equal(lb.fmask[:T].cpu(), torch.ones(T, dtype=torch.int32))
+    torch.testing.assert_close(lb.tok[0][0, :T].float(), h_ref.float(), atol=2e-2, rtol=1e-2)
+    assert int(lb.tok[1].abs().sum()) == 0
+    assert [int(a[0]) for a in lb.arrive] == [1, 1]
