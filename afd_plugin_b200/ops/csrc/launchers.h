@@ -43,6 +43,7 @@ struct MlaQO {
   int64_t out_sb, out_sh;
 };
 int mla_decode_num_splits(int batch, int max_seq_len, int num_sms);
+cudaError_t mla_decode_prepare_device();
 void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
                        const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                        int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,

@@ -337,6 +337,12 @@ int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
   return s > max_s ? max_s : s;
 }
 
+// Opts the decode kernel into its dynamic shared memory on the current device.
+cudaError_t mla_decode_prepare_device() {
+  return cudaFuncSetAttribute(mla::mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)sizeof(mla::Smem) + 1024);
+}
+
 void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
                        const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                        int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,

@@ -1,0 +1,101 @@
+"""Allocation-free MLA decode C entry point vs the torch op on the same kernels.
+
+Calls ``afd_mla_decode_noalloc`` through its exported C symbol (ctypes on the
+in-tree extension) and compares two calls in a row against
+``torch.ops.afd_b200.mla_decode``.  Collected last on purpose (file name), and
+also passes on its own.
+"""
+
+import ctypes
+import math
+
+import pytest
+import torch
+
+from afd_plugin_b200.ops import _ext
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+ETOOBIG = 2
+
+
+def _lib():
+    _ext.ops()  # loads the extension (and fails loudly if it is missing)
+    lib = ctypes.CDLL(_ext.loaded_path())
+    f = lib.afd_mla_decode_noalloc
+    i64, i32, vp = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+    f.argtypes = [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i32, i32, vp, i32, i32, vp, i32, i32, i32,
+                  ctypes.c_float, vp, vp]
+    f.restype = i32
+    lib.afd_mla_decode_noalloc_scratch_bytes.argtypes = [i32, i32, i32]
+    lib.afd_mla_decode_noalloc_scratch_bytes.restype = ctypes.c_uint64
+    lib.afd_mla_decode_noalloc_status.argtypes = [ctypes.POINTER(i32), i32]
+    lib.afd_mla_decode_noalloc_status.restype = i32
+    lib.afd_mla_decode_noalloc_last_error.restype = ctypes.c_char_p
+    return lib
+
+
+def _paged(B, lens, bs=64):
+    nblk = [math.ceil(n / bs) for n in lens]
+    total = sum(nblk) + 3
+    cache = torch.randn(total, bs, 576, device=DEV, dtype=torch.bfloat16)
+    perm = torch.randperm(total - 1)[: sum(nblk)] + 1
+    table = torch.zeros(B, max(nblk), dtype=torch.int32)
+    o = 0
+    for b, nb in enumerate(nblk):
+        table[b, :nb] = perm[o : o + nb].to(torch.int32)
+        o += nb
+    return cache, table.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV)
+
+
+def _call(lib, q, cache, table, seq, out, scale, splits, heads=None):
+    B, H = q.shape[0], q.shape[1] if heads is None else heads
+    q_lat, q_pe = q[..., :512], q[..., 512:]
+    return lib.afd_mla_decode_noalloc(
+        q_lat.data_ptr(), q_lat.stride(0), q_lat.stride(1), q_pe.data_ptr(), q_pe.stride(0), q_pe.stride(1),
+        out.data_ptr(), out.stride(0), out.stride(1), cache.data_ptr(), cache.shape[0], cache.shape[1],
+        table.data_ptr(), table.stride(0), table.shape[1], seq.data_ptr(), B, H, splits, scale,
+        torch.cuda.current_stream().cuda_stream, None)
+
+
+@pytest.mark.parametrize("splits", [4, 0])
+def test_noalloc_matches_torch_op_twice(splits):
+    torch.manual_seed(7 + splits)
+    lib = _lib()
+    C = _ext.ops()
+    lens = [1, 31, 32, 33, 64, 200, 1029]
+    B, H = len(lens), 16
+    cache, table, seq = _paged(B, lens)
+    scale = 1 / math.sqrt(192)
+    st = ctypes.c_int(0)
+    assert lib.afd_mla_decode_noalloc_status(ctypes.byref(st), 1) == 0
+    qs = [torch.randn(B, H, 576, device=DEV, dtype=torch.bfloat16) for _ in range(3)]
+    outs = [torch.empty(B, H, 512, device=DEV, dtype=torch.bfloat16) for _ in range(3)]
+    # warm-up call: one-time set-up for this device
+    assert _call(lib, qs[0], cache, table, seq, outs[0], scale, splits) == 0, lib.afd_mla_decode_noalloc_last_error()
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for i in (1, 2):  # two calls in a row, the second reusing the scratch
+        rc = _call(lib, qs[i], cache, table, seq, outs[i], scale, splits)
+        assert rc == 0, lib.afd_mla_decode_noalloc_last_error()
+    torch.cuda.synchronize()
+    # cudaMalloc works in 2 MiB pages: any device allocation by the calls shows up here
+    assert free_before - torch.cuda.mem_get_info()[0] < 2 << 20, "the entry point took device memory"
+    for i in (0, 1, 2):
+        want = C.mla_decode(qs[i][..., :512], qs[i][..., 512:], cache, table, seq, scale, splits, False)
+        torch.testing.assert_close(outs[i].float(), want.float(), atol=1e-2, rtol=1e-2)
+    assert lib.afd_mla_decode_noalloc_status(ctypes.byref(st), 0) == 0 and st.value == 0
+
+
+def test_noalloc_rejects_oversized_split_scratch():
+    lib = _lib()
+    lens = [64] * 7
+    cache, table, seq = _paged(len(lens), lens)
+    q = torch.randn(len(lens), 16, 576, device=DEV, dtype=torch.bfloat16)
+    out = torch.zeros(len(lens), 16, 512, device=DEV, dtype=torch.bfloat16)
+    splits = 80  # 7 x 80 x 16 partial rows of 2 KiB each: more than the 16 MiB scratch
+    assert lib.afd_mla_decode_noalloc_scratch_bytes(len(lens), 16, splits) > 16 << 20
+    assert _call(lib, q, cache, table, seq, out, 0.1, splits) == ETOOBIG
+    assert b"static scratch" in lib.afd_mla_decode_noalloc_last_error()
+    torch.cuda.synchronize()
+    assert int(out.abs().sum()) == 0, "a rejected call must launch nothing"
