@@ -1,0 +1,100 @@
+"""Grouped expert GEMM (tcgen05) at decode shapes: device time and weight bandwidth.
+
+Decode MoE GEMMs are weight-streaming: every expert's weights are read once
+per step while only a few tokens reuse them.  The figure of merit is the
+weight bytes moved per second against the measured HBM copy bandwidth
+(``MEASURED_PEAKS.json`` at the repository root, when present).
+
+    python -m afd_plugin_b200.bench.grouped_gemm_bench [--shapes dsv2-lite-f2,...]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+# name: (local experts, hidden, intermediate, tokens per expert)
+SHAPES = {
+    "dsv2-lite-f2": (32, 2048, 1408, 24),     # DeepSeek-V2-Lite, 6A2F: 256 tokens x top-6 over 64 experts
+    "dsv2-lite-f1": (64, 2048, 1408, 24),     # DeepSeek-V2-Lite, one FFN rank holds every expert
+    "qwen3-30b-f4": (32, 2048, 768, 32),      # Qwen3-30B-A3B, 4A4F: 512 tokens x top-8 over 128 experts
+    "dsv3-f4": (64, 7168, 2048, 16),          # DeepSeek-V3 shapes, 4A4F: 512 tokens x top-8 over 256 experts
+}
+
+
+def _peak_gbs() -> tuple[float, str]:
+    path = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def _time_us(fn, reps: int, iters: int = 5) -> float:
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / (iters * reps)
+
+
+def run(shape: str, reps: int, tokens_per_expert: int | None = None) -> dict:
+    from afd_plugin_b200.ops import _ext
+
+    C = _ext.ops()
+    E, H, I, tpe = SHAPES[shape]
+    tpe = tokens_per_expert or tpe
+    dev = "cuda"
+    rows = E * tpe
+    counts = torch.full((E,), tpe, dtype=torch.int32, device=dev)
+    offsets = (torch.arange(E, dtype=torch.int32, device=dev) * tpe).contiguous()
+    a1 = (torch.randn(rows, H, device=dev) * 0.1).to(torch.bfloat16)
+    w13 = (torch.randn(E, 2 * I, H, device=dev) * 0.02).to(torch.bfloat16)
+    a2 = (torch.randn(rows, I, device=dev) * 0.1).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, device=dev) * 0.02).to(torch.bfloat16)
+    peak, kind = _peak_gbs()
+    out = {"shape": shape, "experts": E, "hidden": H, "intermediate": I, "tokens_per_expert": tpe}
+    for name, fn, wbytes in (
+        ("gemm1_swiglu", lambda: C.grouped_gemm_ex(a1, w13, offsets, counts, 1, -1), w13.numel() * 2),
+        ("gemm2", lambda: C.grouped_gemm_ex(a2, w2, offsets, counts, 0, -1), w2.numel() * 2),
+    ):
+        us = _time_us(fn, reps)
+        gbs = wbytes / (us * 1e-6) / 1e9
+        out[name + "_us"] = round(us, 2)
+        out[name + "_weight_GBps"] = round(gbs, 1)
+        out[name + f"_frac_of_{kind}_hbm"] = round(gbs / peak, 3)
+    torch.cuda.synchronize()
+    out["status"] = int(C.read_status(torch.cuda.current_device()))
+    return out
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--shapes", default=",".join(SHAPES))
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--tokens-per-expert", type=int, default=None)
+    args = ap.parse_args(argv)
+    for shape in args.shapes.split(","):
+        print(json.dumps(run(shape, args.reps, args.tokens_per_expert)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -375,7 +375,7 @@ class FusedAttentionExecutor(FFNExecutor):
 
 
 class FusedFFNRunner:
-    """FFN-side step: wait, expand, tcgen05 grouped GEMMs, combine-send."""
+    """FFN-side step: expand (after a bounded arrival wait), tcgen05 grouped GEMMs, combine-send."""
 
     def __init__(self, model, connector: B200FusedAFDConnector, engine_config):
         from afd_plugin_b200.runtime.cuda_graph import validate_cuda_graph_mode
@@ -391,17 +391,27 @@ class FusedFFNRunner:
         self.f_rank = connector.role_rank
         self.home_a0 = self.f_rank * d.ratio
         self.e_offset = self.f_rank * d.e_local
+        # Shared experts packed as virtual experts (chunks of the routed width):
+        # home rows are copied into their segments and run in the routed GEMMs.
+        self.n_chunks = max((l.mlp.experts.n_extra for i, l in enumerate(model.layers)
+                             if model.arch.is_moe_layer(i)), default=0)
+        self.J = d.top_k + max(1, self.n_chunks)  # staging slots per token
+        self.shared_base = d.rows
+        self.shared_stride = d.ratio * d.t_cap
+        rows = d.rows + self.n_chunks * self.shared_stride
         # Local buffers (never touched by peers).
-        self.x = torch.empty(S, max(1, d.rows), H, dtype=torch.bfloat16, device=dev)
-        self.meta = torch.zeros(S, max(1, d.rows), dtype=torch.int32, device=dev)
-        self.rw = torch.zeros(S, max(1, d.rows), dtype=torch.float32, device=dev)
-        self.counts = torch.zeros(S, d.e_local + d.ratio, dtype=torch.int32, device=dev)
-        self.staging = torch.empty(S, A, d.t_cap, d.slots, H, dtype=torch.bfloat16, device=dev)
+        self.x = torch.empty(S, max(1, rows), H, dtype=torch.bfloat16, device=dev)
+        self.meta = torch.zeros(S, max(1, rows), dtype=torch.int32, device=dev)
+        self.rw = torch.zeros(S, max(1, rows), dtype=torch.float32, device=dev)
+        self.counts = torch.zeros(S, d.e_local + max(d.ratio, self.n_chunks), dtype=torch.int32, device=dev)
+        self.staging = torch.empty(S, A, d.t_cap, self.J, H, dtype=torch.bfloat16, device=dev)
         stage_stride = self.staging[0, 0].numel() * self.staging.element_size()
         self.staging_ptrs = [
             torch.tensor([self.staging[s].data_ptr() + a * stage_stride for a in range(A)], dtype=torch.int64,
                          device=dev) for s in range(S)]
         self.off_routed = torch.arange(d.e_local, dtype=torch.int32, device=dev) * d.cap
+        self.off_all = torch.cat([self.off_routed, self.shared_base + torch.arange(
+            self.n_chunks, dtype=torch.int32, device=dev) * self.shared_stride]).to(torch.int32)
         self.off_shared = torch.arange(d.ratio, dtype=torch.int32, device=dev) * d.t_cap
         # Shared / dense rows are the home sources' token rows; their (source, token, slot) map is static.
         t = torch.arange(d.t_cap, dtype=torch.int32)
@@ -426,6 +436,9 @@ class FusedFFNRunner:
                 ex = mlp.experts
                 if ex.w13_scale is not None:
                     raise NotImplementedError("fused FFN path: fp8 block-scaled experts not wired yet")
+                if self.n_chunks:
+                    self.layer_w.append((ex.w13_all, ex.w2_all, None, None))
+                    continue
                 shared = mlp.shared_experts
                 sw13 = shared.w13.unsqueeze(0) if shared is not None else None
                 sw2 = shared.w2.unsqueeze(0) if shared is not None else None
@@ -437,15 +450,24 @@ class FusedFFNRunner:
         c, d = self.c, self.c.dims
         C = torch.ops.afd_b200
         A, H = d.num_attn, d.hidden
-        C.afd_wait(c.arrive[s], layer_idx, c.epoch[s : s + 1], A, c.timeout_ns)
         w13, w2, sw13, sw2 = self.layer_w[layer_idx]
         is_moe = w13 is not None
+        merged = is_moe and self.n_chunks > 0
         counts = self.counts[s]
+        n_chunks = self.n_chunks if merged else 0
+        # expand waits (bounded) for every Attention rank's arrival first
         C.afd_expand(c.tok[s], c.rid[s], c.rwt[s], c.tcount[s], self.x[s], self.meta[s], self.rw[s], counts,
-                     [A, d.t_cap, d.top_k, d.e_local, self.e_offset, d.cap, d.ratio, self.home_a0, int(is_moe)])
+                     [A, d.t_cap, d.top_k, d.e_local, self.e_offset, d.cap, d.ratio, self.home_a0, int(is_moe),
+                      n_chunks, self.shared_base, self.shared_stride],
+                     c.arrive[s], layer_idx, c.epoch[s : s + 1], A, c.timeout_ns)
         home_rows = c.tok[s][self.home_a0 : self.home_a0 + d.ratio].reshape(d.ratio * d.t_cap, H)
         launches = []
-        if is_moe:
+        if merged:
+            # routed experts and shared-expert chunks in one GEMM per projection
+            ne = d.e_local + n_chunks
+            h_r = C.grouped_gemm_ex(self.x[s], w13, self.off_all, counts[:ne], 1, ne)
+            launches.append((h_r, w2, self.off_all, counts[:ne], ne, self.meta[s], self.rw[s]))
+        elif is_moe:
             h_r = C.grouped_gemm_ex(self.x[s], w13, self.off_routed, counts[: d.e_local], 1, d.e_local)
             launches.append((h_r, w2, self.off_routed, counts[: d.e_local], d.e_local, self.meta[s], self.rw[s]))
         if sw13 is not None:
@@ -455,11 +477,13 @@ class FusedFFNRunner:
         for h, w, off, cnt, wexp, meta, rw in launches:
             # Expert outputs land in local staging slots; the last CTA clears the counters.
             C.grouped_gemm_scatter(h, w, off, cnt, wexp, meta, rw, self.staging_ptrs[s], self.no_flags,
-                                   c.done[s, 1:2], counts, [d.slots, H, total, 0, layer_idx])
+                                   c.done[s, 1:2], counts, [self.J, H, total, 0, layer_idx])
+        has_home = merged or sw13 is not None
         C.afd_combine_send(self.staging[s], c.rid[s], c.rwt[s], c.tcount[s], c.comb_ptrs[s], c.comb_flag_ptrs[s],
                            c.done[s, 2:3], H,
-                           [A, d.t_cap, d.top_k, d.slots, d.e_local, self.e_offset, d.ratio, self.home_a0,
-                            int(is_moe), int(sw13 is not None), self.f_rank, d.num_ffn, layer_idx, 0])
+                           [A, d.t_cap, d.top_k, self.J, d.e_local, self.e_offset, d.ratio, self.home_a0,
+                            int(is_moe), int(has_home), self.f_rank, d.num_ffn, layer_idx, 0,
+                            n_chunks if merged else 1])
 
     def _step(self, stages) -> None:
         for s in stages:

@@ -4,17 +4,19 @@
 // one of its experts (or is its home rank for the shared expert / dense MLP)
 // and comes back as one pre-reduced row per such rank.
 //
-// afd_dispatch      (Attention side, per layer and ubatch), three kernels:
-//   norm    residual += attn_out; h = RMSNorm(residual) * w (one CTA per token)
+// afd_dispatch      (Attention side, per layer and ubatch), two kernels:
+//   norm    residual += attn_out; h = RMSNorm(residual) * w (one CTA per
+//           token); h goes straight to every FFN rank's token buffer (the home
+//           rank only for a dense layer), so the rows travel while routing runs
 //   router  logits = h . gate^T on the tensor cores, split over (token tile,
 //           expert tile) CTAs; the last CTA of a token tile runs the top-k and
-//           sends the token's routing (k ids + weights) to every FFN rank
-//   send    one warp per (token, destination FFN rank) stores h into that
-//           rank's token buffer; the last CTA publishes the token count and
-//           bumps every FFN rank's arrival counter (release, system scope).
-// afd_expand        (FFN side) copies each received row into the contiguous
-//   segment of every local expert it routes to (local HBM), building the
-//   grouped GEMM's row -> (source, token, slot) map.
+//           sends the token's routing (k ids + weights) to every FFN rank; the
+//           last tile publishes the token count and bumps every FFN rank's
+//           arrival counter (release, system scope).
+// afd_expand        (FFN side) waits for every Attention rank, then copies
+//   each received row into the contiguous segment of every local expert it
+//   routes to (local HBM), and home rows into the shared-expert chunks'
+//   segments, building the grouped GEMM's row -> (source, token, slot) map.
 // afd_combine_send  (FFN side, after the expert GEMMs) sums a token's local
 //   expert outputs (+ shared expert) and stores one row into the source
 //   Attention rank's combine slot; the last CTA bumps every Attention rank's
@@ -35,9 +37,13 @@ namespace fused {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kRouterThreads = 512;
+constexpr int kRouterWarps = kRouterThreads / 32;
 constexpr int kMaxK = 16;
+constexpr int kMaxSlots = 32;     // routed slots + shared-expert chunks
+constexpr int kMaxA = 64;         // Attention ranks
 constexpr int kNormMaxVec = 4;    // H <= 8 * kThreads * kNormMaxVec = 8192
-constexpr int kRouteTile = 16;    // tokens per router CTA (one m16 MMA tile)
+constexpr int kRouteTile = 16;    // tokens per router CTA (one m16 MMA tile, one warp each for top-k)
 constexpr int kMaxRouteE = 512;   // experts (matches the warp top-k)
 
 using bf16 = __nv_bfloat16;
@@ -50,6 +56,9 @@ AFD_DEVICE uint64_t ld_acquire_sys(const uint64_t* p) {
 AFD_DEVICE void red_release_sys_add(uint64_t* p, uint64_t v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+AFD_DEVICE void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+AFD_DEVICE void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // 16-byte load that bypasses L1 (rows written by a peer GPU).
 AFD_DEVICE Vec16<bf16> load16_cg(const bf16* p) {
   Vec16<bf16> out;
@@ -68,35 +77,38 @@ AFD_DEVICE bool wait_flag(const uint64_t* flag, uint64_t target, int64_t timeout
   return true;
 }
 
-// Warp-wide row copy of H bf16 elements (H % 8 == 0), four 16-byte loads in flight per lane.
-AFD_DEVICE void warp_copy_row(bf16* dst, const bf16* src, int H, int lane) {
-  const int nv = H / 8;
-  int v = lane;
-  for (; v + 96 < nv; v += 128) {
-    Vec16<bf16> x0 = load16(src + v * 8), x1 = load16(src + (v + 32) * 8);
-    Vec16<bf16> x2 = load16(src + (v + 64) * 8), x3 = load16(src + (v + 96) * 8);
-    store16(dst + v * 8, x0);
-    store16(dst + (v + 32) * 8, x1);
-    store16(dst + (v + 64) * 8, x2);
-    store16(dst + (v + 96) * 8, x3);
+// CTA-level completion count.  Thread 0 releases the CTA's stores at system
+// scope (bar.sync makes the other threads' stores part of that release) and
+// counts the CTA in; in the last of `expected` CTAs it resets the counter and
+// runs `publish`.
+template <typename Publish>
+AFD_DEVICE void finish_grid(unsigned* ctr, unsigned expected, Publish publish) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    if (atomicAdd(ctr, 1u) == expected - 1) {
+      *ctr = 0u;
+      fence_acq_rel_sys();
+      publish();
+    }
   }
-  for (; v < nv; v += 32) store16(dst + v * 8, load16(src + v * 8));
 }
 
-// Last-CTA completion: every CTA makes its peer stores visible system-wide and
-// counts itself; the last one resets the counter and runs `publish`.
-template <typename Publish>
-AFD_DEVICE void finish_grid(unsigned* done_ctr, Publish publish) {
-  __shared__ int s_last;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(done_ctr, 1u) == gridDim.x - 1);
-  __syncthreads();
-  if (s_last && threadIdx.x == 0) {
-    *done_ctr = 0u;
-    __threadfence_system();
-    publish();
+// Exclusive prefix of the per-source token counts in shared memory; returns
+// the total.  Called by one thread after the arrival acquire.
+AFD_DEVICE int source_prefix(const int32_t* tcount, int A, int* pre) {
+  int run = 0;
+  for (int a = 0; a < A; ++a) {
+    pre[a] = run;
+    run += __ldcg(tcount + a);
   }
+  pre[A] = run;
+  return run;
+}
+AFD_DEVICE int source_of(const int* pre, int A, int q) {
+  int a = 0;
+  while (a + 1 < A && pre[a + 1] <= q) ++a;
+  return a;
 }
 
 __global__ void epoch_kernel(uint64_t* epoch) { *epoch += 1; }
@@ -107,9 +119,17 @@ __global__ void wait_kernel(const uint64_t* flag, const uint64_t* epoch, uint64_
   if (!wait_flag(flag, (*epoch) * arrivals, timeout_ns)) atomicExch(status, kStatusWaitTimeout);
 }
 
-// ---- dispatch, step 1 (one CTA per token): residual += attn_out; h = RMSNorm(residual) * w.
-// h goes to local scratch; with a shared expert / dense MLP the home FFN rank
-// gets the row right here (its destination does not depend on routing).
+AFD_DEVICE void publish_dispatch(const DispatchParams& p) {
+  for (int f = 0; f < p.num_ffn; ++f) atomicExch_system(reinterpret_cast<int*>(p.tcount_ptrs[f]) + p.attn_rank, p.T);
+  for (int f = 0; f < p.num_ffn; ++f) red_release_sys_add(reinterpret_cast<uint64_t*>(p.flag_ptrs[f]) + p.layer, 1ull);
+}
+
+// ---- dispatch, step 1 (one CTA per token): residual += attn_out;
+// h = RMSNorm(residual) * w, kept locally for the router and stored straight
+// into the FFN ranks' token buffers: every FFN rank for an MoE layer (the
+// routing, which follows, tells each rank which rows it answers), the home
+// rank only for a dense layer.  A dense layer has no router step, so this
+// kernel also publishes the arrival.
 __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams p) {
   __shared__ float s_red[kWarps];
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -142,9 +162,9 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
   const float inv = rsqrtf(tot / (float)p.H + p.eps);
   const bf16* nw = static_cast<const bf16*>(p.norm_w);
   bf16* h = static_cast<bf16*>(p.h) + (size_t)t * p.H;
-  bf16* home = p.has_shared ? reinterpret_cast<bf16*>(p.tok_ptrs[p.home_f]) +
-                                  ((size_t)p.attn_rank * p.t_cap + t) * p.H
-                            : nullptr;
+  const size_t row_off = ((size_t)p.attn_rank * p.t_cap + t) * p.H;
+  const int f_lo = p.moe ? 0 : p.home_f;
+  const int f_hi = p.moe ? p.num_ffn : (p.has_shared ? p.home_f + 1 : p.home_f);
 #pragma unroll
   for (int u = 0; u < kNormMaxVec; ++u) {
     const int v = threadIdx.x + u * kThreads;
@@ -154,24 +174,32 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         y.v[j] = __float2bfloat16_rn(__bfloat162float(x[u].v[j]) * inv * __bfloat162float(w.v[j]));
-      store16(h + v * 8, y);
-      if (home) store16(home + v * 8, y);
+      if (p.moe) store16(h + v * 8, y);
+      for (int f = f_lo; f < f_hi; ++f) store16(reinterpret_cast<bf16*>(p.tok_ptrs[f]) + row_off + v * 8, y);
     }
   }
-  if (!p.moe && threadIdx.x == 0) p.fmask[t] = p.has_shared ? (int32_t)(1u << p.home_f) : 0;
-  if (home) __threadfence_system();
+  if (p.moe) {
+    __syncthreads();
+    if (threadIdx.x == 0) fence_acq_rel_sys();
+  } else {
+    if (threadIdx.x == 0) p.fmask[t] = p.has_shared ? (int32_t)(1u << p.home_f) : 0;
+    finish_grid(p.done_ctr, gridDim.x, [&] { publish_dispatch(p); });
+  }
 }
 
-// ---- dispatch, step 2 (MoE layers): router logits on the tensor cores, then top-k.
-// Grid (token tiles of 16, expert tiles of 8 * NT).  Each warp takes every 8th
-// 16-wide K step (split K), the CTA sums the eight partial tiles.  The last
-// CTA to finish a token tile (per-tile counter) routes its 16 tokens: writes
-// the ids / weights to every FFN rank and the destination mask locally.
+// ---- dispatch, step 2 (MoE layers): router logits on the tensor cores, top-k,
+// routing metadata, arrival.
+// Grid (token tiles of 16, expert tiles of 8 * NT).  Each of the 16 warps takes
+// every 16th 16-wide K step (split K); the CTA sums the partial tiles.  The
+// last CTA to finish a token tile (per-tile counter) routes its tokens, one
+// warp per token, sends the ids / weights to every FFN rank and records which
+// FFN ranks answer each token; the last token tile publishes the arrival.
 template <int NT>
-__global__ void __launch_bounds__(kThreads) dispatch_router_kernel(DispatchParams p) {
+__global__ void __launch_bounds__(kRouterThreads, 1) dispatch_router_kernel(DispatchParams p) {
   constexpr int EB = 8 * NT;
   __shared__ __align__(16) float sbuf[kRouteTile * kMaxRouteE];
   __shared__ int s_last;
+  static_assert(kRouterWarps * kRouteTile * EB <= kRouteTile * kMaxRouteE, "split-K buffer");
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouteTile;
   const int nt = min(kRouteTile, p.T - t0);
@@ -195,7 +223,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_router_kernel(DispatchParam
   for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
   const int ksteps = p.H / 16;
 #pragma unroll 4
-  for (int ks = warp; ks < ksteps; ks += kWarps) {
+  for (int ks = warp; ks < ksteps; ks += kRouterWarps) {
     const int k = ks * 16;
     uint32_t a[4];
     a[0] = ok0 ? ld32(h0 + k) : 0u;
@@ -219,27 +247,30 @@ __global__ void __launch_bounds__(kThreads) dispatch_router_kernel(DispatchParam
     red[(warp * kRouteTile + g + 8) * EB + n * 8 + c + 1] = acc[n][3];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < kRouteTile * EB; i += kThreads) {
+  for (int i = threadIdx.x; i < kRouteTile * EB; i += kRouterThreads) {
     const int r = i / EB, col = i % EB;
     float sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) sum += red[(w * kRouteTile + r) * EB + col];
+    for (int w = 0; w < kRouterWarps; ++w) sum += red[(w * kRouteTile + r) * EB + col];
     if (r < nt && e0 + col < p.E) p.logits[(size_t)(t0 + r) * p.E + e0 + col] = sum;
   }
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(&p.route_ctr[blockIdx.x], 1u) == gridDim.y - 1);
+  if (threadIdx.x == 0) {
+    fence_acq_rel_gpu();
+    s_last = (atomicAdd(&p.route_ctr[blockIdx.x], 1u) == gridDim.y - 1);
+    if (s_last) fence_acq_rel_gpu();
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   float* lg = sbuf;  // [16][E]
-  for (int i = threadIdx.x; i < nt * p.E; i += kThreads) lg[i] = __ldcg(p.logits + (size_t)t0 * p.E + i);
+  for (int i = threadIdx.x; i < nt * p.E; i += kRouterThreads) lg[i] = __ldcg(p.logits + (size_t)t0 * p.E + i);
   __syncthreads();
-  for (int i = warp; i < nt; i += kWarps) {
-    const int t = t0 + i;
+  if (warp < nt) {
+    const int t = t0 + warp;
     float w;
     int id;
-    warp_route(lg + i * p.E, p.gate_bias, p.E, p.k, p.scoring, p.renorm, p.n_group, p.topk_group, p.scale, w, id);
+    warp_route(lg + warp * p.E, p.gate_bias, p.E, p.k, p.scoring, p.renorm, p.n_group, p.topk_group, p.scale, w,
+               id);
     const unsigned bit = lane < p.k ? (1u << (id / p.e_local)) : 0u;
     const unsigned mask = __reduce_or_sync(0xffffffffu, bit) | (p.has_shared ? (1u << p.home_f) : 0u);
     const size_t off = ((size_t)p.attn_rank * p.t_cap + t) * p.k;
@@ -252,60 +283,66 @@ __global__ void __launch_bounds__(kThreads) dispatch_router_kernel(DispatchParam
     if (lane == 0) p.fmask[t] = (int32_t)mask;
   }
   if (threadIdx.x == 0) p.route_ctr[blockIdx.x] = 0u;
-  __threadfence_system();
+  finish_grid(p.done_ctr, gridDim.x, [&] { publish_dispatch(p); });
 }
 
-// ---- dispatch, step 3: one warp per (token, FFN rank) row store; the last CTA
-// publishes the token count and bumps every FFN rank's arrival counter.
-__global__ void __launch_bounds__(kThreads) dispatch_send_kernel(DispatchParams p) {
+// ---- FFN side: wait for every Attention rank, then one warp per received
+// (source, token) row: copy it into the segment of every local expert it
+// routes to, and (home sources) into every shared-expert chunk's segment.
+// Expert counters start at zero (cleared after the previous use).
+__global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
+  __shared__ int s_pre[kMaxA + 1];
+  __shared__ int s_row[kWarps][kMaxSlots];
+  __shared__ int s_ok;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * kWarps + warp;
-  const int t = gw / p.num_ffn, f = gw % p.num_ffn;
-  if (t < p.T) {
-    const unsigned mask = (unsigned)p.fmask[t];
-    if (((mask >> f) & 1u) && !(p.has_shared && f == p.home_f)) {
-      bf16* dst = reinterpret_cast<bf16*>(p.tok_ptrs[f]) + ((size_t)p.attn_rank * p.t_cap + t) * p.H;
-      warp_copy_row(dst, static_cast<const bf16*>(p.h) + (size_t)t * p.H, p.H, lane);
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    if (p.flag) ok = wait_flag(p.flag, (*p.epoch) * p.arrivals, p.timeout_ns);
+    if (!ok) atomicExch(p.status, kStatusWaitTimeout);
+    s_ok = ok;
+    if (ok) {
+      source_prefix(p.tcount, p.A, s_pre);
+      if (blockIdx.x == 0) {
+        if (p.n_chunks > 0) {
+          const int home_total = s_pre[p.home_a0 + p.ratio] - s_pre[p.home_a0];
+          for (int ch = 0; ch < p.n_chunks; ++ch) p.counts[p.e_local + ch] = home_total;
+        } else {
+          for (int i = 0; i < p.ratio; ++i) p.counts[p.e_local + i] = s_pre[p.home_a0 + i + 1] - s_pre[p.home_a0 + i];
+        }
+      }
     }
   }
-  finish_grid(p.done_ctr, [&] {
-    for (int ff = 0; ff < p.num_ffn; ++ff)
-      atomicExch_system(reinterpret_cast<int*>(p.tcount_ptrs[ff]) + p.attn_rank, p.T);
-    __threadfence_system();
-    for (int ff = 0; ff < p.num_ffn; ++ff)
-      red_release_sys_add(reinterpret_cast<uint64_t*>(p.flag_ptrs[ff]) + p.layer, 1ull);
-  });
-}
-
-// One warp per (source, token): copy the row into every local expert segment it
-// routes to.  Counters start at zero (cleared after the previous use).
-__global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
-  __shared__ int s_row[kWarps][kMaxK];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  if (blockIdx.x == 0 && threadIdx.x < p.ratio) p.counts[p.e_local + threadIdx.x] = p.tcount[p.home_a0 + threadIdx.x];
-  if (!p.moe) return;
+  __syncthreads();
+  if (!s_ok || !p.moe) return;
   const bf16* tok = static_cast<const bf16*>(p.tok);
   bf16* x = static_cast<bf16*>(p.x);
   const int nv = p.H / 8;
-  for (int pair = blockIdx.x * kWarps + warp; pair < p.A * p.t_cap; pair += gridDim.x * kWarps) {
-    const int a = pair / p.t_cap, t = pair % p.t_cap;
-    if (t >= p.tcount[a]) continue;
+  const int total = s_pre[p.A];
+  const int slots = p.k + p.n_chunks;
+  for (int q = blockIdx.x * kWarps + warp; q < total; q += gridDim.x * kWarps) {
+    const int a = source_of(s_pre, p.A, q);
+    const int t = q - s_pre[a];
+    const int pair = a * p.t_cap + t;
     const size_t base = (size_t)pair * p.k;
     int row = -1;
     if (lane < p.k) {
-      const int le = p.rid[base + lane] - p.e_offset;
+      const int le = __ldcg(p.rid + base + lane) - p.e_offset;
       if (le >= 0 && le < p.e_local) {
         const int slot = atomicAdd(&p.counts[le], 1);
         if (slot < p.cap) {
           row = le * p.cap + slot;
           p.meta[row] = (a << 24) | (t << 8) | lane;
-          p.rw[row] = p.rwt[base + lane];
+          p.rw[row] = __ldcg(p.rwt + base + lane);
         } else {
           atomicExch(p.status, kStatusBadIndex);
         }
       }
-      s_row[warp][lane] = row;
+    } else if (lane < slots && a >= p.home_a0 && a < p.home_a0 + p.ratio) {
+      row = p.shared_base + (lane - p.k) * p.shared_stride + (s_pre[a] - s_pre[p.home_a0]) + t;
+      p.meta[row] = (a << 24) | (t << 8) | lane;
+      p.rw[row] = 1.f;
     }
+    if (lane < slots) s_row[warp][lane] = row;
     const unsigned used = __ballot_sync(0xffffffffu, row >= 0);
     __syncwarp();
     if (used) {
@@ -319,17 +356,23 @@ __global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
   }
 }
 
-// One warp per (source, token): sum this rank's slots for the token and store
-// the row into the source's combine slot [t][f_rank].
+// One warp per received (source, token): sum this rank's slots for the token
+// (routed experts it owns; the shared-expert slots for home sources) and
+// store the row into the source's combine slot [t][f_rank].
 __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParams p) {
+  __shared__ int s_pre[kMaxA + 1];
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) source_prefix(p.tcount, p.A, s_pre);
+  __syncthreads();
   const int nv = p.H / 8;
-  for (int pair = blockIdx.x * kWarps + warp; pair < p.A * p.t_cap; pair += gridDim.x * kWarps) {
-    const int a = pair / p.t_cap, t = pair % p.t_cap;
-    if (t >= p.tcount[a]) continue;
+  const int total = s_pre[p.A];
+  for (int q = blockIdx.x * kWarps + warp; q < total; q += gridDim.x * kWarps) {
+    const int a = source_of(s_pre, p.A, q);
+    const int t = q - s_pre[a];
+    const int pair = a * p.t_cap + t;
     const bool home = p.has_shared && a >= p.home_a0 && a < p.home_a0 + p.ratio;
     bool hit = false;
-    float w = 0.f;  // echo mode: the slot's routing weight (1 for the shared slot)
+    float w = 0.f;  // echo mode: the slot's routing weight (1 for a shared slot)
     if (lane < p.k) {
       if (p.moe) {
         const int le = p.rid[(size_t)pair * p.k + lane] - p.e_offset;
@@ -338,7 +381,7 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
           w = p.echo ? p.rwt[(size_t)pair * p.k + lane] : 1.f;
         }
       }
-    } else if (lane == p.k) {
+    } else if (lane < p.k + p.home_slots) {
       hit = home;
       w = home ? 1.f : 0.f;
     }
@@ -351,7 +394,7 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
       for (int v = lane; v < nv; v += 32) {
         Vec16<bf16> xv = load16_cg(row + v * 8);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xv.v[q] = __float2bfloat16_rn(__bfloat162float(xv.v[q]) * wsum);
+        for (int qq = 0; qq < 8; ++qq) xv.v[qq] = __float2bfloat16_rn(__bfloat162float(xv.v[qq]) * wsum);
         store16(dst + v * 8, xv);
       }
     } else {
@@ -361,16 +404,16 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
         for (unsigned m = used; m; m &= m - 1) {
           const Vec16<bf16> xv = load16(st + (size_t)(__ffs(m) - 1) * p.H + v * 8);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(xv.v[q]);
+          for (int qq = 0; qq < 8; ++qq) acc[qq] += __bfloat162float(xv.v[qq]);
         }
         Vec16<bf16> o;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) o.v[q] = __float2bfloat16_rn(acc[q]);
+        for (int qq = 0; qq < 8; ++qq) o.v[qq] = __float2bfloat16_rn(acc[qq]);
         store16(dst + v * 8, o);
       }
     }
   }
-  finish_grid(p.done_ctr, [&] {
+  finish_grid(p.done_ctr, gridDim.x, [&] {
     for (int a = 0; a < p.A; ++a) red_release_sys_add(reinterpret_cast<uint64_t*>(p.flag_ptrs[a]) + p.layer, 1ull);
   });
 }
@@ -417,25 +460,22 @@ void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arriv
   fused::wait_kernel<<<1, 32, 0, s>>>(flag, epoch, arrivals, timeout_ns, status);
 }
 
-// Three launches: norm (one CTA per token), router (MoE layers only), send.
-// The router's expert tile widens with the token count so the grid stays
-// near two CTAs per SM.
+// Two launches: norm + row stores (one CTA per token), then the router for
+// MoE layers.  The router's expert tile widens with the token count so the
+// grid stays near two CTAs per SM.
 void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s) {
   using namespace fused;
-  const int T = std::max(1, p.T);
-  if (p.T > 0) dispatch_norm_kernel<<<p.T, kThreads, 0, s>>>(p);
-  if (p.moe && p.T > 0) {
-    const int mt = (T + kRouteTile - 1) / kRouteTile;
-    const int target = 148 * 2;
-    if (mt * ((p.E + 7) / 8) <= target)
-      dispatch_router_kernel<1><<<dim3(mt, (p.E + 7) / 8), kThreads, 0, s>>>(p);
-    else if (mt * ((p.E + 15) / 16) <= target)
-      dispatch_router_kernel<2><<<dim3(mt, (p.E + 15) / 16), kThreads, 0, s>>>(p);
-    else
-      dispatch_router_kernel<4><<<dim3(mt, (p.E + 31) / 32), kThreads, 0, s>>>(p);
-  }
-  const int warps = T * p.num_ffn;
-  dispatch_send_kernel<<<(warps + kWarps - 1) / kWarps, kThreads, 0, s>>>(p);
+  if (p.T <= 0) return;
+  dispatch_norm_kernel<<<p.T, kThreads, 0, s>>>(p);
+  if (!p.moe) return;
+  const int mt = (p.T + kRouteTile - 1) / kRouteTile;
+  const int target = 148 * 2;
+  if (mt * ((p.E + 7) / 8) <= target)
+    dispatch_router_kernel<1><<<dim3(mt, (p.E + 7) / 8), kRouterThreads, 0, s>>>(p);
+  else if (mt * ((p.E + 15) / 16) <= target)
+    dispatch_router_kernel<2><<<dim3(mt, (p.E + 15) / 16), kRouterThreads, 0, s>>>(p);
+  else
+    dispatch_router_kernel<4><<<dim3(mt, (p.E + 31) / 32), kRouterThreads, 0, s>>>(p);
 }
 
 static int warp_grid(int items, int max_ctas) {
@@ -443,13 +483,13 @@ static int warp_grid(int items, int max_ctas) {
 }
 
 void launch_afd_expand(const ExpandParams& p, cudaStream_t s) {
-  fused::expand_kernel<<<warp_grid(p.A * p.t_cap, 148 * 4), fused::kThreads, 0, s>>>(p);
+  fused::expand_kernel<<<warp_grid(p.A * p.t_cap, 148), fused::kThreads, 0, s>>>(p);
 }
 
 void launch_afd_combine_send(const CombineSendParams& p, cudaStream_t s) {
-  fused::combine_send_kernel<<<warp_grid(p.A * p.t_cap, 148 * 4), fused::kThreads, 0, s>>>(p);
+  fused::combine_send_kernel<<<warp_grid(p.A * p.t_cap, 148), fused::kThreads, 0, s>>>(p);
 }
 
 void launch_afd_combine(const CombineParams& p, cudaStream_t s) {
-  fused::combine_kernel<<<warp_grid(p.T, 148 * 2), fused::kThreads, 0, s>>>(p);
+  fused::combine_kernel<<<warp_grid(p.T, 148), fused::kThreads, 0, s>>>(p);
 }

@@ -400,11 +400,14 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
   launch_afd_dispatch(p, stream());
 }
 
-// cfg: [A, t_cap, k, e_local, e_offset, cap, ratio, home_a0, moe]
+// cfg: [A, t_cap, k, e_local, e_offset, cap, ratio, home_a0, moe(, n_chunks, shared_base, shared_stride)]
+// With `flag`, every CTA first waits (bounded) until flag[flag_index] >= epoch * arrivals.
 void afd_expand(const at::Tensor& tok, const at::Tensor& rid, const at::Tensor& rwt, const at::Tensor& tcount,
-                at::Tensor& x, at::Tensor& meta, at::Tensor& rw, at::Tensor& counts, std::vector<int64_t> cfg) {
+                at::Tensor& x, at::Tensor& meta, at::Tensor& rw, at::Tensor& counts, std::vector<int64_t> cfg,
+                const c10::optional<at::Tensor>& flag, int64_t flag_index, const c10::optional<at::Tensor>& epoch,
+                int64_t arrivals, int64_t timeout_ns) {
   check_cuda(tok, "tok");
-  TORCH_CHECK(cfg.size() == 9, "afd_expand: cfg has 9 entries");
+  TORCH_CHECK(cfg.size() == 9 || cfg.size() == 12, "afd_expand: cfg has 9 or 12 entries");
   ExpandParams p{};
   p.tok = tok.data_ptr();
   p.rid = rid.data_ptr<int32_t>();
@@ -424,17 +427,32 @@ void afd_expand(const at::Tensor& tok, const at::Tensor& rid, const at::Tensor& 
   p.ratio = (int)cfg[6];
   p.home_a0 = (int)cfg[7];
   p.moe = (int)cfg[8];
+  if (cfg.size() == 12) {
+    p.n_chunks = (int)cfg[9];
+    p.shared_base = (int)cfg[10];
+    p.shared_stride = (int)cfg[11];
+  }
+  TORCH_CHECK(p.A <= 64 && p.k <= 16 && p.k + p.n_chunks <= 32 && p.H % 8 == 0,
+              "afd_expand: at most 64 sources, k <= 16, k + shared chunks <= 32");
+  if (flag.has_value() && flag->defined()) {
+    TORCH_CHECK(epoch.has_value() && epoch->defined(), "afd_expand: a wait needs the epoch tensor");
+    p.flag = reinterpret_cast<const uint64_t*>(flag->data_ptr()) + flag_index;
+    p.epoch = reinterpret_cast<const uint64_t*>(epoch->data_ptr());
+    p.arrivals = (uint64_t)arrivals;
+    p.timeout_ns = timeout_ns;
+  }
   p.status = status_ptr(tok);
   c10::cuda::CUDAGuard g(tok.device());
   launch_afd_expand(p, stream());
 }
 
-// cfg: [A, t_cap, k, J, e_local, e_offset, ratio, home_a0, moe, has_shared, f_rank, num_ffn, layer, echo]
+// cfg: [A, t_cap, k, J, e_local, e_offset, ratio, home_a0, moe, has_shared, f_rank, num_ffn, layer, echo
+//       (, home_slots = J - k)]
 void afd_combine_send(const at::Tensor& staging, const at::Tensor& rid, const at::Tensor& rwt,
                       const at::Tensor& tcount, const at::Tensor& dst_ptrs, const at::Tensor& flag_ptrs,
                       at::Tensor& done_ctr, int64_t H, std::vector<int64_t> cfg) {
   check_cuda(staging, "staging");
-  TORCH_CHECK(cfg.size() == 14, "afd_combine_send: cfg has 14 entries");
+  TORCH_CHECK(cfg.size() == 14 || cfg.size() == 15, "afd_combine_send: cfg has 14 or 15 entries");
   CombineSendParams p{};
   p.staging = staging.data_ptr();
   p.rid = rid.data_ptr<int32_t>();
@@ -455,6 +473,9 @@ void afd_combine_send(const at::Tensor& staging, const at::Tensor& rid, const at
   p.num_ffn = (int)cfg[11];
   p.layer = (int)cfg[12];
   p.echo = (int)cfg[13];
+  p.home_slots = cfg.size() == 15 ? (int)cfg[14] : p.J - p.k;
+  TORCH_CHECK(p.home_slots >= 0 && p.k + p.home_slots <= p.J, "afd_combine_send: home slots exceed J");
+  TORCH_CHECK(p.A <= 64 && p.k <= 16 && p.J <= 32 && p.J >= p.k, "afd_combine_send: at most 64 sources, k <= J <= 32");
   p.dst_ptrs = dst_ptrs.data_ptr<int64_t>();
   p.flag_ptrs = flag_ptrs.data_ptr<int64_t>();
   p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
@@ -561,7 +582,8 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("afd_dispatch(Tensor attn_out, Tensor(a!) residual, Tensor norm_w, float eps, Tensor gate_w, Tensor? gate_bias, "
         "float scale, Tensor ptrs, Tensor(b!) fmask, Tensor(c!) done_ctr, int[] cfg) -> ()");
   m.def("afd_expand(Tensor tok, Tensor rid, Tensor rwt, Tensor tcount, Tensor(a!) x, Tensor(b!) meta, Tensor(c!) rw, "
-        "Tensor(d!) counts, int[] cfg) -> ()");
+        "Tensor(d!) counts, int[] cfg, Tensor? flag=None, int flag_index=0, Tensor? epoch=None, int arrivals=0, "
+        "int timeout_ns=0) -> ()");
   m.def("afd_combine_send(Tensor staging, Tensor rid, Tensor rwt, Tensor tcount, Tensor dst_ptrs, Tensor flag_ptrs, "
         "Tensor(a!) done_ctr, int H, int[] cfg) -> ()");
   m.def("afd_combine(Tensor comb, Tensor fmask, int T, Tensor flags, int layer, Tensor epoch, int arrivals, "

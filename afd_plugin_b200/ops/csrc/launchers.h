@@ -106,8 +106,16 @@ struct ExpandParams {
   void* x;                // [e_local * cap, H] expert segments
   int32_t* meta;          // [e_local * cap] (src << 24 | token << 8 | slot)
   float* rw;              // [e_local * cap]
-  int32_t* counts;        // [e_local + ratio]: routed rows, then home-source token counts
+  int32_t* counts;        // [e_local + n_chunks] (or [e_local + ratio] without shared chunks)
   int A, t_cap, k, H, e_local, e_offset, cap, ratio, home_a0, moe;
+  // Shared experts as virtual experts: chunk c's rows are every home source's
+  // tokens, stored at x[shared_base + c * shared_stride + home position].
+  int n_chunks, shared_base, shared_stride;
+  // Arrival wait folded into the kernel (flag == nullptr: no wait).
+  const uint64_t* flag;
+  const uint64_t* epoch;
+  uint64_t arrivals;
+  int64_t timeout_ns;
   int* status;
 };
 // FFN side: per (source, token) sum of this rank's expert outputs (+ shared),
@@ -119,6 +127,7 @@ struct CombineSendParams {
   const int32_t* tcount;  // [A]
   int A, t_cap, k, J, H, e_local, e_offset, ratio, home_a0, moe, has_shared, f_rank, num_ffn, layer;
   int echo;               // 1: transport-only stand-in (scale the token row by its local weights)
+  int home_slots;         // shared-expert slots k .. k + home_slots - 1 filled for home sources
   const int64_t* dst_ptrs;   // [A] combine buffers [t_cap, F, H] (stage base)
   const int64_t* flag_ptrs;  // [A] combine counters [layers]
   unsigned* done_ctr;
