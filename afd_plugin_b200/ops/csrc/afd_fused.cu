@@ -28,6 +28,8 @@
 // Counters only grow: the n-th use of a stage expects epoch[stage] * arrivals,
 // so captured graphs replay without resets.  No wait is unbounded: on expiry
 // a kernel records kStatusWaitTimeout and returns.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "launchers.h"
 #include "routing.cuh"
@@ -39,7 +41,6 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRouterThreads = 512;
 constexpr int kRouterWarps = kRouterThreads / 32;
-constexpr int kMaxK = 16;
 constexpr int kMaxSlots = 32;     // routed slots + shared-expert chunks
 constexpr int kMaxA = 64;         // Attention ranks
 constexpr int kNormMaxVec = 4;    // H <= 8 * kThreads * kNormMaxVec = 8192
@@ -77,10 +78,12 @@ AFD_DEVICE bool wait_flag(const uint64_t* flag, uint64_t target, int64_t timeout
   return true;
 }
 
-// CTA-level completion count.  Thread 0 releases the CTA's stores at system
-// scope (bar.sync makes the other threads' stores part of that release) and
-// counts the CTA in; in the last of `expected` CTAs it resets the counter and
-// runs `publish`.
+// CTA-level completion count.  Thread 0 makes the CTA's stores (peer stores
+// included) visible at system scope -- bar.sync puts the other threads'
+// stores under that fence -- and counts the CTA in; the last of `expected`
+// CTAs resets the counter and runs `publish`, whose flag updates are
+// releases.  One system fence per CTA, all in parallel: the last CTA adds no
+// fence of its own besides the release, so a chain of fences never forms.
 template <typename Publish>
 AFD_DEVICE void finish_grid(unsigned* ctr, unsigned expected, Publish publish) {
   __syncthreads();
@@ -88,7 +91,6 @@ AFD_DEVICE void finish_grid(unsigned* ctr, unsigned expected, Publish publish) {
     fence_acq_rel_sys();
     if (atomicAdd(ctr, 1u) == expected - 1) {
       *ctr = 0u;
-      fence_acq_rel_sys();
       publish();
     }
   }
@@ -111,6 +113,45 @@ AFD_DEVICE int source_of(const int* pre, int A, int q) {
   return a;
 }
 
+// out[v] = sum over the rows selected by `mask` of src + bit * stride, for this
+// lane's 16-byte vectors; four vectors per row are loaded before any is used.
+template <bool kBypassL1>
+AFD_DEVICE void warp_sum_rows(bf16* out, const bf16* src, size_t stride, unsigned mask, int H, int lane,
+                              float scale = 1.f) {
+  const int nv = H / 8;
+  for (int v0 = lane; v0 < nv; v0 += 128) {
+    float acc[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[u][q] = 0.f;
+    for (unsigned m = mask; m; m &= m - 1) {
+      const bf16* row = src + (size_t)(__ffs(m) - 1) * stride;
+      Vec16<bf16> x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int v = v0 + u * 32;
+        if (v < nv) x[u] = kBypassL1 ? load16_cg(row + v * 8) : load16(row + v * 8);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (v0 + u * 32 < nv)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[u][q] += __bfloat162float(x[u].v[q]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int v = v0 + u * 32;
+      if (v < nv) {
+        Vec16<bf16> o;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o.v[q] = __float2bfloat16_rn(acc[u][q] * scale);
+        store16(out + v * 8, o);
+      }
+    }
+  }
+}
+
 __global__ void epoch_kernel(uint64_t* epoch) { *epoch += 1; }
 
 __global__ void wait_kernel(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns,
@@ -119,8 +160,9 @@ __global__ void wait_kernel(const uint64_t* flag, const uint64_t* epoch, uint64_
   if (!wait_flag(flag, (*epoch) * arrivals, timeout_ns)) atomicExch(status, kStatusWaitTimeout);
 }
 
+// The token count was stored by the norm kernel (an earlier kernel, so it is
+// complete); the arrival is a release on every FFN rank's counter.
 AFD_DEVICE void publish_dispatch(const DispatchParams& p) {
-  for (int f = 0; f < p.num_ffn; ++f) atomicExch_system(reinterpret_cast<int*>(p.tcount_ptrs[f]) + p.attn_rank, p.T);
   for (int f = 0; f < p.num_ffn; ++f) red_release_sys_add(reinterpret_cast<uint64_t*>(p.flag_ptrs[f]) + p.layer, 1ull);
 }
 
@@ -132,6 +174,8 @@ AFD_DEVICE void publish_dispatch(const DispatchParams& p) {
 // kernel also publishes the arrival.
 __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams p) {
   __shared__ float s_red[kWarps];
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   const int nv = p.H / 8;
@@ -178,13 +222,14 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
       for (int f = f_lo; f < f_hi; ++f) store16(reinterpret_cast<bf16*>(p.tok_ptrs[f]) + row_off + v * 8, y);
     }
   }
-  if (p.moe) {
-    __syncthreads();
-    if (threadIdx.x == 0) fence_acq_rel_sys();
-  } else {
+  if (t == 0 && threadIdx.x < p.num_ffn)  // token count for every FFN rank (plain store)
+    reinterpret_cast<volatile int*>(p.tcount_ptrs[threadIdx.x])[p.attn_rank] = p.T;
+  if (!p.moe) {
     if (threadIdx.x == 0) p.fmask[t] = p.has_shared ? (int32_t)(1u << p.home_f) : 0;
     finish_grid(p.done_ctr, gridDim.x, [&] { publish_dispatch(p); });
   }
+  // MoE layers: the router kernel publishes; this kernel's stores are complete
+  // when it finishes, which precedes the router's release.
 }
 
 // ---- dispatch, step 2 (MoE layers): router logits on the tensor cores, top-k,
@@ -200,6 +245,8 @@ __global__ void __launch_bounds__(kRouterThreads, 1) dispatch_router_kernel(Disp
   __shared__ __align__(16) float sbuf[kRouteTile * kMaxRouteE];
   __shared__ int s_last;
   static_assert(kRouterWarps * kRouteTile * EB <= kRouteTile * kMaxRouteE, "split-K buffer");
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouteTile;
   const int nt = min(kRouteTile, p.T - t0);
@@ -295,9 +342,11 @@ __global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
   __shared__ int s_row[kWarps][kMaxSlots];
   __shared__ int s_ok;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  pdl_wait();  // before reading the epoch: the first layer's predecessor bumps it
+  pdl_launch_dependents();
+  bool ok = true;
+  if (threadIdx.x == 0 && p.flag) ok = wait_flag(p.flag, (*p.epoch) * p.arrivals, p.timeout_ns);
   if (threadIdx.x == 0) {
-    bool ok = true;
-    if (p.flag) ok = wait_flag(p.flag, (*p.epoch) * p.arrivals, p.timeout_ns);
     if (!ok) atomicExch(p.status, kStatusWaitTimeout);
     s_ok = ok;
     if (ok) {
@@ -347,9 +396,17 @@ __global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
     __syncwarp();
     if (used) {
       const bf16* src = tok + (size_t)pair * p.H;
-      for (int v = lane; v < nv; v += 32) {
-        const Vec16<bf16> xv = load16_cg(src + v * 8);
-        for (unsigned m = used; m; m &= m - 1) store16(x + (size_t)s_row[warp][__ffs(m) - 1] * p.H + v * 8, xv);
+      for (int v0 = lane; v0 < nv; v0 += 128) {
+        Vec16<bf16> xv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (v0 + u * 32 < nv) xv[u] = load16_cg(src + (v0 + u * 32) * 8);
+        for (unsigned m = used; m; m &= m - 1) {
+          bf16* dst = x + (size_t)s_row[warp][__ffs(m) - 1] * p.H;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (v0 + u * 32 < nv) store16(dst + (v0 + u * 32) * 8, xv[u]);
+        }
       }
     }
     __syncwarp();
@@ -362,9 +419,10 @@ __global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
 __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParams p) {
   __shared__ int s_pre[kMaxA + 1];
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();
   if (threadIdx.x == 0) source_prefix(p.tcount, p.A, s_pre);
   __syncthreads();
-  const int nv = p.H / 8;
   const int total = s_pre[p.A];
   for (int q = blockIdx.x * kWarps + warp; q < total; q += gridDim.x * kWarps) {
     const int a = source_of(s_pre, p.A, q);
@@ -390,27 +448,10 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
     bf16* dst = reinterpret_cast<bf16*>(p.dst_ptrs[a]) + ((size_t)t * p.num_ffn + p.f_rank) * p.H;
     if (p.echo) {
       const float wsum = warp_sum(w);
-      const bf16* row = static_cast<const bf16*>(p.staging) + (size_t)pair * p.H;
-      for (int v = lane; v < nv; v += 32) {
-        Vec16<bf16> xv = load16_cg(row + v * 8);
-#pragma unroll
-        for (int qq = 0; qq < 8; ++qq) xv.v[qq] = __float2bfloat16_rn(__bfloat162float(xv.v[qq]) * wsum);
-        store16(dst + v * 8, xv);
-      }
+      warp_sum_rows<true>(dst, static_cast<const bf16*>(p.staging) + (size_t)pair * p.H, 0, 1u, p.H, lane, wsum);
     } else {
-      const bf16* st = static_cast<const bf16*>(p.staging) + (size_t)pair * p.J * p.H;
-      for (int v = lane; v < nv; v += 32) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (unsigned m = used; m; m &= m - 1) {
-          const Vec16<bf16> xv = load16(st + (size_t)(__ffs(m) - 1) * p.H + v * 8);
-#pragma unroll
-          for (int qq = 0; qq < 8; ++qq) acc[qq] += __bfloat162float(xv.v[qq]);
-        }
-        Vec16<bf16> o;
-#pragma unroll
-        for (int qq = 0; qq < 8; ++qq) o.v[qq] = __float2bfloat16_rn(acc[qq]);
-        store16(dst + v * 8, o);
-      }
+      warp_sum_rows<false>(dst, static_cast<const bf16*>(p.staging) + (size_t)pair * p.J * p.H, (size_t)p.H, used,
+                           p.H, lane);
     }
   }
   finish_grid(p.done_ctr, gridDim.x, [&] {
@@ -422,33 +463,31 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
 __global__ void __launch_bounds__(kThreads) combine_kernel(CombineParams p) {
   __shared__ bool ok;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();
   if (threadIdx.x == 0) ok = wait_flag(p.flag + p.layer, (*p.epoch) * p.arrivals, p.timeout_ns);
   __syncthreads();
   if (!ok) {
     if (threadIdx.x == 0) atomicExch(p.status, kStatusWaitTimeout);
     return;
   }
-  const int nv = p.H / 8;
   for (int t = blockIdx.x * kWarps + warp; t < p.T; t += gridDim.x * kWarps) {
     const unsigned mask = (unsigned)p.fmask[t];
-    const bf16* base = static_cast<const bf16*>(p.comb) + (size_t)t * p.F * p.H;
-    bf16* out = static_cast<bf16*>(p.out) + (size_t)t * p.H;
-    for (int v = lane; v < nv; v += 32) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (unsigned m = mask; m; m &= m - 1) {
-        const Vec16<bf16> xv = load16_cg(base + (size_t)(__ffs(m) - 1) * p.H + v * 8);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(xv.v[q]);
-      }
-      Vec16<bf16> o;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) o.v[q] = __float2bfloat16_rn(acc[q]);
-      store16(out + v * 8, o);
-    }
+    warp_sum_rows<true>(static_cast<bf16*>(p.out) + (size_t)t * p.H,
+                        static_cast<const bf16*>(p.comb) + (size_t)t * p.F * p.H, (size_t)p.H, mask, p.H, lane);
   }
 }
 
 }  // namespace fused
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("AFD_DISABLE_PDL");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
 }  // namespace afd
 
 using namespace afd;
@@ -466,16 +505,16 @@ void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arriv
 void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s) {
   using namespace fused;
   if (p.T <= 0) return;
-  dispatch_norm_kernel<<<p.T, kThreads, 0, s>>>(p);
+  launch_pdl(dispatch_norm_kernel, dim3(p.T), dim3(kThreads), 0, s, p);
   if (!p.moe) return;
   const int mt = (p.T + kRouteTile - 1) / kRouteTile;
   const int target = 148 * 2;
   if (mt * ((p.E + 7) / 8) <= target)
-    dispatch_router_kernel<1><<<dim3(mt, (p.E + 7) / 8), kRouterThreads, 0, s>>>(p);
+    launch_pdl(dispatch_router_kernel<1>, dim3(mt, (p.E + 7) / 8), dim3(kRouterThreads), 0, s, p);
   else if (mt * ((p.E + 15) / 16) <= target)
-    dispatch_router_kernel<2><<<dim3(mt, (p.E + 15) / 16), kRouterThreads, 0, s>>>(p);
+    launch_pdl(dispatch_router_kernel<2>, dim3(mt, (p.E + 15) / 16), dim3(kRouterThreads), 0, s, p);
   else
-    dispatch_router_kernel<4><<<dim3(mt, (p.E + 31) / 32), kRouterThreads, 0, s>>>(p);
+    launch_pdl(dispatch_router_kernel<4>, dim3(mt, (p.E + 31) / 32), dim3(kRouterThreads), 0, s, p);
 }
 
 static int warp_grid(int items, int max_ctas) {
@@ -483,13 +522,13 @@ static int warp_grid(int items, int max_ctas) {
 }
 
 void launch_afd_expand(const ExpandParams& p, cudaStream_t s) {
-  fused::expand_kernel<<<warp_grid(p.A * p.t_cap, 148), fused::kThreads, 0, s>>>(p);
+  launch_pdl(fused::expand_kernel, dim3(warp_grid(p.A * p.t_cap, 148)), dim3(fused::kThreads), 0, s, p);
 }
 
 void launch_afd_combine_send(const CombineSendParams& p, cudaStream_t s) {
-  fused::combine_send_kernel<<<warp_grid(p.A * p.t_cap, 148), fused::kThreads, 0, s>>>(p);
+  launch_pdl(fused::combine_send_kernel, dim3(warp_grid(p.A * p.t_cap, 148)), dim3(fused::kThreads), 0, s, p);
 }
 
 void launch_afd_combine(const CombineParams& p, cudaStream_t s) {
-  fused::combine_kernel<<<warp_grid(p.T, 148), fused::kThreads, 0, s>>>(p);
+  launch_pdl(fused::combine_kernel, dim3(warp_grid(p.T, 148)), dim3(fused::kThreads), 0, s, p);
 }

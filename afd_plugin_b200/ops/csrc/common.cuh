@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define AFD_DEVICE __device__ __forceinline__
 
 namespace afd {
@@ -20,6 +22,35 @@ enum StatusCode : int {
   kStatusBadIndex = 2,
   kStatusBadShape = 3,
 };
+
+// ------------------------------------------------ programmatic dependent launch
+// A kernel launched with launch_pdl() may start while its predecessor on the
+// stream is finishing.  It must call pdl_wait() before it reads anything the
+// predecessor wrote (or writes anything the predecessor reads); the wait
+// returns once the predecessor grid has completed and its memory is visible.
+// pdl_launch_dependents() lets the next PDL kernel start launching.
+AFD_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+AFD_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// AFD_DISABLE_PDL=1 in the environment turns the early launch off (plain
+// stream order); the kernels' pdl_wait() then returns at once.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------- conversions
 template <typename T> AFD_DEVICE float to_f32(T v);

@@ -105,12 +105,13 @@ AFD_DEVICE uint64_t ld_acquire_sys(const uint64_t* p) {
 
 // Scatter epilogue bookkeeping: every CTA of the layer arrives once; the last
 // one clears the local expert counters and signals every Attention rank.
+// Local destinations (num_dst == 0) need device-scope ordering only.
 AFD_DEVICE void scatter_arrive(const ScatterParams& sp) {
-  __threadfence_system();
+  if (sp.num_dst > 0) __threadfence_system(); else __threadfence();
   if (atomicAdd(sp.done_ctr, 1u) == (unsigned)sp.total_ctas - 1) {
     for (int i = 0; i < sp.n_reset; ++i) sp.counts_reset[i] = 0;
     *sp.done_ctr = 0u;
-    __threadfence_system();
+    if (sp.num_dst > 0) __threadfence_system(); else __threadfence();
     for (int a = 0; a < sp.num_dst; ++a)
       asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(reinterpret_cast<uint64_t*>(sp.flag_ptrs[a]) +
                                                                      sp.layer),
@@ -180,6 +181,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // Set-up above overlaps the previous kernel; everything below reads its results.
+  pdl_wait();
+  pdl_launch_dependents();
 
   auto w_rows = [&](const Item& it, int& r0, int& r1) {
     if (EPI == 1) {
@@ -325,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       }
     }
     if (EPI == 2) {
-      __threadfence_system();
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (warp == 2 && lane == 0) scatter_arrive(sp);
     }
@@ -382,9 +385,8 @@ void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* e
       set = true;
     }
     const int grid = grouped_gemm_grid(n_tiles * e_local);
-    gg::grouped_gemm_kernel<EPI><<<grid, gg::kThreads, smem, s>>>(wmap, amap, (__nv_bfloat16*)d, expert_offsets,
-                                                                    expert_counts, n, w_stride, k, ld, n_tiles,
-                                                                    e_local, status, spv);
+    launch_pdl(gg::grouped_gemm_kernel<EPI>, dim3(grid), dim3(gg::kThreads), (size_t)smem, s, wmap, amap,
+               (__nv_bfloat16*)d, expert_offsets, expert_counts, n, w_stride, k, ld, n_tiles, e_local, status, spv);
   };
   if (epilogue == 1) {
     go(std::integral_constant<int, 1>{}, (n / 2) / 64, n / 2);
