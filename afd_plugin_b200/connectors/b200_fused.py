@@ -347,7 +347,7 @@ class FusedAttentionExecutor(FFNExecutor):
         if is_moe and gate is None:
             raise RuntimeError("fused dispatch needs the MoE gate on the Attention role")
         scoring, renorm, n_group, topk_group, k = _routing_cfg(a)
-        has_shared = (not is_moe) or a.n_shared_experts > 0
+        has_shared = (not is_moe) or a.has_shared_experts
         cfg = [a.n_routed_experts if is_moe else 1, d.top_k, scoring, renorm, n_group, topk_group, int(is_moe),
                int(has_shared), d.num_ffn, d.e_local, d.t_cap, c.role_rank, c.role_rank // d.ratio, layer_idx]
         gate_w = gate.weight if is_moe else layer.post_attention_layernorm.weight
@@ -430,6 +430,7 @@ class FusedFFNRunner:
         """Per layer: routed (w13, w2) and the home-token weights (shared experts or dense MLP)."""
         a = self.model.arch
         self.layer_w = []
+        self.shared_gate_w = []  # per MoE layer: shared-expert gate weight [1, H] or None
         for i, layer in enumerate(self.model.layers):
             mlp = layer.mlp
             if a.is_moe_layer(i):
@@ -438,13 +439,18 @@ class FusedFFNRunner:
                     raise NotImplementedError("fused FFN path: fp8 block-scaled experts not wired yet")
                 if self.n_chunks:
                     self.layer_w.append((ex.w13_all, ex.w2_all, None, None))
+                    self.shared_gate_w.append(mlp.shared_expert_gate)
                     continue
+                if mlp.shared_expert_gate is not None:
+                    raise NotImplementedError("fused FFN path: a gated shared expert needs the packed (chunked) layout")
+                self.shared_gate_w.append(None)
                 shared = mlp.shared_experts
                 sw13 = shared.w13.unsqueeze(0) if shared is not None else None
                 sw2 = shared.w2.unsqueeze(0) if shared is not None else None
                 self.layer_w.append((ex.w13, ex.w2, sw13, sw2))
             else:
                 self.layer_w.append((None, None, mlp.w13.unsqueeze(0), mlp.w2.unsqueeze(0)))
+                self.shared_gate_w.append(None)
 
     def _layer(self, layer_idx: int, s: int) -> None:
         c, d = self.c, self.c.dims
@@ -462,6 +468,16 @@ class FusedFFNRunner:
                      c.arrive[s], layer_idx, c.epoch[s : s + 1], A, c.timeout_ns)
         home_rows = c.tok[s][self.home_a0 : self.home_a0 + d.ratio].reshape(d.ratio * d.t_cap, H)
         launches = []
+        sgw = self.shared_gate_w[layer_idx]
+        if merged and sgw is not None:
+            # Gated shared expert: each home row's weight is sigmoid(x . w), set in
+            # the rows' routing weights before the down projection applies them.
+            span = self.shared_stride
+            rows = self.x[s][self.shared_base : self.shared_base + span]
+            g = torch.sigmoid(torch.mv(rows, sgw[0]).float())
+            for ch in range(n_chunks):
+                lo = self.shared_base + ch * span
+                self.rw[s][lo : lo + span].copy_(g)
         if merged:
             # routed experts and shared-expert chunks in one GEMM per projection
             ne = d.e_local + n_chunks

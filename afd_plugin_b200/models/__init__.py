@@ -18,6 +18,8 @@ from afd_plugin_b200.models.model import (
     AFDDeepseekV3ForCausalLM,
     AFDGlmMoeDsaForCausalLM,
     AFDQwen3MoeForCausalLM,
+    AFDQwen3NextForCausalLM,
+    AFDQwen3_5MoeForCausalLM,
     weight_roles,
 )
 
@@ -28,6 +30,9 @@ MODEL_REGISTRY: dict[str, type[AFDCausalLM]] = {
     "DeepseekV32ForCausalLM": AFDDeepseekV3ForCausalLM,
     "GlmMoeDsaForCausalLM": AFDGlmMoeDsaForCausalLM,
     "Qwen3MoeForCausalLM": AFDQwen3MoeForCausalLM,
+    "Qwen3NextForCausalLM": AFDQwen3NextForCausalLM,
+    "Qwen3_5MoeForCausalLM": AFDQwen3_5MoeForCausalLM,
+    "Qwen3_5MoeForConditionalGeneration": AFDQwen3_5MoeForCausalLM,
 }
 MODEL_REGISTRY.update({"AFD" + k: v for k, v in list(MODEL_REGISTRY.items())})
 

@@ -15,6 +15,8 @@ from typing import Any
 
 DEEPSEEK_ARCHS = ("DeepseekForCausalLM", "DeepseekV2ForCausalLM", "DeepseekV3ForCausalLM", "GlmMoeDsaForCausalLM")
 QWEN3_MOE_ARCHS = ("Qwen3MoeForCausalLM",)
+DEEPSEEK_V4_ARCHS = ("DeepseekV4ForCausalLM",)
+QWEN3_5_ARCHS = ("Qwen3NextForCausalLM", "Qwen3_5MoeForCausalLM", "Qwen3_5MoeForConditionalGeneration")
 
 
 @dataclass(frozen=True)
@@ -55,6 +57,26 @@ class ModelArchConfig:
     rope_scaling: dict | None = None
     max_position_embeddings: int = 4096
     tie_word_embeddings: bool = False
+    # Hybrid linear attention (Qwen3.5 / Qwen3-Next): per-layer kinds and the
+    # Gated DeltaNet shapes.  ``layer_types`` None means every layer is full attention.
+    layer_types: tuple[str, ...] | None = None
+    linear_num_key_heads: int = 0
+    linear_num_value_heads: int = 0
+    linear_key_head_dim: int = 0
+    linear_value_head_dim: int = 0
+    linear_conv_kernel_dim: int = 4
+    partial_rotary_factor: float = 1.0
+    attn_output_gate: bool = False  # full attention: output * sigmoid(gate half of q_proj)
+    shared_expert_intermediate_size: int = 0  # overrides n_shared_experts * moe_intermediate_size
+    shared_expert_gate: bool = False  # shared expert output * sigmoid(x . w)
+    norm_offset_one: bool = False  # checkpoint RMSNorm weights are stored as (w - 1)
+    # DeepSeek-V4: manifold-constrained hyper-connections (hc_mult residual
+    # streams) and hash routing (expert ids from a token-id table) in the first
+    # num_hash_layers MoE layers.
+    hc_mult: int = 0
+    hc_sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
+    num_hash_layers: int = 0
     # "fp8_block": e4m3 weights with 128x128 scales for experts and dense MLPs.
     quant: str | None = None
     weight_block_size: tuple[int, int] = (128, 128)
@@ -103,7 +125,42 @@ class ModelArchConfig:
 
     @property
     def shared_intermediate_size(self) -> int:
+        if self.shared_expert_intermediate_size:
+            return self.shared_expert_intermediate_size
         return self.moe_intermediate_size * self.n_shared_experts
+
+    @property
+    def has_shared_experts(self) -> bool:
+        return self.shared_intermediate_size > 0
+
+    def is_linear_attention_layer(self, layer_idx: int) -> bool:
+        return self.layer_types is not None and self.layer_types[layer_idx] == "linear_attention"
+
+    @property
+    def linear_attention_layers(self) -> tuple[int, ...]:
+        return tuple(i for i in range(self.num_hidden_layers) if self.is_linear_attention_layer(i))
+
+    @property
+    def full_attention_layers(self) -> tuple[int, ...]:
+        return tuple(i for i in range(self.num_hidden_layers) if not self.is_linear_attention_layer(i))
+
+    @property
+    def rotary_dim(self) -> int:
+        if self.is_mla:
+            return self.qk_rope_head_dim
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
+    def linear_key_dim(self) -> int:
+        return self.linear_num_key_heads * self.linear_key_head_dim
+
+    @property
+    def linear_value_dim(self) -> int:
+        return self.linear_num_value_heads * self.linear_value_head_dim
+
+    @property
+    def linear_conv_dim(self) -> int:
+        return 2 * self.linear_key_dim + self.linear_value_dim
 
     def scaled(self, **overrides: Any) -> "ModelArchConfig":
         return replace(self, **overrides)
@@ -126,6 +183,42 @@ class ModelArchConfig:
         if qc.get("quant_method") == "fp8":
             quant = "fp8_block"
             block = tuple(qc.get("weight_block_size", [128, 128]))
+        if arch in DEEPSEEK_V4_ARCHS or hf.get("model_type") == "deepseek_v4":
+            return cls(
+                architecture="DeepseekV4ForCausalLM",
+                hidden_size=hf["hidden_size"],
+                num_hidden_layers=hf["num_hidden_layers"],
+                vocab_size=hf["vocab_size"],
+                num_attention_heads=hf["num_attention_heads"],
+                attention_type="mla",
+                q_lora_rank=hf.get("q_lora_rank"),
+                kv_lora_rank=hf["kv_lora_rank"],
+                qk_nope_head_dim=hf["qk_nope_head_dim"],
+                qk_rope_head_dim=hf["qk_rope_head_dim"],
+                v_head_dim=hf["v_head_dim"],
+                intermediate_size=hf.get("intermediate_size", 0),
+                first_k_dense_replace=hf.get("first_k_dense_replace", 0),
+                n_routed_experts=hf["n_routed_experts"],
+                num_experts_per_tok=hf["num_experts_per_tok"],
+                moe_intermediate_size=hf["moe_intermediate_size"],
+                n_shared_experts=hf.get("n_shared_experts") or 0,
+                scoring_func=hf.get("scoring_func", "sqrtsoftplus"),
+                topk_method=hf.get("topk_method", "noaux_tc"),
+                n_group=hf.get("n_group") or 1,
+                topk_group=hf.get("topk_group") or 1,
+                norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
+                routed_scaling_factor=float(hf.get("routed_scaling_factor", 1.5)),
+                rms_norm_eps=hf.get("rms_norm_eps", 1e-6),
+                rope_theta=hf.get("rope_theta", 10000.0),
+                rope_scaling=hf.get("rope_scaling"),
+                max_position_embeddings=hf.get("max_position_embeddings", 65536),
+                hc_mult=hf["hc_mult"],
+                hc_sinkhorn_iters=hf.get("hc_sinkhorn_iters", 20),
+                hc_eps=hf.get("hc_eps", 1e-6),
+                num_hash_layers=hf.get("num_hash_layers", 0),
+                quant=quant,
+                weight_block_size=block,
+            )
         if arch in DEEPSEEK_ARCHS or hf.get("model_type", "").startswith("deepseek"):
             return cls(
                 architecture=arch or "DeepseekV2ForCausalLM",
@@ -187,6 +280,49 @@ class ModelArchConfig:
                 rope_scaling=hf.get("rope_scaling"),
                 max_position_embeddings=hf.get("max_position_embeddings", 40960),
                 tie_word_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                quant=quant,
+                weight_block_size=block,
+            )
+        if arch in QWEN3_5_ARCHS or hf.get("model_type") in ("qwen3_next", "qwen3_5_moe", "qwen3_5_moe_text"):
+            L = hf["num_hidden_layers"]
+            types = hf.get("layer_types")
+            if types is None:
+                interval = hf.get("full_attention_interval", 4)
+                types = ["full_attention" if (i + 1) % interval == 0 else "linear_attention" for i in range(L)]
+            if hf.get("mlp_only_layers"):
+                raise ValueError("Qwen3.5 mlp_only_layers are not supported")
+            return cls(
+                architecture=arch if arch in QWEN3_5_ARCHS else "Qwen3NextForCausalLM",
+                hidden_size=hf["hidden_size"],
+                num_hidden_layers=L,
+                vocab_size=hf["vocab_size"],
+                num_attention_heads=hf["num_attention_heads"],
+                attention_type="gqa",
+                num_key_value_heads=hf["num_key_value_heads"],
+                head_dim=hf.get("head_dim") or hf["hidden_size"] // hf["num_attention_heads"],
+                qk_norm=True,
+                intermediate_size=hf.get("intermediate_size", 0),
+                moe_layer_freq=hf.get("decoder_sparse_step", 1),
+                n_routed_experts=hf["num_experts"],
+                num_experts_per_tok=hf["num_experts_per_tok"],
+                moe_intermediate_size=hf["moe_intermediate_size"],
+                shared_expert_intermediate_size=hf.get("shared_expert_intermediate_size", 0),
+                shared_expert_gate=bool(hf.get("shared_expert_intermediate_size", 0)),
+                norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
+                rms_norm_eps=hf.get("rms_norm_eps", 1e-6),
+                rope_theta=hf.get("rope_theta", 10000000.0),
+                rope_scaling=hf.get("rope_scaling"),
+                max_position_embeddings=hf.get("max_position_embeddings", 262144),
+                tie_word_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                layer_types=tuple(types),
+                linear_num_key_heads=hf["linear_num_key_heads"],
+                linear_num_value_heads=hf["linear_num_value_heads"],
+                linear_key_head_dim=hf["linear_key_head_dim"],
+                linear_value_head_dim=hf["linear_value_head_dim"],
+                linear_conv_kernel_dim=hf.get("linear_conv_kernel_dim", 4),
+                partial_rotary_factor=float(hf.get("partial_rotary_factor", 0.25)),
+                attn_output_gate=True,
+                norm_offset_one=True,
                 quant=quant,
                 weight_block_size=block,
             )
@@ -367,6 +503,92 @@ TINY_DSV2_MLA512 = TINY_DSV2.scaled(
     kv_lora_rank=512, qk_rope_head_dim=64, qk_nope_head_dim=128, v_head_dim=128, num_attention_heads=16
 )
 
+# Qwen3-Next-80B-A3B shapes (the published config of the Qwen3.5 / Qwen3-Next
+# hybrid family): 48 layers, every 4th full attention, 512 experts top-10.
+QWEN3_NEXT_80B_A3B = ModelArchConfig(
+    architecture="Qwen3NextForCausalLM",
+    hidden_size=2048,
+    num_hidden_layers=48,
+    vocab_size=151936,
+    num_attention_heads=16,
+    attention_type="gqa",
+    num_key_value_heads=2,
+    head_dim=256,
+    qk_norm=True,
+    intermediate_size=5120,
+    n_routed_experts=512,
+    num_experts_per_tok=10,
+    moe_intermediate_size=512,
+    shared_expert_intermediate_size=512,
+    shared_expert_gate=True,
+    norm_topk_prob=True,
+    rms_norm_eps=1e-6,
+    rope_theta=10000000.0,
+    max_position_embeddings=262144,
+    layer_types=tuple("full_attention" if (i + 1) % 4 == 0 else "linear_attention" for i in range(48)),
+    linear_num_key_heads=16,
+    linear_num_value_heads=32,
+    linear_key_head_dim=128,
+    linear_value_head_dim=128,
+    linear_conv_kernel_dim=4,
+    partial_rotary_factor=0.25,
+    attn_output_gate=True,
+    norm_offset_one=True,
+)
+
+TINY_QWEN3_5 = QWEN3_NEXT_80B_A3B.scaled(
+    architecture="Qwen3_5MoeForCausalLM",
+    hidden_size=256,
+    num_hidden_layers=4,
+    vocab_size=1024,
+    num_attention_heads=4,
+    num_key_value_heads=2,
+    head_dim=64,
+    n_routed_experts=8,
+    num_experts_per_tok=2,
+    moe_intermediate_size=128,
+    shared_expert_intermediate_size=128,
+    max_position_embeddings=2048,
+    layer_types=("linear_attention", "linear_attention", "linear_attention", "full_attention"),
+    linear_num_key_heads=2,
+    linear_num_value_heads=4,
+    linear_key_head_dim=32,
+    linear_value_head_dim=32,
+)
+
+
+# DeepSeek-V4-style test shapes: MLA attention, 4 mHC residual streams, hash
+# routing in the first MoE layer, sqrt-softplus scoring with a selection bias.
+TINY_DSV4 = ModelArchConfig(
+    architecture="DeepseekV4ForCausalLM",
+    hidden_size=256,
+    num_hidden_layers=3,
+    vocab_size=1024,
+    num_attention_heads=4,
+    attention_type="mla",
+    q_lora_rank=64,
+    kv_lora_rank=64,
+    qk_nope_head_dim=32,
+    qk_rope_head_dim=32,
+    v_head_dim=32,
+    intermediate_size=512,
+    first_k_dense_replace=1,
+    n_routed_experts=8,
+    num_experts_per_tok=2,
+    moe_intermediate_size=128,
+    n_shared_experts=1,
+    scoring_func="sqrtsoftplus",
+    topk_method="noaux_tc",
+    norm_topk_prob=True,
+    routed_scaling_factor=1.5,
+    max_position_embeddings=2048,
+    hc_mult=4,
+    hc_sinkhorn_iters=20,
+    hc_eps=1e-6,
+    num_hash_layers=2,
+)
+
+
 PRESETS: dict[str, ModelArchConfig] = {
     "tiny-dsv2-mla512": TINY_DSV2_MLA512,
     "tiny-dsv2": TINY_DSV2,
@@ -375,6 +597,9 @@ PRESETS: dict[str, ModelArchConfig] = {
     "deepseek-v2-lite": DSV2_LITE,
     "qwen3-30b-a3b": QWEN3_30B_A3B,
     "deepseek-v3-32l": DSV3_32L,
+    "tiny-qwen3.5": TINY_QWEN3_5,
+    "tiny-dsv4": TINY_DSV4,
+    "qwen3-next-80b-a3b": QWEN3_NEXT_80B_A3B,
 }
 
 
@@ -391,8 +616,11 @@ __all__ = [
     "ModelArchConfig",
     "PRESETS",
     "QWEN3_30B_A3B",
+    "QWEN3_NEXT_80B_A3B",
+    "TINY_QWEN3_5",
     "TINY_DSV2",
     "TINY_DSV3",
+    "TINY_DSV4",
     "TINY_QWEN3_MOE",
     "get_preset",
     "yarn_get_mscale",

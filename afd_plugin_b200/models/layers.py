@@ -7,6 +7,8 @@ fp32 CPU oracle and the bf16 sm_100a path.
 
 from __future__ import annotations
 
+import math
+
 from dataclasses import dataclass
 
 import torch
@@ -35,6 +37,21 @@ class AttentionMetadata:
     seq_lens: torch.Tensor  # [B] int32
     is_decode: bool = True
     prefill_seqs: list[tuple[int, int, int]] | None = None
+    # Linear-attention (Gated DeltaNet) layers: per-sequence recurrent state.
+    # state_slots [S] picks each sequence's state row, cu_seqlens [S + 1]
+    # bounds its tokens, state_reset [S] starts it from a zero state.  None on
+    # a decode step means one token per sequence with slot = row.
+    state_slots: torch.Tensor | None = None
+    cu_seqlens: torch.Tensor | None = None
+    state_reset: torch.Tensor | None = None
+
+    def linear_state_args(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+        if self.state_slots is not None:
+            return self.cu_seqlens, self.state_slots, self.state_reset
+        T = self.num_tokens
+        dev = self.positions.device
+        rows = torch.arange(T + 1, dtype=torch.int32, device=dev)
+        return rows, rows[:T], None
 
     @property
     def num_tokens(self) -> int:
@@ -188,6 +205,156 @@ class GQAAttention(nn.Module):
         return ops.linear(o.reshape(T, self.nq * self.d), self.o_proj)
 
 
+
+class GatedDeltaNet(nn.Module):
+    """Gated DeltaNet linear attention (Qwen3.5 / Qwen3-Next ``linear_attn``).
+
+    One input projection ``in_proj [conv_dim + value_dim + 2 nv, H]`` with
+    rows ordered q | k | v | z | b | a (the checkpoint's per-key-head grouped
+    ``in_proj_qkvz`` / ``in_proj_ba`` rows are regrouped at load time), a
+    depthwise causal convolution over q | k | v with a rolling state, the gated
+    delta rule with an fp32 recurrent state per (sequence, value head), the
+    gated RMSNorm and ``out_proj``.  Behaviour of the layer the reference's
+    Qwen3.5 wrapper runs natively (``afd_plugin/model_executor/models/qwen3_5.py``,
+    Attention-owned ``linear_attn``).
+    """
+
+    def __init__(self, arch: ModelArchConfig, dtype, device):
+        super().__init__()
+        self.arch = arch
+        self.nk, self.nv = arch.linear_num_key_heads, arch.linear_num_value_heads
+        self.dk, self.dv = arch.linear_key_head_dim, arch.linear_value_head_dim
+        self.K = arch.linear_conv_kernel_dim
+        self.key_dim, self.value_dim = arch.linear_key_dim, arch.linear_value_dim
+        self.conv_dim = arch.linear_conv_dim
+        H = arch.hidden_size
+        self.in_proj = _param((self.conv_dim + self.value_dim + 2 * self.nv, H), dtype, device)
+        self.conv_weight = _param((self.conv_dim, self.K), dtype, device)
+        self.A_log = _param((self.nv,), torch.float32, device)
+        self.dt_bias = _param((self.nv,), torch.float32, device)
+        self.norm_weight = _param((self.dv,), dtype, device)
+        self.out_proj = _param((H, self.value_dim), dtype, device)
+        self.eps = arch.rms_norm_eps
+
+    # checkpoint layout -> fused rows
+    def set_in_proj_qkvz(self, w: torch.Tensor) -> None:
+        r = self.nv // self.nk
+        g = w.view(self.nk, 2 * self.dk + 2 * r * self.dv, -1)
+        q, k = g[:, : self.dk], g[:, self.dk : 2 * self.dk]
+        v = g[:, 2 * self.dk : 2 * self.dk + r * self.dv]
+        z = g[:, 2 * self.dk + r * self.dv :]
+        rows = torch.cat([t.reshape(-1, t.shape[-1]) for t in (q, k, v, z)])
+        self.in_proj.data[: self.conv_dim + self.value_dim].copy_(rows.to(self.in_proj.device, self.in_proj.dtype))
+
+    def set_in_proj_ba(self, w: torch.Tensor) -> None:
+        r = self.nv // self.nk
+        g = w.view(self.nk, 2 * r, -1)
+        rows = torch.cat([g[:, :r].reshape(-1, g.shape[-1]), g[:, r:].reshape(-1, g.shape[-1])])
+        self.in_proj.data[self.conv_dim + self.value_dim :].copy_(rows.to(self.in_proj.device, self.in_proj.dtype))
+
+    def _cuda_ok(self, h: torch.Tensor) -> bool:
+        return (h.is_cuda and self.dk in (32, 64, 128) and self.dv % 32 == 0 and self.dv >= self.dk
+                and (self.dk < 128 or self.dv <= 128) and 2 <= self.K <= 8)
+
+    def forward(self, h: torch.Tensor, meta: AttentionMetadata, state: tuple[torch.Tensor, torch.Tensor], cos_sin=None):
+        conv_state, ssm_state = state
+        proj = ops.linear(h, self.in_proj)
+        cd, vd, nv = self.conv_dim, self.value_dim, self.nv
+        z = proj[:, cd : cd + vd]
+        b = proj[:, cd + vd : cd + vd + nv]
+        a = proj[:, cd + vd + nv :]
+        cu, slots, reset = meta.linear_state_args()
+        if self._cuda_ok(h):
+            C = ops._cuda_ops()
+            conv = C.gdn_conv(proj[:, :cd], self.conv_weight, conv_state, cu, slots, reset)
+            o = C.gdn_recurrent(conv, z, a, b, self.A_log, self.dt_bias, self.norm_weight, self.eps, ssm_state, cu,
+                                slots, reset, self.nk)
+            return ops.linear(o, self.out_proj)
+        return ops.linear(self._forward_reference(proj, z, a, b, conv_state, ssm_state, cu, slots, reset).to(h.dtype),
+                          self.out_proj)
+
+    def _forward_reference(self, proj, z, a, b, conv_state, ssm_state, cu, slots, reset) -> torch.Tensor:
+        from afd_plugin_b200.ops import reference as ref
+
+        T = proj.shape[0]
+        nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
+        r = nv // nk
+        out = torch.empty(T, nv * dv, device=proj.device)
+        cu_l = cu.tolist()
+        for i, sl in enumerate(slots.tolist()):
+            t0, t1 = cu_l[i], cu_l[i + 1]
+            fresh = reset is not None and bool(reset[i])
+            n = t1 - t0
+            if n == 0:
+                continue
+            conv, new_conv = ref.causal_conv1d(proj[t0:t1, : self.conv_dim], self.conv_weight,
+                                               None if fresh else conv_state[sl])
+            conv_state[sl].copy_(new_conv.to(conv_state.dtype))
+            conv = conv.to(proj.dtype).float()
+            q = conv[:, : nk * dk].view(n, nk, dk).repeat_interleave(r, dim=1)
+            k = conv[:, nk * dk : 2 * nk * dk].view(n, nk, dk).repeat_interleave(r, dim=1)
+            v = conv[:, 2 * nk * dk :].view(n, nv, dv)
+            g, beta = ref.gdn_gates(a[t0:t1], b[t0:t1], self.A_log, self.dt_bias)
+            o, st = ref.gated_delta_rule(q, k, v, g, beta, None if fresh else ssm_state[sl])
+            ssm_state[sl].copy_(st)
+            out[t0:t1] = ref.rms_norm_gated(o, z[t0:t1].view(n, nv, dv), self.norm_weight, self.eps).reshape(n, -1)
+        return out
+
+
+class GatedGQAAttention(nn.Module):
+    """Full attention of the Qwen3.5 / Qwen3-Next family.
+
+    ``q_proj`` emits a query and an output gate per head (checkpoint rows
+    interleaved per head: query d, gate d); per-head QK RMSNorm; RoPE on the
+    first ``rotary_dim`` dims (NeoX pairing); GQA over the paged cache;
+    ``o_proj(attn * sigmoid(gate))``.
+    """
+
+    def __init__(self, arch: ModelArchConfig, dtype, device):
+        super().__init__()
+        self.arch = arch
+        self.nq, self.nkv, self.d = arch.num_attention_heads, arch.num_key_value_heads, arch.head_dim
+        self.rot = arch.rotary_dim
+        self.scale = 1.0 / math.sqrt(self.d)
+        H = arch.hidden_size
+        # rows: q (nq d) | gate (nq d) | k (nkv d) | v (nkv d)
+        self.qkv_proj = _param(((2 * self.nq + 2 * self.nkv) * self.d, H), dtype, device)
+        self.q_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
+        self.k_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
+        self.o_proj = _param((H, self.nq * self.d), dtype, device)
+
+    def set_q_proj(self, w: torch.Tensor) -> None:
+        g = w.view(self.nq, 2, self.d, -1)
+        nqd = self.nq * self.d
+        self.qkv_proj.data[:nqd].copy_(g[:, 0].reshape(nqd, -1).to(self.qkv_proj.device, self.qkv_proj.dtype))
+        self.qkv_proj.data[nqd : 2 * nqd].copy_(g[:, 1].reshape(nqd, -1).to(self.qkv_proj.device, self.qkv_proj.dtype))
+
+    def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache: tuple[torch.Tensor, torch.Tensor], cos_sin):
+        T = h.shape[0]
+        nq, nkv, d = self.nq, self.nkv, self.d
+        qkv = ops.linear(h, self.qkv_proj)
+        q, gate, k, v = qkv.split([nq * d, nq * d, nkv * d, nkv * d], dim=-1)
+        q = self.q_norm(q.reshape(T * nq, d)).view(T, nq, d)
+        k = self.k_norm(k.reshape(T * nkv, d)).view(T, nkv, d)
+        v = v.reshape(T, nkv, d)
+        ops.rope_(q[..., : self.rot], meta.positions, cos_sin, interleaved=False)
+        ops.rope_(k[..., : self.rot], meta.positions, cos_sin, interleaved=False)
+        k_cache, v_cache = kv_cache
+        ops.gqa_cache_write(k_cache, v_cache, k, v, meta.slot_mapping)
+        if meta.is_decode:
+            o = ops.gqa_decode(q, k_cache, v_cache, meta.block_table, meta.seq_lens, self.scale)
+        else:
+            from afd_plugin_b200.ops import reference as ref
+
+            o = torch.empty_like(q)
+            for start, end, seq in meta.prefill_seqs or []:
+                o[start:end] = ref.gqa_prefill(
+                    q[start:end], k_cache, v_cache, meta.block_table[seq], meta.positions[start:end], self.scale
+                )
+        o = o.reshape(T, nq * d) * torch.sigmoid(gate.float()).to(o.dtype)
+        return ops.linear(o, self.o_proj)
+
+
 class DenseMLP(nn.Module):
     """SwiGLU MLP with gate and up stacked in ``w13 [2I, H]``."""
 
@@ -308,14 +475,15 @@ class MoEBlock(nn.Module):
             raise ValueError(f"{E} experts do not split over {ep_size} expert-parallel ranks")
         n_local = E // ep_size
         self.gate = MoEGate(arch, dtype, device) if with_gate else None
-        chunked = (arch.n_shared_experts > 0 and arch.quant is None and arch.moe_intermediate_size % 64 == 0)
-        self.n_shared_chunks = arch.n_shared_experts if chunked else 0
+        I, Is = arch.moe_intermediate_size, arch.shared_intermediate_size
+        chunked = (Is > 0 and arch.quant is None and I % 64 == 0 and Is % I == 0)
+        self.n_shared_chunks = Is // I if chunked else 0
         self.experts = RoutedExperts(arch, n_local, ep_rank * n_local, dtype, device, n_extra=self.n_shared_chunks)
         self.shared_experts = (
-            DenseMLP(arch.hidden_size, arch.shared_intermediate_size, dtype, device, arch.quant)
-            if arch.n_shared_experts
-            else None
+            DenseMLP(arch.hidden_size, Is, dtype, device, arch.quant) if arch.has_shared_experts else None
         )
+        # Qwen3.5 / Qwen3-Next: the shared expert's output is scaled by sigmoid(x . w) per token.
+        self.shared_expert_gate = _param((1, arch.hidden_size), dtype, device) if arch.shared_expert_gate else None
 
     def finalize(self) -> None:
         if self.shared_experts is not None:
@@ -334,14 +502,26 @@ class MoEBlock(nn.Module):
     def forward_experts(self, h: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
                         include_shared: bool = True) -> torch.Tensor:
         ex = self.experts
+        sg = self.shared_gate(h) if include_shared else None
         if h.is_cuda and include_shared and self.n_shared_chunks:
-            # Routed and shared experts in the same grouped GEMMs.
-            return ops.moe_experts(h, ex.w13_all, ex.w2_all, topk_weights, topk_ids, expert_offset=ex.offset,
+            # Routed and shared experts in the same grouped GEMMs; with a shared
+            # gate its per-token weight rides along as the chunks' routing weight.
+            w = topk_weights
+            if sg is not None:
+                w = torch.cat([topk_weights.float(), sg.expand(-1, self.n_shared_chunks)], dim=1)
+            return ops.moe_experts(h, ex.w13_all, ex.w2_all, w, topk_ids, expert_offset=ex.offset,
                                    n_shared=self.n_shared_chunks)
         out = ex(h, topk_weights, topk_ids)
         if include_shared and self.shared_experts is not None:
-            out = out + self.shared_experts(h)
+            s = self.shared_experts(h)
+            out = out + (s if sg is None else (s.float() * sg).to(s.dtype))
         return out
+
+    def shared_gate(self, h: torch.Tensor) -> torch.Tensor | None:
+        """sigmoid(h . w_sg) [T, 1] fp32, or None without a shared-expert gate."""
+        if self.shared_expert_gate is None:
+            return None
+        return torch.sigmoid(h.float() @ self.shared_expert_gate.float().t())
 
 
 __all__ = [

@@ -35,6 +35,8 @@ from afd_plugin_b200.models.configs import ModelArchConfig
 from afd_plugin_b200.models.layers import (
     AttentionMetadata,
     DenseMLP,
+    GatedDeltaNet,
+    GatedGQAAttention,
     GQAAttention,
     MLAAttention,
     MoEBlock,
@@ -76,7 +78,7 @@ def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention:
             continue
         stage = parts[i + 2]
         rest = parts[i + 3 :]
-        if stage == "self_attn":
+        if stage in ("self_attn", "linear_attn"):
             return _ATTN
         if stage != "mlp":
             return _BOTH
@@ -99,8 +101,16 @@ class DecoderLayer(nn.Module):
         self.input_layernorm = RMSNorm(arch.hidden_size, eps, dtype, device) if has_attn else None
         self.post_attention_layernorm = RMSNorm(arch.hidden_size, eps, dtype, device) if has_attn else None
         self.self_attn = None
+        self.is_linear_attn = arch.is_linear_attention_layer(idx)
         if has_attn:
-            self.self_attn = MLAAttention(arch, dtype, device) if arch.is_mla else GQAAttention(arch, dtype, device)
+            if self.is_linear_attn:
+                self.self_attn = GatedDeltaNet(arch, dtype, device)
+            elif arch.attn_output_gate:
+                self.self_attn = GatedGQAAttention(arch, dtype, device)
+            elif arch.is_mla:
+                self.self_attn = MLAAttention(arch, dtype, device)
+            else:
+                self.self_attn = GQAAttention(arch, dtype, device)
         self.mlp: nn.Module | None = None
         self.gate_only = None
         if role == "colocated":
@@ -161,7 +171,7 @@ class AFDCausalLM(nn.Module):
         self.lm_head = _param((arch.vocab_size, arch.hidden_size), dtype, device) if has_attn else None
         self.cos_sin = None
         if has_attn:
-            rot = arch.qk_rope_head_dim if arch.is_mla else arch.head_dim
+            rot = arch.rotary_dim
             npos = max_positions or min(arch.max_position_embeddings, 8192)
             self.cos_sin = ref.rope_cos_sin_cache(rot, npos, arch.rope_theta, arch.rope_scaling, device)
 
@@ -411,6 +421,93 @@ class AFDQwen3MoeForCausalLM(AFDCausalLM):
         yield ParamSpec(p + "o_proj.weight", tuple(attn.o_proj.shape), _copy(attn.o_proj))
 
 
+def _copy_plus_one(dst: torch.Tensor) -> Callable[[torch.Tensor], None]:
+    """Zero-centred RMSNorm weight: the checkpoint stores (w - 1)."""
+
+    def setter(src: torch.Tensor) -> None:
+        dst.data.copy_((src.float() + 1.0).to(dst.device, dst.dtype))
+
+    return setter
+
+
+class AFDQwen3_5MoeForCausalLM(AFDCausalLM):
+    """Qwen3.5 / Qwen3-Next MoE: Gated DeltaNet + gated full attention, MoE with a gated shared expert.
+
+    Roles as in the reference wrapper (``afd_plugin/model_executor/models/qwen3_5.py:46-73``):
+    ``linear_attn`` / ``self_attn`` / norms / embeddings / LM head on the
+    Attention side; the MoE gate, routed experts, shared expert and shared-expert
+    gate on the FFN side (the gate is also loaded on the Attention side when the
+    fused connector routes there).  Text-only.
+    """
+
+    family = "qwen3_5"
+
+    def _validate_arch(self, arch: ModelArchConfig) -> None:
+        if arch.layer_types is None or not arch.attn_output_gate or arch.is_mla:
+            raise ValueError("Qwen3.5 wrapper requires hybrid layer_types with gated GQA full attention")
+        if arch.first_k_dense_replace or arch.moe_layer_freq != 1:
+            raise ValueError("Qwen3.5 wrapper expects every layer to be an MoE layer")
+
+    def param_specs(self) -> Iterator[ParamSpec]:
+        a = self.arch
+        H = a.hidden_size
+        if self.embed_tokens is not None:
+            yield ParamSpec("model.embed_tokens.weight", tuple(self.embed_tokens.shape), _copy(self.embed_tokens))
+            yield ParamSpec("model.norm.weight", (H,), _copy_plus_one(self.norm.weight), "zeros")
+            yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
+        for i, layer in enumerate(self.layers):
+            p = f"model.layers.{i}."
+            if layer.input_layernorm is not None:
+                yield ParamSpec(p + "input_layernorm.weight", (H,), _copy_plus_one(layer.input_layernorm.weight), "zeros")
+                yield ParamSpec(p + "post_attention_layernorm.weight", (H,),
+                                _copy_plus_one(layer.post_attention_layernorm.weight), "zeros")
+                if layer.is_linear_attn:
+                    yield from self._linear_attn_specs(p + "linear_attn.", layer.self_attn)
+                else:
+                    yield from self._gated_attn_specs(p + "self_attn.", layer.self_attn)
+            if layer.gate_only is not None:
+                yield from _gate_specs(p + "mlp.gate.", layer.gate_only)
+            mlp = layer.mlp
+            if isinstance(mlp, MoEBlock):
+                if mlp.gate is not None:
+                    yield from _gate_specs(p + "mlp.gate.", mlp.gate)
+                ex = mlp.experts
+                I = a.moe_intermediate_size
+                for le in range(ex.n_local):
+                    q = f"{p}mlp.experts.{ex.offset + le}."
+                    yield from _swiglu_specs(q, ex.w13[le], ex.w2[le], None, None, I, H)
+                if mlp.shared_experts is not None:
+                    yield from _mlp_specs(p + "mlp.shared_expert.", mlp.shared_experts, a.shared_intermediate_size)
+                if mlp.shared_expert_gate is not None:
+                    yield ParamSpec(p + "mlp.shared_expert_gate.weight", (1, H), _copy(mlp.shared_expert_gate))
+
+    def _linear_attn_specs(self, p: str, la: GatedDeltaNet) -> Iterator[ParamSpec]:
+        H = self.arch.hidden_size
+        yield ParamSpec(p + "in_proj_qkvz.weight", (2 * la.key_dim + 2 * la.value_dim, H), la.set_in_proj_qkvz)
+        yield ParamSpec(p + "in_proj_ba.weight", (2 * la.nv, H), la.set_in_proj_ba)
+        yield ParamSpec(p + "conv1d.weight", (la.conv_dim, 1, la.K),
+                        lambda t, _w=la.conv_weight: _w.data.copy_(t.reshape(_w.shape).to(_w.device, _w.dtype)))
+        yield ParamSpec(p + "dt_bias", (la.nv,), _copy(la.dt_bias), "ones")
+        yield ParamSpec(p + "A_log", (la.nv,), _copy(la.A_log), "zeros")
+        yield ParamSpec(p + "norm.weight", (la.dv,), _copy(la.norm_weight), "ones")
+        yield ParamSpec(p + "out_proj.weight", (H, la.value_dim), _copy(la.out_proj))
+
+    def _gated_attn_specs(self, p: str, at: GatedGQAAttention) -> Iterator[ParamSpec]:
+        H = self.arch.hidden_size
+        nq, nkv, d = at.nq, at.nkv, at.d
+        base = 2 * nq * d
+        yield ParamSpec(p + "q_proj.weight", (2 * nq * d, H), at.set_q_proj)
+        yield ParamSpec(p + "k_proj.weight", (nkv * d, H), _rows(at.qkv_proj, base, base + nkv * d))
+        yield ParamSpec(p + "v_proj.weight", (nkv * d, H), _rows(at.qkv_proj, base + nkv * d, base + 2 * nkv * d))
+        yield ParamSpec(p + "q_norm.weight", (d,), _copy_plus_one(at.q_norm.weight), "zeros")
+        yield ParamSpec(p + "k_norm.weight", (d,), _copy_plus_one(at.k_norm.weight), "zeros")
+        yield ParamSpec(p + "o_proj.weight", (H, nq * d), _copy(at.o_proj))
+
+
+class AFDQwen3NextForCausalLM(AFDQwen3_5MoeForCausalLM):
+    pass
+
+
 __all__ = [
     "AFDCausalLM",
     "AFDDeepseekForCausalLM",
@@ -418,6 +515,8 @@ __all__ = [
     "AFDDeepseekV3ForCausalLM",
     "AFDGlmMoeDsaForCausalLM",
     "AFDQwen3MoeForCausalLM",
+    "AFDQwen3NextForCausalLM",
+    "AFDQwen3_5MoeForCausalLM",
     "ParamSpec",
     "ROLES",
     "weight_roles",

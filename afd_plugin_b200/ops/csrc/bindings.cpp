@@ -548,6 +548,83 @@ at::Tensor grouped_gemm_ex(const at::Tensor& a, const at::Tensor& w, const at::T
   return d;
 }
 
+// ------------------------------------------------------------------ gated delta net
+// x [T, >= C] (last dim contiguous, rows may be strided); weight [C, K]; state [slots, C, K - 1].
+at::Tensor gdn_conv(const at::Tensor& x, const at::Tensor& weight, at::Tensor& state, const at::Tensor& cu_seqlens,
+                    const at::Tensor& slots, const c10::optional<at::Tensor>& reset) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && weight.scalar_type() == at::kBFloat16 &&
+                  state.scalar_type() == at::kBFloat16, "gdn_conv: bf16 tensors");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && weight.is_contiguous() && state.is_contiguous(), "gdn_conv: layout");
+  const int C = (int)weight.size(0), K = (int)weight.size(1);
+  TORCH_CHECK(K >= 2 && K <= 8 && x.size(1) >= C && state.size(1) == C && state.size(2) == K - 1,
+              "gdn_conv: 2 <= K <= 8, state [slots, C, K - 1]");
+  TORCH_CHECK(cu_seqlens.scalar_type() == at::kInt && slots.scalar_type() == at::kInt, "gdn_conv: int32 metadata");
+  auto y = at::empty({x.size(0), C}, x.options());
+  GdnConvParams p{};
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  p.ldx = x.stride(0);
+  p.weight = reinterpret_cast<const __nv_bfloat16*>(weight.data_ptr());
+  p.state = reinterpret_cast<__nv_bfloat16*>(state.data_ptr());
+  p.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  p.cu_seqlens = cu_seqlens.data_ptr<int32_t>();
+  p.slots = slots.data_ptr<int32_t>();
+  p.reset = (reset.has_value() && reset->defined()) ? reset->data_ptr<int32_t>() : nullptr;
+  p.num_seqs = (int)slots.size(0);
+  p.C = C;
+  p.K = K;
+  if (p.num_seqs == 0 || x.size(0) == 0) return y;
+  c10::cuda::CUDAGuard g(x.device());
+  launch_gdn_conv(p, stream());
+  return y;
+}
+
+// qkv [T, 2 nk dk + nv dv] (q | k | v); z [T, nv dv]; a, b [T, nv]; state [slots, nv, dk, dv] fp32.
+at::Tensor gdn_recurrent(const at::Tensor& qkv, const at::Tensor& z, const at::Tensor& a, const at::Tensor& b,
+                         const at::Tensor& A_log, const at::Tensor& dt_bias, const at::Tensor& norm_w, double eps,
+                         at::Tensor& state, const at::Tensor& cu_seqlens, const at::Tensor& slots,
+                         const c10::optional<at::Tensor>& reset, int64_t nk) {
+  check_cuda(qkv, "qkv");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && z.scalar_type() == at::kBFloat16 &&
+                  a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gdn_recurrent: bf16 inputs");
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 4,
+              "gdn_recurrent: fp32 state [slots, nv, dk, dv]");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat, "gdn_recurrent: fp32 A_log / dt_bias");
+  TORCH_CHECK(qkv.stride(1) == 1 && z.stride(1) == 1 && a.stride(1) == 1 && b.stride(1) == 1 && a.stride(0) == b.stride(0),
+              "gdn_recurrent: last dims contiguous, a / b with one row stride");
+  const int nv = (int)state.size(1), dk = (int)state.size(2), dv = (int)state.size(3);
+  TORCH_CHECK(nk > 0 && nv % nk == 0 && dv >= dk && dv % 32 == 0 && dv <= 256 && norm_w.numel() == dv,
+              "gdn_recurrent: nv % nk == 0, dk <= dv <= 256, dv % 32 == 0");
+  TORCH_CHECK(qkv.size(1) >= 2 * nk * dk + nv * dv && z.size(1) >= nv * dv && a.size(1) >= nv, "gdn_recurrent: widths");
+  auto out = at::empty({qkv.size(0), (int64_t)nv * dv}, qkv.options());
+  GdnRecurrentParams p{};
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  p.ld_qkv = qkv.stride(0);
+  p.z = reinterpret_cast<const __nv_bfloat16*>(z.data_ptr());
+  p.ld_z = z.stride(0);
+  p.a = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+  p.b = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr());
+  p.ld_ab = a.stride(0);
+  p.A_log = A_log.data_ptr<float>();
+  p.dt_bias = dt_bias.data_ptr<float>();
+  p.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr());
+  p.eps = (float)eps;
+  p.state = state.data_ptr<float>();
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.cu_seqlens = cu_seqlens.data_ptr<int32_t>();
+  p.slots = slots.data_ptr<int32_t>();
+  p.reset = (reset.has_value() && reset->defined()) ? reset->data_ptr<int32_t>() : nullptr;
+  p.num_seqs = (int)slots.size(0);
+  p.nk = (int)nk;
+  p.nv = nv;
+  p.dk = dk;
+  p.dv = dv;
+  if (p.num_seqs == 0 || qkv.size(0) == 0) return out;
+  c10::cuda::CUDAGuard g(qkv.device());
+  TORCH_CHECK(launch_gdn_recurrent(p, stream()), "gdn_recurrent: key head dim must be 32, 64 or 128");
+  return out;
+}
+
 // ------------------------------------------------------------------ status
 int64_t gg_grid(int64_t n_items) { return grouped_gemm_grid((int)n_items); }
 
@@ -577,6 +654,9 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("moe_combine(Tensor ys, Tensor topk_w, Tensor token_slot_row, Tensor? shared) -> Tensor");
   m.def("decode_advance(Tensor(a!) input_ids, Tensor(b!) positions, Tensor(c!) slots, Tensor(d!) seq_lens, "
         "Tensor next_tokens, Tensor block_table, int block_size, int wrap_at, int wrap_to) -> ()");
+  m.def("gdn_conv(Tensor x, Tensor weight, Tensor(a!) state, Tensor cu_seqlens, Tensor slots, Tensor? reset) -> Tensor");
+  m.def("gdn_recurrent(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor A_log, Tensor dt_bias, Tensor norm_w, "
+        "float eps, Tensor(a!) state, Tensor cu_seqlens, Tensor slots, Tensor? reset, int nk) -> Tensor");
   m.def("afd_epoch(Tensor(a!) epoch) -> ()");
   m.def("afd_wait(Tensor flag, int index, Tensor epoch, int arrivals, int timeout_ns) -> ()");
   m.def("afd_dispatch(Tensor attn_out, Tensor(a!) residual, Tensor norm_w, float eps, Tensor gate_w, Tensor? gate_bias, "
@@ -613,6 +693,8 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("moe_combine", &moe_combine);
   m.impl("decode_advance", &decode_advance);
   m.impl("afd_epoch", &afd_epoch);
+  m.impl("gdn_conv", &gdn_conv);
+  m.impl("gdn_recurrent", &gdn_recurrent);
   m.impl("afd_wait", &afd_wait);
   m.impl("afd_dispatch", &afd_dispatch);
   m.impl("afd_combine", &afd_combine);

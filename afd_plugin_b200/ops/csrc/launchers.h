@@ -178,3 +178,37 @@ int grouped_gemm_grid(int n_items);
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,
                          const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
                          int* status, cudaStream_t s, int w_experts = -1, const ScatterParams* sp = nullptr);
+
+// ---- gdn.cu (Gated DeltaNet)
+struct GdnConvParams {
+  const __nv_bfloat16* x;  // [T, >= C], row stride ldx (q | k | v channels first)
+  int64_t ldx;
+  const __nv_bfloat16* weight;  // [C, K]
+  __nv_bfloat16* state;         // [slots, C, K - 1] last K - 1 inputs, oldest first
+  __nv_bfloat16* y;             // [T, C]
+  const int32_t* cu_seqlens;    // [S + 1]
+  const int32_t* slots;         // [S]
+  const int32_t* reset;         // [S] or null
+  int num_seqs, C, K;
+};
+struct GdnRecurrentParams {
+  const __nv_bfloat16* qkv;  // [T, 2 * nk * dk + nv * dv] (q | k | v), row stride ld_qkv
+  int64_t ld_qkv;
+  const __nv_bfloat16* z;    // [T, nv * dv] gate, row stride ld_z
+  int64_t ld_z;
+  const __nv_bfloat16* a;    // [T, nv] (decay input), row stride ld_ab
+  const __nv_bfloat16* b;    // [T, nv] (beta input)
+  int64_t ld_ab;
+  const float* A_log;        // [nv]
+  const float* dt_bias;      // [nv]
+  const __nv_bfloat16* norm_w;  // [dv]
+  float eps;
+  float* state;              // [slots, nv, dk, dv]
+  __nv_bfloat16* out;        // [T, nv * dv]
+  const int32_t* cu_seqlens;
+  const int32_t* slots;
+  const int32_t* reset;
+  int num_seqs, nk, nv, dk, dv;
+};
+void launch_gdn_conv(const GdnConvParams& p, cudaStream_t s);
+bool launch_gdn_recurrent(const GdnRecurrentParams& p, cudaStream_t s);

@@ -119,8 +119,14 @@ def topk_route(
     n_group: int = 1,
     topk_group: int = 1,
     routed_scaling_factor: float = 1.0,
+    forced_ids: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Return ``(weights fp32 [T,k], ids int32 [T,k])``.
+
+    * sqrtsoftplus scoring (DeepSeek-V4): scores sqrt(softplus(logits)),
+      selection like sigmoid scoring.
+    * ``forced_ids`` [T, k] (hash routing): experts given, weights gathered
+      from the scores.
 
     * softmax scoring: probabilities over all experts, optional group limit,
       pick top-k probabilities.
@@ -135,11 +141,18 @@ def topk_route(
     if scoring == "softmax":
         scores = torch.softmax(lf, dim=-1)
         select = scores
-    elif scoring == "sigmoid":
-        scores = torch.sigmoid(lf)
+    elif scoring in ("sigmoid", "sqrtsoftplus"):
+        scores = torch.sigmoid(lf) if scoring == "sigmoid" else torch.sqrt(torch.nn.functional.softplus(lf))
         select = scores + (bias.float() if bias is not None else 0.0)
     else:
         raise ValueError(f"unknown scoring {scoring!r}")
+    if forced_ids is not None:
+        # hash routing: the experts are given (per token id); weights from the scores
+        ids = forced_ids.long()
+        weights = scores.gather(1, ids)
+        if renormalize:
+            weights = weights / weights.sum(dim=-1, keepdim=True)
+        return (weights * routed_scaling_factor).float(), ids.to(torch.int32)
     if n_group > 1 and topk_group < n_group:
         grouped = select.view(T, n_group, E // n_group)
         if scoring == "sigmoid":
@@ -342,6 +355,120 @@ def gqa_prefill(
     s = s.masked_fill(mask[:, None, None, :], float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.einsum("tkgn,nkd->tkgd", p, v).reshape(T, Hq, D).to(q.dtype)
+
+
+# ------------------------------------------------------ gated delta net (linear attention)
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """x / sqrt(sum(x^2) + eps) over the last dim, in fp32."""
+    xf = x.float()
+    return xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + eps)
+
+
+def causal_conv1d(x: torch.Tensor, weight: torch.Tensor, state: torch.Tensor | None = None,
+                  activation: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """Depthwise causal convolution of one sequence.
+
+    ``x`` [T, C], ``weight`` [C, K]; ``state`` [C, K-1] holds the K-1 inputs
+    before x (oldest first), zeros when None.  y[t, c] = sum_j w[c, j] *
+    u[t + j, c] over u = [state; x]; SiLU when ``activation``.  Returns
+    (y [T, C] fp32, new state [C, K-1] fp32).
+    """
+    T, C = x.shape
+    K = weight.shape[1]
+    prev = torch.zeros(C, K - 1, device=x.device) if state is None else state.float()
+    u = torch.cat([prev.t(), x.float()], dim=0)  # [K-1+T, C]
+    w = weight.float()
+    y = torch.zeros(T, C, device=x.device)
+    for j in range(K):
+        y += u[j : j + T] * w[:, j]
+    if activation:
+        y = y * torch.sigmoid(y)
+    return y, u[T:].t().contiguous()
+
+
+def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                     state: torch.Tensor | None = None, scale: float | None = None,
+                     qk_l2norm: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gated delta rule over one sequence, token by token (the recurrent form).
+
+    q, k [T, Hv, dk]; v [T, Hv, dv]; g [T, Hv] log-decay (<= 0); beta [T, Hv];
+    state [Hv, dk, dv].  Per token and head, with S the state:
+        S = exp(g) S;  S = S + k (beta (v - S^T k))^T;  o = S^T q * scale
+    (the gated delta rule of Yang et al., "Gated Delta Networks").  Returns
+    (o [T, Hv, dv] fp32, final state fp32).
+    """
+    T, Hv, dk = q.shape
+    dv = v.shape[-1]
+    qf, kf = (l2norm(q), l2norm(k)) if qk_l2norm else (q.float(), k.float())
+    scale = dk ** -0.5 if scale is None else scale
+    S = torch.zeros(Hv, dk, dv, device=q.device) if state is None else state.float().clone()
+    out = torch.zeros(T, Hv, dv, device=q.device)
+    for t in range(T):
+        S = S * torch.exp(g[t].float())[:, None, None]
+        kv = torch.einsum("hkv,hk->hv", S, kf[t])
+        u = beta[t].float()[:, None] * (v[t].float() - kv)
+        S = S + torch.einsum("hk,hv->hkv", kf[t], u)
+        out[t] = torch.einsum("hkv,hk->hv", S, qf[t]) * scale
+    return out, S
+
+
+def rms_norm_gated(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm over the last dim, times weight, times SiLU(z); fp32 result."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()
+    zf = z.float()
+    return y * (zf * torch.sigmoid(zf))
+
+
+def gdn_gates(a: torch.Tensor, b: torch.Tensor, A_log: torch.Tensor,
+              dt_bias: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gated DeltaNet gates: g = -exp(A_log) * softplus(a + dt_bias), beta = sigmoid(b)."""
+    g = -torch.exp(A_log.float()) * torch.nn.functional.softplus(a.float() + dt_bias.float())
+    return g, torch.sigmoid(b.float())
+
+
+# ------------------------------------------------------ manifold-constrained hyper-connections
+def sinkhorn(logits: torch.Tensor, iters: int, eps: float) -> torch.Tensor:
+    """Sinkhorn-Knopp projection of exp(logits) [..., n, n] towards a doubly
+    stochastic matrix: alternate row and column normalisation ``iters`` times."""
+    m = torch.exp(logits.float() - logits.float().amax(dim=(-2, -1), keepdim=True)) + eps
+    for _ in range(iters):
+        m = m / (m.sum(-1, keepdim=True) + eps)
+        m = m / (m.sum(-2, keepdim=True) + eps)
+    return m
+
+
+def mhc_mix(residual: torch.Tensor, fn: torch.Tensor, base: torch.Tensor, scale: torch.Tensor, *, norm_eps: float,
+            hc_eps: float, post_alpha: float, sinkhorn_iters: int):
+    """Mixing coefficients of one mHC sub-layer from the residual streams.
+
+    residual [T, n, H]; fn [(2 + n) n, n H]; base [(2 + n) n]; scale [3].
+    With x = RMSNorm(flatten(residual)) (no weight) and m = x fn^T:
+      pre  = sigmoid(scale0 m[:n] + base[:n]) + hc_eps          [T, n]
+      post = post_alpha sigmoid(scale1 m[n:2n] + base[n:2n])     [T, n]
+      res  = Sinkhorn(scale2 m[2n:] + base[2n:])                 [T, n, n]
+    (manifold-constrained hyper-connections, Xie et al., DeepSeek-AI 2025).
+    """
+    T, n, H = residual.shape
+    x = residual.float().reshape(T, n * H)
+    x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + norm_eps)
+    m = x @ fn.float().t()
+    b = base.float()
+    sc = scale.float()
+    pre = torch.sigmoid(sc[0] * m[:, :n] + b[:n]) + hc_eps
+    post = post_alpha * torch.sigmoid(sc[1] * m[:, n : 2 * n] + b[n : 2 * n])
+    res = sinkhorn((sc[2] * m[:, 2 * n :] + b[2 * n :]).view(T, n, n), sinkhorn_iters, hc_eps)
+    return pre, post, res
+
+
+def mhc_pre(residual: torch.Tensor, pre: torch.Tensor) -> torch.Tensor:
+    """Sub-layer input: sum_i pre_i * residual_i -> [T, H] fp32."""
+    return torch.einsum("tn,tnh->th", pre.float(), residual.float())
+
+
+def mhc_post(residual: torch.Tensor, out: torch.Tensor, post: torch.Tensor, res: torch.Tensor) -> torch.Tensor:
+    """New streams: residual_i' = sum_j res_ij residual_j + post_i * out -> [T, n, H] fp32."""
+    return torch.einsum("tij,tjh->tih", res.float(), residual.float()) + post.float()[..., None] * out.float()[:, None]
 
 
 __all__ = [name for name in globals() if not name.startswith("_") and callable(globals()[name])]

@@ -43,6 +43,7 @@ class Request:
     max_tokens: int
     output: list[int] = field(default_factory=list)
     blocks: list[int] = field(default_factory=list)
+    state_slot: int = -1  # linear-attention state row (Gated DeltaNet models)
 
     @property
     def num_tokens(self) -> int:
@@ -87,7 +88,10 @@ class LLMEngine:
         self.max_blocks_per_seq = math.ceil(mc.max_model_len / self.block_size)
         if num_blocks is None:
             num_blocks = cc.num_blocks or (self.max_batch * self.max_blocks_per_seq + 1)
-        self.kv = KVCache(model.arch, num_blocks, self.block_size, model.dtype, self.device)
+        # One linear-attention state row per running request plus a padding row.
+        self.kv = KVCache(model.arch, num_blocks, self.block_size, model.dtype, self.device,
+                          max_seqs=self.max_batch + 1)
+        self._free_state_slots = list(range(self.max_batch - 1, -1, -1))
         self.ffn = ffn_executor or LocalFFNExecutor(model)
         num_ub = engine_config.parallel_config.num_ubatches if engine_config.parallel_config.use_ubatching else 1
         self.runner = ModelRunner(model, self.kv, self.ffn, max_batch=self.max_batch,
@@ -108,6 +112,7 @@ class LLMEngine:
         self._h_table = mk(self.max_batch, self.max_blocks_per_seq, dt=torch.int32)
         self._h_lens = mk(self.max_batch, dt=torch.int32)
         self._h_next = mk(self.max_batch, dt=torch.int32)
+        self._h_state = mk(self.max_batch, dt=torch.int32)
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
 
@@ -148,6 +153,7 @@ class LLMEngine:
         for p, t in zip(prompts, first_tokens):
             req = Request(next(self._ids), list(p), max(1, self.config.model_config.max_model_len - len(p)))
             self._ensure_blocks(req, len(p) + max(1, reserve_tokens))
+            req.state_slot = self._free_state_slots.pop()
             req.output.append(int(t))
             self.running.append(req)
             ids.append(req.req_id)
@@ -169,7 +175,9 @@ class LLMEngine:
             self._h_table[i].fill_(PAD_BLOCK)
             self._h_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
             self._h_lens[i] = pos + 1
+            self._h_state[i] = r.state_slot
         n = len(reqs)
+        b.state_slots[:n].copy_(self._h_state[:n])
         b.input_ids[:n].copy_(self._h_ids[:n])
         b.positions[:n].copy_(self._h_pos[:n])
         b.slot_mapping[:n].copy_(self._h_slot[:n])
@@ -188,6 +196,9 @@ class LLMEngine:
     def _finish(self, req: Request) -> None:
         self.kv.allocator.free(req.blocks)
         req.blocks = []
+        if req.state_slot >= 0:
+            self._free_state_slots.append(req.state_slot)
+            req.state_slot = -1
         self.finished[req.req_id] = req
 
     # ---------------------------------------------------------------- step
@@ -205,14 +216,16 @@ class LLMEngine:
     def _prefill_step(self, admit: list[Request], votes) -> dict[int, int]:
         if not admit:
             # Another Attention rank prefills: take part with one placeholder row.
-            admit_tokens, tables, starts = [[0]], [[PAD_BLOCK]], [0]
+            admit_tokens, tables, starts, slots = [[0]], [[PAD_BLOCK]], [0], None
         else:
             for r in admit:
                 self._ensure_blocks(r, len(r.prompt) + 1)
+                r.state_slot = self._free_state_slots.pop()
             admit_tokens = [r.prompt for r in admit]
             tables = [r.blocks for r in admit]
             starts = [0] * len(admit)
-        toks = self.runner.prefill(admit_tokens, tables, starts,
+            slots = [r.state_slot for r in admit]
+        toks = self.runner.prefill(admit_tokens, tables, starts, slots,
                                    **self._across(votes, sum(len(t) for t in admit_tokens)))
         toks = toks.cpu().tolist()
         out = {}
@@ -248,12 +261,16 @@ class LLMEngine:
             self._h_slot[i] = r.blocks[pos // bs] * bs + pos % bs
             self._h_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
             self._h_lens[i] = pos + 1
+            self._h_state[i] = r.state_slot
         if run_b > B:
             self._h_ids[B:run_b] = 0
             self._h_pos[B:run_b] = 0
             self._h_slot[B:run_b] = PAD_BLOCK * bs
             self._h_lens[B:run_b] = 1
+            self._h_state[B:run_b] = self.runner.pad_state_slot
         b = self.runner.buf
+        if self.runner.has_linear_state:
+            b.state_slots[:run_b].copy_(self._h_state[:run_b], non_blocking=True)
         b.input_ids[:run_b].copy_(self._h_ids[:run_b], non_blocking=True)
         b.positions[:run_b].copy_(self._h_pos[:run_b], non_blocking=True)
         b.slot_mapping[:run_b].copy_(self._h_slot[:run_b], non_blocking=True)

@@ -164,7 +164,9 @@ class FFNModelRunner:
             mine = padded[self.ep_rank * n_max : (self.ep_rank + 1) * n_max]
         out = mine[: h.shape[0]].to(h.dtype)
         if moe.shared_experts is not None:
-            out = out + moe.shared_experts(h)
+            shared = moe.shared_experts(h)
+            sg = moe.shared_gate(h)
+            out = out + (shared if sg is None else (shared.float() * sg).to(shared.dtype))
         return out
 
     # ------------------------------------------------------------ serving

@@ -1,4 +1,4 @@
-"""Paged KV cache: device pool plus a host-side block allocator.
+"""Paged KV cache (plus linear-attention state): device pool and a host-side block allocator.
 
 MLA layers cache one ``kv_lora + rope`` latent row per token
 (``[L, blocks, block_size, 576]`` for DeepSeek); GQA layers cache K and V
@@ -41,6 +41,14 @@ PAD_BLOCK = 0
 
 
 class KVCache:
+    """Per-layer decode state.
+
+    Full-attention layers get paged KV; Gated DeltaNet (linear attention)
+    layers get per-sequence recurrent state instead: a conv state
+    ``[max_seqs, conv_dim, K - 1]`` and an fp32 delta-rule state
+    ``[max_seqs, nv, dk, dv]``, addressed by the sequence's state slot.
+    """
+
     def __init__(
         self,
         arch: ModelArchConfig,
@@ -48,11 +56,16 @@ class KVCache:
         block_size: int,
         dtype: torch.dtype,
         device: torch.device | str,
+        *,
+        max_seqs: int = 1,
     ):
         self.arch = arch
         self.num_blocks = num_blocks
         self.block_size = block_size
-        L = arch.num_hidden_layers
+        self.max_seqs = max_seqs
+        attn_layers = arch.full_attention_layers
+        self._kv_index = {layer: i for i, layer in enumerate(attn_layers)}
+        L = len(attn_layers)
         if arch.is_mla:
             self.kv = torch.zeros(L, num_blocks, block_size, arch.kv_lora_rank + arch.qk_rope_head_dim,
                                   dtype=dtype, device=device)
@@ -62,25 +75,51 @@ class KVCache:
             self.k = torch.zeros(shape, dtype=dtype, device=device)
             self.v = torch.zeros(shape, dtype=dtype, device=device)
             self.kv = None
+        lin = arch.linear_attention_layers
+        self._state_index = {layer: i for i, layer in enumerate(lin)}
+        self.conv_state = self.ssm_state = None
+        if lin:
+            self.conv_state = torch.zeros(len(lin), max_seqs, arch.linear_conv_dim, arch.linear_conv_kernel_dim - 1,
+                                          dtype=dtype, device=device)
+            self.ssm_state = torch.zeros(len(lin), max_seqs, arch.linear_num_value_heads, arch.linear_key_head_dim,
+                                         arch.linear_value_head_dim, dtype=torch.float32, device=device)
         self.allocator = BlockAllocator(num_blocks)
 
     def layer(self, i: int):
+        if i in self._state_index:
+            j = self._state_index[i]
+            return (self.conv_state[j], self.ssm_state[j])
+        j = self._kv_index[i]
         if self.kv is not None:
-            return self.kv[i]
-        return (self.k[i], self.v[i])
+            return self.kv[j]
+        return (self.k[j], self.v[j])
 
     @staticmethod
     def bytes_per_block(arch: ModelArchConfig, block_size: int, dtype: torch.dtype) -> int:
         elem = torch.empty((), dtype=dtype).element_size()
-        return arch.num_hidden_layers * block_size * arch.kv_cache_width * elem
+        return len(arch.full_attention_layers) * block_size * arch.kv_cache_width * elem
+
+    @staticmethod
+    def state_bytes_per_seq(arch: ModelArchConfig, dtype: torch.dtype) -> int:
+        """Recurrent-state bytes one sequence holds over all linear-attention layers."""
+        lin = len(arch.linear_attention_layers)
+        if not lin:
+            return 0
+        elem = torch.empty((), dtype=dtype).element_size()
+        conv = arch.linear_conv_dim * (arch.linear_conv_kernel_dim - 1) * elem
+        ssm = arch.linear_num_value_heads * arch.linear_key_head_dim * arch.linear_value_head_dim * 4
+        return lin * (conv + ssm)
 
     def fill_random_(self, seed: int = 0, std: float = 1.0) -> None:
         """Synthetic cache contents for decode-only benchmarks (prefill skipped)."""
-        g = torch.Generator(device=self.kv.device if self.kv is not None else self.k.device)
+        dev = next(t for t in (self.kv, self.k, self.conv_state) if t is not None).device
+        g = torch.Generator(device=dev)
         g.manual_seed(seed)
-        for t in (self.kv, self.k, self.v):
+        for t in (self.kv, self.k, self.v, self.conv_state):
             if t is not None:
                 t.normal_(0.0, std, generator=g)
+        if self.ssm_state is not None:
+            self.ssm_state.normal_(0.0, 0.02, generator=g)
 
 
 __all__ = ["BlockAllocator", "KVCache", "PAD_BLOCK"]

@@ -36,6 +36,8 @@ class DecodeBuffers:
     block_table: torch.Tensor
     seq_lens: torch.Tensor
     next_tokens: torch.Tensor
+    state_slots: torch.Tensor  # linear-attention state row of each batch row
+    rows: torch.Tensor         # 0..max_batch (one-token sequence bounds)
 
     @classmethod
     def allocate(cls, max_batch: int, max_blocks: int, device) -> "DecodeBuffers":
@@ -47,6 +49,8 @@ class DecodeBuffers:
             block_table=z(max_batch, max_blocks, dt=torch.int32),
             seq_lens=torch.ones(max_batch, dtype=torch.int32, device=device),
             next_tokens=z(max_batch, dt=torch.int32),
+            state_slots=z(max_batch, dt=torch.int32),
+            rows=torch.arange(max_batch + 1, dtype=torch.int32, device=device),
         )
 
 
@@ -86,6 +90,10 @@ class ModelRunner:
         self.buf = DecodeBuffers.allocate(max_batch, max_blocks_per_seq, self.device)
         self.graphs: dict[int, _Graph] = {}
         self.graph_pool = None
+        # Gated DeltaNet layers keep per-sequence state; the last state row pads.
+        self.has_linear_state = bool(model.arch.linear_attention_layers)
+        self.pad_state_slot = kv_cache.max_seqs - 1
+        self.buf.state_slots.fill_(self.pad_state_slot)
 
     # ------------------------------------------------------------ forward
     def _layers(self, h: torch.Tensor, meta: AttentionMetadata, stage: int):
@@ -135,6 +143,8 @@ class ModelRunner:
                 block_table=b.block_table[lo:hi],
                 seq_lens=b.seq_lens[lo:hi],
                 is_decode=True,
+                state_slots=b.state_slots[lo:hi] if self.has_linear_state else None,
+                cu_seqlens=b.rows[: hi - lo + 1] if self.has_linear_state else None,
             ))
         return metas
 
@@ -202,6 +212,7 @@ class ModelRunner:
         b.slot_mapping[lo:hi] = PAD_BLOCK * self.kv.block_size
         b.block_table[lo:hi] = PAD_BLOCK
         b.seq_lens[lo:hi] = 1
+        b.state_slots[lo:hi] = self.pad_state_slot
 
     def release_graphs(self) -> None:
         self.graphs.clear()
@@ -209,8 +220,13 @@ class ModelRunner:
 
     # ------------------------------------------------------------ prefill
     def prefill(self, token_lists: list[list[int]], block_tables: list[list[int]], start_positions: list[int],
-                **flags) -> torch.Tensor:
-        """Run prompt tokens (eager, one stage); returns the next token of each sequence."""
+                state_slots: list[int] | None = None, **flags) -> torch.Tensor:
+        """Run prompt tokens (eager, one stage); returns the next token of each sequence.
+
+        ``state_slots`` gives each sequence's linear-attention state row (the
+        padding row when None); a sequence starting at position 0 starts from a
+        zero state.
+        """
         bs = self.kv.block_size
         ids, pos, slots, seqs = [], [], [], []
         t = 0
@@ -234,6 +250,14 @@ class ModelRunner:
             is_decode=False,
             prefill_seqs=seqs,
         )
+        if self.has_linear_state:
+            slots_l = state_slots if state_slots is not None else [self.pad_state_slot] * len(token_lists)
+            cu = [0]
+            for toks in token_lists:
+                cu.append(cu[-1] + len(toks))
+            meta.state_slots = torch.tensor(slots_l, dtype=torch.int32, device=dev)
+            meta.cu_seqlens = torch.tensor(cu, dtype=torch.int32, device=dev)
+            meta.state_reset = torch.tensor([int(p0 == 0) for p0 in start_positions], dtype=torch.int32, device=dev)
         input_ids = torch.tensor(ids, dtype=torch.int32, device=dev)
         logits = self.forward(input_ids, [meta], (0, t), **flags)
         last = torch.tensor([e - 1 for _, e, _ in seqs], device=dev)

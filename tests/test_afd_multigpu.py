@@ -27,15 +27,15 @@ def _prompts(n, length, vocab=1024, seed=0):
     return torch.randint(0, vocab, (n, length), generator=g).tolist()
 
 
-def _colocated(prompts, max_tokens):
-    arch = get_preset(PRESET)
+def _colocated(prompts, max_tokens, preset=PRESET):
+    arch = get_preset(preset)
     ec = EngineConfig(ModelConfig(arch, dtype=torch.bfloat16, enforce_eager=True, max_model_len=128), max_num_seqs=8)
     m = build_model(arch, role="colocated", dtype=torch.bfloat16, device="cuda", seed=0, max_positions=128)
     return LLMEngine(ec, m).generate(prompts, max_tokens)
 
 
-def _run(afd, prompts, max_tokens, **kw):
-    spec = LocalAFDSpec(preset=PRESET, afd=afd, prompts=prompts, max_tokens=max_tokens, dtype="bfloat16",
+def _run(afd, prompts, max_tokens, preset=PRESET, **kw):
+    spec = LocalAFDSpec(preset=preset, afd=afd, prompts=prompts, max_tokens=max_tokens, dtype="bfloat16",
                         backend="nccl", **kw)
     res = launch_local(spec, join_timeout_s=240)
     errs = {r: v for r, v in res.items() if "error" in v}
@@ -68,5 +68,17 @@ def test_fused_connector_1a1f(eager, dbo):
     afd = {"num_attention_ranks": 1, "num_ffn_ranks": 1, "connector": "B200FusedAFDConnector",
            "connector_extra_config": {"max_tokens_per_rank": 128, "wait_timeout_ms": 20000}}
     outs = _run(afd, prompts, 6, enforce_eager=eager, use_ubatching=dbo, capture_sizes=[4])
+    assert [o[0] for o in outs] == [o[0] for o in ref]
+    assert _agreement(outs, ref) >= 0.75
+
+
+def test_fused_connector_qwen3_5_1a1f():
+    """Hybrid Gated DeltaNet model through the fused connector (gated shared expert on the FFN side)."""
+    _need(2)
+    prompts = _prompts(4, 16)
+    ref = _colocated(prompts, 6, preset="tiny-qwen3.5")
+    afd = {"num_attention_ranks": 1, "num_ffn_ranks": 1, "connector": "B200FusedAFDConnector",
+           "connector_extra_config": {"max_tokens_per_rank": 128, "wait_timeout_ms": 20000}}
+    outs = _run(afd, prompts, 6, preset="tiny-qwen3.5", enforce_eager=False, capture_sizes=[4])
     assert [o[0] for o in outs] == [o[0] for o in ref]
     assert _agreement(outs, ref) >= 0.75

@@ -65,3 +65,11 @@ def test_dbo_two_ubatches_matches():
     outs, _ = _run("tiny-dsv2", {"num_attention_ranks": 1, "num_ffn_ranks": 1}, prompts, max_tokens=6,
                    use_ubatching=True)
     assert outs == ref
+
+
+def test_qwen3_5_hybrid_2a1f():
+    """Gated DeltaNet + gated attention on the Attention side, gated shared expert on the FFN side."""
+    prompts = _prompts(n=4, length=12)
+    ref = _colocated("tiny-qwen3.5", prompts, 6)
+    outs, _ = _run("tiny-qwen3.5", {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=6)
+    assert outs == ref

@@ -24,7 +24,7 @@ def _prompts(n, length, vocab, seed=0):
     return torch.randint(0, vocab, (n, length), generator=g).tolist()
 
 
-@pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-dsv2-mla512", "tiny-qwen3-moe"])
+@pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-dsv2-mla512", "tiny-qwen3-moe", "tiny-qwen3.5"])
 def test_graph_decode_matches_eager(preset):
     prompts = _prompts(6, 20, 1024)
     eager = _engine(preset, eager=True).generate(prompts, 8)
@@ -80,3 +80,34 @@ def test_dbo_graph_matches_single_ubatch():
     eng = LLMEngine(ec, m)
     eng.capture_graphs()
     assert eng.generate(prompts, 6) == base
+
+
+def test_qwen3_5_logits_track_fp32_reference():
+    """Gated DeltaNet + gated attention + gated shared expert: bf16 kernels vs the fp32 CPU model."""
+    from afd_plugin_b200.runtime.engine import Request
+
+    arch = get_preset("tiny-qwen3.5")
+    prompts = _prompts(3, 16, arch.vocab_size, seed=5)
+    res = {}
+    first_cpu = None
+    for dev, dt in (("cpu", torch.float32), ("cuda", torch.bfloat16)):
+        e = _engine("tiny-qwen3.5", eager=True, device=dev, dtype=dt, init_on="cpu")
+        reqs = [Request(i, p, 1) for i, p in enumerate(prompts)]
+        for r in reqs:
+            e._ensure_blocks(r, len(r.prompt) + 2)
+        first = e.runner.prefill([r.prompt for r in reqs], [r.blocks for r in reqs], [0] * 3, [0, 1, 2])
+        if first_cpu is None:
+            first_cpu = first.cpu()
+        first = first_cpu
+        b = e.runner.buf
+        for i, r in enumerate(reqs):
+            pos = len(r.prompt)
+            b.input_ids[i] = int(first[i])
+            b.positions[i] = pos
+            b.slot_mapping[i] = r.blocks[pos // e.block_size] * e.block_size + pos % e.block_size
+            b.block_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
+            b.seq_lens[i] = pos + 1
+            b.state_slots[i] = i
+        logits = e.runner.forward(b.input_ids[:3], e.runner._decode_metas(3, (0, 3)), (0, 3))
+        res[dev] = logits.float().cpu()
+    torch.testing.assert_close(res["cuda"], res["cpu"], atol=0.05, rtol=0.05)
