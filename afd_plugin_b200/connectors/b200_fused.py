@@ -294,7 +294,9 @@ class B200FusedAFDConnector(AFDConnectorBase):
 
 def _routing_cfg(arch) -> tuple[int, int, int, int, int]:
     grouped = arch.topk_method in ("group_limited_greedy", "noaux_tc")
-    scoring = 0 if arch.scoring_func == "softmax" else 1
+    from afd_plugin_b200.ops import SCORING_IDS
+
+    scoring = SCORING_IDS[arch.scoring_func]
     return (scoring, int(arch.norm_topk_prob), arch.n_group if grouped else 1, arch.topk_group if grouped else 1,
             arch.num_experts_per_tok)
 
@@ -352,10 +354,24 @@ class FusedAttentionExecutor(FFNExecutor):
                int(has_shared), d.num_ffn, d.e_local, d.t_cap, c.role_rank, c.role_rank // d.ratio, layer_idx]
         gate_w = gate.weight if is_moe else layer.post_attention_layernorm.weight
         bias = gate.e_score_correction_bias if is_moe else None
+        hash_table = ids = None
+        if is_moe and gate.tid2eid is not None:
+            hash_table = gate.tid2eid
+        if self.model.fused_post_norm:
+            x, res, norm_w, eps = attn_out.contiguous(), residual, layer.post_attention_layernorm.weight, \
+                layer.post_attention_layernorm.eps
+        else:
+            # The model's own residual scheme (mHC) produces the FFN input; the
+            # kernel only routes and sends it.
+            x, residual = self.model.post_attention_norm(layer_idx, attn_out, residual)
+            x = x.contiguous()
+            res, norm_w, eps = x, x, 0.0
+            cfg.append(1)
+        if hash_table is not None:
+            ids = self.model.ffn_extra(layer_idx, residual)["input_ids"].to(torch.int32).contiguous()
         torch.ops.afd_b200.afd_dispatch(
-            attn_out.contiguous(), residual, layer.post_attention_layernorm.weight, layer.post_attention_layernorm.eps,
-            gate_w, bias, float(a.routed_scaling_factor), c.dispatch_ptrs[stage_idx], c.fmask[stage_idx],
-            c.dctr[stage_idx], cfg)
+            x, res, norm_w, eps, gate_w, bias, float(a.routed_scaling_factor), c.dispatch_ptrs[stage_idx],
+            c.fmask[stage_idx], c.dctr[stage_idx], cfg, hash_table, ids)
         return (T, residual)
 
     def recv(self, layer_idx, handle, stage_idx):

@@ -16,6 +16,7 @@ from afd_plugin_b200.models.model import (
     AFDDeepseekForCausalLM,
     AFDDeepseekV2ForCausalLM,
     AFDDeepseekV3ForCausalLM,
+    AFDDeepseekV4ForCausalLM,
     AFDGlmMoeDsaForCausalLM,
     AFDQwen3MoeForCausalLM,
     AFDQwen3NextForCausalLM,
@@ -28,6 +29,7 @@ MODEL_REGISTRY: dict[str, type[AFDCausalLM]] = {
     "DeepseekV2ForCausalLM": AFDDeepseekV2ForCausalLM,
     "DeepseekV3ForCausalLM": AFDDeepseekV3ForCausalLM,
     "DeepseekV32ForCausalLM": AFDDeepseekV3ForCausalLM,
+    "DeepseekV4ForCausalLM": AFDDeepseekV4ForCausalLM,
     "GlmMoeDsaForCausalLM": AFDGlmMoeDsaForCausalLM,
     "Qwen3MoeForCausalLM": AFDQwen3MoeForCausalLM,
     "Qwen3NextForCausalLM": AFDQwen3NextForCausalLM,

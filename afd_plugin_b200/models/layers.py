@@ -44,6 +44,8 @@ class AttentionMetadata:
     state_slots: torch.Tensor | None = None
     cu_seqlens: torch.Tensor | None = None
     state_reset: torch.Tensor | None = None
+    # Token ids of the step's rows (hash-routed MoE layers need them).
+    input_ids: torch.Tensor | None = None
 
     def linear_state_args(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
         if self.state_slots is not None:
@@ -382,24 +384,45 @@ class DenseMLP(nn.Module):
 
 
 class MoEGate(nn.Module):
-    def __init__(self, arch: ModelArchConfig, dtype, device):
+    """Router.  ``hash_routing`` (DeepSeek-V4 hash layers): the experts come from
+    a token-id table ``tid2eid [vocab, k]``; the scores only weight them."""
+
+    def __init__(self, arch: ModelArchConfig, dtype, device, *, hash_routing: bool = False):
         super().__init__()
         self.arch = arch
         self.weight = _param((arch.n_routed_experts, arch.hidden_size), dtype, device)
-        if arch.topk_method == "noaux_tc":
+        self.tid2eid = None
+        if hash_routing:
+            self.tid2eid = torch.zeros(arch.vocab_size, arch.num_experts_per_tok, dtype=torch.int32, device=device)
+            self.e_score_correction_bias = None
+        elif arch.topk_method == "noaux_tc":
             self.e_score_correction_bias = _param((arch.n_routed_experts,), torch.float32, device)
         else:
             self.e_score_correction_bias = None
 
-    def logits(self, h: torch.Tensor) -> torch.Tensor:
-        return (h.float() @ self.weight.float().t()) if not h.is_cuda else torch.mm(h, self.weight.t()).float()
+    def finalize(self) -> None:
+        """fp32 copy of the gate: router logits are computed in fp32 on every path
+        (the fused dispatch kernel accumulates them in fp32 too), so routing
+        decisions agree between colocated and disaggregated runs."""
+        self.weight_f32 = self.weight.detach().float()
 
-    def route(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        w = getattr(self, "weight_f32", None)
+        if w is None or w.device != h.device:
+            w = self.weight.float()
+        return h.float() @ w.t()
+
+    def route(self, logits: torch.Tensor, input_ids: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         a = self.arch
         from afd_plugin_b200.models.routing_simulator import balanced_routing_enabled, balanced_topk
 
         if balanced_routing_enabled():
             return balanced_topk(logits.shape[0], a.n_routed_experts, a.num_experts_per_tok, device=logits.device)
+        forced = None
+        if self.tid2eid is not None:
+            if input_ids is None:
+                raise RuntimeError("hash-routed MoE layer needs the tokens' input_ids")
+            forced = self.tid2eid[input_ids.long()]
         return ops.topk_route(
             logits,
             a.num_experts_per_tok,
@@ -409,6 +432,7 @@ class MoEGate(nn.Module):
             n_group=a.n_group if a.topk_method in ("group_limited_greedy", "noaux_tc") else 1,
             topk_group=a.topk_group if a.topk_method in ("group_limited_greedy", "noaux_tc") else 1,
             routed_scaling_factor=a.routed_scaling_factor,
+            forced_ids=forced,
         )
 
 
@@ -467,14 +491,16 @@ class RoutedExperts(nn.Module):
 class MoEBlock(nn.Module):
     """Gate + routed experts (+ shared experts).  ``ep_rank/ep_size`` shard the experts."""
 
-    def __init__(self, arch: ModelArchConfig, dtype, device, *, ep_rank: int = 0, ep_size: int = 1, with_gate: bool = True):
+    def __init__(self, arch: ModelArchConfig, dtype, device, *, ep_rank: int = 0, ep_size: int = 1, with_gate: bool = True,
+                 layer_idx: int = -1):
         super().__init__()
         self.arch = arch
         E = arch.n_routed_experts
         if E % ep_size:
             raise ValueError(f"{E} experts do not split over {ep_size} expert-parallel ranks")
         n_local = E // ep_size
-        self.gate = MoEGate(arch, dtype, device) if with_gate else None
+        self.hash_routing = 0 <= layer_idx < arch.num_hash_layers
+        self.gate = MoEGate(arch, dtype, device, hash_routing=self.hash_routing) if with_gate else None
         I, Is = arch.moe_intermediate_size, arch.shared_intermediate_size
         chunked = (Is > 0 and arch.quant is None and I % 64 == 0 and Is % I == 0)
         self.n_shared_chunks = Is // I if chunked else 0
@@ -488,15 +514,18 @@ class MoEBlock(nn.Module):
     def finalize(self) -> None:
         if self.shared_experts is not None:
             self.experts.pack_shared(self.shared_experts)
+        if self.gate is not None:
+            self.gate.finalize()
 
-    def forward(self, h: torch.Tensor, router_logits: torch.Tensor | None = None) -> torch.Tensor:
+    def forward(self, h: torch.Tensor, router_logits: torch.Tensor | None = None,
+                input_ids: torch.Tensor | None = None) -> torch.Tensor:
         if router_logits is None:
             if self.gate is None:
                 raise RuntimeError("MoE block without a gate needs router_logits")
             router_logits = self.gate.logits(h)
         if self.gate is None:
             raise RuntimeError("MoE block needs gate parameters (bias / routing config) to route")
-        w, ids = self.gate.route(router_logits)
+        w, ids = self.gate.route(router_logits, input_ids)
         return self.forward_experts(h, w, ids)
 
     def forward_experts(self, h: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,

@@ -59,6 +59,8 @@ class ParamSpec:
     init: str = "normal"  # "normal" | "ones" | "zeros"
     # fp8-quantised target: random init quantises, checkpoints may carry a scale.
     fp8_scale_name: str | None = None
+    # init == "custom": the random-init value comes from make()
+    make: Callable[[], torch.Tensor] | None = None
 
 
 def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention: bool,
@@ -69,6 +71,8 @@ def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention:
     (``deepseek_v2.py:69-92``, ``qwen3_moe.py:51-62``).
     """
     parts = name.split(".")
+    if arch.hc_mult:
+        return _v4_weight_roles(name, parts, route_on_attention=route_on_attention)
     for i, p in enumerate(parts[:-2]):
         if p != "layers":
             continue
@@ -87,6 +91,28 @@ def weight_roles(name: str, arch: ModelArchConfig, *, compute_gate_on_attention:
         if rest and rest[0] == "gate" and (compute_gate_on_attention or route_on_attention):
             return _BOTH
         return _FFN
+    return _BOTH
+
+
+def _v4_weight_roles(name: str, parts: list[str], *, route_on_attention: bool) -> frozenset[str]:
+    """DeepSeek-V4 naming (reference ``deepseek_v4.py:45-60``): the ``ffn`` stage of a
+    layer is FFN-owned, every other layer stage and the ``hc_head`` tensors are
+    Attention-owned, other top-level tensors are needed by both."""
+    if parts[-1].startswith("hc_head"):
+        return _ATTN
+    for i, p in enumerate(parts[:-2]):
+        if p != "layers":
+            continue
+        try:
+            int(parts[i + 1])
+        except ValueError:
+            continue
+        stage = parts[i + 2]
+        if stage == "ffn":
+            if route_on_attention and len(parts) > i + 3 and parts[i + 3] == "gate":
+                return _BOTH
+            return _FFN
+        return _ATTN
     return _BOTH
 
 
@@ -114,18 +140,18 @@ class DecoderLayer(nn.Module):
         self.mlp: nn.Module | None = None
         self.gate_only = None
         if role == "colocated":
-            self.mlp = MoEBlock(arch, dtype, device) if self.is_moe else DenseMLP(
+            self.mlp = MoEBlock(arch, dtype, device, layer_idx=idx) if self.is_moe else DenseMLP(
                 arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
         elif role == "attention":
             if self.is_moe and (gate_on_attn or route_on_attn):
                 from afd_plugin_b200.models.layers import MoEGate
 
-                self.gate_only = MoEGate(arch, dtype, device)
+                self.gate_only = MoEGate(arch, dtype, device, hash_routing=idx < arch.num_hash_layers)
             elif gate_on_attn:
                 self.mlp = DenseMLP(arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
         else:  # ffn
             if self.is_moe:
-                self.mlp = MoEBlock(arch, dtype, device, ep_rank=ep_rank, ep_size=ep_size)
+                self.mlp = MoEBlock(arch, dtype, device, ep_rank=ep_rank, ep_size=ep_size, layer_idx=idx)
             elif not gate_on_attn:
                 self.mlp = DenseMLP(arch.hidden_size, arch.intermediate_size, dtype, device, arch.quant)
 
@@ -211,7 +237,20 @@ class AFDCausalLM(nn.Module):
             raise RuntimeError(f"layer {layer_idx} FFN is not owned by role {self.role!r}")
         if self.role == "ffn" and self.compute_gate_on_attention and layer.is_moe:
             raise RuntimeError("Attention-side gate: the FFN role must call compute_experts_output")
+        if layer.is_moe and kwargs.get("input_ids") is not None:
+            return layer.mlp(hidden_states, input_ids=kwargs["input_ids"])
         return layer.mlp(hidden_states)
+
+    def ffn_extra(self, layer_idx: int, residual) -> dict:
+        """Extra tensors the FFN of ``layer_idx`` needs besides the hidden states."""
+        return {}
+
+    def ffn_needs_input_ids(self, layer_idx: int) -> bool:
+        return False
+
+    # Whether the post-attention step is residual add + RMSNorm (the fused
+    # dispatch kernel runs it); models with other residual schemes return False.
+    fused_post_norm = True
 
     def compute_experts_output(self, hidden_states: torch.Tensor, layer_idx: int,
                                router_logits: torch.Tensor) -> torch.Tensor:
@@ -278,6 +317,8 @@ class AFDCausalLM(nn.Module):
         for layer in self.layers:
             if isinstance(layer.mlp, MoEBlock):
                 layer.mlp.finalize()
+            if layer.gate_only is not None:
+                layer.gate_only.finalize()
 
     def init_random(self, seed: int = 0, std: float = 0.02, *, generate_on: str | None = None) -> None:
         """Seeded N(0, std) init; each tensor's stream depends only on (seed, name).
@@ -291,7 +332,9 @@ class AFDCausalLM(nn.Module):
                 self.device if self.device.type == "cuda" else torch.device("cpu"))
             g = torch.Generator(device=gen_dev)
             g.manual_seed((seed * 1_000_003 + zlib.crc32(spec.name.encode())) & 0x7FFFFFFFFFFFFFFF)
-            if spec.init == "ones":
+            if spec.init == "custom" and spec.make is not None:
+                t = spec.make()
+            elif spec.init == "ones":
                 t = torch.ones(spec.shape, dtype=torch.float32, device=gen_dev)
             elif spec.init == "zeros":
                 t = torch.zeros(spec.shape, dtype=torch.float32, device=gen_dev)
@@ -421,6 +464,145 @@ class AFDQwen3MoeForCausalLM(AFDCausalLM):
         yield ParamSpec(p + "o_proj.weight", tuple(attn.o_proj.shape), _copy(attn.o_proj))
 
 
+class AFDDeepseekV4ForCausalLM(AFDDeepseekV2ForCausalLM):
+    """DeepSeek-V4 family: MLA attention, manifold-constrained hyper-connections
+    (mHC: ``hc_mult`` residual streams mixed per sub-layer), hash-routed MoE in
+    the first ``num_hash_layers`` layers, sqrt-softplus routing scores.
+
+    The AFD split sits around each layer's FFN, as in the reference wrapper
+    (``afd_plugin/model_executor/models/deepseek_v4.py:122-283``): the
+    Attention side keeps every mHC stream and mixing parameter and sends the
+    normalised FFN input plus the token ids (hash routing); the FFN side runs
+    the MoE.  The residual travelling between hooks is the tuple
+    ``(streams [T, n, H] fp32, post [T, n], res [T, n, n], input_ids)``.
+    """
+
+    family = "deepseek_v4"
+    fused_post_norm = False
+    post_alpha = 2.0
+
+    def __init__(self, arch: ModelArchConfig, **kw):
+        super().__init__(arch, **kw)
+        n, H = arch.hc_mult, arch.hidden_size
+        mix = (2 + n) * n
+        dev = self.device
+        if self.role in ("colocated", "attention"):
+            for layer in self.layers:
+                layer.hc_attn_fn = _param((mix, n * H), torch.float32, dev)
+                layer.hc_attn_base = _param((mix,), torch.float32, dev)
+                layer.hc_attn_scale = _param((3,), torch.float32, dev)
+                layer.hc_ffn_fn = _param((mix, n * H), torch.float32, dev)
+                layer.hc_ffn_base = _param((mix,), torch.float32, dev)
+                layer.hc_ffn_scale = _param((3,), torch.float32, dev)
+            self.hc_head_fn = _param((n, n * H), torch.float32, dev)
+            self.hc_head_base = _param((n,), torch.float32, dev)
+            self.hc_head_scale = _param((1,), torch.float32, dev)
+
+    def _validate_arch(self, arch: ModelArchConfig) -> None:
+        if not arch.is_mla or arch.hc_mult < 1:
+            raise ValueError("DeepSeek-V4 wrapper requires MLA attention and hc_mult >= 1")
+
+    # ------------------------------------------------------------- mHC
+    def _mix(self, fn, base, scale, streams):
+        a = self.arch
+        return ref.mhc_mix(streams, fn, base, scale, norm_eps=a.rms_norm_eps, hc_eps=a.hc_eps,
+                           post_alpha=self.post_alpha, sinkhorn_iters=a.hc_sinkhorn_iters)
+
+    def run_attention(self, layer_idx, h, residual, meta, kv_cache):
+        layer = self.layers[layer_idx]
+        if residual is None:  # embeddings: every stream starts as the token embedding
+            ids = meta.input_ids
+            streams = h.float()[:, None, :].expand(h.shape[0], self.arch.hc_mult, h.shape[1]).contiguous()
+        else:
+            streams, post, res, ids = residual
+            streams = ref.mhc_post(streams, h, post, res)
+        pre, post, res = self._mix(layer.hc_attn_fn, layer.hc_attn_base, layer.hc_attn_scale, streams)
+        x = layer.input_layernorm(ref.mhc_pre(streams, pre).to(self.dtype))
+        return layer.self_attn(x, meta, kv_cache, self.cos_sin), (streams, post, res, ids)
+
+    def post_attention_norm(self, layer_idx, attn_out, residual):
+        layer = self.layers[layer_idx]
+        streams, post, res, ids = residual
+        streams = ref.mhc_post(streams, attn_out, post, res)
+        pre, post, res = self._mix(layer.hc_ffn_fn, layer.hc_ffn_base, layer.hc_ffn_scale, streams)
+        x = layer.post_attention_layernorm(ref.mhc_pre(streams, pre).to(self.dtype))
+        return x, (streams, post, res, ids)
+
+    def final_logits(self, h, residual):
+        a = self.arch
+        streams, post, res, _ = residual
+        streams = ref.mhc_post(streams, h, post, res)
+        T = streams.shape[0]
+        xf = streams.reshape(T, -1)
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + a.rms_norm_eps)
+        w = torch.sigmoid(self.hc_head_scale[0] * (xf @ self.hc_head_fn.t()) + self.hc_head_base) + a.hc_eps
+        x = self.norm(torch.einsum("tn,tnh->th", w, streams).to(self.dtype))
+        return ops.linear(x, self.lm_head)
+
+    def ffn_extra(self, layer_idx, residual) -> dict:
+        if self.ffn_needs_input_ids(layer_idx):
+            return {"input_ids": residual[3]}
+        return {}
+
+    def ffn_needs_input_ids(self, layer_idx: int) -> bool:
+        return self.arch.is_moe_layer(layer_idx) and layer_idx < self.arch.num_hash_layers
+
+    # ----------------------------------------------------------- weights
+    def param_specs(self) -> Iterator[ParamSpec]:
+        a = self.arch
+        H = a.hidden_size
+        if self.embed_tokens is not None:
+            yield ParamSpec("model.embed_tokens.weight", tuple(self.embed_tokens.shape), _copy(self.embed_tokens))
+            yield ParamSpec("model.norm.weight", (H,), _copy(self.norm.weight), "ones")
+            yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
+            yield ParamSpec("model.hc_head_fn", tuple(self.hc_head_fn.shape), _copy(self.hc_head_fn))
+            yield ParamSpec("model.hc_head_base", tuple(self.hc_head_base.shape), _copy(self.hc_head_base), "zeros")
+            yield ParamSpec("model.hc_head_scale", (1,), _copy(self.hc_head_scale), "ones")
+        for i, layer in enumerate(self.layers):
+            p = f"model.layers.{i}."
+            if layer.input_layernorm is not None:
+                yield ParamSpec(p + "attn_norm.weight", (H,), _copy(layer.input_layernorm.weight), "ones")
+                yield ParamSpec(p + "ffn_norm.weight", (H,), _copy(layer.post_attention_layernorm.weight), "ones")
+                for which in ("attn", "ffn"):
+                    fn, base, sc = (getattr(layer, f"hc_{which}_{x}") for x in ("fn", "base", "scale"))
+                    yield ParamSpec(p + f"hc_{which}_fn", tuple(fn.shape), _copy(fn))
+                    yield ParamSpec(p + f"hc_{which}_base", tuple(base.shape), _copy(base), "zeros")
+                    yield ParamSpec(p + f"hc_{which}_scale", (3,), _copy(sc), "ones")
+                yield from self._attn_specs(p + "attn.", layer.self_attn)
+            if layer.gate_only is not None:
+                yield from _v4_gate_specs(p + "ffn.gate.", layer.gate_only, a)
+            mlp = layer.mlp
+            if isinstance(mlp, DenseMLP):
+                yield from _mlp_specs(p + "ffn.", mlp, a.intermediate_size)
+            elif isinstance(mlp, MoEBlock):
+                if mlp.gate is not None:
+                    yield from _v4_gate_specs(p + "ffn.gate.", mlp.gate, a)
+                ex = mlp.experts
+                for le in range(ex.n_local):
+                    q = f"{p}ffn.experts.{ex.offset + le}."
+                    s13 = None if ex.w13_scale is None else ex.w13_scale[le]
+                    s2 = None if ex.w2_scale is None else ex.w2_scale[le]
+                    yield from _swiglu_specs(q, ex.w13[le], ex.w2[le], s13, s2, a.moe_intermediate_size, H)
+                if mlp.shared_experts is not None:
+                    yield from _mlp_specs(p + "ffn.shared_experts.", mlp.shared_experts, a.shared_intermediate_size)
+
+
+def _v4_gate_specs(p: str, gate, arch: ModelArchConfig) -> Iterator[ParamSpec]:
+    yield ParamSpec(p + "weight", tuple(gate.weight.shape), _copy(gate.weight))
+    if gate.e_score_correction_bias is not None:
+        yield ParamSpec(p + "e_score_correction_bias", tuple(gate.e_score_correction_bias.shape),
+                        _copy(gate.e_score_correction_bias), "zeros")
+    if gate.tid2eid is not None:
+        V, k, E = arch.vocab_size, arch.num_experts_per_tok, arch.n_routed_experts
+
+        def table() -> torch.Tensor:  # seeded stand-in: k distinct experts per token id
+            v = torch.arange(V)[:, None]
+            return ((v * 7919 + torch.arange(k)[None, :] * (E // k + 1)) % E).to(torch.float32)
+
+        yield ParamSpec(p + "tid2eid", (V, k), lambda t, _g=gate: _g.tid2eid.copy_(t.to(torch.int32)), "custom",
+                        make=table)
+
+
 def _copy_plus_one(dst: torch.Tensor) -> Callable[[torch.Tensor], None]:
     """Zero-centred RMSNorm weight: the checkpoint stores (w - 1)."""
 
@@ -513,6 +695,7 @@ __all__ = [
     "AFDDeepseekForCausalLM",
     "AFDDeepseekV2ForCausalLM",
     "AFDDeepseekV3ForCausalLM",
+    "AFDDeepseekV4ForCausalLM",
     "AFDGlmMoeDsaForCausalLM",
     "AFDQwen3MoeForCausalLM",
     "AFDQwen3NextForCausalLM",

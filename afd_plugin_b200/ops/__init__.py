@@ -14,7 +14,7 @@ import torch
 from afd_plugin_b200.ops import reference as ref
 from afd_plugin_b200.ops._ext import ops as _cuda_ops
 
-SCORING_IDS = {"softmax": 0, "sigmoid": 1}
+SCORING_IDS = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 
 
 def _cuda(t: torch.Tensor) -> bool:
@@ -65,10 +65,12 @@ def topk_route(
     n_group: int = 1,
     topk_group: int = 1,
     routed_scaling_factor: float = 1.0,
+    forced_ids: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     if _cuda(logits):
+        forced = None if forced_ids is None else forced_ids.to(torch.int32).contiguous()
         return _cuda_ops().topk_route(
-            logits, top_k, SCORING_IDS[scoring], renormalize, bias, n_group, topk_group, routed_scaling_factor
+            logits, top_k, SCORING_IDS[scoring], renormalize, bias, n_group, topk_group, routed_scaling_factor, forced
         )
     return ref.topk_route(
         logits,
@@ -79,6 +81,7 @@ def topk_route(
         n_group=n_group,
         topk_group=topk_group,
         routed_scaling_factor=routed_scaling_factor,
+        forced_ids=forced_ids,
     )
 
 

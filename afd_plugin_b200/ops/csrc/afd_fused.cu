@@ -167,7 +167,8 @@ AFD_DEVICE void publish_dispatch(const DispatchParams& p) {
 }
 
 // ---- dispatch, step 1 (one CTA per token): residual += attn_out;
-// h = RMSNorm(residual) * w, kept locally for the router and stored straight
+// h = RMSNorm(residual) * w (or h = attn_out when the model normalised it
+// already, prenorm), kept locally for the router and stored straight
 // into the FFN ranks' token buffers: every FFN rank for an MoE layer (the
 // routing, which follows, tells each rank which rows it answers), the home
 // rank only for a dense layer.  A dense layer has no router step, so this
@@ -187,7 +188,12 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
   for (int u = 0; u < kNormMaxVec; ++u) {
     const int v = threadIdx.x + u * kThreads;
     if (v < nv) {
-      const Vec16<bf16> xa = load16(a + v * 8), xr = load16(r + v * 8);
+      const Vec16<bf16> xa = load16(a + v * 8);
+      if (p.prenorm) {
+        x[u] = xa;
+        continue;
+      }
+      const Vec16<bf16> xr = load16(r + v * 8);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         x[u].v[j] = __float2bfloat16_rn(__bfloat162float(xa.v[j]) + __bfloat162float(xr.v[j]));
@@ -197,13 +203,16 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
       store16(r + v * 8, x[u]);
     }
   }
-  ss = warp_sum(ss);
-  if (lane == 0) s_red[warp] = ss;
-  __syncthreads();
-  float tot = 0.f;
+  float inv = 1.f;
+  if (!p.prenorm) {
+    ss = warp_sum(ss);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) tot += s_red[w];
-  const float inv = rsqrtf(tot / (float)p.H + p.eps);
+    for (int w = 0; w < kWarps; ++w) tot += s_red[w];
+    inv = rsqrtf(tot / (float)p.H + p.eps);
+  }
   const bf16* nw = static_cast<const bf16*>(p.norm_w);
   bf16* h = static_cast<bf16*>(p.h) + (size_t)t * p.H;
   const size_t row_off = ((size_t)p.attn_rank * p.t_cap + t) * p.H;
@@ -213,11 +222,13 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
   for (int u = 0; u < kNormMaxVec; ++u) {
     const int v = threadIdx.x + u * kThreads;
     if (v < nv) {
-      const Vec16<bf16> w = load16(nw + v * 8);
-      Vec16<bf16> y;
+      Vec16<bf16> y = x[u];
+      if (!p.prenorm) {
+        const Vec16<bf16> w = load16(nw + v * 8);
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        y.v[j] = __float2bfloat16_rn(__bfloat162float(x[u].v[j]) * inv * __bfloat162float(w.v[j]));
+        for (int j = 0; j < 8; ++j)
+          y.v[j] = __float2bfloat16_rn(__bfloat162float(x[u].v[j]) * inv * __bfloat162float(w.v[j]));
+      }
       if (p.moe) store16(h + v * 8, y);
       for (int f = f_lo; f < f_hi; ++f) store16(reinterpret_cast<bf16*>(p.tok_ptrs[f]) + row_off + v * 8, y);
     }
@@ -316,8 +327,9 @@ __global__ void __launch_bounds__(kRouterThreads, 1) dispatch_router_kernel(Disp
     const int t = t0 + warp;
     float w;
     int id;
+    const int32_t* forced = p.hash_table ? p.hash_table + (size_t)p.input_ids[t] * p.k : nullptr;
     warp_route(lg + warp * p.E, p.gate_bias, p.E, p.k, p.scoring, p.renorm, p.n_group, p.topk_group, p.scale, w,
-               id);
+               id, forced);
     const unsigned bit = lane < p.k ? (1u << (id / p.e_local)) : 0u;
     const unsigned mask = __reduce_or_sync(0xffffffffu, bit) | (p.has_shared ? (1u << p.home_f) : 0u);
     const size_t off = ((size_t)p.attn_rank * p.t_cap + t) * p.k;

@@ -97,9 +97,11 @@ void rope_(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin
               (int)x.size(2), x.stride(0), x.stride(1), interleaved, dtype_code(x), stream());
 }
 
+// scoring: 0 softmax, 1 sigmoid, 2 sqrt(softplus); forced [T, k] int32 (hash routing) fixes the experts.
 std::tuple<at::Tensor, at::Tensor> topk_route(const at::Tensor& logits, int64_t k, int64_t scoring, bool renorm,
                                              const c10::optional<at::Tensor>& bias, int64_t n_group,
-                                             int64_t topk_group, double scale) {
+                                             int64_t topk_group, double scale,
+                                             const c10::optional<at::Tensor>& forced) {
   check_cuda(logits, "logits");
   auto lf = logits.to(at::kFloat).contiguous();
   const int T = (int)lf.size(0), E = (int)lf.size(1);
@@ -113,10 +115,17 @@ std::tuple<at::Tensor, at::Tensor> topk_route(const at::Tensor& logits, int64_t 
     bf = bias->to(at::kFloat).contiguous();
     bp = bf.data_ptr<float>();
   }
+  const int32_t* fp = nullptr;
+  if (forced.has_value() && forced->defined()) {
+    TORCH_CHECK(forced->scalar_type() == at::kInt && forced->is_contiguous() && forced->size(0) == T &&
+                    forced->size(1) == k, "topk_route: forced ids [T, k] int32");
+    fp = forced->data_ptr<int32_t>();
+  }
+  TORCH_CHECK(scoring >= 0 && scoring <= 2, "topk_route: scoring 0 softmax, 1 sigmoid, 2 sqrtsoftplus");
   c10::cuda::CUDAGuard g(logits.device());
   if (T > 0)
     launch_topk_route(lf.data_ptr<float>(), bp, w.data_ptr<float>(), ids.data_ptr<int32_t>(), T, E, (int)k,
-                      (int)scoring, renorm, (int)n_group, (int)topk_group, (float)scale, stream());
+                      (int)scoring, renorm, (int)n_group, (int)topk_group, (float)scale, fp, stream());
   return {w, ids};
 }
 
@@ -339,14 +348,17 @@ void afd_wait(const at::Tensor& flag, int64_t index, const at::Tensor& epoch, in
 //               attn_rank, home_f, layer]; ptrs [5, F]: tok, rid, rwt, tcount, arrive flags on each FFN rank.
 // done_ctr: int32 [>= 1 + ceil(T / 16)], zero before the first use and left zero by every call
 // ([0] send-kernel completion, [1:] router token tiles).
+// cfg[14] (optional) = prenorm: attn_out is already the FFN input; residual and norm_w are then unused.
+// hash_table [vocab, k] int32 + input_ids [T] int32: hash-routed layer (experts from the table).
 void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Tensor& norm_w, double eps,
                   const at::Tensor& gate_w, const c10::optional<at::Tensor>& gate_bias, double scale,
-                  const at::Tensor& ptrs, at::Tensor& fmask, at::Tensor& done_ctr, std::vector<int64_t> cfg) {
+                  const at::Tensor& ptrs, at::Tensor& fmask, at::Tensor& done_ctr, std::vector<int64_t> cfg,
+                  const c10::optional<at::Tensor>& hash_table, const c10::optional<at::Tensor>& input_ids) {
   check_cuda(attn_out, "attn_out");
   TORCH_CHECK(attn_out.scalar_type() == at::kBFloat16 && residual.scalar_type() == at::kBFloat16,
               "afd_dispatch: bf16 activations");
   TORCH_CHECK(attn_out.is_contiguous() && residual.is_contiguous() && gate_w.is_contiguous(), "afd_dispatch: layout");
-  TORCH_CHECK(cfg.size() == 14, "afd_dispatch: cfg has 14 entries");
+  TORCH_CHECK(cfg.size() == 14 || cfg.size() == 15, "afd_dispatch: cfg has 14 or 15 entries");
   TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.dim() == 2 && ptrs.size(0) == 5, "afd_dispatch: ptrs [5, F]");
   DispatchParams p{};
   p.attn_out = attn_out.data_ptr();
@@ -376,6 +388,16 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
   p.attn_rank = (int)cfg[11];
   p.home_f = (int)cfg[12];
   p.layer = (int)cfg[13];
+  p.prenorm = cfg.size() == 15 ? (int)cfg[14] : 0;
+  if (hash_table.has_value() && hash_table->defined()) {
+    TORCH_CHECK(input_ids.has_value() && input_ids->defined() && input_ids->scalar_type() == at::kInt &&
+                    input_ids->is_contiguous() && input_ids->numel() == attn_out.size(0),
+                "afd_dispatch: hash routing needs int32 input_ids [T]");
+    TORCH_CHECK(hash_table->scalar_type() == at::kInt && hash_table->is_contiguous() &&
+                    hash_table->size(1) == (int64_t)cfg[1], "afd_dispatch: hash table [vocab, k] int32");
+    p.hash_table = hash_table->data_ptr<int32_t>();
+    p.input_ids = input_ids->data_ptr<int32_t>();
+  }
   TORCH_CHECK(p.k <= 16 && p.H % 16 == 0 && p.H <= 8192 && p.T <= p.t_cap && p.num_ffn <= 32 && p.E <= 512,
               "afd_dispatch: k <= 16, H % 16 == 0, H <= 8192, T <= t_cap, at most 32 FFN ranks, E <= 512");
   const int64_t tiles = (p.T + 15) / 16;
@@ -640,7 +662,7 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("silu_and_mul(Tensor x) -> Tensor");
   m.def("rope_(Tensor(a!) x, Tensor positions, Tensor cos_sin, bool interleaved) -> ()");
   m.def("topk_route(Tensor logits, int k, int scoring, bool renorm, Tensor? bias, int n_group, int topk_group, "
-        "float scale) -> (Tensor, Tensor)");
+        "float scale, Tensor? forced=None) -> (Tensor, Tensor)");
   m.def("mla_cache_write(Tensor(a!) cache, Tensor kv_a, Tensor w, float eps, Tensor positions, Tensor cos_sin, "
         "Tensor slots, int L) -> ()");
   m.def("gqa_cache_write(Tensor(a!) kc, Tensor(b!) vc, Tensor k, Tensor v, Tensor slots) -> ()");
@@ -660,7 +682,8 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("afd_epoch(Tensor(a!) epoch) -> ()");
   m.def("afd_wait(Tensor flag, int index, Tensor epoch, int arrivals, int timeout_ns) -> ()");
   m.def("afd_dispatch(Tensor attn_out, Tensor(a!) residual, Tensor norm_w, float eps, Tensor gate_w, Tensor? gate_bias, "
-        "float scale, Tensor ptrs, Tensor(b!) fmask, Tensor(c!) done_ctr, int[] cfg) -> ()");
+        "float scale, Tensor ptrs, Tensor(b!) fmask, Tensor(c!) done_ctr, int[] cfg, Tensor? hash_table=None, "
+        "Tensor? input_ids=None) -> ()");
   m.def("afd_expand(Tensor tok, Tensor rid, Tensor rwt, Tensor tcount, Tensor(a!) x, Tensor(b!) meta, Tensor(c!) rw, "
         "Tensor(d!) counts, int[] cfg, Tensor? flag=None, int flag_index=0, Tensor? epoch=None, int arrivals=0, "
         "int timeout_ns=0) -> ()");

@@ -138,13 +138,15 @@ __global__ void rope_kernel(T* __restrict__ x, const int64_t* __restrict__ pos, 
 // One warp per token (see routing.cuh for the selection rules).
 __global__ void topk_route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
                                   float* __restrict__ out_w, int32_t* __restrict__ out_id, int tokens, int E, int k,
-                                  int scoring, bool renorm, int n_group, int topk_group, float scale) {
+                                  int scoring, bool renorm, int n_group, int topk_group, float scale,
+                                  const int32_t* __restrict__ forced) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (warp >= tokens) return;
   float w;
   int id;
-  warp_route(logits + (size_t)warp * E, bias, E, k, scoring, renorm, n_group, topk_group, scale, w, id);
+  warp_route(logits + (size_t)warp * E, bias, E, k, scoring, renorm, n_group, topk_group, scale, w, id,
+             forced ? forced + (size_t)warp * k : nullptr);
   if (lane < k) {
     out_w[(size_t)warp * k + lane] = w;
     out_id[(size_t)warp * k + lane] = id;
@@ -247,11 +249,12 @@ void launch_rope(void* x, const int64_t* pos, const float* cos_sin, int tokens, 
 }
 
 void launch_topk_route(const float* logits, const float* bias, float* w, int32_t* ids, int tokens, int E, int k,
-                       int scoring, bool renorm, int n_group, int topk_group, float scale, cudaStream_t s) {
+                       int scoring, bool renorm, int n_group, int topk_group, float scale, const int32_t* forced,
+                       cudaStream_t s) {
   const int warps_per_block = 4;
   dim3 grid((tokens + warps_per_block - 1) / warps_per_block);
   topk_route_kernel<<<grid, 32 * warps_per_block, 0, s>>>(logits, bias, w, ids, tokens, E, k, scoring, renorm,
-                                                          n_group, topk_group, scale);
+                                                          n_group, topk_group, scale, forced);
 }
 
 void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float eps, const int64_t* pos,

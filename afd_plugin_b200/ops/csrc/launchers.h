@@ -16,7 +16,8 @@ void launch_silu_and_mul(void* out, const void* in, int rows, int d, int dtype, 
 void launch_rope(void* x, const int64_t* pos, const float* cos_sin, int tokens, int heads, int rot, int64_t st,
                  int64_t sh, bool interleaved, int dtype, cudaStream_t s);
 void launch_topk_route(const float* logits, const float* bias, float* w, int32_t* ids, int tokens, int E, int k,
-                       int scoring, bool renorm, int n_group, int topk_group, float scale, cudaStream_t s);
+                       int scoring, bool renorm, int n_group, int topk_group, float scale, const int32_t* forced,
+                       cudaStream_t s);
 void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float eps, const int64_t* pos,
                             const float* cos_sin, const int64_t* slots, int tokens, int L, int R, int64_t kv_stride,
                             int dtype, cudaStream_t s);
@@ -95,6 +96,9 @@ struct DispatchParams {
   unsigned* route_ctr;         // local [ceil(T / 16)] router completion counters (zero between uses)
   void* h;                     // local scratch [T, H] bf16: normalised rows
   float* logits;               // local scratch [T, E] fp32: router logits
+  int prenorm;                 // 1: attn_out is already the FFN input (no residual add / norm)
+  const int32_t* hash_table;   // [vocab, k] expert ids per token id (hash-routed layer) or null
+  const int32_t* input_ids;    // [T] token ids (with hash_table)
   int* status;
 };
 // FFN side: received token rows -> per-expert contiguous segments (local copies).

@@ -9,9 +9,12 @@ constexpr int kRouteMaxPerLane = 16;  // E <= 512
 
 // `row` holds E fp32 logits (global or shared memory).  Lanes 0..k-1 receive
 // (weight, expert id) of the r-th selected expert.  Ties break toward the
-// lower expert id.  scoring: 0 softmax, 1 sigmoid (+bias for selection only).
+// lower expert id.  scoring: 0 softmax, 1 sigmoid, 2 sqrt(softplus) (1 and 2
+// add the bias for selection only).  `forced` (hash routing) gives the k
+// expert ids; only their weights come from the scores.
 AFD_DEVICE void warp_route(const float* row, const float* bias, int E, int k, int scoring, bool renorm,
-                           int n_group, int topk_group, float scale, float& out_w, int& out_id) {
+                           int n_group, int topk_group, float scale, float& out_w, int& out_id,
+                           const int32_t* forced = nullptr) {
   const int lane = threadIdx.x & 31;
   float score[kRouteMaxPerLane], sel[kRouteMaxPerLane];
   float mx = -INFINITY;
@@ -41,9 +44,32 @@ AFD_DEVICE void warp_route(const float* row, const float* bias, int E, int k, in
 #pragma unroll
     for (int j = 0; j < kRouteMaxPerLane; ++j) {
       const int e = j * 32 + lane;
-      score[j] = (e < E) ? 1.f / (1.f + __expf(-score[j])) : 0.f;
+      const float x = score[j];
+      const float act = scoring == 1 ? 1.f / (1.f + __expf(-x)) : sqrtf(x > 20.f ? x : log1pf(__expf(x)));
+      score[j] = (e < E) ? act : 0.f;
       sel[j] = (e < E) ? score[j] + (bias ? bias[e] : 0.f) : -INFINITY;
     }
+  }
+  if (forced != nullptr) {
+    float wsum = 0.f, my_w = 0.f;
+    int my_id = 0;
+    for (int r = 0; r < k; ++r) {
+      const int id = forced[r];
+      const int jj = id >> 5;
+      float v = 0.f;
+#pragma unroll
+      for (int j = 0; j < kRouteMaxPerLane; ++j)
+        if (j == jj) v = score[j];
+      const float wv = __shfl_sync(0xffffffffu, v, id & 31);
+      wsum += wv;
+      if (lane == r) {
+        my_w = wv;
+        my_id = id;
+      }
+    }
+    out_w = (renorm ? my_w / wsum : my_w) * scale;
+    out_id = my_id;
+    return;
   }
   if (n_group > 1 && topk_group < n_group) {
     const int gsize = E / n_group;

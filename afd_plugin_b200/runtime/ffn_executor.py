@@ -56,7 +56,7 @@ class LocalFFNExecutor(FFNExecutor):
 
     def send(self, layer_idx, attn_out, residual, stage_idx):
         h, residual = self.model.post_attention_norm(layer_idx, attn_out, residual)
-        return self.model.compute_ffn_output(h, layer_idx), residual
+        return self.model.compute_ffn_output(h, layer_idx, **self.model.ffn_extra(layer_idx, residual)), residual
 
     def recv(self, layer_idx, handle, stage_idx):
         return handle
@@ -120,7 +120,9 @@ class ConnectorFFNExecutor(FFNExecutor):
             metadata=AFDTransferMetadata.create_attention_metadata(
                 layer_idx=layer_idx, stage_idx=stage_idx, seq_len=int(h.shape[0]))
         )
-        kwargs = {}
+        kwargs = dict(model.ffn_extra(layer_idx, residual))
+        if "input_ids" in kwargs:
+            kwargs["input_ids"] = kwargs["input_ids"].to(torch.int32)
         if self.gate_on_attn:
             kwargs["router_logits"] = model.compute_router_logits(layer_idx, h)
         self.connector.send_attn_output(h, ctx, **kwargs)

@@ -110,12 +110,15 @@ class FFNModelRunner:
         for layer in model.ffn_layer_indices():
             is_moe = model.arch.is_moe_layer(layer)
             routing_spec = model.get_experts_routing_spec(layer) if (is_moe and gate_on_attn) else None
+            want_ids = model.ffn_needs_input_ids(layer)
             for stage in stages:
                 kw = {"routing_spec": routing_spec} if routing_spec is not None else {}
+                if want_ids:
+                    kw["recv_input_ids"] = True
                 recv = c.recv_attn_output(ubatch_idx=stage, **kw)
                 recv.context.metadata.layer_idx = layer
                 recv.context.metadata.stage_idx = stage
-                out = self.compute(layer, stage, recv.hidden_states, recv.router_logits)
+                out = self.compute(layer, stage, recv.hidden_states, recv.router_logits, recv.input_ids)
                 c.send_ffn_output(out, recv.context)
         flush = getattr(c, "flush", None)
         if callable(flush):
@@ -123,17 +126,19 @@ class FFNModelRunner:
         return out
 
     # ------------------------------------------------------------ compute
-    def compute(self, layer: int, stage: int, h: torch.Tensor, router_logits: torch.Tensor | None) -> torch.Tensor:
+    def compute(self, layer: int, stage: int, h: torch.Tensor, router_logits: torch.Tensor | None,
+                input_ids: torch.Tensor | None = None) -> torch.Tensor:
         model = self.model
         if not model.arch.is_moe_layer(layer):
             return model.compute_ffn_output(h, layer)
         if self.ep_size == 1:
             if router_logits is not None:
                 return model.compute_experts_output(h, layer, router_logits)
-            return model.compute_ffn_output(h, layer)
-        return self._moe_expert_parallel(layer, stage, h, router_logits)
+            return model.compute_ffn_output(h, layer, input_ids=input_ids)
+        return self._moe_expert_parallel(layer, stage, h, router_logits, input_ids)
 
-    def _moe_expert_parallel(self, layer: int, stage: int, h: torch.Tensor, router_logits) -> torch.Tensor:
+    def _moe_expert_parallel(self, layer: int, stage: int, h: torch.Tensor, router_logits,
+                             input_ids: torch.Tensor | None = None) -> torch.Tensor:
         moe = self.model.layers[layer].mlp
         counts = self._ffn_counts[stage]
         n_max = max(counts)
@@ -148,7 +153,8 @@ class FFNModelRunner:
 
         h_all = gather(h)
         logits_all = gather(router_logits) if router_logits is not None else moe.gate.logits(h_all)
-        w, ids = moe.gate.route(logits_all)
+        ids_all = gather(input_ids.view(-1, 1)).view(-1) if input_ids is not None else None
+        w, ids = moe.gate.route(logits_all, ids_all)
         partial = moe.experts(h_all, w, ids).float()
         # Reduce the partial sums back to their owners.
         padded = partial.new_zeros((self.ep_size * n_max, H))

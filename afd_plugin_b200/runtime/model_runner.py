@@ -125,6 +125,8 @@ class ModelRunner:
         counts = {s: splits[s + 1] - splits[s] for s in range(len(splits) - 1)}
         self.ffn.begin_step(counts, **step_flags)
         self.ffn.step_prologue()
+        for s, m in enumerate(metas):
+            m.input_ids = input_ids[splits[s] : splits[s + 1]]
         embeds = [self.model.embed(input_ids[splits[s] : splits[s + 1]]) for s in range(len(splits) - 1)]
         outs = self._run_stages(embeds, metas)
         self.ffn.end_step()

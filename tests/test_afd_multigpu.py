@@ -82,3 +82,15 @@ def test_fused_connector_qwen3_5_1a1f():
     outs = _run(afd, prompts, 6, preset="tiny-qwen3.5", enforce_eager=False, capture_sizes=[4])
     assert [o[0] for o in outs] == [o[0] for o in ref]
     assert _agreement(outs, ref) >= 0.75
+
+
+def test_fused_connector_dsv4_1a1f():
+    """mHC on the Attention side (pre-normalised dispatch) and hash routing in the router kernel."""
+    _need(2)
+    prompts = _prompts(4, 16)
+    ref = _colocated(prompts, 6, preset="tiny-dsv4")
+    afd = {"num_attention_ranks": 1, "num_ffn_ranks": 1, "connector": "B200FusedAFDConnector",
+           "connector_extra_config": {"max_tokens_per_rank": 128, "wait_timeout_ms": 20000}}
+    outs = _run(afd, prompts, 6, preset="tiny-dsv4", enforce_eager=False, capture_sizes=[4])
+    assert [o[0] for o in outs] == [o[0] for o in ref]
+    assert _agreement(outs, ref) >= 0.75

@@ -73,3 +73,18 @@ def test_qwen3_5_hybrid_2a1f():
     ref = _colocated("tiny-qwen3.5", prompts, 6)
     outs, _ = _run("tiny-qwen3.5", {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=6)
     assert outs == ref
+
+
+def test_dsv4_mhc_hash_routing_2a1f():
+    """mHC streams stay on the Attention side; hash-routed layers ship the token ids to the FFN."""
+    prompts = _prompts(n=4, length=12)
+    ref = _colocated("tiny-dsv4", prompts, 6)
+    outs, _ = _run("tiny-dsv4", {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=6)
+    assert outs == ref
+
+
+def test_dsv4_expert_parallel_2a2f():
+    prompts = _prompts(n=4, length=12)
+    ref = _colocated("tiny-dsv4", prompts, 5)
+    outs, _ = _run("tiny-dsv4", {"num_attention_ranks": 2, "num_ffn_ranks": 2}, prompts, max_tokens=5)
+    assert outs == ref

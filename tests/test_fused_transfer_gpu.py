@@ -173,3 +173,26 @@ def test_dispatch_dense_layer_goes_home_only():
     torch.testing.assert_close(lb.tok[0][0, :T].float(), h_ref.float(), atol=2e-2, rtol=1e-2)
     assert int(lb.tok[1].abs().sum()) == 0
     assert [int(a[0]) for a in lb.arrive] == [1, 1]
+
+
+def test_dispatch_prenormed_hash_routed():
+    """Pre-normalised rows (no residual / norm) and experts forced by a token-id table."""
+    torch.manual_seed(11)
+    C = _ext.ops()
+    F, H, E, k, t_cap, T, vocab = 2, 256, 64, 4, 64, 29, 100
+    lb = _Loopback(F, t_cap, H, E, k)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    gate = (torch.randn(E, H, device=DEV) / H**0.5).to(torch.bfloat16)
+    table = torch.randint(0, E, (vocab, k), device=DEV, dtype=torch.int32)
+    ids_tok = torch.randint(0, vocab, (T,), device=DEV, dtype=torch.int32)
+    cfg = [E, k, 2, 1, 1, 1, 1, 1, F, E // F, t_cap, 0, 0, 0, 1]
+    C.afd_dispatch(x, x, x, 0.0, gate, None, 1.5, lb.ptrs, lb.fmask, lb.dctr, cfg, table, ids_tok)
+    torch.cuda.synchronize()
+    for f in range(F):
+        torch.testing.assert_close(lb.tok[f][0, :T], x, atol=0, rtol=0)  # rows sent as given
+    logits = x.float() @ gate.float().t()
+    w_ref, id_ref = ref.topk_route(logits, k, scoring="sqrtsoftplus", renormalize=True, routed_scaling_factor=1.5,
+                                   forced_ids=table[ids_tok.long()])
+    assert torch.equal(lb.rid[0][0, :T].cpu(), id_ref.cpu())
+    torch.testing.assert_close(lb.rwt[1][0, :T], w_ref, atol=1e-3, rtol=1e-3)
+    assert int(lb.dctr.abs().sum()) == 0 and [int(a[0]) for a in lb.arrive] == [1, 1]

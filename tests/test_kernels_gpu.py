@@ -79,6 +79,24 @@ def test_topk_route(cfg):
     _close(w, w_ref, 1e-5, 1e-5)
 
 
+@pytest.mark.parametrize("renorm", [True, False])
+def test_topk_route_sqrtsoftplus_and_hash(renorm):
+    """DeepSeek-V4 routing: sqrt(softplus) scores with a selection bias, and hash-forced experts."""
+    E, k = 64, 6
+    logits = torch.randn(150, E, device=DEV)
+    bias = torch.randn(E, device=DEV) * 0.1
+    cfg = dict(scoring="sqrtsoftplus", renormalize=renorm, routed_scaling_factor=1.5)
+    w, ids = ops.topk_route(logits, k, bias=bias, **cfg)
+    w_ref, ids_ref = ref.topk_route(logits.cpu(), k, bias=bias.cpu(), **cfg)
+    assert torch.equal(ids.cpu(), ids_ref)
+    _close(w, w_ref, 1e-5, 1e-5)
+    forced = torch.randint(0, E, (150, k), device=DEV, dtype=torch.int32)
+    w, ids = ops.topk_route(logits, k, forced_ids=forced, **cfg)
+    w_ref, ids_ref = ref.topk_route(logits.cpu(), k, forced_ids=forced.cpu(), **cfg)
+    assert torch.equal(ids.cpu(), ids_ref)
+    _close(w, w_ref, 1e-5, 1e-5)
+
+
 def _paged_cache(B, lens, width, bs=64, dtype=torch.bfloat16, extra_blocks=3):
     nblk_seq = [math.ceil(n / bs) for n in lens]
     total = sum(nblk_seq) + extra_blocks

@@ -12,7 +12,7 @@ from afd_plugin_b200.models.configs import ModelArchConfig
 from afd_plugin_b200.models.loader import load_weights
 from afd_plugin_b200.runtime.engine import LLMEngine
 
-PRESETS = ["tiny-dsv2", "tiny-qwen3-moe", "tiny-dsv3", "tiny-qwen3.5"]
+PRESETS = ["tiny-dsv2", "tiny-qwen3-moe", "tiny-dsv3", "tiny-qwen3.5", "tiny-dsv4"]
 
 
 def _engine(preset, **kw):
