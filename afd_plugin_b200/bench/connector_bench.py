@@ -47,6 +47,7 @@ def _args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--paths", default="fused,nccl")
     ap.add_argument("--out", default="")
+    ap.add_argument("--fp8", action="store_true", help="rows travel as e4m3 with 1x128 scales (fused path)")
     ap.add_argument("--breakdown", action="store_true",
                     help="time each kernel of single round trips (barrier between trips)")
     return ap.parse_args(argv)
@@ -74,6 +75,7 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
     afd = afd_config_from_mapping({
         "role": role, "connector": "B200FusedAFDConnector", "num_attention_ranks": A, "num_ffn_ranks": F,
         "connector_extra_config": {"max_tokens_per_rank": t_cap, "expert_capacity_factor": 4.0,
+                                   "fp8_dispatch": bool(args.fp8),
                                    "wait_timeout_ms": 20000}})
     ec = EngineConfig(ModelConfig(arch, dtype=torch.bfloat16), additional_config={"afd": {}}, max_num_seqs=t_cap)
     conn = B200FusedAFDConnector(rank, rank, ec, afd, role_rank)
@@ -105,7 +107,8 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
             C.afd_combine_send(conn.tok[0], conn.rid[0], conn.rwt[0], conn.tcount[0], conn.comb_ptrs[0],
                                conn.comb_flag_ptrs[0], conn.done[0, 2:3], H,
                                [A, d.t_cap, args.topk, d.slots, d.e_local, role_rank * d.e_local, d.ratio,
-                                role_rank * d.ratio, 1, 0, role_rank, F, 0, 1])
+                                role_rank * d.ratio, 1, 0, role_rank, F, 0, 1],
+                               tok_scale=conn.tok_scale[0] if conn.dims.fp8 else None)
 
         fn = step_attn if role == "attention" else step_ffn
         if args.breakdown:
@@ -132,13 +135,15 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
         else:
             dest = 0
         dest = int(_max_over_ranks(float(dest)))
-        bytes_per_attn = 2 * dest * H * 2 + 2 * T * args.topk * 8 * F  # rows out + back, routing metadata
+        out_row = H + H // 32 if args.fp8 else 2 * H  # e4m3 row + fp32 scale per 128 columns, or bf16
+        bytes_per_attn = dest * (out_row + 2 * H) + 2 * T * args.topk * 8 * F  # rows out + back, routing metadata
         gbps = bytes_per_attn / (us * 1e-6) / 1e9
         # roofline: each direction limited by one GPU's NVLink; the busiest GPU is an FFN rank
         # receiving from its share of the Attention ranks.
         ffn_rows = dest * A / F
-        ideal_us = max(dest, ffn_rows) * H * 2 / (NVLINK_GBPS * 1e9) * 1e6
-        results.append({"path": "fused", "tokens": T, "us": round(us, 2), "GBps": round(gbps, 1),
+        ideal_us = max(dest, ffn_rows) * max(out_row, 2 * H) / (NVLINK_GBPS * 1e9) * 1e6
+        results.append({"path": "fused-fp8" if args.fp8 else "fused", "tokens": T, "us": round(us, 2),
+                        "GBps": round(gbps, 1),
                         "rows_per_token": round(dest / max(1, T), 2),
                         "roofline_frac": round(ideal_us / us, 3), "status": status})
     conn.close()
@@ -172,7 +177,8 @@ def _breakdown(args, role, T, conn, x, res, norm_w, gate_w, role_rank, d, A, F, 
             C.afd_combine_send(conn.tok[0], conn.rid[0], conn.rwt[0], conn.tcount[0], conn.comb_ptrs[0],
                                conn.comb_flag_ptrs[0], conn.done[0, 2:3], H,
                                [A, d.t_cap, args.topk, d.slots, d.e_local, role_rank * d.e_local, d.ratio,
-                                role_rank * d.ratio, 1, 0, role_rank, F, 0, 1])
+                                role_rank * d.ratio, 1, 0, role_rank, F, 0, 1],
+                               tok_scale=conn.tok_scale[0] if conn.dims.fp8 else None)
         ev[3].record()
         torch.cuda.synchronize()
         if it >= args.warmup:

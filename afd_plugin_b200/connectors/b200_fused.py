@@ -86,8 +86,6 @@ class B200FusedExtraInfo(ConnectorExtraInfo):
             fp8_dispatch=coerce_extra_bool(raw.get("fp8_dispatch", False), field_name="fp8_dispatch"),
             expert_capacity_factor=_positive_float(raw.get("expert_capacity_factor")),
         )
-        if out.fp8_dispatch:
-            raise ValueError("B200FusedAFDConnector: fp8_dispatch is not available yet (bf16 rows are sent)")
         return out
 
     def to_mapping(self) -> dict[str, Any]:
@@ -119,6 +117,8 @@ class FusedLayout:
     top_k: int
     t_cap: int  # tokens per Attention rank per stage
     capacity_factor: float | None = None
+    # Rows travel as e4m3 with one fp32 scale per 128 columns (half the NVLink bytes).
+    fp8: bool = False
 
     @property
     def ratio(self) -> int:
@@ -151,7 +151,11 @@ class FusedLayout:
         """Regions every rank maps (peers write into them)."""
         L = HeapLayout()
         S, A, F = self.stages, self.num_attn, self.num_ffn
-        L.add("tok", (S, A, self.t_cap, self.hidden), torch.bfloat16)      # FFN side: token rows per source
+        if self.fp8:
+            L.add("tok", (S, A, self.t_cap, self.hidden), torch.uint8)     # FFN side: e4m3 token rows per source
+            L.add("tok_scale", (S, A, self.t_cap, self.hidden // 128), torch.float32)
+        else:
+            L.add("tok", (S, A, self.t_cap, self.hidden), torch.bfloat16)  # FFN side: token rows per source
         L.add("rid", (S, A, self.t_cap, self.top_k), torch.int32)          # FFN side: routed expert ids
         L.add("rwt", (S, A, self.t_cap, self.top_k), torch.float32)        # FFN side: routing weights
         L.add("tcount", (S, A), torch.int32)                               # FFN side: tokens per source
@@ -199,7 +203,9 @@ class B200FusedAFDConnector(AFDConnectorBase):
             num_attn=self.attn_size, num_ffn=self.ffn_size, stages=stages, layers=arch.num_hidden_layers,
             hidden=arch.hidden_size, experts=max(arch.n_routed_experts, self.ffn_size),
             top_k=max(arch.num_experts_per_tok, 1), t_cap=t_cap,
-            capacity_factor=self.extra_info.expert_capacity_factor)
+            capacity_factor=self.extra_info.expert_capacity_factor, fp8=bool(self.extra_info.fp8_dispatch))
+        if self.dims.fp8 and arch.hidden_size % 128:
+            raise ValueError("fp8_dispatch needs the hidden size to be a multiple of 128")
         self.timeout_ns = int(self.extra_info.wait_timeout_ms) * 1_000_000
         self.heap = None
         self.control_group = None
@@ -237,6 +243,7 @@ class B200FusedAFDConnector(AFDConnectorBase):
         d, h = self.dims, self.heap
         for name in ("tok", "rid", "rwt", "tcount", "arrive", "comb", "comb_flag", "epoch", "done"):
             setattr(self, name, h.view(name))
+        self.tok_scale = h.view("tok_scale") if d.fp8 else None
         self.fmask = torch.zeros(d.stages, d.t_cap, dtype=torch.int32, device=self.device)
         # dispatch completion counters: [0] send kernel, [1:] router token tiles of 16
         self.dctr = torch.zeros(d.stages, 1 + (d.t_cap + 15) // 16, dtype=torch.int32, device=self.device)
@@ -247,8 +254,9 @@ class B200FusedAFDConnector(AFDConnectorBase):
         # Attention side, per stage: [5, F] -> tok, rid, rwt, tcount, arrive on each FFN rank.
         # FFN side, per stage: comb / comb_flag on each Attention rank.
         self.dispatch_ptrs, self.comb_ptrs, self.comb_flag_ptrs = [], [], []
+        names = ("tok", "rid", "rwt", "tcount", "arrive") + (("tok_scale",) if d.fp8 else ())
         for s in range(d.stages):
-            rows = [h.ptr_table(ffn_world, n, s * sb(n)) for n in ("tok", "rid", "rwt", "tcount", "arrive")]
+            rows = [h.ptr_table(ffn_world, n, s * sb(n)) for n in names]
             self.dispatch_ptrs.append(torch.stack(rows))
             self.comb_ptrs.append(h.ptr_table(attn_world, "comb", s * sb("comb")))
             self.comb_flag_ptrs.append(h.ptr_table(attn_world, "comb_flag", s * sb("comb_flag")))
@@ -421,6 +429,8 @@ class FusedFFNRunner:
         self.rw = torch.zeros(S, max(1, rows), dtype=torch.float32, device=dev)
         self.counts = torch.zeros(S, d.e_local + max(d.ratio, self.n_chunks), dtype=torch.int32, device=dev)
         self.staging = torch.empty(S, A, d.t_cap, self.J, H, dtype=torch.bfloat16, device=dev)
+        # e4m3 rows: expand writes bf16 copies of the home sources' rows here
+        self.home_x = (torch.zeros(S, d.ratio * d.t_cap, H, dtype=torch.bfloat16, device=dev) if d.fp8 else None)
         stage_stride = self.staging[0, 0].numel() * self.staging.element_size()
         self.staging_ptrs = [
             torch.tensor([self.staging[s].data_ptr() + a * stage_stride for a in range(A)], dtype=torch.int64,
@@ -446,15 +456,16 @@ class FusedFFNRunner:
         """Per layer: routed (w13, w2) and the home-token weights (shared experts or dense MLP)."""
         a = self.model.arch
         self.layer_w = []
+        self.layer_s = []  # fp8 block scales matching layer_w (None entries for bf16 weights)
         self.shared_gate_w = []  # per MoE layer: shared-expert gate weight [1, H] or None
+        u = lambda t: None if t is None else t.unsqueeze(0)  # noqa: E731
         for i, layer in enumerate(self.model.layers):
             mlp = layer.mlp
             if a.is_moe_layer(i):
                 ex = mlp.experts
-                if ex.w13_scale is not None:
-                    raise NotImplementedError("fused FFN path: fp8 block-scaled experts not wired yet")
                 if self.n_chunks:
                     self.layer_w.append((ex.w13_all, ex.w2_all, None, None))
+                    self.layer_s.append((None, None, None, None))
                     self.shared_gate_w.append(mlp.shared_expert_gate)
                     continue
                 if mlp.shared_expert_gate is not None:
@@ -464,8 +475,11 @@ class FusedFFNRunner:
                 sw13 = shared.w13.unsqueeze(0) if shared is not None else None
                 sw2 = shared.w2.unsqueeze(0) if shared is not None else None
                 self.layer_w.append((ex.w13, ex.w2, sw13, sw2))
+                self.layer_s.append((ex.w13_scale, ex.w2_scale, u(shared.w13_scale) if shared is not None else None,
+                                     u(shared.w2_scale) if shared is not None else None))
             else:
                 self.layer_w.append((None, None, mlp.w13.unsqueeze(0), mlp.w2.unsqueeze(0)))
+                self.layer_s.append((None, None, u(mlp.w13_scale), u(mlp.w2_scale)))
                 self.shared_gate_w.append(None)
 
     def _layer(self, layer_idx: int, s: int) -> None:
@@ -473,6 +487,12 @@ class FusedFFNRunner:
         C = torch.ops.afd_b200
         A, H = d.num_attn, d.hidden
         w13, w2, sw13, sw2 = self.layer_w[layer_idx]
+        s13, s2, ss13, ss2 = self.layer_s[layer_idx]
+
+        def gemm1(x, w, scale, off, cnt, ne):
+            if scale is not None:
+                return C.grouped_gemm_w8(x, w, scale, off, cnt, 1, ne)
+            return C.grouped_gemm_ex(x, w, off, cnt, 1, ne)
         is_moe = w13 is not None
         merged = is_moe and self.n_chunks > 0
         counts = self.counts[s]
@@ -481,8 +501,12 @@ class FusedFFNRunner:
         C.afd_expand(c.tok[s], c.rid[s], c.rwt[s], c.tcount[s], self.x[s], self.meta[s], self.rw[s], counts,
                      [A, d.t_cap, d.top_k, d.e_local, self.e_offset, d.cap, d.ratio, self.home_a0, int(is_moe),
                       n_chunks, self.shared_base, self.shared_stride],
-                     c.arrive[s], layer_idx, c.epoch[s : s + 1], A, c.timeout_ns)
-        home_rows = c.tok[s][self.home_a0 : self.home_a0 + d.ratio].reshape(d.ratio * d.t_cap, H)
+                     c.arrive[s], layer_idx, c.epoch[s : s + 1], A, c.timeout_ns,
+                     c.tok_scale[s] if d.fp8 else None, self.home_x[s] if d.fp8 else None)
+        if d.fp8:
+            home_rows = self.home_x[s]
+        else:
+            home_rows = c.tok[s][self.home_a0 : self.home_a0 + d.ratio].reshape(d.ratio * d.t_cap, H)
         launches = []
         sgw = self.shared_gate_w[layer_idx]
         if merged and sgw is not None:
@@ -498,18 +522,19 @@ class FusedFFNRunner:
             # routed experts and shared-expert chunks in one GEMM per projection
             ne = d.e_local + n_chunks
             h_r = C.grouped_gemm_ex(self.x[s], w13, self.off_all, counts[:ne], 1, ne)
-            launches.append((h_r, w2, self.off_all, counts[:ne], ne, self.meta[s], self.rw[s]))
+            launches.append((h_r, w2, self.off_all, counts[:ne], ne, self.meta[s], self.rw[s], None))
         elif is_moe:
-            h_r = C.grouped_gemm_ex(self.x[s], w13, self.off_routed, counts[: d.e_local], 1, d.e_local)
-            launches.append((h_r, w2, self.off_routed, counts[: d.e_local], d.e_local, self.meta[s], self.rw[s]))
+            h_r = gemm1(self.x[s], w13, s13, self.off_routed, counts[: d.e_local], d.e_local)
+            launches.append((h_r, w2, self.off_routed, counts[: d.e_local], d.e_local, self.meta[s], self.rw[s], s2))
         if sw13 is not None:
-            h_s = C.grouped_gemm_ex(home_rows, sw13, self.off_shared, counts[d.e_local :], 1, 1)
-            launches.append((h_s, sw2, self.off_shared, counts[d.e_local :], 1, self.meta_shared, self.rw_shared))
-        total = sum(int(C.grouped_gemm_grid((H // 128) * int(cnt.numel()))) for _, _, _, cnt, _, _, _ in launches)
-        for h, w, off, cnt, wexp, meta, rw in launches:
+            h_s = gemm1(home_rows, sw13, ss13, self.off_shared, counts[d.e_local : d.e_local + d.ratio], 1)
+            launches.append((h_s, sw2, self.off_shared, counts[d.e_local : d.e_local + d.ratio], 1, self.meta_shared,
+                             self.rw_shared, ss2))
+        total = sum(int(C.grouped_gemm_grid((H // 128) * int(ln[3].numel()))) for ln in launches)
+        for h, w, off, cnt, wexp, meta, rw, scale in launches:
             # Expert outputs land in local staging slots; the last CTA clears the counters.
             C.grouped_gemm_scatter(h, w, off, cnt, wexp, meta, rw, self.staging_ptrs[s], self.no_flags,
-                                   c.done[s, 1:2], counts, [self.J, H, total, 0, layer_idx])
+                                   c.done[s, 1:2], counts, [self.J, H, total, 0, layer_idx], scale)
         has_home = merged or sw13 is not None
         C.afd_combine_send(self.staging[s], c.rid[s], c.rwt[s], c.tcount[s], c.comb_ptrs[s], c.comb_flag_ptrs[s],
                            c.done[s, 2:3], H,

@@ -375,6 +375,14 @@ class DenseMLP(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.quant == "fp8_block":
+            if x.is_cuda and x.shape[0] > 0:
+                # one-"expert" grouped GEMMs on the fp8 weights (tiles dequantised in shared memory)
+                C = ops._cuda_ops()
+                T = x.shape[0]
+                off = torch.zeros(1, dtype=torch.int32, device=x.device)
+                cnt = torch.full((1,), T, dtype=torch.int32, device=x.device)
+                h = C.grouped_gemm_w8(x.contiguous(), self.w13.unsqueeze(0), self.w13_scale.unsqueeze(0), off, cnt, 1, 1)
+                return C.grouped_gemm_w8(h, self.w2.unsqueeze(0), self.w2_scale.unsqueeze(0), off, cnt, 0, 1)
             from afd_plugin_b200.ops import reference as ref
 
             w13 = ref.dequant_block(self.w13, self.w13_scale).to(x.dtype)

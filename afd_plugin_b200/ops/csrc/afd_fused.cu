@@ -28,6 +28,8 @@
 // Counters only grow: the n-th use of a stage expects epoch[stage] * arrivals,
 // so captured graphs replay without resets.  No wait is unbounded: on expiry
 // a kernel records kStatusWaitTimeout and returns.
+#include <cuda_fp8.h>
+
 #include <cstdlib>
 
 #include "common.cuh"
@@ -152,6 +154,40 @@ AFD_DEVICE void warp_sum_rows(bf16* out, const bf16* src, size_t stride, unsigne
   }
 }
 
+// e4m3 <-> bf16 helpers for rows that travel as fp8 with one scale per 128 columns.
+AFD_DEVICE uint2 pack_e4m3x8(const Vec16<bf16>& y, float inv) {
+  uint32_t w[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+        make_float2(__bfloat162float(y.v[4 * i]) * inv, __bfloat162float(y.v[4 * i + 1]) * inv), __NV_SATFINITE,
+        __NV_E4M3);
+    const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+        make_float2(__bfloat162float(y.v[4 * i + 2]) * inv, __bfloat162float(y.v[4 * i + 3]) * inv), __NV_SATFINITE,
+        __NV_E4M3);
+    w[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+  return make_uint2(w[0], w[1]);
+}
+// 16 e4m3 values -> 16 bf16 times `scale` (two 16-byte vectors).
+AFD_DEVICE void unpack_e4m3x16(uint4 raw, float scale, Vec16<bf16>& a, Vec16<bf16>& b) {
+  const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)((in[i] >> (16 * h)) & 0xFFFFu), __NV_E4M3);
+      __half2 h2;
+      *reinterpret_cast<__half2_raw*>(&h2) = hr;
+      const float2 f = __half22float2(h2);
+      Vec16<bf16>& dst = i < 2 ? a : b;
+      const int j = (i & 1) * 4 + h * 2;
+      dst.v[j] = __float2bfloat16_rn(f.x * scale);
+      dst.v[j + 1] = __float2bfloat16_rn(f.y * scale);
+    }
+  }
+}
+
 __global__ void epoch_kernel(uint64_t* epoch) { *epoch += 1; }
 
 __global__ void wait_kernel(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns,
@@ -218,18 +254,37 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
   const size_t row_off = ((size_t)p.attn_rank * p.t_cap + t) * p.H;
   const int f_lo = p.moe ? 0 : p.home_f;
   const int f_hi = p.moe ? p.num_ffn : (p.has_shared ? p.home_f + 1 : p.home_f);
+  const size_t row = (size_t)p.attn_rank * p.t_cap + t;
 #pragma unroll
   for (int u = 0; u < kNormMaxVec; ++u) {
     const int v = threadIdx.x + u * kThreads;
-    if (v < nv) {
-      Vec16<bf16> y = x[u];
-      if (!p.prenorm) {
-        const Vec16<bf16> w = load16(nw + v * 8);
+    const bool valid = v < nv;
+    Vec16<bf16> y = x[u];
+    if (valid && !p.prenorm) {
+      const Vec16<bf16> w = load16(nw + v * 8);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          y.v[j] = __float2bfloat16_rn(__bfloat162float(x[u].v[j]) * inv * __bfloat162float(w.v[j]));
+      for (int j = 0; j < 8; ++j)
+        y.v[j] = __float2bfloat16_rn(__bfloat162float(x[u].v[j]) * inv * __bfloat162float(w.v[j]));
+    }
+    if (valid && p.moe) store16(h + v * 8, y);
+    if (p.scale_ptrs != nullptr) {
+      // e4m3 with one scale per 128 columns: the 16 vectors of a group sit in one half-warp
+      float amax = 0.f;
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(y.v[j])));
       }
-      if (p.moe) store16(h + v * 8, y);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = fmaxf(amax, 1e-12f) / 448.f;
+      if (valid) {
+        const uint2 q = pack_e4m3x8(y, 1.f / sc);
+        for (int f = f_lo; f < f_hi; ++f) {
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(p.tok_ptrs[f]) + row * p.H + v * 8) = q;
+          if ((threadIdx.x & 15) == 0) reinterpret_cast<float*>(p.scale_ptrs[f])[row * (p.H / 128) + v / 16] = sc;
+        }
+      }
+    } else if (valid) {
       for (int f = f_lo; f < f_hi; ++f) store16(reinterpret_cast<bf16*>(p.tok_ptrs[f]) + row_off + v * 8, y);
     }
   }
@@ -374,9 +429,11 @@ __global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
     }
   }
   __syncthreads();
-  if (!s_ok || !p.moe) return;
+  const bool fp8 = p.tok_scale != nullptr;
+  if (!s_ok || (!p.moe && !fp8)) return;
   const bf16* tok = static_cast<const bf16*>(p.tok);
   bf16* x = static_cast<bf16*>(p.x);
+  bf16* home_x = static_cast<bf16*>(p.home_x);
   const int nv = p.H / 8;
   const int total = s_pre[p.A];
   const int slots = p.k + p.n_chunks;
@@ -385,6 +442,53 @@ __global__ void __launch_bounds__(kThreads) expand_kernel(ExpandParams p) {
     const int t = q - s_pre[a];
     const int pair = a * p.t_cap + t;
     const size_t base = (size_t)pair * p.k;
+    const bool home = a >= p.home_a0 && a < p.home_a0 + p.ratio;
+    if (fp8) {
+      // e4m3 rows: dequantise once into every target (expert segments, shared
+      // chunks, and the bf16 copy of home rows used by the dense / shared GEMMs).
+      int row = -1;
+      if (p.moe && lane < p.k) {
+        const int le = __ldcg(p.rid + base + lane) - p.e_offset;
+        if (le >= 0 && le < p.e_local) {
+          const int slot = atomicAdd(&p.counts[le], 1);
+          if (slot < p.cap) {
+            row = le * p.cap + slot;
+            p.meta[row] = (a << 24) | (t << 8) | lane;
+            p.rw[row] = __ldcg(p.rwt + base + lane);
+          } else {
+            atomicExch(p.status, kStatusBadIndex);
+          }
+        }
+      } else if (p.moe && lane >= p.k && lane < slots && home) {
+        row = p.shared_base + (lane - p.k) * p.shared_stride + (s_pre[a] - s_pre[p.home_a0]) + t;
+        p.meta[row] = (a << 24) | (t << 8) | lane;
+        p.rw[row] = 1.f;
+      }
+      if (lane < slots) s_row[warp][lane] = row;
+      const unsigned used = __ballot_sync(0xffffffffu, row >= 0);
+      __syncwarp();
+      bf16* hx = home && home_x ? home_x + ((size_t)(a - p.home_a0) * p.t_cap + t) * p.H : nullptr;
+      if (used || hx) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(p.tok) + (size_t)pair * p.H;
+        const float* sc = p.tok_scale + (size_t)pair * (p.H / 128);
+        for (int c = lane; c < p.H / 16; c += 32) {
+          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(src + c * 16));
+          Vec16<bf16> lo, hi;
+          unpack_e4m3x16(raw, __ldcg(sc + c / 8), lo, hi);
+          for (unsigned m = used; m; m &= m - 1) {
+            bf16* dst = x + (size_t)s_row[warp][__ffs(m) - 1] * p.H + c * 16;
+            store16(dst, lo);
+            store16(dst + 8, hi);
+          }
+          if (hx) {
+            store16(hx + c * 16, lo);
+            store16(hx + c * 16 + 8, hi);
+          }
+        }
+      }
+      __syncwarp();
+      continue;
+    }
     int row = -1;
     if (lane < p.k) {
       const int le = __ldcg(p.rid + base + lane) - p.e_offset;
@@ -458,7 +562,18 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
     const unsigned used = __ballot_sync(0xffffffffu, hit);
     if (!used) continue;
     bf16* dst = reinterpret_cast<bf16*>(p.dst_ptrs[a]) + ((size_t)t * p.num_ffn + p.f_rank) * p.H;
-    if (p.echo) {
+    if (p.echo && p.tok_scale != nullptr) {
+      // transport-only stand-in with e4m3 rows: dequantise and scale
+      const float wsum = warp_sum(w);
+      const uint8_t* src = static_cast<const uint8_t*>(p.staging) + (size_t)pair * p.H;
+      const float* sc = p.tok_scale + (size_t)pair * (p.H / 128);
+      for (int c = lane; c < p.H / 16; c += 32) {
+        Vec16<bf16> lo, hi;
+        unpack_e4m3x16(__ldcg(reinterpret_cast<const uint4*>(src + c * 16)), __ldcg(sc + c / 8) * wsum, lo, hi);
+        store16(dst + c * 16, lo);
+        store16(dst + c * 16 + 8, hi);
+      }
+    } else if (p.echo) {
       const float wsum = warp_sum(w);
       warp_sum_rows<true>(dst, static_cast<const bf16*>(p.staging) + (size_t)pair * p.H, 0, 1u, p.H, lane, wsum);
     } else {

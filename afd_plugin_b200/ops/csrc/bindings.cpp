@@ -345,7 +345,8 @@ void afd_wait(const at::Tensor& flag, int64_t index, const at::Tensor& epoch, in
 }
 
 // cfg (int64): [E, k, scoring, renorm, n_group, topk_group, moe, has_shared, num_ffn, e_local, t_cap,
-//               attn_rank, home_f, layer]; ptrs [5, F]: tok, rid, rwt, tcount, arrive flags on each FFN rank.
+//               attn_rank, home_f, layer]; ptrs [5, F]: tok, rid, rwt, tcount, arrive flags on each FFN rank
+//               ([6, F] adds the e4m3 rows' scale buffers: rows then travel as e4m3 with 1 x 128 scales).
 // done_ctr: int32 [>= 1 + ceil(T / 16)], zero before the first use and left zero by every call
 // ([0] send-kernel completion, [1:] router token tiles).
 // cfg[14] (optional) = prenorm: attn_out is already the FFN input; residual and norm_w are then unused.
@@ -359,7 +360,8 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
               "afd_dispatch: bf16 activations");
   TORCH_CHECK(attn_out.is_contiguous() && residual.is_contiguous() && gate_w.is_contiguous(), "afd_dispatch: layout");
   TORCH_CHECK(cfg.size() == 14 || cfg.size() == 15, "afd_dispatch: cfg has 14 or 15 entries");
-  TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.dim() == 2 && ptrs.size(0) == 5, "afd_dispatch: ptrs [5, F]");
+  TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.dim() == 2 && (ptrs.size(0) == 5 || ptrs.size(0) == 6),
+              "afd_dispatch: ptrs [5, F] (bf16 rows) or [6, F] (e4m3 rows + scales)");
   DispatchParams p{};
   p.attn_out = attn_out.data_ptr();
   p.residual = residual.data_ptr();
@@ -414,6 +416,10 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
   p.rwt_ptrs = pt + 2 * F;
   p.tcount_ptrs = pt + 3 * F;
   p.flag_ptrs = pt + 4 * F;
+  if (ptrs.size(0) == 6) {
+    TORCH_CHECK(p.H % 128 == 0, "afd_dispatch: e4m3 rows need H % 128 == 0");
+    p.scale_ptrs = pt + 5 * F;
+  }
   p.fmask = fmask.data_ptr<int32_t>();
   p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
   p.route_ctr = p.done_ctr + 1;
@@ -427,7 +433,8 @@ void afd_dispatch(const at::Tensor& attn_out, at::Tensor& residual, const at::Te
 void afd_expand(const at::Tensor& tok, const at::Tensor& rid, const at::Tensor& rwt, const at::Tensor& tcount,
                 at::Tensor& x, at::Tensor& meta, at::Tensor& rw, at::Tensor& counts, std::vector<int64_t> cfg,
                 const c10::optional<at::Tensor>& flag, int64_t flag_index, const c10::optional<at::Tensor>& epoch,
-                int64_t arrivals, int64_t timeout_ns) {
+                int64_t arrivals, int64_t timeout_ns, const c10::optional<at::Tensor>& tok_scale,
+                const c10::optional<at::Tensor>& home_x) {
   check_cuda(tok, "tok");
   TORCH_CHECK(cfg.size() == 9 || cfg.size() == 12, "afd_expand: cfg has 9 or 12 entries");
   ExpandParams p{};
@@ -463,6 +470,16 @@ void afd_expand(const at::Tensor& tok, const at::Tensor& rid, const at::Tensor& 
     p.arrivals = (uint64_t)arrivals;
     p.timeout_ns = timeout_ns;
   }
+  if (tok_scale.has_value() && tok_scale->defined()) {
+    TORCH_CHECK(tok.scalar_type() == at::kByte && tok_scale->scalar_type() == at::kFloat && p.H % 128 == 0,
+                "afd_expand: e4m3 rows are uint8 [A, t_cap, H] with fp32 scales [A, t_cap, H / 128]");
+    p.tok_scale = tok_scale->data_ptr<float>();
+    if (home_x.has_value() && home_x->defined()) {
+      TORCH_CHECK(home_x->scalar_type() == at::kBFloat16 && home_x->numel() >= (int64_t)p.ratio * p.t_cap * p.H,
+                  "afd_expand: home_x [ratio * t_cap, H] bf16");
+      p.home_x = home_x->data_ptr();
+    }
+  }
   p.status = status_ptr(tok);
   c10::cuda::CUDAGuard g(tok.device());
   launch_afd_expand(p, stream());
@@ -472,7 +489,8 @@ void afd_expand(const at::Tensor& tok, const at::Tensor& rid, const at::Tensor& 
 //       (, home_slots = J - k)]
 void afd_combine_send(const at::Tensor& staging, const at::Tensor& rid, const at::Tensor& rwt,
                       const at::Tensor& tcount, const at::Tensor& dst_ptrs, const at::Tensor& flag_ptrs,
-                      at::Tensor& done_ctr, int64_t H, std::vector<int64_t> cfg) {
+                      at::Tensor& done_ctr, int64_t H, std::vector<int64_t> cfg,
+                      const c10::optional<at::Tensor>& tok_scale) {
   check_cuda(staging, "staging");
   TORCH_CHECK(cfg.size() == 14 || cfg.size() == 15, "afd_combine_send: cfg has 14 or 15 entries");
   CombineSendParams p{};
@@ -496,6 +514,11 @@ void afd_combine_send(const at::Tensor& staging, const at::Tensor& rid, const at
   p.layer = (int)cfg[12];
   p.echo = (int)cfg[13];
   p.home_slots = cfg.size() == 15 ? (int)cfg[14] : p.J - p.k;
+  if (tok_scale.has_value() && tok_scale->defined()) {
+    TORCH_CHECK(p.echo && staging.scalar_type() == at::kByte && H % 128 == 0,
+                "afd_combine_send: e4m3 staging rows are an echo-mode stand-in only");
+    p.tok_scale = tok_scale->data_ptr<float>();
+  }
   TORCH_CHECK(p.home_slots >= 0 && p.k + p.home_slots <= p.J, "afd_combine_send: home slots exceed J");
   TORCH_CHECK(p.A <= 64 && p.k <= 16 && p.J <= 32 && p.J >= p.k, "afd_combine_send: at most 64 sources, k <= J <= 32");
   p.dst_ptrs = dst_ptrs.data_ptr<int64_t>();
@@ -530,14 +553,18 @@ at::Tensor afd_combine(const at::Tensor& comb, const at::Tensor& fmask, int64_t 
 
 // Grouped GEMM whose epilogue scatters rows into peer combine buffers.
 // sp_ptrs (int64 [4]): meta, rw, dst_ptr_table, flag_ptr_table; sp_cfg: [J, H, total_ctas, num_dst, layer, n_reset]
+void check_w8(const at::Tensor& w, const at::Tensor& scale, int64_t N, int64_t K, const char* who);
+
 void grouped_gemm_scatter(const at::Tensor& a, const at::Tensor& w, const at::Tensor& offsets, const at::Tensor& counts,
                           int64_t w_experts, const at::Tensor& meta, const at::Tensor& rw, const at::Tensor& dst_ptrs,
                           const at::Tensor& flag_ptrs, at::Tensor& done_ctr, at::Tensor& counts_reset,
-                          std::vector<int64_t> cfg) {
+                          std::vector<int64_t> cfg, const c10::optional<at::Tensor>& w_scale) {
   check_cuda(a, "a");
   TORCH_CHECK(cfg.size() == 5, "grouped_gemm_scatter: cfg [J, H, total_ctas, num_dst, layer]");
   const int64_t R = a.size(0), K = a.size(1), N = w.size(1);
   TORCH_CHECK(N % 128 == 0 && K % 64 == 0 && w.size(2) == K, "grouped_gemm_scatter: shapes");
+  const bool w8 = w_scale.has_value() && w_scale->defined();
+  if (w8) check_w8(w, *w_scale, N, K, "grouped_gemm_scatter");
   ScatterParams sp{};
   sp.meta = meta.data_ptr<int32_t>();
   sp.rw = rw.data_ptr<float>();
@@ -552,8 +579,45 @@ void grouped_gemm_scatter(const at::Tensor& a, const at::Tensor& w, const at::Te
   sp.counts_reset = counts_reset.data_ptr<int32_t>();
   sp.n_reset = (int)counts_reset.numel();
   c10::cuda::CUDAGuard g(a.device());
+  if (w8) {
+    launch_grouped_gemm_w8(nullptr, a.data_ptr(), w.data_ptr(), w_scale->data_ptr<float>(), offsets.data_ptr<int32_t>(),
+                           counts.data_ptr<int32_t>(), (int)counts.numel(), (int)R, (int)N, (int)K, 2, status_ptr(a),
+                           stream(), (int)w_experts, &sp);
+    return;
+  }
   launch_grouped_gemm(nullptr, a.data_ptr(), w.data_ptr(), offsets.data_ptr<int32_t>(), counts.data_ptr<int32_t>(),
                       (int)counts.numel(), (int)R, (int)N, (int)K, 2, status_ptr(a), stream(), (int)w_experts, &sp);
+}
+
+// fp8 weights w [E, N, K] (float8_e4m3fn), block scales [E, ceil(N / 128), K / 128] fp32.
+void check_w8(const at::Tensor& w, const at::Tensor& scale, int64_t N, int64_t K, const char* who) {
+  TORCH_CHECK(w.scalar_type() == at::kFloat8_e4m3fn && w.is_contiguous(), who, ": fp8 e4m3 weights, contiguous");
+  TORCH_CHECK(K % 128 == 0, who, ": K must be a multiple of 128 for fp8 weights");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.is_contiguous() && scale.dim() == 3 &&
+                  scale.size(0) == w.size(0) && scale.size(1) == (N + 127) / 128 && scale.size(2) == K / 128,
+              who, ": block scales [E, ceil(N/128), K/128] fp32");
+}
+
+// D = A x W^T per expert segment with fp8 block-scaled weights; epilogue 0 plain, 1 SwiGLU.
+at::Tensor grouped_gemm_w8(const at::Tensor& a, const at::Tensor& w, const at::Tensor& w_scale,
+                           const at::Tensor& offsets, const at::Tensor& counts, int64_t epilogue, int64_t w_experts) {
+  check_cuda(a, "a");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && a.is_contiguous(), "grouped_gemm_w8: bf16 activations, contiguous");
+  const int64_t R = a.size(0), K = a.size(1), N = w.size(-2);
+  TORCH_CHECK(w.dim() == 3 && w.size(-1) == K, "grouped_gemm_w8: w [E, N, K]");
+  check_w8(w, w_scale, N, K, "grouped_gemm_w8");
+  if (epilogue == 1) {
+    TORCH_CHECK(N % 2 == 0 && (N / 2) % 128 == 0, "grouped_gemm_w8: SwiGLU needs I % 128 == 0 (scale blocks)");
+  } else {
+    TORCH_CHECK(N % 128 == 0, "grouped_gemm_w8: N must be a multiple of 128");
+  }
+  const int64_t n_out = epilogue == 1 ? N / 2 : N;
+  auto d = at::empty({R, n_out}, a.options());
+  c10::cuda::CUDAGuard g(a.device());
+  launch_grouped_gemm_w8(d.data_ptr(), a.data_ptr(), w.data_ptr(), w_scale.data_ptr<float>(), offsets.data_ptr<int32_t>(),
+                         counts.data_ptr<int32_t>(), (int)counts.numel(), (int)R, (int)N, (int)K, (int)epilogue,
+                         status_ptr(a), stream(), (int)w_experts, nullptr);
+  return d;
 }
 
 at::Tensor grouped_gemm_ex(const at::Tensor& a, const at::Tensor& w, const at::Tensor& offsets,
@@ -686,13 +750,16 @@ TORCH_LIBRARY(afd_b200, m) {
         "Tensor? input_ids=None) -> ()");
   m.def("afd_expand(Tensor tok, Tensor rid, Tensor rwt, Tensor tcount, Tensor(a!) x, Tensor(b!) meta, Tensor(c!) rw, "
         "Tensor(d!) counts, int[] cfg, Tensor? flag=None, int flag_index=0, Tensor? epoch=None, int arrivals=0, "
-        "int timeout_ns=0) -> ()");
+        "int timeout_ns=0, Tensor? tok_scale=None, Tensor? home_x=None) -> ()");
   m.def("afd_combine_send(Tensor staging, Tensor rid, Tensor rwt, Tensor tcount, Tensor dst_ptrs, Tensor flag_ptrs, "
-        "Tensor(a!) done_ctr, int H, int[] cfg) -> ()");
+        "Tensor(a!) done_ctr, int H, int[] cfg, Tensor? tok_scale=None) -> ()");
   m.def("afd_combine(Tensor comb, Tensor fmask, int T, Tensor flags, int layer, Tensor epoch, int arrivals, "
         "int timeout_ns) -> Tensor");
   m.def("grouped_gemm_scatter(Tensor a, Tensor w, Tensor offsets, Tensor counts, int w_experts, Tensor meta, Tensor rw, "
-        "Tensor dst_ptrs, Tensor flag_ptrs, Tensor(a!) done_ctr, Tensor(b!) counts_reset, int[] cfg) -> ()");
+        "Tensor dst_ptrs, Tensor flag_ptrs, Tensor(a!) done_ctr, Tensor(b!) counts_reset, int[] cfg, "
+        "Tensor? w_scale=None) -> ()");
+  m.def("grouped_gemm_w8(Tensor a, Tensor w, Tensor w_scale, Tensor offsets, Tensor counts, int epilogue, "
+        "int w_experts) -> Tensor");
   m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
   m.def("grouped_gemm_grid(int n_items) -> int");
   m.def("read_status(int device) -> int");
@@ -723,6 +790,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("afd_combine", &afd_combine);
   m.impl("grouped_gemm_scatter", &grouped_gemm_scatter);
   m.impl("grouped_gemm_ex", &grouped_gemm_ex);
+  m.impl("grouped_gemm_w8", &grouped_gemm_w8);
   m.impl("afd_expand", &afd_expand);
   m.impl("afd_combine_send", &afd_combine_send);
 }

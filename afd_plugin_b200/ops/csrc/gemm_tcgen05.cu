@@ -22,6 +22,8 @@
 
 #include <type_traits>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 #include "launchers.h"
 
@@ -341,6 +343,313 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   }
 }
 
+// ===================================================================== fp8 weights
+// Block-scaled fp8 (e4m3) weights with bf16 activations ("W8A16"): TMA streams
+// 128-row x 128-K fp8 weight tiles (half the HBM bytes of bf16), four
+// converter warps dequantise each tile with its 128 x 128 block scale into two
+// 128B-swizzled bf16 tiles in shared memory, and the tcgen05 MMA reads those.
+// Warp roles: 0 TMA producer, 1 TMEM + MMA issuer, 2-5 epilogue, 6-9 converter.
+namespace gg8 {
+
+constexpr int kBK = 128;                       // K per stage (one fp8 row = 128 B)
+constexpr int kBM = 128;
+constexpr int kSub = 64;
+constexpr int kMaxSub = 2;                     // tokens per pass <= 128
+constexpr int kStages = 3;
+constexpr int kCvt = 2;
+constexpr int kThreads = 10 * 32;
+constexpr int kWBytes = kBM * kBK;             // 16 KB fp8
+constexpr int kWcHalf = kBM * 64 * 2;          // 16 KB: 128 rows x 64 K bf16
+constexpr int kSubBytes = kSub * 64 * 2;       // 8 KB: 64 tokens x 64 K bf16
+constexpr int kAHalf = kMaxSub * kSubBytes;    // 16 KB: one K half of the A stage
+constexpr uint32_t kAccCols = 128;
+constexpr uint32_t kTmemCols = 256;
+
+struct Smem {
+  alignas(1024) uint8_t w[kStages][kWBytes];
+  alignas(1024) uint8_t a[kStages][2 * kAHalf];
+  alignas(1024) uint8_t wc[kCvt][2 * kWcHalf];
+  float xchg[32 * 64];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t cfull[kCvt];
+  uint64_t cempty[kCvt];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+AFD_DEVICE uint4 cvt16(uint4 raw, float scale, uint4& hi) {
+  // 16 e4m3 values -> 16 bf16 (scaled); returns the first 8, `hi` the last 8.
+  const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t out[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((in[i] >> (16 * h)) & 0xFFFFu);
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+      __half2 h2;
+      *reinterpret_cast<__half2_raw*>(&h2) = hr;
+      const float2 f = __half22float2(h2);
+      out[i * 2 + h] = pack_bf16(f.x * scale, f.y * scale);
+    }
+  }
+  hi = make_uint4(out[4], out[5], out[6], out[7]);
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
+    const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap a_map,
+    const float* __restrict__ w_scale, __nv_bfloat16* __restrict__ d, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ counts, int n_w, int w_stride_rows, int k_dim, int ld_d, int n_tiles, int n_experts,
+    int w_experts, int* __restrict__ status, const ScatterParams sp) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int kb_total = k_dim / kBK;
+  const int n_items = n_tiles * n_experts;
+  constexpr int kPassRows = kMaxSub * kSub;
+  const int nblk_n = (n_w + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int c = 0; c < kCvt; ++c) {
+      mbar_init(&sm.cfull[c], 128);
+      mbar_init(&sm.cempty[c], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  gg::tc_fence_before();
+  __syncthreads();
+  gg::tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // rows of the 128-row weight tile: [r0, r0 + 64) and [r1, r1 + 64)
+  auto w_rows = [&](const gg::Item& it, int& r0, int& r1) {
+    if (EPI == 1) {
+      r0 = it.nt * 64;
+      r1 = n_w / 2 + it.nt * 64;
+    } else {
+      r0 = it.nt * kBM;
+      r1 = r0 + 64;
+    }
+  };
+
+  if (warp == 0) {
+    // ----------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tensormap(&w_map);
+      prefetch_tensormap(&a_map);
+      int it_count = 0, idx = blockIdx.x;
+      gg::Item it;
+      bool ok = true;
+      while (ok && gg::next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+        int r0, r1;
+        w_rows(it, r0, r1);
+        const int wb = it.e * w_stride_rows;
+        const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+        for (int p = 0; p < n_pass && ok; ++p) {
+          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
+            const int st = it_count % kStages;
+            if (!mbar_wait_bounded(&sm.empty[st], ((it_count / kStages) & 1) ^ 1)) {
+              atomicExch(status, kStatusWaitTimeout);
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&sm.full[st], kWBytes + 2 * n_sub * kSubBytes);
+            tma_load_2d(sm.w[st], &w_map, &sm.full[st], kb * kBK, wb + r0);
+            tma_load_2d(sm.w[st] + kWBytes / 2, &w_map, &sm.full[st], kb * kBK, wb + r1);
+            for (int h = 0; h < 2; ++h)
+              for (int s2 = 0; s2 < n_sub; ++s2)
+                tma_load_2d(sm.a[st] + h * kAHalf + s2 * kSubBytes, &a_map, &sm.full[st], kb * kBK + h * 64,
+                            it.seg + p * kPassRows + s2 * kSub);
+          }
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------- converter
+    const int ct = threadIdx.x - 6 * 32;  // 0..127
+    int it_count = 0, idx = blockIdx.x;
+    gg::Item it;
+    bool ok = true;
+    while (ok && gg::next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+      int r0, r1;
+      w_rows(it, r0, r1);
+      const int ew = w_experts == 1 ? 0 : it.e;
+      const float* sc_lo = w_scale + ((size_t)ew * nblk_n + r0 / 128) * kb_total;
+      const float* sc_hi = w_scale + ((size_t)ew * nblk_n + r1 / 128) * kb_total;
+      const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+      for (int p = 0; p < n_pass && ok; ++p) {
+        for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
+          const int st = it_count % kStages;
+          const int cs = it_count % kCvt;
+          if (!mbar_wait_bounded(&sm.full[st], (it_count / kStages) & 1) ||
+              !mbar_wait_bounded(&sm.cempty[cs], ((it_count / kCvt) & 1) ^ 1)) {
+            atomicExch(status, kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+          const float s_lo = sc_lo[kb], s_hi = sc_hi[kb];
+          const uint8_t* src = sm.w[st];
+          uint8_t* dst = sm.wc[cs];
+#pragma unroll 2
+          for (int q = ct; q < kBM * 8; q += 128) {
+            const int r = q >> 3, c = q & 7;
+            const uint4 raw = *reinterpret_cast<const uint4*>(src + r * 128 + ((c ^ (r & 7)) << 4));
+            uint4 hi;
+            const uint4 lo = cvt16(raw, r < 64 ? s_lo : s_hi, hi);
+            uint8_t* tile = dst + (c >> 2) * kWcHalf + r * 128;
+            const int d0 = (c & 3) * 2;
+            *reinterpret_cast<uint4*>(tile + ((d0 ^ (r & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(tile + (((d0 + 1) ^ (r & 7)) << 4)) = hi;
+          }
+          fence_proxy_async();
+          mbar_arrive(&sm.cfull[cs]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int it_count = 0, acc_count = 0, idx = blockIdx.x;
+      gg::Item it;
+      bool ok = true;
+      while (ok && gg::next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+        const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+        for (int p = 0; p < n_pass && ok; ++p, ++acc_count) {
+          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          const uint32_t idesc = gg::make_idesc(kBM, n_sub * kSub);
+          const int ab = acc_count & 1;
+          if (!mbar_wait_bounded(&sm.acc_empty[ab], ((acc_count >> 1) & 1) ^ 1)) {
+            atomicExch(status, kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+          gg::tc_fence_after();
+          const uint32_t tacc = tmem + ab * kAccCols;
+          for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
+            const int st = it_count % kStages;
+            const int cs = it_count % kCvt;
+            if (!mbar_wait_bounded(&sm.full[st], (it_count / kStages) & 1) ||
+                !mbar_wait_bounded(&sm.cfull[cs], (it_count / kCvt) & 1)) {
+              atomicExch(status, kStatusWaitTimeout);
+              ok = false;
+              break;
+            }
+            gg::tc_fence_after();
+            const uint32_t wa = smem_u32(sm.wc[cs]);
+            const uint32_t aa = smem_u32(sm.a[st]);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const int h = kk >> 2;
+              gg::umma(tacc, gg::make_desc(wa + h * kWcHalf + (kk & 3) * 32),
+                       gg::make_desc(aa + h * kAHalf + (kk & 3) * 32), idesc, (kb | kk) != 0);
+            }
+            gg::umma_commit(&sm.empty[st]);
+            gg::umma_commit(&sm.cempty[cs]);
+          }
+          if (ok) gg::umma_commit(&sm.acc_full[ab]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int acc_count = 0, idx = blockIdx.x;
+    gg::Item it;
+    bool ok = true;
+    while (ok && gg::next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+      const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+      for (int p = 0; p < n_pass; ++p, ++acc_count) {
+        const int ab = acc_count & 1;
+        if (!mbar_wait_bounded(&sm.acc_full[ab], (acc_count >> 1) & 1)) {
+          atomicExch(status, kStatusWaitTimeout);
+          ok = false;
+          break;
+        }
+        gg::tc_fence_after();
+        const int n_cols = min(kPassRows, it.cnt - p * kPassRows);
+        const int r_base = it.seg + p * kPassRows;
+        const uint32_t tacc = tmem + ab * kAccCols + ((uint32_t)(quarter * 32) << 16);
+        for (int c0 = 0; c0 < n_cols; c0 += 32) {
+          float v[32];
+          gg::tmem_ld32(tacc + c0, v);
+          if (EPI == 0) {
+            const int col = it.nt * kBM + row;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (c0 + j < n_cols) d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(v[j]);
+          } else if (EPI == 2) {
+            const int col = it.nt * kBM + row;
+#pragma unroll 4
+            for (int j = 0; j < 32; ++j) {
+              if (c0 + j < n_cols) {
+                const int r = r_base + c0 + j;
+                const int m = sp.meta[r];
+                const int src = (m >> 24) & 0xFF, tok = (m >> 8) & 0xFFFF, slot = m & 0xFF;
+                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sp.dst_ptrs[src]);
+                dst[((size_t)tok * sp.J + slot) * sp.H + col] = __float2bfloat16_rn(sp.rw[r] * v[j]);
+              }
+            }
+          } else {
+            if (quarter >= 2) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sm.xchg[j * 64 + (row - 64)] = v[j];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (quarter < 2) {
+              const int col = it.nt * 64 + row;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (c0 + j < n_cols) {
+                  const float g = v[j];
+                  const float u = sm.xchg[j * 64 + row];
+                  d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
+                }
+              }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+          }
+        }
+        gg::tc_fence_before();
+        if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
+      }
+    }
+    if (EPI == 2) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0) gg::scatter_arrive(sp);
+    }
+  }
+  gg::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    gg::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+}  // namespace gg8
+
 static void encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols * 2};
@@ -394,5 +703,46 @@ void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* e
     go(std::integral_constant<int, 2>{}, n / gg::kBM, n);
   } else {
     go(std::integral_constant<int, 0>{}, n / gg::kBM, n);
+  }
+}
+
+
+void launch_grouped_gemm_w8(void* d, const void* a, const void* w, const float* w_scale, const int32_t* expert_offsets,
+                            const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
+                            int* status, cudaStream_t s, int w_experts, const ScatterParams* sp) {
+  if (w_experts < 0) w_experts = e_local;
+  CUtensorMap wmap, amap;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)w_experts * n};
+    const cuuint64_t strides[1] = {(cuuint64_t)k};
+    const cuuint32_t box[2] = {gg::gg8::kBK, 64};
+    const cuuint32_t estr[2] = {1, 1};
+    get_tensor_map_encoder()(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  gg::encode_2d(&amap, a, rows_cap, k, gg::gg8::kSub);
+  const int smem = (int)sizeof(gg::gg8::Smem) + 1024;
+  const int w_stride = (w_experts == 1) ? 0 : n;
+  ScatterParams none{};
+  const ScatterParams& spv = sp ? *sp : none;
+  auto go = [&](auto epi_tag, int n_tiles, int ld) {
+    constexpr int EPI = decltype(epi_tag)::value;
+    static bool set = false;
+    if (!set) {
+      cudaFuncSetAttribute(gg::gg8::grouped_gemm_w8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      set = true;
+    }
+    const int grid = grouped_gemm_grid(n_tiles * e_local);
+    launch_pdl(gg::gg8::grouped_gemm_w8_kernel<EPI>, dim3(grid), dim3(gg::gg8::kThreads), (size_t)smem, s, wmap, amap, w_scale,
+               (__nv_bfloat16*)d, expert_offsets, expert_counts, n, w_stride, k, ld, n_tiles, e_local, w_experts,
+               status, spv);
+  };
+  if (epilogue == 1) {
+    go(std::integral_constant<int, 1>{}, (n / 2) / 64, n / 2);
+  } else if (epilogue == 2) {
+    go(std::integral_constant<int, 2>{}, n / gg::gg8::kBM, n);
+  } else {
+    go(std::integral_constant<int, 0>{}, n / gg::gg8::kBM, n);
   }
 }

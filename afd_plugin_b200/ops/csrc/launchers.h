@@ -91,6 +91,7 @@ struct DispatchParams {
   const int64_t* rwt_ptrs;     // [F] fp32 [A, t_cap, k] routing weights
   const int64_t* tcount_ptrs;  // [F] int32 [A] tokens per source
   const int64_t* flag_ptrs;    // [F] uint64 arrival counters [layers]
+  const int64_t* scale_ptrs;   // [F] fp32 [A, t_cap, H / 128] row scales (e4m3 rows) or null (bf16 rows)
   int32_t* fmask;              // local [t_cap]: FFN ranks that answer token t
   unsigned* done_ctr;          // local CTA-completion counter of the send kernel
   unsigned* route_ctr;         // local [ceil(T / 16)] router completion counters (zero between uses)
@@ -110,6 +111,8 @@ struct ExpandParams {
   void* x;                // [e_local * cap, H] expert segments
   int32_t* meta;          // [e_local * cap] (src << 24 | token << 8 | slot)
   float* rw;              // [e_local * cap]
+  const float* tok_scale; // [A, t_cap, H / 128] when the rows arrive as e4m3 (tok is then bytes), else null
+  void* home_x;           // [ratio * t_cap, H] bf16 copies of the home sources' rows (e4m3 rows only)
   int32_t* counts;        // [e_local + n_chunks] (or [e_local + ratio] without shared chunks)
   int A, t_cap, k, H, e_local, e_offset, cap, ratio, home_a0, moe;
   // Shared experts as virtual experts: chunk c's rows are every home source's
@@ -131,6 +134,7 @@ struct CombineSendParams {
   const int32_t* tcount;  // [A]
   int A, t_cap, k, J, H, e_local, e_offset, ratio, home_a0, moe, has_shared, f_rank, num_ffn, layer;
   int echo;               // 1: transport-only stand-in (scale the token row by its local weights)
+  const float* tok_scale; // echo with e4m3 rows: [A, t_cap, H / 128] scales (staging holds the e4m3 rows)
   int home_slots;         // shared-expert slots k .. k + home_slots - 1 filled for home sources
   const int64_t* dst_ptrs;   // [A] combine buffers [t_cap, F, H] (stage base)
   const int64_t* flag_ptrs;  // [A] combine counters [layers]
@@ -177,6 +181,12 @@ struct ScatterParams {
 // epilogue: 0 = store bf16, 1 = SiLU(gate) * up over paired halves (N = 2I -> I).
 // CTAs of a persistent grouped-GEMM launch over n_items (expert, tile) items.
 int grouped_gemm_grid(int n_items);
+// Same with block-scaled fp8 (e4m3) weights: w [E, N, K] bytes, w_scale
+// [E, ceil(N / 128), K / 128] fp32 (128 x 128 blocks); bf16 activations.
+// K % 128 == 0; epilogue 1 needs I % 64 == 0 and epilogue 0 / 2 N % 128 == 0.
+void launch_grouped_gemm_w8(void* d, const void* a, const void* w, const float* w_scale, const int32_t* expert_offsets,
+                            const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
+                            int* status, cudaStream_t s, int w_experts, const ScatterParams* sp);
 // w_expert_rows: rows between consecutive experts in W (0 = one weight set
 // shared by every segment, e.g. shared experts / dense MLP over per-source segments).
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,

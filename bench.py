@@ -37,7 +37,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode output tok/s (8xB200, max over ranks) + p50 TPOT, AFD vs NCCL connector"
 BASELINE_VALUE = None  # BASELINE.md publishes no GPU number for this metric
-TOPOLOGY = {1: (0, 0), 2: (1, 1), 4: (3, 1), 8: (6, 2)}
+TOPOLOGY = {1: (0, 0), 2: (1, 1), 4: (2, 2), 8: (6, 2)}  # 4 GPUs: 2A2F halves each FFN rank's expert weights
 MODEL_DESC = {
     "deepseek-v2-lite": "DeepSeek-V2-Lite (27 layers, 64 experts top-6, MLA 16 heads)",
     "qwen3-30b-a3b": "Qwen3-30B-A3B (48 layers, 128 experts top-8, GQA 32q/4kv)",

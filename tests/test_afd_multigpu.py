@@ -94,3 +94,14 @@ def test_fused_connector_dsv4_1a1f():
     outs = _run(afd, prompts, 6, preset="tiny-dsv4", enforce_eager=False, capture_sizes=[4])
     assert [o[0] for o in outs] == [o[0] for o in ref]
     assert _agreement(outs, ref) >= 0.75
+
+
+def test_fused_connector_fp8_rows_1a1f():
+    """e4m3 rows (1 x 128 scales) across NVLink: held to near-agreement with the bf16 colocated model."""
+    _need(2)
+    prompts = _prompts(4, 16)
+    ref = _colocated(prompts, 6)
+    afd = {"num_attention_ranks": 1, "num_ffn_ranks": 1, "connector": "B200FusedAFDConnector",
+           "connector_extra_config": {"max_tokens_per_rank": 128, "wait_timeout_ms": 20000, "fp8_dispatch": True}}
+    outs = _run(afd, prompts, 6, enforce_eager=False, capture_sizes=[4])
+    assert _agreement(outs, ref) >= 0.5

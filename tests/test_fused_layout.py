@@ -23,5 +23,14 @@ def test_extra_config_strict():
         B200FusedExtraInfo.from_mapping({"bogus": 1})
     with pytest.raises(ValueError):
         B200FusedExtraInfo.from_mapping({"wait_timeout_ms": 0})
-    with pytest.raises(ValueError):
-        B200FusedExtraInfo.from_mapping({"fp8_dispatch": True})
+    assert B200FusedExtraInfo.from_mapping({"fp8_dispatch": True}).fp8_dispatch
+    with pytest.raises(TypeError):
+        B200FusedExtraInfo.from_mapping({"fp8_dispatch": "maybe"})
+
+
+def test_fp8_rows_halve_token_buffer():
+    bf = FusedLayout(num_attn=6, num_ffn=2, stages=1, layers=27, hidden=2048, experts=64, top_k=6, t_cap=43)
+    f8 = FusedLayout(num_attn=6, num_ffn=2, stages=1, layers=27, hidden=2048, experts=64, top_k=6, t_cap=43, fp8=True)
+    lb, l8 = bf.heap_layout(), f8.heap_layout()
+    assert l8["tok"].nbytes * 2 == lb["tok"].nbytes
+    assert l8["tok_scale"].nbytes == 6 * 43 * 16 * 4 and "tok_scale" not in lb.regions

@@ -196,3 +196,46 @@ def test_dispatch_prenormed_hash_routed():
     assert torch.equal(lb.rid[0][0, :T].cpu(), id_ref.cpu())
     torch.testing.assert_close(lb.rwt[1][0, :T], w_ref, atol=1e-3, rtol=1e-3)
     assert int(lb.dctr.abs().sum()) == 0 and [int(a[0]) for a in lb.arrive] == [1, 1]
+
+
+def test_dispatch_fp8_rows_then_expand():
+    """Rows travel as e4m3 with one scale per 128 columns; expand dequantises into bf16 segments and home rows."""
+    torch.manual_seed(21)
+    C = _ext.ops()
+    F, H, E, k, t_cap, T = 2, 512, 16, 4, 64, 23
+    lb = _Loopback(F, t_cap, H, E, k)
+    lb.tok = [torch.zeros(1, t_cap, H, dtype=torch.uint8, device=DEV) for _ in range(F)]
+    lb.scales = [torch.zeros(1, t_cap, H // 128, dtype=torch.float32, device=DEV) for _ in range(F)]
+    rows = [[t.data_ptr() for t in grp] for grp in (lb.tok, lb.rid, lb.rwt, lb.tcount, lb.arrive, lb.scales)]
+    ptrs = torch.tensor(rows, dtype=torch.int64, device=DEV)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    res0 = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    norm_w = torch.ones(H, device=DEV, dtype=torch.bfloat16)
+    gate = (torch.randn(E, H, device=DEV) / H**0.5).to(torch.bfloat16)
+    res = res0.clone()
+    cfg = [E, k, 0, 1, 1, 1, 1, 1, F, E // F, t_cap, 0, 0, 0]
+    C.afd_dispatch(x, res, norm_w, 1e-6, gate, None, 1.0, ptrs, lb.fmask, lb.dctr, cfg)
+    torch.cuda.synchronize()
+    _, h_ref = _ref_norm(x, res0, norm_w, 1e-6)
+    for f in range(F):
+        q = lb.tok[f][0, :T].view(torch.float8_e4m3fn).float().view(T, H // 128, 128)
+        deq = (q * lb.scales[f][0, :T, :, None]).view(T, H)
+        torch.testing.assert_close(deq, h_ref.float(), atol=0.08, rtol=0.07)
+    # FFN rank 0 (home of source 0): dequantise into expert segments and the home copy
+    e_local, cap = E // F, t_cap
+    xs = torch.zeros(e_local * cap, H, dtype=torch.bfloat16, device=DEV)
+    meta = torch.full((e_local * cap,), -1, dtype=torch.int32, device=DEV)
+    rw = torch.zeros(e_local * cap, dtype=torch.float32, device=DEV)
+    counts = torch.zeros(e_local + 1, dtype=torch.int32, device=DEV)
+    home_x = torch.zeros(t_cap, H, dtype=torch.bfloat16, device=DEV)
+    C.afd_expand(lb.tok[0], lb.rid[0], lb.rwt[0], lb.tcount[0], xs, meta, rw, counts,
+                 [1, t_cap, k, e_local, 0, cap, 1, 0, 1], tok_scale=lb.scales[0], home_x=home_x)
+    torch.cuda.synchronize()
+    q = lb.tok[0][0, :T].view(torch.float8_e4m3fn).float().view(T, H // 128, 128)
+    deq = (q * lb.scales[0][0, :T, :, None]).view(T, H)
+    torch.testing.assert_close(home_x[:T].float(), deq, atol=1e-2, rtol=1e-2)
+    for le in range(e_local):
+        n = int(counts[le])
+        m = meta[le * cap : le * cap + n].long()
+        tt = (m >> 8) & 0xFFFF
+        torch.testing.assert_close(xs[le * cap : le * cap + n].float(), deq[tt], atol=1e-2, rtol=1e-2)

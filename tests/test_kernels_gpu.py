@@ -178,3 +178,52 @@ def test_moe_expert_parallel_slice():
     full = ref.moe_experts(x.float(), w13.float(), w2.float(), tw, tid)
     part = sum(ops.moe_experts(x, w13[o:o + 8], w2[o:o + 8], tw, tid, expert_offset=o).float() for o in (0, 8))
     _close(part, full, 3e-2, 3e-2)
+
+
+def _quant_experts(w):
+    qs, ss = zip(*(ref.quant_fp8_block_weight(w[e].float()) for e in range(w.shape[0])))
+    q, s = torch.stack(qs), torch.stack(ss)
+    deq = torch.stack([ref.dequant_block(q[e], s[e]) for e in range(w.shape[0])])
+    return q, s.contiguous(), deq
+
+
+@pytest.mark.parametrize("counts_list", [[3, 0, 130, 64], [1, 1, 1, 1, 1, 1, 1, 1], [200]])
+@pytest.mark.parametrize("epilogue", [0, 1])
+def test_grouped_gemm_w8_matches_dequantised_reference(counts_list, epilogue):
+    """fp8 block-scaled weights (tiles dequantised in shared memory) vs fp32 math on the dequantised weights."""
+    torch.manual_seed(len(counts_list) * 10 + epilogue)
+    C = _ext.ops()
+    E, K, N = len(counts_list), 512, 384 if epilogue == 0 else 512
+    counts = torch.tensor(counts_list, dtype=torch.int32, device=DEV)
+    offsets = torch.zeros(E, dtype=torch.int32, device=DEV)
+    offsets[1:] = counts.cumsum(0)[:-1]
+    R = int(counts.sum())
+    a = (torch.randn(R + 5, K, device=DEV) * 0.5).to(torch.bfloat16)
+    w = torch.randn(E, N, K, device=DEV) * 0.05
+    q, s, deq = _quant_experts(w)
+    out = C.grouped_gemm_w8(a, q, s, offsets, counts, epilogue, E)
+    torch.cuda.synchronize()
+    for e in range(E):
+        o, c = int(offsets[e]), int(counts[e])
+        if c == 0:
+            continue
+        y = a[o : o + c].float() @ deq[e].t()
+        if epilogue == 1:
+            g, u = y[:, : N // 2], y[:, N // 2 :]
+            y = g * torch.sigmoid(g) * u
+        got = out[o : o + c].float()
+        sc = y.abs().max().item() + 1e-6
+        _close(got / sc, y / sc, 2e-2)
+
+
+def test_moe_experts_fp8_weights():
+    T, k, E, H, I = 96, 6, 16, 512, 256
+    torch.manual_seed(5)
+    x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
+    q13, s13, d13 = _quant_experts(torch.randn(E, 2 * I, H, device=DEV) * 0.05)
+    q2, s2, d2 = _quant_experts(torch.randn(E, H, I, device=DEV) * 0.05)
+    tw, tid = ref.topk_route(torch.randn(T, E, device=DEV), k, renormalize=True)
+    out = ops.moe_experts(x, q13, q2, tw, tid, w13_scale=s13, w2_scale=s2)
+    expect = ref.moe_experts(x.float(), d13, d2, tw, tid)
+    scale = expect.abs().max().item()
+    _close(out / scale, expect / scale, 2e-2)
