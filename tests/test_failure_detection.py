@@ -62,14 +62,18 @@ def _hb_rank(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=20))
+    # start together (process start-up times differ by seconds under load)
+    store.add("ready", 1)
+    while int(store.add("ready", 0)) < world:
+        time.sleep(0.01)
     wd = HeartbeatWatchdog(store, rank, world, period_s=0.05, timeout_s=0.5).start()
     if rank == 1:
         time.sleep(0.3)
         wd.stop()  # rank 1 "dies": stops beating but keeps the process alive for the store
-        time.sleep(2.0)
+        time.sleep(3.0)
         q.put((rank, []))
         return
-    time.sleep(1.5)
+    time.sleep(2.0)
     dead = sorted(wd.dead_peers())
     wd.stop()
     q.put((rank, dead))
