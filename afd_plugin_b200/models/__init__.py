@@ -60,8 +60,11 @@ def build_model(
     max_positions: int | None = None,
     route_on_attention: bool = False,
     init_on: str | None = None,
+    tp=None,
 ) -> AFDCausalLM:
+    """``tp`` (:class:`afd_plugin_b200.models.layers.TPInfo`) shards the attention heads."""
     cls = model_class_for(arch)
+    kw = {} if tp is None else {"tp": tp}
     model = cls(
         arch,
         role=role,
@@ -72,6 +75,7 @@ def build_model(
         ep_size=ep_size,
         max_positions=max_positions,
         route_on_attention=route_on_attention,
+        **kw,
     )
     if checkpoint is None:
         model.init_random(seed, generate_on=init_on)

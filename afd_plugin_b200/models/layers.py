@@ -60,6 +60,33 @@ class AttentionMetadata:
         return int(self.positions.shape[0])
 
 
+@dataclass(frozen=True)
+class TPInfo:
+    """Attention tensor parallelism: this rank's share of the heads.
+
+    Heads are split evenly over ``size`` ranks; the output projection is
+    row-parallel, so each rank's partial output is summed over ``group``.
+    """
+
+    rank: int = 0
+    size: int = 1
+    group: object | None = None
+
+    def shard(self, n: int, what: str) -> tuple[int, int]:
+        """(first index, count) of this rank's share of ``n`` items."""
+        if n % self.size:
+            raise ValueError(f"{what}={n} does not split over tensor-parallel size {self.size}")
+        per = n // self.size
+        return self.rank * per, per
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.size > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(x, group=self.group)
+        return x
+
+
 class RMSNorm(nn.Module):
     def __init__(self, dim: int, eps: float, dtype, device):
         super().__init__()
@@ -75,10 +102,12 @@ class RMSNorm(nn.Module):
 class MLAAttention(nn.Module):
     """DeepSeek multi-head latent attention, absorbed form for cache reads."""
 
-    def __init__(self, arch: ModelArchConfig, dtype, device):
+    def __init__(self, arch: ModelArchConfig, dtype, device, tp: TPInfo = TPInfo()):
         super().__init__()
         self.arch = arch
-        H, nh = arch.hidden_size, arch.num_attention_heads
+        self.tp = tp
+        H = arch.hidden_size
+        self.head0, nh = tp.shard(arch.num_attention_heads, "num_attention_heads")
         self.num_heads = nh
         self.qk_nope = arch.qk_nope_head_dim
         self.qk_rope = arch.qk_rope_head_dim
@@ -110,8 +139,9 @@ class MLAAttention(nn.Module):
         return self.in_proj[self.n_q_in :]
 
     def set_kv_b_proj(self, w: torch.Tensor) -> None:
-        nh = self.num_heads
-        w = w.view(nh, self.qk_nope + self.v_dim, self.kv_lora)
+        """Full checkpoint ``kv_b_proj [heads * (nope + v), kv_lora]``; keeps this rank's heads."""
+        w = w.view(self.arch.num_attention_heads, self.qk_nope + self.v_dim, self.kv_lora)
+        w = w[self.head0 : self.head0 + self.num_heads]
         self.w_uk.data.copy_(w[:, : self.qk_nope, :])
         self.w_uv_t.data.copy_(w[:, self.qk_nope :, :].transpose(1, 2))
 
@@ -141,7 +171,7 @@ class MLAAttention(nn.Module):
             o_lat = ops.mla_decode_split(q_lat.transpose(0, 1), q_pe, kv_cache, meta.block_table, meta.seq_lens,
                                          self.scale, head_major_out=True)
             o = torch.bmm(o_lat, self.w_uv_t).transpose(0, 1).reshape(T, self.num_heads * self.v_dim)
-            return ops.linear(o, self.o_proj)
+            return self.tp.all_reduce(ops.linear(o, self.o_proj))
         # [H, T, nope] x [H, nope, kv_lora] -> [H, T, kv_lora]
         if h.is_cuda:
             q_lat = torch.bmm(q_nope.transpose(0, 1), self.w_uk)
@@ -164,17 +194,18 @@ class MLAAttention(nn.Module):
         else:
             o = torch.bmm(o_lat.transpose(0, 1).float(), self.w_uv_t.float()).to(h.dtype)
         o = o.transpose(0, 1).reshape(T, self.num_heads * self.v_dim)
-        return ops.linear(o, self.o_proj)
+        return self.tp.all_reduce(ops.linear(o, self.o_proj))
 
 
 class GQAAttention(nn.Module):
     """Grouped-query attention with per-head QK RMSNorm (Qwen3)."""
 
-    def __init__(self, arch: ModelArchConfig, dtype, device):
+    def __init__(self, arch: ModelArchConfig, dtype, device, tp: TPInfo = TPInfo()):
         super().__init__()
         self.arch = arch
-        self.nq = arch.num_attention_heads
-        self.nkv = arch.num_key_value_heads
+        self.tp = tp
+        self.q0, self.nq = tp.shard(arch.num_attention_heads, "num_attention_heads")
+        self.kv0, self.nkv = tp.shard(arch.num_key_value_heads, "num_key_value_heads")
         self.d = arch.head_dim
         self.scale = arch.softmax_scale
         H = arch.hidden_size
@@ -204,7 +235,7 @@ class GQAAttention(nn.Module):
                 o[start:end] = ref.gqa_prefill(
                     q[start:end], k_cache, v_cache, meta.block_table[seq], meta.positions[start:end], self.scale
                 )
-        return ops.linear(o.reshape(T, self.nq * self.d), self.o_proj)
+        return self.tp.all_reduce(ops.linear(o.reshape(T, self.nq * self.d), self.o_proj))
 
 
 

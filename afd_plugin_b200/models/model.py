@@ -41,6 +41,7 @@ from afd_plugin_b200.models.layers import (
     MLAAttention,
     MoEBlock,
     RMSNorm,
+    TPInfo,
     _param,
 )
 from afd_plugin_b200.ops import reference as ref
@@ -118,7 +119,7 @@ def _v4_weight_roles(name: str, parts: list[str], *, route_on_attention: bool) -
 
 class DecoderLayer(nn.Module):
     def __init__(self, arch: ModelArchConfig, idx: int, role: str, dtype, device, *, gate_on_attn: bool,
-                 ep_rank: int, ep_size: int, route_on_attn: bool = False):
+                 ep_rank: int, ep_size: int, route_on_attn: bool = False, tp: TPInfo = TPInfo()):
         super().__init__()
         self.idx = idx
         self.is_moe = arch.is_moe_layer(idx)
@@ -129,14 +130,16 @@ class DecoderLayer(nn.Module):
         self.self_attn = None
         self.is_linear_attn = arch.is_linear_attention_layer(idx)
         if has_attn:
+            if (self.is_linear_attn or arch.attn_output_gate) and tp.size > 1:
+                raise NotImplementedError("attention tensor parallelism covers MLA and GQA attention")
             if self.is_linear_attn:
                 self.self_attn = GatedDeltaNet(arch, dtype, device)
             elif arch.attn_output_gate:
                 self.self_attn = GatedGQAAttention(arch, dtype, device)
             elif arch.is_mla:
-                self.self_attn = MLAAttention(arch, dtype, device)
+                self.self_attn = MLAAttention(arch, dtype, device, tp)
             else:
-                self.self_attn = GQAAttention(arch, dtype, device)
+                self.self_attn = GQAAttention(arch, dtype, device, tp)
         self.mlp: nn.Module | None = None
         self.gate_only = None
         if role == "colocated":
@@ -173,6 +176,7 @@ class AFDCausalLM(nn.Module):
         ep_size: int = 1,
         max_positions: int | None = None,
         route_on_attention: bool = False,
+        tp: TPInfo = TPInfo(),
     ):
         super().__init__()
         if role not in ROLES:
@@ -186,11 +190,12 @@ class AFDCausalLM(nn.Module):
         # Routing on the Attention side without moving dense MLPs there (fused connector).
         self.route_on_attention = route_on_attention
         self.ep_rank, self.ep_size = ep_rank, ep_size
+        self.tp = tp
         has_attn = role in ("colocated", "attention")
         self.embed_tokens = _param((arch.vocab_size, arch.hidden_size), dtype, device) if has_attn else None
         self.layers = nn.ModuleList(
             DecoderLayer(arch, i, role, dtype, device, gate_on_attn=compute_gate_on_attention,
-                         ep_rank=ep_rank, ep_size=ep_size, route_on_attn=route_on_attention)
+                         ep_rank=ep_rank, ep_size=ep_size, route_on_attn=route_on_attention, tp=tp)
             for i in range(arch.num_hidden_layers)
         )
         self.norm = RMSNorm(arch.hidden_size, arch.rms_norm_eps, dtype, device) if has_attn else None
@@ -209,6 +214,13 @@ class AFDCausalLM(nn.Module):
     @property
     def num_layers(self) -> int:
         return self.arch.num_hidden_layers
+
+    @property
+    def cache_arch(self) -> ModelArchConfig:
+        """Shapes of this rank's KV cache (a tensor-parallel GQA rank caches its own KV heads)."""
+        if self.tp.size > 1 and not self.arch.is_mla:
+            return self.arch.scaled(num_key_value_heads=self.arch.num_key_value_heads // self.tp.size)
+        return self.arch
 
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
         return self.embed_tokens[input_ids.long()]
@@ -359,6 +371,24 @@ def _rows(dst: torch.Tensor, start: int, stop: int) -> Callable[[torch.Tensor], 
     return setter
 
 
+def _rows_of(dst: torch.Tensor, dst0: int, src0: int, n: int) -> Callable[[torch.Tensor], None]:
+    """Copy rows [src0, src0 + n) of a full checkpoint tensor into dst rows [dst0, dst0 + n)."""
+
+    def setter(src: torch.Tensor) -> None:
+        dst.data[dst0 : dst0 + n].copy_(src[src0 : src0 + n].to(dst.device, dst.dtype))
+
+    return setter
+
+
+def _cols_of(dst: torch.Tensor, src0: int) -> Callable[[torch.Tensor], None]:
+    """Copy columns [src0, src0 + dst.shape[1]) of a full checkpoint tensor into dst."""
+
+    def setter(src: torch.Tensor) -> None:
+        dst.data.copy_(src[:, src0 : src0 + dst.shape[1]].to(dst.device, dst.dtype))
+
+    return setter
+
+
 def _fp8_rows(dst_w: torch.Tensor, dst_s: torch.Tensor, start: int, stop: int) -> Callable[[torch.Tensor], None]:
     """Setter for an fp8 block-quantised slice: quantises unless given e4m3 data."""
 
@@ -411,20 +441,24 @@ class AFDDeepseekV2ForCausalLM(AFDCausalLM):
             raise ValueError("DeepSeek wrapper requires MLA attention")
 
     def _attn_specs(self, p: str, attn: MLAAttention) -> Iterator[ParamSpec]:
+        """Full checkpoint shapes; a tensor-parallel rank keeps its heads' rows / columns."""
         a = self.arch
+        H, nh_all = a.hidden_size, a.num_attention_heads
+        qk = a.qk_head_dim
         nq = attn.n_q_in
         nkv = a.kv_lora_rank + a.qk_rope_head_dim
+        h0, nh = attn.head0, attn.num_heads
         if a.q_lora_rank:
-            yield ParamSpec(p + "q_a_proj.weight", (nq, a.hidden_size), _rows(attn.in_proj, 0, nq))
+            yield ParamSpec(p + "q_a_proj.weight", (nq, H), _rows(attn.in_proj, 0, nq))
             yield ParamSpec(p + "q_a_layernorm.weight", (a.q_lora_rank,), _copy(attn.q_a_layernorm.weight), "ones")
-            yield ParamSpec(p + "q_b_proj.weight", tuple(attn.q_b_proj.shape), _copy(attn.q_b_proj))
+            yield ParamSpec(p + "q_b_proj.weight", (nh_all * qk, a.q_lora_rank), _rows_of(attn.q_b_proj, 0, h0 * qk, nh * qk))
         else:
-            yield ParamSpec(p + "q_proj.weight", (nq, a.hidden_size), _rows(attn.in_proj, 0, nq))
-        yield ParamSpec(p + "kv_a_proj_with_mqa.weight", (nkv, a.hidden_size), _rows(attn.in_proj, nq, nq + nkv))
+            yield ParamSpec(p + "q_proj.weight", (nh_all * qk, H), _rows_of(attn.in_proj, 0, h0 * qk, nh * qk))
+        yield ParamSpec(p + "kv_a_proj_with_mqa.weight", (nkv, H), _rows(attn.in_proj, nq, nq + nkv))
         yield ParamSpec(p + "kv_a_layernorm.weight", (a.kv_lora_rank,), _copy(attn.kv_a_layernorm.weight), "ones")
-        shape = (a.num_attention_heads * (a.qk_nope_head_dim + a.v_head_dim), a.kv_lora_rank)
+        shape = (nh_all * (a.qk_nope_head_dim + a.v_head_dim), a.kv_lora_rank)
         yield ParamSpec(p + "kv_b_proj.weight", shape, lambda t, _a=attn: _a.set_kv_b_proj(t.to(_a.w_uk.device, _a.w_uk.dtype)))
-        yield ParamSpec(p + "o_proj.weight", tuple(attn.o_proj.shape), _copy(attn.o_proj))
+        yield ParamSpec(p + "o_proj.weight", (H, nh_all * a.v_head_dim), _cols_of(attn.o_proj, h0 * a.v_head_dim))
 
 
 class AFDDeepseekV3ForCausalLM(AFDDeepseekV2ForCausalLM):
@@ -454,14 +488,17 @@ class AFDQwen3MoeForCausalLM(AFDCausalLM):
             raise ValueError("Qwen3-MoE wrapper requires GQA attention with QK-norm")
 
     def _attn_specs(self, p: str, attn: GQAAttention) -> Iterator[ParamSpec]:
+        """Full checkpoint shapes; a tensor-parallel rank keeps its heads' rows / columns."""
         d, nq, nkv = attn.d, attn.nq, attn.nkv
-        H = self.arch.hidden_size
-        yield ParamSpec(p + "q_proj.weight", (nq * d, H), _rows(attn.qkv_proj, 0, nq * d))
-        yield ParamSpec(p + "k_proj.weight", (nkv * d, H), _rows(attn.qkv_proj, nq * d, (nq + nkv) * d))
-        yield ParamSpec(p + "v_proj.weight", (nkv * d, H), _rows(attn.qkv_proj, (nq + nkv) * d, (nq + 2 * nkv) * d))
+        a = self.arch
+        H, nq_all, nkv_all = a.hidden_size, a.num_attention_heads, a.num_key_value_heads
+        yield ParamSpec(p + "q_proj.weight", (nq_all * d, H), _rows_of(attn.qkv_proj, 0, attn.q0 * d, nq * d))
+        yield ParamSpec(p + "k_proj.weight", (nkv_all * d, H), _rows_of(attn.qkv_proj, nq * d, attn.kv0 * d, nkv * d))
+        yield ParamSpec(p + "v_proj.weight", (nkv_all * d, H),
+                        _rows_of(attn.qkv_proj, (nq + nkv) * d, attn.kv0 * d, nkv * d))
         yield ParamSpec(p + "q_norm.weight", (d,), _copy(attn.q_norm.weight), "ones")
         yield ParamSpec(p + "k_norm.weight", (d,), _copy(attn.k_norm.weight), "ones")
-        yield ParamSpec(p + "o_proj.weight", tuple(attn.o_proj.shape), _copy(attn.o_proj))
+        yield ParamSpec(p + "o_proj.weight", (H, nq_all * d), _cols_of(attn.o_proj, attn.q0 * d))
 
 
 class AFDDeepseekV4ForCausalLM(AFDDeepseekV2ForCausalLM):

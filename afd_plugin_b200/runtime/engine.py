@@ -89,8 +89,8 @@ class LLMEngine:
         if num_blocks is None:
             num_blocks = cc.num_blocks or (self.max_batch * self.max_blocks_per_seq + 1)
         # One linear-attention state row per running request plus a padding row.
-        self.kv = KVCache(model.arch, num_blocks, self.block_size, model.dtype, self.device,
-                          max_seqs=self.max_batch + 1)
+        self.kv = KVCache(getattr(model, "cache_arch", model.arch), num_blocks, self.block_size, model.dtype,
+                          self.device, max_seqs=self.max_batch + 1)
         self._free_state_slots = list(range(self.max_batch - 1, -1, -1))
         self.ffn = ffn_executor or LocalFFNExecutor(model)
         num_ub = engine_config.parallel_config.num_ubatches if engine_config.parallel_config.use_ubatching else 1

@@ -40,6 +40,8 @@ class LocalAFDSpec:
     timeout_s: int = 60
     # fault injection on the host (tests): {"rank": r, "kind": "raise"|"exit", "at_step": n}
     fault: dict | None = None
+    # attention tensor parallelism: num_attention_ranks = DP x tp
+    tp: int = 1
 
 
 def free_port() -> int:
@@ -58,8 +60,8 @@ def build_engine_config(spec: LocalAFDSpec):
     return EngineConfig(
         model_config=ModelConfig(arch, dtype=dtype, enforce_eager=spec.enforce_eager,
                                  max_model_len=spec.max_model_len, seed=spec.seed),
-        parallel_config=ParallelConfig(data_parallel_size=A, use_ubatching=spec.use_ubatching,
-                                       num_ubatches=2 if spec.use_ubatching else 1),
+        parallel_config=ParallelConfig(data_parallel_size=A // spec.tp, tensor_parallel_size=spec.tp,
+                                       use_ubatching=spec.use_ubatching, num_ubatches=2 if spec.use_ubatching else 1),
         compilation_config=CompilationConfig(cudagraph_capture_sizes=list(spec.capture_sizes)),
         additional_config={"afd": dict(spec.afd)},
         max_num_seqs=spec.max_num_seqs,
@@ -109,7 +111,8 @@ def _rank_main(world_rank: int, world_size: int, port: int, spec: LocalAFDSpec, 
             from afd_plugin_b200.runtime.workers import AFDAttentionWorker
 
             w = AFDAttentionWorker(config, local_rank=local_rank)
-            mine = split_prompts(spec.prompts, A)[role_rank]
+            # tensor-parallel peers serve the same requests (their data-parallel rank's share)
+            mine = split_prompts(spec.prompts, A // spec.tp)[role_rank // spec.tp]
             ids = [w.engine.add_request(p, spec.max_tokens) for p in mine]
             if not spec.enforce_eager and backend == "nccl":
                 w.engine.capture_graphs()
@@ -127,7 +130,7 @@ def _rank_main(world_rank: int, world_size: int, port: int, spec: LocalAFDSpec, 
                     os._exit(3)
                 w.engine.step()
                 step += 1
-            outs = [w.engine.finished[i].output for i in ids]
+            outs = [w.engine.finished[i].output for i in ids] if role_rank % spec.tp == 0 else []
             if A > 1:
                 dist.barrier(group=group)
             w.shutdown()

@@ -33,16 +33,29 @@ FFN_SHUTDOWN_TIMEOUT_SECONDS = 5.0
 class AFDGroups:
     attention_group: object | None  # gloo group over Attention ranks (step agreement)
     ffn_group: object | None  # group over FFN ranks (expert parallel exchange)
+    tp_group: object | None = None  # this Attention rank's tensor-parallel peers (tp_size > 1)
 
 
-def init_afd_groups(mapping: AFDRankMapping) -> AFDGroups:
-    """Collective over the whole AFD world."""
+def init_afd_groups(mapping: AFDRankMapping, tp_size: int = 1) -> AFDGroups:
+    """Collective over the whole AFD world.
+
+    Tensor-parallel groups are consecutive Attention role ranks
+    ``[dp * tp, dp * tp + tp)`` (the reference's role-rank linearisation).
+    """
     attn = dist.new_group(list(mapping.attention_world_ranks), backend="gloo")
     backend = dist.get_backend()
     ffn = dist.new_group(list(mapping.ffn_world_ranks), backend=backend)
+    mine = None
+    if tp_size > 1:
+        ranks = list(mapping.attention_world_ranks)
+        for start in range(0, len(ranks), tp_size):
+            grp = dist.new_group(ranks[start : start + tp_size], backend=backend)
+            if mapping.role == "attention" and mapping.world_rank in ranks[start : start + tp_size]:
+                mine = grp
     return AFDGroups(
         attention_group=attn if mapping.role == "attention" else None,
         ffn_group=ffn if mapping.role == "ffn" else None,
+        tp_group=mine,
     )
 
 
@@ -72,7 +85,8 @@ class _WorkerBase:
         self.connector = AFDConnectorFactory.create_connector(
             self.world_rank, local_rank, engine_config, self.afd, role_rank)
         self.connector.init_afd_connector()
-        self.groups = init_afd_groups(self.mapping)
+        self.tp_size = int(getattr(engine_config.parallel_config, "tensor_parallel_size", 1))
+        self.groups = init_afd_groups(self.mapping, self.tp_size)
 
 
 class AFDAttentionWorker(_WorkerBase):
@@ -82,12 +96,15 @@ class AFDAttentionWorker(_WorkerBase):
         from afd_plugin_b200.runtime.engine import AttentionCoordinator, LLMEngine
         from afd_plugin_b200.runtime.ffn_executor import ConnectorFFNExecutor
 
+        from afd_plugin_b200.models.layers import TPInfo
+
         mc = engine_config.model_config
+        tp = TPInfo(self.role_rank % self.tp_size, self.tp_size, self.groups.tp_group)
         self.model = build_model(
             mc.arch, role="attention", dtype=mc.dtype, device=self.device,
             compute_gate_on_attention=self.afd.compute_gate_on_attention,
             route_on_attention=self.afd.connector == B200_FUSED_CONNECTOR,
-            seed=mc.seed if seed is None else seed, checkpoint=mc.checkpoint, max_positions=mc.max_model_len)
+            seed=mc.seed if seed is None else seed, checkpoint=mc.checkpoint, max_positions=mc.max_model_len, tp=tp)
         A = self.afd.num_attention_ranks
         if self.afd.connector == B200_FUSED_CONNECTOR:
             executor = self.connector.make_executor(self.model)

@@ -88,3 +88,12 @@ def test_dsv4_expert_parallel_2a2f():
     ref = _colocated("tiny-dsv4", prompts, 5)
     outs, _ = _run("tiny-dsv4", {"num_attention_ranks": 2, "num_ffn_ranks": 2}, prompts, max_tokens=5)
     assert outs == ref
+
+
+@pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-qwen3-moe"])
+def test_attention_tp2_matches_colocated(preset):
+    """Two Attention ranks as one DP rank with TP=2 (heads split, o_proj all-reduced) + 1 FFN rank."""
+    prompts = _prompts(n=3, length=12)
+    ref = _colocated(preset, prompts, 6)
+    outs, _ = _run(preset, {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=6, tp=2)
+    assert outs == ref
