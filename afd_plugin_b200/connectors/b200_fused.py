@@ -586,7 +586,10 @@ class FusedFFNRunner:
         host can queue the next step while the device runs.  The device status
         is checked every ``check_every`` steps and at the end.
         """
+        from afd_plugin_b200.utils.profiler import RoleProfiler
+
         cp = self.c.control_plane
+        prof = RoleProfiler("ffn")
         n = 0
         try:
             while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
@@ -595,10 +598,12 @@ class FusedFFNRunner:
                     break
                 self.execute_model(payload)
                 n += 1
+                prof.step()
                 if n % check_every == 0:
                     self._check()
         finally:
             torch.cuda.synchronize(self.device)
+            prof.close()
         self._check()
         return n
 

@@ -115,6 +115,9 @@ class LLMEngine:
         self._h_state = mk(self.max_batch, dt=torch.int32)
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
+        from afd_plugin_b200.utils.profiler import RoleProfiler
+
+        self.profiler = RoleProfiler("attention")
 
     # ------------------------------------------------------------ helpers
     @classmethod
@@ -203,6 +206,15 @@ class LLMEngine:
 
     # ---------------------------------------------------------------- step
     def step(self) -> dict[int, int]:
+        out = self._step()
+        self.profiler.step()
+        return out
+
+    def close(self) -> None:
+        """Flush an active profiler trace."""
+        self.profiler.close()
+
+    def _step(self) -> dict[int, int]:
         admit = []
         while self.waiting and len(self.running) + len(admit) < self.max_batch:
             admit.append(self.waiting.pop(0))

@@ -181,15 +181,22 @@ class FFNModelRunner:
         cp = self.connector.control_plane
         if cp is None:
             raise NotImplementedError("FFN serving needs a control-plane-driven connector")
+        from afd_plugin_b200.utils.profiler import RoleProfiler
+
+        prof = RoleProfiler("ffn")
         n = 0
-        while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
-            payload = cp.recv_dp_metadata_list()
-            if payload.is_shutdown:
-                break
-            self.execute_model(payload)
-            if self.device.type == "cuda":
-                torch.cuda.synchronize(self.device)
-            n += 1
+        try:
+            while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
+                payload = cp.recv_dp_metadata_list()
+                if payload.is_shutdown:
+                    break
+                self.execute_model(payload)
+                if self.device.type == "cuda":
+                    torch.cuda.synchronize(self.device)
+                n += 1
+                prof.step()
+        finally:
+            prof.close()
         return n
 
     def release_graphs(self) -> None:
