@@ -56,7 +56,14 @@ def _time_us(fn, reps: int, iters: int = 5) -> float:
     return e0.elapsed_time(e1) * 1e3 / (iters * reps)
 
 
-def run(shape: str, reps: int, tokens_per_expert: int | None = None) -> dict:
+def _quant(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    from afd_plugin_b200.ops import reference as ref
+
+    qs, ss = zip(*(ref.quant_fp8_block_weight(w[e]) for e in range(w.shape[0])))
+    return torch.stack(qs).contiguous(), torch.stack(ss).contiguous()
+
+
+def run(shape: str, reps: int, tokens_per_expert: int | None = None, fp8: bool = False) -> dict:
     from afd_plugin_b200.ops import _ext
 
     C = _ext.ops()
@@ -71,11 +78,22 @@ def run(shape: str, reps: int, tokens_per_expert: int | None = None) -> dict:
     a2 = (torch.randn(rows, I, device=dev) * 0.1).to(torch.bfloat16)
     w2 = (torch.randn(E, H, I, device=dev) * 0.02).to(torch.bfloat16)
     peak, kind = _peak_gbs()
-    out = {"shape": shape, "experts": E, "hidden": H, "intermediate": I, "tokens_per_expert": tpe}
-    for name, fn, wbytes in (
-        ("gemm1_swiglu", lambda: C.grouped_gemm_ex(a1, w13, offsets, counts, 1, -1), w13.numel() * 2),
-        ("gemm2", lambda: C.grouped_gemm_ex(a2, w2, offsets, counts, 0, -1), w2.numel() * 2),
-    ):
+    out = {"shape": shape, "experts": E, "hidden": H, "intermediate": I, "tokens_per_expert": tpe,
+           "weights": "fp8 e4m3, 128x128 block scales" if fp8 else "bf16"}
+    if fp8:
+        q13, s13 = _quant(w13)
+        q2, s2 = _quant(w2)
+        del w13, w2
+        cases = (
+            ("gemm1_swiglu", lambda: C.grouped_gemm_w8(a1, q13, s13, offsets, counts, 1, E), q13.numel() + s13.numel() * 4),
+            ("gemm2", lambda: C.grouped_gemm_w8(a2, q2, s2, offsets, counts, 0, E), q2.numel() + s2.numel() * 4),
+        )
+    else:
+        cases = (
+            ("gemm1_swiglu", lambda: C.grouped_gemm_ex(a1, w13, offsets, counts, 1, -1), w13.numel() * 2),
+            ("gemm2", lambda: C.grouped_gemm_ex(a2, w2, offsets, counts, 0, -1), w2.numel() * 2),
+        )
+    for name, fn, wbytes in cases:
         us = _time_us(fn, reps)
         gbs = wbytes / (us * 1e-6) / 1e9
         out[name + "_us"] = round(us, 2)
@@ -91,9 +109,10 @@ def main(argv=None) -> None:
     ap.add_argument("--shapes", default=",".join(SHAPES))
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--tokens-per-expert", type=int, default=None)
+    ap.add_argument("--fp8", action="store_true", help="fp8 block-scaled weights (grouped_gemm_w8)")
     args = ap.parse_args(argv)
     for shape in args.shapes.split(","):
-        print(json.dumps(run(shape, args.reps, args.tokens_per_expert)), flush=True)
+        print(json.dumps(run(shape, args.reps, args.tokens_per_expert, fp8=args.fp8)), flush=True)
 
 
 if __name__ == "__main__":
