@@ -446,6 +446,9 @@ class MoEGate(nn.Module):
         self.weight_f32 = self.weight.detach().float()
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
+        if h.is_cuda and h.dtype == self.weight.dtype == torch.bfloat16:
+            # bf16 operands, fp32 accumulation and output in one cuBLAS call
+            return torch.mm(h, self.weight.t(), out_dtype=torch.float32)
         w = getattr(self, "weight_f32", None)
         if w is None or w.device != h.device:
             w = self.weight.float()

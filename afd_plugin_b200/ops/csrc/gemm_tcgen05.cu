@@ -348,16 +348,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
 // 128-row x 128-K fp8 weight tiles (half the HBM bytes of bf16), four
 // converter warps dequantise each tile with its 128 x 128 block scale into two
 // 128B-swizzled bf16 tiles in shared memory, and the tcgen05 MMA reads those.
-// Warp roles: 0 TMA producer, 1 TMEM + MMA issuer, 2-5 epilogue, 6-9 converter.
+// Warp roles: 0 TMA producer, 1 TMEM + MMA issuer, 2-5 epilogue, 6-13 converter.
+// Decode gives a few tokens per expert, so a pass takes 64 tokens and the
+// shared memory goes to pipeline depth (4 TMA stages) and to the converted ring.
 namespace gg8 {
 
 constexpr int kBK = 128;                       // K per stage (one fp8 row = 128 B)
 constexpr int kBM = 128;
 constexpr int kSub = 64;
-constexpr int kMaxSub = 2;                     // tokens per pass <= 128
-constexpr int kStages = 3;
+constexpr int kMaxSub = 1;                     // tokens per pass <= 64
+constexpr int kStages = 4;
 constexpr int kCvt = 2;
-constexpr int kThreads = 10 * 32;
+constexpr int kCvtWarps = 8;
+constexpr int kCvtThreads = kCvtWarps * 32;
+constexpr int kThreads = (6 + kCvtWarps) * 32;
 constexpr int kWBytes = kBM * kBK;             // 16 KB fp8
 constexpr int kWcHalf = kBM * 64 * 2;          // 16 KB: 128 rows x 64 K bf16
 constexpr int kSubBytes = kSub * 64 * 2;       // 8 KB: 64 tokens x 64 K bf16
@@ -420,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
       mbar_init(&sm.empty[s], 1);
     }
     for (int c = 0; c < kCvt; ++c) {
-      mbar_init(&sm.cfull[c], 128);
+      mbar_init(&sm.cfull[c], kCvtThreads);
       mbar_init(&sm.cempty[c], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -487,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
     }
   } else if (warp >= 6) {
     // ---------------------------------------------------------- converter
-    const int ct = threadIdx.x - 6 * 32;  // 0..127
+    const int ct = threadIdx.x - 6 * 32;  // 0 .. kCvtThreads - 1
     int it_count = 0, idx = blockIdx.x;
     gg::Item it;
     bool ok = true;
@@ -511,8 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
           const float s_lo = sc_lo[kb], s_hi = sc_hi[kb];
           const uint8_t* src = sm.w[st];
           uint8_t* dst = sm.wc[cs];
-#pragma unroll 2
-          for (int q = ct; q < kBM * 8; q += 128) {
+#pragma unroll
+          for (int q = ct; q < kBM * 8; q += kCvtThreads) {
             const int r = q >> 3, c = q & 7;
             const uint4 raw = *reinterpret_cast<const uint4*>(src + r * 128 + ((c ^ (r & 7)) << 4));
             uint4 hi;
