@@ -1,0 +1,91 @@
+"""Serve completions over HTTP.
+
+Colocated (one process):
+    python -m afd_plugin_b200.serving --preset tiny-dsv2 --port 8000
+
+AFD (one process per GPU; Attention rank 0 serves HTTP):
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m afd_plugin_b200.serving \\
+        --preset deepseek-v2-lite --afd '{"num_attention_ranks": 1, "num_ffn_ranks": 1,
+                                          "connector": "B200FusedAFDConnector"}'
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description="afd_plugin_b200 completions server")
+    ap.add_argument("--preset", default="tiny-dsv2")
+    ap.add_argument("--checkpoint", default=None, help="HF safetensors directory (random init when absent)")
+    ap.add_argument("--dtype", default="bfloat16")
+    ap.add_argument("--afd", default="", help='JSON additional_config["afd"] (empty: colocated)')
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--max-num-seqs", type=int, default=64)
+    ap.add_argument("--max-model-len", type=int, default=4096)
+    ap.add_argument("--eager", action="store_true")
+    args = ap.parse_args(argv)
+
+    import torch
+    import uvicorn
+
+    from afd_plugin_b200.engine_config import CompilationConfig, EngineConfig, ModelConfig, ParallelConfig
+    from afd_plugin_b200.models.configs import get_preset
+    from afd_plugin_b200.serving.api_server import EngineLoop, build_app
+
+    arch = get_preset(args.preset)
+    dtype = getattr(torch, args.dtype)
+    afd = json.loads(args.afd) if args.afd else {}
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if not afd:
+        from afd_plugin_b200.runtime.engine import LLMEngine
+
+        ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=args.eager, max_model_len=args.max_model_len,
+                                      checkpoint=args.checkpoint),
+                          compilation_config=CompilationConfig(cudagraph_capture_sizes=[args.max_num_seqs]),
+                          max_num_seqs=args.max_num_seqs)
+        engine = LLMEngine.colocated(ec, device="cuda" if torch.cuda.is_available() else "cpu")
+        loop = EngineLoop(engine).start()
+        uvicorn.run(build_app(loop), host=args.host, port=args.port)
+        return
+
+    import torch.distributed as dist
+
+    from afd_plugin_b200.parallel.topology import role_of_world_rank
+    from afd_plugin_b200.runtime.workers import AFDAttentionWorker, AFDFFNWorker
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    backend = "nccl" if torch.cuda.is_available() else "gloo"
+    if backend == "nccl":
+        torch.cuda.set_device(local)
+    dist.init_process_group(backend=backend)
+    A, F = int(afd["num_attention_ranks"]), int(afd["num_ffn_ranks"])
+    if world != A + F:
+        raise SystemExit(f"world size {world} != num_attention_ranks + num_ffn_ranks = {A + F}")
+    role, role_rank = role_of_world_rank(rank, attention_size=A, ffn_size=F)
+    ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=args.eager, max_model_len=args.max_model_len,
+                                  checkpoint=args.checkpoint),
+                      parallel_config=ParallelConfig(data_parallel_size=A),
+                      compilation_config=CompilationConfig(cudagraph_capture_sizes=[args.max_num_seqs]),
+                      additional_config={"afd": dict(afd, role=role)}, max_num_seqs=args.max_num_seqs)
+    if role == "ffn":
+        w = AFDFFNWorker(ec, local_rank=local)
+        w.run_ffn_server_loop()
+        w.shutdown()
+        return
+    w = AFDAttentionWorker(ec, local_rank=local)
+    if not args.eager and backend == "nccl":
+        w.engine.capture_graphs()
+    loop = EngineLoop(w.engine, group=w.groups.attention_group, world=A, rank=role_rank).start()
+    if role_rank == 0:
+        uvicorn.run(build_app(loop), host=args.host, port=args.port)
+    else:
+        loop.join()
+
+
+if __name__ == "__main__":
+    main()

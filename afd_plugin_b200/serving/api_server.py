@@ -1,0 +1,178 @@
+"""OpenAI-style completions server over :class:`LLMEngine`.
+
+``EngineLoop`` owns the engine on a background thread: requests are queued
+from any thread, the loop admits them and steps the engine while work is
+pending, and each request's future resolves with its tokens.  In an AFD
+deployment every Attention rank runs an ``EngineLoop``; rank 0 serves HTTP
+and the ranks agree each iteration (over the Attention group) whether any of
+them has work, so all of them step together (the coordinator pads idle ranks
+with a placeholder row, as the reference's DP dummy batches do).
+
+Endpoints: ``GET /health``, ``GET /metrics`` (engine counters),
+``POST /v1/completions`` with ``{"prompt": str | [int], "max_tokens": int}``.
+Without a tokenizer in the image, text is mapped to token ids byte by byte
+(``byte_tokenize``), which keeps the server usable for smoke tests and
+benchmark drivers that send token ids directly.
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from concurrent.futures import Future
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+from pydantic import BaseModel
+
+
+class CompletionRequest(BaseModel):
+    prompt: str | list[int]
+    max_tokens: int = 16
+    model: str | None = None
+
+
+def byte_tokenize(text: str, vocab_size: int) -> list[int]:
+    return [b % vocab_size for b in text.encode("utf-8")] or [0]
+
+
+def byte_detokenize(ids: list[int]) -> str:
+    return bytes(i % 256 for i in ids).decode("utf-8", errors="replace")
+
+
+@dataclass
+class _Pending:
+    prompt: list[int]
+    max_tokens: int
+    future: Future
+    submitted: float = field(default_factory=time.perf_counter)
+
+
+class EngineLoop:
+    """Steps an engine on a background thread.
+
+    ``group`` / ``world`` / ``rank``: the Attention ranks that must step
+    together (None for a single engine).
+    """
+
+    def __init__(self, engine, *, group=None, world: int = 1, rank: int = 0, idle_sleep_s: float = 0.001):
+        self.engine = engine
+        self.group, self.world, self.rank = group, world, rank
+        self.idle_sleep_s = idle_sleep_s
+        self._queue: list[_Pending] = []
+        self._lock = threading.Lock()
+        self._inflight: dict[int, _Pending] = {}
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+        self.error: BaseException | None = None
+        self.stats = {"requests": 0, "completed": 0, "generated_tokens": 0, "steps": 0, "ttft_s_sum": 0.0}
+
+    # ------------------------------------------------------------ clients
+    def submit(self, prompt: list[int], max_tokens: int) -> Future:
+        limit = self.engine.config.model_config.max_model_len
+        if len(prompt) + int(max_tokens) > limit:
+            raise ValueError(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds max_model_len {limit}")
+        fut: Future = Future()
+        with self._lock:
+            self._queue.append(_Pending(list(prompt), int(max_tokens), fut))
+            self.stats["requests"] += 1
+        return fut
+
+    # --------------------------------------------------------------- loop
+    def start(self) -> "EngineLoop":
+        self._thread = threading.Thread(target=self._run, name="afd-engine-loop", daemon=True)
+        self._thread.start()
+        return self
+
+    def stop(self, timeout: float = 60.0) -> None:
+        """Stop this loop; with peers, every rank's loop leaves at the same iteration."""
+        self._stop.set()
+        self.join(timeout)
+
+    def join(self, timeout: float | None = None) -> None:
+        """Wait until the loop ends (a peer's stop ends it on every rank)."""
+        if self._thread is not None:
+            self._thread.join(timeout)
+            if not self._thread.is_alive():
+                self._thread = None
+
+    def _agree(self, work: bool, stop: bool) -> tuple[bool, bool]:
+        """(any rank has work, any rank stops) -- one collective per iteration on every rank."""
+        if self.group is None or self.world <= 1:
+            return work, stop
+        flag = torch.tensor([int(work), int(stop)])
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+        return bool(flag[0]), bool(flag[1])
+
+    def _run(self) -> None:
+        eng = self.engine
+        try:
+            if eng.device.type == "cuda":
+                torch.cuda.set_device(eng.device)
+            while True:
+                with self._lock:
+                    new, self._queue = self._queue, []
+                for p in new:
+                    rid = eng.add_request(p.prompt, p.max_tokens)
+                    self._inflight[rid] = p
+                work, stop = self._agree(eng.has_unfinished(), self._stop.is_set())
+                if stop:
+                    break
+                if not work:
+                    time.sleep(self.idle_sleep_s)
+                    continue
+                eng.step()
+                self.stats["steps"] += 1
+                for rid in [r for r in self._inflight if r in eng.finished]:
+                    p = self._inflight.pop(rid)
+                    out = eng.finished.pop(rid).output
+                    self.stats["completed"] += 1
+                    self.stats["generated_tokens"] += len(out)
+                    p.future.set_result(out)
+        except BaseException as exc:  # noqa: BLE001 - surfaced to every waiting client
+            self.error = exc
+            for p in list(self._inflight.values()) + self._queue:
+                if not p.future.done():
+                    p.future.set_exception(exc)
+
+
+def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout_s: float = 600.0):
+    """FastAPI app serving ``loop`` (rank 0 of the Attention side)."""
+    from fastapi import FastAPI, HTTPException
+
+    vocab = loop.engine.model.arch.vocab_size
+    app = FastAPI(title="afd_plugin_b200")
+
+    @app.get("/health")
+    def health():
+        if loop.error is not None:
+            raise HTTPException(status_code=503, detail=f"engine failed: {loop.error!r}")
+        return {"status": "ok"}
+
+    @app.get("/metrics")
+    def metrics():
+        return dict(loop.stats)
+
+    @app.post("/v1/completions")
+    def completions(req: CompletionRequest):
+        if req.max_tokens < 1:
+            raise HTTPException(status_code=400, detail="max_tokens must be positive")
+        ids = req.prompt if isinstance(req.prompt, list) else byte_tokenize(req.prompt, vocab)
+        if any((not isinstance(t, int)) or t < 0 or t >= vocab for t in ids):
+            raise HTTPException(status_code=400, detail=f"prompt token ids must be in [0, {vocab})")
+        try:
+            out = loop.submit(ids, req.max_tokens).result(timeout=request_timeout_s)
+        except ValueError as exc:
+            raise HTTPException(status_code=400, detail=str(exc)) from exc
+        return {
+            "object": "text_completion",
+            "model": req.model or model_name,
+            "choices": [{"index": 0, "token_ids": out, "text": byte_detokenize(out), "finish_reason": "length"}],
+            "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)},
+        }
+
+    return app
+
+
+__all__ = ["EngineLoop", "build_app", "byte_detokenize", "byte_tokenize"]

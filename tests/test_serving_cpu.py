@@ -1,0 +1,121 @@
+"""HTTP completions server over a colocated engine (CPU)."""
+
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+
+import pytest
+import requests
+import torch
+
+from afd_plugin_b200.engine_config import EngineConfig, ModelConfig
+from afd_plugin_b200.models import build_model, get_preset
+from afd_plugin_b200.runtime.engine import LLMEngine
+from afd_plugin_b200.runtime.launcher import free_port
+from afd_plugin_b200.serving import EngineLoop, build_app, byte_detokenize, byte_tokenize
+
+
+def _engine():
+    arch = get_preset("tiny-dsv2")
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96), max_num_seqs=4)
+    return LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=96))
+
+
+@pytest.fixture
+def server():
+    import uvicorn
+
+    loop = EngineLoop(_engine()).start()
+    port = free_port()
+    srv = uvicorn.Server(uvicorn.Config(build_app(loop), host="127.0.0.1", port=port, log_level="warning"))
+    t = threading.Thread(target=srv.run, daemon=True)
+    t.start()
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(200):
+        try:
+            if requests.get(url + "/health", timeout=1).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.05)
+    yield url, loop
+    srv.should_exit = True
+    t.join(10)
+    loop.stop()
+
+
+def test_completions_match_engine_generate(server):
+    url, loop = server
+    prompts = [[5, 9, 100, 7, 3, 1], [42] * 10, [1, 2, 3], [900, 800, 700, 600]]
+    want = _engine().generate(prompts, 6)
+    with ThreadPoolExecutor(4) as ex:  # concurrent requests are batched by the engine loop
+        resp = list(ex.map(lambda p: requests.post(url + "/v1/completions", json={"prompt": p, "max_tokens": 6},
+                                                   timeout=60).json(), prompts))
+    assert [r["choices"][0]["token_ids"] for r in resp] == want
+    assert resp[0]["usage"] == {"prompt_tokens": 6, "completion_tokens": 6, "total_tokens": 12}
+    m = requests.get(url + "/metrics", timeout=5).json()
+    assert m["completed"] == 4 and m["generated_tokens"] == 24
+
+
+def test_text_prompt_and_validation(server):
+    url, _ = server
+    r = requests.post(url + "/v1/completions", json={"prompt": "hello", "max_tokens": 3}, timeout=60).json()
+    assert len(r["choices"][0]["token_ids"]) == 3 and r["usage"]["prompt_tokens"] == 5
+    assert requests.post(url + "/v1/completions", json={"prompt": [5000], "max_tokens": 3}, timeout=10).status_code == 400
+    assert requests.post(url + "/v1/completions", json={"prompt": [1] * 95, "max_tokens": 8},
+                         timeout=10).status_code == 400
+    assert byte_detokenize(byte_tokenize("héllo", 1024)) == "héllo"
+
+
+def _afd_serving_rank(world_rank, port, prompts, q):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from afd_plugin_b200.runtime.launcher import LocalAFDSpec, build_engine_config
+    from afd_plugin_b200.parallel.topology import role_of_world_rank
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=world_rank, world_size=3, timeout=timedelta(seconds=60))
+    role, role_rank = role_of_world_rank(world_rank, attention_size=2, ffn_size=1)
+    spec = LocalAFDSpec(preset="tiny-dsv2", afd={"num_attention_ranks": 2, "num_ffn_ranks": 1, "role": role})
+    ec = build_engine_config(spec)
+    if role == "ffn":
+        from afd_plugin_b200.runtime.workers import AFDFFNWorker
+
+        w = AFDFFNWorker(ec)
+        w.run_ffn_server_loop()
+        w.shutdown()
+        q.put((world_rank, None))
+        return
+    from afd_plugin_b200.runtime.workers import AFDAttentionWorker
+
+    w = AFDAttentionWorker(ec)
+    loop = EngineLoop(w.engine, group=w.groups.attention_group, world=2, rank=role_rank).start()
+    outs = None
+    if role_rank == 0:  # only the HTTP rank gets requests; rank 1 steps along with placeholder rows
+        futs = [loop.submit(p, 5) for p in prompts]
+        outs = [f.result(timeout=120) for f in futs]
+        loop.stop()
+    else:
+        loop.join()  # ends when rank 0 stops
+    w.shutdown()
+    q.put((world_rank, outs))
+
+
+def test_engine_loop_lockstep_across_attention_ranks():
+    import torch.multiprocessing as mp
+
+    prompts = [[5, 9, 100, 7, 3, 1], [42] * 10, [1, 2, 3]]
+    want = _engine().generate(prompts, 5)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_afd_serving_rank, args=(r, port, prompts, q)) for r in range(3)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=180) for _ in range(3))
+    for p in ps:
+        p.join(30)
+    assert got[1] == want
