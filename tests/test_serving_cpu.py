@@ -119,3 +119,41 @@ def test_engine_loop_lockstep_across_attention_ranks():
     for p in ps:
         p.join(30)
     assert got[1] == want
+
+
+def test_proxy_balances_over_two_servers():
+    import uvicorn
+
+    from afd_plugin_b200.serving.proxy import build_proxy_app
+
+    servers, loops, urls = [], [], []
+    for _ in range(2):
+        loop = EngineLoop(_engine()).start()
+        port = free_port()
+        srv = uvicorn.Server(uvicorn.Config(build_app(loop), host="127.0.0.1", port=port, log_level="warning"))
+        threading.Thread(target=srv.run, daemon=True).start()
+        servers.append(srv)
+        loops.append(loop)
+        urls.append(f"http://127.0.0.1:{port}")
+    pport = free_port()
+    proxy = uvicorn.Server(uvicorn.Config(build_proxy_app(urls), host="127.0.0.1", port=pport, log_level="warning"))
+    threading.Thread(target=proxy.run, daemon=True).start()
+    purl = f"http://127.0.0.1:{pport}"
+    for _ in range(200):
+        try:
+            if requests.get(purl + "/health", timeout=2).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.05)
+    prompts = [[5, 9, 100, 7], [42] * 6, [1, 2, 3], [900, 800]]
+    want = _engine().generate(prompts, 4)
+    with ThreadPoolExecutor(4) as ex:
+        got = list(ex.map(lambda p: requests.post(purl + "/v1/completions", json={"prompt": p, "max_tokens": 4},
+                                                  timeout=60).json()["choices"][0]["token_ids"], prompts))
+    assert got == want
+    h = requests.get(purl + "/health", timeout=10).json()
+    assert all(h["backends"].values()) and sum(h["served"].values()) == 4 and min(h["served"].values()) >= 1
+    for s in servers + [proxy]:
+        s.should_exit = True
+    for lp in loops:
+        lp.stop()
