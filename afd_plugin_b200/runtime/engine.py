@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import itertools
 import math
+import time
 from dataclasses import dataclass, field
 
 import torch
@@ -118,6 +119,10 @@ class LLMEngine:
         from afd_plugin_b200.utils.profiler import RoleProfiler
 
         self.profiler = RoleProfiler("attention")
+        from afd_plugin_b200.utils.metrics import StepMetrics
+
+        self.metrics = StepMetrics()
+        self._last_phase = "decode"
 
     # ------------------------------------------------------------ helpers
     @classmethod
@@ -206,13 +211,18 @@ class LLMEngine:
 
     # ---------------------------------------------------------------- step
     def step(self) -> dict[int, int]:
+        t0 = time.perf_counter()
         out = self._step()
+        self.metrics.record(phase=self._last_phase, batch=len(out), tokens=len(out),
+                            ms=(time.perf_counter() - t0) * 1e3, h2d_bytes=self.last_h2d_bytes,
+                            d2h_bytes=self.last_d2h_bytes)
         self.profiler.step()
         return out
 
     def close(self) -> None:
-        """Flush an active profiler trace."""
+        """Flush an active profiler trace and the metrics stream."""
         self.profiler.close()
+        self.metrics.close()
 
     def _step(self) -> dict[int, int]:
         admit = []
@@ -222,7 +232,9 @@ class LLMEngine:
         ntok = sum(len(r.prompt) for r in admit) if is_prefill else len(self.running)
         votes = self.coordinator.exchange(ntok, is_prefill)
         if any(p for _, p in votes):
+            self._last_phase = "prefill"
             return self._prefill_step(admit, votes)
+        self._last_phase = "decode"
         return self._decode_step(votes)
 
     def _prefill_step(self, admit: list[Request], votes) -> dict[int, int]:

@@ -152,7 +152,11 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     @app.get("/metrics")
     def metrics():
-        return dict(loop.stats)
+        out = dict(loop.stats)
+        m = getattr(loop.engine, "metrics", None)
+        if m is not None:
+            out.update(m.summary())
+        return out
 
     @app.post("/v1/completions")
     def completions(req: CompletionRequest):

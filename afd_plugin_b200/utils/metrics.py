@@ -1,0 +1,56 @@
+"""Per-step serving metrics: rolling summary and optional JSONL stream.
+
+``AFD_METRICS_JSONL=<path>`` appends one JSON object per engine step
+(phase, batch, generated tokens, step milliseconds, host<->device bytes).
+``StepMetrics.summary()`` gives tokens/s and p50 / p90 step time over the
+recorded decode steps.  Step times are host wall-clock around a step that
+ends with the device->host read of its tokens, so they include the device
+work; benchmark numbers come from CUDA events in ``bench.py`` instead.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import time
+
+
+class StepMetrics:
+    def __init__(self, path: str | None = None, *, keep: int = 100_000):
+        self.path = path if path is not None else os.environ.get("AFD_METRICS_JSONL") or None
+        self.keep = keep
+        self.decode_ms: list[float] = []
+        self.decode_tokens = 0
+        self.steps = 0
+        self._fh = open(self.path, "a", buffering=1) if self.path else None  # noqa: SIM115
+
+    def record(self, *, phase: str, batch: int, tokens: int, ms: float, h2d_bytes: int = 0,
+               d2h_bytes: int = 0) -> None:
+        self.steps += 1
+        if phase == "decode":
+            self.decode_tokens += tokens
+            self.decode_ms.append(ms)
+            if len(self.decode_ms) > self.keep:
+                self.decode_ms = self.decode_ms[-self.keep :]
+        if self._fh is not None:
+            self._fh.write(json.dumps({"step": self.steps, "phase": phase, "batch": batch, "tokens": tokens,
+                                       "ms": round(ms, 4), "h2d_bytes": h2d_bytes, "d2h_bytes": d2h_bytes,
+                                       "t": round(time.time(), 6)}) + "\n")
+
+    def summary(self) -> dict:
+        ms = sorted(self.decode_ms)
+        if not ms:
+            return {"steps": self.steps, "decode_steps": 0}
+        pick = lambda q: ms[min(len(ms) - 1, int(q * (len(ms) - 1) + 0.5))]  # noqa: E731
+        total_s = sum(ms) / 1e3
+        return {"steps": self.steps, "decode_steps": len(ms), "decode_tokens": self.decode_tokens,
+                "decode_tok_per_s": round(self.decode_tokens / total_s, 2) if total_s > 0 else 0.0,
+                "p50_step_ms": round(pick(0.5), 4), "p90_step_ms": round(pick(0.9), 4)}
+
+    def close(self) -> None:
+        if self._fh is not None:
+            self._fh.close()
+            self._fh = None
+
+
+__all__ = ["StepMetrics"]
