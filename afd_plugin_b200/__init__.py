@@ -34,8 +34,17 @@ MODEL_ALIASES: dict[str, str] = {
     "DeepseekV2ForCausalLM": "AFDDeepseekV2ForCausalLM",
     "DeepseekV3ForCausalLM": "AFDDeepseekV3ForCausalLM",
     "DeepseekV32ForCausalLM": "AFDDeepseekV32ForCausalLM",
+    "DeepseekV4ForCausalLM": "AFDDeepseekV4ForCausalLM",
     "GlmMoeDsaForCausalLM": "AFDGlmMoeDsaForCausalLM",
     "Qwen3MoeForCausalLM": "AFDQwen3MoeForCausalLM",
+    "Qwen3_5MoeForConditionalGeneration": "AFDQwen3_5MoeForConditionalGeneration",
+    "Qwen3_5MoeForCausalLM": "AFDQwen3_5MoeForCausalLM",
+    "Qwen3NextForCausalLM": "AFDQwen3NextForCausalLM",
+}
+# Aliases whose wrapper class carries another name.
+_ALIAS_CLASS = {
+    "AFDDeepseekV32ForCausalLM": "AFDDeepseekV3ForCausalLM",
+    "AFDQwen3_5MoeForConditionalGeneration": "AFDQwen3_5MoeForCausalLM",
 }
 
 _REGISTERED = False
@@ -73,7 +82,7 @@ def register_afd() -> dict[str, str]:
     from afd_plugin_b200.models import MODEL_REGISTRY
 
     for arch, alias in MODEL_ALIASES.items():
-        MODEL_REGISTRY.setdefault(alias, MODEL_REGISTRY[arch] if arch in MODEL_REGISTRY else MODEL_REGISTRY["DeepseekV3ForCausalLM"])
+        MODEL_REGISTRY.setdefault(alias, MODEL_REGISTRY[arch])
     try:  # optional: publish into vLLM when present
         from vllm import ModelRegistry  # type: ignore
 
@@ -88,7 +97,7 @@ def register_afd() -> dict[str, str]:
 
 
 def _class_name(alias: str) -> str:
-    return "AFDDeepseekV3ForCausalLM" if alias == "AFDDeepseekV32ForCausalLM" else alias
+    return _ALIAS_CLASS.get(alias, alias)
 
 
 __all__ = ["MODEL_ALIASES", "__version__", "register_afd", *_LAZY]
