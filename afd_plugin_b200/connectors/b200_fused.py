@@ -616,5 +616,10 @@ class FusedFFNRunner:
         self._graphs.clear()
         self._pool = None
 
+    def reload_weights(self, checkpoint: str | None = None, *, seed: int = 0) -> None:
+        """Reload the expert weights in place between steps; captured graphs stay valid."""
+        self.model.reload_weights(checkpoint, seed=seed)
+        self._prepare_weights()
+
 
 __all__ = ["B200FusedAFDConnector", "B200FusedExtraInfo", "FusedAttentionExecutor", "FusedFFNRunner", "FusedLayout"]

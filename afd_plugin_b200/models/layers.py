@@ -442,8 +442,13 @@ class MoEGate(nn.Module):
     def finalize(self) -> None:
         """fp32 copy of the gate: router logits are computed in fp32 on every path
         (the fused dispatch kernel accumulates them in fp32 too), so routing
-        decisions agree between colocated and disaggregated runs."""
-        self.weight_f32 = self.weight.detach().float()
+        decisions agree between colocated and disaggregated runs.  A reload
+        refreshes the copy in place."""
+        w = getattr(self, "weight_f32", None)
+        if w is not None and w.shape == self.weight.shape and w.device == self.weight.device:
+            w.copy_(self.weight.detach())
+        else:
+            self.weight_f32 = self.weight.detach().float()
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         if h.is_cuda and h.dtype == self.weight.dtype == torch.bfloat16:

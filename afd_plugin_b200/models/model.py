@@ -324,6 +324,28 @@ class AFDCausalLM(nn.Module):
     def _attn_specs(self, p: str, attn) -> Iterator[ParamSpec]:
         raise NotImplementedError
 
+    def reload_weights(self, checkpoint: str | None = None, *, seed: int = 0) -> None:
+        """Reload every parameter of this role in place.
+
+        ``checkpoint`` is an HF safetensors directory; without one the seeded
+        random init runs again.  Parameters keep their storage, so CUDA graphs
+        captured against them, the fused connector's cached weight views and
+        peer-visible pointers stay valid.  Counterpart of the FFN runner's
+        ``reload_weights`` (``afd_plugin/v1/worker/ffn_model_runner.py:288-291``),
+        which rebuilds the model instead.
+        """
+        ptrs = {id(p): p.data_ptr() for p in self.parameters()}
+        if checkpoint is None:
+            self.init_random(seed)
+        else:
+            from afd_plugin_b200.models.loader import load_checkpoint
+
+            load_checkpoint(self, checkpoint)
+        self.finalize_weights()
+        moved = [p for p in self.parameters() if ptrs.get(id(p)) != p.data_ptr()]
+        if moved:
+            raise RuntimeError(f"reload_weights reallocated {len(moved)} parameters")
+
     def finalize_weights(self) -> None:
         """Derived layouts after loading (shared experts packed as virtual experts)."""
         for layer in self.layers:

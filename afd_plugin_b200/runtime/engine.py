@@ -219,6 +219,10 @@ class LLMEngine:
         self.profiler.step()
         return out
 
+    def reload_weights(self, checkpoint: str | None = None, *, seed: int = 0) -> None:
+        """Reload this engine's weights in place between steps; captured decode graphs stay valid."""
+        self.model.reload_weights(checkpoint, seed=seed)
+
     def close(self) -> None:
         """Flush an active profiler trace and the metrics stream."""
         self.profiler.close()

@@ -203,5 +203,12 @@ class FFNModelRunner:
         self._graphs.clear()
         self._pool = None
 
+    def reload_weights(self, checkpoint: str | None = None, *, seed: int = 0) -> None:
+        """Reload the FFN weights in place between steps (``ffn_model_runner.py:288-291``).
+
+        Parameters keep their storage, so cached graphs replay the new weights.
+        """
+        self.model.reload_weights(checkpoint, seed=seed)
+
 
 __all__ = ["FFNModelRunner"]

@@ -115,6 +115,12 @@ class AFDAttentionWorker(_WorkerBase):
         coord = AttentionCoordinator(self.groups.attention_group, A, self.role_rank)
         self.engine = LLMEngine(engine_config, self.model, executor, coordinator=coord)
 
+    def reload_weights(self, checkpoint: str | None = None, *, seed: int | None = None) -> None:
+        """Reload the Attention-side weights in place from ``checkpoint`` (default: the configured source)."""
+        mc = self.config.model_config
+        self.model.reload_weights(checkpoint if checkpoint is not None else mc.checkpoint,
+                                  seed=mc.seed if seed is None else seed)
+
     def shutdown(self) -> None:
         """Stop the FFN loops (control senders only) and release graphs."""
         self.engine.runner.release_graphs()
@@ -190,6 +196,14 @@ class AFDFFNWorker(_WorkerBase):
         self._thread = None
         self._stop = None
         self.raise_ffn_loop_error_if_any()
+
+    def reload_weights(self, checkpoint: str | None = None, *, seed: int | None = None) -> None:
+        """Reload the FFN weights in place; the serving loop must be stopped (no step in flight)."""
+        if self.is_loop_alive():
+            raise RuntimeError("stop the FFN server loop before reloading weights")
+        mc = self.config.model_config
+        self.model_runner.reload_weights(checkpoint if checkpoint is not None else mc.checkpoint,
+                                         seed=mc.seed if seed is None else seed)
 
     def shutdown(self) -> None:
         self.stop_ffn_server_loop()

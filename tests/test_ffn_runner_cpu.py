@@ -240,3 +240,29 @@ def test_ffn_worker_rejects_scheduler_driven_execute_model():
     worker = object.__new__(AFDFFNWorker)
     with pytest.raises(RuntimeError, match="connector-driven"):
         worker.execute_model(None)
+
+
+def test_reload_weights_delegates_and_worker_refuses_while_serving():
+    from afd_plugin_b200.runtime.workers import AFDFFNWorker
+
+    model = FakeModel()
+    seen = []
+    model.reload_weights = lambda ckpt, seed=0: seen.append((ckpt, seed))
+    runner = FFNModelRunner(model, FakeConnector(), _cfg())
+    runner.reload_weights("/ckpt", seed=3)
+    assert seen == [("/ckpt", 3)]
+
+    worker = object.__new__(AFDFFNWorker)
+    worker.config = SimpleNamespace(model_config=SimpleNamespace(checkpoint=None, seed=11))
+    worker.model_runner = runner
+    release = threading.Event()
+    worker._thread = threading.Thread(target=release.wait, daemon=True)
+    worker._thread.start()
+    try:
+        with pytest.raises(RuntimeError, match="stop the FFN server loop"):
+            worker.reload_weights()
+    finally:
+        release.set()
+        worker._thread.join()
+    worker.reload_weights()
+    assert seen[-1] == (None, 11)

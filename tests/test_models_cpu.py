@@ -134,3 +134,51 @@ def test_hf_config_parse_dsv3():
           "quantization_config": {"quant_method": "fp8", "weight_block_size": [128, 128]}}
     a = ModelArchConfig.from_hf_config(hf)
     assert a.quant == "fp8_block" and a.is_moe_layer(3) and not a.is_moe_layer(2) and a.n_group == 8
+
+
+@pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-qwen3.5", "tiny-dsv4"])
+def test_reload_weights_in_place(preset):
+    arch = get_preset(preset)
+    m = build_model(arch, role="colocated", dtype=torch.float32, seed=1)
+    ptrs = [p.data_ptr() for p in m.parameters()]
+    m.reload_weights(seed=2)
+    assert [p.data_ptr() for p in m.parameters()] == ptrs
+    fresh = build_model(arch, role="colocated", dtype=torch.float32, seed=2)
+    for (n, a), (_, b) in zip(m.named_parameters(), fresh.named_parameters()):
+        assert torch.equal(a, b), n
+    moe = next(l.mlp for l in m.layers if hasattr(l.mlp, "experts"))
+    if moe.gate is not None:
+        assert torch.equal(moe.gate.weight_f32, fresh_gate(fresh).weight_f32)
+
+
+def fresh_gate(model):
+    return next(l.mlp for l in model.layers if hasattr(l.mlp, "experts")).gate
+
+
+
+def test_reload_weights_from_checkpoint_on_split_roles(tmp_path):
+    from safetensors.torch import save_file
+
+    arch = get_preset("tiny-dsv2")
+    src = build_model(arch, role="colocated", dtype=torch.float32, seed=7)
+    tensors = {}
+    for spec in src.param_specs():
+        gen = torch.Generator().manual_seed(zlib_crc(spec.name))
+        tensors[spec.name] = torch.randn(spec.shape, generator=gen) * 0.02
+    save_file(tensors, str(tmp_path / "model.safetensors"))
+    ffn = build_model(arch, role="ffn", dtype=torch.float32, seed=0, ep_rank=1, ep_size=2)
+    ptrs = [p.data_ptr() for p in ffn.parameters()]
+    ffn.reload_weights(str(tmp_path))
+    assert [p.data_ptr() for p in ffn.parameters()] == ptrs
+    ref = build_model(arch, role="ffn", dtype=torch.float32, checkpoint=str(tmp_path), ep_rank=1, ep_size=2)
+    for (n, a), (_, b) in zip(ffn.named_parameters(), ref.named_parameters()):
+        assert torch.equal(a, b), n
+    # packed shared-expert slots follow the reloaded shared expert
+    ex = ffn.layers[1].mlp.experts
+    assert torch.equal(ex.w13_all[ex.n_local:], ref.layers[1].mlp.experts.w13_all[ex.n_local:])
+
+
+def zlib_crc(name: str) -> int:
+    import zlib
+
+    return zlib.crc32(name.encode()) & 0xFFFF
