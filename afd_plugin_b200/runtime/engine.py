@@ -45,6 +45,7 @@ class Request:
     output: list[int] = field(default_factory=list)
     blocks: list[int] = field(default_factory=list)
     state_slot: int = -1  # linear-attention state row (Gated DeltaNet models)
+    hold_kv: bool = False  # keep the cache rows after finishing, for export to a decode engine
 
     @property
     def num_tokens(self) -> int:
@@ -105,6 +106,10 @@ class LLMEngine:
         self.waiting: list[Request] = []
         self.running: list[Request] = []
         self.finished: dict[int, Request] = {}
+        # Prefill -> decode hand-off: finished requests whose cache rows are kept
+        # for export, and imported requests waiting for a batch slot.
+        self.held: dict[int, tuple[Request, float]] = {}
+        self._kv_waiting: list[tuple[Request, object]] = []
         pin = self.device.type == "cuda"
         mk = lambda *s, dt: torch.zeros(*s, dtype=dt, pin_memory=pin)  # noqa: E731
         self._h_ids = mk(self.max_batch, dt=torch.int32)
@@ -140,12 +145,85 @@ class LLMEngine:
             if size <= self.max_batch:
                 self.runner.capture(size)
 
-    def add_request(self, prompt: list[int], max_tokens: int) -> int:
+    def add_request(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False) -> int:
+        """Queue a request; with ``hold_kv`` its cache rows outlive it until :meth:`export_kv`."""
         if len(prompt) + max_tokens > self.config.model_config.max_model_len:
             raise ValueError("prompt + max_tokens exceeds max_model_len")
-        req = Request(next(self._ids), list(prompt), max_tokens)
+        req = Request(next(self._ids), list(prompt), max_tokens, hold_kv=hold_kv)
         self.waiting.append(req)
         return req.req_id
+
+    # -------------------------------------------- prefill -> decode hand-off
+    def export_kv(self, req_id: int) -> bytes:
+        """Serialise a held request's cache rows and recurrent state, then free them."""
+        from afd_plugin_b200.runtime import kv_transfer as kt
+
+        req, _ = self.held.pop(req_id)
+        try:
+            n = req.num_tokens - 1
+            tensors = kt.export_request_state(self.kv, req.blocks, n, req.state_slot)
+            tokens = (req.prompt + req.output)[:n]
+            return kt.pack(kt.RequestState(tokens, req.output[-1], len(req.prompt), tensors))
+        finally:
+            self._release(req)
+
+    def release_kv(self, req_id: int) -> bool:
+        """Drop a held request's cache rows without exporting them."""
+        entry = self.held.pop(req_id, None)
+        if entry is not None:
+            self._release(entry[0])
+        return entry is not None
+
+    def expire_held(self, max_age_s: float) -> list[int]:
+        """Release held cache rows older than ``max_age_s`` (a decode side that never fetched)."""
+        now = time.monotonic()
+        old = [rid for rid, (_, t) in self.held.items() if now - t > max_age_s]
+        for rid in old:
+            self.release_kv(rid)
+        return old
+
+    def add_prefilled_request(self, blob: bytes, max_tokens: int, *,
+                              prompt: list[int] | None = None) -> tuple[int, list[int]]:
+        """Queue a request whose prompt was prefilled elsewhere (payload from :meth:`export_kv`).
+
+        The request joins the running batch at the next step with a free slot;
+        its first decode step feeds the exporter's next token.  ``prompt``, when
+        given, must equal the payload's prompt.  Returns the request id and the
+        token ids whose cache rows came with the payload.
+        """
+        from afd_plugin_b200.runtime import kv_transfer as kt
+
+        state = kt.unpack(blob)
+        if prompt is not None and state.tokens[: state.prompt_len] != list(prompt):
+            raise ValueError("the KV payload was prefilled for a different prompt")
+        n = len(state.tokens)
+        if n + max_tokens > self.config.model_config.max_model_len:
+            raise ValueError("prefilled tokens + max_tokens exceeds max_model_len")
+        if max_tokens < 1:
+            raise ValueError("max_tokens must be positive")
+        geo = kt.geometry(self.kv)
+        for name, t in state.tensors.items():
+            if name not in geo:
+                raise ValueError(f"KV payload carries tensors this engine has no cache for: {name!r}")
+        req = Request(next(self._ids), state.tokens, max_tokens)
+        req.output.append(state.next_token)
+        self._kv_waiting.append((req, state))
+        return req.req_id, state.tokens
+
+    def _admit_prefilled(self) -> None:
+        from afd_plugin_b200.runtime import kv_transfer as kt
+
+        while self._kv_waiting and len(self.running) < self.max_batch:
+            req, state = self._kv_waiting.pop(0)
+            n = len(state.tokens)
+            self._ensure_blocks(req, n + 1)
+            req.state_slot = self._free_state_slots.pop()
+            try:
+                kt.import_request_state(self.kv, req.blocks, req.state_slot, state.tensors, n)
+            except ValueError:
+                self._release(req)
+                raise
+            (self._finish(req) if req.finished else self.running.append(req))
 
     def admit_prefilled(self, prompts: list[list[int]], first_tokens: list[int], *, reserve_tokens: int = 0) -> list[int]:
         """Admit requests whose prompt KV is already in the cache (decode-only mode).
@@ -194,19 +272,25 @@ class LLMEngine:
         return n
 
     def has_unfinished(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self._kv_waiting)
 
     def _ensure_blocks(self, req: Request, upto_tokens: int) -> None:
         need = math.ceil(upto_tokens / self.block_size) - len(req.blocks)
         if need > 0:
             req.blocks.extend(self.kv.allocator.allocate(need))
 
-    def _finish(self, req: Request) -> None:
+    def _release(self, req: Request) -> None:
         self.kv.allocator.free(req.blocks)
         req.blocks = []
         if req.state_slot >= 0:
             self._free_state_slots.append(req.state_slot)
             req.state_slot = -1
+
+    def _finish(self, req: Request) -> None:
+        if req.hold_kv:
+            self.held[req.req_id] = (req, time.monotonic())
+        else:
+            self._release(req)
         self.finished[req.req_id] = req
 
     # ---------------------------------------------------------------- step
@@ -229,6 +313,10 @@ class LLMEngine:
         self.metrics.close()
 
     def _step(self) -> dict[int, int]:
+        if self._kv_waiting:
+            self._admit_prefilled()
+            if not (self.waiting or self.running) and self.coordinator.size == 1:
+                return {}  # every imported request finished on its transferred token
         admit = []
         while self.waiting and len(self.running) + len(admit) < self.max_batch:
             admit.append(self.waiting.pop(0))

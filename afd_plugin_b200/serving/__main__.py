@@ -49,7 +49,8 @@ def main(argv=None) -> None:
                           max_num_seqs=args.max_num_seqs)
         engine = LLMEngine.colocated(ec, device="cuda" if torch.cuda.is_available() else "cpu")
         loop = EngineLoop(engine).start()
-        uvicorn.run(build_app(loop), host=args.host, port=args.port)
+        uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
+                    port=args.port)
         return
 
     import torch.distributed as dist
@@ -82,7 +83,8 @@ def main(argv=None) -> None:
         w.engine.capture_graphs()
     loop = EngineLoop(w.engine, group=w.groups.attention_group, world=A, rank=role_rank).start()
     if role_rank == 0:
-        uvicorn.run(build_app(loop), host=args.host, port=args.port)
+        uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
+                    port=args.port)
     else:
         loop.join()
 

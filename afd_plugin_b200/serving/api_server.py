@@ -9,7 +9,17 @@ them has work, so all of them step together (the coordinator pads idle ranks
 with a placeholder row, as the reference's DP dummy batches do).
 
 Endpoints: ``GET /health``, ``GET /metrics`` (engine counters),
-``POST /v1/completions`` with ``{"prompt": str | [int], "max_tokens": int}``.
+``POST /v1/completions`` with ``{"prompt": str | [int], "max_tokens": int}``,
+and for prefill -> decode disaggregation ``GET`` / ``DELETE /v1/kv/{id}``.
+
+Disaggregated prefill uses the request field ``kv_transfer_params`` with the
+keys of the reference's proxy tool (``tools/proxy_server.py:850-867``):
+``{"do_remote_decode": true}`` makes this server prefill, keep the request's
+cache rows and answer with ``kv_transfer_params`` naming where to fetch them;
+``{"do_remote_prefill": true, "remote_request_id", "remote_host",
+"remote_port"}`` makes it pull those rows (``runtime/kv_transfer.py``) and
+decode from the transferred token on.
+
 Without a tokenizer in the image, text is mapped to token ids byte by byte
 (``byte_tokenize``), which keeps the server usable for smoke tests and
 benchmark drivers that send token ids directly.
@@ -31,6 +41,7 @@ class CompletionRequest(BaseModel):
     prompt: str | list[int]
     max_tokens: int = 16
     model: str | None = None
+    kv_transfer_params: dict | None = None
 
 
 def byte_tokenize(text: str, vocab_size: int) -> list[int]:
@@ -47,6 +58,8 @@ class _Pending:
     max_tokens: int
     future: Future
     submitted: float = field(default_factory=time.perf_counter)
+    hold_kv: bool = False
+    kv_blob: bytes | None = None  # prefilled elsewhere: the exported cache rows
 
 
 class EngineLoop:
@@ -56,11 +69,14 @@ class EngineLoop:
     together (None for a single engine).
     """
 
-    def __init__(self, engine, *, group=None, world: int = 1, rank: int = 0, idle_sleep_s: float = 0.001):
+    def __init__(self, engine, *, group=None, world: int = 1, rank: int = 0, idle_sleep_s: float = 0.001,
+                 kv_hold_timeout_s: float = 120.0):
         self.engine = engine
         self.group, self.world, self.rank = group, world, rank
         self.idle_sleep_s = idle_sleep_s
+        self.kv_hold_timeout_s = kv_hold_timeout_s
         self._queue: list[_Pending] = []
+        self._calls: list[tuple[object, Future]] = []
         self._lock = threading.Lock()
         self._inflight: dict[int, _Pending] = {}
         self._stop = threading.Event()
@@ -69,14 +85,34 @@ class EngineLoop:
         self.stats = {"requests": 0, "completed": 0, "generated_tokens": 0, "steps": 0, "ttft_s_sum": 0.0}
 
     # ------------------------------------------------------------ clients
-    def submit(self, prompt: list[int], max_tokens: int) -> Future:
+    def submit(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False) -> Future:
+        """Queue a request; the future resolves with its tokens and carries ``req_id`` once admitted."""
         limit = self.engine.config.model_config.max_model_len
         if len(prompt) + int(max_tokens) > limit:
             raise ValueError(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds max_model_len {limit}")
+        if self.error is not None:
+            raise RuntimeError("engine loop has failed") from self.error
         fut: Future = Future()
         with self._lock:
-            self._queue.append(_Pending(list(prompt), int(max_tokens), fut))
+            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, hold_kv=hold_kv))
             self.stats["requests"] += 1
+        return fut
+
+    def submit_prefilled(self, prompt: list[int], kv_blob: bytes, max_tokens: int) -> Future:
+        """Queue a request whose prompt was prefilled by another engine (see ``export_kv``)."""
+        if self.error is not None:
+            raise RuntimeError("engine loop has failed") from self.error
+        fut: Future = Future()
+        with self._lock:
+            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob))
+            self.stats["requests"] += 1
+        return fut
+
+    def call(self, fn) -> Future:
+        """Run ``fn(engine)`` on the loop thread between steps (engine state is not thread-safe)."""
+        fut: Future = Future()
+        with self._lock:
+            self._calls.append((fn, fut))
         return fut
 
     # --------------------------------------------------------------- loop
@@ -113,8 +149,24 @@ class EngineLoop:
             while True:
                 with self._lock:
                     new, self._queue = self._queue, []
+                    calls, self._calls = self._calls, []
+                for fn, fut in calls:
+                    try:
+                        fut.set_result(fn(eng))
+                    except Exception as exc:  # noqa: BLE001 - handed to the caller
+                        fut.set_exception(exc)
+                if eng.held:
+                    eng.expire_held(self.kv_hold_timeout_s)
                 for p in new:
-                    rid = eng.add_request(p.prompt, p.max_tokens)
+                    try:
+                        if p.kv_blob is not None:
+                            rid, _ = eng.add_prefilled_request(p.kv_blob, p.max_tokens, prompt=p.prompt)
+                        else:
+                            rid = eng.add_request(p.prompt, p.max_tokens, hold_kv=p.hold_kv)
+                    except ValueError as exc:
+                        p.future.set_exception(exc)
+                        continue
+                    p.future.req_id = rid
                     self._inflight[rid] = p
                 work, stop = self._agree(eng.has_unfinished(), self._stop.is_set())
                 if stop:
@@ -135,14 +187,50 @@ class EngineLoop:
             for p in list(self._inflight.values()) + self._queue:
                 if not p.future.done():
                     p.future.set_exception(exc)
+            for _, fut in self._calls:
+                if not fut.done():
+                    fut.set_exception(exc)
 
 
-def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout_s: float = 600.0):
-    """FastAPI app serving ``loop`` (rank 0 of the Attention side)."""
+def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout_s: float = 600.0,
+              advertise_host: str = "127.0.0.1", advertise_port: int = 8000):
+    """FastAPI app serving ``loop`` (rank 0 of the Attention side).
+
+    ``advertise_host`` / ``advertise_port`` are what a prefill answer tells the
+    decode server to fetch the cache rows from.
+    """
+    import requests
     from fastapi import FastAPI, HTTPException
+    from fastapi.responses import Response
 
     vocab = loop.engine.model.arch.vocab_size
     app = FastAPI(title="afd_plugin_b200")
+
+    def _fetch_kv(params: dict) -> bytes:
+        try:
+            url = f"http://{params['remote_host']}:{int(params['remote_port'])}/v1/kv/{int(params['remote_request_id'])}"
+        except (KeyError, TypeError, ValueError) as exc:
+            raise HTTPException(status_code=400, detail=f"incomplete kv_transfer_params: {exc}") from exc
+        try:
+            r = requests.get(url, timeout=request_timeout_s)
+        except requests.RequestException as exc:
+            raise HTTPException(status_code=502, detail=f"KV fetch from {url} failed: {exc}") from exc
+        if r.status_code != 200:
+            raise HTTPException(status_code=502, detail=f"KV fetch from {url}: HTTP {r.status_code}")
+        return r.content
+
+    @app.get("/v1/kv/{req_id}")
+    def get_kv(req_id: int):
+        try:
+            blob = loop.call(lambda eng: eng.export_kv(req_id)).result(timeout=request_timeout_s)
+        except KeyError as exc:
+            raise HTTPException(status_code=404, detail=f"no held KV for request {req_id}") from exc
+        return Response(content=blob, media_type="application/octet-stream")
+
+    @app.delete("/v1/kv/{req_id}")
+    def drop_kv(req_id: int):
+        released = loop.call(lambda eng: eng.release_kv(req_id)).result(timeout=request_timeout_s)
+        return {"released": bool(released)}
 
     @app.get("/health")
     def health():
@@ -165,16 +253,28 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         ids = req.prompt if isinstance(req.prompt, list) else byte_tokenize(req.prompt, vocab)
         if any((not isinstance(t, int)) or t < 0 or t >= vocab for t in ids):
             raise HTTPException(status_code=400, detail=f"prompt token ids must be in [0, {vocab})")
+        params = req.kv_transfer_params or {}
+        prefill_only = bool(params.get("do_remote_decode"))
         try:
-            out = loop.submit(ids, req.max_tokens).result(timeout=request_timeout_s)
+            if params.get("do_remote_prefill"):
+                fut = loop.submit_prefilled(ids, _fetch_kv(params), req.max_tokens)
+            else:
+                fut = loop.submit(ids, req.max_tokens, hold_kv=prefill_only)
+            out = fut.result(timeout=request_timeout_s)
         except ValueError as exc:
             raise HTTPException(status_code=400, detail=str(exc)) from exc
-        return {
+        body = {
             "object": "text_completion",
             "model": req.model or model_name,
             "choices": [{"index": 0, "token_ids": out, "text": byte_detokenize(out), "finish_reason": "length"}],
             "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)},
         }
+        if prefill_only:
+            body["kv_transfer_params"] = {
+                "do_remote_prefill": True, "do_remote_decode": False,
+                "remote_request_id": fut.req_id, "remote_host": advertise_host, "remote_port": advertise_port,
+            }
+        return body
 
     return app
 

@@ -1,13 +1,24 @@
-"""Load-balancing proxy in front of several completion servers.
+"""Load-balancing proxy in front of completion servers, with prefill -> decode disaggregation.
 
-Routes each ``POST /v1/completions`` to the backend with the fewest requests
-in flight (ties: round robin) and forwards the JSON answer; ``GET /health``
-reports the backends.  The counterpart of the reference's proxy tool
-(``tools/proxy_server.py``) for data-parallel serving instances; the
-prefill -> decode KV hand-off that tool also drives (through LMCache) is not
-part of this framework.
+Two modes, the ones of the reference's proxy tool (``tools/proxy_server.py``):
+
+* ``--backends``: each ``POST /v1/completions`` goes to the backend with the
+  least load in flight (ties: round robin) and the JSON answer is forwarded.
+* ``--prefill`` + ``--decode``: the request first runs on a prefill server with
+  ``max_tokens=1`` and ``kv_transfer_params={"do_remote_decode": true}``
+  (the prefill leg of ``tools/proxy_server.py:850-867``); that server keeps the
+  request's cache rows and answers with where to fetch them.  The original
+  request then goes to a decode server with those ``kv_transfer_params``; it
+  pulls the rows and decodes.  If the decode leg fails, the proxy asks the
+  prefill server to drop the held rows.
+
+Load is counted in prompt tokens for prefill servers and in requested tokens
+for decode servers, so long prompts spread over the prefill pool the way the
+reference's length-based scores do (``tools/proxy_server.py:205-211``).
+``GET /health`` reports every backend.
 
     python -m afd_plugin_b200.serving.proxy --backends http://127.0.0.1:8001,http://127.0.0.1:8002 --port 8000
+    python -m afd_plugin_b200.serving.proxy --prefill http://127.0.0.1:8001 --decode http://127.0.0.1:8002
 """
 
 from __future__ import annotations
@@ -26,69 +37,143 @@ class Balancer:
             raise ValueError("the proxy needs at least one backend")
         self.backends = [b.rstrip("/") for b in backends]
         self.inflight = {b: 0 for b in self.backends}
+        self.load = {b: 0.0 for b in self.backends}
         self.served = {b: 0 for b in self.backends}
         self._rr = itertools.cycle(range(len(self.backends)))
         self._lock = threading.Lock()
 
-    def acquire(self) -> str:
+    def acquire(self, load: float = 1.0) -> str:
         with self._lock:
             start = next(self._rr)
             order = self.backends[start:] + self.backends[:start]
-            b = min(order, key=lambda x: self.inflight[x])
+            b = min(order, key=lambda x: (self.load[x], self.inflight[x]))
             self.inflight[b] += 1
+            self.load[b] += load
             return b
 
-    def release(self, b: str) -> None:
+    def release(self, b: str, load: float = 1.0) -> None:
         with self._lock:
             self.inflight[b] -= 1
+            self.load[b] = max(0.0, self.load[b] - load)
             self.served[b] += 1
 
+    def snapshot(self) -> dict:
+        with self._lock:
+            return {"inflight": dict(self.inflight), "served": dict(self.served)}
 
-def build_proxy_app(backends: list[str], *, timeout_s: float = 600.0):
+
+def _prompt_len(body: dict) -> int:
+    p = body.get("prompt", "")
+    return max(1, len(p) if isinstance(p, list) else len(str(p).encode("utf-8")))
+
+
+def build_prefill_request(body: dict) -> dict:
+    """The prefill leg: one token, cache rows held for a decode server."""
+    out = dict(body)
+    out["kv_transfer_params"] = {"do_remote_decode": True, "do_remote_prefill": False}
+    out["max_tokens"] = 1
+    out["stream"] = False
+    return out
+
+
+def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | None = None,
+                    decode: list[str] | None = None, timeout_s: float = 600.0):
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import JSONResponse
 
-    bal = Balancer(backends)
+    pd = bool(prefill or decode)
+    if pd and not (prefill and decode):
+        raise ValueError("disaggregated mode needs both prefill and decode servers")
+    if pd and backends:
+        raise ValueError("give either backends or prefill + decode servers")
+    pools = {"prefill": Balancer(prefill), "decode": Balancer(decode)} if pd else {"backend": Balancer(backends or [])}
     app = FastAPI(title="afd_plugin_b200 proxy")
-    app.state.balancer = bal
+    app.state.pools = pools
+    app.state.balancer = pools.get("backend")
+
+    def _post(url: str, body: dict):
+        try:
+            return requests.post(url, json=body, timeout=timeout_s)
+        except requests.RequestException as exc:
+            raise HTTPException(status_code=502, detail=f"backend {url} failed: {exc}") from exc
+
+    def _plain(body: dict):
+        bal = pools["backend"]
+        b = bal.acquire()
+        try:
+            r = _post(b + "/v1/completions", body)
+        finally:
+            bal.release(b)
+        return r.status_code, r.json()
+
+    def _disaggregated(body: dict):
+        pre, dec = pools["prefill"], pools["decode"]
+        n_prompt = float(_prompt_len(body))
+        p = pre.acquire(n_prompt)
+        try:
+            r1 = _post(p + "/v1/completions", build_prefill_request(body))
+        finally:
+            pre.release(p, n_prompt)
+        if r1.status_code != 200:
+            return r1.status_code, r1.json()
+        params = r1.json().get("kv_transfer_params")
+        if not params:
+            raise HTTPException(status_code=502, detail=f"prefill server {p} returned no kv_transfer_params")
+        n_dec = float(body.get("max_tokens", 16))
+        d = dec.acquire(n_dec)
+        ok = False
+        try:
+            r2 = _post(d + "/v1/completions", dict(body, kv_transfer_params=params))
+            ok = r2.status_code == 200
+        finally:
+            dec.release(d, n_dec)
+            if not ok:  # the decode side never fetched the rows: free them now
+                try:
+                    requests.delete(f"{p}/v1/kv/{params['remote_request_id']}", timeout=10)
+                except requests.RequestException:
+                    pass
+        return r2.status_code, r2.json()
 
     @app.get("/health")
     def health():
-        status = {}
-        for b in bal.backends:
-            try:
-                status[b] = requests.get(b + "/health", timeout=2).ok
-            except requests.RequestException:
-                status[b] = False
-        return {"backends": status, "inflight": dict(bal.inflight), "served": dict(bal.served)}
+        out = {}
+        for name, bal in pools.items():
+            status = {}
+            for b in bal.backends:
+                try:
+                    status[b] = requests.get(b + "/health", timeout=2).ok
+                except requests.RequestException:
+                    status[b] = False
+            out[name] = dict(bal.snapshot(), backends=status)
+        if not pd:  # flat layout for the single-pool proxy
+            out = out["backend"]
+        return out
 
     @app.post("/v1/completions")
     async def completions(request: Request):
-        body = await request.json()
-        b = bal.acquire()
-        try:
-            import anyio
+        import anyio
 
-            r = await anyio.to_thread.run_sync(lambda: requests.post(b + "/v1/completions", json=body,
-                                                                     timeout=timeout_s))
-        except requests.RequestException as exc:
-            raise HTTPException(status_code=502, detail=f"backend {b} failed: {exc}") from exc
-        finally:
-            bal.release(b)
-        return JSONResponse(status_code=r.status_code, content=r.json())
+        body = await request.json()
+        code, content = await anyio.to_thread.run_sync(lambda: (_disaggregated if pd else _plain)(body))
+        return JSONResponse(status_code=code, content=content)
 
     return app
 
 
 def main(argv=None) -> None:
-    ap = argparse.ArgumentParser(description="least-loaded proxy over completion servers")
-    ap.add_argument("--backends", required=True, help="comma-separated base URLs")
+    ap = argparse.ArgumentParser(description="load-balancing / prefill-decode proxy over completion servers")
+    ap.add_argument("--backends", default="", help="comma-separated base URLs (aggregated serving)")
+    ap.add_argument("--prefill", default="", help="comma-separated prefill server URLs")
+    ap.add_argument("--decode", default="", help="comma-separated decode server URLs")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     args = ap.parse_args(argv)
     import uvicorn
 
-    uvicorn.run(build_proxy_app(args.backends.split(",")), host=args.host, port=args.port)
+    split = lambda s: [x for x in s.split(",") if x]  # noqa: E731
+    app = build_proxy_app(split(args.backends) or None, prefill=split(args.prefill) or None,
+                          decode=split(args.decode) or None)
+    uvicorn.run(app, host=args.host, port=args.port)
 
 
 if __name__ == "__main__":

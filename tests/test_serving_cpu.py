@@ -157,3 +157,61 @@ def test_proxy_balances_over_two_servers():
         s.should_exit = True
     for lp in loops:
         lp.stop()
+
+
+def _serve(app):
+    import uvicorn
+
+    port = free_port()
+    srv = uvicorn.Server(uvicorn.Config(app(port), host="127.0.0.1", port=port, log_level="warning"))
+    threading.Thread(target=srv.run, daemon=True).start()
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(400):
+        try:
+            if requests.get(url + "/health", timeout=2).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.05)
+    return srv, url
+
+
+def test_disaggregated_prefill_decode_through_proxy():
+    """Prefill server -> KV rows over HTTP -> decode server; tokens equal one engine's."""
+    from afd_plugin_b200.serving.proxy import build_proxy_app
+
+    pre_loop, dec_loop = EngineLoop(_engine()).start(), EngineLoop(_engine()).start()
+    pre, pre_url = _serve(lambda port: build_app(pre_loop, advertise_port=port))
+    dec, dec_url = _serve(lambda port: build_app(dec_loop, advertise_port=port))
+    proxy, purl = _serve(lambda port: build_proxy_app(prefill=[pre_url], decode=[dec_url]))
+    try:
+        prompts = [[5, 9, 100, 7], [42] * 6, [1, 2, 3], [900, 800]]
+        want = _engine().generate(prompts, 5)
+        with ThreadPoolExecutor(4) as ex:
+            got = list(ex.map(lambda p: requests.post(purl + "/v1/completions", json={"prompt": p, "max_tokens": 5},
+                                                      timeout=120).json()["choices"][0]["token_ids"], prompts))
+        assert got == want
+        h = requests.get(purl + "/health", timeout=10).json()
+        assert sum(h["prefill"]["served"].values()) == 4 and sum(h["decode"]["served"].values()) == 4
+        # every held row was fetched: the prefill engine holds nothing
+        assert pre_loop.call(lambda eng: len(eng.held)).result(timeout=30) == 0
+        assert dec_loop.stats["completed"] == 4 and pre_loop.stats["completed"] == 4
+
+        # a prefill leg answers with where to fetch the rows; a second fetch is a 404
+        r = requests.post(pre_url + "/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 1,
+                                                              "kv_transfer_params": {"do_remote_decode": True}},
+                          timeout=60).json()
+        params = r["kv_transfer_params"]
+        assert params["do_remote_prefill"] and params["remote_port"] == int(pre_url.rsplit(":", 1)[1])
+        bad = requests.post(dec_url + "/v1/completions", json={"prompt": [3, 4, 6], "max_tokens": 2,
+                                                                "kv_transfer_params": params}, timeout=60)
+        assert bad.status_code == 400 and "different prompt" in bad.json()["detail"]
+        again = requests.post(dec_url + "/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 2,
+                                                                  "kv_transfer_params": params}, timeout=60)
+        assert again.status_code == 502
+        assert requests.delete(f"{pre_url}/v1/kv/{params['remote_request_id']}", timeout=10).json() == \
+            {"released": False}
+    finally:
+        for s in (pre, dec, proxy):
+            s.should_exit = True
+        pre_loop.stop()
+        dec_loop.stop()
