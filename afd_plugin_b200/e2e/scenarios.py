@@ -1,0 +1,91 @@
+"""Fixed end-to-end serving scenarios.
+
+The AFD rows keep the names and topologies of the reference's scenario table
+(``tests/e2e/runner.py:361-395``: baseline, eager / graph / graph+DBO at 2A1F
+and 2A2F); the ``afd-fused-*`` rows run the NVLink-fused connector.  The
+baseline is one colocated engine (no AFD) rather than the reference's DP4
+vLLM deployment.
+"""
+
+from __future__ import annotations
+
+import json
+from dataclasses import dataclass
+
+NCCL = "P2pNcclAFDConnector"
+FUSED = "B200FusedAFDConnector"
+
+
+@dataclass(frozen=True)
+class Scenario:
+    name: str
+    baseline: bool
+    graph: bool
+    dbo: bool
+    attention_ranks: int
+    ffn_ranks: int
+    connector: str = NCCL
+
+    @property
+    def world_size(self) -> int:
+        return 1 if self.baseline else self.attention_ranks + self.ffn_ranks
+
+    @property
+    def needs_cuda(self) -> bool:
+        return self.connector == FUSED
+
+    def afd_config(self, extra: dict | None = None) -> dict:
+        if self.baseline:
+            return {}
+        cfg = {"num_attention_ranks": self.attention_ranks, "num_ffn_ranks": self.ffn_ranks,
+               "connector": self.connector}
+        if extra:
+            cfg["connector_extra_config"] = dict(extra)
+        return cfg
+
+
+def _s(name, baseline, graph, dbo, a, f, connector=NCCL) -> tuple[str, Scenario]:
+    return name, Scenario(name, baseline, graph, dbo, a, f, connector)
+
+
+SCENARIOS: dict[str, Scenario] = dict([
+    _s("baseline-eager", True, False, False, 1, 0),
+    _s("baseline-graph", True, True, False, 1, 0),
+    _s("afd-eager-1a1f", False, False, False, 1, 1),
+    _s("afd-eager-2a1f", False, False, False, 2, 1),
+    _s("afd-graph-2a1f", False, True, False, 2, 1),
+    _s("afd-graph-dbo-2a1f", False, True, True, 2, 1),
+    _s("afd-eager-2a2f", False, False, False, 2, 2),
+    _s("afd-graph-2a2f", False, True, False, 2, 2),
+    _s("afd-graph-dbo-2a2f", False, True, True, 2, 2),
+    _s("afd-fused-graph-1a1f", False, True, False, 1, 1, FUSED),
+    _s("afd-fused-graph-2a2f", False, True, False, 2, 2, FUSED),
+    _s("afd-fused-graph-dbo-2a2f", False, True, True, 2, 2, FUSED),
+    _s("afd-fused-graph-6a2f", False, True, False, 6, 2, FUSED),
+])
+
+
+def server_command(scn: Scenario, *, python: str, preset: str, port: int, master_port: int,
+                   checkpoint: str | None = None, dtype: str = "bfloat16", max_num_seqs: int = 16,
+                   max_model_len: int = 2048, capture_size: int = 8, seed: int = 0,
+                   connector_extra: dict | None = None) -> list[str]:
+    """The command line that serves ``scn`` on ``port`` (torchrun for AFD worlds)."""
+    serve = ["-m", "afd_plugin_b200.serving", "--preset", preset, "--dtype", dtype, "--port", str(port),
+             "--host", "127.0.0.1", "--max-num-seqs", str(max_num_seqs), "--max-model-len", str(max_model_len),
+             "--seed", str(seed)]
+    if checkpoint:
+        serve += ["--checkpoint", checkpoint]
+    if scn.graph:
+        serve += ["--capture-sizes", str(min(capture_size, max_num_seqs))]
+    else:
+        serve += ["--eager"]
+    if scn.dbo:
+        serve += ["--dbo"]
+    if scn.baseline:
+        return [python, *serve]
+    serve += ["--afd", json.dumps(scn.afd_config(connector_extra), separators=(",", ":"))]
+    return [python, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", str(scn.world_size),
+            "--master-addr", "127.0.0.1", "--master-port", str(master_port), *serve]
+
+
+__all__ = ["FUSED", "NCCL", "SCENARIOS", "Scenario", "server_command"]

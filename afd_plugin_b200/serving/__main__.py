@@ -27,7 +27,12 @@ def main(argv=None) -> None:
     ap.add_argument("--max-num-seqs", type=int, default=64)
     ap.add_argument("--max-model-len", type=int, default=4096)
     ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--capture-sizes", default="", help="comma-separated decode graph batch sizes "
+                    "(default: --max-num-seqs)")
+    ap.add_argument("--dbo", action="store_true", help="two-ubatch overlap of attention and FFN (AFD only)")
+    ap.add_argument("--seed", type=int, default=0, help="random-init seed when no checkpoint is given")
     args = ap.parse_args(argv)
+    sizes = [int(x) for x in args.capture_sizes.split(",") if x] or [args.max_num_seqs]
 
     import torch
     import uvicorn
@@ -44,10 +49,12 @@ def main(argv=None) -> None:
         from afd_plugin_b200.runtime.engine import LLMEngine
 
         ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=args.eager, max_model_len=args.max_model_len,
-                                      checkpoint=args.checkpoint),
-                          compilation_config=CompilationConfig(cudagraph_capture_sizes=[args.max_num_seqs]),
+                                      checkpoint=args.checkpoint, seed=args.seed),
+                          compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
                           max_num_seqs=args.max_num_seqs)
         engine = LLMEngine.colocated(ec, device="cuda" if torch.cuda.is_available() else "cpu")
+        if not args.eager and engine.device.type == "cuda":
+            engine.capture_graphs()
         loop = EngineLoop(engine).start()
         uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
                     port=args.port)
@@ -69,9 +76,10 @@ def main(argv=None) -> None:
         raise SystemExit(f"world size {world} != num_attention_ranks + num_ffn_ranks = {A + F}")
     role, role_rank = role_of_world_rank(rank, attention_size=A, ffn_size=F)
     ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=args.eager, max_model_len=args.max_model_len,
-                                  checkpoint=args.checkpoint),
-                      parallel_config=ParallelConfig(data_parallel_size=A),
-                      compilation_config=CompilationConfig(cudagraph_capture_sizes=[args.max_num_seqs]),
+                                  checkpoint=args.checkpoint, seed=args.seed),
+                      parallel_config=ParallelConfig(data_parallel_size=A, use_ubatching=args.dbo,
+                                                     num_ubatches=2 if args.dbo else 1),
+                      compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
                       additional_config={"afd": dict(afd, role=role)}, max_num_seqs=args.max_num_seqs)
     if role == "ffn":
         w = AFDFFNWorker(ec, local_rank=local)
@@ -85,8 +93,10 @@ def main(argv=None) -> None:
     if role_rank == 0:
         uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
                     port=args.port)
+        loop.stop()  # every Attention rank's loop leaves at the same iteration
     else:
         loop.join()
+    w.shutdown()  # stops the FFN ranks' serve loops
 
 
 if __name__ == "__main__":

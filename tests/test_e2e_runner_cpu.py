@@ -1,0 +1,106 @@
+"""End-to-end runner: scenario table, command lines, agreement gate, process-group teardown (CPU)."""
+
+from __future__ import annotations
+
+import json
+import sys
+import time
+
+import pytest
+
+from afd_plugin_b200.e2e import runner
+from afd_plugin_b200.e2e.process_utils import group_alive, start_server, stop_server, wait_for_health
+from afd_plugin_b200.e2e.scenarios import FUSED, NCCL, SCENARIOS, server_command
+
+
+def test_scenario_table_covers_reference_topologies():
+    for name, (graph, dbo, a, f) in {
+        "afd-eager-2a1f": (False, False, 2, 1), "afd-graph-2a1f": (True, False, 2, 1),
+        "afd-graph-dbo-2a1f": (True, True, 2, 1), "afd-eager-2a2f": (False, False, 2, 2),
+        "afd-graph-2a2f": (True, False, 2, 2), "afd-graph-dbo-2a2f": (True, True, 2, 2),
+    }.items():
+        s = SCENARIOS[name]
+        assert (s.graph, s.dbo, s.attention_ranks, s.ffn_ranks, s.connector) == (graph, dbo, a, f, NCCL)
+    assert SCENARIOS["baseline-graph"].world_size == 1
+    assert SCENARIOS["afd-fused-graph-6a2f"].world_size == 8 and SCENARIOS["afd-fused-graph-6a2f"].needs_cuda
+
+
+def test_server_commands():
+    base = server_command(SCENARIOS["baseline-graph"], python="py", preset="p", port=9, master_port=10,
+                          max_num_seqs=4, capture_size=8)
+    assert base[:3] == ["py", "-m", "afd_plugin_b200.serving"]
+    assert base[base.index("--capture-sizes") + 1] == "4" and "--afd" not in base and "--eager" not in base
+    afd = server_command(SCENARIOS["afd-graph-dbo-2a2f"], python="py", preset="p", port=9, master_port=10,
+                         checkpoint="/ckpt")
+    assert afd[1:4] == ["-m", "torch.distributed.run", "--nnodes"]
+    assert afd[afd.index("--nproc-per-node") + 1] == "4" and afd[afd.index("--master-addr") + 1] == "127.0.0.1"
+    assert "--dbo" in afd and afd[afd.index("--checkpoint") + 1] == "/ckpt"
+    cfg = json.loads(afd[afd.index("--afd") + 1])
+    assert cfg == {"num_attention_ranks": 2, "num_ffn_ranks": 2, "connector": NCCL}
+    fused = server_command(SCENARIOS["afd-fused-graph-2a2f"], python="py", preset="p", port=9, master_port=10,
+                           connector_extra={"fp8_dispatch": True})
+    cfg = json.loads(fused[fused.index("--afd") + 1])
+    assert cfg["connector"] == FUSED and cfg["connector_extra_config"] == {"fp8_dispatch": True}
+    eager = server_command(SCENARIOS["afd-eager-2a1f"], python="py", preset="p", port=9, master_port=10)
+    assert "--eager" in eager and "--capture-sizes" not in eager
+
+
+def test_compare_and_gate():
+    ref = [[1, 2, 3], [4, 5, 6], [7, 8, 9], [1, 1, 1]]
+    out = [[1, 2, 3], [4, 5, 0], [0, 8, 9], [1, 1, 1]]
+    m = runner.compare(out, ref)
+    assert m["exact_match"] == 0.5 and m["first_token_match"] == 0.75
+    assert m["mean_prefix_agreement"] == pytest.approx((1 + 2 / 3 + 0 + 1) / 4)
+    assert runner.gate(m, min_exact=0.5, min_first=0.75) == []
+    assert len(runner.gate(m, min_exact=0.9, min_first=0.9)) == 2
+    with pytest.raises(ValueError):
+        runner.compare(out[:2], ref)
+    p1 = runner.make_prompts(5, 100, seed=3)
+    assert p1 == runner.make_prompts(5, 100, seed=3) and all(0 <= t < 100 for p in p1 for t in p)
+
+
+def _py(code: str) -> list[str]:
+    return [sys.executable, "-c", code]
+
+
+def test_stop_escalates_to_kill_and_reaps_the_group(tmp_path):
+    # the leader ignores SIGTERM and has a child that also ignores it
+    code = ("import signal, subprocess, sys, time; signal.signal(signal.SIGTERM, signal.SIG_IGN); "
+            "subprocess.Popen([sys.executable, '-c', 'import signal, time; "
+            "signal.signal(signal.SIGTERM, signal.SIG_IGN); time.sleep(120)']); time.sleep(120)")
+    srv = start_server(_py(code), log_path=str(tmp_path / "log.txt"))
+    time.sleep(1.0)
+    assert group_alive(srv.pgid)
+    assert stop_server(srv, term_timeout_s=1.0, kill_timeout_s=10.0) == "killed"
+    assert not group_alive(srv.pgid)
+
+
+def test_stop_terminates_cooperative_group_and_reports_exited():
+    srv = start_server(_py("import time; time.sleep(120)"))
+    time.sleep(0.3)
+    assert stop_server(srv, term_timeout_s=10.0) == "terminated"
+    done = start_server(_py("pass"))
+    done.proc.wait(30)
+    time.sleep(0.2)
+    assert stop_server(done) == "exited"
+
+
+def test_wait_for_health_reports_an_early_exit(tmp_path):
+    srv = start_server(_py("print('boom'); raise SystemExit(3)"), log_path=str(tmp_path / "log.txt"))
+    with pytest.raises(RuntimeError, match="code 3") as ei:
+        wait_for_health(srv, "http://127.0.0.1:9", timeout_s=30, interval_s=0.05)
+    assert "boom" in str(ei.value)
+    stop_server(srv)
+
+
+def test_runner_cpu_baseline_vs_afd(tmp_path):
+    """Colocated engine and a 2A1F NCCL-connector deployment (gloo on CPU) serve identical tokens."""
+    out = tmp_path / "e2e.json"
+    rc = runner.main(["--scenarios", "baseline-eager,afd-eager-2a1f", "--preset", "tiny-dsv2", "--dtype", "float32",
+                      "--device", "cpu", "--num-prompts", "4", "--max-tokens", "4", "--max-model-len", "128",
+                      "--max-num-seqs", "4", "--min-exact-match", "1.0", "--startup-timeout", "240",
+                      "--log-dir", str(tmp_path / "logs"), "--output", str(out)])
+    assert rc == 0
+    res = json.loads(out.read_text())["results"]
+    assert res[1]["agreement"]["exact_match"] == 1.0 and res[1]["gate"] == "pass"
+    assert all(r["teardown"] in ("terminated", "killed", "exited") for r in res)
