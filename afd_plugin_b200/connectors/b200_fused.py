@@ -566,7 +566,8 @@ class FusedFFNRunner:
             g = torch.cuda.CUDAGraph()
             if self._pool is None:
                 self._pool = torch.cuda.graph_pool_handle()
-            with torch.cuda.graph(g, pool=self._pool):
+            with torch.profiler.record_function(f"ffn_capture_{self.c.dims.t_cap}_{len(stages)}"), \
+                    torch.cuda.graph(g, pool=self._pool):
                 self._step(stages)
             self._graphs[key] = g
             return

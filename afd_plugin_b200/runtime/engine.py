@@ -325,9 +325,11 @@ class LLMEngine:
         votes = self.coordinator.exchange(ntok, is_prefill)
         if any(p for _, p in votes):
             self._last_phase = "prefill"
-            return self._prefill_step(admit, votes)
+            with torch.profiler.record_function("afd_prefill_step"):
+                return self._prefill_step(admit, votes)
         self._last_phase = "decode"
-        return self._decode_step(votes)
+        with torch.profiler.record_function("afd_decode_step"):
+            return self._decode_step(votes)
 
     def _prefill_step(self, admit: list[Request], votes) -> dict[int, int]:
         if not admit:

@@ -89,7 +89,7 @@ class FFNModelRunner:
         graph = torch.cuda.CUDAGraph()
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
-        with torch.cuda.graph(graph, pool=self._pool):
+        with torch.profiler.record_function(f"ffn_capture_{key}"), torch.cuda.graph(graph, pool=self._pool):
             self._ffn_forward(payload, update_state=False)
         self._graphs[key] = {"graph": graph}
 

@@ -199,7 +199,9 @@ class ModelRunner:
         begin = self.ffn.begin_step
         self.ffn.begin_step = lambda *a, **k: None  # suppressed inside the graph
         try:
-            with torch.cuda.graph(graph, pool=self.graph_pool):
+            # named like the reference's capture ranges (attention_model_runner.py:491-496)
+            with torch.profiler.record_function(f"capture_{batch}_{'dbo' if len(splits) > 2 else 'full'}"), \
+                    torch.cuda.graph(graph, pool=self.graph_pool):
                 self._decode_body(batch, splits)
         finally:
             self.ffn.begin_step = begin

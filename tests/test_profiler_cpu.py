@@ -38,3 +38,22 @@ def test_trace_written(tmp_path, monkeypatch):
         p.step()
     p.close()
     assert any(f.name.endswith(".json") or ".pt.trace" in f.name for f in tmp_path.iterdir())
+
+
+def test_engine_steps_are_named_in_the_attention_trace(tmp_path, monkeypatch):
+    from afd_plugin_b200.engine_config import EngineConfig, ModelConfig
+    from afd_plugin_b200.models import build_model, get_preset
+    from afd_plugin_b200.runtime.engine import LLMEngine
+
+    monkeypatch.setenv("AFD_GPU_ATTENTION_PROFILER_ENABLE", "1")
+    monkeypatch.setenv("AFD_GPU_ATTENTION_PROFILER_WAIT", "0")
+    monkeypatch.setenv("AFD_GPU_ATTENTION_PROFILER_WARMUP", "0")
+    monkeypatch.setenv("AFD_GPU_ATTENTION_PROFILER_ACTIVE", "4")
+    monkeypatch.setenv("AFD_GPU_ATTENTION_PROFILER_DIR", str(tmp_path))
+    arch = get_preset("tiny-dsv2")
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=64), max_num_seqs=2)
+    eng = LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=64))
+    eng.generate([[1, 2, 3]], 4)
+    eng.close()
+    text = "".join(f.read_text(errors="replace") for f in tmp_path.iterdir() if f.is_file())
+    assert "afd_prefill_step" in text and "afd_decode_step" in text
