@@ -297,6 +297,8 @@ class GatedDeltaNet(nn.Module):
         b = proj[:, cd + vd : cd + vd + nv]
         a = proj[:, cd + vd + nv :]
         cu, slots, reset = meta.linear_state_args()
+        if ops.checks.enabled():
+            ops.checks.state_slots("gated_delta_net", slots, max_seqs=ssm_state.shape[0])
         if self._cuda_ok(h):
             C = ops._cuda_ops()
             conv = C.gdn_conv(proj[:, :cd], self.conv_weight, conv_state, cu, slots, reset)

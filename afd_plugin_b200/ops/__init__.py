@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import torch
 
+from afd_plugin_b200.ops import checks
 from afd_plugin_b200.ops import reference as ref
 from afd_plugin_b200.ops._ext import ops as _cuda_ops
 
@@ -67,6 +68,8 @@ def topk_route(
     routed_scaling_factor: float = 1.0,
     forced_ids: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
+    if forced_ids is not None and checks.enabled():
+        checks.expert_ids("topk_route", forced_ids, num_experts=logits.shape[-1])
     if _cuda(logits):
         forced = None if forced_ids is None else forced_ids.to(torch.int32).contiguous()
         return _cuda_ops().topk_route(
@@ -96,6 +99,9 @@ def mla_decode(
     *,
     num_splits: int = 0,
 ) -> torch.Tensor:
+    if checks.enabled():
+        checks.paged_attention("mla_decode", block_table, seq_lens, num_blocks=kv_cache.shape[0],
+                               block_size=kv_cache.shape[1])
     if _cuda(q):
         if q.shape[-1] == 576 and kv_lora_rank == 512 and q.shape[1] % 16 == 0:
             return _cuda_ops().mla_decode(q[..., :512], q[..., 512:], kv_cache, block_table, seq_lens, scale,
@@ -133,6 +139,9 @@ def mla_decode_split(
     Returns ``[H, B, 512]`` (head-major, ready for the per-head V up-projection)
     or ``[B, H, 512]``.  CUDA only (the kernel's native interface).
     """
+    if checks.enabled():
+        checks.paged_attention("mla_decode", block_table, seq_lens, num_blocks=kv_cache.shape[0],
+                               block_size=kv_cache.shape[1])
     return _cuda_ops().mla_decode(q_lat, q_pe, kv_cache, block_table, seq_lens, scale, num_splits, head_major_out)
 
 
@@ -146,6 +155,9 @@ def gqa_decode(
     *,
     num_splits: int = 0,
 ) -> torch.Tensor:
+    if checks.enabled():
+        checks.paged_attention("gqa_decode", block_table, seq_lens, num_blocks=k_cache.shape[0],
+                               block_size=k_cache.shape[1])
     if _cuda(q):
         if q.shape[-1] == 128 and q.shape[1] // k_cache.shape[2] <= 16 and k_cache.shape[1] % 32 == 0:
             return _cuda_ops().gqa_decode(q.contiguous(), k_cache, v_cache, block_table, seq_lens, scale, num_splits)
@@ -182,6 +194,8 @@ def mla_cache_write(
 
     ``kv_a [T, kv_lora + rope]`` is the ``kv_a_proj_with_mqa`` output.
     """
+    if checks.enabled():
+        checks.cache_slots("mla_cache_write", slot_mapping, num_slots=kv_cache.shape[0] * kv_cache.shape[1])
     if _cuda(kv_a):
         _cuda_ops().mla_cache_write(kv_cache, kv_a, norm_weight, eps, positions, cos_sin, slot_mapping, kv_lora_rank)
         return
@@ -194,6 +208,8 @@ def mla_cache_write(
 def gqa_cache_write(
     k_cache: torch.Tensor, v_cache: torch.Tensor, k: torch.Tensor, v: torch.Tensor, slot_mapping: torch.Tensor
 ) -> None:
+    if checks.enabled():
+        checks.cache_slots("gqa_cache_write", slot_mapping, num_slots=k_cache.shape[0] * k_cache.shape[1])
     if _cuda(k):
         _cuda_ops().gqa_cache_write(k_cache, v_cache, k, v, slot_mapping)
         return
@@ -221,6 +237,8 @@ def moe_experts(
     With ``n_shared`` the last ``n_shared`` experts of ``w13``/``w2`` are shared
     chunks applied to every token with weight 1 (CUDA path).
     """
+    if checks.enabled():
+        checks.expert_ids("moe_experts", topk_ids, weights=topk_weights)
     if _cuda(x):
         from afd_plugin_b200.ops.moe import moe_experts_cuda
 
