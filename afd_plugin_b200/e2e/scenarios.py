@@ -2,9 +2,9 @@
 
 The AFD rows keep the names and topologies of the reference's scenario table
 (``tests/e2e/runner.py:361-395``: baseline, eager / graph / graph+DBO at 2A1F
-and 2A2F); the ``afd-fused-*`` rows run the NVLink-fused connector.  The
-baseline is one colocated engine (no AFD) rather than the reference's DP4
-vLLM deployment.
+and 2A2F, attention TP2); the ``afd-fused-*`` rows run the NVLink-fused
+connector.  The baseline is one colocated engine (no AFD) rather than the
+reference's DP4 vLLM deployment.
 """
 
 from __future__ import annotations
@@ -25,6 +25,7 @@ class Scenario:
     attention_ranks: int
     ffn_ranks: int
     connector: str = NCCL
+    tp: int = 1  # attention tensor parallelism (attention_ranks = DP x tp)
 
     @property
     def world_size(self) -> int:
@@ -44,8 +45,8 @@ class Scenario:
         return cfg
 
 
-def _s(name, baseline, graph, dbo, a, f, connector=NCCL) -> tuple[str, Scenario]:
-    return name, Scenario(name, baseline, graph, dbo, a, f, connector)
+def _s(name, baseline, graph, dbo, a, f, connector=NCCL, tp=1) -> tuple[str, Scenario]:
+    return name, Scenario(name, baseline, graph, dbo, a, f, connector, tp)
 
 
 SCENARIOS: dict[str, Scenario] = dict([
@@ -58,6 +59,8 @@ SCENARIOS: dict[str, Scenario] = dict([
     _s("afd-eager-2a2f", False, False, False, 2, 2),
     _s("afd-graph-2a2f", False, True, False, 2, 2),
     _s("afd-graph-dbo-2a2f", False, True, True, 2, 2),
+    _s("afd-eager-tp2-1f", False, False, False, 2, 1, tp=2),
+    _s("afd-graph-tp2-2f", False, True, False, 2, 2, tp=2),
     _s("afd-fused-graph-1a1f", False, True, False, 1, 1, FUSED),
     _s("afd-fused-graph-2a2f", False, True, False, 2, 2, FUSED),
     _s("afd-fused-graph-dbo-2a2f", False, True, True, 2, 2, FUSED),
@@ -81,6 +84,8 @@ def server_command(scn: Scenario, *, python: str, preset: str, port: int, master
         serve += ["--eager"]
     if scn.dbo:
         serve += ["--dbo"]
+    if scn.tp > 1:
+        serve += ["--tp", str(scn.tp)]
     if scn.baseline:
         return [python, *serve]
     serve += ["--afd", json.dumps(scn.afd_config(connector_extra), separators=(",", ":"))]

@@ -34,6 +34,8 @@ class AFDGroups:
     attention_group: object | None  # gloo group over Attention ranks (step agreement)
     ffn_group: object | None  # group over FFN ranks (expert parallel exchange)
     tp_group: object | None = None  # this Attention rank's tensor-parallel peers (tp_size > 1)
+    tp_cpu_group: object | None = None  # the same peers over gloo (host-side request fan-out)
+    tp_leader: int = -1  # world rank of this rank's TP leader (tp_size > 1)
 
 
 def init_afd_groups(mapping: AFDRankMapping, tp_size: int = 1) -> AFDGroups:
@@ -45,17 +47,22 @@ def init_afd_groups(mapping: AFDRankMapping, tp_size: int = 1) -> AFDGroups:
     attn = dist.new_group(list(mapping.attention_world_ranks), backend="gloo")
     backend = dist.get_backend()
     ffn = dist.new_group(list(mapping.ffn_world_ranks), backend=backend)
-    mine = None
+    mine = mine_cpu = None
+    leader = -1
     if tp_size > 1:
         ranks = list(mapping.attention_world_ranks)
         for start in range(0, len(ranks), tp_size):
-            grp = dist.new_group(ranks[start : start + tp_size], backend=backend)
-            if mapping.role == "attention" and mapping.world_rank in ranks[start : start + tp_size]:
-                mine = grp
+            peers = ranks[start : start + tp_size]
+            grp = dist.new_group(peers, backend=backend)
+            grp_cpu = dist.new_group(peers, backend="gloo")
+            if mapping.role == "attention" and mapping.world_rank in peers:
+                mine, mine_cpu, leader = grp, grp_cpu, peers[0]
     return AFDGroups(
         attention_group=attn if mapping.role == "attention" else None,
         ffn_group=ffn if mapping.role == "ffn" else None,
         tp_group=mine,
+        tp_cpu_group=mine_cpu,
+        tp_leader=leader,
     )
 
 

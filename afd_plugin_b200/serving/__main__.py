@@ -3,7 +3,8 @@
 Colocated (one process):
     python -m afd_plugin_b200.serving --preset tiny-dsv2 --port 8000
 
-AFD (one process per GPU; Attention rank 0 serves HTTP):
+AFD (one process per GPU; Attention rank 0 serves HTTP; ``--tp`` shards the
+attention heads over consecutive Attention ranks):
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m afd_plugin_b200.serving \\
         --preset deepseek-v2-lite --afd '{"num_attention_ranks": 1, "num_ffn_ranks": 1,
                                           "connector": "B200FusedAFDConnector"}'
@@ -31,6 +32,8 @@ def main(argv=None) -> None:
                     "(default: --max-num-seqs)")
     ap.add_argument("--dbo", action="store_true", help="two-ubatch overlap of attention and FFN (AFD only)")
     ap.add_argument("--seed", type=int, default=0, help="random-init seed when no checkpoint is given")
+    ap.add_argument("--tp", type=int, default=1, help="attention tensor parallelism (AFD only; "
+                    "num_attention_ranks = DP x TP)")
     args = ap.parse_args(argv)
     sizes = [int(x) for x in args.capture_sizes.split(",") if x] or [args.max_num_seqs]
 
@@ -74,11 +77,13 @@ def main(argv=None) -> None:
     A, F = int(afd["num_attention_ranks"]), int(afd["num_ffn_ranks"])
     if world != A + F:
         raise SystemExit(f"world size {world} != num_attention_ranks + num_ffn_ranks = {A + F}")
+    if args.tp < 1 or A % args.tp:
+        raise SystemExit(f"--tp {args.tp} must divide num_attention_ranks {A}")
     role, role_rank = role_of_world_rank(rank, attention_size=A, ffn_size=F)
     ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=args.eager, max_model_len=args.max_model_len,
                                   checkpoint=args.checkpoint, seed=args.seed),
-                      parallel_config=ParallelConfig(data_parallel_size=A, use_ubatching=args.dbo,
-                                                     num_ubatches=2 if args.dbo else 1),
+                      parallel_config=ParallelConfig(data_parallel_size=A // args.tp, tensor_parallel_size=args.tp,
+                                                     use_ubatching=args.dbo, num_ubatches=2 if args.dbo else 1),
                       compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
                       additional_config={"afd": dict(afd, role=role)}, max_num_seqs=args.max_num_seqs)
     if role == "ffn":
@@ -89,7 +94,8 @@ def main(argv=None) -> None:
     w = AFDAttentionWorker(ec, local_rank=local)
     if not args.eager and backend == "nccl":
         w.engine.capture_graphs()
-    loop = EngineLoop(w.engine, group=w.groups.attention_group, world=A, rank=role_rank).start()
+    loop = EngineLoop(w.engine, group=w.groups.attention_group, world=A, rank=role_rank,
+                      tp_group=w.groups.tp_cpu_group, tp_size=args.tp, tp_src=w.groups.tp_leader).start()
     if role_rank == 0:
         uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
                     port=args.port)

@@ -66,13 +66,19 @@ class EngineLoop:
     """Steps an engine on a background thread.
 
     ``group`` / ``world`` / ``rank``: the Attention ranks that must step
-    together (None for a single engine).
+    together (None for a single engine).  With attention tensor parallelism
+    (``tp_size > 1``) only the TP leader (world rank ``tp_src``) takes
+    requests; each iteration it broadcasts the new ones over ``tp_group`` (a
+    gloo group of its TP peers) and every peer admits the same requests in the
+    same order, so their engines hold identical batches.
     """
 
     def __init__(self, engine, *, group=None, world: int = 1, rank: int = 0, idle_sleep_s: float = 0.001,
-                 kv_hold_timeout_s: float = 120.0):
+                 kv_hold_timeout_s: float = 120.0, tp_group=None, tp_size: int = 1, tp_src: int = 0):
         self.engine = engine
         self.group, self.world, self.rank = group, world, rank
+        self.tp_group, self.tp_size, self.tp_src = tp_group, tp_size, tp_src
+        self.tp_leader = tp_size <= 1 or dist.get_rank() == tp_src
         self.idle_sleep_s = idle_sleep_s
         self.kv_hold_timeout_s = kv_hold_timeout_s
         self._queue: list[_Pending] = []
@@ -85,13 +91,20 @@ class EngineLoop:
         self.stats = {"requests": 0, "completed": 0, "generated_tokens": 0, "steps": 0, "ttft_s_sum": 0.0}
 
     # ------------------------------------------------------------ clients
+    def _check_entry(self, handoff: bool) -> None:
+        if self.error is not None:
+            raise RuntimeError("engine loop has failed") from self.error
+        if not self.tp_leader:
+            raise RuntimeError("requests enter through the TP leader's loop")
+        if handoff and self.tp_size > 1:
+            raise ValueError("prefill/decode KV hand-off is not supported with attention tensor parallelism")
+
     def submit(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False) -> Future:
         """Queue a request; the future resolves with its tokens and carries ``req_id`` once admitted."""
+        self._check_entry(hold_kv)
         limit = self.engine.config.model_config.max_model_len
         if len(prompt) + int(max_tokens) > limit:
             raise ValueError(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds max_model_len {limit}")
-        if self.error is not None:
-            raise RuntimeError("engine loop has failed") from self.error
         fut: Future = Future()
         with self._lock:
             self._queue.append(_Pending(list(prompt), int(max_tokens), fut, hold_kv=hold_kv))
@@ -100,8 +113,7 @@ class EngineLoop:
 
     def submit_prefilled(self, prompt: list[int], kv_blob: bytes, max_tokens: int) -> Future:
         """Queue a request whose prompt was prefilled by another engine (see ``export_kv``)."""
-        if self.error is not None:
-            raise RuntimeError("engine loop has failed") from self.error
+        self._check_entry(True)
         fut: Future = Future()
         with self._lock:
             self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob))
@@ -133,6 +145,14 @@ class EngineLoop:
             if not self._thread.is_alive():
                 self._thread = None
 
+    def _fan_out(self, new: list[_Pending]) -> list[_Pending]:
+        """TP leader -> peers: this iteration's new requests (one gloo broadcast)."""
+        obj = [[(p.prompt, p.max_tokens) for p in new]] if self.tp_leader else [None]
+        dist.broadcast_object_list(obj, src=self.tp_src, group=self.tp_group)
+        if self.tp_leader:
+            return new
+        return [_Pending(list(pr), int(mt), Future()) for pr, mt in obj[0]]
+
     def _agree(self, work: bool, stop: bool) -> tuple[bool, bool]:
         """(any rank has work, any rank stops) -- one collective per iteration on every rank."""
         if self.group is None or self.world <= 1:
@@ -150,6 +170,8 @@ class EngineLoop:
                 with self._lock:
                     new, self._queue = self._queue, []
                     calls, self._calls = self._calls, []
+                if self.tp_size > 1:
+                    new = self._fan_out(new)
                 for fn, fut in calls:
                     try:
                         fut.set_result(fn(eng))

@@ -42,7 +42,9 @@ def test_server_commands():
     cfg = json.loads(fused[fused.index("--afd") + 1])
     assert cfg["connector"] == FUSED and cfg["connector_extra_config"] == {"fp8_dispatch": True}
     eager = server_command(SCENARIOS["afd-eager-2a1f"], python="py", preset="p", port=9, master_port=10)
-    assert "--eager" in eager and "--capture-sizes" not in eager
+    assert "--eager" in eager and "--capture-sizes" not in eager and "--tp" not in eager
+    tp = server_command(SCENARIOS["afd-eager-tp2-1f"], python="py", preset="p", port=9, master_port=10)
+    assert tp[tp.index("--tp") + 1] == "2" and tp[tp.index("--nproc-per-node") + 1] == "3"
 
 
 def test_compare_and_gate():
@@ -94,13 +96,14 @@ def test_wait_for_health_reports_an_early_exit(tmp_path):
 
 
 def test_runner_cpu_baseline_vs_afd(tmp_path):
-    """Colocated engine and a 2A1F NCCL-connector deployment (gloo on CPU) serve identical tokens."""
+    """Colocated engine, a 2A1F NCCL-connector deployment and attention TP2 (gloo on CPU) serve identical tokens."""
     out = tmp_path / "e2e.json"
-    rc = runner.main(["--scenarios", "baseline-eager,afd-eager-2a1f", "--preset", "tiny-dsv2", "--dtype", "float32",
-                      "--device", "cpu", "--num-prompts", "4", "--max-tokens", "4", "--max-model-len", "128",
+    rc = runner.main(["--scenarios", "baseline-eager,afd-eager-2a1f,afd-eager-tp2-1f", "--preset", "tiny-dsv2",
+                      "--dtype", "float32", "--device", "cpu", "--num-prompts", "4", "--max-tokens", "4", "--max-model-len", "128",
                       "--max-num-seqs", "4", "--min-exact-match", "1.0", "--startup-timeout", "240",
                       "--log-dir", str(tmp_path / "logs"), "--output", str(out)])
     assert rc == 0
     res = json.loads(out.read_text())["results"]
-    assert res[1]["agreement"]["exact_match"] == 1.0 and res[1]["gate"] == "pass"
+    for r in res[1:]:
+        assert r["agreement"]["exact_match"] == 1.0 and r["gate"] == "pass", r["scenario"]
     assert all(r["teardown"] in ("terminated", "killed", "exited") for r in res)
