@@ -33,6 +33,12 @@ class ModelArchConfig:
     qk_nope_head_dim: int = 0
     qk_rope_head_dim: int = 0
     v_head_dim: int = 0
+    # DeepSeek sparse attention (DeepSeek-V3.2, GLM-MoE-DSA): a lightning
+    # indexer scores every cached token and each query attends to its
+    # ``index_topk`` best ones.  0 = dense MLA.
+    index_topk: int = 0
+    index_n_heads: int = 0
+    index_head_dim: int = 0
     # GQA
     num_key_value_heads: int = 0
     head_dim: int = 0
@@ -99,6 +105,10 @@ class ModelArchConfig:
         return tuple(i for i in range(self.num_hidden_layers) if self.is_moe_layer(i))
 
     @property
+    def has_indexer(self) -> bool:
+        return self.is_mla and self.index_topk > 0
+
+    @property
     def qk_head_dim(self) -> int:
         return self.qk_nope_head_dim + self.qk_rope_head_dim
 
@@ -106,7 +116,7 @@ class ModelArchConfig:
     def kv_cache_width(self) -> int:
         """Elements cached per token per layer (MLA: latent+rope; GQA: K and V)."""
         if self.is_mla:
-            return self.kv_lora_rank + self.qk_rope_head_dim
+            return self.kv_lora_rank + self.qk_rope_head_dim + (self.index_head_dim if self.has_indexer else 0)
         return 2 * self.num_key_value_heads * self.head_dim
 
     @property
@@ -250,6 +260,9 @@ class ModelArchConfig:
                 rope_scaling=hf.get("rope_scaling"),
                 max_position_embeddings=hf.get("max_position_embeddings", 4096),
                 tie_word_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                index_topk=int(hf.get("index_topk") or 0),
+                index_n_heads=int(hf.get("index_n_heads") or 0),
+                index_head_dim=int(hf.get("index_head_dim") or 0),
                 quant=quant,
                 weight_block_size=block,
             )
@@ -497,6 +510,16 @@ TINY_DSV3 = DSV3_32L.scaled(
     quant=None,
 )
 
+# DeepSeek-V3.2 shapes on the 32-layer DSV3 body: DeepSeek sparse attention
+# with a 64-head, 128-dim lightning indexer selecting 2048 tokens per query.
+DSV32_32L = DSV3_32L.scaled(architecture="DeepseekV32ForCausalLM", index_topk=2048, index_n_heads=64,
+                            index_head_dim=128)
+
+# Tiny DeepSeek-V3.2: the indexer keeps 8 tokens, so prompts of a few dozen
+# tokens exercise the sparse path.
+TINY_DSV32 = TINY_DSV3.scaled(architecture="DeepseekV32ForCausalLM", index_topk=8, index_n_heads=4,
+                              index_head_dim=48)
+
 # Tiny DeepSeek with the production MLA shapes (latent 512 + rope 64, 16
 # heads), so GPU tests exercise the specialised decode kernel.
 TINY_DSV2_MLA512 = TINY_DSV2.scaled(
@@ -593,6 +616,8 @@ PRESETS: dict[str, ModelArchConfig] = {
     "tiny-dsv2-mla512": TINY_DSV2_MLA512,
     "tiny-dsv2": TINY_DSV2,
     "tiny-dsv3": TINY_DSV3,
+    "tiny-dsv32": TINY_DSV32,
+    "deepseek-v3.2-32l": DSV32_32L,
     "tiny-qwen3-moe": TINY_QWEN3_MOE,
     "deepseek-v2-lite": DSV2_LITE,
     "qwen3-30b-a3b": QWEN3_30B_A3B,
@@ -612,6 +637,7 @@ def get_preset(name: str) -> ModelArchConfig:
 
 __all__ = [
     "DSV2_LITE",
+    "DSV32_32L",
     "DSV3_32L",
     "ModelArchConfig",
     "PRESETS",

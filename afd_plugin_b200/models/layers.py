@@ -16,6 +16,7 @@ from torch import nn
 
 from afd_plugin_b200 import ops
 from afd_plugin_b200.models.configs import ModelArchConfig
+from afd_plugin_b200.ops import reference as ref
 
 
 def _param(shape, dtype, device) -> nn.Parameter:
@@ -46,6 +47,10 @@ class AttentionMetadata:
     state_reset: torch.Tensor | None = None
     # Token ids of the step's rows (hash-routed MoE layers need them).
     input_ids: torch.Tensor | None = None
+    # DeepSeek sparse attention, decode steps: some sequence is longer than
+    # index_topk, so the indexer must select (a host decision, made before a
+    # step so dense steps can replay graphs).
+    sparse_decode: bool = False
 
     def linear_state_args(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
         if self.state_slots is not None:
@@ -99,8 +104,86 @@ class RMSNorm(nn.Module):
         return ops.fused_add_rms_norm(x, residual, self.weight, self.eps)
 
 
+class DSAIndexer(nn.Module):
+    """Lightning indexer of DeepSeek sparse attention (DeepSeek-V3.2, GLM-MoE-DSA).
+
+    Per token: ``q = wq_b(q_latent)`` split into ``index_n_heads`` heads of
+    ``index_head_dim``; ``k = LayerNorm(wk(x))`` (one ``index_head_dim`` row,
+    cached per position beside the MLA latent); head weights
+    ``weights_proj(x) / sqrt(heads) / sqrt(index_head_dim)``.  The first
+    ``qk_rope_head_dim`` dims of q and k are rotated with NeoX pairing.  A
+    query scores a cached position ``sum_h w_h * relu(q_h . k)`` and attends
+    to the ``index_topk`` best positions at or before it.  This is the indexer
+    the reference's DeepSeek-V3.2 path runs on the Attention role
+    (``afd_plugin/model_executor/models/deepseek_v2.py:638-650`` allocates its
+    top-k buffer there).  DeepSeek rotates q and k by a Hadamard matrix before
+    quantising them to fp8; the rotation is orthogonal, so it leaves these
+    fp32 scores unchanged and is not applied.
+    """
+
+    def __init__(self, arch: ModelArchConfig, dtype, device):
+        super().__init__()
+        if not arch.q_lora_rank:
+            raise ValueError("the DeepSeek sparse-attention indexer reads the q_lora latent")
+        H = arch.hidden_size
+        self.nh, self.d = arch.index_n_heads, arch.index_head_dim
+        self.rope = arch.qk_rope_head_dim
+        self.topk = arch.index_topk
+        self.wq_b = _param((self.nh * self.d, arch.q_lora_rank), dtype, device)
+        self.wk = _param((self.d, H), dtype, device)
+        self.k_norm_weight = _param((self.d,), dtype, device)
+        self.k_norm_bias = _param((self.d,), dtype, device)
+        self.weights_proj = _param((self.nh, H), dtype, device)
+        self.w_scale = (self.nh ** -0.5) * (self.d ** -0.5)
+
+    def keys(self, x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+        k = torch.nn.functional.layer_norm(ops.linear(x, self.wk).float(), (self.d,), self.k_norm_weight.float(),
+                                           self.k_norm_bias.float(), 1e-6).to(x.dtype)
+        ops.rope_(k.view(-1, 1, self.d)[..., : self.rope], positions, cos_sin, interleaved=False)
+        return k
+
+    def queries(self, x: torch.Tensor, q_latent: torch.Tensor, positions: torch.Tensor,
+                cos_sin: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        q = ops.linear(q_latent, self.wq_b).view(-1, self.nh, self.d)
+        ops.rope_(q[..., : self.rope], positions, cos_sin, interleaved=False)
+        return q, ops.linear(x, self.weights_proj).float() * self.w_scale
+
+    def select_decode(self, q: torch.Tensor, w: torch.Tensor, index_cache: torch.Tensor,
+                      meta: AttentionMetadata) -> torch.Tensor:
+        """Kept positions ``[B, min(topk, max_len)]`` per decode row (-1 pads)."""
+        bs = index_cache.shape[1]
+        n_max = int(meta.seq_lens.max())
+        cols = (n_max + bs - 1) // bs
+        B = meta.block_table.shape[0]
+        k = index_cache[meta.block_table[:, :cols].long()].view(B, cols * bs, self.d)
+        scores = ref.dsa_index_scores(q, w, k)
+        valid = torch.arange(cols * bs, device=q.device)[None, :] < meta.seq_lens.long()[:, None]
+        return ref.dsa_select(scores, valid, self.topk)
+
+    def select_prefill(self, q: torch.Tensor, w: torch.Tensor, index_cache: torch.Tensor,
+                       block_row: torch.Tensor, positions: torch.Tensor) -> torch.Tensor | None:
+        """``keep [t, n]`` for one sequence's queries, or None when every query sees all its keys."""
+        n = int(positions.max()) + 1
+        if n <= self.topk:
+            return None
+        k = ref.gather_paged(index_cache, block_row, n)
+        scores = ref.dsa_index_scores(q, w, k)
+        valid = torch.arange(n, device=q.device)[None, :] <= positions.long()[:, None]
+        pos = ref.dsa_select(scores, valid, self.topk)
+        hits = torch.zeros(pos.shape[0], n, dtype=torch.int32, device=q.device)
+        return hits.scatter_add_(1, pos.clamp_min(0), (pos >= 0).int()) > 0
+
+
 class MLAAttention(nn.Module):
-    """DeepSeek multi-head latent attention, absorbed form for cache reads."""
+    """DeepSeek multi-head latent attention, absorbed form for cache reads.
+
+    With ``arch.index_topk`` (DeepSeek sparse attention) the layer owns a
+    :class:`DSAIndexer` and its cache argument is ``(latent cache, indexer
+    key cache)``.  Prefill queries attend to their selected positions; a
+    decode step selects only when ``meta.sparse_decode`` (some sequence is
+    longer than ``index_topk``), otherwise every position is selected and the
+    dense decode kernel runs.
+    """
 
     def __init__(self, arch: ModelArchConfig, dtype, device, tp: TPInfo = TPInfo()):
         super().__init__()
@@ -127,6 +210,7 @@ class MLAAttention(nn.Module):
         self.w_uk = _param((nh, self.qk_nope, self.kv_lora), dtype, device)
         self.w_uv_t = _param((nh, self.kv_lora, self.v_dim), dtype, device)
         self.o_proj = _param((H, nh * self.v_dim), dtype, device)
+        self.indexer = DSAIndexer(arch, dtype, device) if arch.has_indexer else None
 
     @property
     def q_proj(self) -> torch.Tensor:
@@ -145,27 +229,40 @@ class MLAAttention(nn.Module):
         self.w_uk.data.copy_(w[:, : self.qk_nope, :])
         self.w_uv_t.data.copy_(w[:, self.qk_nope :, :].transpose(1, 2))
 
-    def project(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """``(q [T, H, qk], kv_a [T, kv_lora + rope])``; both may be strided views."""
+    def project(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+        """``(q [T, H, qk], kv_a [T, kv_lora + rope], q_latent [T, q_lora] | None)``; views may be strided."""
         y = ops.linear(h, self.in_proj)
         kv_a = y[:, self.n_q_in :]
+        q_latent = None
         if self.arch.q_lora_rank:
-            q = ops.linear(self.q_a_layernorm(y[:, : self.n_q_in].contiguous()), self.q_b_proj)
+            q_latent = self.q_a_layernorm(y[:, : self.n_q_in].contiguous())
+            q = ops.linear(q_latent, self.q_b_proj)
         else:
             q = y[:, : self.n_q_in]
-        return q.view(h.shape[0], self.num_heads, self.qk_nope + self.qk_rope), kv_a
+        return q.view(h.shape[0], self.num_heads, self.qk_nope + self.qk_rope), kv_a, q_latent
 
-    def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache: torch.Tensor, cos_sin: torch.Tensor):
+    def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache, cos_sin: torch.Tensor):
+        index_cache = None
+        if isinstance(kv_cache, tuple):
+            kv_cache, index_cache = kv_cache
         T = h.shape[0]
-        q, kv_a = self.project(h)
+        q, kv_a, q_latent = self.project(h)
         ops.mla_cache_write(
             kv_cache, kv_a, self.kv_a_layernorm.weight, self.kv_a_layernorm.eps,
             meta.positions, cos_sin, meta.slot_mapping, self.kv_lora,
         )
+        sparse = False
+        if self.indexer is not None:
+            k_idx = self.indexer.keys(h, meta.positions, cos_sin)
+            index_cache.view(-1, self.indexer.d).index_copy_(0, meta.slot_mapping.long(), k_idx)
+            sparse = meta.sparse_decode or not meta.is_decode
+            if sparse:
+                qi, wi = self.indexer.queries(h, q_latent, meta.positions, cos_sin)
         q_pe = q[..., self.qk_nope :]
         ops.rope_(q_pe, meta.positions, cos_sin, interleaved=True)
         q_nope = q[..., : self.qk_nope]
-        if h.is_cuda and meta.is_decode and self.kv_lora == 512 and self.qk_rope == 64 and self.num_heads % 16 == 0:
+        if (h.is_cuda and meta.is_decode and not sparse and self.kv_lora == 512 and self.qk_rope == 64
+                and self.num_heads % 16 == 0):
             # Head-major end to end: [H,T,128]x[H,128,512] -> kernel -> [H,T,512]x[H,512,v].
             q_lat = torch.bmm(q_nope.transpose(0, 1), self.w_uk)
             o_lat = ops.mla_decode_split(q_lat.transpose(0, 1), q_pe, kv_cache, meta.block_table, meta.seq_lens,
@@ -178,16 +275,22 @@ class MLAAttention(nn.Module):
         else:
             q_lat = torch.bmm(q_nope.transpose(0, 1).float(), self.w_uk.float()).to(h.dtype)
         q_full = torch.cat([q_lat.transpose(0, 1), q_pe], dim=-1).contiguous()  # [T, H, 576]
-        if meta.is_decode:
+        if meta.is_decode and sparse:
+            keep_pos = self.indexer.select_decode(qi, wi, index_cache, meta)
+            o_lat = ops.mla_decode_sparse(q_full, kv_cache, meta.block_table, meta.seq_lens, keep_pos, self.scale,
+                                          self.kv_lora)
+        elif meta.is_decode:
             o_lat = ops.mla_decode(q_full, kv_cache, meta.block_table, meta.seq_lens, self.scale, self.kv_lora)
         else:
-            from afd_plugin_b200.ops import reference as ref
-
             o_lat = torch.empty(T, self.num_heads, self.kv_lora, dtype=h.dtype, device=h.device)
             for start, end, seq in meta.prefill_seqs or []:
+                keep = None
+                if self.indexer is not None:
+                    keep = self.indexer.select_prefill(qi[start:end], wi[start:end], index_cache,
+                                                       meta.block_table[seq], meta.positions[start:end])
                 o_lat[start:end] = ref.mla_prefill(
                     q_full[start:end], kv_cache, meta.block_table[seq], meta.positions[start:end],
-                    self.scale, self.kv_lora,
+                    self.scale, self.kv_lora, keep,
                 )
         if h.is_cuda:
             o = torch.bmm(o_lat.transpose(0, 1), self.w_uv_t)  # [H, T, v]

@@ -481,6 +481,14 @@ class AFDDeepseekV2ForCausalLM(AFDCausalLM):
         shape = (nh_all * (a.qk_nope_head_dim + a.v_head_dim), a.kv_lora_rank)
         yield ParamSpec(p + "kv_b_proj.weight", shape, lambda t, _a=attn: _a.set_kv_b_proj(t.to(_a.w_uk.device, _a.w_uk.dtype)))
         yield ParamSpec(p + "o_proj.weight", (H, nh_all * a.v_head_dim), _cols_of(attn.o_proj, h0 * a.v_head_dim))
+        ix = attn.indexer
+        if ix is not None:  # replicated on every tensor-parallel rank
+            q = p + "indexer."
+            yield ParamSpec(q + "wq_b.weight", tuple(ix.wq_b.shape), _copy(ix.wq_b))
+            yield ParamSpec(q + "wk.weight", tuple(ix.wk.shape), _copy(ix.wk))
+            yield ParamSpec(q + "k_norm.weight", tuple(ix.k_norm_weight.shape), _copy(ix.k_norm_weight), "ones")
+            yield ParamSpec(q + "k_norm.bias", tuple(ix.k_norm_bias.shape), _copy(ix.k_norm_bias), "zeros")
+            yield ParamSpec(q + "weights_proj.weight", tuple(ix.weights_proj.shape), _copy(ix.weights_proj))
 
 
 class AFDDeepseekV3ForCausalLM(AFDDeepseekV2ForCausalLM):

@@ -145,6 +145,31 @@ def mla_decode_split(
     return _cuda_ops().mla_decode(q_lat, q_pe, kv_cache, block_table, seq_lens, scale, num_splits, head_major_out)
 
 
+def mla_decode_sparse(
+    q: torch.Tensor,
+    kv_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    keep_pos: torch.Tensor,
+    scale: float,
+    kv_lora_rank: int,
+) -> torch.Tensor:
+    """MLA decode over the positions a DeepSeek-sparse-attention indexer kept.
+
+    ``keep_pos [B, K]`` lists each row's selected positions (-1 = unused).
+    Gather + two small batched GEMMs on both devices: no dedicated sparse
+    kernel yet (dense steps, i.e. every sequence within ``index_topk``
+    tokens, keep using the MLA decode kernel).
+    """
+    if checks.enabled():
+        checks.paged_attention("mla_decode_sparse", block_table, seq_lens, num_blocks=kv_cache.shape[0],
+                               block_size=kv_cache.shape[1])
+        bad = (keep_pos >= seq_lens.view(-1, 1).to(keep_pos.dtype)).any()
+        if bool(bad):
+            raise checks.KernelInputError("mla_decode_sparse: a kept position lies beyond its sequence")
+    return ref.mla_decode_sparse(q, kv_cache, block_table, keep_pos, scale, kv_lora_rank)
+
+
 def gqa_decode(
     q: torch.Tensor,
     k_cache: torch.Tensor,

@@ -300,15 +300,70 @@ def mla_prefill(
     positions: torch.Tensor,
     scale: float,
     kv_lora_rank: int,
+    keep: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Causal absorbed MLA for ``T`` query tokens of ONE sequence."""
+    """Causal absorbed MLA for ``T`` query tokens of ONE sequence.
+
+    ``keep [T, n]`` (DeepSeek sparse attention) restricts each query to the
+    cached positions its indexer selected.
+    """
     n = int(positions.max()) + 1
     kv = gather_paged(kv_cache, block_table, n).float()
     s = torch.einsum("thd,nd->thn", q.float(), kv) * scale
     mask = torch.arange(n, device=q.device)[None, :] > positions.long()[:, None]
+    if keep is not None:
+        mask = mask | ~keep[:, :n]
     s = s.masked_fill(mask[:, None, :], float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.einsum("thn,nd->thd", p, kv[:, :kv_lora_rank]).to(q.dtype)
+
+
+def dsa_index_scores(q: torch.Tensor, w: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    """Lightning-indexer scores ``[T, N]``: ``sum_h w[t, h] * relu(q[t, h] . k[n])``.
+
+    ``q [T, heads, d]``, ``w [T, heads]`` (already scaled), ``k [N, d]`` or
+    ``[T, N, d]`` (per-query key sets, as in a batched decode step).  The
+    DeepSeek-V3.2 indexer (its ``fp8_index``) computes this on fp8 operands;
+    here it is fp32.
+    """
+    if k.dim() == 2:
+        logits = torch.einsum("thd,nd->thn", q.float(), k.float())
+    else:
+        logits = torch.einsum("thd,tnd->thn", q.float(), k.float())
+    return torch.einsum("thn,th->tn", logits.clamp_min(0.0), w.float())
+
+
+def dsa_select(scores: torch.Tensor, valid: torch.Tensor, topk: int) -> torch.Tensor:
+    """Positions ``[T, min(topk, N)]`` of the best-scoring valid keys per query; -1 pads.
+
+    Equal scores are common (the ReLU zeroes many of them); ties go to the
+    earlier position (a stable sort), so the selection does not depend on how
+    many padded columns the score matrix has -- a decode step and a prefill of
+    the same tokens select the same positions.
+    """
+    k = min(int(topk), scores.shape[-1])
+    order = scores.masked_fill(~valid, float("-inf")).sort(dim=-1, descending=True, stable=True).indices
+    idx = order[..., :k]
+    return torch.where(valid.gather(-1, idx), idx, torch.full_like(idx, -1))
+
+
+def mla_decode_sparse(
+    q: torch.Tensor,
+    kv_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    keep_pos: torch.Tensor,
+    scale: float,
+    kv_lora_rank: int,
+) -> torch.Tensor:
+    """Absorbed MLA decode over the selected positions ``keep_pos [B, K]`` (-1 = unused) only."""
+    bs, D = kv_cache.shape[1], kv_cache.shape[-1]
+    pos = keep_pos.long().clamp_min(0)
+    slots = block_table.long().gather(1, pos // bs) * bs + pos % bs
+    kv = kv_cache.reshape(-1, D)[slots].float()  # [B, K, D]
+    s = torch.einsum("bhd,bkd->bhk", q.float(), kv) * scale
+    s = s.masked_fill((keep_pos < 0)[:, None, :], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("bhk,bkd->bhd", p, kv[..., :kv_lora_rank]).to(q.dtype)
 
 
 def gqa_decode(

@@ -61,13 +61,16 @@ class AttentionCoordinator:
 
     def __init__(self, group=None, size: int = 1, rank: int = 0):
         self.group, self.size, self.rank = group, size, rank
+        self.any_sparse = False  # after exchange(): some rank needs a sparse-attention decode step
 
-    def exchange(self, num_tokens: int, is_prefill: bool) -> list[tuple[int, bool]]:
+    def exchange(self, num_tokens: int, is_prefill: bool, *, sparse: bool = False) -> list[tuple[int, bool]]:
         if self.group is None or self.size == 1:
+            self.any_sparse = sparse
             return [(num_tokens, is_prefill)]
-        mine = torch.tensor([num_tokens, int(is_prefill)], dtype=torch.int64)
+        mine = torch.tensor([num_tokens, int(is_prefill), int(sparse)], dtype=torch.int64)
         out = [torch.empty_like(mine) for _ in range(self.size)]
         dist.all_gather(out, mine, group=self.group)
+        self.any_sparse = any(bool(t[2]) for t in out)
         return [(int(t[0]), bool(t[1])) for t in out]
 
 
@@ -322,7 +325,9 @@ class LLMEngine:
             admit.append(self.waiting.pop(0))
         is_prefill = bool(admit)
         ntok = sum(len(r.prompt) for r in admit) if is_prefill else len(self.running)
-        votes = self.coordinator.exchange(ntok, is_prefill)
+        topk = getattr(self.model.arch, "index_topk", 0)
+        sparse = bool(topk) and any(r.num_tokens > topk for r in self.running)
+        votes = self.coordinator.exchange(ntok, is_prefill, sparse=sparse)
         if any(p for _, p in votes):
             self._last_phase = "prefill"
             with torch.profiler.record_function("afd_prefill_step"):
@@ -366,7 +371,11 @@ class LLMEngine:
         B = len(reqs)
         top = max(max(n for n, _ in votes), 1)
         padded = pad_to_capture_size(top, self.capture_sizes) if self.use_graphs else None
-        use_graph = padded is not None and padded in self.runner.graphs
+        # Graphs hold the dense decode: a step that must select sparse
+        # positions (DeepSeek sparse attention past index_topk) runs eagerly.
+        sparse = self.coordinator.any_sparse
+        use_graph = padded is not None and padded in self.runner.graphs and not sparse
+        self.runner.sparse_decode = sparse
         # All Attention ranks run the same (padded) batch so FFN stages line up.
         run_b = padded if use_graph else top
         bs = self.block_size

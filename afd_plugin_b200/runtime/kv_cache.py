@@ -1,7 +1,9 @@
 """Paged KV cache (plus linear-attention state): device pool and a host-side block allocator.
 
 MLA layers cache one ``kv_lora + rope`` latent row per token
-(``[L, blocks, block_size, 576]`` for DeepSeek); GQA layers cache K and V
+(``[L, blocks, block_size, 576]`` for DeepSeek), plus the sparse-attention
+indexer's key row when the model has one (``index_k``, DeepSeek-V3.2 /
+GLM-MoE-DSA); GQA layers cache K and V
 (``[L, blocks, block_size, kv_heads, head_dim]`` each).  A token's slot is
 ``block_id * block_size + offset``.
 """
@@ -66,10 +68,15 @@ class KVCache:
         attn_layers = arch.full_attention_layers
         self._kv_index = {layer: i for i, layer in enumerate(attn_layers)}
         L = len(attn_layers)
+        self.index_k = None
         if arch.is_mla:
             self.kv = torch.zeros(L, num_blocks, block_size, arch.kv_lora_rank + arch.qk_rope_head_dim,
                                   dtype=dtype, device=device)
             self.k = self.v = None
+            if arch.has_indexer:
+                # DeepSeek sparse attention: the indexer's key row per position
+                self.index_k = torch.zeros(L, num_blocks, block_size, arch.index_head_dim, dtype=dtype,
+                                           device=device)
         else:
             shape = (L, num_blocks, block_size, arch.num_key_value_heads, arch.head_dim)
             self.k = torch.zeros(shape, dtype=dtype, device=device)
@@ -90,6 +97,8 @@ class KVCache:
             j = self._state_index[i]
             return (self.conv_state[j], self.ssm_state[j])
         j = self._kv_index[i]
+        if self.index_k is not None:
+            return (self.kv[j], self.index_k[j])
         if self.kv is not None:
             return self.kv[j]
         return (self.k[j], self.v[j])
@@ -115,7 +124,7 @@ class KVCache:
         dev = next(t for t in (self.kv, self.k, self.conv_state) if t is not None).device
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
-        for t in (self.kv, self.k, self.v, self.conv_state):
+        for t in (self.kv, self.index_k, self.k, self.v, self.conv_state):
             if t is not None:
                 t.normal_(0.0, std, generator=g)
         if self.ssm_state is not None:

@@ -5,7 +5,8 @@ and exports them; a decode engine imports them into freshly allocated blocks
 and continues from the next token.  The exported state is exactly what the
 decode kernels read:
 
-* MLA layers: the latent rows ``kv [L, n, kv_lora + rope]``;
+* MLA layers: the latent rows ``kv [L, n, kv_lora + rope]`` (and the
+  sparse-attention indexer's keys ``index_k [L, n, index_head_dim]``);
 * GQA layers: ``k`` / ``v`` ``[L, n, kv_heads, head_dim]``;
 * Gated DeltaNet layers: the request's ``conv_state`` and fp32 ``ssm_state``.
 
@@ -53,6 +54,8 @@ def geometry(cache: KVCache) -> dict:
     g: dict = {}
     if cache.kv is not None:
         g["kv"] = [cache.kv.shape[0], cache.kv.shape[3]]
+    if cache.index_k is not None:
+        g["index_k"] = [cache.index_k.shape[0], cache.index_k.shape[3]]
     if cache.k is not None:
         g["k"] = g["v"] = [cache.k.shape[0], *cache.k.shape[3:]]
     if cache.conv_state is not None:
@@ -70,6 +73,9 @@ def export_request_state(cache: KVCache, blocks: list[int], n: int, state_slot: 
         if cache.kv is not None:
             L, W = cache.kv.shape[0], cache.kv.shape[3]
             out["kv"] = cache.kv.view(L, -1, W).index_select(1, slots).cpu()
+            if cache.index_k is not None:
+                Wi = cache.index_k.shape[3]
+                out["index_k"] = cache.index_k.view(L, -1, Wi).index_select(1, slots).cpu()
         else:
             L, tail = cache.k.shape[0], cache.k.shape[3:]
             out["k"] = cache.k.view(L, -1, *tail).index_select(1, slots).cpu()
@@ -88,7 +94,7 @@ def import_request_state(cache: KVCache, blocks: list[int], state_slot: int, ten
         t = tensors.get(name)
         if t is None:
             raise ValueError(f"KV payload lacks {name!r}")
-        paged = name in ("kv", "k", "v")
+        paged = name in ("kv", "index_k", "k", "v")
         got = [t.shape[0], *t.shape[2:]] if paged else [t.shape[0], *t.shape[1:]]
         if got != list(want) or (paged and t.shape[1] != n):
             raise ValueError(f"KV payload {name} has shape {tuple(t.shape)}; this engine expects {want} "
@@ -102,6 +108,9 @@ def import_request_state(cache: KVCache, blocks: list[int], state_slot: int, ten
         if cache.kv is not None:
             L, W = cache.kv.shape[0], cache.kv.shape[3]
             cache.kv.view(L, -1, W).index_copy_(1, slots, tensors["kv"].to(dev, cache.kv.dtype))
+            if cache.index_k is not None:
+                Wi = cache.index_k.shape[3]
+                cache.index_k.view(L, -1, Wi).index_copy_(1, slots, tensors["index_k"].to(dev, cache.index_k.dtype))
         else:
             L, tail = cache.k.shape[0], cache.k.shape[3:]
             cache.k.view(L, -1, *tail).index_copy_(1, slots, tensors["k"].to(dev, cache.k.dtype))

@@ -94,6 +94,9 @@ class ModelRunner:
         self.has_linear_state = bool(model.arch.linear_attention_layers)
         self.pad_state_slot = kv_cache.max_seqs - 1
         self.buf.state_slots.fill_(self.pad_state_slot)
+        # DeepSeek sparse attention: set by the engine for eager decode steps
+        # in which some sequence is longer than index_topk.
+        self.sparse_decode = False
 
     # ------------------------------------------------------------ forward
     def _layers(self, h: torch.Tensor, meta: AttentionMetadata, stage: int):
@@ -147,6 +150,7 @@ class ModelRunner:
                 is_decode=True,
                 state_slots=b.state_slots[lo:hi] if self.has_linear_state else None,
                 cu_seqlens=b.rows[: hi - lo + 1] if self.has_linear_state else None,
+                sparse_decode=self.sparse_decode,
             ))
         return metas
 
@@ -182,6 +186,7 @@ class ModelRunner:
     def capture(self, batch: int, *, warmup: int = 2) -> None:
         """Capture one FULL decode graph for a padded batch size."""
         splits = ubatch_splits(batch, self.num_ubatches)
+        self.sparse_decode = False  # graphs hold the dense decode
         self._pad_rows(0, batch)
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))

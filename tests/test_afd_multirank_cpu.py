@@ -97,3 +97,19 @@ def test_attention_tp2_matches_colocated(preset):
     ref = _colocated(preset, prompts, 6)
     outs, _ = _run(preset, {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=6, tp=2)
     assert outs == ref
+
+
+def test_dsv32_sparse_attention_2a2f():
+    """DeepSeek sparse attention (indexer on the Attention side, prompts past index_topk) across 2A2F."""
+    prompts = _prompts(n=4, length=20)
+    ref = _colocated("tiny-dsv32", prompts, 6)
+    outs, _ = _run("tiny-dsv32", {"num_attention_ranks": 2, "num_ffn_ranks": 2}, prompts, max_tokens=6)
+    assert outs == ref
+
+
+def test_dsv32_attention_tp2():
+    """The indexer is replicated on both tensor-parallel ranks; the MLA heads are split."""
+    prompts = _prompts(n=3, length=16)
+    ref = _colocated("tiny-dsv32", prompts, 5)
+    outs, _ = _run("tiny-dsv32", {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=5, tp=2)
+    assert outs == ref

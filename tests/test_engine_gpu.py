@@ -34,6 +34,17 @@ def test_graph_decode_matches_eager(preset):
     assert eng.generate(prompts, 8) == eager
 
 
+def test_dsa_dense_steps_replay_graphs_then_sparse_steps_run_eagerly():
+    """DeepSeek sparse attention: within index_topk the captured dense graph replays; past it the
+    engine selects positions eagerly.  Tokens equal an all-eager engine's."""
+    prompts = _prompts(4, 5, 1024)  # index_topk 8: decode steps 1-3 dense, later ones sparse
+    eager = _engine("tiny-dsv32", eager=True).generate(prompts, 8)
+    eng = _engine("tiny-dsv32", eager=False)
+    eng.capture_graphs()
+    assert 8 in eng.runner.graphs
+    assert eng.generate(prompts, 8) == eager
+
+
 def test_gpu_prefill_logits_track_fp32_reference():
     """bf16 kernel path vs the fp32 reference model: next-token logits stay close."""
     from afd_plugin_b200.runtime.engine import Request
