@@ -122,6 +122,13 @@ class LLMEngine:
         self._h_lens = mk(self.max_batch, dt=torch.int32)
         self._h_next = mk(self.max_batch, dt=torch.int32)
         self._h_state = mk(self.max_batch, dt=torch.int32)
+        # numpy views of the pinned staging tensors: a decode step fills them
+        # with a few vectorised writes instead of per-element tensor indexing
+        self._n_ids, self._n_pos, self._n_slot, self._n_table, self._n_lens, self._n_next, self._n_state = (
+            t.numpy() for t in (self._h_ids, self._h_pos, self._h_slot, self._h_table, self._h_lens, self._h_next,
+                                self._h_state))
+        # (req_id, number of blocks) each staged block-table row holds; rows are rewritten only on change
+        self._row_key: list[tuple[int, int] | None] = [None] * self.max_batch
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
         from afd_plugin_b200.utils.profiler import RoleProfiler
@@ -253,18 +260,9 @@ class LLMEngine:
 
         Returns the batch size; used to prime device-resident decode loops.
         """
-        bs = self.block_size
         b = self.runner.buf
         reqs = self.running
-        for i, r in enumerate(reqs):
-            pos = r.num_tokens - 1
-            self._h_ids[i] = r.output[-1]
-            self._h_pos[i] = pos
-            self._h_slot[i] = r.blocks[pos // bs] * bs + pos % bs
-            self._h_table[i].fill_(PAD_BLOCK)
-            self._h_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
-            self._h_lens[i] = pos + 1
-            self._h_state[i] = r.state_slot
+        self._stage_decode_inputs(reqs, len(reqs))
         n = len(reqs)
         b.state_slots[:n].copy_(self._h_state[:n])
         b.input_ids[:n].copy_(self._h_ids[:n])
@@ -364,6 +362,38 @@ class LLMEngine:
         # Ranks that are not prefilling join with one placeholder row.
         return {"tokens_across_attn": {0: tuple(max(1, n) if p else 1 for n, p in votes)}}
 
+    def _stage_decode_inputs(self, reqs: list[Request], run_b: int) -> None:
+        """Fill the pinned staging rows ``[0, run_b)`` for a decode step (padding rows after the requests)."""
+        bs = self.block_size
+        B = len(reqs)
+        pos = [r.num_tokens - 1 for r in reqs]
+        for r, p in zip(reqs, pos):
+            if len(r.blocks) * bs <= p:
+                self._ensure_blocks(r, p + 1)
+        self._n_ids[:B] = [r.output[-1] if r.output else r.prompt[-1] for r in reqs]
+        self._n_pos[:B] = pos
+        self._n_slot[:B] = [r.blocks[p // bs] * bs + p % bs for r, p in zip(reqs, pos)]
+        self._n_lens[:B] = self._n_pos[:B] + 1
+        self._n_state[:B] = [r.state_slot for r in reqs]
+        table, keys = self._n_table, self._row_key
+        for i, r in enumerate(reqs):
+            key = (r.req_id, len(r.blocks))
+            if keys[i] != key:
+                n = len(r.blocks)
+                table[i, :n] = r.blocks
+                table[i, n:] = PAD_BLOCK
+                keys[i] = key
+        if run_b > B:
+            self._n_ids[B:run_b] = 0
+            self._n_pos[B:run_b] = 0
+            self._n_slot[B:run_b] = PAD_BLOCK * bs
+            self._n_lens[B:run_b] = 1
+            self._n_state[B:run_b] = self.runner.pad_state_slot
+            for i in range(B, run_b):
+                if keys[i] is not None:
+                    table[i] = PAD_BLOCK
+                    keys[i] = None
+
     def _decode_step(self, votes) -> dict[int, int]:
         from afd_plugin_b200.runtime.model_runner import ubatch_splits
 
@@ -378,23 +408,7 @@ class LLMEngine:
         self.runner.sparse_decode = sparse
         # All Attention ranks run the same (padded) batch so FFN stages line up.
         run_b = padded if use_graph else top
-        bs = self.block_size
-        self._h_table[:run_b].fill_(PAD_BLOCK)
-        for i, r in enumerate(reqs):
-            pos = r.num_tokens - 1
-            self._ensure_blocks(r, pos + 1)
-            self._h_ids[i] = r.output[-1] if r.output else r.prompt[-1]
-            self._h_pos[i] = pos
-            self._h_slot[i] = r.blocks[pos // bs] * bs + pos % bs
-            self._h_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
-            self._h_lens[i] = pos + 1
-            self._h_state[i] = r.state_slot
-        if run_b > B:
-            self._h_ids[B:run_b] = 0
-            self._h_pos[B:run_b] = 0
-            self._h_slot[B:run_b] = PAD_BLOCK * bs
-            self._h_lens[B:run_b] = 1
-            self._h_state[B:run_b] = self.runner.pad_state_slot
+        self._stage_decode_inputs(reqs, run_b)
         b = self.runner.buf
         if self.runner.has_linear_state:
             b.state_slots[:run_b].copy_(self._h_state[:run_b], non_blocking=True)
@@ -420,8 +434,7 @@ class LLMEngine:
         self.last_d2h_bytes = run_b * 4
         out = {}
         still = []
-        for i, r in enumerate(reqs):
-            t = int(self._h_next[i])
+        for r, t in zip(reqs, self._n_next[:B].tolist()):
             r.output.append(t)
             out[r.req_id] = t
             (self._finish(r) if r.finished else still.append(r))

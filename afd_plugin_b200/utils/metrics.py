@@ -13,13 +13,15 @@ from __future__ import annotations
 import json
 import os
 import time
+from collections import deque
 
 
 class StepMetrics:
     def __init__(self, path: str | None = None, *, keep: int = 100_000):
         self.path = path if path is not None else os.environ.get("AFD_METRICS_JSONL") or None
         self.keep = keep
-        self.decode_ms: list[float] = []
+        # the most recent ``keep`` decode steps: (ms, tokens)
+        self._window: deque[tuple[float, int]] = deque(maxlen=keep)
         self.decode_tokens = 0
         self.steps = 0
         self._fh = open(self.path, "a", buffering=1) if self.path else None  # noqa: SIM115
@@ -29,22 +31,26 @@ class StepMetrics:
         self.steps += 1
         if phase == "decode":
             self.decode_tokens += tokens
-            self.decode_ms.append(ms)
-            if len(self.decode_ms) > self.keep:
-                self.decode_ms = self.decode_ms[-self.keep :]
+            self._window.append((ms, tokens))
         if self._fh is not None:
             self._fh.write(json.dumps({"step": self.steps, "phase": phase, "batch": batch, "tokens": tokens,
                                        "ms": round(ms, 4), "h2d_bytes": h2d_bytes, "d2h_bytes": d2h_bytes,
                                        "t": round(time.time(), 6)}) + "\n")
 
+    @property
+    def decode_ms(self) -> list[float]:
+        return [m for m, _ in self._window]
+
     def summary(self) -> dict:
+        """Totals since start; rates and percentiles over the most recent ``keep`` decode steps."""
         ms = sorted(self.decode_ms)
         if not ms:
             return {"steps": self.steps, "decode_steps": 0}
         pick = lambda q: ms[min(len(ms) - 1, int(q * (len(ms) - 1) + 0.5))]  # noqa: E731
         total_s = sum(ms) / 1e3
+        window_tokens = sum(t for _, t in self._window)
         return {"steps": self.steps, "decode_steps": len(ms), "decode_tokens": self.decode_tokens,
-                "decode_tok_per_s": round(self.decode_tokens / total_s, 2) if total_s > 0 else 0.0,
+                "decode_tok_per_s": round(window_tokens / total_s, 2) if total_s > 0 else 0.0,
                 "p50_step_ms": round(pick(0.5), 4), "p90_step_ms": round(pick(0.9), 4)}
 
     def close(self) -> None:
