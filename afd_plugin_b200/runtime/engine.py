@@ -417,7 +417,8 @@ class LLMEngine:
         b.slot_mapping[:run_b].copy_(self._h_slot[:run_b], non_blocking=True)
         b.block_table[:run_b].copy_(self._h_table[:run_b], non_blocking=True)
         b.seq_lens[:run_b].copy_(self._h_lens[:run_b], non_blocking=True)
-        self.last_h2d_bytes = run_b * (4 + 8 + 8 + 4 + 4 * self.max_blocks_per_seq)
+        self.last_h2d_bytes = run_b * (4 + 8 + 8 + 4 + 4 * self.max_blocks_per_seq
+                                       + (4 if self.runner.has_linear_state else 0))
         flags = {}
         if len(votes) > 1:
             sp = ubatch_splits(run_b, self.runner.num_ubatches)
