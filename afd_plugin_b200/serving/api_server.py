@@ -60,6 +60,7 @@ class _Pending:
     submitted: float = field(default_factory=time.perf_counter)
     hold_kv: bool = False
     kv_blob: bytes | None = None  # prefilled elsewhere: the exported cache rows
+    first_token_at: float | None = None
 
 
 class EngineLoop:
@@ -88,7 +89,8 @@ class EngineLoop:
         self._stop = threading.Event()
         self._thread: threading.Thread | None = None
         self.error: BaseException | None = None
-        self.stats = {"requests": 0, "completed": 0, "generated_tokens": 0, "steps": 0, "ttft_s_sum": 0.0}
+        self.stats = {"requests": 0, "completed": 0, "generated_tokens": 0, "steps": 0,
+                      "ttft_s_sum": 0.0, "ttft_count": 0, "tpot_s_sum": 0.0, "tpot_count": 0}
 
     # ------------------------------------------------------------ clients
     def _check_entry(self, handoff: bool) -> None:
@@ -196,13 +198,23 @@ class EngineLoop:
                 if not work:
                     time.sleep(self.idle_sleep_s)
                     continue
-                eng.step()
+                produced = eng.step()
+                now = time.perf_counter()
                 self.stats["steps"] += 1
+                for rid in produced:
+                    p = self._inflight.get(rid)
+                    if p is not None and p.first_token_at is None:
+                        p.first_token_at = now
+                        self.stats["ttft_s_sum"] += now - p.submitted
+                        self.stats["ttft_count"] += 1
                 for rid in [r for r in self._inflight if r in eng.finished]:
                     p = self._inflight.pop(rid)
                     out = eng.finished.pop(rid).output
                     self.stats["completed"] += 1
                     self.stats["generated_tokens"] += len(out)
+                    if p.first_token_at is not None and len(out) > 1:
+                        self.stats["tpot_s_sum"] += (now - p.first_token_at) / (len(out) - 1)
+                        self.stats["tpot_count"] += 1
                     p.future.set_result(out)
         except BaseException as exc:  # noqa: BLE001 - surfaced to every waiting client
             self.error = exc
@@ -263,6 +275,9 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
     @app.get("/metrics")
     def metrics():
         out = dict(loop.stats)
+        st = loop.stats
+        out["mean_ttft_s"] = round(st["ttft_s_sum"] / st["ttft_count"], 6) if st["ttft_count"] else None
+        out["mean_tpot_s"] = round(st["tpot_s_sum"] / st["tpot_count"], 6) if st["tpot_count"] else None
         m = getattr(loop.engine, "metrics", None)
         if m is not None:
             out.update(m.summary())

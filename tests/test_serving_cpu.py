@@ -54,6 +54,8 @@ def test_completions_match_engine_generate(server):
     assert resp[0]["usage"] == {"prompt_tokens": 6, "completion_tokens": 6, "total_tokens": 12}
     m = requests.get(url + "/metrics", timeout=5).json()
     assert m["completed"] == 4 and m["generated_tokens"] == 24
+    assert m["ttft_count"] == 4 and m["tpot_count"] == 4
+    assert 0 < m["mean_ttft_s"] < 60 and 0 < m["mean_tpot_s"] < 60
 
 
 def test_text_prompt_and_validation(server):
