@@ -229,6 +229,36 @@ class ModelArchConfig:
                 quant=quant,
                 weight_block_size=block,
             )
+        if (arch == "DeepseekForCausalLM" or hf.get("model_type") == "deepseek") and "kv_lora_rank" not in hf:
+            # DeepSeek V1 (DeepSeekMoE): multi-head attention, fine-grained + shared experts
+            heads = hf["num_attention_heads"]
+            return cls(
+                architecture="DeepseekForCausalLM",
+                hidden_size=hf["hidden_size"],
+                num_hidden_layers=hf["num_hidden_layers"],
+                vocab_size=hf["vocab_size"],
+                num_attention_heads=heads,
+                attention_type="gqa",
+                num_key_value_heads=hf.get("num_key_value_heads") or heads,
+                head_dim=hf.get("head_dim") or hf["hidden_size"] // heads,
+                qk_norm=False,
+                intermediate_size=hf["intermediate_size"],
+                first_k_dense_replace=hf.get("first_k_dense_replace", 0),
+                moe_layer_freq=hf.get("moe_layer_freq", 1),
+                n_routed_experts=hf.get("n_routed_experts") or 0,
+                num_experts_per_tok=hf.get("num_experts_per_tok") or 0,
+                moe_intermediate_size=hf.get("moe_intermediate_size", 0),
+                n_shared_experts=hf.get("n_shared_experts") or 0,
+                scoring_func=hf.get("scoring_func", "softmax"),
+                norm_topk_prob=bool(hf.get("norm_topk_prob", False)),
+                rms_norm_eps=hf.get("rms_norm_eps", 1e-6),
+                rope_theta=hf.get("rope_theta", 10000.0),
+                rope_scaling=hf.get("rope_scaling"),
+                max_position_embeddings=hf.get("max_position_embeddings", 4096),
+                tie_word_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                quant=quant,
+                weight_block_size=block,
+            )
         if arch in DEEPSEEK_ARCHS or hf.get("model_type", "").startswith("deepseek"):
             return cls(
                 architecture=arch or "DeepseekV2ForCausalLM",
@@ -510,6 +540,41 @@ TINY_DSV3 = DSV3_32L.scaled(
     quant=None,
 )
 
+# DeepSeek V1 (deepseek-moe-16b): multi-head attention (16 x 128), 64
+# fine-grained experts top-6 plus 2 shared experts, layer 0 dense.
+DSV1_MOE_16B = ModelArchConfig(
+    architecture="DeepseekForCausalLM",
+    hidden_size=2048,
+    num_hidden_layers=28,
+    vocab_size=102400,
+    num_attention_heads=16,
+    attention_type="gqa",
+    num_key_value_heads=16,
+    head_dim=128,
+    intermediate_size=10944,
+    first_k_dense_replace=1,
+    n_routed_experts=64,
+    num_experts_per_tok=6,
+    moe_intermediate_size=1408,
+    n_shared_experts=2,
+    max_position_embeddings=4096,
+)
+
+TINY_DSV1 = DSV1_MOE_16B.scaled(
+    hidden_size=256,
+    num_hidden_layers=3,
+    vocab_size=1024,
+    num_attention_heads=4,
+    num_key_value_heads=4,
+    head_dim=64,
+    intermediate_size=512,
+    n_routed_experts=8,
+    num_experts_per_tok=2,
+    moe_intermediate_size=128,
+    n_shared_experts=1,
+    max_position_embeddings=2048,
+)
+
 # DeepSeek-V3.2 shapes on the 32-layer DSV3 body: DeepSeek sparse attention
 # with a 64-head, 128-dim lightning indexer selecting 2048 tokens per query.
 DSV32_32L = DSV3_32L.scaled(architecture="DeepseekV32ForCausalLM", index_topk=2048, index_n_heads=64,
@@ -617,6 +682,8 @@ PRESETS: dict[str, ModelArchConfig] = {
     "tiny-dsv2": TINY_DSV2,
     "tiny-dsv3": TINY_DSV3,
     "tiny-dsv32": TINY_DSV32,
+    "tiny-dsv1": TINY_DSV1,
+    "deepseek-moe-16b": DSV1_MOE_16B,
     "deepseek-v3.2-32l": DSV32_32L,
     "tiny-qwen3-moe": TINY_QWEN3_MOE,
     "deepseek-v2-lite": DSV2_LITE,
@@ -637,6 +704,7 @@ def get_preset(name: str) -> ModelArchConfig:
 
 __all__ = [
     "DSV2_LITE",
+    "DSV1_MOE_16B",
     "DSV32_32L",
     "DSV3_32L",
     "ModelArchConfig",

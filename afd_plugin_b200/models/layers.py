@@ -301,7 +301,8 @@ class MLAAttention(nn.Module):
 
 
 class GQAAttention(nn.Module):
-    """Grouped-query attention with per-head QK RMSNorm (Qwen3)."""
+    """Grouped-query attention, with per-head QK RMSNorm when ``arch.qk_norm`` (Qwen3);
+    without it, the multi-head attention of DeepSeek V1 (``kv heads == heads``)."""
 
     def __init__(self, arch: ModelArchConfig, dtype, device, tp: TPInfo = TPInfo()):
         super().__init__()
@@ -313,16 +314,22 @@ class GQAAttention(nn.Module):
         self.scale = arch.softmax_scale
         H = arch.hidden_size
         self.qkv_proj = _param(((self.nq + 2 * self.nkv) * self.d, H), dtype, device)
-        self.q_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
-        self.k_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
+        self.qk_norm = arch.qk_norm
+        if self.qk_norm:
+            self.q_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
+            self.k_norm = RMSNorm(self.d, arch.rms_norm_eps, dtype, device)
         self.o_proj = _param((H, self.nq * self.d), dtype, device)
 
     def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache: tuple[torch.Tensor, torch.Tensor], cos_sin):
         T = h.shape[0]
         qkv = ops.linear(h, self.qkv_proj)
         q, k, v = qkv.split([self.nq * self.d, self.nkv * self.d, self.nkv * self.d], dim=-1)
-        q = self.q_norm(q.reshape(T * self.nq, self.d)).view(T, self.nq, self.d)
-        k = self.k_norm(k.reshape(T * self.nkv, self.d)).view(T, self.nkv, self.d)
+        if self.qk_norm:
+            q = self.q_norm(q.reshape(T * self.nq, self.d)).view(T, self.nq, self.d)
+            k = self.k_norm(k.reshape(T * self.nkv, self.d)).view(T, self.nkv, self.d)
+        else:  # contiguous head rows for the in-place rope and the cache-write kernel
+            q = q.reshape(T, self.nq, self.d).contiguous()
+            k = k.reshape(T, self.nkv, self.d).contiguous()
         v = v.reshape(T, self.nkv, self.d)
         ops.rope_(q, meta.positions, cos_sin, interleaved=False)
         ops.rope_(k, meta.positions, cos_sin, interleaved=False)

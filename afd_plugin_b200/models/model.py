@@ -446,6 +446,20 @@ def _mlp_specs(p: str, mlp: DenseMLP, inter: int) -> Iterator[ParamSpec]:
     yield from _swiglu_specs(p, mlp.w13, mlp.w2, mlp.w13_scale, mlp.w2_scale, inter, hidden)
 
 
+def _gqa_specs(p: str, attn: GQAAttention, a: ModelArchConfig) -> Iterator[ParamSpec]:
+    """Full checkpoint shapes of ``q/k/v/o_proj`` (+ QK norms); a tensor-parallel rank keeps its heads."""
+    d, nq, nkv = attn.d, attn.nq, attn.nkv
+    H, nq_all, nkv_all = a.hidden_size, a.num_attention_heads, a.num_key_value_heads
+    yield ParamSpec(p + "q_proj.weight", (nq_all * d, H), _rows_of(attn.qkv_proj, 0, attn.q0 * d, nq * d))
+    yield ParamSpec(p + "k_proj.weight", (nkv_all * d, H), _rows_of(attn.qkv_proj, nq * d, attn.kv0 * d, nkv * d))
+    yield ParamSpec(p + "v_proj.weight", (nkv_all * d, H),
+                    _rows_of(attn.qkv_proj, (nq + nkv) * d, attn.kv0 * d, nkv * d))
+    if attn.qk_norm:
+        yield ParamSpec(p + "q_norm.weight", (d,), _copy(attn.q_norm.weight), "ones")
+        yield ParamSpec(p + "k_norm.weight", (d,), _copy(attn.k_norm.weight), "ones")
+    yield ParamSpec(p + "o_proj.weight", (H, nq_all * d), _cols_of(attn.o_proj, attn.q0 * d))
+
+
 def _gate_specs(p: str, gate) -> Iterator[ParamSpec]:
     yield ParamSpec(p + "weight", tuple(gate.weight.shape), _copy(gate.weight))
     if gate.e_score_correction_bias is not None:
@@ -496,7 +510,20 @@ class AFDDeepseekV3ForCausalLM(AFDDeepseekV2ForCausalLM):
 
 
 class AFDDeepseekForCausalLM(AFDDeepseekV2ForCausalLM):
-    pass
+    """DeepSeek V1 (DeepSeekMoE): multi-head attention (``q/k/v/o_proj``, no QK
+    norm) with the DeepSeek MoE; MLA checkpoints of this class name load as V2.
+    The reference picks the same split by ``model_type == "deepseek"``
+    (``afd_plugin/model_executor/models/deepseek_v2.py:333-337``)."""
+
+    def _validate_arch(self, arch: ModelArchConfig) -> None:
+        if not arch.is_mla and arch.qk_norm:
+            raise ValueError("DeepSeek V1 attention has no QK norm")
+
+    def _attn_specs(self, p: str, attn) -> Iterator[ParamSpec]:
+        if self.arch.is_mla:
+            yield from super()._attn_specs(p, attn)
+        else:
+            yield from _gqa_specs(p, attn, self.arch)
 
 
 class AFDGlmMoeDsaForCausalLM(AFDDeepseekV2ForCausalLM):
@@ -518,17 +545,7 @@ class AFDQwen3MoeForCausalLM(AFDCausalLM):
             raise ValueError("Qwen3-MoE wrapper requires GQA attention with QK-norm")
 
     def _attn_specs(self, p: str, attn: GQAAttention) -> Iterator[ParamSpec]:
-        """Full checkpoint shapes; a tensor-parallel rank keeps its heads' rows / columns."""
-        d, nq, nkv = attn.d, attn.nq, attn.nkv
-        a = self.arch
-        H, nq_all, nkv_all = a.hidden_size, a.num_attention_heads, a.num_key_value_heads
-        yield ParamSpec(p + "q_proj.weight", (nq_all * d, H), _rows_of(attn.qkv_proj, 0, attn.q0 * d, nq * d))
-        yield ParamSpec(p + "k_proj.weight", (nkv_all * d, H), _rows_of(attn.qkv_proj, nq * d, attn.kv0 * d, nkv * d))
-        yield ParamSpec(p + "v_proj.weight", (nkv_all * d, H),
-                        _rows_of(attn.qkv_proj, (nq + nkv) * d, attn.kv0 * d, nkv * d))
-        yield ParamSpec(p + "q_norm.weight", (d,), _copy(attn.q_norm.weight), "ones")
-        yield ParamSpec(p + "k_norm.weight", (d,), _copy(attn.k_norm.weight), "ones")
-        yield ParamSpec(p + "o_proj.weight", (H, nq_all * d), _cols_of(attn.o_proj, attn.q0 * d))
+        yield from _gqa_specs(p, attn, self.arch)
 
 
 class AFDDeepseekV4ForCausalLM(AFDDeepseekV2ForCausalLM):

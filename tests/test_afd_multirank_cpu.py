@@ -113,3 +113,11 @@ def test_dsv32_attention_tp2():
     ref = _colocated("tiny-dsv32", prompts, 5)
     outs, _ = _run("tiny-dsv32", {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=5, tp=2)
     assert outs == ref
+
+
+def test_deepseek_v1_mha_2a1f():
+    """DeepSeek V1: multi-head attention on the Attention side, routed + shared experts on the FFN side."""
+    prompts = _prompts(n=4, length=12)
+    ref = _colocated("tiny-dsv1", prompts, 6)
+    outs, _ = _run("tiny-dsv1", {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=6)
+    assert outs == ref

@@ -24,7 +24,8 @@ def _prompts(n, length, vocab, seed=0):
     return torch.randint(0, vocab, (n, length), generator=g).tolist()
 
 
-@pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-dsv2-mla512", "tiny-qwen3-moe", "tiny-qwen3.5", "tiny-dsv4"])
+@pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-dsv2-mla512", "tiny-qwen3-moe", "tiny-qwen3.5", "tiny-dsv4",
+                                    "tiny-dsv1"])
 def test_graph_decode_matches_eager(preset):
     prompts = _prompts(6, 20, 1024)
     eager = _engine(preset, eager=True).generate(prompts, 8)

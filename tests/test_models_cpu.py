@@ -12,7 +12,7 @@ from afd_plugin_b200.models.configs import ModelArchConfig
 from afd_plugin_b200.models.loader import load_weights
 from afd_plugin_b200.runtime.engine import LLMEngine
 
-PRESETS = ["tiny-dsv2", "tiny-qwen3-moe", "tiny-dsv3", "tiny-qwen3.5", "tiny-dsv4"]
+PRESETS = ["tiny-dsv2", "tiny-qwen3-moe", "tiny-dsv3", "tiny-qwen3.5", "tiny-dsv4", "tiny-dsv1", "tiny-dsv32"]
 
 
 def _engine(preset, **kw):
@@ -182,3 +182,18 @@ def zlib_crc(name: str) -> int:
     import zlib
 
     return zlib.crc32(name.encode()) & 0xFFFF
+
+
+def test_deepseek_v1_config_is_multi_head_attention():
+    hf = {"architectures": ["DeepseekForCausalLM"], "model_type": "deepseek", "hidden_size": 2048,
+          "num_hidden_layers": 28, "vocab_size": 102400, "num_attention_heads": 16, "num_key_value_heads": 16,
+          "intermediate_size": 10944, "moe_intermediate_size": 1408, "n_routed_experts": 64,
+          "num_experts_per_tok": 6, "n_shared_experts": 2, "first_k_dense_replace": 1, "moe_layer_freq": 1,
+          "scoring_func": "softmax", "norm_topk_prob": False}
+    a = ModelArchConfig.from_hf_config(hf)
+    assert a.attention_type == "gqa" and a.head_dim == 128 and not a.qk_norm
+    assert MODEL_REGISTRY[a.architecture].__name__ == "AFDDeepseekForCausalLM"
+    assert a == get_preset("deepseek-moe-16b").scaled(rope_scaling=None)
+    m = build_model(get_preset("tiny-dsv1"), role="attention", dtype=torch.float32, seed=0)
+    names = {s.name for s in m.param_specs()}
+    assert "model.layers.1.self_attn.k_proj.weight" in names and not any("q_norm" in n for n in names)
