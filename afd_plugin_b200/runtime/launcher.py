@@ -79,9 +79,7 @@ def split_prompts(prompts: list[list[int]], n: int) -> list[list[list[int]]]:
     return out
 
 
-def _rank_main(world_rank: int, world_size: int, port: int, spec: LocalAFDSpec, results) -> None:
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
+def _rank_main(world_rank: int, world_size: int, rendezvous: str, spec: LocalAFDSpec, results) -> None:
     try:
         from afd_plugin_b200.parallel.topology import role_of_world_rank
 
@@ -92,7 +90,7 @@ def _rank_main(world_rank: int, world_size: int, port: int, spec: LocalAFDSpec, 
         local_rank = world_rank
         if backend == "nccl":
             torch.cuda.set_device(local_rank)
-        dist.init_process_group(backend=backend, rank=world_rank, world_size=world_size,
+        dist.init_process_group(backend=backend, init_method=rendezvous, rank=world_rank, world_size=world_size,
                                 timeout=timedelta(seconds=spec.timeout_s))
         afd = dict(spec.afd, role=role)
         spec_local = LocalAFDSpec(**{**spec.__dict__, "afd": afd})
@@ -149,12 +147,18 @@ def launch_local(spec: LocalAFDSpec, *, join_timeout_s: float = 180.0) -> dict[i
     world = A + F
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
-    port = free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, spec, results), daemon=False) for r in range(world)]
-    for p in procs:
-        p.start()
+    # Rendezvous through a file of a fresh directory: no port to race for
+    # (a port probed free can be taken again before rank 0 binds it).
+    import shutil
+    import tempfile
     import time
 
+    rdv_dir = tempfile.mkdtemp(prefix="afd_rdv_")
+    rendezvous = "file://" + os.path.join(rdv_dir, "store")
+    procs = [ctx.Process(target=_rank_main, args=(r, world, rendezvous, spec, results), daemon=False)
+             for r in range(world)]
+    for p in procs:
+        p.start()
     deadline = time.time() + join_timeout_s
     for p in procs:
         p.join(timeout=max(0.1, deadline - time.time()))
@@ -169,6 +173,7 @@ def launch_local(spec: LocalAFDSpec, *, join_timeout_s: float = 180.0) -> dict[i
             out.setdefault(r, {"error": "timeout: rank still running"})
         elif p.exitcode not in (0, None) and r not in out:
             out[r] = {"error": f"exit code {p.exitcode}"}
+    shutil.rmtree(rdv_dir, ignore_errors=True)
     return out
 
 
