@@ -103,7 +103,8 @@ class LLMEngine:
                                   max_blocks_per_seq=self.max_blocks_per_seq, num_ubatches=num_ub)
         self.coordinator = coordinator or AttentionCoordinator()
         policy = validate_cuda_graph_mode(engine_config, role="attention")
-        self.use_graphs = policy.enabled and self.device.type == "cuda"
+        self.use_graphs = (policy.enabled and self.device.type == "cuda"
+                           and getattr(self.ffn, "supports_graph_capture", True))
         self.capture_sizes = sorted(engine_config.compilation_config.cudagraph_capture_sizes) if self.use_graphs else []
         self._ids = itertools.count()
         self.waiting: list[Request] = []

@@ -30,7 +30,13 @@ from afd_plugin_b200.connectors.metadata import (
 
 
 class FFNExecutor:
-    """Interface; ``begin_step`` is called once per forward before layer 0."""
+    """Interface; ``begin_step`` is called once per forward before layer 0.
+
+    ``supports_graph_capture``: whether a decode step through this executor
+    may be captured into a CUDA graph (the engine runs eagerly otherwise).
+    """
+
+    supports_graph_capture = True
 
     def begin_step(self, stage_tokens: dict[int, int], **flags: Any) -> None:
         """``flags``: is_warmup / is_graph_capturing / is_graph_replaying / tokens_across_attn."""
@@ -80,6 +86,9 @@ class ConnectorFFNExecutor(FFNExecutor):
     def __init__(self, model, connector, *, attn_dp_group=None, attn_size: int = 1, attn_rank: int = 0):
         self.model = model
         self.connector = connector
+        # Point-to-point sends through torch.distributed are not captured into
+        # graphs here; the FFN side of this connector runs eagerly as well.
+        self.supports_graph_capture = bool(getattr(connector, "supports_graph_capture", False))
         self.group = attn_dp_group
         self.attn_size = attn_size
         self.attn_rank = attn_rank

@@ -266,3 +266,12 @@ def test_reload_weights_delegates_and_worker_refuses_while_serving():
         worker._thread.join()
     worker.reload_weights()
     assert seen[-1] == (None, 11)
+
+
+def test_attention_side_graphs_follow_the_connector():
+    from afd_plugin_b200.runtime.ffn_executor import ConnectorFFNExecutor, LocalFFNExecutor
+
+    model = SimpleNamespace(compute_gate_on_attention=False)
+    assert ConnectorFFNExecutor(model, SimpleNamespace()).supports_graph_capture is False
+    assert ConnectorFFNExecutor(model, SimpleNamespace(supports_graph_capture=True)).supports_graph_capture
+    assert LocalFFNExecutor(model).supports_graph_capture
