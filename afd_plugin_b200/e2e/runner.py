@@ -86,7 +86,22 @@ def gate(metrics: dict, *, min_exact: float, min_first: float) -> list[str]:
     return bad
 
 
-def run_scenario(scn: Scenario, args, prompts: list[list[int]], *, log_dir: str) -> dict:
+_PORT_TAKEN = ("address already in use", "EADDRINUSE", "error while attempting to bind")
+
+
+def run_scenario(scn: Scenario, args, prompts: list[list[int]], *, log_dir: str, attempts: int = 3) -> dict:
+    """Serve ``scn`` and run the prompts; a server that lost its probed port to
+    another process is started again on fresh ports (up to ``attempts`` times)."""
+    for attempt in range(1, attempts + 1):
+        try:
+            return _run_scenario_once(scn, args, prompts, log_dir=log_dir)
+        except RuntimeError as exc:
+            if attempt == attempts or not any(m in str(exc) for m in _PORT_TAKEN):
+                raise
+    raise AssertionError("unreachable")
+
+
+def _run_scenario_once(scn: Scenario, args, prompts: list[list[int]], *, log_dir: str) -> dict:
     port, master = free_port(), free_port()
     cmd = server_command(scn, python=sys.executable, preset=args.preset, port=port, master_port=master,
                          checkpoint=args.checkpoint, dtype=args.dtype, max_num_seqs=args.max_num_seqs,

@@ -107,3 +107,27 @@ def test_runner_cpu_baseline_vs_afd(tmp_path):
     for r in res[1:]:
         assert r["agreement"]["exact_match"] == 1.0 and r["gate"] == "pass", r["scenario"]
     assert all(r["teardown"] in ("terminated", "killed", "exited") for r in res)
+
+
+def test_scenario_restarts_on_a_taken_port(monkeypatch, tmp_path):
+    calls = []
+
+    def once(scn, args, prompts, *, log_dir):
+        calls.append(1)
+        if len(calls) < 3:
+            raise RuntimeError("server exited with code 1 before it was healthy:\n[Errno 98] address already in use")
+        return {"scenario": scn.name, "outputs": []}
+
+    monkeypatch.setattr(runner, "_run_scenario_once", once)
+    res = runner.run_scenario(SCENARIOS["afd-eager-2a1f"], None, [], log_dir=str(tmp_path))
+    assert res["scenario"] == "afd-eager-2a1f" and len(calls) == 3
+    calls.clear()
+
+    def broken(scn, args, prompts, *, log_dir):
+        calls.append(1)
+        raise RuntimeError("server exited with code 1 before it was healthy:\nValueError: bad config")
+
+    monkeypatch.setattr(runner, "_run_scenario_once", broken)
+    with pytest.raises(RuntimeError, match="bad config"):
+        runner.run_scenario(SCENARIOS["afd-eager-2a1f"], None, [], log_dir=str(tmp_path))
+    assert len(calls) == 1
