@@ -1,6 +1,7 @@
 """Failure detection without any GPU fault: host-side injected failures on gloo ranks."""
 
 import os
+import tempfile
 import time
 from datetime import timedelta
 
@@ -9,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from afd_plugin_b200.runtime.launcher import LocalAFDSpec, free_port, launch_local
+from afd_plugin_b200.runtime.launcher import LocalAFDSpec, launch_local
 from afd_plugin_b200.runtime.watchdog import HeartbeatWatchdog
 
 
@@ -58,10 +59,9 @@ def test_ffn_loop_error_reraised():
         w.execute_model()
 
 
-def _hb_rank(rank, world, port, q):
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=20))
+def _hb_rank(rank, world, path, q):
+    store = dist.FileStore(path, world)
+    store.set_timeout(timedelta(seconds=20))
     # start together (process start-up times differ by seconds under load)
     store.add("ready", 1)
     while int(store.add("ready", 0)) < world:
@@ -83,8 +83,8 @@ def _hb_rank(rank, world, port, q):
 def test_heartbeat_watchdog_detects_silent_peer():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = free_port()
-    ps = [ctx.Process(target=_hb_rank, args=(r, 3, port, q)) for r in range(3)]
+    path = os.path.join(tempfile.mkdtemp(prefix="afd_hb_"), "store")
+    ps = [ctx.Process(target=_hb_rank, args=(r, 3, path, q)) for r in range(3)]
     for p in ps:
         p.start()
     for p in ps:

@@ -1,5 +1,7 @@
 """HTTP completions server over a colocated engine (CPU)."""
 
+import os
+import tempfile
 import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
@@ -68,7 +70,7 @@ def test_text_prompt_and_validation(server):
     assert byte_detokenize(byte_tokenize("héllo", 1024)) == "héllo"
 
 
-def _afd_serving_rank(world_rank, port, prompts, q):
+def _afd_serving_rank(world_rank, rendezvous, prompts, q):
     import os
     from datetime import timedelta
 
@@ -77,9 +79,8 @@ def _afd_serving_rank(world_rank, port, prompts, q):
     from afd_plugin_b200.runtime.launcher import LocalAFDSpec, build_engine_config
     from afd_plugin_b200.parallel.topology import role_of_world_rank
 
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=world_rank, world_size=3, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", init_method=rendezvous, rank=world_rank, world_size=3,
+                            timeout=timedelta(seconds=60))
     role, role_rank = role_of_world_rank(world_rank, attention_size=2, ffn_size=1)
     spec = LocalAFDSpec(preset="tiny-dsv2", afd={"num_attention_ranks": 2, "num_ffn_ranks": 1, "role": role})
     ec = build_engine_config(spec)
@@ -113,8 +114,8 @@ def test_engine_loop_lockstep_across_attention_ranks():
     want = _engine().generate(prompts, 5)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = free_port()
-    ps = [ctx.Process(target=_afd_serving_rank, args=(r, port, prompts, q)) for r in range(3)]
+    rendezvous = "file://" + os.path.join(tempfile.mkdtemp(prefix="afd_rdv_"), "store")
+    ps = [ctx.Process(target=_afd_serving_rank, args=(r, rendezvous, prompts, q)) for r in range(3)]
     for p in ps:
         p.start()
     got = dict(q.get(timeout=180) for _ in range(3))
