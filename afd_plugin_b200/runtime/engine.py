@@ -164,6 +164,21 @@ class LLMEngine:
         self.waiting.append(req)
         return req.req_id
 
+    def request(self, req_id: int) -> Request | None:
+        """The request with this id (waiting, running, imported or finished), or None."""
+        if req_id in self.finished:
+            return self.finished[req_id]
+        for r in self.running:
+            if r.req_id == req_id:
+                return r
+        for r in self.waiting:
+            if r.req_id == req_id:
+                return r
+        for r, _ in self._kv_waiting:
+            if r.req_id == req_id:
+                return r
+        return None
+
     # -------------------------------------------- prefill -> decode hand-off
     def export_kv(self, req_id: int) -> bytes:
         """Serialise a held request's cache rows and recurrent state, then free them."""

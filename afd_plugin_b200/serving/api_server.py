@@ -9,7 +9,8 @@ them has work, so all of them step together (the coordinator pads idle ranks
 with a placeholder row, as the reference's DP dummy batches do).
 
 Endpoints: ``GET /health``, ``GET /metrics`` (engine counters),
-``POST /v1/completions`` with ``{"prompt": str | [int], "max_tokens": int}``,
+``POST /v1/completions`` with ``{"prompt": str | [int], "max_tokens": int,
+"stream": bool}`` (streamed as server-sent events, one chunk per token),
 and for prefill -> decode disaggregation ``GET`` / ``DELETE /v1/kv/{id}``.
 
 Disaggregated prefill uses the request field ``kv_transfer_params`` with the
@@ -27,6 +28,8 @@ benchmark drivers that send token ids directly.
 
 from __future__ import annotations
 
+import json
+import queue
 import threading
 import time
 from concurrent.futures import Future
@@ -42,6 +45,7 @@ class CompletionRequest(BaseModel):
     max_tokens: int = 16
     model: str | None = None
     kv_transfer_params: dict | None = None
+    stream: bool = False
 
 
 def byte_tokenize(text: str, vocab_size: int) -> list[int]:
@@ -61,6 +65,10 @@ class _Pending:
     hold_kv: bool = False
     kv_blob: bytes | None = None  # prefilled elsewhere: the exported cache rows
     first_token_at: float | None = None
+    # streaming: every new token goes here as it is produced, then None (or the error)
+    stream: queue.Queue | None = None
+    req: object | None = None  # the engine's Request, for streaming
+    sent: int = 0
 
 
 class EngineLoop:
@@ -101,24 +109,30 @@ class EngineLoop:
         if handoff and self.tp_size > 1:
             raise ValueError("prefill/decode KV hand-off is not supported with attention tensor parallelism")
 
-    def submit(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False) -> Future:
-        """Queue a request; the future resolves with its tokens and carries ``req_id`` once admitted."""
+    def submit(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False,
+               stream: queue.Queue | None = None) -> Future:
+        """Queue a request; the future resolves with its tokens and carries ``req_id`` once admitted.
+
+        With ``stream`` every token is also put on that queue as soon as it is
+        produced, followed by None (or the exception that ended the request).
+        """
         self._check_entry(hold_kv)
         limit = self.engine.config.model_config.max_model_len
         if len(prompt) + int(max_tokens) > limit:
             raise ValueError(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds max_model_len {limit}")
         fut: Future = Future()
         with self._lock:
-            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, hold_kv=hold_kv))
+            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, hold_kv=hold_kv, stream=stream))
             self.stats["requests"] += 1
         return fut
 
-    def submit_prefilled(self, prompt: list[int], kv_blob: bytes, max_tokens: int) -> Future:
+    def submit_prefilled(self, prompt: list[int], kv_blob: bytes, max_tokens: int, *,
+                         stream: queue.Queue | None = None) -> Future:
         """Queue a request whose prompt was prefilled by another engine (see ``export_kv``)."""
         self._check_entry(True)
         fut: Future = Future()
         with self._lock:
-            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob))
+            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob, stream=stream))
             self.stats["requests"] += 1
         return fut
 
@@ -146,6 +160,13 @@ class EngineLoop:
             self._thread.join(timeout)
             if not self._thread.is_alive():
                 self._thread = None
+
+    @staticmethod
+    def _push_tokens(p: _Pending) -> None:
+        out = p.req.output if p.req is not None else []
+        for t in out[p.sent :]:
+            p.stream.put(t)
+        p.sent = len(out)
 
     def _fan_out(self, new: list[_Pending]) -> list[_Pending]:
         """TP leader -> peers: this iteration's new requests (one gloo broadcast)."""
@@ -189,9 +210,14 @@ class EngineLoop:
                             rid = eng.add_request(p.prompt, p.max_tokens, hold_kv=p.hold_kv)
                     except ValueError as exc:
                         p.future.set_exception(exc)
+                        if p.stream is not None:
+                            p.stream.put(exc)
                         continue
                     p.future.req_id = rid
                     self._inflight[rid] = p
+                    if p.stream is not None:
+                        p.req = eng.request(rid)
+                        self._push_tokens(p)  # a transferred first token streams at once
                 work, stop = self._agree(eng.has_unfinished(), self._stop.is_set())
                 if stop:
                     break
@@ -203,10 +229,14 @@ class EngineLoop:
                 self.stats["steps"] += 1
                 for rid in produced:
                     p = self._inflight.get(rid)
-                    if p is not None and p.first_token_at is None:
+                    if p is None:
+                        continue
+                    if p.first_token_at is None:
                         p.first_token_at = now
                         self.stats["ttft_s_sum"] += now - p.submitted
                         self.stats["ttft_count"] += 1
+                    if p.stream is not None:
+                        self._push_tokens(p)
                 for rid in [r for r in self._inflight if r in eng.finished]:
                     p = self._inflight.pop(rid)
                     out = eng.finished.pop(rid).output
@@ -215,12 +245,17 @@ class EngineLoop:
                     if p.first_token_at is not None and len(out) > 1:
                         self.stats["tpot_s_sum"] += (now - p.first_token_at) / (len(out) - 1)
                         self.stats["tpot_count"] += 1
+                    if p.stream is not None:
+                        self._push_tokens(p)
+                        p.stream.put(None)
                     p.future.set_result(out)
         except BaseException as exc:  # noqa: BLE001 - surfaced to every waiting client
             self.error = exc
             for p in list(self._inflight.values()) + self._queue:
                 if not p.future.done():
                     p.future.set_exception(exc)
+                if p.stream is not None:
+                    p.stream.put(exc)
             for _, fut in self._calls:
                 if not fut.done():
                     fut.set_exception(exc)
@@ -235,7 +270,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
     """
     import requests
     from fastapi import FastAPI, HTTPException
-    from fastapi.responses import Response
+    from fastapi.responses import Response, StreamingResponse
 
     vocab = loop.engine.model.arch.vocab_size
     app = FastAPI(title="afd_plugin_b200")
@@ -252,6 +287,27 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         if r.status_code != 200:
             raise HTTPException(status_code=502, detail=f"KV fetch from {url}: HTTP {r.status_code}")
         return r.content
+
+    def _sse(tokens: queue.Queue, n_prompt: int, model: str):
+        """Server-sent events: one chunk per token, a final chunk with usage, then ``[DONE]``."""
+        n = 0
+        while True:
+            try:
+                t = tokens.get(timeout=request_timeout_s)
+            except queue.Empty:
+                t = TimeoutError("no token within the request timeout")
+            if t is None:
+                break
+            if isinstance(t, BaseException):
+                yield "data: " + json.dumps({"error": {"message": str(t), "type": type(t).__name__}}) + "\n\n"
+                return
+            n += 1
+            yield "data: " + json.dumps({"object": "text_completion", "model": model, "choices": [
+                {"index": 0, "token_ids": [t], "text": byte_detokenize([t]), "finish_reason": None}]}) + "\n\n"
+        yield "data: " + json.dumps({"object": "text_completion", "model": model, "choices": [
+            {"index": 0, "token_ids": [], "text": "", "finish_reason": "length"}],
+            "usage": {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n}}) + "\n\n"
+        yield "data: [DONE]\n\n"
 
     @app.get("/v1/kv/{req_id}")
     def get_kv(req_id: int):
@@ -292,11 +348,15 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             raise HTTPException(status_code=400, detail=f"prompt token ids must be in [0, {vocab})")
         params = req.kv_transfer_params or {}
         prefill_only = bool(params.get("do_remote_decode"))
+        stream = queue.Queue() if req.stream and not prefill_only else None
         try:
             if params.get("do_remote_prefill"):
-                fut = loop.submit_prefilled(ids, _fetch_kv(params), req.max_tokens)
+                fut = loop.submit_prefilled(ids, _fetch_kv(params), req.max_tokens, stream=stream)
             else:
-                fut = loop.submit(ids, req.max_tokens, hold_kv=prefill_only)
+                fut = loop.submit(ids, req.max_tokens, hold_kv=prefill_only, stream=stream)
+            if stream is not None:
+                return StreamingResponse(_sse(stream, len(ids), req.model or model_name),
+                                         media_type="text/event-stream")
             out = fut.result(timeout=request_timeout_s)
         except ValueError as exc:
             raise HTTPException(status_code=400, detail=str(exc)) from exc

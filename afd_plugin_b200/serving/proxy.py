@@ -15,7 +15,9 @@ Two modes, the ones of the reference's proxy tool (``tools/proxy_server.py``):
 Load is counted in prompt tokens for prefill servers and in requested tokens
 for decode servers, so long prompts spread over the prefill pool the way the
 reference's length-based scores do (``tools/proxy_server.py:205-211``).
-``GET /health`` reports every backend.
+Streaming requests (``"stream": true``) are relayed chunk by chunk; in the
+disaggregated mode only the decode leg streams.  ``GET /health`` reports
+every backend.
 
     python -m afd_plugin_b200.serving.proxy --backends http://127.0.0.1:8001,http://127.0.0.1:8002 --port 8000
     python -m afd_plugin_b200.serving.proxy --prefill http://127.0.0.1:8001 --decode http://127.0.0.1:8002
@@ -79,7 +81,7 @@ def build_prefill_request(body: dict) -> dict:
 def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | None = None,
                     decode: list[str] | None = None, timeout_s: float = 600.0):
     from fastapi import FastAPI, HTTPException
-    from fastapi.responses import JSONResponse
+    from fastapi.responses import JSONResponse, StreamingResponse
 
     pd = bool(prefill or decode)
     if pd and not (prefill and decode):
@@ -91,20 +93,44 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
     app.state.pools = pools
     app.state.balancer = pools.get("backend")
 
-    def _post(url: str, body: dict):
+    def _post(url: str, body: dict, *, stream: bool = False):
         try:
-            return requests.post(url, json=body, timeout=timeout_s)
+            return requests.post(url, json=body, timeout=timeout_s, stream=stream)
         except requests.RequestException as exc:
             raise HTTPException(status_code=502, detail=f"backend {url} failed: {exc}") from exc
+
+    def _answer(r, release):
+        """JSON answers are read whole; event streams are relayed chunk by chunk.
+
+        ``release`` runs once the backend's answer has been consumed.
+        """
+        if r.status_code != 200 or not r.headers.get("content-type", "").startswith("text/event-stream"):
+            try:
+                return JSONResponse(status_code=r.status_code, content=r.json())
+            finally:
+                r.close()
+                release()
+
+        def relay():
+            try:
+                for chunk in r.iter_content(chunk_size=None):
+                    if chunk:
+                        yield chunk
+            finally:
+                r.close()
+                release()
+
+        return StreamingResponse(relay(), media_type="text/event-stream")
 
     def _plain(body: dict):
         bal = pools["backend"]
         b = bal.acquire()
         try:
-            r = _post(b + "/v1/completions", body)
-        finally:
+            r = _post(b + "/v1/completions", body, stream=bool(body.get("stream")))
+        except BaseException:
             bal.release(b)
-        return r.status_code, r.json()
+            raise
+        return _answer(r, lambda: bal.release(b))
 
     def _disaggregated(body: dict):
         pre, dec = pools["prefill"], pools["decode"]
@@ -115,24 +141,28 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
         finally:
             pre.release(p, n_prompt)
         if r1.status_code != 200:
-            return r1.status_code, r1.json()
+            return JSONResponse(status_code=r1.status_code, content=r1.json())
         params = r1.json().get("kv_transfer_params")
         if not params:
             raise HTTPException(status_code=502, detail=f"prefill server {p} returned no kv_transfer_params")
         n_dec = float(body.get("max_tokens", 16))
         d = dec.acquire(n_dec)
-        ok = False
+
+        def drop_held_rows():  # the decode side never fetched the rows: free them now
+            try:
+                requests.delete(f"{p}/v1/kv/{params['remote_request_id']}", timeout=10)
+            except requests.RequestException:
+                pass
+
         try:
-            r2 = _post(d + "/v1/completions", dict(body, kv_transfer_params=params))
-            ok = r2.status_code == 200
-        finally:
+            r2 = _post(d + "/v1/completions", dict(body, kv_transfer_params=params), stream=bool(body.get("stream")))
+        except BaseException:
             dec.release(d, n_dec)
-            if not ok:  # the decode side never fetched the rows: free them now
-                try:
-                    requests.delete(f"{p}/v1/kv/{params['remote_request_id']}", timeout=10)
-                except requests.RequestException:
-                    pass
-        return r2.status_code, r2.json()
+            drop_held_rows()
+            raise
+        if r2.status_code != 200:
+            drop_held_rows()
+        return _answer(r2, lambda: dec.release(d, n_dec))
 
     @app.get("/health")
     def health():
@@ -154,8 +184,7 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
         import anyio
 
         body = await request.json()
-        code, content = await anyio.to_thread.run_sync(lambda: (_disaggregated if pd else _plain)(body))
-        return JSONResponse(status_code=code, content=content)
+        return await anyio.to_thread.run_sync(lambda: (_disaggregated if pd else _plain)(body))
 
     return app
 

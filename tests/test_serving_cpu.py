@@ -218,3 +218,62 @@ def test_disaggregated_prefill_decode_through_proxy():
             s.should_exit = True
         pre_loop.stop()
         dec_loop.stop()
+
+
+def _stream_tokens(url, body):
+    import json as _json
+
+    toks, usage, events = [], None, 0
+    with requests.post(url + "/v1/completions", json=dict(body, stream=True), stream=True, timeout=60) as r:
+        assert r.status_code == 200 and r.headers["content-type"].startswith("text/event-stream")
+        for line in r.iter_lines():
+            if not line or not line.startswith(b"data: "):
+                continue
+            data = line[len(b"data: "):]
+            if data == b"[DONE]":
+                break
+            events += 1
+            msg = _json.loads(data)
+            toks += msg["choices"][0]["token_ids"]
+            usage = msg.get("usage", usage)
+    return toks, usage, events
+
+
+def test_streaming_completions(server):
+    url, _ = server
+    prompt = [5, 9, 100, 7, 3, 1]
+    want = _engine().generate([prompt], 6)[0]
+    toks, usage, events = _stream_tokens(url, {"prompt": prompt, "max_tokens": 6})
+    assert toks == want and events == 7  # one event per token plus the final one with usage
+    assert usage == {"prompt_tokens": 6, "completion_tokens": 6, "total_tokens": 12}
+    r = requests.post(url + "/v1/completions", json={"prompt": [1] * 95, "max_tokens": 8, "stream": True}, timeout=10)
+    assert r.status_code == 400
+
+
+def test_streaming_through_proxies_and_serve_bench():
+    from afd_plugin_b200.bench import serve_bench
+    from afd_plugin_b200.serving.proxy import build_proxy_app
+
+    loops = [EngineLoop(_engine()).start() for _ in range(3)]
+    a, a_url = _serve(lambda port: build_app(loops[0], advertise_port=port))
+    pre, pre_url = _serve(lambda port: build_app(loops[1], advertise_port=port))
+    dec, dec_url = _serve(lambda port: build_app(loops[2], advertise_port=port))
+    plain, plain_url = _serve(lambda port: build_proxy_app([a_url]))
+    pd, pd_url = _serve(lambda port: build_proxy_app(prefill=[pre_url], decode=[dec_url]))
+    try:
+        prompt = [42] * 7
+        want = _engine().generate([prompt], 5)[0]
+        assert _stream_tokens(plain_url, {"prompt": prompt, "max_tokens": 5})[0] == want
+        assert _stream_tokens(pd_url, {"prompt": prompt, "max_tokens": 5})[0] == want
+        summary = serve_bench.main(["--url", pd_url, "--num-prompts", "6", "--input-len", "9", "--output-len", "4",
+                                    "--request-rate", "inf", "--max-concurrency", "3", "--vocab-size", "1024"])
+        assert summary["completed"] == 6 and summary["failed"] == 0
+        assert summary["total_output_tokens"] == 24 and summary["mean_ttft_ms"] > 0
+        assert summary["mean_tpot_ms"] > 0 and summary["p99_e2el_ms"] >= summary["median_e2el_ms"]
+        h = requests.get(pd_url + "/health", timeout=10).json()
+        assert sum(h["decode"]["served"].values()) == 7 and all(v == 0 for v in h["decode"]["inflight"].values())
+    finally:
+        for s in (a, pre, dec, plain, pd):
+            s.should_exit = True
+        for lp in loops:
+            lp.stop()
