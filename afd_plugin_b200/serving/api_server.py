@@ -11,6 +11,7 @@ with a placeholder row, as the reference's DP dummy batches do).
 Endpoints: ``GET /health``, ``GET /metrics`` (engine counters),
 ``POST /v1/completions`` with ``{"prompt": str | [int], "max_tokens": int,
 "stream": bool}`` (streamed as server-sent events, one chunk per token),
+``POST /v1/chat/completions`` (``messages``; rendered by :func:`chat_prompt`),
 and for prefill -> decode disaggregation ``GET`` / ``DELETE /v1/kv/{id}``.
 
 Disaggregated prefill uses the request field ``kv_transfer_params`` with the
@@ -46,6 +47,29 @@ class CompletionRequest(BaseModel):
     model: str | None = None
     kv_transfer_params: dict | None = None
     stream: bool = False
+
+
+class ChatMessage(BaseModel):
+    role: str
+    content: str
+
+
+class ChatCompletionRequest(BaseModel):
+    messages: list[ChatMessage]
+    max_tokens: int | None = None
+    max_completion_tokens: int | None = None
+    model: str | None = None
+    kv_transfer_params: dict | None = None
+    stream: bool = False
+
+
+def chat_prompt(messages: list[ChatMessage]) -> str:
+    """Plain role-tagged transcript ending in the assistant tag.
+
+    No tokenizer or chat template ships with the image, so chat requests are
+    rendered this way and byte-tokenised like text prompts.
+    """
+    return "".join(f"<|{m.role}|>{m.content}\n" for m in messages) + "<|assistant|>"
 
 
 def byte_tokenize(text: str, vocab_size: int) -> list[int]:
@@ -288,7 +312,20 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             raise HTTPException(status_code=502, detail=f"KV fetch from {url}: HTTP {r.status_code}")
         return r.content
 
-    def _sse(tokens: queue.Queue, n_prompt: int, model: str):
+    def _chunk(chat: bool, model: str, tokens: list[int], finish: str | None, usage: dict | None = None) -> str:
+        if chat:
+            delta = {"role": "assistant", "content": byte_detokenize(tokens)} if tokens else {}
+            msg = {"object": "chat.completion.chunk", "model": model,
+                   "choices": [{"index": 0, "delta": delta, "token_ids": tokens, "finish_reason": finish}]}
+        else:
+            msg = {"object": "text_completion", "model": model,
+                   "choices": [{"index": 0, "token_ids": tokens, "text": byte_detokenize(tokens),
+                                "finish_reason": finish}]}
+        if usage is not None:
+            msg["usage"] = usage
+        return "data: " + json.dumps(msg) + "\n\n"
+
+    def _sse(tokens: queue.Queue, n_prompt: int, model: str, chat: bool):
         """Server-sent events: one chunk per token, a final chunk with usage, then ``[DONE]``."""
         n = 0
         while True:
@@ -302,12 +339,43 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
                 yield "data: " + json.dumps({"error": {"message": str(t), "type": type(t).__name__}}) + "\n\n"
                 return
             n += 1
-            yield "data: " + json.dumps({"object": "text_completion", "model": model, "choices": [
-                {"index": 0, "token_ids": [t], "text": byte_detokenize([t]), "finish_reason": None}]}) + "\n\n"
-        yield "data: " + json.dumps({"object": "text_completion", "model": model, "choices": [
-            {"index": 0, "token_ids": [], "text": "", "finish_reason": "length"}],
-            "usage": {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n}}) + "\n\n"
+            yield _chunk(chat, model, [t], None)
+        yield _chunk(chat, model, [], "length",
+                     {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n})
         yield "data: [DONE]\n\n"
+
+    def _generate(ids: list[int], max_tokens: int, params: dict | None, stream_req: bool, model: str, chat: bool):
+        if max_tokens < 1:
+            raise HTTPException(status_code=400, detail="max_tokens must be positive")
+        if any((not isinstance(t, int)) or t < 0 or t >= vocab for t in ids):
+            raise HTTPException(status_code=400, detail=f"prompt token ids must be in [0, {vocab})")
+        params = params or {}
+        prefill_only = bool(params.get("do_remote_decode"))
+        stream = queue.Queue() if stream_req and not prefill_only else None
+        try:
+            if params.get("do_remote_prefill"):
+                fut = loop.submit_prefilled(ids, _fetch_kv(params), max_tokens, stream=stream)
+            else:
+                fut = loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream)
+            if stream is not None:
+                return StreamingResponse(_sse(stream, len(ids), model, chat), media_type="text/event-stream")
+            out = fut.result(timeout=request_timeout_s)
+        except ValueError as exc:
+            raise HTTPException(status_code=400, detail=str(exc)) from exc
+        usage = {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)}
+        if chat:
+            body = {"object": "chat.completion", "model": model, "usage": usage, "choices": [
+                {"index": 0, "message": {"role": "assistant", "content": byte_detokenize(out)}, "token_ids": out,
+                 "finish_reason": "length"}]}
+        else:
+            body = {"object": "text_completion", "model": model, "usage": usage, "choices": [
+                {"index": 0, "token_ids": out, "text": byte_detokenize(out), "finish_reason": "length"}]}
+        if prefill_only:
+            body["kv_transfer_params"] = {
+                "do_remote_prefill": True, "do_remote_decode": False,
+                "remote_request_id": fut.req_id, "remote_host": advertise_host, "remote_port": advertise_port,
+            }
+        return body
 
     @app.get("/v1/kv/{req_id}")
     def get_kv(req_id: int):
@@ -341,39 +409,16 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     @app.post("/v1/completions")
     def completions(req: CompletionRequest):
-        if req.max_tokens < 1:
-            raise HTTPException(status_code=400, detail="max_tokens must be positive")
         ids = req.prompt if isinstance(req.prompt, list) else byte_tokenize(req.prompt, vocab)
-        if any((not isinstance(t, int)) or t < 0 or t >= vocab for t in ids):
-            raise HTTPException(status_code=400, detail=f"prompt token ids must be in [0, {vocab})")
-        params = req.kv_transfer_params or {}
-        prefill_only = bool(params.get("do_remote_decode"))
-        stream = queue.Queue() if req.stream and not prefill_only else None
-        try:
-            if params.get("do_remote_prefill"):
-                fut = loop.submit_prefilled(ids, _fetch_kv(params), req.max_tokens, stream=stream)
-            else:
-                fut = loop.submit(ids, req.max_tokens, hold_kv=prefill_only, stream=stream)
-            if stream is not None:
-                return StreamingResponse(_sse(stream, len(ids), req.model or model_name),
-                                         media_type="text/event-stream")
-            out = fut.result(timeout=request_timeout_s)
-        except ValueError as exc:
-            raise HTTPException(status_code=400, detail=str(exc)) from exc
-        body = {
-            "object": "text_completion",
-            "model": req.model or model_name,
-            "choices": [{"index": 0, "token_ids": out, "text": byte_detokenize(out), "finish_reason": "length"}],
-            "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)},
-        }
-        if prefill_only:
-            body["kv_transfer_params"] = {
-                "do_remote_prefill": True, "do_remote_decode": False,
-                "remote_request_id": fut.req_id, "remote_host": advertise_host, "remote_port": advertise_port,
-            }
-        return body
+        return _generate(ids, req.max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, False)
+
+    @app.post("/v1/chat/completions")
+    def chat_completions(req: ChatCompletionRequest):
+        max_tokens = req.max_completion_tokens or req.max_tokens or 16
+        ids = byte_tokenize(chat_prompt(req.messages), vocab)
+        return _generate(ids, max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, True)
 
     return app
 
 
-__all__ = ["EngineLoop", "build_app", "byte_detokenize", "byte_tokenize"]
+__all__ = ["EngineLoop", "build_app", "byte_detokenize", "byte_tokenize", "chat_prompt"]

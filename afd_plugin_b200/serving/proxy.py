@@ -2,8 +2,9 @@
 
 Two modes, the ones of the reference's proxy tool (``tools/proxy_server.py``):
 
-* ``--backends``: each ``POST /v1/completions`` goes to the backend with the
-  least load in flight (ties: round robin) and the JSON answer is forwarded.
+* ``--backends``: each ``POST /v1/completions`` (or ``/v1/chat/completions``)
+  goes to the backend with the least load in flight (ties: round robin) and
+  the answer is forwarded.
 * ``--prefill`` + ``--decode``: the request first runs on a prefill server with
   ``max_tokens=1`` and ``kv_transfer_params={"do_remote_decode": true}``
   (the prefill leg of ``tools/proxy_server.py:850-867``); that server keeps the
@@ -65,6 +66,8 @@ class Balancer:
 
 
 def _prompt_len(body: dict) -> int:
+    if "messages" in body:
+        return max(1, sum(len(str(m.get("content", "")).encode("utf-8")) for m in body["messages"]))
     p = body.get("prompt", "")
     return max(1, len(p) if isinstance(p, list) else len(str(p).encode("utf-8")))
 
@@ -74,6 +77,8 @@ def build_prefill_request(body: dict) -> dict:
     out = dict(body)
     out["kv_transfer_params"] = {"do_remote_decode": True, "do_remote_prefill": False}
     out["max_tokens"] = 1
+    if "max_completion_tokens" in out:
+        out["max_completion_tokens"] = 1
     out["stream"] = False
     return out
 
@@ -122,22 +127,22 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
 
         return StreamingResponse(relay(), media_type="text/event-stream")
 
-    def _plain(body: dict):
+    def _plain(body: dict, path: str):
         bal = pools["backend"]
         b = bal.acquire()
         try:
-            r = _post(b + "/v1/completions", body, stream=bool(body.get("stream")))
+            r = _post(b + path, body, stream=bool(body.get("stream")))
         except BaseException:
             bal.release(b)
             raise
         return _answer(r, lambda: bal.release(b))
 
-    def _disaggregated(body: dict):
+    def _disaggregated(body: dict, path: str):
         pre, dec = pools["prefill"], pools["decode"]
         n_prompt = float(_prompt_len(body))
         p = pre.acquire(n_prompt)
         try:
-            r1 = _post(p + "/v1/completions", build_prefill_request(body))
+            r1 = _post(p + path, build_prefill_request(body))
         finally:
             pre.release(p, n_prompt)
         if r1.status_code != 200:
@@ -155,7 +160,7 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
                 pass
 
         try:
-            r2 = _post(d + "/v1/completions", dict(body, kv_transfer_params=params), stream=bool(body.get("stream")))
+            r2 = _post(d + path, dict(body, kv_transfer_params=params), stream=bool(body.get("stream")))
         except BaseException:
             dec.release(d, n_dec)
             drop_held_rows()
@@ -179,12 +184,19 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
             out = out["backend"]
         return out
 
-    @app.post("/v1/completions")
-    async def completions(request: Request):
+    async def _route(request: Request, path: str):
         import anyio
 
         body = await request.json()
-        return await anyio.to_thread.run_sync(lambda: (_disaggregated if pd else _plain)(body))
+        return await anyio.to_thread.run_sync(lambda: (_disaggregated if pd else _plain)(body, path))
+
+    @app.post("/v1/completions")
+    async def completions(request: Request):
+        return await _route(request, "/v1/completions")
+
+    @app.post("/v1/chat/completions")
+    async def chat_completions(request: Request):
+        return await _route(request, "/v1/chat/completions")
 
     return app
 

@@ -277,3 +277,40 @@ def test_streaming_through_proxies_and_serve_bench():
             s.should_exit = True
         for lp in loops:
             lp.stop()
+
+
+def test_chat_completions_direct_and_disaggregated():
+    from afd_plugin_b200.serving import api_server
+    from afd_plugin_b200.serving.proxy import build_proxy_app
+
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}]
+    ids = byte_tokenize(api_server.chat_prompt([api_server.ChatMessage(**m) for m in msgs]), 1024)
+    want = _engine().generate([ids], 4)[0]
+    loops = [EngineLoop(_engine()).start() for _ in range(2)]
+    pre, pre_url = _serve(lambda port: build_app(loops[0], advertise_port=port))
+    dec, dec_url = _serve(lambda port: build_app(loops[1], advertise_port=port))
+    pd, pd_url = _serve(lambda port: build_proxy_app(prefill=[pre_url], decode=[dec_url]))
+    try:
+        r = requests.post(dec_url + "/v1/chat/completions", json={"messages": msgs, "max_completion_tokens": 4},
+                          timeout=60).json()
+        assert r["object"] == "chat.completion" and r["choices"][0]["token_ids"] == want
+        assert r["choices"][0]["message"]["role"] == "assistant" and r["usage"]["prompt_tokens"] == len(ids)
+        r = requests.post(pd_url + "/v1/chat/completions", json={"messages": msgs, "max_tokens": 4},
+                          timeout=60).json()
+        assert r["choices"][0]["token_ids"] == want
+        toks = []
+        with requests.post(pd_url + "/v1/chat/completions", json={"messages": msgs, "max_tokens": 4, "stream": True},
+                           stream=True, timeout=60) as s:
+            for line in s.iter_lines():
+                if line.startswith(b"data: {"):
+                    import json as _json
+
+                    msg = _json.loads(line[6:])
+                    assert msg["object"] == "chat.completion.chunk"
+                    toks += msg["choices"][0]["token_ids"]
+        assert toks == want
+    finally:
+        for s_ in (pre, dec, pd):
+            s_.should_exit = True
+        for lp in loops:
+            lp.stop()
