@@ -46,6 +46,7 @@ class Request:
     blocks: list[int] = field(default_factory=list)
     state_slot: int = -1  # linear-attention state row (Gated DeltaNet models)
     hold_kv: bool = False  # keep the cache rows after finishing, for export to a decode engine
+    aborted: bool = False  # ended by abort() before reaching max_tokens
 
     @property
     def num_tokens(self) -> int:
@@ -163,6 +164,24 @@ class LLMEngine:
         req = Request(next(self._ids), list(prompt), max_tokens, hold_kv=hold_kv)
         self.waiting.append(req)
         return req.req_id
+
+    def abort(self, req_id: int) -> bool:
+        """End a waiting or running request now (client gone); it moves to ``finished`` with
+        ``aborted`` set and the tokens it has.  Returns False if it is not live."""
+        for lst in (self.waiting, self.running):
+            for i, r in enumerate(lst):
+                if r.req_id == req_id:
+                    del lst[i]
+                    r.aborted, r.hold_kv = True, False
+                    self._finish(r)
+                    return True
+        for i, (r, _) in enumerate(self._kv_waiting):
+            if r.req_id == req_id:
+                del self._kv_waiting[i]
+                r.aborted = True
+                self.finished[req_id] = r
+                return True
+        return False
 
     def request(self, req_id: int) -> Request | None:
         """The request with this id (waiting, running, imported or finished), or None."""

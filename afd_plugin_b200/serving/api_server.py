@@ -121,7 +121,7 @@ class EngineLoop:
         self._stop = threading.Event()
         self._thread: threading.Thread | None = None
         self.error: BaseException | None = None
-        self.stats = {"requests": 0, "completed": 0, "generated_tokens": 0, "steps": 0,
+        self.stats = {"requests": 0, "completed": 0, "aborted": 0, "generated_tokens": 0, "steps": 0,
                       "ttft_s_sum": 0.0, "ttft_count": 0, "tpot_s_sum": 0.0, "tpot_count": 0}
 
     # ------------------------------------------------------------ clients
@@ -159,6 +159,18 @@ class EngineLoop:
             self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob, stream=stream))
             self.stats["requests"] += 1
         return fut
+
+    def abort(self, req_id: int) -> Future:
+        """Stop a request whose client went away (resolves with the tokens it has).
+
+        Not available with attention tensor parallelism: the TP peers would
+        keep the request, so it runs to completion there.
+        """
+        if self.tp_size > 1:
+            fut: Future = Future()
+            fut.set_result(False)
+            return fut
+        return self.call(lambda eng: eng.abort(req_id))
 
     def call(self, fn) -> Future:
         """Run ``fn(engine)`` on the loop thread between steps (engine state is not thread-safe)."""
@@ -224,6 +236,8 @@ class EngineLoop:
                         fut.set_result(fn(eng))
                     except Exception as exc:  # noqa: BLE001 - handed to the caller
                         fut.set_exception(exc)
+                if calls:
+                    self._resolve_finished(time.perf_counter())  # e.g. requests a call aborted
                 if eng.held:
                     eng.expire_held(self.kv_hold_timeout_s)
                 for p in new:
@@ -261,28 +275,36 @@ class EngineLoop:
                         self.stats["ttft_count"] += 1
                     if p.stream is not None:
                         self._push_tokens(p)
-                for rid in [r for r in self._inflight if r in eng.finished]:
-                    p = self._inflight.pop(rid)
-                    out = eng.finished.pop(rid).output
-                    self.stats["completed"] += 1
-                    self.stats["generated_tokens"] += len(out)
-                    if p.first_token_at is not None and len(out) > 1:
-                        self.stats["tpot_s_sum"] += (now - p.first_token_at) / (len(out) - 1)
-                        self.stats["tpot_count"] += 1
-                    if p.stream is not None:
-                        self._push_tokens(p)
-                        p.stream.put(None)
-                    p.future.set_result(out)
+                self._resolve_finished(now)
         except BaseException as exc:  # noqa: BLE001 - surfaced to every waiting client
-            self.error = exc
-            for p in list(self._inflight.values()) + self._queue:
-                if not p.future.done():
-                    p.future.set_exception(exc)
-                if p.stream is not None:
-                    p.stream.put(exc)
-            for _, fut in self._calls:
-                if not fut.done():
-                    fut.set_exception(exc)
+            self._fail_all(exc)
+
+    def _resolve_finished(self, now: float) -> None:
+        eng = self.engine
+        for rid in [r for r in self._inflight if r in eng.finished]:
+            p = self._inflight.pop(rid)
+            req = eng.finished.pop(rid)
+            out = req.output
+            self.stats["aborted" if req.aborted else "completed"] += 1
+            self.stats["generated_tokens"] += len(out)
+            if p.first_token_at is not None and len(out) > 1 and not req.aborted:
+                self.stats["tpot_s_sum"] += (now - p.first_token_at) / (len(out) - 1)
+                self.stats["tpot_count"] += 1
+            if p.stream is not None:
+                self._push_tokens(p)
+                p.stream.put(None)
+            p.future.set_result(out)
+
+    def _fail_all(self, exc: BaseException) -> None:
+        self.error = exc
+        for p in list(self._inflight.values()) + self._queue:
+            if not p.future.done():
+                p.future.set_exception(exc)
+            if p.stream is not None:
+                p.stream.put(exc)
+        for _, fut in self._calls:
+            if not fut.done():
+                fut.set_exception(exc)
 
 
 def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout_s: float = 600.0,
@@ -325,24 +347,44 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             msg["usage"] = usage
         return "data: " + json.dumps(msg) + "\n\n"
 
-    def _sse(tokens: queue.Queue, n_prompt: int, model: str, chat: bool):
-        """Server-sent events: one chunk per token, a final chunk with usage, then ``[DONE]``."""
-        n = 0
-        while True:
-            try:
-                t = tokens.get(timeout=request_timeout_s)
-            except queue.Empty:
-                t = TimeoutError("no token within the request timeout")
-            if t is None:
-                break
-            if isinstance(t, BaseException):
-                yield "data: " + json.dumps({"error": {"message": str(t), "type": type(t).__name__}}) + "\n\n"
-                return
-            n += 1
-            yield _chunk(chat, model, [t], None)
-        yield _chunk(chat, model, [], "length",
-                     {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n})
-        yield "data: [DONE]\n\n"
+    async def _sse(tokens: queue.Queue, fut: Future, n_prompt: int, model: str, chat: bool):
+        """Server-sent events: one chunk per token, a final chunk with usage, then ``[DONE]``.
+
+        Runs on the event loop; a client that disconnects cancels it at its
+        next await, and the request is then aborted so it stops taking a
+        batch slot.
+        """
+        import functools
+
+        import anyio
+
+        n, ended = 0, False
+        deadline = time.monotonic() + request_timeout_s
+        try:
+            while True:
+                try:
+                    t = await anyio.to_thread.run_sync(functools.partial(tokens.get, timeout=0.25))
+                except queue.Empty:
+                    if time.monotonic() < deadline:
+                        continue
+                    t = TimeoutError("no token within the request timeout")
+                if t is None:
+                    break
+                if isinstance(t, BaseException):
+                    ended = True
+                    yield "data: " + json.dumps({"error": {"message": str(t), "type": type(t).__name__}}) + "\n\n"
+                    return
+                n += 1
+                deadline = time.monotonic() + request_timeout_s
+                yield _chunk(chat, model, [t], None)
+            ended = True
+            yield _chunk(chat, model, [], "length",
+                         {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n})
+            yield "data: [DONE]\n\n"
+        finally:
+            rid = getattr(fut, "req_id", None)
+            if not ended and rid is not None:
+                loop.abort(rid)
 
     def _generate(ids: list[int], max_tokens: int, params: dict | None, stream_req: bool, model: str, chat: bool):
         if max_tokens < 1:
@@ -358,7 +400,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             else:
                 fut = loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream)
             if stream is not None:
-                return StreamingResponse(_sse(stream, len(ids), model, chat), media_type="text/event-stream")
+                return StreamingResponse(_sse(stream, fut, len(ids), model, chat), media_type="text/event-stream")
             out = fut.result(timeout=request_timeout_s)
         except ValueError as exc:
             raise HTTPException(status_code=400, detail=str(exc)) from exc

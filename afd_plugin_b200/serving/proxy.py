@@ -116,9 +116,17 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
                 r.close()
                 release()
 
-        def relay():
+        async def relay():
+            # on the event loop, so a client disconnect cancels it at the next
+            # await; closing the backend connection then aborts the request there
+            import anyio
+
+            chunks = r.iter_content(chunk_size=None)
             try:
-                for chunk in r.iter_content(chunk_size=None):
+                while True:
+                    chunk = await anyio.to_thread.run_sync(next, chunks, None)
+                    if chunk is None:
+                        break
                     if chunk:
                         yield chunk
             finally:

@@ -314,3 +314,87 @@ def test_chat_completions_direct_and_disaggregated():
             s_.should_exit = True
         for lp in loops:
             lp.stop()
+
+
+def test_client_disconnect_aborts_the_stream():
+    eng = _engine()
+    step = eng.step
+
+    def slow_step():
+        time.sleep(0.05)
+        return step()
+
+    eng.step = slow_step
+    loop = EngineLoop(eng).start()
+    srv, url = _serve(lambda port: build_app(loop, advertise_port=port))
+    try:
+        r = requests.post(url + "/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 80, "stream": True},
+                          stream=True, timeout=60)
+        it = r.iter_lines()
+        got = 0
+        for line in it:
+            if line.startswith(b"data: {"):
+                got += 1
+                if got == 3:
+                    break
+        r.close()
+        deadline = time.time() + 20
+        while time.time() < deadline and loop.stats["aborted"] == 0:
+            time.sleep(0.05)
+        assert loop.stats["aborted"] == 1 and loop.stats["completed"] == 0
+        assert not eng.running and not eng.waiting
+        assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks - 1
+    finally:
+        srv.should_exit = True
+        loop.stop()
+
+
+def test_engine_abort_frees_a_waiting_or_running_request():
+    eng = _engine()
+    a = eng.add_request([1, 2, 3], 10)
+    b = eng.add_request([4, 5], 10)
+    eng.step()
+    assert eng.abort(a) and eng.finished[a].aborted and len(eng.finished[a].output) == 1
+    c = eng.add_request([6], 4)
+    assert eng.abort(c) and eng.finished[c].output == []
+    assert not eng.abort(12345)
+    while eng.has_unfinished():
+        eng.step()
+    assert len(eng.finished[b].output) == 10 and not eng.finished[b].aborted
+    assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks - 1
+
+
+def test_client_disconnect_through_the_proxy_aborts_at_the_backend():
+    from afd_plugin_b200.serving.proxy import build_proxy_app
+
+    eng = _engine()
+    step = eng.step
+
+    def slow_step():
+        time.sleep(0.05)
+        return step()
+
+    eng.step = slow_step
+    loop = EngineLoop(eng).start()
+    srv, url = _serve(lambda port: build_app(loop, advertise_port=port))
+    proxy, purl = _serve(lambda port: build_proxy_app([url]))
+    try:
+        r = requests.post(purl + "/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 80, "stream": True},
+                          stream=True, timeout=60)
+        got = 0
+        for line in r.iter_lines():
+            if line.startswith(b"data: {"):
+                got += 1
+                if got == 3:
+                    break
+        r.close()
+        deadline = time.time() + 20
+        while time.time() < deadline and loop.stats["aborted"] == 0:
+            time.sleep(0.05)
+        assert loop.stats["aborted"] == 1
+        h = requests.get(purl + "/health", timeout=10).json()
+        assert all(v == 0 for v in h["inflight"].values())
+    finally:
+        for s_ in (srv, proxy):
+            s_.should_exit = True
+        loop.stop()
