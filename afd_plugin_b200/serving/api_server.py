@@ -432,6 +432,11 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         released = loop.call(lambda eng: eng.release_kv(req_id)).result(timeout=request_timeout_s)
         return {"released": bool(released)}
 
+    @app.post("/reset_prefix_cache")
+    def reset_prefix_cache():
+        # The engine caches no prompt prefixes across requests; nothing to reset.
+        return {"reset": False, "reason": "this engine keeps no prefix cache"}
+
     @app.get("/health")
     def health():
         if loop.error is not None:

@@ -17,8 +17,10 @@ Load is counted in prompt tokens for prefill servers and in requested tokens
 for decode servers, so long prompts spread over the prefill pool the way the
 reference's length-based scores do (``tools/proxy_server.py:205-211``).
 Streaming requests (``"stream": true``) are relayed chunk by chunk; in the
-disaggregated mode only the decode leg streams.  ``GET /health`` reports
-every backend.
+disaggregated mode only the decode leg streams.  ``GET /health`` (alias
+``/healthcheck``) reports every backend; ``POST /instances/add`` and
+``/instances/remove`` change the pools while serving; ``POST
+/reset_prefix_cache`` is forwarded to every backend.
 
     python -m afd_plugin_b200.serving.proxy --backends http://127.0.0.1:8001,http://127.0.0.1:8002 --port 8000
     python -m afd_plugin_b200.serving.proxy --prefill http://127.0.0.1:8001 --decode http://127.0.0.1:8002
@@ -27,28 +29,75 @@ every backend.
 from __future__ import annotations
 
 import argparse
-import itertools
 import threading
 
 import requests
 from fastapi import Request
 
 
+def normalize_url(addr: str) -> str:
+    """``host:port`` or a URL -> ``http://host:port`` without a trailing slash."""
+    addr = addr.strip().rstrip("/")
+    return addr if "://" in addr else "http://" + addr
+
+
 class Balancer:
+    """Backends of one role with their in-flight load.
+
+    Backends can be added and removed while serving (the reference proxy's
+    ``/instances/add`` and ``/instances/remove``); a backend removed while it
+    still has requests in flight is isolated -- it gets no new ones -- and
+    leaves once they are done.
+    """
+
     def __init__(self, backends: list[str]):
         if not backends:
             raise ValueError("the proxy needs at least one backend")
-        self.backends = [b.rstrip("/") for b in backends]
-        self.inflight = {b: 0 for b in self.backends}
-        self.load = {b: 0.0 for b in self.backends}
-        self.served = {b: 0 for b in self.backends}
-        self._rr = itertools.cycle(range(len(self.backends)))
+        self.backends: list[str] = []
+        self.inflight: dict[str, int] = {}
+        self.load: dict[str, float] = {}
+        self.served: dict[str, int] = {}
+        self.isolated: set[str] = set()
+        self._rr = 0
         self._lock = threading.Lock()
+        for b in backends:
+            self.add(b)
+
+    def add(self, b: str) -> bool:
+        b = normalize_url(b)
+        with self._lock:
+            self.isolated.discard(b)
+            if b in self.inflight:
+                return False
+            self.backends.append(b)
+            self.inflight[b], self.load[b], self.served[b] = 0, 0.0, 0
+            return True
+
+    def remove(self, b: str) -> str:
+        """"removed", "isolated" (leaves when drained) or "unknown"."""
+        b = normalize_url(b)
+        with self._lock:
+            if b not in self.inflight:
+                return "unknown"
+            if self.inflight[b] == 0:
+                self._drop(b)
+                return "removed"
+            self.isolated.add(b)
+            return "isolated"
+
+    def _drop(self, b: str) -> None:
+        self.backends.remove(b)
+        self.isolated.discard(b)
+        for d in (self.inflight, self.load, self.served):
+            d.pop(b, None)
 
     def acquire(self, load: float = 1.0) -> str:
         with self._lock:
-            start = next(self._rr)
-            order = self.backends[start:] + self.backends[:start]
+            live = [b for b in self.backends if b not in self.isolated]
+            if not live:
+                raise RuntimeError("no backend available")
+            self._rr = (self._rr + 1) % len(live)
+            order = live[self._rr:] + live[: self._rr]
             b = min(order, key=lambda x: (self.load[x], self.inflight[x]))
             self.inflight[b] += 1
             self.load[b] += load
@@ -56,13 +105,18 @@ class Balancer:
 
     def release(self, b: str, load: float = 1.0) -> None:
         with self._lock:
+            if b not in self.inflight:
+                return
             self.inflight[b] -= 1
             self.load[b] = max(0.0, self.load[b] - load)
             self.served[b] += 1
+            if b in self.isolated and self.inflight[b] == 0:
+                self._drop(b)
 
     def snapshot(self) -> dict:
         with self._lock:
-            return {"inflight": dict(self.inflight), "served": dict(self.served)}
+            return {"inflight": dict(self.inflight), "served": dict(self.served),
+                    "isolated": sorted(self.isolated)}
 
 
 def _prompt_len(body: dict) -> int:
@@ -83,8 +137,20 @@ def build_prefill_request(body: dict) -> dict:
     return out
 
 
+def _healthy(url: str, timeout_s: float = 2.0) -> bool:
+    try:
+        return requests.get(url + "/health", timeout=timeout_s).status_code == 200
+    except requests.RequestException:
+        return False
+
+
 def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | None = None,
-                    decode: list[str] | None = None, timeout_s: float = 600.0):
+                    decode: list[str] | None = None, timeout_s: float = 600.0, max_retries: int = 3,
+                    retry_delay_s: float = 0.2, instance_retry_s: float = 5.0, instance_retry_max: int = 60):
+    """``max_retries`` / ``retry_delay_s``: a backend that cannot be reached is
+    retried with exponential back-off (``tools/proxy_server.py:869-892``).
+    Instances added while unhealthy wait and are checked every
+    ``instance_retry_s`` up to ``instance_retry_max`` times."""
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import JSONResponse, StreamingResponse
 
@@ -99,10 +165,47 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
     app.state.balancer = pools.get("backend")
 
     def _post(url: str, body: dict, *, stream: bool = False):
-        try:
-            return requests.post(url, json=body, timeout=timeout_s, stream=stream)
-        except requests.RequestException as exc:
-            raise HTTPException(status_code=502, detail=f"backend {url} failed: {exc}") from exc
+        import time
+
+        for attempt in range(1, max_retries + 1):
+            try:
+                return requests.post(url, json=body, timeout=timeout_s, stream=stream)
+            except requests.ConnectionError as exc:
+                if attempt == max_retries:
+                    raise HTTPException(status_code=502, detail=f"backend {url} failed: {exc}") from exc
+                time.sleep(retry_delay_s * 2 ** (attempt - 1))
+            except requests.RequestException as exc:
+                raise HTTPException(status_code=502, detail=f"backend {url} failed: {exc}") from exc
+        raise AssertionError("unreachable")
+
+    waiting: dict[tuple[str, str], int] = {}  # (role, url) -> checks so far
+    waiting_lock = threading.Lock()
+
+    def _retry_waiting():
+        import time
+
+        while True:
+            time.sleep(instance_retry_s)
+            with waiting_lock:
+                items = list(waiting.items())
+            for (role, url), tries in items:
+                ok = _healthy(url)
+                with waiting_lock:
+                    if ok:
+                        pools[role].add(url)
+                        waiting.pop((role, url), None)
+                    elif tries + 1 >= instance_retry_max:
+                        waiting.pop((role, url), None)
+                    else:
+                        waiting[(role, url)] = tries + 1
+
+    threading.Thread(target=_retry_waiting, name="afd-proxy-instances", daemon=True).start()
+
+    def _instances():
+        out = {f"current_{role}_instances": list(bal.backends) for role, bal in pools.items()}
+        with waiting_lock:
+            out["waiting_instances"] = [f"{role}:{url}" for role, url in waiting]
+        return out
 
     def _answer(r, release):
         """JSON answers are read whole; event streams are relayed chunk by chunk.
@@ -135,9 +238,15 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
 
         return StreamingResponse(relay(), media_type="text/event-stream")
 
+    def _acquire(bal: Balancer, load: float = 1.0) -> str:
+        try:
+            return bal.acquire(load)
+        except RuntimeError as exc:
+            raise HTTPException(status_code=503, detail=str(exc)) from exc
+
     def _plain(body: dict, path: str):
         bal = pools["backend"]
-        b = bal.acquire()
+        b = _acquire(bal)
         try:
             r = _post(b + path, body, stream=bool(body.get("stream")))
         except BaseException:
@@ -148,7 +257,7 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
     def _disaggregated(body: dict, path: str):
         pre, dec = pools["prefill"], pools["decode"]
         n_prompt = float(_prompt_len(body))
-        p = pre.acquire(n_prompt)
+        p = _acquire(pre, n_prompt)
         try:
             r1 = _post(p + path, build_prefill_request(body))
         finally:
@@ -159,7 +268,7 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
         if not params:
             raise HTTPException(status_code=502, detail=f"prefill server {p} returned no kv_transfer_params")
         n_dec = float(body.get("max_tokens", 16))
-        d = dec.acquire(n_dec)
+        d = _acquire(dec, n_dec)
 
         def drop_held_rows():  # the decode side never fetched the rows: free them now
             try:
@@ -176,6 +285,60 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
         if r2.status_code != 200:
             drop_held_rows()
         return _answer(r2, lambda: dec.release(d, n_dec))
+
+    @app.post("/instances/add")
+    async def add_instances(request: Request):
+        """``{"type": "prefill" | "decode" | "backend", "instances": ["host:port", ...]}``;
+        unhealthy instances wait and are added once ``/health`` answers."""
+        import anyio
+
+        req = await request.json()
+        role = req.get("type", "" if pd else "backend")
+        if role not in pools:
+            return JSONResponse(status_code=400, content={"error": f"instance type {role!r} is not one of {sorted(pools)}"})
+        urls = [normalize_url(u) for u in ([req["instances"]] if isinstance(req.get("instances"), str)
+                                           else req.get("instances", []))]
+        added, queued = [], []
+        for u in urls:
+            if await anyio.to_thread.run_sync(_healthy, u):
+                pools[role].add(u)
+                added.append(u)
+            else:
+                with waiting_lock:
+                    waiting[(role, u)] = 0
+                queued.append(u)
+        return dict(_instances(), added=added, waiting_to_be_added=queued)
+
+    @app.post("/instances/remove")
+    async def remove_instances(request: Request):
+        """``{"type": ..., "instances": [...]}``; busy instances are isolated and leave when drained."""
+        req = await request.json()
+        role = req.get("type", "" if pd else "backend")
+        if role not in pools:
+            return JSONResponse(status_code=400, content={"error": f"instance type {role!r} is not one of {sorted(pools)}"})
+        urls = [normalize_url(u) for u in ([req["instances"]] if isinstance(req.get("instances"), str)
+                                           else req.get("instances", []))]
+        result = {u: pools[role].remove(u) for u in urls}
+        with waiting_lock:
+            for u in urls:
+                if waiting.pop((role, u), None) is not None:
+                    result[u] = "removed"
+        return dict(_instances(), result=result)
+
+    @app.post("/reset_prefix_cache")
+    def reset_prefix_cache():
+        out = {}
+        for bal in pools.values():
+            for b in bal.backends:
+                try:
+                    out[b] = requests.post(b + "/reset_prefix_cache", timeout=10).json()
+                except (requests.RequestException, ValueError) as exc:
+                    out[b] = {"error": repr(exc)}
+        return out
+
+    @app.get("/healthcheck")
+    def healthcheck():
+        return health()
 
     @app.get("/health")
     def health():
@@ -216,12 +379,15 @@ def main(argv=None) -> None:
     ap.add_argument("--decode", default="", help="comma-separated decode server URLs")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--max-retries", type=int, default=3)
+    ap.add_argument("--retry-delay", type=float, default=0.2)
     args = ap.parse_args(argv)
     import uvicorn
 
     split = lambda s: [x for x in s.split(",") if x]  # noqa: E731
     app = build_proxy_app(split(args.backends) or None, prefill=split(args.prefill) or None,
-                          decode=split(args.decode) or None)
+                          decode=split(args.decode) or None, max_retries=args.max_retries,
+                          retry_delay_s=args.retry_delay)
     uvicorn.run(app, host=args.host, port=args.port)
 
 

@@ -398,3 +398,54 @@ def test_client_disconnect_through_the_proxy_aborts_at_the_backend():
         for s_ in (srv, proxy):
             s_.should_exit = True
         loop.stop()
+
+
+def test_balancer_add_remove_and_drain():
+    from afd_plugin_b200.serving.proxy import Balancer
+
+    bal = Balancer(["127.0.0.1:1", "http://127.0.0.1:2/"])
+    assert bal.backends == ["http://127.0.0.1:1", "http://127.0.0.1:2"]
+    a = bal.acquire(5.0)
+    b = bal.acquire(1.0)
+    assert {a, b} == set(bal.backends)
+    assert bal.remove(a) == "isolated" and bal.acquire() == b  # isolated: no new requests
+    bal.release(b)
+    bal.release(a, 5.0)  # drained -> gone
+    assert a not in bal.backends and bal.remove(a) == "unknown"
+    assert bal.remove(b) == "isolated"
+    bal.release(b)
+    assert bal.backends == []
+    with pytest.raises(RuntimeError):
+        bal.acquire()
+    assert bal.add("127.0.0.1:3") and not bal.add("http://127.0.0.1:3")
+
+
+def test_proxy_instances_endpoints():
+    from afd_plugin_b200.serving.proxy import build_proxy_app
+
+    loops = [EngineLoop(_engine()).start() for _ in range(2)]
+    a, a_url = _serve(lambda port: build_app(loops[0], advertise_port=port))
+    b, b_url = _serve(lambda port: build_app(loops[1], advertise_port=port))
+    proxy, purl = _serve(lambda port: build_proxy_app([a_url], instance_retry_s=0.2, max_retries=1))
+    try:
+        dead = f"127.0.0.1:{free_port()}"
+        r = requests.post(purl + "/instances/add", json={"type": "backend", "instances": [b_url, dead]},
+                          timeout=30).json()
+        assert r["added"] == [b_url] and r["waiting_to_be_added"] == ["http://" + dead]
+        assert set(r["current_backend_instances"]) == {a_url, b_url}
+        r = requests.post(purl + "/instances/remove", json={"type": "backend", "instances": [a_url, dead]},
+                          timeout=30).json()
+        assert r["result"] == {a_url: "removed", "http://" + dead: "removed"}
+        assert r["current_backend_instances"] == [b_url] and r["waiting_instances"] == []
+        out = requests.post(purl + "/v1/completions", json={"prompt": [1, 2], "max_tokens": 2}, timeout=60)
+        assert out.status_code == 200
+        assert loops[1].stats["completed"] == 1 and loops[0].stats["completed"] == 0
+        bad = requests.post(purl + "/instances/add", json={"type": "prefill", "instances": [a_url]}, timeout=30)
+        assert bad.status_code == 400
+        assert requests.get(purl + "/healthcheck", timeout=10).json()["backends"] == {b_url: True}
+        assert requests.post(purl + "/reset_prefix_cache", timeout=10).json()[b_url]["reset"] is False
+    finally:
+        for s_ in (a, b, proxy):
+            s_.should_exit = True
+        for lp in loops:
+            lp.stop()
