@@ -101,24 +101,59 @@ def run_scenario(scn: Scenario, args, prompts: list[list[int]], *, log_dir: str,
     raise AssertionError("unreachable")
 
 
-def _run_scenario_once(scn: Scenario, args, prompts: list[list[int]], *, log_dir: str) -> dict:
-    port, master = free_port(), free_port()
-    cmd = server_command(scn, python=sys.executable, preset=args.preset, port=port, master_port=master,
-                         checkpoint=args.checkpoint, dtype=args.dtype, max_num_seqs=args.max_num_seqs,
-                         max_model_len=args.max_model_len, capture_size=args.capture_size, seed=args.seed)
+def _server_env(args, devices: list[str] | None) -> dict:
     env = dict(os.environ)
     # the servers import this package from the same tree as the runner
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     env["PYTHONPATH"] = os.pathsep.join([root] + [p for p in env.get("PYTHONPATH", "").split(os.pathsep) if p])
     if args.device == "cpu":
         env["CUDA_VISIBLE_DEVICES"] = ""
-    elif args.devices:
-        env["CUDA_VISIBLE_DEVICES"] = args.devices
-    log_path = os.path.join(log_dir, f"{scn.name}.log")
-    url = f"http://127.0.0.1:{port}"
-    server = start_server(cmd, env=env, log_path=log_path)
-    result = {"scenario": scn.name, "cmd": cmd, "log": log_path}
+    elif devices is not None:
+        env["CUDA_VISIBLE_DEVICES"] = ",".join(devices)
+    return env
+
+
+def _launch(scn: Scenario, args, log_path: str, devices: list[str] | None):
+    port, master = free_port(), free_port()
+    cmd = server_command(scn, python=sys.executable, preset=args.preset, port=port, master_port=master,
+                         checkpoint=args.checkpoint, dtype=args.dtype, max_num_seqs=args.max_num_seqs,
+                         max_model_len=args.max_model_len, capture_size=args.capture_size, seed=args.seed)
+    server = start_server(cmd, env=_server_env(args, devices), log_path=log_path)
+    return server, f"http://127.0.0.1:{port}", cmd
+
+
+def _run_scenario_once(scn: Scenario, args, prompts: list[list[int]], *, log_dir: str) -> dict:
+    from dataclasses import replace
+
+    all_devices = [d for d in args.devices.split(",") if d] if args.devices else None
+    if all_devices is None and args.device == "cuda" and scn.prefill is not None:
+        all_devices = [str(i) for i in range(scn.total_devices)]
+    servers = []
+    result = {"scenario": scn.name}
     try:
+        if scn.prefill is None:
+            server, url, cmd = _launch(scn, args, os.path.join(log_dir, f"{scn.name}.log"), all_devices)
+            servers.append(server)
+            result.update(cmd=cmd, log=server.log_path)
+        else:
+            # disjoint devices: the prefill server first, then the decode deployment
+            n_pre = scn.prefill.world_size
+            pre_dev = all_devices[:n_pre] if all_devices else None
+            dec_dev = all_devices[n_pre:] if all_devices else None
+            pre, pre_url, _ = _launch(scn.prefill, args, os.path.join(log_dir, f"{scn.name}.prefill.log"), pre_dev)
+            servers.append(pre)
+            dec, dec_url, cmd = _launch(replace(scn, prefill=None), args,
+                                        os.path.join(log_dir, f"{scn.name}.decode.log"), dec_dev)
+            servers.append(dec)
+            wait_for_health(pre, pre_url, timeout_s=args.startup_timeout)
+            wait_for_health(dec, dec_url, timeout_s=args.startup_timeout)
+            pport = free_port()
+            proxy = start_server([sys.executable, "-m", "afd_plugin_b200.serving.proxy", "--prefill", pre_url,
+                                  "--decode", dec_url, "--port", str(pport)], env=_server_env(args, []),
+                                 log_path=os.path.join(log_dir, f"{scn.name}.proxy.log"))
+            servers.append(proxy)
+            server, url = proxy, f"http://127.0.0.1:{pport}"
+            result.update(cmd=cmd, log=dec.log_path)
         result["startup_s"] = round(wait_for_health(server, url, timeout_s=args.startup_timeout), 2)
         t0 = time.perf_counter()
         outs = send_requests(url, prompts, args.max_tokens, concurrency=args.concurrency,
@@ -127,7 +162,7 @@ def _run_scenario_once(scn: Scenario, args, prompts: list[list[int]], *, log_dir
         result.update(outputs=outs, wall_s=round(dt, 3),
                       output_tok_per_s=round(sum(len(o) for o in outs) / max(dt, 1e-9), 1))
     finally:
-        result["teardown"] = stop_server(server)
+        result["teardown"] = ",".join(stop_server(s_) for s_ in reversed(servers))
     return result
 
 

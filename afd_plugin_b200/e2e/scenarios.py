@@ -26,14 +26,22 @@ class Scenario:
     ffn_ranks: int
     connector: str = NCCL
     tp: int = 1  # attention tensor parallelism (attention_ranks = DP x tp)
+    # Prefill/decode disaggregation: this scenario's server decodes behind the
+    # proxy, and a server of the ``prefill`` scenario runs the prompts.
+    prefill: "Scenario | None" = None
 
     @property
     def world_size(self) -> int:
+        """Processes (GPUs) of this scenario's own server (the decode side of a PD scenario)."""
         return 1 if self.baseline else self.attention_ranks + self.ffn_ranks
 
     @property
+    def total_devices(self) -> int:
+        return self.world_size + (self.prefill.world_size if self.prefill is not None else 0)
+
+    @property
     def needs_cuda(self) -> bool:
-        return self.connector == FUSED
+        return self.connector == FUSED or (self.prefill is not None and self.prefill.needs_cuda)
 
     def afd_config(self, extra: dict | None = None) -> dict:
         if self.baseline:
@@ -49,7 +57,13 @@ def _s(name, baseline, graph, dbo, a, f, connector=NCCL, tp=1) -> tuple[str, Sce
     return name, Scenario(name, baseline, graph, dbo, a, f, connector, tp)
 
 
-SCENARIOS: dict[str, Scenario] = dict([
+def _pd(name, decode: str, prefill: str) -> tuple[str, Scenario]:
+    from dataclasses import replace
+
+    return name, replace(_BASE[decode], name=name, prefill=_BASE[prefill])
+
+
+_BASE: dict[str, Scenario] = dict([
     _s("baseline-eager", True, False, False, 1, 0),
     _s("baseline-graph", True, True, False, 1, 0),
     _s("afd-eager-1a1f", False, False, False, 1, 1),
@@ -66,6 +80,13 @@ SCENARIOS: dict[str, Scenario] = dict([
     _s("afd-fused-graph-dbo-2a2f", False, True, True, 2, 2, FUSED),
     _s("afd-fused-graph-6a2f", False, True, False, 6, 2, FUSED),
 ])
+
+# Prefill on a colocated server, decode on an AFD deployment, the proxy in front.
+SCENARIOS: dict[str, Scenario] = dict(_BASE, **dict([
+    _pd("pd-baseline-to-afd-eager-1a1f", "afd-eager-1a1f", "baseline-eager"),
+    _pd("pd-baseline-to-afd-eager-2a1f", "afd-eager-2a1f", "baseline-eager"),
+    _pd("pd-baseline-to-afd-fused-graph-1a1f", "afd-fused-graph-1a1f", "baseline-graph"),
+]))
 
 
 def server_command(scn: Scenario, *, python: str, preset: str, port: int, master_port: int,

@@ -106,7 +106,7 @@ def test_runner_cpu_baseline_vs_afd(tmp_path):
     res = json.loads(out.read_text())["results"]
     for r in res[1:]:
         assert r["agreement"]["exact_match"] == 1.0 and r["gate"] == "pass", r["scenario"]
-    assert all(r["teardown"] in ("terminated", "killed", "exited") for r in res)
+    assert all(t in ("terminated", "killed", "exited") for r in res for t in r["teardown"].split(","))
 
 
 def test_scenario_restarts_on_a_taken_port(monkeypatch, tmp_path):
@@ -131,3 +131,18 @@ def test_scenario_restarts_on_a_taken_port(monkeypatch, tmp_path):
     with pytest.raises(RuntimeError, match="bad config"):
         runner.run_scenario(SCENARIOS["afd-eager-2a1f"], None, [], log_dir=str(tmp_path))
     assert len(calls) == 1
+
+
+def test_pd_scenario_prefill_colocated_decode_afd(tmp_path):
+    """Prefill on a colocated server, KV rows over HTTP, decode on a 2A1F AFD deployment behind the proxy."""
+    scn = SCENARIOS["pd-baseline-to-afd-eager-2a1f"]
+    assert scn.prefill.baseline and scn.world_size == 3 and scn.total_devices == 4
+    out = tmp_path / "pd.json"
+    rc = runner.main(["--scenarios", "baseline-eager,pd-baseline-to-afd-eager-2a1f", "--preset", "tiny-dsv2",
+                      "--dtype", "float32", "--device", "cpu", "--num-prompts", "4", "--max-tokens", "4",
+                      "--max-model-len", "128", "--max-num-seqs", "4", "--min-exact-match", "1.0",
+                      "--startup-timeout", "240", "--log-dir", str(tmp_path / "logs"), "--output", str(out)])
+    assert rc == 0
+    res = json.loads(out.read_text())["results"]
+    assert res[1]["agreement"]["exact_match"] == 1.0
+    assert len(res[1]["teardown"].split(",")) == 3
