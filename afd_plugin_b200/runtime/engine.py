@@ -47,6 +47,8 @@ class Request:
     state_slot: int = -1  # linear-attention state row (Gated DeltaNet models)
     hold_kv: bool = False  # keep the cache rows after finishing, for export to a decode engine
     aborted: bool = False  # ended by abort() before reaching max_tokens
+    synthetic_prefill: bool = False  # decode-bench: prompt KV is whatever the cache holds; output[0] is the
+    # last prompt token, not a generated one
 
     @property
     def num_tokens(self) -> int:
@@ -260,15 +262,31 @@ class LLMEngine:
 
         while self._kv_waiting and len(self.running) < self.max_batch:
             req, state = self._kv_waiting.pop(0)
-            n = len(state.tokens)
+            n = len(req.prompt)
             self._ensure_blocks(req, n + 1)
             req.state_slot = self._free_state_slots.pop()
-            try:
-                kt.import_request_state(self.kv, req.blocks, req.state_slot, state.tensors, n)
-            except ValueError:
-                self._release(req)
-                raise
+            if state is not None:
+                try:
+                    kt.import_request_state(self.kv, req.blocks, req.state_slot, state.tensors, n)
+                except ValueError:
+                    self._release(req)
+                    raise
             (self._finish(req) if req.finished else self.running.append(req))
+
+    def add_synthetic_request(self, prompt: list[int], max_tokens: int) -> int:
+        """Queue a decode-bench request: every prompt token but the last counts as prefilled
+        (its cache rows are whatever the cache holds, e.g. after :meth:`KVCache.fill_random_`),
+        and decoding starts by feeding the last prompt token.  ``max_tokens`` tokens are
+        generated; ``output[0]`` is that last prompt token.  The serving counterpart of the
+        reference's ``AFDDecodeBenchConnector`` (``tools/benchmarks/decode_bench.py:41-140``)."""
+        if len(prompt) < 1 or max_tokens < 1:
+            raise ValueError("decode-bench requests need a prompt and max_tokens >= 1")
+        if len(prompt) + max_tokens > self.config.model_config.max_model_len:
+            raise ValueError("prompt + max_tokens exceeds max_model_len")
+        req = Request(next(self._ids), list(prompt[:-1]), max_tokens + 1, synthetic_prefill=True)
+        req.output.append(int(prompt[-1]))
+        self._kv_waiting.append((req, None))
+        return req.req_id
 
     def admit_prefilled(self, prompts: list[list[int]], first_tokens: list[int], *, reserve_tokens: int = 0) -> list[int]:
         """Admit requests whose prompt KV is already in the cache (decode-only mode).

@@ -32,6 +32,9 @@ def main(argv=None) -> None:
                     "(default: --max-num-seqs)")
     ap.add_argument("--dbo", action="store_true", help="two-ubatch overlap of attention and FFN (AFD only)")
     ap.add_argument("--seed", type=int, default=0, help="random-init seed when no checkpoint is given")
+    ap.add_argument("--decode-bench", action="store_true",
+                    help="take every prompt as prefilled (random cache rows) and only decode: long-ISL decode "
+                         "benchmarks without prefill")
     ap.add_argument("--tp", type=int, default=1, help="attention tensor parallelism (AFD only; "
                     "num_attention_ranks = DP x TP)")
     args = ap.parse_args(argv)
@@ -58,7 +61,9 @@ def main(argv=None) -> None:
         engine = LLMEngine.colocated(ec, device="cuda" if torch.cuda.is_available() else "cpu")
         if not args.eager and engine.device.type == "cuda":
             engine.capture_graphs()
-        loop = EngineLoop(engine).start()
+        if args.decode_bench:
+            engine.kv.fill_random_(seed=args.seed)
+        loop = EngineLoop(engine, decode_bench=args.decode_bench).start()
         uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
                     port=args.port)
         return
@@ -94,8 +99,11 @@ def main(argv=None) -> None:
     w = AFDAttentionWorker(ec, local_rank=local)
     if not args.eager and backend == "nccl":
         w.engine.capture_graphs()
+    if args.decode_bench:
+        w.engine.kv.fill_random_(seed=args.seed)
     loop = EngineLoop(w.engine, group=w.groups.attention_group, world=A, rank=role_rank,
-                      tp_group=w.groups.tp_cpu_group, tp_size=args.tp, tp_src=w.groups.tp_leader).start()
+                      tp_group=w.groups.tp_cpu_group, tp_size=args.tp, tp_src=w.groups.tp_leader,
+                      decode_bench=args.decode_bench).start()
     if role_rank == 0:
         uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
                     port=args.port)

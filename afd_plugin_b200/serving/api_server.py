@@ -107,8 +107,11 @@ class EngineLoop:
     """
 
     def __init__(self, engine, *, group=None, world: int = 1, rank: int = 0, idle_sleep_s: float = 0.001,
-                 kv_hold_timeout_s: float = 120.0, tp_group=None, tp_size: int = 1, tp_src: int = 0):
+                 kv_hold_timeout_s: float = 120.0, tp_group=None, tp_size: int = 1, tp_src: int = 0,
+                 decode_bench: bool = False):
         self.engine = engine
+        # decode-bench serving: prompts are taken as prefilled (no prefill step)
+        self.decode_bench = decode_bench
         self.group, self.world, self.rank = group, world, rank
         self.tp_group, self.tp_size, self.tp_src = tp_group, tp_size, tp_src
         self.tp_leader = tp_size <= 1 or dist.get_rank() == tp_src
@@ -244,6 +247,9 @@ class EngineLoop:
                     try:
                         if p.kv_blob is not None:
                             rid, _ = eng.add_prefilled_request(p.kv_blob, p.max_tokens, prompt=p.prompt)
+                        elif self.decode_bench and not p.hold_kv:
+                            rid = eng.add_synthetic_request(p.prompt, p.max_tokens)
+                            p.sent = 1  # output[0] is the last prompt token: never streamed
                         else:
                             rid = eng.add_request(p.prompt, p.max_tokens, hold_kv=p.hold_kv)
                     except ValueError as exc:
@@ -284,7 +290,7 @@ class EngineLoop:
         for rid in [r for r in self._inflight if r in eng.finished]:
             p = self._inflight.pop(rid)
             req = eng.finished.pop(rid)
-            out = req.output
+            out = req.output[1:] if req.synthetic_prefill else req.output
             self.stats["aborted" if req.aborted else "completed"] += 1
             self.stats["generated_tokens"] += len(out)
             if p.first_token_at is not None and len(out) > 1 and not req.aborted:

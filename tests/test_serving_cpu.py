@@ -449,3 +449,23 @@ def test_proxy_instances_endpoints():
             s_.should_exit = True
         for lp in loops:
             lp.stop()
+
+
+def test_decode_bench_serving_skips_prefill():
+    eng = _engine()
+    eng.kv.fill_random_(seed=0)
+    loop = EngineLoop(eng, decode_bench=True).start()
+    srv, url = _serve(lambda port: build_app(loop, advertise_port=port))
+    try:
+        prompts = [[7] * 40, [3] * 25]
+        outs = [requests.post(url + "/v1/completions", json={"prompt": p, "max_tokens": 5}, timeout=60).json()
+                for p in prompts]
+        assert [len(o["choices"][0]["token_ids"]) for o in outs] == [5, 5]
+        toks, usage, _ = _stream_tokens(url, {"prompt": [9] * 30, "max_tokens": 4})
+        assert len(toks) == 4 and usage["completion_tokens"] == 4
+        m = requests.get(url + "/metrics", timeout=5).json()
+        # every step was a decode step: no prefill ran
+        assert m["steps"] == m["decode_steps"] and m["generated_tokens"] == 14
+    finally:
+        srv.should_exit = True
+        loop.stop()
