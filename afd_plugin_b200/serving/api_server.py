@@ -410,6 +410,8 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             out = fut.result(timeout=request_timeout_s)
         except ValueError as exc:
             raise HTTPException(status_code=400, detail=str(exc)) from exc
+        except RuntimeError as exc:  # the engine loop failed (or this rank takes no requests)
+            raise HTTPException(status_code=503, detail=str(exc)) from exc
         usage = {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)}
         if chat:
             body = {"object": "chat.completion", "model": model, "usage": usage, "choices": [

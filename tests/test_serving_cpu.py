@@ -469,3 +469,23 @@ def test_decode_bench_serving_skips_prefill():
     finally:
         srv.should_exit = True
         loop.stop()
+
+
+def test_failed_engine_answers_503():
+    eng = _engine()
+
+    def broken_step():
+        raise RuntimeError("device lost")
+
+    eng.step = broken_step
+    loop = EngineLoop(eng).start()
+    srv, url = _serve(lambda port: build_app(loop, advertise_port=port))
+    try:
+        first = requests.post(url + "/v1/completions", json={"prompt": [1, 2], "max_tokens": 2}, timeout=60)
+        assert first.status_code == 503 and "device lost" in first.json()["detail"]
+        assert requests.get(url + "/health", timeout=5).status_code == 503
+        again = requests.post(url + "/v1/completions", json={"prompt": [1, 2], "max_tokens": 2}, timeout=60)
+        assert again.status_code == 503
+    finally:
+        srv.should_exit = True
+        loop.stop()
