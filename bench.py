@@ -36,7 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode output tok/s (8xB200, max over ranks) + p50 TPOT, AFD vs NCCL connector"
-BASELINE_VALUE = None  # BASELINE.md publishes no GPU number for this metric
+BASELINE_VALUE = None  # the reference publishes no GPU number for this metric
 TOPOLOGY = {1: (0, 0), 2: (1, 1), 4: (2, 2), 8: (6, 2)}  # 4 GPUs: 2A2F halves each FFN rank's expert weights
 MODEL_DESC = {
     "deepseek-v2-lite": "DeepSeek-V2-Lite (27 layers, 64 experts top-6, MLA 16 heads)",
