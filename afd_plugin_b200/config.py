@@ -173,7 +173,13 @@ def connector_extra_config_from_mapping(raw: Mapping[str, Any]) -> dict[str, Any
 def _additional_config(source: Any) -> Mapping[str, Any] | None:
     if source is None:
         return None
-    extra = source if isinstance(source, Mapping) else getattr(source, "additional_config", None)
+    if isinstance(source, Mapping):
+        extra = source
+    elif hasattr(source, "additional_config"):
+        extra = source.additional_config
+    else:
+        # a config object without the field is a caller bug, not "AFD off"
+        raise AttributeError(f"{type(source).__name__} has no additional_config to read the AFD config from")
     if extra is None:
         return None
     if not isinstance(extra, Mapping):
