@@ -35,6 +35,7 @@ from afd_plugin_b200.runtime.cuda_graph import pad_to_capture_size, validate_cud
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor, LocalFFNExecutor
 from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache
 from afd_plugin_b200.runtime.model_runner import ModelRunner
+from afd_plugin_b200.runtime.sampling import GREEDY, SamplingParams, make_generator, sample
 
 
 @dataclass
@@ -49,6 +50,8 @@ class Request:
     aborted: bool = False  # ended by abort() before reaching max_tokens
     synthetic_prefill: bool = False  # decode-bench: prompt KV is whatever the cache holds; output[0] is the
     # last prompt token, not a generated one
+    sampling: SamplingParams = GREEDY
+    generator: torch.Generator | None = None  # the request's own noise stream (seeded requests)
 
     @property
     def num_tokens(self) -> int:
@@ -142,6 +145,9 @@ class LLMEngine:
 
         self.metrics = StepMetrics()
         self._last_phase = "decode"
+        # noise for sampled requests without their own seed (same seed on every
+        # tensor-parallel peer, so peers draw the same tokens)
+        self._sample_gen = make_generator(engine_config.model_config.seed, self.device)
 
     # ------------------------------------------------------------ helpers
     @classmethod
@@ -159,13 +165,33 @@ class LLMEngine:
             if size <= self.max_batch:
                 self.runner.capture(size)
 
-    def add_request(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False) -> int:
-        """Queue a request; with ``hold_kv`` its cache rows outlive it until :meth:`export_kv`."""
+    def add_request(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False,
+                    sampling: SamplingParams | None = None) -> int:
+        """Queue a request; with ``hold_kv`` its cache rows outlive it until :meth:`export_kv`.
+
+        ``sampling`` (default greedy) sets temperature / top-k / top-p / seed.
+        """
         if len(prompt) + max_tokens > self.config.model_config.max_model_len:
             raise ValueError("prompt + max_tokens exceeds max_model_len")
         req = Request(next(self._ids), list(prompt), max_tokens, hold_kv=hold_kv)
+        self._set_sampling(req, sampling)
         self.waiting.append(req)
         return req.req_id
+
+    def _set_sampling(self, req: Request, sampling: SamplingParams | None) -> None:
+        if sampling is not None:
+            req.sampling = sampling
+            if sampling.seed is not None and not sampling.greedy:
+                req.generator = make_generator(sampling.seed, self.device)
+
+    def _sample(self, reqs: list[Request], tokens: torch.Tensor) -> torch.Tensor:
+        """Replace the argmax of sampled requests' rows in ``tokens`` (from the runner's last logits)."""
+        if all(r.sampling.greedy for r in reqs):
+            return tokens
+        drawn = sample(self.runner.last_logits[: len(reqs)], [r.sampling for r in reqs],
+                       [r.generator for r in reqs], self._sample_gen)
+        tokens[: len(reqs)].copy_(drawn)
+        return tokens
 
     def abort(self, req_id: int) -> bool:
         """End a waiting or running request now (client gone); it moves to ``finished`` with
@@ -210,7 +236,8 @@ class LLMEngine:
             n = req.num_tokens - 1
             tensors = kt.export_request_state(self.kv, req.blocks, n, req.state_slot)
             tokens = (req.prompt + req.output)[:n]
-            return kt.pack(kt.RequestState(tokens, req.output[-1], len(req.prompt), tensors))
+            rng = req.generator.get_state() if req.generator is not None else None
+            return kt.pack(kt.RequestState(tokens, req.output[-1], len(req.prompt), tensors, rng))
         finally:
             self._release(req)
 
@@ -229,8 +256,8 @@ class LLMEngine:
             self.release_kv(rid)
         return old
 
-    def add_prefilled_request(self, blob: bytes, max_tokens: int, *,
-                              prompt: list[int] | None = None) -> tuple[int, list[int]]:
+    def add_prefilled_request(self, blob: bytes, max_tokens: int, *, prompt: list[int] | None = None,
+                              sampling: SamplingParams | None = None) -> tuple[int, list[int]]:
         """Queue a request whose prompt was prefilled elsewhere (payload from :meth:`export_kv`).
 
         The request joins the running batch at the next step with a free slot;
@@ -253,6 +280,9 @@ class LLMEngine:
             if name not in geo:
                 raise ValueError(f"KV payload carries tensors this engine has no cache for: {name!r}")
         req = Request(next(self._ids), state.tokens, max_tokens)
+        self._set_sampling(req, sampling)
+        if req.generator is not None and state.rng_state is not None:
+            req.generator.set_state(state.rng_state)  # continue the prefill side's noise stream
         req.output.append(state.next_token)
         self._kv_waiting.append((req, state))
         return req.req_id, state.tokens
@@ -273,7 +303,8 @@ class LLMEngine:
                     raise
             (self._finish(req) if req.finished else self.running.append(req))
 
-    def add_synthetic_request(self, prompt: list[int], max_tokens: int) -> int:
+    def add_synthetic_request(self, prompt: list[int], max_tokens: int, *,
+                              sampling: SamplingParams | None = None) -> int:
         """Queue a decode-bench request: every prompt token but the last counts as prefilled
         (its cache rows are whatever the cache holds, e.g. after :meth:`KVCache.fill_random_`),
         and decoding starts by feeding the last prompt token.  ``max_tokens`` tokens are
@@ -284,6 +315,7 @@ class LLMEngine:
         if len(prompt) + max_tokens > self.config.model_config.max_model_len:
             raise ValueError("prompt + max_tokens exceeds max_model_len")
         req = Request(next(self._ids), list(prompt[:-1]), max_tokens + 1, synthetic_prefill=True)
+        self._set_sampling(req, sampling)
         req.output.append(int(prompt[-1]))
         self._kv_waiting.append((req, None))
         return req.req_id
@@ -401,6 +433,8 @@ class LLMEngine:
             slots = [r.state_slot for r in admit]
         toks = self.runner.prefill(admit_tokens, tables, starts, slots,
                                    **self._across(votes, sum(len(t) for t in admit_tokens)))
+        if admit:
+            toks = self._sample(admit, toks)
         toks = toks.cpu().tolist()
         out = {}
         for r, t in zip(admit, toks):
@@ -478,7 +512,7 @@ class LLMEngine:
             flags["tokens_across_attn"] = {
                 s: tuple(sp[s + 1] - sp[s] for _ in votes) for s in range(len(sp) - 1)
             }
-        nxt = self.runner.decode_step(run_b, use_graph=use_graph, **flags)
+        nxt = self._sample(reqs, self.runner.decode_step(run_b, use_graph=use_graph, **flags))
         self._h_next[:run_b].copy_(nxt, non_blocking=True)
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()

@@ -41,6 +41,11 @@ class RequestState:
     next_token: int  # the token the decode engine feeds first
     prompt_len: int
     tensors: dict[str, torch.Tensor]
+    # a seeded sampled request's generator state, so the decode side continues its noise stream
+    rng_state: torch.Tensor | None = None
+
+
+_RNG_KEY = "__rng_state__"
 
 
 def _slots(blocks: list[int], n: int, block_size: int, device) -> torch.Tensor:
@@ -125,7 +130,10 @@ def pack(state: RequestState) -> bytes:
 
     meta = {"format": FORMAT, "tokens": state.tokens, "next_token": int(state.next_token),
             "prompt_len": int(state.prompt_len)}
-    return save({k: v.contiguous() for k, v in state.tensors.items()}, metadata={"afd_kv": json.dumps(meta)})
+    tensors = {k: v.contiguous() for k, v in state.tensors.items()}
+    if state.rng_state is not None:
+        tensors[_RNG_KEY] = state.rng_state.contiguous()
+    return save(tensors, metadata={"afd_kv": json.dumps(meta)})
 
 
 def unpack(blob: bytes) -> RequestState:
@@ -141,8 +149,10 @@ def unpack(blob: bytes) -> RequestState:
     meta = json.loads(raw)
     if meta.get("format") != FORMAT:
         raise ValueError(f"unsupported KV payload format {meta.get('format')!r}")
+    tensors = load(blob)
+    rng = tensors.pop(_RNG_KEY, None)
     return RequestState([int(t) for t in meta["tokens"]], int(meta["next_token"]), int(meta["prompt_len"]),
-                        load(blob))
+                        tensors, rng)
 
 
 __all__ = ["FORMAT", "RequestState", "export_request_state", "geometry", "import_request_state", "pack", "unpack"]

@@ -59,6 +59,7 @@ class _Graph:
     graph: torch.cuda.CUDAGraph
     batch: int
     ubatch_splits: tuple[int, ...]
+    logits: torch.Tensor | None = None  # the graph's logits output (static address)
 
 
 def ubatch_splits(batch: int, num_ubatches: int) -> tuple[int, ...]:
@@ -97,6 +98,8 @@ class ModelRunner:
         # DeepSeek sparse attention: set by the engine for eager decode steps
         # in which some sequence is longer than index_topk.
         self.sparse_decode = False
+        # logits of the last prefill (one row per sequence) or decode step (one per row)
+        self.last_logits: torch.Tensor | None = None
 
     # ------------------------------------------------------------ forward
     def _layers(self, h: torch.Tensor, meta: AttentionMetadata, stage: int):
@@ -154,10 +157,11 @@ class ModelRunner:
             ))
         return metas
 
-    def _decode_body(self, batch: int, splits: tuple[int, ...], **flags) -> None:
+    def _decode_body(self, batch: int, splits: tuple[int, ...], **flags) -> torch.Tensor:
         b = self.buf
         logits = self.forward(b.input_ids[:batch], self._decode_metas(batch, splits), splits, **flags)
         b.next_tokens[:batch].copy_(ops.argmax(logits))
+        return logits
 
     def decode_step(self, batch: int, *, use_graph: bool = True, **flags) -> torch.Tensor:
         """Run one decode step on ``buf[:batch]``; returns ``next_tokens[:batch]`` (device)."""
@@ -166,8 +170,9 @@ class ModelRunner:
             self.ffn.begin_step({s: g.ubatch_splits[s + 1] - g.ubatch_splits[s]
                                  for s in range(len(g.ubatch_splits) - 1)}, is_graph_replaying=True, **flags)
             g.graph.replay()
+            self.last_logits = g.logits
         else:
-            self._decode_body(batch, ubatch_splits(batch, self.num_ubatches), **flags)
+            self.last_logits = self._decode_body(batch, ubatch_splits(batch, self.num_ubatches), **flags)
         return self.buf.next_tokens[:batch]
 
     def advance_on_device(self, batch: int, *, wrap_at: int = 0, wrap_to: int = 0) -> None:
@@ -207,11 +212,11 @@ class ModelRunner:
             # named like the reference's capture ranges (attention_model_runner.py:491-496)
             with torch.profiler.record_function(f"capture_{batch}_{'dbo' if len(splits) > 2 else 'full'}"), \
                     torch.cuda.graph(graph, pool=self.graph_pool):
-                self._decode_body(batch, splits)
+                logits = self._decode_body(batch, splits)
         finally:
             self.ffn.begin_step = begin
         torch.cuda.synchronize(self.device)
-        self.graphs[batch] = _Graph(graph, batch, splits)
+        self.graphs[batch] = _Graph(graph, batch, splits, logits)
 
     def _pad_rows(self, lo: int, hi: int) -> None:
         """Padding rows read/write only the reserved padding block."""
@@ -270,7 +275,8 @@ class ModelRunner:
         input_ids = torch.tensor(ids, dtype=torch.int32, device=dev)
         logits = self.forward(input_ids, [meta], (0, t), **flags)
         last = torch.tensor([e - 1 for _, e, _ in seqs], device=dev)
-        return ops.argmax(logits[last])
+        self.last_logits = logits[last]
+        return ops.argmax(self.last_logits)
 
 
 __all__ = ["DecodeBuffers", "ModelRunner", "ubatch_splits"]

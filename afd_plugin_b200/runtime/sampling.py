@@ -1,0 +1,105 @@
+"""Per-request sampling: temperature, top-k, top-p (nucleus) and per-request seeds.
+
+Greedy requests (``temperature == 0``, the default) keep the argmax the
+decode graph computes; a step with sampled requests draws their tokens from
+the step's logits afterwards, on the device, in one batched pass:
+
+* logits / temperature, then the top-k and top-p masks (ties at the k-th
+  value are kept, as a sort-based mask does);
+* a draw by the exponential race ``argmax(p_i / E_i)`` with ``E_i ~ Exp(1)``,
+  which selects token i with probability ``p_i`` -- the noise comes from the
+  engine's generator, or from the request's own when it carries a seed, so a
+  seeded request reproduces its tokens whatever else is in the batch.
+
+The reference takes these parameters through vLLM's sampler; the field names
+and meanings follow the OpenAI completions API it serves.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class SamplingParams:
+    temperature: float = 0.0  # 0: greedy
+    top_k: int = 0  # 0: off
+    top_p: float = 1.0
+    seed: int | None = None
+
+    def __post_init__(self) -> None:
+        if self.temperature < 0:
+            raise ValueError("temperature must be >= 0")
+        if self.top_k < 0:
+            raise ValueError("top_k must be >= 0")
+        if not 0.0 < self.top_p <= 1.0:
+            raise ValueError("top_p must be in (0, 1]")
+
+    @property
+    def greedy(self) -> bool:
+        return self.temperature == 0.0 or self.top_k == 1
+
+
+GREEDY = SamplingParams()
+
+
+def make_generator(seed: int, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed) & 0x7FFFFFFFFFFFFFFF)
+    return g
+
+
+def filtered_probs(logits: torch.Tensor, params: list[SamplingParams]) -> torch.Tensor:
+    """Row-wise probabilities after temperature, top-k and top-p; ``logits [n, V]``."""
+    x = logits.float()
+    dev = x.device
+    temp = torch.tensor([max(p.temperature, 1e-6) for p in params], device=dev).unsqueeze(1)
+    x = x / temp
+    V = x.shape[1]
+    ks = [p.top_k if 0 < p.top_k < V else 0 for p in params]
+    need_sort = any(ks) or any(p.top_p < 1.0 for p in params)
+    if need_sort:
+        sorted_x, _ = x.sort(dim=-1, descending=True)
+        if any(ks):
+            kk = torch.tensor([k if k else V for k in ks], device=dev)
+            kth = sorted_x.gather(1, (kk - 1).unsqueeze(1))
+            x = x.masked_fill(x < kth, float("-inf"))
+            sorted_x = sorted_x.masked_fill(torch.arange(V, device=dev)[None, :] >= kk[:, None], float("-inf"))
+        top_p = torch.tensor([p.top_p for p in params], device=dev).unsqueeze(1)
+        if bool((top_p < 1.0).any()):
+            sp = torch.softmax(sorted_x, dim=-1)
+            # keep the smallest prefix whose mass reaches top_p (the first token always stays)
+            before = sp.cumsum(dim=-1) - sp
+            keep_sorted = before < top_p
+            n_keep = keep_sorted.sum(dim=-1, keepdim=True).clamp_min(1)
+            cutoff = sorted_x.gather(1, n_keep - 1)
+            x = x.masked_fill(x < cutoff, float("-inf"))
+    return torch.softmax(x, dim=-1)
+
+
+def sample(logits: torch.Tensor, params: list[SamplingParams], generators: list[torch.Generator | None],
+           default_generator: torch.Generator | None = None) -> torch.Tensor:
+    """One token per row of ``logits [n, V]`` (int32); greedy rows take the argmax."""
+    out = torch.argmax(logits.float(), dim=-1).to(torch.int32)
+    rows = [i for i, p in enumerate(params) if not p.greedy]
+    if not rows:
+        return out
+    idx = torch.tensor(rows, device=logits.device)
+    probs = filtered_probs(logits.index_select(0, idx), [params[i] for i in rows])
+    noise = torch.empty_like(probs)
+    shared = [j for j, i in enumerate(rows) if generators[i] is None]
+    if shared:
+        sel = torch.tensor(shared, device=logits.device)
+        noise[sel] = torch.empty(len(shared), probs.shape[1], device=probs.device).exponential_(
+            generator=default_generator)
+    for j, i in enumerate(rows):
+        if generators[i] is not None:
+            noise[j].exponential_(generator=generators[i])
+    drawn = torch.argmax(probs / noise.clamp_min(1e-30), dim=-1).to(torch.int32)
+    out[idx] = drawn
+    return out
+
+
+__all__ = ["GREEDY", "SamplingParams", "filtered_probs", "make_generator", "sample"]

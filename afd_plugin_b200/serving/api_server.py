@@ -40,8 +40,25 @@ import torch
 import torch.distributed as dist
 from pydantic import BaseModel
 
+from afd_plugin_b200.runtime.sampling import SamplingParams
 
-class CompletionRequest(BaseModel):
+
+class SamplingFields(BaseModel):
+    """OpenAI-style sampling fields; an omitted or zero ``temperature`` decodes greedily."""
+
+    temperature: float | None = None
+    top_p: float | None = None
+    top_k: int | None = None
+    seed: int | None = None
+
+    def sampling(self) -> SamplingParams | None:
+        if self.temperature is None and self.top_p is None and self.top_k is None and self.seed is None:
+            return None
+        return SamplingParams(temperature=float(self.temperature or 0.0), top_k=int(self.top_k or 0),
+                              top_p=float(self.top_p if self.top_p is not None else 1.0), seed=self.seed)
+
+
+class CompletionRequest(SamplingFields):
     prompt: str | list[int]
     max_tokens: int = 16
     model: str | None = None
@@ -54,7 +71,7 @@ class ChatMessage(BaseModel):
     content: str
 
 
-class ChatCompletionRequest(BaseModel):
+class ChatCompletionRequest(SamplingFields):
     messages: list[ChatMessage]
     max_tokens: int | None = None
     max_completion_tokens: int | None = None
@@ -93,6 +110,7 @@ class _Pending:
     stream: queue.Queue | None = None
     req: object | None = None  # the engine's Request, for streaming
     sent: int = 0
+    sampling: SamplingParams | None = None
 
 
 class EngineLoop:
@@ -137,7 +155,7 @@ class EngineLoop:
             raise ValueError("prefill/decode KV hand-off is not supported with attention tensor parallelism")
 
     def submit(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False,
-               stream: queue.Queue | None = None) -> Future:
+               stream: queue.Queue | None = None, sampling: SamplingParams | None = None) -> Future:
         """Queue a request; the future resolves with its tokens and carries ``req_id`` once admitted.
 
         With ``stream`` every token is also put on that queue as soon as it is
@@ -149,17 +167,19 @@ class EngineLoop:
             raise ValueError(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds max_model_len {limit}")
         fut: Future = Future()
         with self._lock:
-            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, hold_kv=hold_kv, stream=stream))
+            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, hold_kv=hold_kv, stream=stream,
+                                        sampling=sampling))
             self.stats["requests"] += 1
         return fut
 
     def submit_prefilled(self, prompt: list[int], kv_blob: bytes, max_tokens: int, *,
-                         stream: queue.Queue | None = None) -> Future:
+                         stream: queue.Queue | None = None, sampling: SamplingParams | None = None) -> Future:
         """Queue a request whose prompt was prefilled by another engine (see ``export_kv``)."""
         self._check_entry(True)
         fut: Future = Future()
         with self._lock:
-            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob, stream=stream))
+            self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob, stream=stream,
+                                        sampling=sampling))
             self.stats["requests"] += 1
         return fut
 
@@ -209,11 +229,11 @@ class EngineLoop:
 
     def _fan_out(self, new: list[_Pending]) -> list[_Pending]:
         """TP leader -> peers: this iteration's new requests (one gloo broadcast)."""
-        obj = [[(p.prompt, p.max_tokens) for p in new]] if self.tp_leader else [None]
+        obj = [[(p.prompt, p.max_tokens, p.sampling) for p in new]] if self.tp_leader else [None]
         dist.broadcast_object_list(obj, src=self.tp_src, group=self.tp_group)
         if self.tp_leader:
             return new
-        return [_Pending(list(pr), int(mt), Future()) for pr, mt in obj[0]]
+        return [_Pending(list(pr), int(mt), Future(), sampling=sp) for pr, mt, sp in obj[0]]
 
     def _agree(self, work: bool, stop: bool) -> tuple[bool, bool]:
         """(any rank has work, any rank stops) -- one collective per iteration on every rank."""
@@ -246,12 +266,13 @@ class EngineLoop:
                 for p in new:
                     try:
                         if p.kv_blob is not None:
-                            rid, _ = eng.add_prefilled_request(p.kv_blob, p.max_tokens, prompt=p.prompt)
+                            rid, _ = eng.add_prefilled_request(p.kv_blob, p.max_tokens, prompt=p.prompt,
+                                                               sampling=p.sampling)
                         elif self.decode_bench and not p.hold_kv:
-                            rid = eng.add_synthetic_request(p.prompt, p.max_tokens)
+                            rid = eng.add_synthetic_request(p.prompt, p.max_tokens, sampling=p.sampling)
                             p.sent = 1  # output[0] is the last prompt token: never streamed
                         else:
-                            rid = eng.add_request(p.prompt, p.max_tokens, hold_kv=p.hold_kv)
+                            rid = eng.add_request(p.prompt, p.max_tokens, hold_kv=p.hold_kv, sampling=p.sampling)
                     except ValueError as exc:
                         p.future.set_exception(exc)
                         if p.stream is not None:
@@ -392,7 +413,12 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             if not ended and rid is not None:
                 loop.abort(rid)
 
-    def _generate(ids: list[int], max_tokens: int, params: dict | None, stream_req: bool, model: str, chat: bool):
+    def _generate(ids: list[int], max_tokens: int, params: dict | None, stream_req: bool, model: str, chat: bool,
+                  fields: SamplingFields):
+        try:
+            sampling = fields.sampling()
+        except ValueError as exc:
+            raise HTTPException(status_code=400, detail=str(exc)) from exc
         if max_tokens < 1:
             raise HTTPException(status_code=400, detail="max_tokens must be positive")
         if any((not isinstance(t, int)) or t < 0 or t >= vocab for t in ids):
@@ -402,9 +428,9 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         stream = queue.Queue() if stream_req and not prefill_only else None
         try:
             if params.get("do_remote_prefill"):
-                fut = loop.submit_prefilled(ids, _fetch_kv(params), max_tokens, stream=stream)
+                fut = loop.submit_prefilled(ids, _fetch_kv(params), max_tokens, stream=stream, sampling=sampling)
             else:
-                fut = loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream)
+                fut = loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream, sampling=sampling)
             if stream is not None:
                 return StreamingResponse(_sse(stream, fut, len(ids), model, chat), media_type="text/event-stream")
             out = fut.result(timeout=request_timeout_s)
@@ -465,13 +491,14 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
     @app.post("/v1/completions")
     def completions(req: CompletionRequest):
         ids = req.prompt if isinstance(req.prompt, list) else byte_tokenize(req.prompt, vocab)
-        return _generate(ids, req.max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, False)
+        return _generate(ids, req.max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, False,
+                         req)
 
     @app.post("/v1/chat/completions")
     def chat_completions(req: ChatCompletionRequest):
         max_tokens = req.max_completion_tokens or req.max_tokens or 16
         ids = byte_tokenize(chat_prompt(req.messages), vocab)
-        return _generate(ids, max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, True)
+        return _generate(ids, max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, True, req)
 
     return app
 

@@ -1,0 +1,130 @@
+"""Sampling: temperature / top-k / top-p masks, the exponential-race draw, seeds, engine and server wiring."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from afd_plugin_b200.engine_config import EngineConfig, ModelConfig
+from afd_plugin_b200.models import build_model, get_preset
+from afd_plugin_b200.runtime.engine import LLMEngine
+from afd_plugin_b200.runtime.sampling import GREEDY, SamplingParams, filtered_probs, make_generator, sample
+
+
+def _engine(seed=0):
+    arch = get_preset("tiny-dsv2")
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96, seed=seed),
+                      max_num_seqs=4)
+    return LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=96))
+
+
+def test_greedy_rows_and_top_k_one_are_argmax():
+    logits = torch.randn(4, 50, generator=torch.Generator().manual_seed(0))
+    params = [GREEDY, SamplingParams(temperature=0.7, top_k=1), GREEDY, SamplingParams(temperature=2.0, top_k=1)]
+    assert torch.equal(sample(logits, params, [None] * 4), logits.argmax(-1).int())
+
+
+def test_draws_follow_the_distribution():
+    base = torch.tensor([2.0, 1.0, 0.5, 0.0, -1.0])
+    n = 20000
+    logits = base.repeat(n, 1)
+    toks = sample(logits, [SamplingParams(temperature=1.0)] * n, [None] * n, make_generator(1, "cpu"))
+    freq = torch.bincount(toks.long(), minlength=5).float() / n
+    assert torch.allclose(freq, torch.softmax(base, 0), atol=0.015)
+    hot = sample(logits, [SamplingParams(temperature=0.5)] * n, [None] * n, make_generator(2, "cpu"))
+    freq = torch.bincount(hot.long(), minlength=5).float() / n
+    assert torch.allclose(freq, torch.softmax(base / 0.5, 0), atol=0.015)
+
+
+def test_top_k_and_top_p_masks():
+    logits = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
+    pk = filtered_probs(logits, [SamplingParams(temperature=1.0, top_k=2)])[0]
+    assert torch.allclose(pk, torch.tensor([0.625, 0.375, 0.0, 0.0]), atol=1e-5)
+    pp = filtered_probs(logits, [SamplingParams(temperature=1.0, top_p=0.7)])[0]
+    assert torch.allclose(pp, torch.tensor([0.625, 0.375, 0.0, 0.0]), atol=1e-5)
+    tiny = filtered_probs(logits, [SamplingParams(temperature=1.0, top_p=0.01)])[0]
+    assert torch.allclose(tiny, torch.tensor([1.0, 0.0, 0.0, 0.0]))
+    with pytest.raises(ValueError):
+        SamplingParams(top_p=0.0)
+    with pytest.raises(ValueError):
+        SamplingParams(temperature=-1.0)
+
+
+def test_seeded_rows_do_not_depend_on_the_batch():
+    logits = torch.randn(3, 40, generator=torch.Generator().manual_seed(3))
+    sp = SamplingParams(temperature=1.0, seed=11)
+    alone = sample(logits[1:2], [sp], [make_generator(11, "cpu")])
+    mixed = sample(logits, [SamplingParams(temperature=1.0), sp, GREEDY],
+                   [None, make_generator(11, "cpu"), None], make_generator(99, "cpu"))
+    assert int(alone[0]) == int(mixed[1]) and int(mixed[2]) == int(logits[2].argmax())
+
+
+def test_engine_sampling_is_seeded_and_greedy_is_unchanged():
+    prompt = [5, 9, 100, 7]
+    greedy = _engine().generate([prompt], 6)[0]
+    sp = SamplingParams(temperature=1.5, top_k=50, seed=123)
+
+    def run(sampling, others=()):
+        eng = _engine()
+        rid = eng.add_request(prompt, 6, sampling=sampling)
+        for o in others:
+            eng.add_request(o, 6, sampling=SamplingParams(temperature=1.0))
+        while eng.has_unfinished():
+            eng.step()
+        return eng.finished[rid].output
+
+    a, b = run(sp), run(sp, others=([1, 2, 3], [4, 4, 4, 4]))
+    assert a == b and len(a) == 6
+    assert run(SamplingParams(temperature=1.5, top_k=50, seed=124)) != a
+    assert run(None) == greedy
+
+
+def test_kv_handoff_continues_a_seeded_stream():
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6]
+    sp = SamplingParams(temperature=1.2, seed=7)
+    ref = _engine()
+    rid = ref.add_request(prompt, 6, sampling=sp)
+    while ref.has_unfinished():
+        ref.step()
+    want = ref.finished[rid].output
+    pre, dec = _engine(), _engine()
+    r1 = pre.add_request(prompt, 1, hold_kv=True, sampling=sp)
+    while pre.has_unfinished():
+        pre.step()
+    r2, _ = dec.add_prefilled_request(pre.export_kv(r1), 6, sampling=sp)
+    while dec.has_unfinished():
+        dec.step()
+    assert dec.finished[r2].output == want
+
+
+def test_server_sampling_fields():
+    import threading
+    import time
+
+    import requests
+    import uvicorn
+
+    from afd_plugin_b200.runtime.launcher import free_port
+    from afd_plugin_b200.serving import EngineLoop, build_app
+
+    loop = EngineLoop(_engine()).start()
+    port = free_port()
+    srv = uvicorn.Server(uvicorn.Config(build_app(loop), host="127.0.0.1", port=port, log_level="warning"))
+    threading.Thread(target=srv.run, daemon=True).start()
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(200):
+        try:
+            if requests.get(url + "/health", timeout=2).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.05)
+    try:
+        body = {"prompt": [5, 9, 100, 7], "max_tokens": 6, "temperature": 1.5, "top_k": 50, "seed": 123}
+        a = requests.post(url + "/v1/completions", json=body, timeout=60).json()["choices"][0]["token_ids"]
+        b = requests.post(url + "/v1/completions", json=body, timeout=60).json()["choices"][0]["token_ids"]
+        assert a == b and len(a) == 6
+        bad = requests.post(url + "/v1/completions", json=dict(body, top_p=1.5), timeout=60)
+        assert bad.status_code == 400 and "top_p" in bad.json()["detail"]
+    finally:
+        srv.should_exit = True
+        loop.stop()
