@@ -83,6 +83,8 @@ class ModelArchConfig:
     hc_sinkhorn_iters: int = 20
     hc_eps: float = 1e-6
     num_hash_layers: int = 0
+    # End-of-sequence token ids: generation stops there unless a request ignores EOS.
+    eos_token_id: tuple[int, ...] = ()
     # "fp8_block": e4m3 weights with 128x128 scales for experts and dense MLPs.
     quant: str | None = None
     weight_block_size: tuple[int, int] = (128, 128)
@@ -183,6 +185,13 @@ class ModelArchConfig:
     # -------------------------------------------------------------- parsing
     @classmethod
     def from_hf_config(cls, hf: dict) -> "ModelArchConfig":
+        cfg = cls._parse_hf(hf)
+        eos = hf.get("eos_token_id", (hf.get("text_config") or {}).get("eos_token_id"))
+        ids = tuple(int(e) for e in (eos if isinstance(eos, (list, tuple)) else [eos]) if e is not None)
+        return replace(cfg, eos_token_id=ids) if ids else cfg
+
+    @classmethod
+    def _parse_hf(cls, hf: dict) -> "ModelArchConfig":
         archs = hf.get("architectures") or [""]
         arch = archs[0]
         if arch.startswith("AFD"):

@@ -52,14 +52,25 @@ class Request:
     # last prompt token, not a generated one
     sampling: SamplingParams = GREEDY
     generator: torch.Generator | None = None  # the request's own noise stream (seeded requests)
+    stop_ids: frozenset[int] = frozenset()  # EOS and stop tokens that end generation
 
     @property
     def num_tokens(self) -> int:
         return len(self.prompt) + len(self.output)
 
     @property
+    def stopped(self) -> bool:
+        """The last generated token is a stop token (a decode-bench request's output[0] is not generated)."""
+        first = 1 if self.synthetic_prefill else 0
+        return bool(self.stop_ids) and len(self.output) > first and self.output[-1] in self.stop_ids
+
+    @property
     def finished(self) -> bool:
-        return len(self.output) >= self.max_tokens
+        return len(self.output) >= self.max_tokens or self.stopped
+
+    @property
+    def finish_reason(self) -> str:
+        return "abort" if self.aborted else ("stop" if self.stopped else "length")
 
 
 class AttentionCoordinator:
@@ -179,10 +190,12 @@ class LLMEngine:
         return req.req_id
 
     def _set_sampling(self, req: Request, sampling: SamplingParams | None) -> None:
-        if sampling is not None:
-            req.sampling = sampling
-            if sampling.seed is not None and not sampling.greedy:
-                req.generator = make_generator(sampling.seed, self.device)
+        sp = sampling if sampling is not None else GREEDY
+        req.sampling = sp
+        if sp.seed is not None and not sp.greedy:
+            req.generator = make_generator(sp.seed, self.device)
+        eos = () if sp.ignore_eos else self.model.arch.eos_token_id
+        req.stop_ids = frozenset(eos) | frozenset(sp.stop_token_ids)
 
     def _sample(self, reqs: list[Request], tokens: torch.Tensor) -> torch.Tensor:
         """Replace the argmax of sampled requests' rows in ``tokens`` (from the runner's last logits)."""
@@ -321,7 +334,7 @@ class LLMEngine:
         return req.req_id
 
     def admit_prefilled(self, prompts: list[list[int]], first_tokens: list[int], *, reserve_tokens: int = 0) -> list[int]:
-        """Admit requests whose prompt KV is already in the cache (decode-only mode).
+        """Admit requests whose prompt KV is already in the cache (decode-only mode; EOS is ignored).
 
         The decode-benchmark counterpart of the reference's
         ``AFDDecodeBenchConnector`` (``tools/benchmarks/decode_bench.py:41-140``),

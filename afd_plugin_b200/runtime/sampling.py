@@ -28,6 +28,9 @@ class SamplingParams:
     top_k: int = 0  # 0: off
     top_p: float = 1.0
     seed: int | None = None
+    # generation also ends at these tokens (and at the model's EOS unless ignore_eos)
+    stop_token_ids: tuple[int, ...] = ()
+    ignore_eos: bool = False
 
     def __post_init__(self) -> None:
         if self.temperature < 0:

@@ -50,12 +50,17 @@ class SamplingFields(BaseModel):
     top_p: float | None = None
     top_k: int | None = None
     seed: int | None = None
+    stop_token_ids: list[int] | None = None
+    ignore_eos: bool | None = None
 
     def sampling(self) -> SamplingParams | None:
-        if self.temperature is None and self.top_p is None and self.top_k is None and self.seed is None:
+        if all(v is None for v in (self.temperature, self.top_p, self.top_k, self.seed, self.stop_token_ids,
+                                   self.ignore_eos)):
             return None
         return SamplingParams(temperature=float(self.temperature or 0.0), top_k=int(self.top_k or 0),
-                              top_p=float(self.top_p if self.top_p is not None else 1.0), seed=self.seed)
+                              top_p=float(self.top_p if self.top_p is not None else 1.0), seed=self.seed,
+                              stop_token_ids=tuple(int(t) for t in self.stop_token_ids or ()),
+                              ignore_eos=bool(self.ignore_eos))
 
 
 class CompletionRequest(SamplingFields):
@@ -317,6 +322,7 @@ class EngineLoop:
             if p.first_token_at is not None and len(out) > 1 and not req.aborted:
                 self.stats["tpot_s_sum"] += (now - p.first_token_at) / (len(out) - 1)
                 self.stats["tpot_count"] += 1
+            p.future.finish_reason = req.finish_reason
             if p.stream is not None:
                 self._push_tokens(p)
                 p.stream.put(None)
@@ -405,7 +411,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
                 deadline = time.monotonic() + request_timeout_s
                 yield _chunk(chat, model, [t], None)
             ended = True
-            yield _chunk(chat, model, [], "length",
+            yield _chunk(chat, model, [], getattr(fut, "finish_reason", "length"),
                          {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n})
             yield "data: [DONE]\n\n"
         finally:
@@ -439,13 +445,14 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         except RuntimeError as exc:  # the engine loop failed (or this rank takes no requests)
             raise HTTPException(status_code=503, detail=str(exc)) from exc
         usage = {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)}
+        reason = getattr(fut, "finish_reason", "length")
         if chat:
             body = {"object": "chat.completion", "model": model, "usage": usage, "choices": [
                 {"index": 0, "message": {"role": "assistant", "content": byte_detokenize(out)}, "token_ids": out,
-                 "finish_reason": "length"}]}
+                 "finish_reason": reason}]}
         else:
             body = {"object": "text_completion", "model": model, "usage": usage, "choices": [
-                {"index": 0, "token_ids": out, "text": byte_detokenize(out), "finish_reason": "length"}]}
+                {"index": 0, "token_ids": out, "text": byte_detokenize(out), "finish_reason": reason}]}
         if prefill_only:
             body["kv_transfer_params"] = {
                 "do_remote_prefill": True, "do_remote_decode": False,

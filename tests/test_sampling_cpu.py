@@ -128,3 +128,39 @@ def test_server_sampling_fields():
     finally:
         srv.should_exit = True
         loop.stop()
+
+
+def test_stop_tokens_and_eos():
+    from dataclasses import replace
+
+    prompt = [5, 9, 100, 7]
+    full = _engine().generate([prompt], 8)[0]
+    stop_at = full[3]
+    eng = _engine()
+    rid = eng.add_request(prompt, 8, sampling=SamplingParams(stop_token_ids=(stop_at,)))
+    while eng.has_unfinished():
+        eng.step()
+    r = eng.finished[rid]
+    cut = full.index(stop_at) + 1
+    assert r.output == full[:cut] and r.finish_reason == "stop"
+    # the model's EOS ends generation unless the request ignores it
+    eos_eng = _engine()
+    eos_eng.model.arch = replace(eos_eng.model.arch, eos_token_id=(stop_at,))
+    a = eos_eng.add_request(prompt, 8)
+    b = eos_eng.add_request(prompt, 8, sampling=SamplingParams(ignore_eos=True))
+    while eos_eng.has_unfinished():
+        eos_eng.step()
+    assert eos_eng.finished[a].output == full[:cut] and eos_eng.finished[b].output == full
+    assert eos_eng.finished[b].finish_reason == "length"
+
+
+def test_hf_eos_parsing():
+    from afd_plugin_b200.models.configs import ModelArchConfig
+
+    hf = {"architectures": ["Qwen3MoeForCausalLM"], "model_type": "qwen3_moe", "hidden_size": 64,
+          "num_hidden_layers": 2, "vocab_size": 100, "num_attention_heads": 4, "num_key_value_heads": 2,
+          "head_dim": 16, "num_experts": 4, "num_experts_per_tok": 2, "moe_intermediate_size": 32,
+          "eos_token_id": [7, 9]}
+    assert ModelArchConfig.from_hf_config(hf).eos_token_id == (7, 9)
+    hf["eos_token_id"] = 3
+    assert ModelArchConfig.from_hf_config(hf).eos_token_id == (3,)
