@@ -21,6 +21,8 @@ def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description="afd_plugin_b200 completions server")
     ap.add_argument("--preset", default="tiny-dsv2")
     ap.add_argument("--checkpoint", default=None, help="HF safetensors directory (random init when absent)")
+    ap.add_argument("--tokenizer", default=None,
+                    help="HF tokenizer directory (default: the checkpoint's; byte tokens when there is none)")
     ap.add_argument("--dtype", default="bfloat16")
     ap.add_argument("--afd", default="", help='JSON additional_config["afd"] (empty: colocated)')
     ap.add_argument("--host", default="127.0.0.1")
@@ -46,6 +48,7 @@ def main(argv=None) -> None:
     from afd_plugin_b200.engine_config import CompilationConfig, EngineConfig, ModelConfig, ParallelConfig
     from afd_plugin_b200.models.configs import get_preset
     from afd_plugin_b200.serving.api_server import EngineLoop, build_app
+    from afd_plugin_b200.serving.tokenizer import load_tokenizer
 
     arch = get_preset(args.preset)
     dtype = getattr(torch, args.dtype)
@@ -64,8 +67,9 @@ def main(argv=None) -> None:
         if args.decode_bench:
             engine.kv.fill_random_(seed=args.seed)
         loop = EngineLoop(engine, decode_bench=args.decode_bench).start()
-        uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
-                    port=args.port)
+        uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port,
+                              tokenizer=load_tokenizer(args.tokenizer or args.checkpoint, arch.vocab_size)),
+                    host=args.host, port=args.port)
         return
 
     import torch.distributed as dist
@@ -105,8 +109,9 @@ def main(argv=None) -> None:
                       tp_group=w.groups.tp_cpu_group, tp_size=args.tp, tp_src=w.groups.tp_leader,
                       decode_bench=args.decode_bench).start()
     if role_rank == 0:
-        uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port), host=args.host,
-                    port=args.port)
+        uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port,
+                              tokenizer=load_tokenizer(args.tokenizer or args.checkpoint, arch.vocab_size)),
+                    host=args.host, port=args.port)
         loop.stop()  # every Attention rank's loop leaves at the same iteration
     else:
         loop.join()

@@ -11,7 +11,8 @@ with a placeholder row, as the reference's DP dummy batches do).
 Endpoints: ``GET /health``, ``GET /metrics`` (engine counters),
 ``POST /v1/completions`` with ``{"prompt": str | [int], "max_tokens": int,
 "stream": bool}`` (streamed as server-sent events, one chunk per token),
-``POST /v1/chat/completions`` (``messages``; rendered by :func:`chat_prompt`),
+``POST /v1/chat/completions`` (``messages``; rendered by the tokenizer's chat
+template, or :func:`chat_prompt` without one),
 and for prefill -> decode disaggregation ``GET`` / ``DELETE /v1/kv/{id}``.
 
 Disaggregated prefill uses the request field ``kv_transfer_params`` with the
@@ -23,7 +24,8 @@ cache rows and answer with ``kv_transfer_params`` naming where to fetch them;
 decode from the transferred token on.
 
 Without a tokenizer in the image, text is mapped to token ids byte by byte
-(``byte_tokenize``), which keeps the server usable for smoke tests and
+(``byte_tokenize``) unless a tokenizer is given (``serving/tokenizer.py``; the
+CLI loads the checkpoint's), which keeps the server usable for smoke tests and
 benchmark drivers that send token ids directly.
 """
 
@@ -41,6 +43,7 @@ import torch.distributed as dist
 from pydantic import BaseModel
 
 from afd_plugin_b200.runtime.sampling import SamplingParams
+from afd_plugin_b200.serving.tokenizer import ByteTokenizer, StreamDetokenizer, Tokenizer, render_chat
 
 
 class SamplingFields(BaseModel):
@@ -86,12 +89,8 @@ class ChatCompletionRequest(SamplingFields):
 
 
 def chat_prompt(messages: list[ChatMessage]) -> str:
-    """Plain role-tagged transcript ending in the assistant tag.
-
-    No tokenizer or chat template ships with the image, so chat requests are
-    rendered this way and byte-tokenised like text prompts.
-    """
-    return "".join(f"<|{m.role}|>{m.content}\n" for m in messages) + "<|assistant|>"
+    """Plain role-tagged transcript ending in the assistant tag (chat without a template)."""
+    return render_chat([{"role": m.role, "content": m.content} for m in messages])
 
 
 def byte_tokenize(text: str, vocab_size: int) -> list[int]:
@@ -341,7 +340,7 @@ class EngineLoop:
 
 
 def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout_s: float = 600.0,
-              advertise_host: str = "127.0.0.1", advertise_port: int = 8000):
+              advertise_host: str = "127.0.0.1", advertise_port: int = 8000, tokenizer: Tokenizer | None = None):
     """FastAPI app serving ``loop`` (rank 0 of the Attention side).
 
     ``advertise_host`` / ``advertise_port`` are what a prefill answer tells the
@@ -352,6 +351,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
     from fastapi.responses import Response, StreamingResponse
 
     vocab = loop.engine.model.arch.vocab_size
+    tok = tokenizer or ByteTokenizer(vocab)
     app = FastAPI(title="afd_plugin_b200")
 
     def _fetch_kv(params: dict) -> bytes:
@@ -367,15 +367,15 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             raise HTTPException(status_code=502, detail=f"KV fetch from {url}: HTTP {r.status_code}")
         return r.content
 
-    def _chunk(chat: bool, model: str, tokens: list[int], finish: str | None, usage: dict | None = None) -> str:
+    def _chunk(chat: bool, model: str, tokens: list[int], text: str, finish: str | None,
+               usage: dict | None = None) -> str:
         if chat:
-            delta = {"role": "assistant", "content": byte_detokenize(tokens)} if tokens else {}
+            delta = {"role": "assistant", "content": text} if tokens else {}
             msg = {"object": "chat.completion.chunk", "model": model,
                    "choices": [{"index": 0, "delta": delta, "token_ids": tokens, "finish_reason": finish}]}
         else:
             msg = {"object": "text_completion", "model": model,
-                   "choices": [{"index": 0, "token_ids": tokens, "text": byte_detokenize(tokens),
-                                "finish_reason": finish}]}
+                   "choices": [{"index": 0, "token_ids": tokens, "text": text, "finish_reason": finish}]}
         if usage is not None:
             msg["usage"] = usage
         return "data: " + json.dumps(msg) + "\n\n"
@@ -392,6 +392,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         import anyio
 
         n, ended = 0, False
+        detok = StreamDetokenizer(tok)
         deadline = time.monotonic() + request_timeout_s
         try:
             while True:
@@ -409,9 +410,9 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
                     return
                 n += 1
                 deadline = time.monotonic() + request_timeout_s
-                yield _chunk(chat, model, [t], None)
+                yield _chunk(chat, model, [t], detok.push(t), None)
             ended = True
-            yield _chunk(chat, model, [], getattr(fut, "finish_reason", "length"),
+            yield _chunk(chat, model, [], "", getattr(fut, "finish_reason", "length"),
                          {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n})
             yield "data: [DONE]\n\n"
         finally:
@@ -448,11 +449,11 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         reason = getattr(fut, "finish_reason", "length")
         if chat:
             body = {"object": "chat.completion", "model": model, "usage": usage, "choices": [
-                {"index": 0, "message": {"role": "assistant", "content": byte_detokenize(out)}, "token_ids": out,
+                {"index": 0, "message": {"role": "assistant", "content": tok.decode(out)}, "token_ids": out,
                  "finish_reason": reason}]}
         else:
             body = {"object": "text_completion", "model": model, "usage": usage, "choices": [
-                {"index": 0, "token_ids": out, "text": byte_detokenize(out), "finish_reason": reason}]}
+                {"index": 0, "token_ids": out, "text": tok.decode(out), "finish_reason": reason}]}
         if prefill_only:
             body["kv_transfer_params"] = {
                 "do_remote_prefill": True, "do_remote_decode": False,
@@ -497,14 +498,14 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     @app.post("/v1/completions")
     def completions(req: CompletionRequest):
-        ids = req.prompt if isinstance(req.prompt, list) else byte_tokenize(req.prompt, vocab)
+        ids = req.prompt if isinstance(req.prompt, list) else tok.encode(req.prompt)
         return _generate(ids, req.max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, False,
                          req)
 
     @app.post("/v1/chat/completions")
     def chat_completions(req: ChatCompletionRequest):
         max_tokens = req.max_completion_tokens or req.max_tokens or 16
-        ids = byte_tokenize(chat_prompt(req.messages), vocab)
+        ids = tok.encode_chat([{"role": m.role, "content": m.content} for m in req.messages])
         return _generate(ids, max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, True, req)
 
     return app

@@ -489,3 +489,53 @@ def test_failed_engine_answers_503():
     finally:
         srv.should_exit = True
         loop.stop()
+
+
+def _word_tokenizer(path):
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    words = ["[UNK]", "<s>", "</s>"] + [f"w{i}" for i in range(200)] + ["hello", "world", "user", "assistant", ":"]
+    tok = Tokenizer(models.WordLevel({w: i for i, w in enumerate(words)}, unk_token="[UNK]"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.decoder = decoders.WordPiece(prefix="##")
+    fast = PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="[UNK]", bos_token="<s>", eos_token="</s>")
+    fast.chat_template = "{% for m in messages %}{{ m['role'] }} : {{ m['content'] }} {% endfor %}assistant :"
+    fast.save_pretrained(str(path))
+    return fast
+
+
+def test_hf_tokenizer_text_chat_and_stream(tmp_path):
+    from afd_plugin_b200.serving.tokenizer import HFTokenizer, load_tokenizer
+
+    fast = _word_tokenizer(tmp_path)
+    tok = load_tokenizer(str(tmp_path), 1024)
+    assert isinstance(tok, HFTokenizer) and tok.encode("hello world") == fast.encode("hello world")
+    assert isinstance(load_tokenizer(None, 1024), type(load_tokenizer(str(tmp_path / "missing"), 1024)))
+    loop = EngineLoop(_engine()).start()
+    srv, url = _serve(lambda port: build_app(loop, advertise_port=port, tokenizer=tok))
+    try:
+        ids = fast.encode("hello world w5 w7")
+        want = _engine().generate([ids], 5)[0]
+        r = requests.post(url + "/v1/completions", json={"prompt": "hello world w5 w7", "max_tokens": 5},
+                          timeout=60).json()
+        assert r["choices"][0]["token_ids"] == want and r["choices"][0]["text"] == fast.decode(
+            want, skip_special_tokens=True)
+        msgs = [{"role": "user", "content": "hello w3"}]
+        chat_ids = fast.apply_chat_template(msgs, tokenize=True, add_generation_prompt=True)
+        chat_ids = list(chat_ids["input_ids"] if hasattr(chat_ids, "keys") else chat_ids)
+        c = requests.post(url + "/v1/chat/completions", json={"messages": msgs, "max_tokens": 3}, timeout=60).json()
+        assert c["usage"]["prompt_tokens"] == len(chat_ids)
+        assert c["choices"][0]["token_ids"] == _engine().generate([chat_ids], 3)[0]
+        text = ""
+        with requests.post(url + "/v1/completions", json={"prompt": "hello world w5 w7", "max_tokens": 5,
+                                                          "stream": True}, stream=True, timeout=60) as s:
+            import json as _json
+
+            for line in s.iter_lines():
+                if line.startswith(b"data: {"):
+                    text += _json.loads(line[6:])["choices"][0]["text"]
+        assert text == r["choices"][0]["text"]
+    finally:
+        srv.should_exit = True
+        loop.stop()
