@@ -474,6 +474,13 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         released = loop.call(lambda eng: eng.release_kv(req_id)).result(timeout=request_timeout_s)
         return {"released": bool(released)}
 
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{
+            "id": model_name, "object": "model", "owned_by": "afd_plugin_b200",
+            "max_model_len": loop.engine.config.model_config.max_model_len,
+            "architecture": loop.engine.model.arch.architecture}]}
+
     @app.post("/reset_prefix_cache")
     def reset_prefix_cache():
         # The engine caches no prompt prefixes across requests; nothing to reset.

@@ -340,6 +340,19 @@ def build_proxy_app(backends: list[str] | None = None, *, prefill: list[str] | N
     def healthcheck():
         return health()
 
+    @app.get("/v1/models")
+    def models():
+        """The model list of the first reachable backend (every backend serves the same model)."""
+        for bal in pools.values():
+            for b in bal.backends:
+                try:
+                    r = requests.get(b + "/v1/models", timeout=5)
+                    if r.status_code == 200:
+                        return r.json()
+                except requests.RequestException:
+                    continue
+        raise HTTPException(status_code=503, detail="no backend answered /v1/models")
+
     @app.get("/health")
     def health():
         out = {}

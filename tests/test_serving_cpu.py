@@ -56,6 +56,8 @@ def test_completions_match_engine_generate(server):
     assert resp[0]["usage"] == {"prompt_tokens": 6, "completion_tokens": 6, "total_tokens": 12}
     m = requests.get(url + "/metrics", timeout=5).json()
     assert m["completed"] == 4 and m["generated_tokens"] == 24
+    models = requests.get(url + "/v1/models", timeout=5).json()
+    assert models["data"][0]["id"] == "afd-b200" and models["data"][0]["max_model_len"] == 96
     assert m["ttft_count"] == 4 and m["tpot_count"] == 4
     assert 0 < m["mean_ttft_s"] < 60 and 0 < m["mean_tpot_s"] < 60
 
@@ -443,6 +445,7 @@ def test_proxy_instances_endpoints():
         bad = requests.post(purl + "/instances/add", json={"type": "prefill", "instances": [a_url]}, timeout=30)
         assert bad.status_code == 400
         assert requests.get(purl + "/healthcheck", timeout=10).json()["backends"] == {b_url: True}
+        assert requests.get(purl + "/v1/models", timeout=10).json()["data"][0]["object"] == "model"
         assert requests.post(purl + "/reset_prefix_cache", timeout=10).json()[b_url]["reset"] is False
     finally:
         for s_ in (a, b, proxy):
