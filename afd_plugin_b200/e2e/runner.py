@@ -11,12 +11,12 @@ bounded concurrency, records the greedy outputs, and stops the group.
 
 Gate: the first scenario is the reference; every later one must reproduce its
 first tokens for at least ``--min-first-token-match`` of the requests and its
-whole outputs for at least ``--min-exact-match``.  The reference's gate is a
-GSM8K score with real weights (``docs/design/module/e2e_testing.md:145-163``);
-with no datasets or checkpoints on hand this runner gates on agreement with
-the colocated engine instead, which a disaggregated deployment must match
-token for token when it computes the same math (fp32, or bf16 up to reduction
-order).
+whole outputs for at least ``--min-exact-match`` -- a disaggregated deployment
+must match the colocated engine token for token when it computes the same
+math (fp32, or bf16 up to reduction order).  With ``--gsm8k-data`` every
+scenario is also gated on GSM8K accuracy (``e2e/gsm8k.py``), the reference's
+gate (``docs/design/module/e2e_testing.md:145-163``); that needs a real
+checkpoint and a local copy of the dataset.
 """
 
 from __future__ import annotations
@@ -161,6 +161,16 @@ def _run_scenario_once(scn: Scenario, args, prompts: list[list[int]], *, log_dir
         dt = time.perf_counter() - t0
         result.update(outputs=outs, wall_s=round(dt, 3),
                       output_tok_per_s=round(sum(len(o) for o in outs) / max(dt, 1e-9), 1))
+        if args.gsm8k_data:
+            from afd_plugin_b200.e2e import gsm8k
+
+            data = gsm8k.load_jsonl(args.gsm8k_data)
+            pool = gsm8k.load_jsonl(args.gsm8k_train) if args.gsm8k_train else data
+            shots = pool[: args.gsm8k_shots]
+            if not args.gsm8k_train:
+                data = data[args.gsm8k_shots:]
+            result["gsm8k"] = gsm8k.evaluate(url, data, shots, limit=args.gsm8k_limit,
+                                             timeout_s=args.request_timeout)
     finally:
         result["teardown"] = ",".join(stop_server(s_) for s_ in reversed(servers))
     return result
@@ -188,6 +198,11 @@ def main(argv=None) -> int:
     ap.add_argument("--request-timeout", type=float, default=600.0)
     ap.add_argument("--min-exact-match", type=float, default=0.0)
     ap.add_argument("--min-first-token-match", type=float, default=0.9)
+    ap.add_argument("--gsm8k-data", default=None, help="GSM8K test JSONL: also gate every scenario on accuracy")
+    ap.add_argument("--gsm8k-train", default=None, help="few-shot examples JSONL (default: head of --gsm8k-data)")
+    ap.add_argument("--gsm8k-shots", type=int, default=8)
+    ap.add_argument("--gsm8k-limit", type=int, default=7)
+    ap.add_argument("--gsm8k-threshold", type=float, default=0.27)
     ap.add_argument("--log-dir", default="e2e_logs")
     ap.add_argument("--output", default=None, help="write the results as JSON here")
     args = ap.parse_args(argv)
@@ -214,6 +229,10 @@ def main(argv=None) -> int:
             failures.append(f"{scn.name}: {exc!r}")
         results.append(res)
         print(json.dumps({k: v for k, v in res.items() if k not in ("outputs", "cmd")}), flush=True)
+    for res in results:
+        g = res.get("gsm8k")
+        if g is not None and g["exact_match_flexible"] < args.gsm8k_threshold:
+            failures.append(f"{res['scenario']}: gsm8k {g['exact_match_flexible']:.3f} < {args.gsm8k_threshold}")
     ref = results[0].get("outputs")
     for res in results[1:]:
         if ref is None or "outputs" not in res:

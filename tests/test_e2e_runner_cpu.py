@@ -146,3 +146,52 @@ def test_pd_scenario_prefill_colocated_decode_afd(tmp_path):
     res = json.loads(out.read_text())["results"]
     assert res[1]["agreement"]["exact_match"] == 1.0
     assert len(res[1]["teardown"].split(",")) == 3
+
+
+def test_gsm8k_parsing_and_prompt():
+    from afd_plugin_b200.e2e import gsm8k
+
+    assert gsm8k.reference_answer("so 3 + 4 = 7.\n#### 7") == "7"
+    assert gsm8k.reference_answer("#### 1,234") == "1234"
+    assert gsm8k.extract_strict("The answer is #### $18.00") == "18"
+    assert gsm8k.extract_strict("no marker 5") is None
+    assert gsm8k.extract_flexible("first 3 then 4.50.") == "4.5"
+    p = gsm8k.build_prompt([{"question": "1+1?", "answer": "#### 2"}], "2+2?")
+    assert p == "Question: 1+1?\nAnswer: #### 2\n\nQuestion: 2+2?\nAnswer:"
+    assert gsm8k._truncate(" #### 4\n\nQuestion: next") == " #### 4"
+
+
+def test_gsm8k_against_a_fake_server(tmp_path):
+    import threading
+
+    import uvicorn
+    from fastapi import FastAPI
+
+    from afd_plugin_b200.e2e import gsm8k
+    from afd_plugin_b200.runtime.launcher import free_port
+
+    data = [{"question": f"What is {i} + {i}?", "answer": f"{i} + {i} = {2 * i}\n#### {2 * i}"} for i in range(12)]
+    path = tmp_path / "gsm8k.jsonl"
+    path.write_text("\n".join(json.dumps(d) for d in data))
+    app = FastAPI()
+
+    @app.post("/v1/completions")
+    def complete(body: dict):
+        q = body["prompt"].rsplit("Question: ", 1)[1]
+        i = int(q.split()[2])
+        text = f" {i} + {i} = {2 * i}\n#### {2 * i}\n\nQuestion: more" if i % 2 == 0 else f" it is {2 * i + 1}"
+        return {"choices": [{"text": text, "token_ids": []}]}
+
+    port = free_port()
+    srv = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+    threading.Thread(target=srv.run, daemon=True).start()
+    time.sleep(1.0)
+    try:
+        rc = gsm8k.main(["--url", f"http://127.0.0.1:{port}", "--data", str(path), "--shots", "2", "--limit", "8",
+                         "--threshold", "0.4", "--output", str(tmp_path / "out.json")])
+        res = json.loads((tmp_path / "out.json").read_text())
+        # questions 2..9: the even ones are answered right
+        assert res["n"] == 8 and res["exact_match_strict"] == 0.5 and res["exact_match_flexible"] == 0.5
+        assert rc == 0 and res["gate"] == "pass"
+    finally:
+        srv.should_exit = True
