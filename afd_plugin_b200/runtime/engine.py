@@ -35,7 +35,7 @@ from afd_plugin_b200.runtime.cuda_graph import pad_to_capture_size, validate_cud
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor, LocalFFNExecutor
 from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache
 from afd_plugin_b200.runtime.model_runner import ModelRunner
-from afd_plugin_b200.runtime.sampling import GREEDY, SamplingParams, make_generator, sample
+from afd_plugin_b200.runtime.sampling import GREEDY, SamplingParams, make_generator, sample, token_logprobs
 
 
 @dataclass
@@ -53,6 +53,10 @@ class Request:
     sampling: SamplingParams = GREEDY
     generator: torch.Generator | None = None  # the request's own noise stream (seeded requests)
     stop_ids: frozenset[int] = frozenset()  # EOS and stop tokens that end generation
+    # with sampling.logprobs: per output token its logprob (None if another engine produced it)
+    # and the top alternatives
+    token_logprobs: list = field(default_factory=list)
+    top_logprobs: list = field(default_factory=list)
 
     @property
     def num_tokens(self) -> int:
@@ -198,12 +202,30 @@ class LLMEngine:
         req.stop_ids = frozenset(eos) | frozenset(sp.stop_token_ids)
 
     def _sample(self, reqs: list[Request], tokens: torch.Tensor) -> torch.Tensor:
-        """Replace the argmax of sampled requests' rows in ``tokens`` (from the runner's last logits)."""
-        if all(r.sampling.greedy for r in reqs):
+        """Replace the argmax of sampled requests' rows in ``tokens`` (from the runner's last logits)
+        and record log-probabilities for requests that asked for them."""
+        plain = True
+        for r in reqs:
+            if not r.sampling.greedy or r.sampling.logprobs is not None:
+                plain = False
+                break
+        if plain:
             return tokens
-        drawn = sample(self.runner.last_logits[: len(reqs)], [r.sampling for r in reqs],
-                       [r.generator for r in reqs], self._sample_gen)
-        tokens[: len(reqs)].copy_(drawn)
+        logits = self.runner.last_logits[: len(reqs)]
+        if not all(r.sampling.greedy for r in reqs):
+            drawn = sample(logits, [r.sampling for r in reqs], [r.generator for r in reqs], self._sample_gen)
+            tokens[: len(reqs)].copy_(drawn)
+        rows = [i for i, r in enumerate(reqs) if r.sampling.logprobs is not None]
+        if rows:
+            idx = torch.tensor(rows, device=logits.device)
+            top_n = max(reqs[i].sampling.logprobs for i in rows)
+            chosen, tops = token_logprobs(logits.index_select(0, idx), tokens[: len(reqs)].index_select(0, idx),
+                                          top_n)
+            for i, c, t in zip(rows, chosen, tops):
+                r = reqs[i]
+                pad = len(r.output) - len(r.token_logprobs)  # tokens this engine did not produce
+                r.token_logprobs.extend([None] * pad + [c])
+                r.top_logprobs.extend([[]] * pad + [t[: r.sampling.logprobs]])
         return tokens
 
     def abort(self, req_id: int) -> bool:

@@ -31,6 +31,8 @@ class SamplingParams:
     # generation also ends at these tokens (and at the model's EOS unless ignore_eos)
     stop_token_ids: tuple[int, ...] = ()
     ignore_eos: bool = False
+    # per generated token: its log-probability under the model, and the ``logprobs`` most likely tokens
+    logprobs: int | None = None
 
     def __post_init__(self) -> None:
         if self.temperature < 0:
@@ -39,6 +41,8 @@ class SamplingParams:
             raise ValueError("top_k must be >= 0")
         if not 0.0 < self.top_p <= 1.0:
             raise ValueError("top_p must be in (0, 1]")
+        if self.logprobs is not None and not 0 <= self.logprobs <= 20:
+            raise ValueError("logprobs must be in [0, 20]")
 
     @property
     def greedy(self) -> bool:
@@ -105,4 +109,15 @@ def sample(logits: torch.Tensor, params: list[SamplingParams], generators: list[
     return out
 
 
-__all__ = ["GREEDY", "SamplingParams", "filtered_probs", "make_generator", "sample"]
+def token_logprobs(logits: torch.Tensor, tokens: torch.Tensor, top_n: int) -> tuple[list[float], list[list]]:
+    """Log-probabilities (of the raw model distribution) of ``tokens`` per row, and each row's
+    ``top_n`` most likely ``(token, logprob)`` pairs."""
+    lp = torch.log_softmax(logits.float(), dim=-1)
+    chosen = lp.gather(1, tokens.long().view(-1, 1)).view(-1).tolist()
+    if top_n <= 0:
+        return chosen, [[] for _ in chosen]
+    v, i = lp.topk(top_n, dim=-1)
+    return chosen, [list(zip(ii, vv)) for ii, vv in zip(i.tolist(), v.tolist())]
+
+
+__all__ = ["GREEDY", "SamplingParams", "filtered_probs", "make_generator", "sample", "token_logprobs"]

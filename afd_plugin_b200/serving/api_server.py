@@ -55,15 +55,29 @@ class SamplingFields(BaseModel):
     seed: int | None = None
     stop_token_ids: list[int] | None = None
     ignore_eos: bool | None = None
+    # completions: an int (top alternatives per token); chat: a bool, with top_logprobs
+    logprobs: int | bool | None = None
+    top_logprobs: int | None = None
+    n: int = 1
 
-    def sampling(self) -> SamplingParams | None:
+    def n_logprobs(self) -> int | None:
+        if self.logprobs is None or self.logprobs is False:
+            return None
+        if self.logprobs is True:
+            return int(self.top_logprobs or 0)
+        return int(self.logprobs)
+
+    def sampling(self, index: int = 0) -> SamplingParams | None:
+        """The parameters of choice ``index`` (seeded choices use seed + index)."""
+        lp = self.n_logprobs()
         if all(v is None for v in (self.temperature, self.top_p, self.top_k, self.seed, self.stop_token_ids,
-                                   self.ignore_eos)):
+                                   self.ignore_eos, lp)):
             return None
         return SamplingParams(temperature=float(self.temperature or 0.0), top_k=int(self.top_k or 0),
-                              top_p=float(self.top_p if self.top_p is not None else 1.0), seed=self.seed,
+                              top_p=float(self.top_p if self.top_p is not None else 1.0),
+                              seed=None if self.seed is None else self.seed + index,
                               stop_token_ids=tuple(int(t) for t in self.stop_token_ids or ()),
-                              ignore_eos=bool(self.ignore_eos))
+                              ignore_eos=bool(self.ignore_eos), logprobs=lp)
 
 
 class CompletionRequest(SamplingFields):
@@ -322,6 +336,8 @@ class EngineLoop:
                 self.stats["tpot_s_sum"] += (now - p.first_token_at) / (len(out) - 1)
                 self.stats["tpot_count"] += 1
             p.future.finish_reason = req.finish_reason
+            skip = 1 if req.synthetic_prefill else 0
+            p.future.logprobs = (req.token_logprobs[skip:], req.top_logprobs[skip:])
             if p.stream is not None:
                 self._push_tokens(p)
                 p.stream.put(None)
@@ -420,10 +436,27 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             if not ended and rid is not None:
                 loop.abort(rid)
 
+    def _logprobs_block(chat: bool, out: list[int], lps: tuple[list, list]) -> dict:
+        chosen, tops = lps
+        pieces = [tok.decode([t]) for t in out]
+        if chat:
+            return {"content": [{"token": piece, "logprob": c,
+                                 "top_logprobs": [{"token": tok.decode([i]), "logprob": v} for i, v in top]}
+                                for piece, c, top in zip(pieces, chosen, tops)]}
+        offsets, pos = [], 0
+        for piece in pieces:
+            offsets.append(pos)
+            pos += len(piece)
+        return {"tokens": pieces, "token_logprobs": chosen, "text_offset": offsets,
+                "top_logprobs": [{tok.decode([i]): v for i, v in top} for top in tops]}
+
     def _generate(ids: list[int], max_tokens: int, params: dict | None, stream_req: bool, model: str, chat: bool,
                   fields: SamplingFields):
         try:
-            sampling = fields.sampling()
+            n = int(fields.n)
+            if n < 1:
+                raise ValueError("n must be >= 1")
+            samplings = [fields.sampling(i) for i in range(n)]
         except ValueError as exc:
             raise HTTPException(status_code=400, detail=str(exc)) from exc
         if max_tokens < 1:
@@ -432,32 +465,43 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             raise HTTPException(status_code=400, detail=f"prompt token ids must be in [0, {vocab})")
         params = params or {}
         prefill_only = bool(params.get("do_remote_decode"))
+        if n > 1 and (stream_req or prefill_only or params.get("do_remote_prefill")):
+            raise HTTPException(status_code=400, detail="n > 1 is served without streaming or KV hand-off")
         stream = queue.Queue() if stream_req and not prefill_only else None
         try:
             if params.get("do_remote_prefill"):
-                fut = loop.submit_prefilled(ids, _fetch_kv(params), max_tokens, stream=stream, sampling=sampling)
+                futs = [loop.submit_prefilled(ids, _fetch_kv(params), max_tokens, stream=stream,
+                                              sampling=samplings[0])]
             else:
-                fut = loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream, sampling=sampling)
+                futs = [loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream, sampling=sp)
+                        for sp in samplings]
             if stream is not None:
-                return StreamingResponse(_sse(stream, fut, len(ids), model, chat), media_type="text/event-stream")
-            out = fut.result(timeout=request_timeout_s)
+                return StreamingResponse(_sse(stream, futs[0], len(ids), model, chat),
+                                         media_type="text/event-stream")
+            outs = [f.result(timeout=request_timeout_s) for f in futs]
         except ValueError as exc:
             raise HTTPException(status_code=400, detail=str(exc)) from exc
         except RuntimeError as exc:  # the engine loop failed (or this rank takes no requests)
             raise HTTPException(status_code=503, detail=str(exc)) from exc
-        usage = {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)}
-        reason = getattr(fut, "finish_reason", "length")
-        if chat:
-            body = {"object": "chat.completion", "model": model, "usage": usage, "choices": [
-                {"index": 0, "message": {"role": "assistant", "content": tok.decode(out)}, "token_ids": out,
-                 "finish_reason": reason}]}
-        else:
-            body = {"object": "text_completion", "model": model, "usage": usage, "choices": [
-                {"index": 0, "token_ids": out, "text": tok.decode(out), "finish_reason": reason}]}
+        n_out = sum(len(o) for o in outs)
+        usage = {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}
+        choices = []
+        for i, (f, out) in enumerate(zip(futs, outs)):
+            reason = getattr(f, "finish_reason", "length")
+            if chat:
+                c = {"index": i, "message": {"role": "assistant", "content": tok.decode(out)}, "token_ids": out,
+                     "finish_reason": reason}
+            else:
+                c = {"index": i, "token_ids": out, "text": tok.decode(out), "finish_reason": reason}
+            if samplings[i] is not None and samplings[i].logprobs is not None:
+                c["logprobs"] = _logprobs_block(chat, out, getattr(f, "logprobs", ([], [])))
+            choices.append(c)
+        body = {"object": "chat.completion" if chat else "text_completion", "model": model, "usage": usage,
+                "choices": choices}
         if prefill_only:
             body["kv_transfer_params"] = {
                 "do_remote_prefill": True, "do_remote_decode": False,
-                "remote_request_id": fut.req_id, "remote_host": advertise_host, "remote_port": advertise_port,
+                "remote_request_id": futs[0].req_id, "remote_host": advertise_host, "remote_port": advertise_port,
             }
         return body
 

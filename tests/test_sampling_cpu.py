@@ -164,3 +164,65 @@ def test_hf_eos_parsing():
     assert ModelArchConfig.from_hf_config(hf).eos_token_id == (7, 9)
     hf["eos_token_id"] = 3
     assert ModelArchConfig.from_hf_config(hf).eos_token_id == (3,)
+
+
+def test_engine_logprobs_match_log_softmax():
+    eng = _engine()
+    prompt = [5, 9, 100, 7]
+    rid = eng.add_request(prompt, 4, sampling=SamplingParams(logprobs=3))
+    while eng.has_unfinished():
+        eng.step()
+    r = eng.finished[rid]
+    assert len(r.token_logprobs) == len(r.output) == 4 and all(len(t) == 3 for t in r.top_logprobs)
+    # greedy: the chosen token is the most likely one
+    for tok, lp, top in zip(r.output, r.token_logprobs, r.top_logprobs):
+        assert top[0][0] == tok and abs(top[0][1] - lp) < 1e-6 and lp <= 0.0
+    # recompute the first token's logprob from a fresh prefill
+    ref = _engine()
+    req = __import__("afd_plugin_b200.runtime.engine", fromlist=["Request"]).Request(0, prompt, 1)
+    ref._ensure_blocks(req, len(prompt) + 1)
+    ref.runner.prefill([prompt], [req.blocks], [0])
+    want = torch.log_softmax(ref.runner.last_logits.float(), -1)[0, r.output[0]].item()
+    assert abs(want - r.token_logprobs[0]) < 1e-5
+
+
+def test_server_n_choices_and_logprobs():
+    import threading
+    import time
+
+    import requests
+    import uvicorn
+
+    from afd_plugin_b200.runtime.launcher import free_port
+    from afd_plugin_b200.serving import EngineLoop, build_app
+
+    loop = EngineLoop(_engine()).start()
+    port = free_port()
+    srv = uvicorn.Server(uvicorn.Config(build_app(loop), host="127.0.0.1", port=port, log_level="warning"))
+    threading.Thread(target=srv.run, daemon=True).start()
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(200):
+        try:
+            if requests.get(url + "/health", timeout=2).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.05)
+    try:
+        body = {"prompt": [5, 9, 100, 7], "max_tokens": 5, "temperature": 1.0, "seed": 5, "n": 3, "logprobs": 2}
+        r = requests.post(url + "/v1/completions", json=body, timeout=60).json()
+        assert [c["index"] for c in r["choices"]] == [0, 1, 2] and r["usage"]["completion_tokens"] == 15
+        lp = r["choices"][0]["logprobs"]
+        assert len(lp["tokens"]) == len(lp["token_logprobs"]) == len(lp["top_logprobs"]) == 5
+        assert all(len(t) <= 2 for t in lp["top_logprobs"]) and lp["text_offset"][0] == 0
+        again = requests.post(url + "/v1/completions", json=body, timeout=60).json()
+        assert [c["token_ids"] for c in again["choices"]] == [c["token_ids"] for c in r["choices"]]
+        chat = requests.post(url + "/v1/chat/completions", json={
+            "messages": [{"role": "user", "content": "hi"}], "max_tokens": 3, "logprobs": True, "top_logprobs": 1},
+            timeout=60).json()
+        content = chat["choices"][0]["logprobs"]["content"]
+        assert len(content) == 3 and len(content[0]["top_logprobs"]) == 1
+        bad = requests.post(url + "/v1/completions", json=dict(body, stream=True), timeout=60)
+        assert bad.status_code == 400
+    finally:
+        srv.should_exit = True
+        loop.stop()
