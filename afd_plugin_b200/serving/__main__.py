@@ -17,30 +17,74 @@ import json
 import os
 
 
-def main(argv=None) -> None:
+def parse_args(argv=None) -> argparse.Namespace:
+    """Server flags; the vLLM spellings used by the reference's launch recipes are accepted too.
+
+    ``--additional-config '{"afd": {...}}'`` (the reference's AFD switch),
+    ``--compilation-config '{"cudagraph_mode": "FULL_DECODE_ONLY", "cudagraph_capture_sizes": [...]}'``,
+    ``--enforce-eager``, ``--enable-dbo``, ``--tensor-parallel-size``,
+    ``--model`` / a positional model path, ``--served-model-name``;
+    ``--enable-expert-parallel`` and the DBO token thresholds are accepted and
+    have nothing to switch (FFN ranks always shard experts; DBO splits any
+    batch of two or more).
+    """
     ap = argparse.ArgumentParser(description="afd_plugin_b200 completions server")
-    ap.add_argument("--preset", default="tiny-dsv2")
-    ap.add_argument("--checkpoint", default=None, help="HF safetensors directory (random init when absent)")
+    ap.add_argument("model_path", nargs="?", default=None, help="HF checkpoint directory (as `vllm serve MODEL`)")
+    ap.add_argument("--preset", default="tiny-dsv2", help="architecture when no checkpoint is given")
+    ap.add_argument("--checkpoint", "--model", dest="checkpoint", default=None,
+                    help="HF safetensors directory (random init when absent)")
     ap.add_argument("--tokenizer", default=None,
                     help="HF tokenizer directory (default: the checkpoint's; byte tokens when there is none)")
+    ap.add_argument("--served-model-name", default="afd-b200")
     ap.add_argument("--dtype", default="bfloat16")
     ap.add_argument("--afd", default="", help='JSON additional_config["afd"] (empty: colocated)')
+    ap.add_argument("--additional-config", default="", help='JSON {"afd": {...}} (the reference\'s switch)')
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--max-num-seqs", type=int, default=64)
     ap.add_argument("--max-model-len", type=int, default=4096)
-    ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--eager", "--enforce-eager", dest="eager", action="store_true")
     ap.add_argument("--capture-sizes", default="", help="comma-separated decode graph batch sizes "
                     "(default: --max-num-seqs)")
-    ap.add_argument("--dbo", action="store_true", help="two-ubatch overlap of attention and FFN (AFD only)")
+    ap.add_argument("--compilation-config", default="", help="JSON with cudagraph_mode / cudagraph_capture_sizes")
+    ap.add_argument("--dbo", "--enable-dbo", dest="dbo", action="store_true",
+                    help="two-ubatch overlap of attention and FFN (AFD only)")
+    ap.add_argument("--dbo-decode-token-threshold", type=int, default=None)
+    ap.add_argument("--dbo-prefill-token-threshold", type=int, default=None)
+    ap.add_argument("--enable-expert-parallel", action="store_true")
     ap.add_argument("--seed", type=int, default=0, help="random-init seed when no checkpoint is given")
     ap.add_argument("--decode-bench", action="store_true",
                     help="take every prompt as prefilled (random cache rows) and only decode: long-ISL decode "
                          "benchmarks without prefill")
-    ap.add_argument("--tp", type=int, default=1, help="attention tensor parallelism (AFD only; "
-                    "num_attention_ranks = DP x TP)")
+    ap.add_argument("--tp", "--tensor-parallel-size", dest="tp", type=int, default=1,
+                    help="attention tensor parallelism (AFD only; num_attention_ranks = DP x TP)")
     args = ap.parse_args(argv)
-    sizes = [int(x) for x in args.capture_sizes.split(",") if x] or [args.max_num_seqs]
+    if args.model_path and not args.checkpoint:
+        args.checkpoint = args.model_path
+    if args.additional_config:
+        extra = json.loads(args.additional_config)
+        if not isinstance(extra, dict):
+            ap.error("--additional-config must be a JSON object")
+        if "afd" in extra:
+            if args.afd:
+                ap.error("give the AFD config once: --afd or --additional-config")
+            args.afd = json.dumps(extra["afd"])
+    sizes = [int(x) for x in args.capture_sizes.split(",") if x]
+    if args.compilation_config:
+        cc = json.loads(args.compilation_config)
+        mode = cc.get("cudagraph_mode")
+        if mode not in (None, "FULL_DECODE_ONLY", "NONE"):
+            ap.error(f"cudagraph_mode {mode!r}: only FULL_DECODE_ONLY (or NONE) is supported")
+        if mode == "NONE":
+            args.eager = True
+        sizes = sizes or [int(x) for x in cc.get("cudagraph_capture_sizes", [])]
+    args.sizes = sizes or [args.max_num_seqs]
+    return args
+
+
+def main(argv=None) -> None:
+    args = parse_args(argv)
+    sizes = args.sizes
 
     import torch
     import uvicorn
@@ -50,7 +94,12 @@ def main(argv=None) -> None:
     from afd_plugin_b200.serving.api_server import EngineLoop, build_app
     from afd_plugin_b200.serving.tokenizer import load_tokenizer
 
-    arch = get_preset(args.preset)
+    if args.checkpoint:
+        from afd_plugin_b200.models.loader import read_hf_config
+
+        arch = read_hf_config(args.checkpoint)
+    else:
+        arch = get_preset(args.preset)
     dtype = getattr(torch, args.dtype)
     afd = json.loads(args.afd) if args.afd else {}
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -68,6 +117,7 @@ def main(argv=None) -> None:
             engine.kv.fill_random_(seed=args.seed)
         loop = EngineLoop(engine, decode_bench=args.decode_bench).start()
         uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port,
+                              model_name=args.served_model_name,
                               tokenizer=load_tokenizer(args.tokenizer or args.checkpoint, arch.vocab_size)),
                     host=args.host, port=args.port)
         return
@@ -110,6 +160,7 @@ def main(argv=None) -> None:
                       decode_bench=args.decode_bench).start()
     if role_rank == 0:
         uvicorn.run(build_app(loop, advertise_host=args.host, advertise_port=args.port,
+                              model_name=args.served_model_name,
                               tokenizer=load_tokenizer(args.tokenizer or args.checkpoint, arch.vocab_size)),
                     host=args.host, port=args.port)
         loop.stop()  # every Attention rank's loop leaves at the same iteration

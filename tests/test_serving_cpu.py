@@ -542,3 +542,24 @@ def test_hf_tokenizer_text_chat_and_stream(tmp_path):
     finally:
         srv.should_exit = True
         loop.stop()
+
+
+def test_server_cli_accepts_reference_recipe_flags():
+    import json as _json
+
+    from afd_plugin_b200.serving.__main__ import parse_args
+
+    a = parse_args(["/models/dsv2-lite", "--additional-config",
+                    '{"afd": {"role": "attention", "num_attention_ranks": 2, "num_ffn_ranks": 2}}',
+                    "--compilation-config", '{"cudagraph_mode": "FULL_DECODE_ONLY", "cudagraph_capture_sizes": [64]}',
+                    "--enable-dbo", "--dbo-decode-token-threshold", "2", "--dbo-prefill-token-threshold", "12",
+                    "--enable-expert-parallel", "--tensor-parallel-size", "1", "--served-model-name", "dsv2"])
+    assert a.checkpoint == "/models/dsv2-lite" and a.sizes == [64] and a.dbo and a.tp == 1 and not a.eager
+    assert _json.loads(a.afd)["num_ffn_ranks"] == 2 and a.served_model_name == "dsv2"
+    b = parse_args(["--compilation-config", '{"cudagraph_mode": "NONE"}', "--max-num-seqs", "8"])
+    assert b.eager and b.sizes == [8] and b.checkpoint is None
+    assert parse_args(["--enforce-eager", "--model", "/m"]).eager
+    with pytest.raises(SystemExit):
+        parse_args(["--compilation-config", '{"cudagraph_mode": "PIECEWISE"}'])
+    with pytest.raises(SystemExit):
+        parse_args(["--afd", "{}", "--additional-config", '{"afd": {}}'])
