@@ -42,6 +42,8 @@ class LocalAFDSpec:
     fault: dict | None = None
     # attention tensor parallelism: num_attention_ranks = DP x tp
     tp: int = 1
+    # HF checkpoint directory: architecture from its config.json, role-filtered weights
+    checkpoint: str | None = None
 
 
 def free_port() -> int:
@@ -54,12 +56,17 @@ def build_engine_config(spec: LocalAFDSpec):
     from afd_plugin_b200.engine_config import CompilationConfig, EngineConfig, ModelConfig, ParallelConfig
     from afd_plugin_b200.models.configs import ModelArchConfig, get_preset
 
-    arch = ModelArchConfig(**spec.arch) if spec.arch else get_preset(spec.preset)
+    if spec.checkpoint:
+        from afd_plugin_b200.models.loader import read_hf_config
+
+        arch = read_hf_config(spec.checkpoint)
+    else:
+        arch = ModelArchConfig(**spec.arch) if spec.arch else get_preset(spec.preset)
     dtype = getattr(torch, spec.dtype)
     A = int(spec.afd.get("num_attention_ranks", 1))
     return EngineConfig(
         model_config=ModelConfig(arch, dtype=dtype, enforce_eager=spec.enforce_eager,
-                                 max_model_len=spec.max_model_len, seed=spec.seed),
+                                 max_model_len=spec.max_model_len, seed=spec.seed, checkpoint=spec.checkpoint),
         parallel_config=ParallelConfig(data_parallel_size=A // spec.tp, tensor_parallel_size=spec.tp,
                                        use_ubatching=spec.use_ubatching, num_ubatches=2 if spec.use_ubatching else 1),
         compilation_config=CompilationConfig(cudagraph_capture_sizes=list(spec.capture_sizes)),

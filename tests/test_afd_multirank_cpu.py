@@ -121,3 +121,49 @@ def test_deepseek_v1_mha_2a1f():
     ref = _colocated("tiny-dsv1", prompts, 6)
     outs, _ = _run("tiny-dsv1", {"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts, max_tokens=6)
     assert outs == ref
+
+
+def test_afd_from_an_hf_checkpoint(tmp_path):
+    """Architecture from config.json, role-filtered weights from safetensors, on every rank."""
+    import json as _json
+    import zlib
+
+    from safetensors.torch import save_file
+
+    from afd_plugin_b200.models.loader import read_hf_config
+
+    a = get_preset("tiny-dsv2")
+    hf = {"architectures": ["DeepseekV2ForCausalLM"], "model_type": "deepseek_v2", "hidden_size": a.hidden_size,
+          "num_hidden_layers": a.num_hidden_layers, "vocab_size": a.vocab_size,
+          "num_attention_heads": a.num_attention_heads, "q_lora_rank": a.q_lora_rank,
+          "kv_lora_rank": a.kv_lora_rank, "qk_nope_head_dim": a.qk_nope_head_dim,
+          "qk_rope_head_dim": a.qk_rope_head_dim, "v_head_dim": a.v_head_dim,
+          "intermediate_size": a.intermediate_size, "first_k_dense_replace": a.first_k_dense_replace,
+          "n_routed_experts": a.n_routed_experts, "num_experts_per_tok": a.num_experts_per_tok,
+          "moe_intermediate_size": a.moe_intermediate_size, "n_shared_experts": a.n_shared_experts,
+          "scoring_func": a.scoring_func, "topk_method": a.topk_method, "n_group": a.n_group,
+          "topk_group": a.topk_group, "norm_topk_prob": a.norm_topk_prob,
+          "routed_scaling_factor": a.routed_scaling_factor, "max_position_embeddings": 2048}
+    (tmp_path / "config.json").write_text(_json.dumps(hf))
+    parsed = read_hf_config(str(tmp_path))
+    src = build_model(parsed, role="colocated", dtype=torch.float32, seed=0)
+    tensors = {}
+    for spec in src.param_specs():
+        g = torch.Generator().manual_seed(zlib.crc32(spec.name.encode()) & 0xFFFF)
+        t = torch.randn(spec.shape, generator=g) * 0.05
+        if spec.init == "ones":
+            t = 1.0 + t * 0.1
+        tensors[spec.name] = t
+    save_file(tensors, str(tmp_path / "model.safetensors"))
+    prompts = _prompts(n=3, length=10)
+    ec = EngineConfig(ModelConfig(parsed, dtype=torch.float32, enforce_eager=True, max_model_len=128,
+                                  checkpoint=str(tmp_path)), max_num_seqs=8)
+    ref = LLMEngine(ec, build_model(parsed, role="colocated", dtype=torch.float32, checkpoint=str(tmp_path),
+                                    max_positions=128)).generate(prompts, 5)
+    res = launch_local(LocalAFDSpec(preset=None, checkpoint=str(tmp_path), prompts=prompts, max_tokens=5,
+                                    afd={"num_attention_ranks": 2, "num_ffn_ranks": 1}))
+    assert not any("error" in v for v in res.values()), res
+    outs = []
+    for r in sorted(res):
+        outs += res[r].get("outputs", [])
+    assert outs == ref
