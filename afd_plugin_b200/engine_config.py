@@ -60,6 +60,8 @@ class CacheConfig:
     num_blocks: int | None = None
     # Fraction of free device memory the KV pool may take when num_blocks is None.
     memory_fraction: float = 0.5
+    # Reuse the KV blocks of a shared prompt prefix (full-attention models only).
+    enable_prefix_caching: bool = False
 
 
 @dataclass

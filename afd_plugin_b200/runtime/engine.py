@@ -33,7 +33,7 @@ import torch.distributed as dist
 from afd_plugin_b200.engine_config import EngineConfig
 from afd_plugin_b200.runtime.cuda_graph import pad_to_capture_size, validate_cuda_graph_mode
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor, LocalFFNExecutor
-from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache
+from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache, block_hashes
 from afd_plugin_b200.runtime.model_runner import ModelRunner
 from afd_plugin_b200.runtime.sampling import GREEDY, SamplingParams, make_generator, sample, token_logprobs
 
@@ -53,6 +53,7 @@ class Request:
     sampling: SamplingParams = GREEDY
     generator: torch.Generator | None = None  # the request's own noise stream (seeded requests)
     stop_ids: frozenset[int] = frozenset()  # EOS and stop tokens that end generation
+    cached_len: int = 0  # prompt tokens whose KV came from the prefix cache
     # with sampling.logprobs: per output token its logprob (None if another engine produced it)
     # and the top alternatives
     token_logprobs: list = field(default_factory=list)
@@ -123,6 +124,9 @@ class LLMEngine:
         self.runner = ModelRunner(model, self.kv, self.ffn, max_batch=self.max_batch,
                                   max_blocks_per_seq=self.max_blocks_per_seq, num_ubatches=num_ub)
         self.coordinator = coordinator or AttentionCoordinator()
+        # Prefix caching shares KV blocks between prompts; recurrent (Gated
+        # DeltaNet) state is per request, so hybrid models never share.
+        self.prefix_caching = bool(getattr(cc, "enable_prefix_caching", False)) and not self.runner.has_linear_state
         policy = validate_cuda_graph_mode(engine_config, role="attention")
         self.use_graphs = (policy.enabled and self.device.type == "cuda"
                            and getattr(self.ffn, "supports_graph_capture", True))
@@ -442,7 +446,10 @@ class LLMEngine:
         while self.waiting and len(self.running) + len(admit) < self.max_batch:
             admit.append(self.waiting.pop(0))
         is_prefill = bool(admit)
-        ntok = sum(len(r.prompt) for r in admit) if is_prefill else len(self.running)
+        if self.prefix_caching:
+            for r in admit:
+                self._reuse_prefix(r)
+        ntok = sum(len(r.prompt) - r.cached_len for r in admit) if is_prefill else len(self.running)
         topk = getattr(self.model.arch, "index_topk", 0)
         sparse = bool(topk) and any(r.num_tokens > topk for r in self.running)
         votes = self.coordinator.exchange(ntok, is_prefill, sparse=sparse)
@@ -462,14 +469,18 @@ class LLMEngine:
             for r in admit:
                 self._ensure_blocks(r, len(r.prompt) + 1)
                 r.state_slot = self._free_state_slots.pop()
-            admit_tokens = [r.prompt for r in admit]
+            admit_tokens = [r.prompt[r.cached_len :] for r in admit]
             tables = [r.blocks for r in admit]
-            starts = [0] * len(admit)
+            starts = [r.cached_len for r in admit]
             slots = [r.state_slot for r in admit]
         toks = self.runner.prefill(admit_tokens, tables, starts, slots,
                                    **self._across(votes, sum(len(t) for t in admit_tokens)))
         if admit:
             toks = self._sample(admit, toks)
+            if self.prefix_caching:
+                for r in admit:  # the prompt's full blocks now hold its KV
+                    for b, h in zip(r.blocks, block_hashes(r.prompt, self.block_size)):
+                        self.kv.allocator.register(b, h)
         toks = toks.cpu().tolist()
         out = {}
         for r, t in zip(admit, toks):
@@ -477,6 +488,21 @@ class LLMEngine:
             out[r.req_id] = int(t)
             (self._finish(r) if r.finished else self.running.append(r))
         return out
+
+    def _reuse_prefix(self, r: Request) -> None:
+        """Take the cached blocks of the longest shared prompt prefix (at least one token is computed)."""
+        if r.blocks or r.cached_len:
+            return
+        usable = (len(r.prompt) - 1) // self.block_size
+        if usable <= 0:
+            return
+        hit = self.kv.allocator.lookup(block_hashes(r.prompt[: usable * self.block_size], self.block_size))
+        r.blocks = hit
+        r.cached_len = len(hit) * self.block_size
+
+    def reset_prefix_cache(self) -> int:
+        """Forget the cached prompt prefixes; returns how many blocks were cached."""
+        return self.kv.allocator.reset_cache()
 
     def _across(self, votes, mine: int) -> dict:
         if len(votes) == 1:

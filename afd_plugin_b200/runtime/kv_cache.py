@@ -10,33 +10,112 @@ GLM-MoE-DSA); GQA layers cache K and V
 
 from __future__ import annotations
 
+from collections import OrderedDict
+
 import torch
 
 from afd_plugin_b200.models.configs import ModelArchConfig
 
 
 class BlockAllocator:
-    """LIFO free list of block ids (block 0 is kept as the padding block)."""
+    """Block ids with reference counts (block 0 is kept as the padding block).
+
+    With prefix caching, a full block of prompt tokens is registered under a
+    hash of its tokens and of every token before it.  When its last user
+    releases it, the block keeps its content on an LRU list; a later prompt
+    with the same prefix takes it back (:meth:`lookup`) instead of computing
+    it again, and allocation reuses such blocks only when no empty one is left.
+    """
 
     def __init__(self, num_blocks: int):
         if num_blocks < 2:
             raise ValueError("need at least two KV blocks")
         self.num_blocks = num_blocks
         self._free = list(range(num_blocks - 1, 0, -1))
+        self._ref = [0] * num_blocks
+        self._hash_of: dict[int, int] = {}  # block -> content hash
+        self._block_of: dict[int, int] = {}  # content hash -> block
+        self._evictable: OrderedDict[int, None] = OrderedDict()  # cached, unreferenced, oldest first
+        self.queries = 0
+        self.hits = 0
 
     @property
     def num_free(self) -> int:
-        return len(self._free)
+        return len(self._free) + len(self._evictable)
+
+    @property
+    def num_cached(self) -> int:
+        return len(self._hash_of)
+
+    def _forget(self, b: int) -> None:
+        h = self._hash_of.pop(b, None)
+        if h is not None and self._block_of.get(h) == b:
+            del self._block_of[h]
 
     def allocate(self, n: int) -> list[int]:
-        if n > len(self._free):
-            raise MemoryError(f"KV cache exhausted: want {n} blocks, {len(self._free)} free")
-        out = self._free[-n:][::-1] if n else []
-        del self._free[len(self._free) - n :]
+        if n > self.num_free:
+            raise MemoryError(f"KV cache exhausted: want {n} blocks, {self.num_free} free")
+        out = []
+        for _ in range(n):
+            if self._free:
+                b = self._free.pop()
+            else:  # evict the least recently released cached block
+                b, _ = self._evictable.popitem(last=False)
+                self._forget(b)
+            self._ref[b] = 1
+            out.append(b)
         return out
 
     def free(self, blocks: list[int]) -> None:
-        self._free.extend(reversed(blocks))
+        for b in reversed(blocks):
+            self._ref[b] -= 1
+            if self._ref[b] > 0:
+                continue
+            if b in self._hash_of:
+                self._evictable[b] = None
+            else:
+                self._free.append(b)
+
+    def lookup(self, hashes: list[int]) -> list[int]:
+        """Blocks of the longest cached prefix of ``hashes``, each taken (reference added)."""
+        out = []
+        for h in hashes:
+            self.queries += 1
+            b = self._block_of.get(h)
+            if b is None:
+                break
+            self.hits += 1
+            if self._ref[b] == 0:
+                self._evictable.pop(b, None)
+            self._ref[b] += 1
+            out.append(b)
+        return out
+
+    def register(self, block: int, h: int) -> None:
+        """Mark ``block`` as holding the full block of tokens with prefix hash ``h``."""
+        if h in self._block_of or block in self._hash_of:
+            return
+        self._hash_of[block] = h
+        self._block_of[h] = block
+
+    def reset_cache(self) -> int:
+        """Forget every cached prefix; returns how many blocks were registered."""
+        n = len(self._hash_of)
+        for b in list(self._evictable):
+            self._free.append(b)
+        self._evictable.clear()
+        self._hash_of.clear()
+        self._block_of.clear()
+        return n
+
+
+def block_hashes(tokens: list[int], block_size: int) -> list[int]:
+    """Chained hashes of the full blocks of ``tokens`` (each covers its block and all before it)."""
+    out, h = [], 0
+    for i in range(len(tokens) // block_size):
+        h = hash((h, tuple(tokens[i * block_size : (i + 1) * block_size])))
+        out.append(h)
+    return out
 
 
 PAD_BLOCK = 0
@@ -131,4 +210,4 @@ class KVCache:
             self.ssm_state.normal_(0.0, 0.02, generator=g)
 
 
-__all__ = ["BlockAllocator", "KVCache", "PAD_BLOCK"]
+__all__ = ["BlockAllocator", "KVCache", "PAD_BLOCK", "block_hashes"]

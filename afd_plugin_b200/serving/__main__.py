@@ -52,6 +52,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--dbo-decode-token-threshold", type=int, default=None)
     ap.add_argument("--dbo-prefill-token-threshold", type=int, default=None)
     ap.add_argument("--enable-expert-parallel", action="store_true")
+    ap.add_argument("--enable-prefix-caching", action="store_true",
+                    help="reuse the KV blocks of shared prompt prefixes (full-attention models)")
     ap.add_argument("--seed", type=int, default=0, help="random-init seed when no checkpoint is given")
     ap.add_argument("--decode-bench", action="store_true",
                     help="take every prompt as prefilled (random cache rows) and only decode: long-ISL decode "
@@ -89,7 +91,7 @@ def main(argv=None) -> None:
     import torch
     import uvicorn
 
-    from afd_plugin_b200.engine_config import CompilationConfig, EngineConfig, ModelConfig, ParallelConfig
+    from afd_plugin_b200.engine_config import CacheConfig, CompilationConfig, EngineConfig, ModelConfig, ParallelConfig
     from afd_plugin_b200.models.configs import get_preset
     from afd_plugin_b200.serving.api_server import EngineLoop, build_app
     from afd_plugin_b200.serving.tokenizer import load_tokenizer
@@ -109,6 +111,7 @@ def main(argv=None) -> None:
         ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=args.eager, max_model_len=args.max_model_len,
                                       checkpoint=args.checkpoint, seed=args.seed),
                           compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
+                          cache_config=CacheConfig(enable_prefix_caching=args.enable_prefix_caching),
                           max_num_seqs=args.max_num_seqs)
         engine = LLMEngine.colocated(ec, device="cuda" if torch.cuda.is_available() else "cpu")
         if not args.eager and engine.device.type == "cuda":
@@ -144,6 +147,7 @@ def main(argv=None) -> None:
                       parallel_config=ParallelConfig(data_parallel_size=A // args.tp, tensor_parallel_size=args.tp,
                                                      use_ubatching=args.dbo, num_ubatches=2 if args.dbo else 1),
                       compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
+                      cache_config=CacheConfig(enable_prefix_caching=args.enable_prefix_caching),
                       additional_config={"afd": dict(afd, role=role)}, max_num_seqs=args.max_num_seqs)
     if role == "ffn":
         w = AFDFFNWorker(ec, local_rank=local)

@@ -527,8 +527,10 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     @app.post("/reset_prefix_cache")
     def reset_prefix_cache():
-        # The engine caches no prompt prefixes across requests; nothing to reset.
-        return {"reset": False, "reason": "this engine keeps no prefix cache"}
+        if not getattr(loop.engine, "prefix_caching", False):
+            return {"reset": False, "reason": "prefix caching is off"}
+        n = loop.call(lambda eng: eng.reset_prefix_cache()).result(timeout=request_timeout_s)
+        return {"reset": True, "cached_blocks_dropped": n}
 
     @app.get("/health")
     def health():
@@ -545,6 +547,10 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         m = getattr(loop.engine, "metrics", None)
         if m is not None:
             out.update(m.summary())
+        alloc = loop.engine.kv.allocator
+        if getattr(loop.engine, "prefix_caching", False):
+            out["prefix_cache_hit_rate"] = round(alloc.hits / alloc.queries, 4) if alloc.queries else None
+        out["kv_blocks_free"] = alloc.num_free
         return out
 
     @app.post("/v1/completions")

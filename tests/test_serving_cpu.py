@@ -446,7 +446,7 @@ def test_proxy_instances_endpoints():
         assert bad.status_code == 400
         assert requests.get(purl + "/healthcheck", timeout=10).json()["backends"] == {b_url: True}
         assert requests.get(purl + "/v1/models", timeout=10).json()["data"][0]["object"] == "model"
-        assert requests.post(purl + "/reset_prefix_cache", timeout=10).json()[b_url]["reset"] is False
+        assert requests.post(purl + "/reset_prefix_cache", timeout=10).json()[b_url]["reset"] is False  # off
     finally:
         for s_ in (a, b, proxy):
             s_.should_exit = True
