@@ -72,6 +72,8 @@ class EngineConfig:
     cache_config: CacheConfig = field(default_factory=CacheConfig)
     additional_config: dict[str, Any] = field(default_factory=dict)
     max_num_seqs: int = 256
+    # Prompt tokens one prefill step may compute (chunked prefill); None = whole prompts.
+    max_num_batched_tokens: int | None = None
 
 
 __all__ = ["CacheConfig", "CompilationConfig", "EngineConfig", "ModelConfig", "ParallelConfig"]

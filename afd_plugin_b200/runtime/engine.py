@@ -138,6 +138,9 @@ class LLMEngine:
         # Prefill -> decode hand-off: finished requests whose cache rows are kept
         # for export, and imported requests waiting for a batch slot.
         self.held: dict[int, tuple[Request, float]] = {}
+        # chunked prefill: admitted requests part-way through their prompt
+        self.prefilling: list[Request] = []
+        self.max_batched_tokens = engine_config.max_num_batched_tokens
         self._kv_waiting: list[tuple[Request, object]] = []
         pin = self.device.type == "cuda"
         mk = lambda *s, dt: torch.zeros(*s, dtype=dt, pin_memory=pin)  # noqa: E731
@@ -235,7 +238,7 @@ class LLMEngine:
     def abort(self, req_id: int) -> bool:
         """End a waiting or running request now (client gone); it moves to ``finished`` with
         ``aborted`` set and the tokens it has.  Returns False if it is not live."""
-        for lst in (self.waiting, self.running):
+        for lst in (self.waiting, self.running, self.prefilling):
             for i, r in enumerate(lst):
                 if r.req_id == req_id:
                     del lst[i]
@@ -257,7 +260,7 @@ class LLMEngine:
         for r in self.running:
             if r.req_id == req_id:
                 return r
-        for r in self.waiting:
+        for r in self.waiting + self.prefilling:
             if r.req_id == req_id:
                 return r
         for r, _ in self._kv_waiting:
@@ -397,7 +400,7 @@ class LLMEngine:
         return n
 
     def has_unfinished(self) -> bool:
-        return bool(self.waiting or self.running or self._kv_waiting)
+        return bool(self.waiting or self.running or self._kv_waiting or self.prefilling)
 
     def _ensure_blocks(self, req: Request, upto_tokens: int) -> None:
         need = math.ceil(upto_tokens / self.block_size) - len(req.blocks)
@@ -440,50 +443,91 @@ class LLMEngine:
     def _step(self) -> dict[int, int]:
         if self._kv_waiting:
             self._admit_prefilled()
-            if not (self.waiting or self.running) and self.coordinator.size == 1:
+            if not (self.waiting or self.running or self.prefilling) and self.coordinator.size == 1:
                 return {}  # every imported request finished on its transferred token
-        admit = []
-        while self.waiting and len(self.running) + len(admit) < self.max_batch:
-            admit.append(self.waiting.pop(0))
-        is_prefill = bool(admit)
-        if self.prefix_caching:
-            for r in admit:
-                self._reuse_prefix(r)
-        ntok = sum(len(r.prompt) - r.cached_len for r in admit) if is_prefill else len(self.running)
+        plan = self._plan_prefill()
+        is_prefill = bool(plan)
+        ntok = sum(take for _, take in plan) if is_prefill else len(self.running)
         topk = getattr(self.model.arch, "index_topk", 0)
         sparse = bool(topk) and any(r.num_tokens > topk for r in self.running)
         votes = self.coordinator.exchange(ntok, is_prefill, sparse=sparse)
         if any(p for _, p in votes):
             self._last_phase = "prefill"
             with torch.profiler.record_function("afd_prefill_step"):
-                return self._prefill_step(admit, votes)
+                return self._prefill_step(plan, votes)
         self._last_phase = "decode"
         with torch.profiler.record_function("afd_decode_step"):
             return self._decode_step(votes)
 
-    def _prefill_step(self, admit: list[Request], votes) -> dict[int, int]:
+    def _plan_prefill(self) -> list[tuple[Request, int]]:
+        """(request, prompt tokens to compute this step) for the next prefill step, or [] for a decode step.
+
+        Requests part-way through their prompt (chunked prefill) continue
+        first, then waiting ones are admitted while batch slots and the
+        ``max_num_batched_tokens`` budget last.  With chunking, a step that
+        follows a prefill step decodes when requests are running, so long
+        prompts do not stall generation.
+        """
+        if not (self.prefilling or self.waiting):
+            return []
+        if self.max_batched_tokens is not None and self._last_phase == "prefill" and self.running:
+            return []
+        left = self.max_batched_tokens if self.max_batched_tokens is not None else float("inf")
+        work, self.prefilling = self.prefilling, []
+        while self.waiting and len(self.running) + len(work) < self.max_batch and left > sum(
+                len(r.prompt) - r.cached_len for r in work):
+            r = self.waiting.pop(0)
+            if self.prefix_caching:
+                self._reuse_prefix(r)
+            work.append(r)
+        plan = []
+        for r in work:
+            take = min(len(r.prompt) - r.cached_len, left)
+            if take <= 0:
+                self.prefilling.append(r)  # keeps its place (and any cached blocks) for the next step
+                continue
+            plan.append((r, int(take)))
+            left -= take
+        return plan
+
+    def _prefill_step(self, plan: list[tuple[Request, int]], votes) -> dict[int, int]:
+        admit = [r for r, _ in plan]
         if not admit:
             # Another Attention rank prefills: take part with one placeholder row.
             admit_tokens, tables, starts, slots = [[0]], [[PAD_BLOCK]], [0], None
         else:
             for r in admit:
                 self._ensure_blocks(r, len(r.prompt) + 1)
-                r.state_slot = self._free_state_slots.pop()
-            admit_tokens = [r.prompt[r.cached_len :] for r in admit]
+                if r.state_slot < 0:
+                    r.state_slot = self._free_state_slots.pop()
+            admit_tokens = [r.prompt[r.cached_len : r.cached_len + take] for r, take in plan]
             tables = [r.blocks for r in admit]
             starts = [r.cached_len for r in admit]
             slots = [r.state_slot for r in admit]
         toks = self.runner.prefill(admit_tokens, tables, starts, slots,
                                    **self._across(votes, sum(len(t) for t in admit_tokens)))
-        if admit:
-            toks = self._sample(admit, toks)
-            if self.prefix_caching:
-                for r in admit:  # the prompt's full blocks now hold its KV
-                    for b, h in zip(r.blocks, block_hashes(r.prompt, self.block_size)):
-                        self.kv.allocator.register(b, h)
-        toks = toks.cpu().tolist()
         out = {}
-        for r, t in zip(admit, toks):
+        if not admit:
+            return out
+        for r, take in plan:
+            r.cached_len += take
+        done = [i for i, r in enumerate(admit) if r.cached_len == len(r.prompt)]
+        for r in admit:
+            if r.cached_len < len(r.prompt):
+                self.prefilling.append(r)  # more chunks to come: no token yet
+        if not done:
+            return out
+        final = [admit[i] for i in done]
+        if len(done) < len(admit):
+            idx = torch.tensor(done, device=toks.device)
+            toks = toks.index_select(0, idx)
+            self.runner.last_logits = self.runner.last_logits.index_select(0, idx)
+        toks = self._sample(final, toks)
+        if self.prefix_caching:
+            for r in final:  # the prompt's full blocks now hold its KV
+                for b, h in zip(r.blocks, block_hashes(r.prompt, self.block_size)):
+                    self.kv.allocator.register(b, h)
+        for r, t in zip(final, toks.cpu().tolist()):
             r.output.append(int(t))
             out[r.req_id] = int(t)
             (self._finish(r) if r.finished else self.running.append(r))

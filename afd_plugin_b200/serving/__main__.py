@@ -43,6 +43,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--max-num-seqs", type=int, default=64)
     ap.add_argument("--max-model-len", type=int, default=4096)
+    ap.add_argument("--max-num-batched-tokens", type=int, default=None,
+                    help="prompt tokens per prefill step (chunked prefill; default: whole prompts)")
     ap.add_argument("--eager", "--enforce-eager", dest="eager", action="store_true")
     ap.add_argument("--capture-sizes", default="", help="comma-separated decode graph batch sizes "
                     "(default: --max-num-seqs)")
@@ -112,7 +114,7 @@ def main(argv=None) -> None:
                                       checkpoint=args.checkpoint, seed=args.seed),
                           compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
                           cache_config=CacheConfig(enable_prefix_caching=args.enable_prefix_caching),
-                          max_num_seqs=args.max_num_seqs)
+                          max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens)
         engine = LLMEngine.colocated(ec, device="cuda" if torch.cuda.is_available() else "cpu")
         if not args.eager and engine.device.type == "cuda":
             engine.capture_graphs()
@@ -148,7 +150,8 @@ def main(argv=None) -> None:
                                                      use_ubatching=args.dbo, num_ubatches=2 if args.dbo else 1),
                       compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
                       cache_config=CacheConfig(enable_prefix_caching=args.enable_prefix_caching),
-                      additional_config={"afd": dict(afd, role=role)}, max_num_seqs=args.max_num_seqs)
+                      additional_config={"afd": dict(afd, role=role)}, max_num_seqs=args.max_num_seqs,
+                      max_num_batched_tokens=args.max_num_batched_tokens)
     if role == "ffn":
         w = AFDFFNWorker(ec, local_rank=local)
         w.run_ffn_server_loop()
