@@ -1,18 +1,23 @@
-"""Standalone decode engine: requests, paged KV, greedy sampling, graphs.
+"""Standalone engine: requests, paged KV, sampling, graphs.
 
 Public API (what a user calls)::
 
     engine = LLMEngine.colocated(engine_config)          # or AFD roles via workers
     outputs = engine.generate(prompts, max_tokens=16)   # list[list[int]]
 
-    rid = engine.add_request(prompt_ids, max_tokens)
+    rid = engine.add_request(prompt_ids, max_tokens, sampling=SamplingParams(...))
     while engine.has_unfinished():
         engine.step()                                   # {req_id: token}
 
-A step is either a prefill of newly admitted requests or a decode of every
-running request.  Decode steps copy their inputs host->device from pinned
-buffers, replay the captured graph of the padded batch size (eager when
-none fits) and read the sampled tokens back.
+A step is either a prefill (whole prompts, or chunks of at most
+``max_num_batched_tokens``) or a decode of every running request.  Decode
+steps copy their inputs host->device from pinned buffers, replay the captured
+graph of the padded batch size (eager when none fits or a sparse-attention
+step needs selection), and read the tokens back; sampled requests draw from
+the step's logits (``runtime/sampling.py``).  Optional prefix caching shares
+the KV blocks of common prompt prefixes; ``hold_kv`` / ``export_kv`` /
+``add_prefilled_request`` hand a request's cache rows to another engine
+(``runtime/kv_transfer.py``); ``abort`` ends a request early.
 
 On AFD Attention ranks several engines (one per rank, data parallel) step in
 lockstep: a per-step exchange over the Attention group agrees on eager vs
