@@ -22,7 +22,7 @@ from typing import Any
 import torch
 import torch.distributed as dist
 
-from afd_plugin_b200.connectors.metadata import AFDControlPayload, AFDDPMetadata
+from afd_plugin_b200.connectors.metadata import AFDControlPayload
 from afd_plugin_b200.runtime.cuda_graph import (
     AFDGraphRunMode,
     graph_run_mode,

@@ -16,7 +16,7 @@ decode step -- both ubatches, all layers -- captures as ONE CUDA graph
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 

@@ -8,7 +8,7 @@ kernels (different bf16 rounding points), so it is held to near-agreement.
 import pytest
 import torch
 
-from afd_plugin_b200.engine_config import CompilationConfig, EngineConfig, ModelConfig
+from afd_plugin_b200.engine_config import EngineConfig, ModelConfig
 from afd_plugin_b200.models import build_model, get_preset
 from afd_plugin_b200.runtime.engine import LLMEngine
 from afd_plugin_b200.runtime.launcher import LocalAFDSpec, launch_local

@@ -72,8 +72,6 @@ def test_gpu_prefill_logits_track_fp32_reference():
             b.slot_mapping[i] = r.blocks[pos // e.block_size] * e.block_size + pos % e.block_size
             b.block_table[i, : len(r.blocks)] = torch.tensor(r.blocks, dtype=torch.int32)
             b.seq_lens[i] = pos + 1
-        from afd_plugin_b200.runtime.model_runner import ubatch_splits
-
         logits = e.runner.forward(b.input_ids[:3], e.runner._decode_metas(3, (0, 3)), (0, 3))
         res[dev] = (first.cpu(), logits.float().cpu())
     torch.testing.assert_close(res["cuda"][1], res["cpu"][1], atol=0.05, rtol=0.05)

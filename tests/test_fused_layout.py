@@ -1,7 +1,6 @@
 """Fused connector layout and options (CPU)."""
 
 import pytest
-import torch
 
 from afd_plugin_b200.connectors.b200_fused import B200FusedExtraInfo, FusedLayout
 

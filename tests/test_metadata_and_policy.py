@@ -3,7 +3,6 @@
 from types import SimpleNamespace
 
 import pytest
-import torch
 
 from afd_plugin_b200.connectors.metadata import (
     AFDControlPayload,
