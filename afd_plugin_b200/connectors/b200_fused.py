@@ -594,6 +594,9 @@ class FusedFFNRunner:
         n = 0
         try:
             while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
+                check = getattr(self, "health_check", None)
+                if check is not None:
+                    check()  # a peer stopped heartbeating: fail before waiting on it
                 payload = cp.recv_dp_metadata_list()
                 if payload.is_shutdown:
                     break

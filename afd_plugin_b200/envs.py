@@ -13,6 +13,8 @@ AFD_FORCE_BALANCED_TOPK_IDS = "AFD_FORCE_BALANCED_TOPK_IDS"
 AFD_B200_WAIT_TIMEOUT_MS = "AFD_B200_WAIT_TIMEOUT_MS"
 # Debug builds of the CUDA kernels check every index and record violations.
 AFD_B200_KERNEL_DEBUG = "AFD_B200_KERNEL_DEBUG"
+# Seconds without a peer heartbeat before a worker reports the peer dead (unset: no heartbeat).
+AFD_HEARTBEAT_TIMEOUT_S = "AFD_HEARTBEAT_TIMEOUT_S"
 ENV_TRUE_VALUES = frozenset({"1", "true", "yes", "on"})
 
 
@@ -46,3 +48,13 @@ __all__ = [
     "kernel_debug_enabled",
     "wait_timeout_ms",
 ]
+
+
+def heartbeat_timeout_s() -> float | None:
+    raw = os.environ.get(AFD_HEARTBEAT_TIMEOUT_S, "").strip()
+    if not raw:
+        return None
+    value = float(raw)
+    if value <= 0:
+        raise ValueError(f"{AFD_HEARTBEAT_TIMEOUT_S} must be positive, got {value}")
+    return value

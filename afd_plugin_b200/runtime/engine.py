@@ -143,6 +143,8 @@ class LLMEngine:
         # Prefill -> decode hand-off: finished requests whose cache rows are kept
         # for export, and imported requests waiting for a batch slot.
         self.held: dict[int, tuple[Request, float]] = {}
+        # called before every step (workers install the peer-heartbeat check)
+        self.health_check = None
         # chunked prefill: admitted requests part-way through their prompt
         self.prefilling: list[Request] = []
         self.max_batched_tokens = engine_config.max_num_batched_tokens
@@ -428,6 +430,8 @@ class LLMEngine:
 
     # ---------------------------------------------------------------- step
     def step(self) -> dict[int, int]:
+        if self.health_check is not None:
+            self.health_check()  # e.g. a peer stopped heartbeating: fail before waiting on it
         t0 = time.perf_counter()
         out = self._step()
         self.metrics.record(phase=self._last_phase, batch=len(out), tokens=len(out),

@@ -14,6 +14,8 @@ import threading
 import time
 from collections.abc import Callable
 
+_DONE = "done"
+
 
 class HeartbeatWatchdog:
     def __init__(self, store, rank: int, world_size: int, *, period_s: float = 0.2, timeout_s: float = 2.0,
@@ -42,9 +44,12 @@ class HeartbeatWatchdog:
             if r == self.rank or r in self._dead:
                 continue
             try:
-                stamp = float(self.store.get(self._key(r)).decode()) if self._has(r) else None
+                raw = self.store.get(self._key(r)).decode() if self._has(r) else None
             except Exception:  # noqa: BLE001 - store unreachable counts as stale
-                stamp = None
+                raw = None
+            if raw == _DONE:
+                continue  # the peer left cleanly
+            stamp = float(raw) if raw is not None else None
             stale = (stamp is None and now - self._start > self.timeout) or (
                 stamp is not None and now - stamp > self.timeout)
             if stale:
@@ -73,10 +78,16 @@ class HeartbeatWatchdog:
         self._thread.start()
         return self
 
-    def stop(self) -> None:
+    def stop(self, *, clean: bool = True) -> None:
+        """Stop beating; with ``clean`` the peers learn this rank left on purpose (no death report)."""
         self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=2 * self.period + 1)
+        if clean:
+            try:
+                self.store.set(self._key(self.rank), _DONE)
+            except Exception:  # noqa: BLE001 - the store may already be gone at exit
+                pass
 
     def dead_peers(self) -> set[int]:
         return set(self._dead)

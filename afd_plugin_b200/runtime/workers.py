@@ -94,6 +94,31 @@ class _WorkerBase:
         self.connector.init_afd_connector()
         self.tp_size = int(getattr(engine_config.parallel_config, "tensor_parallel_size", 1))
         self.groups = init_afd_groups(self.mapping, self.tp_size)
+        self.watchdog = self._start_watchdog()
+
+    def _start_watchdog(self):
+        """Peer heartbeats over the world's store when ``AFD_HEARTBEAT_TIMEOUT_S`` is set."""
+        from afd_plugin_b200.envs import heartbeat_timeout_s
+
+        timeout = heartbeat_timeout_s()
+        if timeout is None:
+            return None
+        from torch.distributed.distributed_c10d import _get_default_store
+
+        from afd_plugin_b200.runtime.watchdog import HeartbeatWatchdog
+
+        return HeartbeatWatchdog(_get_default_store(), self.world_rank, dist.get_world_size(),
+                                 period_s=min(0.5, timeout / 5), timeout_s=timeout, prefix="afd_hb").start()
+
+    def check_peers(self) -> None:
+        """Raise before launching work that would wait on a peer that stopped heartbeating."""
+        if self.watchdog is not None:
+            self.watchdog.raise_if_peer_dead()
+
+    def _stop_watchdog(self) -> None:
+        if self.watchdog is not None:
+            self.watchdog.stop()
+            self.watchdog = None
 
 
 class AFDAttentionWorker(_WorkerBase):
@@ -121,6 +146,8 @@ class AFDAttentionWorker(_WorkerBase):
         self.executor = executor
         coord = AttentionCoordinator(self.groups.attention_group, A, self.role_rank)
         self.engine = LLMEngine(engine_config, self.model, executor, coordinator=coord)
+        if self.watchdog is not None:
+            self.engine.health_check = self.check_peers
 
     def reload_weights(self, checkpoint: str | None = None, *, seed: int | None = None) -> None:
         """Reload the Attention-side weights in place from ``checkpoint`` (default: the configured source)."""
@@ -130,6 +157,7 @@ class AFDAttentionWorker(_WorkerBase):
 
     def shutdown(self) -> None:
         """Stop the FFN loops (control senders only) and release graphs."""
+        self._stop_watchdog()
         self.engine.runner.release_graphs()
         stop = getattr(self.executor, "shutdown_remote", None)
         if callable(stop):
@@ -155,6 +183,8 @@ class AFDFFNWorker(_WorkerBase):
         else:
             self.model_runner = FFNModelRunner(self.model, self.connector, engine_config,
                                                ep_group=self.groups.ffn_group, ep_size=F, ep_rank=self.role_rank)
+        if self.watchdog is not None:
+            self.model_runner.health_check = self.check_peers
         self._thread: threading.Thread | None = None
         self._stop: threading.Event | None = None
         self._error: BaseException | None = None
@@ -213,6 +243,7 @@ class AFDFFNWorker(_WorkerBase):
                                          seed=mc.seed if seed is None else seed)
 
     def shutdown(self) -> None:
+        self._stop_watchdog()
         self.stop_ffn_server_loop()
         release = getattr(self.model_runner, "release_graphs", None)
         if callable(release):

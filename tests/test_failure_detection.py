@@ -69,7 +69,7 @@ def _hb_rank(rank, world, path, q):
     wd = HeartbeatWatchdog(store, rank, world, period_s=0.05, timeout_s=0.5).start()
     if rank == 1:
         time.sleep(0.3)
-        wd.stop()  # rank 1 "dies": stops beating but keeps the process alive for the store
+        wd.stop(clean=False)  # rank 1 "dies": stops beating but keeps the process alive for the store
         time.sleep(3.0)
         q.put((rank, []))
         return
@@ -91,3 +91,42 @@ def test_heartbeat_watchdog_detects_silent_peer():
         p.join(30)
     got = dict(q.get(timeout=5) for _ in range(3))
     assert got[0] == [1] and got[2] == [1]
+
+
+def test_health_check_runs_before_every_step_on_both_roles():
+    """A peer that stopped heartbeating fails the next step on the host, before any wait on it."""
+    from types import SimpleNamespace
+
+    from afd_plugin_b200.engine_config import EngineConfig, ModelConfig
+    from afd_plugin_b200.models import build_model, get_preset
+    from afd_plugin_b200.runtime.engine import LLMEngine
+    from afd_plugin_b200.runtime.ffn_runner import FFNModelRunner
+
+    def dead():
+        raise RuntimeError("AFD peer rank(s) [0] stopped heartbeating")
+
+    arch = get_preset("tiny-dsv2")
+    eng = LLMEngine(EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=64),
+                                 max_num_seqs=2), build_model(arch, role="colocated", dtype=torch.float32))
+    eng.add_request([1, 2, 3], 2)
+    eng.health_check = dead
+    with pytest.raises(RuntimeError, match="stopped heartbeating"):
+        eng.step()
+    assert eng.waiting  # nothing ran
+
+    cp = SimpleNamespace(recv_dp_metadata_list=lambda: pytest.fail("must not wait for a payload"))
+    conn = SimpleNamespace(control_plane=cp, attn_size=1, ffn_size=1)
+    model = SimpleNamespace(device=torch.device("cpu"))
+    cfg = SimpleNamespace(model_config=SimpleNamespace(enforce_eager=True))
+    runner = FFNModelRunner(model, conn, cfg)
+    runner.health_check = dead
+    with pytest.raises(RuntimeError, match="stopped heartbeating"):
+        runner.serve(max_steps=1)
+
+
+def test_heartbeat_quiet_on_clean_runs(monkeypatch):
+    monkeypatch.setenv("AFD_HEARTBEAT_TIMEOUT_S", "1.0")
+    spec = LocalAFDSpec(afd={"num_attention_ranks": 2, "num_ffn_ranks": 1}, prompts=_prompts(n=4), max_tokens=6,
+                        timeout_s=30)
+    res = launch_local(spec, join_timeout_s=90)
+    assert not any("error" in v for v in res.values()), res
