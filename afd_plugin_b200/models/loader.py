@@ -4,7 +4,10 @@ A checkpoint is streamed once; each tensor is kept only when the process's
 AFD role needs it (:func:`afd_plugin_b200.models.model.weight_roles`, the same
 split as the reference's ``_iter_role_weights``) and, for expert tensors, when
 the expert lives on this expert-parallel shard.  fp8 block-scaled checkpoints
-(``weight`` + ``weight_scale_inv``) load without dequantisation.
+(``weight`` + ``weight_scale_inv``) load without dequantisation into the fp8
+expert and MLP weights; fp8 tensors of parameters kept in the model dtype
+(DeepSeek-V3's attention projections, for one) are dequantised with their
+block scales on the way in.
 """
 
 from __future__ import annotations
@@ -55,14 +58,23 @@ def load_weights(model: AFDCausalLM, weights: Iterable[tuple[str, torch.Tensor]]
     specs = {s.name: s for s in model.param_specs()}
     scale_of = {s.fp8_scale_name: s for s in specs.values() if s.fp8_scale_name}
     pending_scales: dict[str, torch.Tensor] = {}
+    # fp8 checkpoint tensors whose parameter is not kept in fp8 (attention projections,
+    # gates, ...): dequantised with their ``weight_scale_inv`` block scales once both are seen
+    fp8_plain: dict[str, torch.Tensor] = {}
+    plain_scales: dict[str, torch.Tensor] = {}
     loaded: set[str] = set()
     stream = iter_role_weights(
         weights, role=model.role, arch=model.arch, compute_gate_on_attention=model.compute_gate_on_attention,
         route_on_attention=getattr(model, "route_on_attention", False),
     )
+    block = tuple(model.arch.weight_block_size)
     for name, t in stream:
         if name in specs:
             spec = specs[name]
+            if t.dtype == torch.float8_e4m3fn and not spec.fp8_scale_name:
+                fp8_plain[name] = t
+                loaded.add(name)
+                continue
             if t.dtype == torch.float8_e4m3fn and spec.fp8_scale_name:
                 pending_scales.setdefault(spec.fp8_scale_name, None)  # type: ignore[arg-type]
             spec.setter(t)
@@ -70,6 +82,15 @@ def load_weights(model: AFDCausalLM, weights: Iterable[tuple[str, torch.Tensor]]
         elif name in scale_of:
             pending_scales[name] = t
             loaded.add(name)
+        elif name.endswith("_scale_inv") and name[: -len("_scale_inv")] in specs:
+            plain_scales[name[: -len("_scale_inv")]] = t
+    for name, t in fp8_plain.items():
+        scale = plain_scales.get(name)
+        if scale is None:
+            raise ValueError(f"fp8 checkpoint tensor {name} has no {name}_scale_inv")
+        from afd_plugin_b200.ops.reference import dequant_block
+
+        specs[name].setter(dequant_block(t, scale.float(), block))
     # Block scales of pre-quantised checkpoints go into the scale slices.
     for sname, st in pending_scales.items():
         if st is None:

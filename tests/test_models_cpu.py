@@ -197,3 +197,38 @@ def test_deepseek_v1_config_is_multi_head_attention():
     m = build_model(get_preset("tiny-dsv1"), role="attention", dtype=torch.float32, seed=0)
     names = {s.name for s in m.param_specs()}
     assert "model.layers.1.self_attn.k_proj.weight" in names and not any("q_norm" in n for n in names)
+
+
+def test_fp8_checkpoint_attention_weights_are_dequantised(tmp_path):
+    """DeepSeek-V3 fp8 checkpoints store attention projections as e4m3 + weight_scale_inv too."""
+    import zlib
+
+    from safetensors.torch import save_file
+
+    from afd_plugin_b200.ops.reference import dequant_block, quant_fp8_block_weight
+
+    arch = get_preset("tiny-dsv3").scaled(quant="fp8_block")
+    src = build_model(arch, role="colocated", dtype=torch.float32, seed=0)
+    tensors, want = {}, {}
+    for spec in src.param_specs():
+        g = torch.Generator().manual_seed(zlib.crc32(spec.name.encode()) & 0xFFFF)
+        w = torch.randn(spec.shape, generator=g) * 0.05
+        if len(spec.shape) == 2 and "self_attn" in spec.name and "norm" not in spec.name:
+            q, s = quant_fp8_block_weight(w)
+            tensors[spec.name], tensors[spec.name + "_scale_inv"] = q, s
+            want[spec.name] = dequant_block(q, s)
+        elif spec.fp8_scale_name:
+            q, s = quant_fp8_block_weight(w)
+            tensors[spec.name], tensors[spec.fp8_scale_name] = q, s
+        else:
+            tensors[spec.name] = w
+    save_file(tensors, str(tmp_path / "model.safetensors"))
+    m = build_model(arch, role="attention", dtype=torch.float32, checkpoint=str(tmp_path))
+    attn = m.layers[1].self_attn
+    q_a = want["model.layers.1.self_attn.q_a_proj.weight"]
+    assert torch.allclose(attn.in_proj[: q_a.shape[0]], q_a)
+    assert torch.allclose(attn.o_proj, want["model.layers.1.self_attn.o_proj.weight"])
+    del tensors["model.layers.1.self_attn.o_proj.weight_scale_inv"]
+    save_file(tensors, str(tmp_path / "model.safetensors"))
+    with pytest.raises(ValueError, match="weight_scale_inv"):
+        build_model(arch, role="attention", dtype=torch.float32, checkpoint=str(tmp_path))
