@@ -40,11 +40,30 @@ def iter_safetensors(path: str) -> Iterator[tuple[str, torch.Tensor]]:
                 yield name, fh.get_tensor(name)
 
 
+def checkpoint_name(name: str) -> str | None:
+    """The name a checkpoint tensor is loaded under, or None when no role loads it.
+
+    Multimodal Qwen3.5 / 3.6 checkpoints keep the text model under
+    ``model.language_model.``; their vision tower (``visual``) and
+    multi-token-prediction head (``mtp``) are not served (the reference's
+    Qwen3.5 wrapper gives those paths no role, ``qwen3_5.py:46-52``).
+    """
+    parts = name.split(".")
+    if "visual" in parts or "mtp" in parts:
+        return None
+    if name.startswith("model.language_model."):
+        return "model." + name[len("model.language_model."):]
+    return name
+
+
 def iter_role_weights(
     weights: Iterable[tuple[str, torch.Tensor]], *, role: str, arch: ModelArchConfig, compute_gate_on_attention: bool,
     route_on_attention: bool = False,
 ) -> Iterator[tuple[str, torch.Tensor]]:
-    for name, t in weights:
+    for raw, t in weights:
+        name = checkpoint_name(raw)
+        if name is None:
+            continue
         if role == "colocated" or role in weight_roles(name, arch, compute_gate_on_attention=compute_gate_on_attention,
                                                        route_on_attention=route_on_attention):
             yield name, t

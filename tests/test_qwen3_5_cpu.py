@@ -133,3 +133,13 @@ def test_from_hf_config_parses_hybrid_layout():
     assert a.layer_types[3] == "full_attention" and a.layer_types[0] == "linear_attention"
     assert a.full_attention_layers == (3, 7) and a.rotary_dim == 64 and a.shared_expert_gate
     assert a.linear_conv_dim == 2 * 16 * 128 + 32 * 128
+
+
+def test_multimodal_checkpoint_names_map_to_the_text_model():
+    from afd_plugin_b200.models.loader import checkpoint_name
+
+    assert checkpoint_name("model.language_model.layers.3.mlp.gate.weight") == "model.layers.3.mlp.gate.weight"
+    assert checkpoint_name("model.visual.blocks.0.attn.qkv.weight") is None
+    assert checkpoint_name("mtp.layers.0.mlp.gate.weight") is None
+    assert checkpoint_name("lm_head.weight") == "lm_head.weight"
+    assert checkpoint_name("model.embed_tokens.weight") == "model.embed_tokens.weight"
