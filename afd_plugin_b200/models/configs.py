@@ -185,6 +185,13 @@ class ModelArchConfig:
     # -------------------------------------------------------------- parsing
     @classmethod
     def from_hf_config(cls, hf: dict) -> "ModelArchConfig":
+        text = hf.get("text_config")
+        if isinstance(text, dict) and "hidden_size" not in hf:
+            # multimodal wrappers (Qwen3.5 / 3.6 ConditionalGeneration) keep the
+            # language model's fields under text_config
+            hf = {**text, "architectures": hf.get("architectures") or text.get("architectures"),
+                  "quantization_config": hf.get("quantization_config") or text.get("quantization_config"),
+                  "eos_token_id": hf.get("eos_token_id", text.get("eos_token_id"))}
         cfg = cls._parse_hf(hf)
         eos = hf.get("eos_token_id", (hf.get("text_config") or {}).get("eos_token_id"))
         ids = tuple(int(e) for e in (eos if isinstance(eos, (list, tuple)) else [eos]) if e is not None)

@@ -143,3 +143,16 @@ def test_multimodal_checkpoint_names_map_to_the_text_model():
     assert checkpoint_name("mtp.layers.0.mlp.gate.weight") is None
     assert checkpoint_name("lm_head.weight") == "lm_head.weight"
     assert checkpoint_name("model.embed_tokens.weight") == "model.embed_tokens.weight"
+
+
+def test_multimodal_config_reads_text_config():
+    text = {"model_type": "qwen3_5_moe_text", "hidden_size": 2048, "num_hidden_layers": 8, "vocab_size": 151936,
+            "num_attention_heads": 16, "num_key_value_heads": 2, "head_dim": 256, "num_experts": 256,
+            "num_experts_per_tok": 8, "moe_intermediate_size": 512, "shared_expert_intermediate_size": 512,
+            "linear_num_key_heads": 16, "linear_num_value_heads": 32, "linear_key_head_dim": 128,
+            "linear_value_head_dim": 128, "full_attention_interval": 4, "eos_token_id": 248044}
+    hf = {"architectures": ["Qwen3_5MoeForConditionalGeneration"], "model_type": "qwen3_5_moe",
+          "text_config": text, "vision_config": {"depth": 27}}
+    a = ModelArchConfig.from_hf_config(hf)
+    assert a.architecture == "Qwen3_5MoeForConditionalGeneration" and a.hidden_size == 2048
+    assert a.n_routed_experts == 256 and a.full_attention_layers == (3, 7) and a.eos_token_id == (248044,)
