@@ -43,8 +43,10 @@ def rope_cos_sin_cache(
 ) -> torch.Tensor:
     """``[max_positions, rotary_dim]`` fp32 table: first half cos, second half sin.
 
-    Supports plain RoPE and DeepSeek YaRN (``type == "yarn"``), whose frequency
-    ramp and magnitude correction follow the YaRN paper (Peng et al. 2023).
+    Supports plain RoPE, linear position interpolation (``type == "linear"``)
+    and YaRN (``type == "yarn"``), whose frequency ramp and magnitude
+    correction follow the YaRN paper (Peng et al. 2023); other scaling types
+    are refused rather than ignored.
     """
     half = rotary_dim // 2
     inv_freq = 1.0 / (base ** (torch.arange(0, rotary_dim, 2, dtype=torch.float64) / rotary_dim))
@@ -75,6 +77,10 @@ def rope_cos_sin_cache(
             return 1.0 if s <= 1 else 0.1 * mm * math.log(s) + 1.0
 
         mscale = get_m(factor, m) / get_m(factor, m_all) if m_all else get_m(factor, m)
+    elif kind == "linear":
+        inv_freq = inv_freq / float(rs["factor"])  # position interpolation
+    elif kind not in (None, "default"):
+        raise ValueError(f"unsupported rope_scaling type {kind!r}")
     t = torch.arange(max_positions, dtype=torch.float64)
     freqs = torch.outer(t, inv_freq)
     cache = torch.cat([freqs.cos() * mscale, freqs.sin() * mscale], dim=-1)

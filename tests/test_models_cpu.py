@@ -232,3 +232,15 @@ def test_fp8_checkpoint_attention_weights_are_dequantised(tmp_path):
     save_file(tensors, str(tmp_path / "model.safetensors"))
     with pytest.raises(ValueError, match="weight_scale_inv"):
         build_model(arch, role="attention", dtype=torch.float32, checkpoint=str(tmp_path))
+
+
+def test_rope_scaling_kinds():
+    from afd_plugin_b200.ops.reference import rope_cos_sin_cache
+
+    plain = rope_cos_sin_cache(8, 16, 10000.0)
+    lin = rope_cos_sin_cache(8, 16, 10000.0, {"type": "linear", "factor": 2.0})
+    # linear interpolation: position p with factor 2 rotates like position p / 2
+    assert torch.allclose(lin[6], plain[3], atol=1e-6)
+    assert torch.equal(rope_cos_sin_cache(8, 16, 10000.0, {"rope_type": "default"}), plain)
+    with pytest.raises(ValueError, match="unsupported rope_scaling"):
+        rope_cos_sin_cache(8, 16, 10000.0, {"type": "dynamic", "factor": 2.0})
