@@ -199,7 +199,10 @@ class AFDCausalLM(nn.Module):
             for i in range(arch.num_hidden_layers)
         )
         self.norm = RMSNorm(arch.hidden_size, arch.rms_norm_eps, dtype, device) if has_attn else None
-        self.lm_head = _param((arch.vocab_size, arch.hidden_size), dtype, device) if has_attn else None
+        if has_attn and arch.tie_word_embeddings:
+            self.lm_head = self.embed_tokens  # tied: the checkpoint carries no lm_head.weight
+        else:
+            self.lm_head = _param((arch.vocab_size, arch.hidden_size), dtype, device) if has_attn else None
         self.cos_sin = None
         if has_attn:
             rot = arch.rotary_dim
@@ -294,7 +297,8 @@ class AFDCausalLM(nn.Module):
         if self.embed_tokens is not None:
             yield ParamSpec("model.embed_tokens.weight", tuple(self.embed_tokens.shape), _copy(self.embed_tokens))
             yield ParamSpec("model.norm.weight", (a.hidden_size,), _copy(self.norm.weight), "ones")
-            yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
+            if not a.tie_word_embeddings:
+                yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
         for i, layer in enumerate(self.layers):
             p = f"model.layers.{i}."
             if layer.input_layernorm is not None:
@@ -638,7 +642,8 @@ class AFDDeepseekV4ForCausalLM(AFDDeepseekV2ForCausalLM):
         if self.embed_tokens is not None:
             yield ParamSpec("model.embed_tokens.weight", tuple(self.embed_tokens.shape), _copy(self.embed_tokens))
             yield ParamSpec("model.norm.weight", (H,), _copy(self.norm.weight), "ones")
-            yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
+            if not a.tie_word_embeddings:
+                yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
             yield ParamSpec("model.hc_head_fn", tuple(self.hc_head_fn.shape), _copy(self.hc_head_fn))
             yield ParamSpec("model.hc_head_base", tuple(self.hc_head_base.shape), _copy(self.hc_head_base), "zeros")
             yield ParamSpec("model.hc_head_scale", (1,), _copy(self.hc_head_scale), "ones")
@@ -720,7 +725,8 @@ class AFDQwen3_5MoeForCausalLM(AFDCausalLM):
         if self.embed_tokens is not None:
             yield ParamSpec("model.embed_tokens.weight", tuple(self.embed_tokens.shape), _copy(self.embed_tokens))
             yield ParamSpec("model.norm.weight", (H,), _copy_plus_one(self.norm.weight), "zeros")
-            yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
+            if not a.tie_word_embeddings:
+                yield ParamSpec("lm_head.weight", tuple(self.lm_head.shape), _copy(self.lm_head))
         for i, layer in enumerate(self.layers):
             p = f"model.layers.{i}."
             if layer.input_layernorm is not None:

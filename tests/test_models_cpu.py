@@ -244,3 +244,19 @@ def test_rope_scaling_kinds():
     assert torch.equal(rope_cos_sin_cache(8, 16, 10000.0, {"rope_type": "default"}), plain)
     with pytest.raises(ValueError, match="unsupported rope_scaling"):
         rope_cos_sin_cache(8, 16, 10000.0, {"type": "dynamic", "factor": 2.0})
+
+
+def test_tied_word_embeddings_share_the_table(tmp_path):
+    from safetensors.torch import save_file
+
+    arch = get_preset("tiny-qwen3-moe").scaled(tie_word_embeddings=True)
+    m = build_model(arch, role="colocated", dtype=torch.float32, seed=0)
+    assert m.lm_head is m.embed_tokens
+    names = [s.name for s in m.param_specs()]
+    assert "lm_head.weight" not in names
+    save_file({s.name: torch.randn(s.shape) * 0.02 for s in m.param_specs()}, str(tmp_path / "model.safetensors"))
+    loaded = build_model(arch, role="attention", dtype=torch.float32, checkpoint=str(tmp_path))
+    assert torch.equal(loaded.lm_head, loaded.embed_tokens)
+    eng_out = LLMEngine(EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=64),
+                                     max_num_seqs=2), m).generate([[1, 2, 3]], 3)
+    assert len(eng_out[0]) == 3
