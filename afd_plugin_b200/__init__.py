@@ -5,8 +5,12 @@ Entry points:
 * :func:`register_afd` -- the ``vllm.general_plugins`` hook (also callable
   standalone): registers the ``AFD<Arch>`` model aliases and validates the
   environment.
-* :class:`afd_plugin_b200.runtime.engine.LLMEngine` -- the standalone engine.
+* :class:`afd_plugin_b200.runtime.engine.LLMEngine` -- the standalone engine
+  (with :class:`~afd_plugin_b200.runtime.sampling.SamplingParams`).
 * :mod:`afd_plugin_b200.runtime.workers` -- Attention / FFN role workers.
+* ``python -m afd_plugin_b200.serving`` -- the completions server;
+  ``python -m afd_plugin_b200.serving.proxy`` -- the load-balancing and
+  prefill/decode proxy; ``python -m afd_plugin_b200.e2e.runner`` -- scenario runs.
 """
 
 from __future__ import annotations
@@ -26,6 +30,7 @@ _LAZY = {
     "FFNModelRunner": "afd_plugin_b200.runtime.ffn_runner",
     "AFDConfig": "afd_plugin_b200.config",
     "EngineConfig": "afd_plugin_b200.engine_config",
+    "SamplingParams": "afd_plugin_b200.runtime.sampling",
 }
 
 # HF architecture -> AFD alias (what ``register_afd`` publishes).
