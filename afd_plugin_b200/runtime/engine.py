@@ -64,9 +64,17 @@ class Request:
     token_logprobs: list = field(default_factory=list)
     top_logprobs: list = field(default_factory=list)
 
+    preemptions: int = 0  # times its blocks were taken back under cache pressure
+
     @property
     def num_tokens(self) -> int:
         return len(self.prompt) + len(self.output)
+
+    @property
+    def kv_tokens(self) -> list[int]:
+        """Tokens whose KV a prefill must produce before decoding (re)starts: the prompt, plus the
+        generated tokens but the last for a request resumed after preemption."""
+        return self.prompt + self.output[:-1] if self.output else self.prompt
 
     @property
     def stopped(self) -> bool:
@@ -145,6 +153,7 @@ class LLMEngine:
         self.held: dict[int, tuple[Request, float]] = {}
         # called before every step (workers install the peer-heartbeat check)
         self.health_check = None
+        self.num_preemptions = 0
         # chunked prefill: admitted requests part-way through their prompt
         self.prefilling: list[Request] = []
         self.max_batched_tokens = engine_config.max_num_batched_tokens
@@ -202,6 +211,8 @@ class LLMEngine:
         """
         if len(prompt) + max_tokens > self.config.model_config.max_model_len:
             raise ValueError("prompt + max_tokens exceeds max_model_len")
+        if math.ceil((len(prompt) + max_tokens) / self.block_size) > self.kv.allocator.num_blocks - 1:
+            raise ValueError("prompt + max_tokens needs more KV blocks than the cache holds")
         req = Request(next(self._ids), list(prompt), max_tokens, hold_kv=hold_kv)
         self._set_sampling(req, sampling)
         self.waiting.append(req)
@@ -454,6 +465,7 @@ class LLMEngine:
             self._admit_prefilled()
             if not (self.waiting or self.running or self.prefilling) and self.coordinator.size == 1:
                 return {}  # every imported request finished on its transferred token
+        self._reserve_decode_blocks()
         plan = self._plan_prefill()
         is_prefill = bool(plan)
         ntok = sum(take for _, take in plan) if is_prefill else len(self.running)
@@ -483,15 +495,23 @@ class LLMEngine:
             return []
         left = self.max_batched_tokens if self.max_batched_tokens is not None else float("inf")
         work, self.prefilling = self.prefilling, []
+        reserved = sum(self._blocks_short(r) for r in work)
         while self.waiting and len(self.running) + len(work) < self.max_batch and left > sum(
-                len(r.prompt) - r.cached_len for r in work):
-            r = self.waiting.pop(0)
+                len(r.kv_tokens) - r.cached_len for r in work):
+            r = self.waiting[0]
             if self.prefix_caching:
                 self._reuse_prefix(r)
-            work.append(r)
+            need = self._blocks_short(r)
+            if reserved + need > self.kv.allocator.num_free:
+                if r.cached_len:  # give the cached blocks back until it can be admitted
+                    self._release(r)
+                    r.cached_len = 0
+                break  # admission waits for blocks to free up
+            reserved += need
+            work.append(self.waiting.pop(0))
         plan = []
         for r in work:
-            take = min(len(r.prompt) - r.cached_len, left)
+            take = min(len(r.kv_tokens) - r.cached_len, left)
             if take <= 0:
                 self.prefilling.append(r)  # keeps its place (and any cached blocks) for the next step
                 continue
@@ -506,10 +526,10 @@ class LLMEngine:
             admit_tokens, tables, starts, slots = [[0]], [[PAD_BLOCK]], [0], None
         else:
             for r in admit:
-                self._ensure_blocks(r, len(r.prompt) + 1)
+                self._ensure_blocks(r, len(r.kv_tokens) + 1)
                 if r.state_slot < 0:
                     r.state_slot = self._free_state_slots.pop()
-            admit_tokens = [r.prompt[r.cached_len : r.cached_len + take] for r, take in plan]
+            admit_tokens = [r.kv_tokens[r.cached_len : r.cached_len + take] for r, take in plan]
             tables = [r.blocks for r in admit]
             starts = [r.cached_len for r in admit]
             slots = [r.state_slot for r in admit]
@@ -520,10 +540,14 @@ class LLMEngine:
             return out
         for r, take in plan:
             r.cached_len += take
-        done = [i for i, r in enumerate(admit) if r.cached_len == len(r.prompt)]
+        done = [i for i, r in enumerate(admit) if r.cached_len == len(r.kv_tokens)]
         for r in admit:
-            if r.cached_len < len(r.prompt):
+            if r.cached_len < len(r.kv_tokens):
                 self.prefilling.append(r)  # more chunks to come: no token yet
+        resumed = [i for i in done if admit[i].output]
+        for i in resumed:  # preempted earlier: its next token is known, decoding simply continues
+            self.running.append(admit[i])
+        done = [i for i in done if not admit[i].output]
         if not done:
             return out
         final = [admit[i] for i in done]
@@ -542,14 +566,46 @@ class LLMEngine:
             (self._finish(r) if r.finished else self.running.append(r))
         return out
 
+    def _blocks_short(self, r: Request) -> int:
+        """Blocks ``r`` still lacks to prefill its KV tokens and decode one position."""
+        return max(0, math.ceil((len(r.kv_tokens) + 1) / self.block_size) - len(r.blocks))
+
+    def _preempt(self, r: Request) -> None:
+        """Take back a running request's blocks; it is recomputed from its tokens when re-admitted."""
+        self._release(r)
+        r.cached_len = 0
+        r.preemptions += 1
+        self.num_preemptions += 1
+        self.waiting.insert(0, r)
+
+    def _reserve_decode_blocks(self) -> None:
+        """Give every running request a block for the position it decodes next; when the cache is
+        full, preempt the most recently admitted requests (before the step's token counts are agreed)."""
+        bs = self.block_size
+        i = 0
+        while i < len(self.running):
+            r = self.running[i]
+            need = (r.num_tokens - 1) // bs + 1 - len(r.blocks)
+            if need <= 0:
+                i += 1
+                continue
+            while self.kv.allocator.num_free < need and len(self.running) > i + 1:
+                self._preempt(self.running.pop())
+            if self.kv.allocator.num_free < need:
+                self._preempt(self.running.pop(i))
+                continue
+            r.blocks.extend(self.kv.allocator.allocate(need))
+            i += 1
+
     def _reuse_prefix(self, r: Request) -> None:
         """Take the cached blocks of the longest shared prompt prefix (at least one token is computed)."""
         if r.blocks or r.cached_len:
             return
-        usable = (len(r.prompt) - 1) // self.block_size
+        kv = r.kv_tokens
+        usable = (len(kv) - 1) // self.block_size
         if usable <= 0:
             return
-        hit = self.kv.allocator.lookup(block_hashes(r.prompt[: usable * self.block_size], self.block_size))
+        hit = self.kv.allocator.lookup(block_hashes(kv[: usable * self.block_size], self.block_size))
         r.blocks = hit
         r.cached_len = len(hit) * self.block_size
 

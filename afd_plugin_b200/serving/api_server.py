@@ -551,6 +551,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         if getattr(loop.engine, "prefix_caching", False):
             out["prefix_cache_hit_rate"] = round(alloc.hits / alloc.queries, 4) if alloc.queries else None
         out["kv_blocks_free"] = alloc.num_free
+        out["preemptions"] = getattr(loop.engine, "num_preemptions", 0)
         return out
 
     @app.post("/v1/completions")
