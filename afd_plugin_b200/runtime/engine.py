@@ -127,7 +127,7 @@ class LLMEngine:
         self.max_batch = engine_config.max_num_seqs
         self.max_blocks_per_seq = math.ceil(mc.max_model_len / self.block_size)
         if num_blocks is None:
-            num_blocks = cc.num_blocks or (self.max_batch * self.max_blocks_per_seq + 1)
+            num_blocks = cc.num_blocks or self._auto_num_blocks(model, cc)
         # One linear-attention state row per running request plus a padding row.
         self.kv = KVCache(getattr(model, "cache_arch", model.arch), num_blocks, self.block_size, model.dtype,
                           self.device, max_seqs=self.max_batch + 1)
@@ -188,6 +188,20 @@ class LLMEngine:
         self._sample_gen = make_generator(engine_config.model_config.seed, self.device)
 
     # ------------------------------------------------------------ helpers
+    def _auto_num_blocks(self, model, cc) -> int:
+        """Enough blocks for every sequence at full length, capped on a GPU by
+        ``memory_fraction`` of its free memory (requests are preempted when the
+        capped pool runs out)."""
+        worst = self.max_batch * self.max_blocks_per_seq + 1
+        if self.device.type != "cuda":
+            return worst
+        arch = getattr(model, "cache_arch", model.arch)
+        per_block = max(1, KVCache.bytes_per_block(arch, self.block_size, model.dtype))
+        free, _ = torch.cuda.mem_get_info(self.device)
+        state = KVCache.state_bytes_per_seq(arch, model.dtype) * (self.max_batch + 1)
+        fit = int((cc.memory_fraction * free - state) // per_block)
+        return max(2, min(worst, fit))
+
     @classmethod
     def colocated(cls, engine_config: EngineConfig, *, device="cuda", seed: int | None = None) -> "LLMEngine":
         from afd_plugin_b200.models import build_model
