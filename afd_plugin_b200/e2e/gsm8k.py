@@ -76,8 +76,8 @@ def evaluate(url: str, data: list[dict], shots: list[dict], *, limit: int | None
     endpoint = url.rstrip("/") + "/v1/completions"
 
     def one(item):
-        r = requests.post(endpoint, json={"prompt": build_prompt(shots, item["question"]), "max_tokens": max_tokens},
-                          timeout=timeout_s)
+        r = requests.post(endpoint, json={"prompt": build_prompt(shots, item["question"]), "max_tokens": max_tokens,
+                                          "stop": ["Question:"]}, timeout=timeout_s)
         r.raise_for_status()
         return _truncate(r.json()["choices"][0]["text"])
 

@@ -59,6 +59,12 @@ class SamplingFields(BaseModel):
     logprobs: int | bool | None = None
     top_logprobs: int | None = None
     n: int = 1
+    stop: str | list[str] | None = None  # text stop sequences (checked on the decoded text)
+
+    def stop_strings(self) -> list[str]:
+        if self.stop is None:
+            return []
+        return [self.stop] if isinstance(self.stop, str) else [x for x in self.stop if x]
 
     def n_logprobs(self) -> int | None:
         if self.logprobs is None or self.logprobs is False:
@@ -129,6 +135,11 @@ class _Pending:
     req: object | None = None  # the engine's Request, for streaming
     sent: int = 0
     sampling: SamplingParams | None = None
+    # text stop sequences: decoded text so far and the text cut before the stop
+    stop_strings: list[str] = field(default_factory=list)
+    text: str = ""
+    checked: int = 0
+    stop_text: str | None = None
 
 
 class EngineLoop:
@@ -146,6 +157,7 @@ class EngineLoop:
                  kv_hold_timeout_s: float = 120.0, tp_group=None, tp_size: int = 1, tp_src: int = 0,
                  decode_bench: bool = False):
         self.engine = engine
+        self.tokenizer = None  # set by build_app: decodes text for stop sequences
         # decode-bench serving: prompts are taken as prefilled (no prefill step)
         self.decode_bench = decode_bench
         self.group, self.world, self.rank = group, world, rank
@@ -173,7 +185,8 @@ class EngineLoop:
             raise ValueError("prefill/decode KV hand-off is not supported with attention tensor parallelism")
 
     def submit(self, prompt: list[int], max_tokens: int, *, hold_kv: bool = False,
-               stream: queue.Queue | None = None, sampling: SamplingParams | None = None) -> Future:
+               stream: queue.Queue | None = None, sampling: SamplingParams | None = None,
+               stop: list[str] | None = None) -> Future:
         """Queue a request; the future resolves with its tokens and carries ``req_id`` once admitted.
 
         With ``stream`` every token is also put on that queue as soon as it is
@@ -186,18 +199,19 @@ class EngineLoop:
         fut: Future = Future()
         with self._lock:
             self._queue.append(_Pending(list(prompt), int(max_tokens), fut, hold_kv=hold_kv, stream=stream,
-                                        sampling=sampling))
+                                        sampling=sampling, stop_strings=list(stop or [])))
             self.stats["requests"] += 1
         return fut
 
     def submit_prefilled(self, prompt: list[int], kv_blob: bytes, max_tokens: int, *,
-                         stream: queue.Queue | None = None, sampling: SamplingParams | None = None) -> Future:
+                         stream: queue.Queue | None = None, sampling: SamplingParams | None = None,
+                         stop: list[str] | None = None) -> Future:
         """Queue a request whose prompt was prefilled by another engine (see ``export_kv``)."""
         self._check_entry(True)
         fut: Future = Future()
         with self._lock:
             self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob, stream=stream,
-                                        sampling=sampling))
+                                        sampling=sampling, stop_strings=list(stop or [])))
             self.stats["requests"] += 1
         return fut
 
@@ -237,6 +251,21 @@ class EngineLoop:
             self._thread.join(timeout)
             if not self._thread.is_alive():
                 self._thread = None
+
+    def _hit_stop(self, p: _Pending) -> bool:
+        """Decode the request's new tokens; True (and the text cut before it) once a stop string shows."""
+        tok = self.tokenizer
+        if tok is None or p.req is None:
+            return False
+        first = 1 if getattr(p.req, "synthetic_prefill", False) else 0
+        ids = p.req.output[first:]
+        p.text = tok.decode(ids)
+        p.checked = len(ids)
+        cut = min((i for i in (p.text.find(st) for st in p.stop_strings) if i >= 0), default=-1)
+        if cut < 0:
+            return False
+        p.stop_text = p.text[:cut]
+        return True
 
     @staticmethod
     def _push_tokens(p: _Pending) -> None:
@@ -298,8 +327,9 @@ class EngineLoop:
                         continue
                     p.future.req_id = rid
                     self._inflight[rid] = p
-                    if p.stream is not None:
+                    if p.stream is not None or p.stop_strings:
                         p.req = eng.request(rid)
+                    if p.stream is not None:
                         self._push_tokens(p)  # a transferred first token streams at once
                 work, stop = self._agree(eng.has_unfinished(), self._stop.is_set())
                 if stop:
@@ -318,6 +348,9 @@ class EngineLoop:
                         p.first_token_at = now
                         self.stats["ttft_s_sum"] += now - p.submitted
                         self.stats["ttft_count"] += 1
+                    if p.stop_strings and self._hit_stop(p):
+                        eng.abort(rid)  # ends it now; resolved below with finish_reason "stop"
+                        continue
                     if p.stream is not None:
                         self._push_tokens(p)
                 self._resolve_finished(now)
@@ -330,12 +363,15 @@ class EngineLoop:
             p = self._inflight.pop(rid)
             req = eng.finished.pop(rid)
             out = req.output[1:] if req.synthetic_prefill else req.output
-            self.stats["aborted" if req.aborted else "completed"] += 1
+            stopped = p.stop_text is not None
+            self.stats["aborted" if req.aborted and not stopped else "completed"] += 1
             self.stats["generated_tokens"] += len(out)
             if p.first_token_at is not None and len(out) > 1 and not req.aborted:
                 self.stats["tpot_s_sum"] += (now - p.first_token_at) / (len(out) - 1)
                 self.stats["tpot_count"] += 1
-            p.future.finish_reason = req.finish_reason
+            p.future.finish_reason = "stop" if p.stop_text is not None else req.finish_reason
+            if p.stop_text is not None:
+                p.future.text = p.stop_text
             skip = 1 if req.synthetic_prefill else 0
             p.future.logprobs = (req.token_logprobs[skip:], req.top_logprobs[skip:])
             if p.stream is not None:
@@ -368,6 +404,8 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     vocab = loop.engine.model.arch.vocab_size
     tok = tokenizer or ByteTokenizer(vocab)
+    if loop.tokenizer is None:
+        loop.tokenizer = tok
     app = FastAPI(title="afd_plugin_b200")
 
     def _fetch_kv(params: dict) -> bytes:
@@ -469,11 +507,12 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             raise HTTPException(status_code=400, detail="n > 1 is served without streaming or KV hand-off")
         stream = queue.Queue() if stream_req and not prefill_only else None
         try:
+            stops = fields.stop_strings()
             if params.get("do_remote_prefill"):
                 futs = [loop.submit_prefilled(ids, _fetch_kv(params), max_tokens, stream=stream,
-                                              sampling=samplings[0])]
+                                              sampling=samplings[0], stop=stops)]
             else:
-                futs = [loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream, sampling=sp)
+                futs = [loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream, sampling=sp, stop=stops)
                         for sp in samplings]
             if stream is not None:
                 return StreamingResponse(_sse(stream, futs[0], len(ids), model, chat),
@@ -488,11 +527,13 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         choices = []
         for i, (f, out) in enumerate(zip(futs, outs)):
             reason = getattr(f, "finish_reason", "length")
+            text = getattr(f, "text", None)
+            text = tok.decode(out) if text is None else text
             if chat:
-                c = {"index": i, "message": {"role": "assistant", "content": tok.decode(out)}, "token_ids": out,
+                c = {"index": i, "message": {"role": "assistant", "content": text}, "token_ids": out,
                      "finish_reason": reason}
             else:
-                c = {"index": i, "token_ids": out, "text": tok.decode(out), "finish_reason": reason}
+                c = {"index": i, "token_ids": out, "text": text, "finish_reason": reason}
             if samplings[i] is not None and samplings[i].logprobs is not None:
                 c["logprobs"] = _logprobs_block(chat, out, getattr(f, "logprobs", ([], [])))
             choices.append(c)

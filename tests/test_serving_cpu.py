@@ -563,3 +563,20 @@ def test_server_cli_accepts_reference_recipe_flags():
         parse_args(["--compilation-config", '{"cudagraph_mode": "PIECEWISE"}'])
     with pytest.raises(SystemExit):
         parse_args(["--afd", "{}", "--additional-config", '{"afd": {}}'])
+
+
+def test_text_stop_sequences(server):
+    url, loop = server
+    prompt = [5, 9, 100, 7, 3, 1]
+    full = _engine().generate([prompt], 12)[0]
+    text = byte_detokenize(full)
+    stop = text[4:6]
+    cut = text.find(stop)
+    r = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 12, "stop": [stop, "\x00zz"]},
+                      timeout=60).json()
+    c = r["choices"][0]
+    assert c["finish_reason"] == "stop" and c["text"] == text[:cut]
+    assert c["token_ids"] == full[: len(c["token_ids"])] and len(c["token_ids"]) < 12
+    plain = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 12, "stop": "\x00zz"},
+                          timeout=60).json()["choices"][0]
+    assert plain["finish_reason"] == "length" and plain["token_ids"] == full
