@@ -595,6 +595,23 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         out["preemptions"] = getattr(loop.engine, "num_preemptions", 0)
         return out
 
+    @app.get("/metrics/prometheus")
+    def metrics_prometheus():
+        """The /metrics counters and gauges in the Prometheus text exposition format."""
+        from fastapi.responses import PlainTextResponse
+
+        m = metrics()
+        kinds = {"requests": "counter", "completed": "counter", "aborted": "counter", "generated_tokens": "counter",
+                 "steps": "counter", "preemptions": "counter", "decode_tokens": "counter"}
+        lines = []
+        for key, value in sorted(m.items()):
+            if not isinstance(value, (int, float)) or isinstance(value, bool):
+                continue
+            name = "afd_" + key + ("_total" if kinds.get(key) == "counter" else "")
+            lines.append(f"# TYPE {name} {kinds.get(key, 'gauge')}")
+            lines.append(f'{name}{{model="{model_name}"}} {float(value)}')
+        return PlainTextResponse("\n".join(lines) + "\n", media_type="text/plain; version=0.0.4")
+
     @app.post("/v1/completions")
     def completions(req: CompletionRequest):
         ids = req.prompt if isinstance(req.prompt, list) else tok.encode(req.prompt)

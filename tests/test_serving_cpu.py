@@ -56,6 +56,9 @@ def test_completions_match_engine_generate(server):
     assert resp[0]["usage"] == {"prompt_tokens": 6, "completion_tokens": 6, "total_tokens": 12}
     m = requests.get(url + "/metrics", timeout=5).json()
     assert m["completed"] == 4 and m["generated_tokens"] == 24
+    prom = requests.get(url + "/metrics/prometheus", timeout=5)
+    assert prom.status_code == 200 and 'afd_completed_total{model="afd-b200"} 4.0' in prom.text
+    assert "# TYPE afd_generated_tokens_total counter" in prom.text
     models = requests.get(url + "/v1/models", timeout=5).json()
     assert models["data"][0]["id"] == "afd-b200" and models["data"][0]["max_model_len"] == 96
     assert m["ttft_count"] == 4 and m["tpot_count"] == 4
