@@ -620,8 +620,10 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     @app.post("/v1/chat/completions")
     def chat_completions(req: ChatCompletionRequest):
-        max_tokens = req.max_completion_tokens or req.max_tokens or 16
         ids = tok.encode_chat([{"role": m.role, "content": m.content} for m in req.messages])
+        # no limit given: the rest of the context (the chat API has no default cap)
+        max_tokens = req.max_completion_tokens or req.max_tokens or max(
+            1, loop.engine.config.model_config.max_model_len - len(ids))
         return _generate(ids, max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, True, req)
 
     return app
