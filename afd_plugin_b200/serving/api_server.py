@@ -193,6 +193,8 @@ class EngineLoop:
         produced, followed by None (or the exception that ended the request).
         """
         self._check_entry(hold_kv)
+        if stop and self.tp_size > 1:  # ending a request early would need the TP peers to end it too
+            raise ValueError("text stop sequences are not supported with attention tensor parallelism")
         limit = self.engine.config.model_config.max_model_len
         if len(prompt) + int(max_tokens) > limit:
             raise ValueError(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds max_model_len {limit}")
@@ -208,6 +210,8 @@ class EngineLoop:
                          stop: list[str] | None = None) -> Future:
         """Queue a request whose prompt was prefilled by another engine (see ``export_kv``)."""
         self._check_entry(True)
+        if stop and self.tp_size > 1:
+            raise ValueError("text stop sequences are not supported with attention tensor parallelism")
         fut: Future = Future()
         with self._lock:
             self._queue.append(_Pending(list(prompt), int(max_tokens), fut, kv_blob=kv_blob, stream=stream,
