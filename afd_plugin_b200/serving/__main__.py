@@ -4,10 +4,20 @@ Colocated (one process):
     python -m afd_plugin_b200.serving --preset tiny-dsv2 --port 8000
 
 AFD (one process per GPU; Attention rank 0 serves HTTP; ``--tp`` shards the
-attention heads over consecutive Attention ranks):
+attention heads over consecutive Attention ranks), either as one torchrun
+world of A + F ranks:
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m afd_plugin_b200.serving \\
         --preset deepseek-v2-lite --afd '{"num_attention_ranks": 1, "num_ffn_ranks": 1,
                                           "connector": "B200FusedAFDConnector"}'
+
+or one launch per role, the way the reference deploys two ``vllm serve``
+instances: each launch gives its ``role`` and the AFD world's ``host`` /
+``port``, and its ranks join that world (FFN ranks first)::
+
+    torchrun --nproc-per-node 2 -m afd_plugin_b200.serving --afd \\
+        '{"role": "ffn", "num_attention_ranks": 6, "num_ffn_ranks": 2, "host": "10.0.0.1", "port": 1239}'
+    torchrun --nproc-per-node 6 -m afd_plugin_b200.serving --port 8000 --afd \\
+        '{"role": "attention", "num_attention_ranks": 6, "num_ffn_ranks": 2, "host": "10.0.0.1", "port": 1239}'
 """
 
 from __future__ import annotations
@@ -132,13 +142,25 @@ def main(argv=None) -> None:
     from afd_plugin_b200.parallel.topology import role_of_world_rank
     from afd_plugin_b200.runtime.workers import AFDAttentionWorker, AFDFFNWorker
 
+    from afd_plugin_b200.config import afd_config_from_mapping
+    from afd_plugin_b200.parallel.process_group import init_afd_world
+
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     backend = "nccl" if torch.cuda.is_available() else "gloo"
     if backend == "nccl":
         torch.cuda.set_device(local)
-    dist.init_process_group(backend=backend)
     A, F = int(afd["num_attention_ranks"]), int(afd["num_ffn_ranks"])
+    given_role = afd.get("role", afd.get("afd_role"))
+    if given_role in ("attention", "ffn") and world == (A if given_role == "attention" else F):
+        # One role per launch, as the reference deploys (an Attention server and an FFN
+        # server): this launch's ranks join the AFD world over tcp://host:port, FFN ranks first.
+        cfg = afd_config_from_mapping(afd)
+        rank = rank + (F if given_role == "attention" else 0)
+        init_afd_world(backend=backend, host=cfg.host, port=cfg.port, world_size=A + F, rank=rank)
+        world = A + F
+    else:
+        dist.init_process_group(backend=backend)
     if world != A + F:
         raise SystemExit(f"world size {world} != num_attention_ranks + num_ffn_ranks = {A + F}")
     if args.tp < 1 or A % args.tp:

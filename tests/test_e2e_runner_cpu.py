@@ -195,3 +195,44 @@ def test_gsm8k_against_a_fake_server(tmp_path):
         assert rc == 0 and res["gate"] == "pass"
     finally:
         srv.should_exit = True
+
+
+def test_roles_launched_separately_join_one_afd_world(tmp_path):
+    """An FFN server and an Attention server started on their own (the reference's deployment) form one world."""
+    import os
+
+    import requests
+
+    from afd_plugin_b200.runtime.launcher import free_port
+
+    afd_port, http = free_port(), free_port()
+    base = {"num_attention_ranks": 1, "num_ffn_ranks": 1, "host": "127.0.0.1", "port": afd_port}
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, RANK="0", WORLD_SIZE="1", LOCAL_RANK="0", CUDA_VISIBLE_DEVICES="",
+               PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    common = [sys.executable, "-m", "afd_plugin_b200.serving", "--preset", "tiny-dsv2", "--dtype", "float32",
+              "--eager", "--max-model-len", "128", "--max-num-seqs", "4"]
+    ffn = start_server(common + ["--port", str(free_port()), "--afd", json.dumps(dict(base, role="ffn"))],
+                       env=env, log_path=str(tmp_path / "ffn.log"))
+    attn = start_server(common + ["--port", str(http), "--afd", json.dumps(dict(base, role="attention"))],
+                        env=env, log_path=str(tmp_path / "attn.log"))
+    try:
+        url = f"http://127.0.0.1:{http}"
+        wait_for_health(attn, url, timeout_s=240)
+        prompts = runner.make_prompts(3, 1024, seed=2, min_len=6, max_len=12)
+        got = runner.send_requests(url, prompts, 4, concurrency=3)
+        import torch
+
+        from afd_plugin_b200.engine_config import EngineConfig, ModelConfig
+        from afd_plugin_b200.models import build_model, get_preset
+        from afd_plugin_b200.runtime.engine import LLMEngine
+
+        arch = get_preset("tiny-dsv2")
+        eng = LLMEngine(EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=128),
+                                     max_num_seqs=4),
+                        build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=128))
+        assert got == eng.generate(prompts, 4)
+        assert requests.get(url + "/health", timeout=5).status_code == 200
+    finally:
+        stop_server(attn)
+        stop_server(ffn)
