@@ -713,8 +713,10 @@ class LLMEngine:
         self.running = still
         return out
 
-    def generate(self, prompts: list[list[int]], max_tokens: int) -> list[list[int]]:
-        ids = [self.add_request(p, max_tokens) for p in prompts]
+    def generate(self, prompts: list[list[int]], max_tokens: int,
+                 sampling: SamplingParams | None = None) -> list[list[int]]:
+        """Run the prompts to completion; returns each one's generated tokens."""
+        ids = [self.add_request(p, max_tokens, sampling=sampling) for p in prompts]
         while self.has_unfinished():
             self.step()
         return [self.finished[i].output for i in ids]
