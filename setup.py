@@ -36,5 +36,6 @@ setup(
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
-    entry_points={"vllm.general_plugins": ["afd = afd_plugin_b200:register_afd"]},
+    entry_points={"vllm.general_plugins": ["afd = afd_plugin_b200:register_afd"],
+                  "console_scripts": ["afd-b200 = afd_plugin_b200.__main__:main"]},
 )

@@ -123,3 +123,16 @@ def test_graft_entry_exposes_build_and_smoke():
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     assert callable(mod.build) and callable(mod.smoke)
+
+
+def test_umbrella_cli_dispatches(capsys):
+    from afd_plugin_b200.__main__ import COMMANDS, main
+
+    assert main(["--help"]) == 0 and "serve" in capsys.readouterr().out
+    assert main(["nope"]) == 2
+    for module, fn in COMMANDS.values():
+        assert callable(getattr(importlib.import_module(module), fn))
+    with pytest.raises(SystemExit) as e:
+        main(["serve", "--help"])
+    assert e.value.code == 0
+    assert "console_scripts" in (ROOT / "setup.py").read_text()
