@@ -193,15 +193,25 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--max-tokens", type=int, default=16)
     ap.add_argument("--backend", default="gloo")
     ap.add_argument("--dtype", default="float32")
+    ap.add_argument("--checkpoint", default=None, help="HF checkpoint directory (else --preset, random init)")
+    ap.add_argument("--tp", type=int, default=1, help="attention tensor parallelism")
+    ap.add_argument("--dbo", action="store_true", help="two-ubatch overlap")
+    ap.add_argument("--graphs", action="store_true", help="capture decode CUDA graphs (nccl backend)")
     args = ap.parse_args(argv)
     afd = json.loads(args.additional_config)["afd"]
     from afd_plugin_b200.models.configs import get_preset
 
-    vocab = get_preset(args.preset).vocab_size
+    if args.checkpoint:
+        from afd_plugin_b200.models.loader import read_hf_config
+
+        vocab = read_hf_config(args.checkpoint).vocab_size
+    else:
+        vocab = get_preset(args.preset).vocab_size
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, vocab, (args.num_prompts, args.prompt_len), generator=g).tolist()
     spec = LocalAFDSpec(preset=args.preset, afd=afd, prompts=prompts, max_tokens=args.max_tokens,
-                        backend=args.backend, dtype=args.dtype)
+                        backend=args.backend, dtype=args.dtype, checkpoint=args.checkpoint, tp=args.tp,
+                        use_ubatching=args.dbo, enforce_eager=not args.graphs)
     res = launch_local(spec)
     print(json.dumps({str(k): v for k, v in sorted(res.items())}))
     return 0 if all("error" not in v for v in res.values()) else 1
