@@ -87,7 +87,8 @@ class SamplingFields(BaseModel):
 
 
 class CompletionRequest(SamplingFields):
-    prompt: str | list[int]
+    # one prompt (text or token ids) or a batch of them
+    prompt: str | list[int] | list[str] | list[list[int]]
     max_tokens: int = 16
     model: str | None = None
     kv_transfer_params: dict | None = None
@@ -618,9 +619,28 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     @app.post("/v1/completions")
     def completions(req: CompletionRequest):
-        ids = req.prompt if isinstance(req.prompt, list) else tok.encode(req.prompt)
-        return _generate(ids, req.max_tokens, req.kv_transfer_params, req.stream, req.model or model_name, False,
-                         req)
+        p = req.prompt
+        batch = isinstance(p, list) and bool(p) and all(isinstance(x, (str, list)) for x in p)
+        if not batch:
+            ids = p if isinstance(p, list) else tok.encode(p)
+            return _generate(ids, req.max_tokens, req.kv_transfer_params, req.stream, req.model or model_name,
+                             False, req)
+        if req.stream or req.kv_transfer_params:
+            raise HTTPException(status_code=400, detail="a batch of prompts is served without streaming or KV hand-off")
+        # a batch: the prompts run concurrently; choice i*n + j is prompt i's j-th completion
+        from concurrent.futures import ThreadPoolExecutor
+
+        all_ids = [x if isinstance(x, list) else tok.encode(x) for x in p]
+        with ThreadPoolExecutor(min(16, len(all_ids))) as ex:
+            bodies = list(ex.map(lambda ids: _generate(ids, req.max_tokens, None, False, req.model or model_name,
+                                                       False, req), all_ids))
+        choices, usage = [], {"prompt_tokens": 0, "completion_tokens": 0, "total_tokens": 0}
+        for body in bodies:
+            for c in body["choices"]:
+                choices.append(dict(c, index=len(choices)))
+            for k in usage:
+                usage[k] += body["usage"][k]
+        return {"object": "text_completion", "model": req.model or model_name, "usage": usage, "choices": choices}
 
     @app.post("/v1/chat/completions")
     def chat_completions(req: ChatCompletionRequest):

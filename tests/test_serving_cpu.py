@@ -583,3 +583,17 @@ def test_text_stop_sequences(server):
     plain = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 12, "stop": "\x00zz"},
                           timeout=60).json()["choices"][0]
     assert plain["finish_reason"] == "length" and plain["token_ids"] == full
+
+
+def test_batch_of_prompts_in_one_request(server):
+    url, _ = server
+    prompts = [[5, 9, 100], [42] * 5, [1, 2, 3, 4]]
+    want = _engine().generate(prompts, 3)
+    r = requests.post(url + "/v1/completions", json={"prompt": prompts, "max_tokens": 3}, timeout=60).json()
+    assert [c["token_ids"] for c in r["choices"]] == want and [c["index"] for c in r["choices"]] == [0, 1, 2]
+    assert r["usage"]["prompt_tokens"] == 12 and r["usage"]["completion_tokens"] == 9
+    t = requests.post(url + "/v1/completions", json={"prompt": ["ab", "cd"], "max_tokens": 2}, timeout=60).json()
+    assert len(t["choices"]) == 2
+    bad = requests.post(url + "/v1/completions", json={"prompt": prompts, "max_tokens": 2, "stream": True},
+                        timeout=60)
+    assert bad.status_code == 400
