@@ -152,7 +152,8 @@ def main(argv=None) -> None:
         torch.cuda.set_device(local)
     A, F = int(afd["num_attention_ranks"]), int(afd["num_ffn_ranks"])
     given_role = afd.get("role", afd.get("afd_role"))
-    if given_role in ("attention", "ffn") and world == (A if given_role == "attention" else F):
+    per_role = given_role in ("attention", "ffn") and world == (A if given_role == "attention" else F)
+    if per_role:
         # One role per launch, as the reference deploys (an Attention server and an FFN
         # server): this launch's ranks join the AFD world over tcp://host:port, FFN ranks first.
         cfg = afd_config_from_mapping(afd)
@@ -176,7 +177,11 @@ def main(argv=None) -> None:
                       max_num_batched_tokens=args.max_num_batched_tokens)
     if role == "ffn":
         w = AFDFFNWorker(ec, local_rank=local)
-        w.run_ffn_server_loop()
+        if per_role and role_rank == 0:
+            # an FFN server launched on its own answers /health while its loop serves
+            _serve_ffn_health(w, args.host, args.port)
+        else:
+            w.run_ffn_server_loop()
         w.shutdown()
         return
     w = AFDAttentionWorker(ec, local_rank=local)
@@ -196,6 +201,35 @@ def main(argv=None) -> None:
     else:
         loop.join()
     w.shutdown()  # stops the FFN ranks' serve loops
+
+
+def _serve_ffn_health(worker, host: str, port: int) -> None:
+    """Run the FFN loop on its thread and ``GET /health`` (200 while it serves) until it ends."""
+    import threading
+    import time
+
+    import uvicorn
+    from fastapi import FastAPI, HTTPException
+
+    app = FastAPI(title="afd_plugin_b200 FFN")
+
+    @app.get("/health")
+    def health():
+        if not worker.is_loop_alive():
+            raise HTTPException(status_code=503, detail="FFN loop not running")
+        return {"status": "ok", "role": "ffn"}
+
+    worker.start_ffn_server_loop()
+    server = uvicorn.Server(uvicorn.Config(app, host=host, port=port, log_level="warning"))
+
+    def watch() -> None:  # the loop ends on the Attention side's shutdown: take the HTTP server down too
+        while worker.is_loop_alive():
+            time.sleep(0.2)
+        server.should_exit = True
+
+    threading.Thread(target=watch, name="afd-ffn-health-watch", daemon=True).start()
+    server.run()
+    worker.stop_ffn_server_loop()
 
 
 if __name__ == "__main__":

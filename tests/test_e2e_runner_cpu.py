@@ -212,7 +212,8 @@ def test_roles_launched_separately_join_one_afd_world(tmp_path):
                PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
     common = [sys.executable, "-m", "afd_plugin_b200.serving", "--preset", "tiny-dsv2", "--dtype", "float32",
               "--eager", "--max-model-len", "128", "--max-num-seqs", "4"]
-    ffn = start_server(common + ["--port", str(free_port()), "--afd", json.dumps(dict(base, role="ffn"))],
+    ffn_http = free_port()
+    ffn = start_server(common + ["--port", str(ffn_http), "--afd", json.dumps(dict(base, role="ffn"))],
                        env=env, log_path=str(tmp_path / "ffn.log"))
     attn = start_server(common + ["--port", str(http), "--afd", json.dumps(dict(base, role="attention"))],
                         env=env, log_path=str(tmp_path / "attn.log"))
@@ -233,6 +234,8 @@ def test_roles_launched_separately_join_one_afd_world(tmp_path):
                         build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=128))
         assert got == eng.generate(prompts, 4)
         assert requests.get(url + "/health", timeout=5).status_code == 200
+        ffn_health = requests.get(f"http://127.0.0.1:{ffn_http}/health", timeout=5)
+        assert ffn_health.status_code == 200 and ffn_health.json()["role"] == "ffn"
     finally:
         stop_server(attn)
         stop_server(ffn)
