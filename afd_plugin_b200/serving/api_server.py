@@ -426,20 +426,26 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             raise HTTPException(status_code=502, detail=f"KV fetch from {url}: HTTP {r.status_code}")
         return r.content
 
+    def _new_id(chat: bool) -> tuple[str, int]:
+        import uuid
+
+        return ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex, int(time.time())
+
     def _chunk(chat: bool, model: str, tokens: list[int], text: str, finish: str | None,
-               usage: dict | None = None) -> str:
+               usage: dict | None = None, ident: tuple[str, int] = ("", 0)) -> str:
         if chat:
-            delta = {"role": "assistant", "content": text} if tokens else {}
-            msg = {"object": "chat.completion.chunk", "model": model,
+            delta = {"role": "assistant", "content": text} if tokens or text else {}
+            msg = {"id": ident[0], "object": "chat.completion.chunk", "created": ident[1], "model": model,
                    "choices": [{"index": 0, "delta": delta, "token_ids": tokens, "finish_reason": finish}]}
         else:
-            msg = {"object": "text_completion", "model": model,
+            msg = {"id": ident[0], "object": "text_completion", "created": ident[1], "model": model,
                    "choices": [{"index": 0, "token_ids": tokens, "text": text, "finish_reason": finish}]}
         if usage is not None:
             msg["usage"] = usage
         return "data: " + json.dumps(msg) + "\n\n"
 
-    async def _sse(tokens: queue.Queue, fut: Future, n_prompt: int, model: str, chat: bool):
+    async def _sse(tokens: queue.Queue, fut: Future, n_prompt: int, model: str, chat: bool,
+                   ident: tuple[str, int] = ("", 0)):
         """Server-sent events: one chunk per token, a final chunk with usage, then ``[DONE]``.
 
         Runs on the event loop; a client that disconnects cancels it at its
@@ -469,10 +475,10 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
                     return
                 n += 1
                 deadline = time.monotonic() + request_timeout_s
-                yield _chunk(chat, model, [t], detok.push(t), None)
+                yield _chunk(chat, model, [t], detok.push(t), None, ident=ident)
             ended = True
-            yield _chunk(chat, model, [], "", getattr(fut, "finish_reason", "length"),
-                         {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n})
+            yield _chunk(chat, model, [], detok.flush(), getattr(fut, "finish_reason", "length"),
+                         {"prompt_tokens": n_prompt, "completion_tokens": n, "total_tokens": n_prompt + n}, ident)
             yield "data: [DONE]\n\n"
         finally:
             rid = getattr(fut, "req_id", None)
@@ -520,7 +526,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
                 futs = [loop.submit(ids, max_tokens, hold_kv=prefill_only, stream=stream, sampling=sp, stop=stops)
                         for sp in samplings]
             if stream is not None:
-                return StreamingResponse(_sse(stream, futs[0], len(ids), model, chat),
+                return StreamingResponse(_sse(stream, futs[0], len(ids), model, chat, _new_id(chat)),
                                          media_type="text/event-stream")
             outs = [f.result(timeout=request_timeout_s) for f in futs]
         except ValueError as exc:
@@ -542,8 +548,9 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             if samplings[i] is not None and samplings[i].logprobs is not None:
                 c["logprobs"] = _logprobs_block(chat, out, getattr(f, "logprobs", ([], [])))
             choices.append(c)
-        body = {"object": "chat.completion" if chat else "text_completion", "model": model, "usage": usage,
-                "choices": choices}
+        ident = _new_id(chat)
+        body = {"id": ident[0], "object": "chat.completion" if chat else "text_completion", "created": ident[1],
+                "model": model, "usage": usage, "choices": choices}
         if prefill_only:
             body["kv_transfer_params"] = {
                 "do_remote_prefill": True, "do_remote_decode": False,
@@ -640,7 +647,9 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
                 choices.append(dict(c, index=len(choices)))
             for k in usage:
                 usage[k] += body["usage"][k]
-        return {"object": "text_completion", "model": req.model or model_name, "usage": usage, "choices": choices}
+        ident = _new_id(False)
+        return {"id": ident[0], "object": "text_completion", "created": ident[1], "model": req.model or model_name,
+                "usage": usage, "choices": choices}
 
     @app.post("/v1/chat/completions")
     def chat_completions(req: ChatCompletionRequest):

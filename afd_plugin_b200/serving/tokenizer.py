@@ -86,8 +86,15 @@ class StreamDetokenizer:
     def push(self, token: int) -> str:
         self.ids.append(int(token))
         text = self.tok.decode(self.ids)
-        if text.endswith("�"):  # a multi-byte character still incomplete
+        if text.endswith("\ufffd"):  # a multi-byte character still incomplete (or invalid)
             return ""
+        return self._emit(text)
+
+    def flush(self) -> str:
+        """Whatever text was held back (the stream has ended)."""
+        return self._emit(self.tok.decode(self.ids))
+
+    def _emit(self, text: str) -> str:
         new = text[len(self.sent):] if text.startswith(self.sent) else text
         self.sent = text
         return new

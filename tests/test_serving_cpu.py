@@ -597,3 +597,25 @@ def test_batch_of_prompts_in_one_request(server):
     bad = requests.post(url + "/v1/completions", json={"prompt": prompts, "max_tokens": 2, "stream": True},
                         timeout=60)
     assert bad.status_code == 400
+
+
+def test_openai_python_client_talks_to_the_server(server):
+    """The official OpenAI client parses every response shape (completions, chat, streams)."""
+    openai = pytest.importorskip("openai")
+    url, _ = server
+    client = openai.OpenAI(base_url=url + "/v1", api_key="unused")
+    prompt = [5, 9, 100, 7, 3, 1]
+    want = _engine().generate([prompt], 5)[0]
+    c = client.completions.create(model="afd-b200", prompt=prompt, max_tokens=5)
+    assert c.id.startswith("cmpl-") and c.choices[0].finish_reason == "length" and c.usage.completion_tokens == 5
+    assert c.choices[0].text == byte_detokenize(want)
+    chunks = list(client.completions.create(model="afd-b200", prompt=prompt, max_tokens=5, stream=True))
+    assert "".join(ch.choices[0].text for ch in chunks) == byte_detokenize(want)
+    chat = client.chat.completions.create(model="afd-b200", messages=[{"role": "user", "content": "hi"}],
+                                          max_tokens=3, temperature=0.0)
+    assert chat.id.startswith("chatcmpl-") and chat.choices[0].message.role == "assistant"
+    stream = client.chat.completions.create(model="afd-b200", messages=[{"role": "user", "content": "hi"}],
+                                            max_tokens=3, stream=True)
+    text = "".join(ch.choices[0].delta.content or "" for ch in stream)
+    assert text == chat.choices[0].message.content
+    assert [m.id for m in client.models.list().data] == ["afd-b200"]
