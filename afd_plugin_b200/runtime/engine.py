@@ -365,6 +365,8 @@ class LLMEngine:
         from afd_plugin_b200.runtime import kv_transfer as kt
 
         while self._kv_waiting and len(self.running) < self.max_batch:
+            if self._blocks_short(self._kv_waiting[0][0]) > self.kv.allocator.num_free:
+                break  # waits until blocks free up
             req, state = self._kv_waiting.pop(0)
             n = len(req.prompt)
             self._ensure_blocks(req, n + 1)

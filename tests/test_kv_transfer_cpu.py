@@ -105,3 +105,23 @@ def test_imported_requests_wait_for_a_batch_slot():
     rid, _ = dec.add_prefilled_request(pre2.export_kv(r), 1)
     assert dec.step() == {}
     assert dec.finished[rid].output == pre2.finished[r].output
+
+
+def test_imported_requests_wait_for_free_blocks():
+    from afd_plugin_b200.engine_config import CacheConfig
+
+    arch = get_preset("tiny-dsv2")
+    pre = _engine("tiny-dsv2")
+    prompts = _prompts(arch.vocab_size)
+    blobs = []
+    for p in prompts:
+        rid = pre.add_request(p, 1, hold_kv=True)
+        _drain(pre)
+        blobs.append(pre.export_kv(rid))
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96),
+                      cache_config=CacheConfig(block_size=4, num_blocks=9), max_num_seqs=4)
+    dec = LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=96))
+    ids = [dec.add_prefilled_request(b, 3)[0] for b in blobs]
+    _drain(dec)  # no MemoryError: imports wait for blocks
+    ref = _engine("tiny-dsv2").generate(prompts, 3)
+    assert [dec.finished[i].output for i in ids] == ref
