@@ -9,6 +9,8 @@ library raises rather than falling back.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from afd_plugin_b200.ops import checks
@@ -153,13 +155,17 @@ def mla_decode_sparse(
     keep_pos: torch.Tensor,
     scale: float,
     kv_lora_rank: int,
+    *,
+    num_splits: int = 0,
 ) -> torch.Tensor:
     """MLA decode over the positions a DeepSeek-sparse-attention indexer kept.
 
     ``keep_pos [B, K]`` lists each row's selected positions (-1 = unused).
-    Gather + two small batched GEMMs on both devices: no dedicated sparse
-    kernel yet (dense steps, i.e. every sequence within ``index_topk``
-    tokens, keep using the MLA decode kernel).
+    With ``AFD_SPARSE_MLA_KERNEL=1`` on a GPU (DeepSeek's 512 + 64 latent,
+    heads a multiple of 16) the sm_100a sparse decode kernel gathers the
+    kept rows (``csrc/mla_decode.cu``, ``kSparse``); otherwise a gather plus
+    two small batched GEMMs.  The switch stays off by default until the
+    kernel's numerics test has passed on a B200.
     """
     if checks.enabled():
         checks.paged_attention("mla_decode_sparse", block_table, seq_lens, num_blocks=kv_cache.shape[0],
@@ -167,7 +173,16 @@ def mla_decode_sparse(
         bad = (keep_pos >= seq_lens.view(-1, 1).to(keep_pos.dtype)).any()
         if bool(bad):
             raise checks.KernelInputError("mla_decode_sparse: a kept position lies beyond its sequence")
+    if (_cuda(q) and sparse_kernel_enabled() and q.dtype == torch.bfloat16 and q.shape[-1] == 576
+            and kv_lora_rank == 512 and q.shape[1] % 16 == 0):
+        return _cuda_ops().mla_decode_sparse(q, kv_cache, block_table, seq_lens.to(torch.int32),
+                                             keep_pos.to(torch.int32).contiguous(), scale, num_splits)
     return ref.mla_decode_sparse(q, kv_cache, block_table, keep_pos, scale, kv_lora_rank)
+
+
+def sparse_kernel_enabled() -> bool:
+    """``AFD_SPARSE_MLA_KERNEL=1`` routes sparse MLA decode to the gather kernel."""
+    return os.environ.get("AFD_SPARSE_MLA_KERNEL", "") in ("1", "true", "on")
 
 
 def gqa_decode(

@@ -208,6 +208,52 @@ at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at:
   return out;
 }
 
+// DeepSeek sparse attention: q [B, H, 576] over the kept positions
+// keep_pos [B, K] int32 (-1 = unused).  Output [B, H, 512].
+at::Tensor mla_decode_sparse(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& block_table,
+                             const at::Tensor& seq_lens, const at::Tensor& keep_pos, double scale, int64_t num_splits) {
+  check_cuda(q, "q");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16, "mla_decode_sparse: bf16 only");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576 && q.stride(2) == 1 && q.stride(0) % 8 == 0 && q.stride(1) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0, "mla_decode_sparse: q [B, H, 576], 16-byte rows");
+  TORCH_CHECK(cache.is_contiguous() && cache.dim() == 3 && cache.size(-1) == 576, "mla_decode_sparse: cache [blocks, bs, 576]");
+  TORCH_CHECK(q.size(1) % 16 == 0, "mla_decode_sparse: heads must be a multiple of 16");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  keep_pos.scalar_type() == at::kInt, "mla_decode_sparse: int32 meta");
+  TORCH_CHECK(block_table.stride(1) == 1, "mla_decode_sparse: block_table rows must be dense");
+  TORCH_CHECK(keep_pos.dim() == 2 && keep_pos.is_contiguous() && keep_pos.size(0) == q.size(0),
+              "mla_decode_sparse: keep_pos [B, K] contiguous");
+  const int B = (int)q.size(0), H = (int)q.size(1), K = (int)keep_pos.size(1);
+  at::Tensor out = at::empty({B, H, 512}, q.options());
+  if (B == 0) return out;
+  int splits = (int)num_splits;
+  if (splits <= 0) {
+    int dev_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+    splits = mla_decode_num_splits(B * (H / 16), K, dev_sms);
+  }
+  at::Tensor po, pl;
+  if (splits > 1) {
+    po = at::empty({B, splits, H, 512}, q.options().dtype(at::kFloat));
+    pl = at::empty({B, splits, H}, q.options().dtype(at::kFloat));
+  }
+  MlaQO qo{};
+  qo.q_lat = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  qo.lat_sb = q.stride(0);
+  qo.lat_sh = q.stride(1);
+  qo.q_pe = qo.q_lat + 512;
+  qo.pe_sb = q.stride(0);
+  qo.pe_sh = q.stride(1);
+  qo.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  qo.out_sb = (int64_t)H * 512;
+  qo.out_sh = 512;
+  c10::cuda::CUDAGuard g(q.device());
+  launch_mla_decode_sparse(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                           keep_pos.data_ptr<int32_t>(), K, splits > 1 ? po.data_ptr<float>() : nullptr,
+                           splits > 1 ? pl.data_ptr<float>() : nullptr, status_ptr(q), B, H, 512, (int)cache.size(1),
+                           (int)block_table.stride(0), splits, (float)scale, stream());
+  return out;
+}
+
 at::Tensor gqa_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& block_table,
                       const at::Tensor& seq_lens, double scale, int64_t num_splits) {
   check_cuda(q, "q");
@@ -732,6 +778,8 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("gqa_cache_write(Tensor(a!) kc, Tensor(b!) vc, Tensor k, Tensor v, Tensor slots) -> ()");
   m.def("mla_decode(Tensor q_lat, Tensor q_pe, Tensor cache, Tensor block_table, Tensor seq_lens, float scale, "
         "int num_splits, bool head_major) -> Tensor");
+  m.def("mla_decode_sparse(Tensor q, Tensor cache, Tensor block_table, Tensor seq_lens, Tensor keep_pos, float scale, "
+        "int num_splits) -> Tensor");
   m.def("gqa_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor seq_lens, float scale, "
         "int num_splits) -> Tensor");
   m.def("moe_align(Tensor topk_ids, int e_local, int offset, int n_shared) -> Tensor[]");
@@ -776,6 +824,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("mla_cache_write", &mla_cache_write);
   m.impl("gqa_cache_write", &gqa_cache_write);
   m.impl("mla_decode", &mla_decode);
+  m.impl("mla_decode_sparse", &mla_decode_sparse);
   m.impl("gqa_decode", &gqa_decode);
   m.impl("moe_align", &moe_align);
   m.impl("moe_gather", &moe_gather);

@@ -49,6 +49,13 @@ void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_
                        const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                        int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
                        int num_splits, float scale, cudaStream_t s);
+// Sparse (DeepSeek sparse attention) decode over keep_pos [B, num_keep] int32
+// (-1 or a position >= seq_lens[b] = unused entry); same outputs and scratch,
+// with splits over the kept entries.
+void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t* block_table, const int32_t* seq_lens,
+                              const int32_t* keep_pos, int num_keep, float* partial_o, float* partial_lse, int* status,
+                              int batch, int heads, int L, int block_size, int max_blocks_per_seq, int num_splits,
+                              float scale, cudaStream_t s);
 
 // ---- gqa_decode.cu
 // q [B, hq, 128], caches [blocks, bs, hkv, 128], out [B, hq, 128] (bf16).

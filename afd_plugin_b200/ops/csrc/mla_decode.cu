@@ -14,9 +14,20 @@
 // does ~37 kFLOP for 16 heads, well under the tensor-core ceiling; the
 // pipeline's job is to keep enough tile bytes in flight to saturate HBM.
 //
+// Sparse variant (DeepSeek sparse attention, kSparse = true): the CTA walks a
+// per-request list of kept positions instead of the whole sequence.  The
+// rows are scattered over the paged cache, so the producer warp gathers them
+// with per-thread cp.async (one token row of 1152 B per lane, 16 B per copy,
+// written at the same swizzled offsets the TMA path produces) and each lane
+// signals the stage's mbarrier with cp.async.mbarrier.arrive.noinc; unused
+// or out-of-range entries are zero-filled (src-size 0) and masked out of the
+// softmax.  The math warps are shared with the dense path.
+//
 // Every mbarrier wait is bounded; on expiry the CTA records
 // kStatusWaitTimeout in `status` and leaves its loop.
 #include <cudaTypedefs.h>
+
+#include <cstring>
 
 #include "common.cuh"
 #include "launchers.h"
@@ -53,10 +64,29 @@ AFD_DEVICE uint32_t swz(int row, int col, int box_bytes) {
   return box * box_bytes + row * 128 + ((chunk ^ (row & 7)) << 4) + ((col & 7) << 1);
 }
 
+// 16-byte global -> shared copy; `src_bytes` 0 writes zeros without reading.
+AFD_DEVICE void cp_async_16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// The mbarrier receives one arrival once this thread's earlier cp.async copies land.
+AFD_DEVICE void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+AFD_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Entry `tok` of request b's kept-position list is a real token.
+AFD_DEVICE bool sparse_entry_valid(const int32_t* __restrict__ keep_pos, int b, int tok, int num_keep, int seq_len) {
+  if (tok >= num_keep) return false;
+  const int p = keep_pos[(size_t)b * num_keep + tok];
+  return p >= 0 && p < seq_len;
+}
+
+template <bool kSparse>
 __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
     const __grid_constant__ CUtensorMap kv_map, const MlaQO qo, const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
     float* __restrict__ part_lse, int* __restrict__ status, int heads, int block_size, int max_blocks,
-    int num_splits, float scale_log2) {
+    int num_splits, float scale_log2, const __nv_bfloat16* __restrict__ cache, const int32_t* __restrict__ keep_pos,
+    int num_keep) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int b = blockIdx.x;
@@ -64,7 +94,8 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
   const int split = blockIdx.z;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const int seq = seq_lens[b];
+  const int seq_len = seq_lens[b];
+  const int seq = kSparse ? num_keep : seq_len;  // entries this CTA's splits walk
   const int n_tiles_total = (seq + kTile - 1) / kTile;
   const int tiles_per_split = (n_tiles_total + num_splits - 1) / num_splits;
   const int tile_begin = split * tiles_per_split;
@@ -73,7 +104,7 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.full[s], kSparse ? kTile : 1);
       mbar_init(&sm.empty[s], kMathWarps);
     }
     fence_barrier_init();
@@ -93,7 +124,32 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
 
   if (warp == kMathWarps) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    if constexpr (kSparse) {
+      // one kept token per lane (kTile == 32), its 72 16-byte chunks gathered
+      const uint32_t kv_smem = smem_u32(sm.kv[0]);
+      for (int i = 0; i < n_tiles; ++i) {
+        const int st = i % kStages;
+        if (i >= kStages &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(&sm.empty[st], ((i / kStages) - 1) & 1))) {
+          if (lane == 0) atomicExch(status, kStatusWaitTimeout);
+          break;
+        }
+        const int tok = (tile_begin + i) * kTile + lane;
+        const bool valid = sparse_entry_valid(keep_pos, b, tok, num_keep, seq_len);
+        const __nv_bfloat16* src = cache;
+        if (valid) {
+          const int p = keep_pos[(size_t)b * num_keep + tok];
+          const int blk = block_table[(size_t)b * max_blocks + p / block_size];
+          src = cache + ((size_t)blk * block_size + p % block_size) * kD;
+        }
+        const uint32_t dst = kv_smem + st * kTileBytes;
+        const uint32_t nbytes = valid ? 16u : 0u;
+#pragma unroll 8
+        for (int c = 0; c < kD / 8; ++c) cp_async_16_zfill(dst + swz(lane, c * 8, kBoxBytes), src + (valid ? c * 8 : 0), nbytes);
+        cp_async_mbar_arrive_noinc(&sm.full[st]);
+      }
+      cp_async_wait_all();
+    } else if (lane == 0) {
       prefetch_tensormap(&kv_map);
       for (int i = 0; i < n_tiles; ++i) {
         const int st = i % kStages;
@@ -168,7 +224,8 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int tok = tok0 + tcol + (j & 1);
-        sacc[j] = (tok < seq) ? sacc[j] * scale_log2 : -INFINITY;
+        const bool keep = kSparse ? sparse_entry_valid(keep_pos, b, tok, num_keep, seq_len) : (tok < seq);
+        sacc[j] = keep ? sacc[j] * scale_log2 : -INFINITY;
       }
       *reinterpret_cast<float2*>(&sS[r0 * kSStride + tcol]) = make_float2(sacc[0], sacc[1]);
       *reinterpret_cast<float2*>(&sS[(r0 + 8) * kSStride + tcol]) = make_float2(sacc[2], sacc[3]);
@@ -339,8 +396,10 @@ int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
 
 // Opts the decode kernel into its dynamic shared memory on the current device.
 cudaError_t mla_decode_prepare_device() {
-  return cudaFuncSetAttribute(mla::mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)sizeof(mla::Smem) + 1024);
+  const int smem = (int)sizeof(mla::Smem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(mla::mla_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(mla::mla_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
@@ -358,14 +417,36 @@ void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_
   const int smem = (int)sizeof(mla::Smem) + 1024;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(mla::mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(mla::mla_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr_set = true;
   }
   dim3 grid(batch, heads / mla::kHeads, num_splits);
   const float scale_log2 = scale * 1.4426950408889634f;
-  mla::mla_decode_kernel<<<grid, mla::kThreads, smem, s>>>(map, qo, block_table, seq_lens, partial_o, partial_lse,
-                                                            status, heads, block_size, max_blocks_per_seq, num_splits,
-                                                            scale_log2);
+  mla::mla_decode_kernel<false><<<grid, mla::kThreads, smem, s>>>(map, qo, block_table, seq_lens, partial_o, partial_lse,
+                                                                   status, heads, block_size, max_blocks_per_seq,
+                                                                   num_splits, scale_log2, nullptr, nullptr, 0);
+  if (num_splits > 1) {
+    mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
+  }
+}
+
+void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t* block_table, const int32_t* seq_lens,
+                              const int32_t* keep_pos, int num_keep, float* partial_o, float* partial_lse, int* status,
+                              int batch, int heads, int L, int block_size, int max_blocks_per_seq, int num_splits,
+                              float scale, cudaStream_t s) {
+  CUtensorMap unused;
+  memset(&unused, 0, sizeof(unused));
+  const int smem = (int)sizeof(mla::Smem) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(mla::mla_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_set = true;
+  }
+  dim3 grid(batch, heads / mla::kHeads, num_splits);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  mla::mla_decode_kernel<true><<<grid, mla::kThreads, smem, s>>>(
+      unused, qo, block_table, seq_lens, partial_o, partial_lse, status, heads, block_size, max_blocks_per_seq,
+      num_splits, scale_log2, reinterpret_cast<const __nv_bfloat16*>(cache), keep_pos, num_keep);
   if (num_splits > 1) {
     mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
   }

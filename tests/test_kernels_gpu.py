@@ -227,3 +227,38 @@ def test_moe_experts_fp8_weights():
     expect = ref.moe_experts(x.float(), d13, d2, tw, tid)
     scale = expect.abs().max().item()
     _close(out / scale, expect / scale, 2e-2)
+
+
+@pytest.mark.parametrize("heads,bs", [(16, 64), (32, 16)])
+@pytest.mark.parametrize("splits", [1, 0, 3])
+def test_mla_decode_sparse(heads, bs, splits):
+    """Gather kernel over kept positions: -1 entries, positions out of order, rows of any block size."""
+    torch.manual_seed(7 * heads + splits)
+    lens = [1, 40, 97, 300, 1029]
+    B, K = len(lens), 96
+    cache, table, seq = _paged_cache(B, lens, 576, bs=bs)
+    keep = torch.full((B, K), -1, dtype=torch.int32)
+    for b, n in enumerate(lens):
+        pick = torch.randperm(n)[: min(n, K - 5)]
+        keep[b, torch.randperm(K)[: len(pick)]] = pick.to(torch.int32)
+    keep = keep.to(DEV)
+    q = torch.randn(B, heads, 576, device=DEV, dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(192)
+    out = _ext.ops().mla_decode_sparse(q, cache, table, seq, keep, scale, splits)
+    expect = ref.mla_decode_sparse(q.float(), cache.float(), table, keep, scale, 512)
+    _close(out, expect, 2e-2, 2e-2)
+
+
+def test_mla_decode_sparse_routing(monkeypatch):
+    """The op takes the kernel under the switch and agrees with the gather + GEMM form."""
+    torch.manual_seed(3)
+    lens = [50, 130]
+    cache, table, seq = _paged_cache(2, lens, 576)
+    keep = torch.stack([torch.randperm(130)[:64] % n for n in lens]).to(torch.int64).to(DEV)
+    q = torch.randn(2, 16, 576, device=DEV, dtype=torch.bfloat16)
+    monkeypatch.setenv("AFD_SPARSE_MLA_KERNEL", "0")
+    base = ops.mla_decode_sparse(q, cache, table, seq, keep, 0.1, 512)
+    monkeypatch.setenv("AFD_SPARSE_MLA_KERNEL", "1")
+    assert ops.sparse_kernel_enabled()
+    got = ops.mla_decode_sparse(q, cache, table, seq, keep, 0.1, 512)
+    _close(got, base, 2e-2, 2e-2)
