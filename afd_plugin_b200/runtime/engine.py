@@ -40,7 +40,8 @@ from afd_plugin_b200.runtime.cuda_graph import pad_to_capture_size, validate_cud
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor, LocalFFNExecutor
 from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache, block_hashes
 from afd_plugin_b200.runtime.model_runner import ModelRunner
-from afd_plugin_b200.runtime.sampling import GREEDY, SamplingParams, make_generator, sample, token_logprobs
+from afd_plugin_b200.runtime.sampling import (GREEDY, SamplingParams, apply_penalties, make_generator, sample,
+                                             token_logprobs)
 
 
 @dataclass
@@ -245,14 +246,19 @@ class LLMEngine:
         and record log-probabilities for requests that asked for them."""
         plain = True
         for r in reqs:
-            if not r.sampling.greedy or r.sampling.logprobs is not None:
+            if not r.sampling.greedy or r.sampling.logprobs is not None or r.sampling.penalized:
                 plain = False
                 break
         if plain:
             return tokens
         logits = self.runner.last_logits[: len(reqs)]
-        if not all(r.sampling.greedy for r in reqs):
-            drawn = sample(logits, [r.sampling for r in reqs], [r.generator for r in reqs], self._sample_gen)
+        params = [r.sampling for r in reqs]
+        penalized = any(p.penalized for p in params)
+        if penalized or not all(p.greedy for p in params):
+            chosen_from = logits
+            if penalized:
+                chosen_from = apply_penalties(logits, params, [r.prompt for r in reqs], [r.output for r in reqs])
+            drawn = sample(chosen_from, params, [r.generator for r in reqs], self._sample_gen)
             tokens[: len(reqs)].copy_(drawn)
         rows = [i for i, r in enumerate(reqs) if r.sampling.logprobs is not None]
         if rows:

@@ -11,6 +11,12 @@ the step's logits afterwards, on the device, in one batched pass:
   engine's generator, or from the request's own when it carries a seed, so a
   seeded request reproduces its tokens whatever else is in the batch.
 
+Penalties run before all of that, on the logits, with vLLM's meanings:
+``presence_penalty`` subtracts a constant from every token already generated,
+``frequency_penalty`` subtracts it once per occurrence, and
+``repetition_penalty`` divides positive logits (multiplies negative ones) of
+every token seen in the prompt or the output.
+
 The reference takes these parameters through vLLM's sampler; the field names
 and meanings follow the OpenAI completions API it serves.
 """
@@ -33,6 +39,9 @@ class SamplingParams:
     ignore_eos: bool = False
     # per generated token: its log-probability under the model, and the ``logprobs`` most likely tokens
     logprobs: int | None = None
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    repetition_penalty: float = 1.0  # 1: off
 
     def __post_init__(self) -> None:
         if self.temperature < 0:
@@ -43,6 +52,14 @@ class SamplingParams:
             raise ValueError("top_p must be in (0, 1]")
         if self.logprobs is not None and not 0 <= self.logprobs <= 20:
             raise ValueError("logprobs must be in [0, 20]")
+        if not -2.0 <= self.presence_penalty <= 2.0 or not -2.0 <= self.frequency_penalty <= 2.0:
+            raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
+        if self.repetition_penalty <= 0.0:
+            raise ValueError("repetition_penalty must be > 0")
+
+    @property
+    def penalized(self) -> bool:
+        return self.presence_penalty != 0.0 or self.frequency_penalty != 0.0 or self.repetition_penalty != 1.0
 
     @property
     def greedy(self) -> bool:
@@ -56,6 +73,40 @@ def make_generator(seed: int, device) -> torch.Generator:
     g = torch.Generator(device=device)
     g.manual_seed(int(seed) & 0x7FFFFFFFFFFFFFFF)
     return g
+
+
+def _token_counts(seqs: list[list[int]], V: int, device) -> torch.Tensor:
+    """``[n, V]`` occurrence counts of each row's tokens."""
+    width = max((len(t) for t in seqs), default=0)
+    counts = torch.zeros(len(seqs), V + 1, device=device)
+    if width:
+        ids = torch.full((len(seqs), width), V, dtype=torch.long)
+        for i, t in enumerate(seqs):
+            if t:
+                ids[i, : len(t)] = torch.tensor(t, dtype=torch.long).clamp_(0, V)
+        counts.scatter_add_(1, ids.to(device), torch.ones(ids.shape, device=device))
+    return counts[:, :V]
+
+
+def apply_penalties(logits: torch.Tensor, params: list[SamplingParams], prompts: list[list[int]],
+                    outputs: list[list[int]]) -> torch.Tensor:
+    """Penalised fp32 copy of ``logits [n, V]``; rows without penalties are unchanged."""
+    x = logits.float().clone()
+    rows = [i for i, p in enumerate(params) if p.penalized]
+    if not rows:
+        return x
+    dev, V = x.device, x.shape[1]
+    idx = torch.tensor(rows, device=dev)
+    sub = x.index_select(0, idx)
+    out_counts = _token_counts([outputs[i] for i in rows], V, dev)
+    rep = torch.tensor([params[i].repetition_penalty for i in rows], device=dev).unsqueeze(1)
+    seen = (out_counts + _token_counts([prompts[i] for i in rows], V, dev)) > 0
+    sub = torch.where(seen, torch.where(sub > 0, sub / rep, sub * rep), sub)
+    freq = torch.tensor([params[i].frequency_penalty for i in rows], device=dev).unsqueeze(1)
+    pres = torch.tensor([params[i].presence_penalty for i in rows], device=dev).unsqueeze(1)
+    sub = sub - freq * out_counts - pres * (out_counts > 0).float()
+    x[idx] = sub
+    return x
 
 
 def filtered_probs(logits: torch.Tensor, params: list[SamplingParams]) -> torch.Tensor:

@@ -60,6 +60,9 @@ class SamplingFields(BaseModel):
     top_logprobs: int | None = None
     n: int = 1
     stop: str | list[str] | None = None  # text stop sequences (checked on the decoded text)
+    presence_penalty: float | None = None
+    frequency_penalty: float | None = None
+    repetition_penalty: float | None = None
 
     def stop_strings(self) -> list[str]:
         if self.stop is None:
@@ -77,13 +80,18 @@ class SamplingFields(BaseModel):
         """The parameters of choice ``index`` (seeded choices use seed + index)."""
         lp = self.n_logprobs()
         if all(v is None for v in (self.temperature, self.top_p, self.top_k, self.seed, self.stop_token_ids,
-                                   self.ignore_eos, lp)):
+                                   self.ignore_eos, lp, self.presence_penalty, self.frequency_penalty,
+                                   self.repetition_penalty)):
             return None
-        return SamplingParams(temperature=float(self.temperature or 0.0), top_k=int(self.top_k or 0),
+        return SamplingParams(temperature=float(self.temperature or 0.0),
+                              top_k=max(0, int(self.top_k or 0)),  # vLLM's -1 = off
                               top_p=float(self.top_p if self.top_p is not None else 1.0),
                               seed=None if self.seed is None else self.seed + index,
                               stop_token_ids=tuple(int(t) for t in self.stop_token_ids or ()),
-                              ignore_eos=bool(self.ignore_eos), logprobs=lp)
+                              ignore_eos=bool(self.ignore_eos), logprobs=lp,
+                              presence_penalty=float(self.presence_penalty or 0.0),
+                              frequency_penalty=float(self.frequency_penalty or 0.0),
+                              repetition_penalty=float(self.repetition_penalty or 1.0))
 
 
 class CompletionRequest(SamplingFields):

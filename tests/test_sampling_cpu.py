@@ -226,3 +226,45 @@ def test_server_n_choices_and_logprobs():
     finally:
         srv.should_exit = True
         loop.stop()
+
+
+def test_penalties_follow_their_definitions():
+    from afd_plugin_b200.runtime.sampling import apply_penalties
+
+    logits = torch.tensor([[2.0, -1.0, 0.5, 3.0, 0.0]] * 3)
+    prompts = [[0], [0], [0]]
+    outputs = [[3, 3, 2], [3, 3, 2], [3, 3, 2]]
+    params = [SamplingParams(presence_penalty=0.5), SamplingParams(frequency_penalty=0.25),
+              SamplingParams(repetition_penalty=2.0)]
+    x = apply_penalties(logits, params, prompts, outputs)
+    assert torch.allclose(x[0], torch.tensor([2.0, -1.0, 0.0, 2.5, 0.0]))
+    assert torch.allclose(x[1], torch.tensor([2.0, -1.0, 0.25, 2.5, 0.0]))
+    assert torch.allclose(x[2], torch.tensor([1.0, -1.0, 0.25, 1.5, 0.0]))  # prompt token 0 too
+    # no penalties: same values
+    assert torch.equal(apply_penalties(logits, [GREEDY] * 3, prompts, outputs), logits)
+    with pytest.raises(ValueError):
+        SamplingParams(repetition_penalty=0.0)
+    with pytest.raises(ValueError):
+        SamplingParams(presence_penalty=3.0)
+
+
+def test_engine_penalties_stop_greedy_repetition():
+    """A strong presence penalty forbids repeating any generated token; greedy otherwise."""
+    eng = _engine()
+    prompt = [3, 1, 4, 1, 5]
+    base = eng.generate([prompt], 24)[0]
+    assert len(set(base)) < len(base), "the tiny model repeats itself greedily"
+    eng2 = _engine()
+    out = eng2.generate([prompt], 24, sampling=SamplingParams(presence_penalty=2.0, frequency_penalty=2.0,
+                                                               repetition_penalty=50.0))[0]
+    assert out[0] == base[0]  # nothing generated yet when the first token is chosen (prompt only matters)
+    assert len(set(out)) > len(set(base))
+
+
+def test_server_penalty_fields_and_vllm_top_k():
+    from afd_plugin_b200.serving.api_server import CompletionRequest
+
+    req = CompletionRequest(prompt="x", presence_penalty=0.5, top_k=-1)
+    sp = req.sampling()
+    assert sp.presence_penalty == 0.5 and sp.top_k == 0 and sp.penalized and sp.greedy
+    assert CompletionRequest(prompt="x").sampling() is None
