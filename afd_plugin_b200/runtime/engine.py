@@ -40,8 +40,8 @@ from afd_plugin_b200.runtime.cuda_graph import pad_to_capture_size, validate_cud
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor, LocalFFNExecutor
 from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache, block_hashes
 from afd_plugin_b200.runtime.model_runner import ModelRunner
-from afd_plugin_b200.runtime.sampling import (GREEDY, SamplingParams, apply_penalties, make_generator, sample,
-                                             token_logprobs)
+from afd_plugin_b200.runtime.sampling import (GREEDY, SamplingParams, apply_penalties, make_generator, mask_tokens,
+                                             sample, token_logprobs)
 
 
 @dataclass
@@ -81,7 +81,8 @@ class Request:
     def stopped(self) -> bool:
         """The last generated token is a stop token (a decode-bench request's output[0] is not generated)."""
         first = 1 if self.synthetic_prefill else 0
-        return bool(self.stop_ids) and len(self.output) > first and self.output[-1] in self.stop_ids
+        return (bool(self.stop_ids) and len(self.output) > max(first, self.sampling.min_tokens)
+                and self.output[-1] in self.stop_ids)
 
     @property
     def finished(self) -> bool:
@@ -246,7 +247,8 @@ class LLMEngine:
         and record log-probabilities for requests that asked for them."""
         plain = True
         for r in reqs:
-            if not r.sampling.greedy or r.sampling.logprobs is not None or r.sampling.penalized:
+            if (not r.sampling.greedy or r.sampling.logprobs is not None or r.sampling.penalized
+                    or self._holds_stops(r)):
                 plain = False
                 break
         if plain:
@@ -254,10 +256,14 @@ class LLMEngine:
         logits = self.runner.last_logits[: len(reqs)]
         params = [r.sampling for r in reqs]
         penalized = any(p.penalized for p in params)
-        if penalized or not all(p.greedy for p in params):
+        held = [sorted(r.stop_ids) if self._holds_stops(r) else [] for r in reqs]
+        if penalized or any(held) or not all(p.greedy for p in params):
             chosen_from = logits
             if penalized:
                 chosen_from = apply_penalties(logits, params, [r.prompt for r in reqs], [r.output for r in reqs])
+            if any(held):
+                chosen_from = mask_tokens(chosen_from.float().clone() if chosen_from is logits else chosen_from,
+                                          held)
             drawn = sample(chosen_from, params, [r.generator for r in reqs], self._sample_gen)
             tokens[: len(reqs)].copy_(drawn)
         rows = [i for i, r in enumerate(reqs) if r.sampling.logprobs is not None]
@@ -272,6 +278,11 @@ class LLMEngine:
                 r.token_logprobs.extend([None] * pad + [c])
                 r.top_logprobs.extend([[]] * pad + [t[: r.sampling.logprobs]])
         return tokens
+
+    @staticmethod
+    def _holds_stops(r: Request) -> bool:
+        """The token about to be chosen is still inside the request's ``min_tokens``."""
+        return bool(r.stop_ids) and len(r.output) < r.sampling.min_tokens
 
     def abort(self, req_id: int) -> bool:
         """End a waiting or running request now (client gone); it moves to ``finished`` with

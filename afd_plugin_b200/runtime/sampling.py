@@ -42,6 +42,8 @@ class SamplingParams:
     presence_penalty: float = 0.0
     frequency_penalty: float = 0.0
     repetition_penalty: float = 1.0  # 1: off
+    # stop tokens (EOS included) cannot end generation, and are not sampled, before this many tokens
+    min_tokens: int = 0
 
     def __post_init__(self) -> None:
         if self.temperature < 0:
@@ -56,6 +58,8 @@ class SamplingParams:
             raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
         if self.repetition_penalty <= 0.0:
             raise ValueError("repetition_penalty must be > 0")
+        if self.min_tokens < 0:
+            raise ValueError("min_tokens must be >= 0")
 
     @property
     def penalized(self) -> bool:
@@ -107,6 +111,15 @@ def apply_penalties(logits: torch.Tensor, params: list[SamplingParams], prompts:
     sub = sub - freq * out_counts - pres * (out_counts > 0).float()
     x[idx] = sub
     return x
+
+
+def mask_tokens(logits: torch.Tensor, banned: list[list[int]]) -> torch.Tensor:
+    """``logits`` with each row's ``banned`` tokens set to -inf (in place on an fp32 copy the caller owns)."""
+    rows = [(i, t) for i, ts in enumerate(banned) for t in ts if 0 <= t < logits.shape[1]]
+    if rows:
+        r, c = zip(*rows)
+        logits[torch.tensor(r, device=logits.device), torch.tensor(c, device=logits.device)] = float("-inf")
+    return logits
 
 
 def filtered_probs(logits: torch.Tensor, params: list[SamplingParams]) -> torch.Tensor:

@@ -268,3 +268,19 @@ def test_server_penalty_fields_and_vllm_top_k():
     sp = req.sampling()
     assert sp.presence_penalty == 0.5 and sp.top_k == 0 and sp.penalized and sp.greedy
     assert CompletionRequest(prompt="x").sampling() is None
+
+
+def test_min_tokens_holds_back_stop_tokens():
+    eng = _engine()
+    prompt = [2, 7, 1, 8]
+    free = eng.generate([prompt], 12)[0]
+    stop = free[1]  # the second greedy token: a stop token ends generation there
+    eng2 = _engine()
+    short = eng2.generate([prompt], 12, sampling=SamplingParams(stop_token_ids=(stop,)))[0]
+    assert short == free[:2]
+    eng3 = _engine()
+    held = eng3.generate([prompt], 12, sampling=SamplingParams(stop_token_ids=(stop,), min_tokens=6))[0]
+    assert stop not in held[:6] and len(held) >= 6
+    assert held[0] == free[0]
+    with pytest.raises(ValueError):
+        SamplingParams(min_tokens=-1)
