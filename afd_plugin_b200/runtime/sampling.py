@@ -44,6 +44,8 @@ class SamplingParams:
     repetition_penalty: float = 1.0  # 1: off
     # stop tokens (EOS included) cannot end generation, and are not sampled, before this many tokens
     min_tokens: int = 0
+    # OpenAI logit_bias: (token id, bias added to its logit) pairs, bias in [-100, 100]
+    logit_bias: tuple[tuple[int, float], ...] = ()
 
     def __post_init__(self) -> None:
         if self.temperature < 0:
@@ -60,10 +62,14 @@ class SamplingParams:
             raise ValueError("repetition_penalty must be > 0")
         if self.min_tokens < 0:
             raise ValueError("min_tokens must be >= 0")
+        if any(not -100.0 <= b <= 100.0 for _, b in self.logit_bias):
+            raise ValueError("logit_bias values must be in [-100, 100]")
 
     @property
     def penalized(self) -> bool:
-        return self.presence_penalty != 0.0 or self.frequency_penalty != 0.0 or self.repetition_penalty != 1.0
+        """The logits are adjusted before the choice (penalties or a logit bias)."""
+        return (self.presence_penalty != 0.0 or self.frequency_penalty != 0.0 or self.repetition_penalty != 1.0
+                or bool(self.logit_bias))
 
     @property
     def greedy(self) -> bool:
@@ -109,6 +115,10 @@ def apply_penalties(logits: torch.Tensor, params: list[SamplingParams], prompts:
     freq = torch.tensor([params[i].frequency_penalty for i in rows], device=dev).unsqueeze(1)
     pres = torch.tensor([params[i].presence_penalty for i in rows], device=dev).unsqueeze(1)
     sub = sub - freq * out_counts - pres * (out_counts > 0).float()
+    for j, i in enumerate(rows):
+        for tok, bias in params[i].logit_bias:
+            if 0 <= tok < V:
+                sub[j, tok] += bias
     x[idx] = sub
     return x
 

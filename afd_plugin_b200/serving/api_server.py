@@ -64,6 +64,7 @@ class SamplingFields(BaseModel):
     frequency_penalty: float | None = None
     repetition_penalty: float | None = None
     min_tokens: int | None = None
+    logit_bias: dict[str, float] | None = None  # token id (as a string, per the OpenAI API) -> bias
 
     def stop_strings(self) -> list[str]:
         if self.stop is None:
@@ -82,7 +83,7 @@ class SamplingFields(BaseModel):
         lp = self.n_logprobs()
         if all(v is None for v in (self.temperature, self.top_p, self.top_k, self.seed, self.stop_token_ids,
                                    self.ignore_eos, lp, self.presence_penalty, self.frequency_penalty,
-                                   self.repetition_penalty, self.min_tokens)):
+                                   self.repetition_penalty, self.min_tokens, self.logit_bias)):
             return None
         return SamplingParams(temperature=float(self.temperature or 0.0),
                               top_k=max(0, int(self.top_k or 0)),  # vLLM's -1 = off
@@ -93,7 +94,8 @@ class SamplingFields(BaseModel):
                               presence_penalty=float(self.presence_penalty or 0.0),
                               frequency_penalty=float(self.frequency_penalty or 0.0),
                               repetition_penalty=float(self.repetition_penalty or 1.0),
-                              min_tokens=int(self.min_tokens or 0))
+                              min_tokens=int(self.min_tokens or 0),
+                              logit_bias=tuple((int(t), float(b)) for t, b in (self.logit_bias or {}).items()))
 
 
 class CompletionRequest(SamplingFields):

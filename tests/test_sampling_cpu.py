@@ -284,3 +284,19 @@ def test_min_tokens_holds_back_stop_tokens():
     assert held[0] == free[0]
     with pytest.raises(ValueError):
         SamplingParams(min_tokens=-1)
+
+
+def test_logit_bias_forces_and_bans_tokens():
+    from afd_plugin_b200.runtime.sampling import apply_penalties
+    from afd_plugin_b200.serving.api_server import CompletionRequest
+
+    logits = torch.tensor([[1.0, 2.0, 3.0]])
+    x = apply_penalties(logits, [SamplingParams(logit_bias=((0, 5.0), (2, -100.0)))], [[]], [[]])
+    assert torch.allclose(x, torch.tensor([[6.0, 2.0, -97.0]]))
+    eng = _engine()
+    out = eng.generate([[4, 4, 2]], 5, sampling=SamplingParams(logit_bias=((17, 100.0),)))[0]
+    assert out == [17] * 5
+    sp = CompletionRequest(prompt="x", logit_bias={"17": 100}).sampling()
+    assert sp.logit_bias == ((17, 100.0),) and sp.greedy
+    with pytest.raises(ValueError):
+        SamplingParams(logit_bias=((1, 101.0),))
