@@ -93,7 +93,7 @@ class SamplingFields(BaseModel):
                               ignore_eos=bool(self.ignore_eos), logprobs=lp,
                               presence_penalty=float(self.presence_penalty or 0.0),
                               frequency_penalty=float(self.frequency_penalty or 0.0),
-                              repetition_penalty=float(self.repetition_penalty or 1.0),
+                              repetition_penalty=1.0 if self.repetition_penalty is None else float(self.repetition_penalty),
                               min_tokens=int(self.min_tokens or 0),
                               logit_bias=tuple((int(t), float(b)) for t, b in (self.logit_bias or {}).items()))
 
@@ -105,6 +105,7 @@ class CompletionRequest(SamplingFields):
     model: str | None = None
     kv_transfer_params: dict | None = None
     stream: bool = False
+    echo: bool = False  # the returned text starts with the prompt
 
 
 class ChatMessage(BaseModel):
@@ -528,6 +529,9 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
         prefill_only = bool(params.get("do_remote_decode"))
         if n > 1 and (stream_req or prefill_only or params.get("do_remote_prefill")):
             raise HTTPException(status_code=400, detail="n > 1 is served without streaming or KV hand-off")
+        echo = bool(getattr(fields, "echo", False)) and not chat
+        if echo and stream_req:
+            raise HTTPException(status_code=400, detail="echo is served without streaming")
         stream = queue.Queue() if stream_req and not prefill_only else None
         try:
             stops = fields.stop_strings()
@@ -556,7 +560,8 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
                 c = {"index": i, "message": {"role": "assistant", "content": text}, "token_ids": out,
                      "finish_reason": reason}
             else:
-                c = {"index": i, "token_ids": out, "text": text, "finish_reason": reason}
+                c = {"index": i, "token_ids": out, "text": (tok.decode(ids) + text) if echo else text,
+                     "finish_reason": reason}
             if samplings[i] is not None and samplings[i].logprobs is not None:
                 c["logprobs"] = _logprobs_block(chat, out, getattr(f, "logprobs", ([], [])))
             choices.append(c)

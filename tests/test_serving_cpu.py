@@ -619,3 +619,22 @@ def test_openai_python_client_talks_to_the_server(server):
     text = "".join(ch.choices[0].delta.content or "" for ch in stream)
     assert text == chat.choices[0].message.content
     assert [m.id for m in client.models.list().data] == ["afd-b200"]
+
+
+def test_completion_echo_and_penalty_fields(server):
+    url, _ = server
+    prompt = [5, 9, 100, 7]
+    body = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 3, "echo": True},
+                         timeout=60).json()
+    want = _engine().generate([prompt], 3)[0]
+    assert body["choices"][0]["text"] == byte_detokenize(prompt) + byte_detokenize(want)
+    assert body["choices"][0]["token_ids"] == want
+    bad = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 3, "echo": True,
+                                                        "stream": True}, timeout=60)
+    assert bad.status_code == 400
+    forced = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 3,
+                                                           "logit_bias": {"17": 100}}, timeout=60).json()
+    assert forced["choices"][0]["token_ids"] == [17, 17, 17]
+    bad = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 3,
+                                                        "repetition_penalty": 0}, timeout=60)
+    assert bad.status_code == 400
