@@ -110,7 +110,21 @@ class CompletionRequest(SamplingFields):
 
 class ChatMessage(BaseModel):
     role: str
-    content: str
+    # a string, or OpenAI content parts ([{"type": "text", "text": ...}, ...]); text parts are joined
+    content: str | list[dict] | None = None
+
+    @property
+    def text(self) -> str:
+        if self.content is None:
+            return ""
+        if isinstance(self.content, str):
+            return self.content
+        parts = []
+        for part in self.content:
+            if part.get("type", "text") != "text":
+                raise ValueError(f"chat content part of type {part.get('type')!r} is not served (text only)")
+            parts.append(str(part.get("text", "")))
+        return "".join(parts)
 
 
 class ChatCompletionRequest(SamplingFields):
@@ -124,7 +138,7 @@ class ChatCompletionRequest(SamplingFields):
 
 def chat_prompt(messages: list[ChatMessage]) -> str:
     """Plain role-tagged transcript ending in the assistant tag (chat without a template)."""
-    return render_chat([{"role": m.role, "content": m.content} for m in messages])
+    return render_chat([{"role": m.role, "content": m.text} for m in messages])
 
 
 def byte_tokenize(text: str, vocab_size: int) -> list[int]:
@@ -670,7 +684,10 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
     @app.post("/v1/chat/completions")
     def chat_completions(req: ChatCompletionRequest):
-        ids = tok.encode_chat([{"role": m.role, "content": m.content} for m in req.messages])
+        try:
+            ids = tok.encode_chat([{"role": m.role, "content": m.text} for m in req.messages])
+        except ValueError as exc:
+            raise HTTPException(status_code=400, detail=str(exc)) from exc
         # no limit given: the rest of the context (the chat API has no default cap)
         max_tokens = req.max_completion_tokens or req.max_tokens or max(
             1, loop.engine.config.model_config.max_model_len - len(ids))

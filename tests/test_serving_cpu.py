@@ -638,3 +638,18 @@ def test_completion_echo_and_penalty_fields(server):
     bad = requests.post(url + "/v1/completions", json={"prompt": prompt, "max_tokens": 3,
                                                         "repetition_penalty": 0}, timeout=60)
     assert bad.status_code == 400
+
+
+def test_chat_content_parts_equal_plain_text(server):
+    url, _ = server
+    plain = requests.post(url + "/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": "hello there"}], "max_tokens": 4}, timeout=60).json()
+    parts = requests.post(url + "/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": [{"type": "text", "text": "hello "},
+                                                  {"type": "text", "text": "there"}]}], "max_tokens": 4},
+        timeout=60).json()
+    assert parts["choices"][0]["token_ids"] == plain["choices"][0]["token_ids"]
+    bad = requests.post(url + "/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": [{"type": "image_url", "image_url": {"url": "x"}}]}],
+        "max_tokens": 4}, timeout=60)
+    assert bad.status_code == 400
