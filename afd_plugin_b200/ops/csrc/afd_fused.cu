@@ -33,6 +33,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "device_state.h"
 #include "launchers.h"
 #include "routing.cuh"
 
@@ -635,7 +636,7 @@ void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s) {
   launch_pdl(dispatch_norm_kernel, dim3(p.T), dim3(kThreads), 0, s, p);
   if (!p.moe) return;
   const int mt = (p.T + kRouteTile - 1) / kRouteTile;
-  const int target = 148 * 2;
+  const int target = device_sm_count() * 2;
   if (mt * ((p.E + 7) / 8) <= target)
     launch_pdl(dispatch_router_kernel<1>, dim3(mt, (p.E + 7) / 8), dim3(kRouterThreads), 0, s, p);
   else if (mt * ((p.E + 15) / 16) <= target)
@@ -649,13 +650,13 @@ static int warp_grid(int items, int max_ctas) {
 }
 
 void launch_afd_expand(const ExpandParams& p, cudaStream_t s) {
-  launch_pdl(fused::expand_kernel, dim3(warp_grid(p.A * p.t_cap, 148)), dim3(fused::kThreads), 0, s, p);
+  launch_pdl(fused::expand_kernel, dim3(warp_grid(p.A * p.t_cap, device_sm_count())), dim3(fused::kThreads), 0, s, p);
 }
 
 void launch_afd_combine_send(const CombineSendParams& p, cudaStream_t s) {
-  launch_pdl(fused::combine_send_kernel, dim3(warp_grid(p.A * p.t_cap, 148)), dim3(fused::kThreads), 0, s, p);
+  launch_pdl(fused::combine_send_kernel, dim3(warp_grid(p.A * p.t_cap, device_sm_count())), dim3(fused::kThreads), 0, s, p);
 }
 
 void launch_afd_combine(const CombineParams& p, cudaStream_t s) {
-  launch_pdl(fused::combine_kernel, dim3(warp_grid(p.T, 148)), dim3(fused::kThreads), 0, s, p);
+  launch_pdl(fused::combine_kernel, dim3(warp_grid(p.T, device_sm_count())), dim3(fused::kThreads), 0, s, p);
 }

@@ -201,10 +201,12 @@ at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at:
   qo.out_sb = head_major ? 512 : (int64_t)H * 512;
   qo.out_sh = head_major ? (int64_t)B * 512 : 512;
   c10::cuda::CUDAGuard g(q_lat.device());
-  launch_mla_decode(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
-                    splits > 1 ? po.data_ptr<float>() : nullptr, splits > 1 ? pl.data_ptr<float>() : nullptr,
-                    status_ptr(q_lat), B, H, 512, 64, bs, nblocks, (int)block_table.stride(0), splits, (float)scale,
-                    stream());
+  const cudaError_t e =
+      launch_mla_decode(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                        splits > 1 ? po.data_ptr<float>() : nullptr, splits > 1 ? pl.data_ptr<float>() : nullptr,
+                        status_ptr(q_lat), B, H, 512, 64, bs, nblocks, (int)block_table.stride(0), splits,
+                        (float)scale, stream());
+  TORCH_CHECK(e == cudaSuccess, "mla_decode: launch failed: ", cudaGetErrorString(e));
   return out;
 }
 
@@ -509,6 +511,8 @@ void afd_expand(const at::Tensor& tok, const at::Tensor& rid, const at::Tensor& 
   }
   TORCH_CHECK(p.A <= 64 && p.k <= 16 && p.k + p.n_chunks <= 32 && p.H % 8 == 0,
               "afd_expand: at most 64 sources, k <= 16, k + shared chunks <= 32");
+  // a row's meta word packs source (8 bits), token (16 bits) and slot (8 bits)
+  TORCH_CHECK(p.t_cap >= 1 && p.t_cap <= 65535, "afd_expand: t_cap must be in [1, 65535] (16-bit token index)");
   if (flag.has_value() && flag->defined()) {
     TORCH_CHECK(epoch.has_value() && epoch->defined(), "afd_expand: a wait needs the epoch tensor");
     p.flag = reinterpret_cast<const uint64_t*>(flag->data_ptr()) + flag_index;
@@ -567,6 +571,7 @@ void afd_combine_send(const at::Tensor& staging, const at::Tensor& rid, const at
   }
   TORCH_CHECK(p.home_slots >= 0 && p.k + p.home_slots <= p.J, "afd_combine_send: home slots exceed J");
   TORCH_CHECK(p.A <= 64 && p.k <= 16 && p.J <= 32 && p.J >= p.k, "afd_combine_send: at most 64 sources, k <= J <= 32");
+  TORCH_CHECK(p.t_cap >= 1 && p.t_cap <= 65535, "afd_combine_send: t_cap must be in [1, 65535] (16-bit token index)");
   p.dst_ptrs = dst_ptrs.data_ptr<int64_t>();
   p.flag_ptrs = flag_ptrs.data_ptr<int64_t>();
   p.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());

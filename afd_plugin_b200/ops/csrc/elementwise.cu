@@ -2,6 +2,7 @@
 // routing top-k, KV-cache writes.  Every kernel moves 16-byte vectors and
 // computes in fp32.
 #include "common.cuh"
+#include "device_state.h"
 #include "launchers.h"
 #include "routing.cuh"
 
@@ -209,7 +210,8 @@ __global__ void gqa_cache_write_kernel(T* __restrict__ kc, T* __restrict__ vc, c
 
 static int grid_for(size_t work, int block) {
   size_t g = (work + block - 1) / block;
-  return (int)(g > 148 * 32 ? 148 * 32 : (g ? g : 1));
+  const size_t cap = (size_t)device_sm_count() * 32;
+  return (int)(g > cap ? cap : (g ? g : 1));
 }
 
 }  // namespace afd

@@ -25,6 +25,7 @@
 #include <cuda_fp8.h>
 
 #include "common.cuh"
+#include "device_state.h"
 #include "launchers.h"
 
 namespace afd {
@@ -670,12 +671,7 @@ static void encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 using namespace afd;
 
 int grouped_gemm_grid(int n_items) {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  }
+  const int sms = device_sm_count();
   return n_items < sms ? (n_items > 0 ? n_items : 1) : sms;
 }
 
@@ -692,11 +688,10 @@ void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* e
   const ScatterParams& spv = sp ? *sp : none;
   auto go = [&](auto epi_tag, int n_tiles, int ld) {
     constexpr int EPI = decltype(epi_tag)::value;
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(gg::grouped_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      set = true;
-    }
+    static PerDeviceOnce attr;
+    attr.run([&] {
+      return cudaFuncSetAttribute(gg::grouped_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
     const int grid = grouped_gemm_grid(n_tiles * e_local);
     launch_pdl(gg::grouped_gemm_kernel<EPI>, dim3(grid), dim3(gg::kThreads), (size_t)smem, s, wmap, amap,
                (__nv_bfloat16*)d, expert_offsets, expert_counts, n, w_stride, k, ld, n_tiles, e_local, status, spv);
@@ -732,11 +727,11 @@ void launch_grouped_gemm_w8(void* d, const void* a, const void* w, const float* 
   const ScatterParams& spv = sp ? *sp : none;
   auto go = [&](auto epi_tag, int n_tiles, int ld) {
     constexpr int EPI = decltype(epi_tag)::value;
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(gg::gg8::grouped_gemm_w8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      set = true;
-    }
+    static PerDeviceOnce attr;
+    attr.run([&] {
+      return cudaFuncSetAttribute(gg::gg8::grouped_gemm_w8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  smem);
+    });
     const int grid = grouped_gemm_grid(n_tiles * e_local);
     launch_pdl(gg::gg8::grouped_gemm_w8_kernel<EPI>, dim3(grid), dim3(gg::gg8::kThreads), (size_t)smem, s, wmap, amap, w_scale,
                (__nv_bfloat16*)d, expert_offsets, expert_counts, n, w_stride, k, ld, n_tiles, e_local, w_experts,

@@ -11,6 +11,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "device_state.h"
 #include "launchers.h"
 
 namespace afd {
@@ -276,11 +277,8 @@ void launch_gqa_decode(void* out, const void* q, const void* kc, const void* vc,
   gqa::encode_3d(&kmap, kc, num_blocks * block_size, hkv);
   gqa::encode_3d(&vmap, vc, num_blocks * block_size, hkv);
   const int smem = (int)sizeof(gqa::Smem) + 1024;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(gqa::gqa_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    set = true;
-  }
+  static PerDeviceOnce attr;
+  attr.run([&] { return cudaFuncSetAttribute(gqa::gqa_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); });
   gqa::gqa_decode_kernel<<<dim3(batch, hkv, num_splits), gqa::kThreads, smem, s>>>(
       kmap, vmap, (const __nv_bfloat16*)q, (__nv_bfloat16*)out, block_table, seq_lens, partial_o, partial_lse, status,
       hq, hkv, block_size, max_blocks_per_seq, num_splits, scale * 1.4426950408889634f);

@@ -45,10 +45,13 @@ struct MlaQO {
 };
 int mla_decode_num_splits(int batch, int max_seq_len, int num_sms);
 cudaError_t mla_decode_prepare_device();
-void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
-                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
-                       int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
-                       int num_splits, float scale, cudaStream_t s);
+// Returns cudaSuccess after launching, or an error with nothing launched: the
+// cache base is not 16-byte aligned (a TMA rule), the shared-memory opt-in
+// failed, or the cache's tensor map could not be encoded.
+cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
+                              const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
+                              int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
+                              int num_splits, float scale, cudaStream_t s);
 // Sparse (DeepSeek sparse attention) decode over keep_pos [B, num_keep] int32
 // (-1 or a position >= seq_lens[b] = unused entry); same outputs and scratch,
 // with splits over the kept entries.

@@ -30,6 +30,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "device_state.h"
 #include "launchers.h"
 
 namespace afd {
@@ -368,13 +369,14 @@ __global__ void mla_combine_kernel(const MlaQO qo, const float* __restrict__ par
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 PFN_cuTensorMapEncodeTiled_v12000 get_tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
     cudaDriverEntryPointQueryResult q;
     void* p = nullptr;
-    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
   return fn;
 }
 
@@ -394,32 +396,37 @@ int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
   return s > max_s ? max_s : s;
 }
 
-// Opts the decode kernel into its dynamic shared memory on the current device.
+// Opts the decode kernels into their dynamic shared memory on the current device.
 cudaError_t mla_decode_prepare_device() {
-  const int smem = (int)sizeof(mla::Smem) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(mla::mla_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(mla::mla_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  static PerDeviceOnce once;
+  return once.run([] {
+    const int smem = (int)sizeof(mla::Smem) + 1024;
+    cudaError_t e =
+        cudaFuncSetAttribute(mla::mla_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(mla::mla_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
 }
 
-void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
-                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
-                       int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
-                       int num_splits, float scale, cudaStream_t s) {
+cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
+                              const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
+                              int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
+                              int num_splits, float scale, cudaStream_t s) {
+  if ((reinterpret_cast<uintptr_t>(cache) & 15u) != 0) return cudaErrorMisalignedAddress;
+  cudaError_t e = mla_decode_prepare_device();
+  if (e != cudaSuccess) return e;
+  auto encode = get_tensor_map_encoder();
+  if (!encode) return cudaErrorNotSupported;
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)(L + R), (cuuint64_t)num_blocks * block_size};
   const cuuint64_t strides[1] = {(cuuint64_t)(L + R) * 2};
   const cuuint32_t box[2] = {mla::kBoxCols, mla::kTile};
   const cuuint32_t estr[2] = {1, 1};
-  get_tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(cache), dims, strides, box,
-                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(cache), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;  // the tensor map could not be encoded: launch nothing
   const int smem = (int)sizeof(mla::Smem) + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(mla::mla_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_set = true;
-  }
   dim3 grid(batch, heads / mla::kHeads, num_splits);
   const float scale_log2 = scale * 1.4426950408889634f;
   mla::mla_decode_kernel<false><<<grid, mla::kThreads, smem, s>>>(map, qo, block_table, seq_lens, partial_o, partial_lse,
@@ -428,6 +435,7 @@ void launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_
   if (num_splits > 1) {
     mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
   }
+  return cudaGetLastError();
 }
 
 void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t* block_table, const int32_t* seq_lens,
@@ -437,11 +445,7 @@ void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t*
   CUtensorMap unused;
   memset(&unused, 0, sizeof(unused));
   const int smem = (int)sizeof(mla::Smem) + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(mla::mla_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_set = true;
-  }
+  if (mla_decode_prepare_device() != cudaSuccess) return;
   dim3 grid(batch, heads / mla::kHeads, num_splits);
   const float scale_log2 = scale * 1.4426950408889634f;
   mla::mla_decode_kernel<true><<<grid, mla::kThreads, smem, s>>>(

@@ -77,8 +77,30 @@ int setup_device(int dev, DeviceSlot*& out) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+// The automatic split count: the torch op's pick, lowered until the partials
+// fit in the static scratch (1 = unsplit, which needs none).
+int auto_splits(int batch, int heads, int max_seq_len, int sms) {
+  int splits = mla_decode_num_splits(batch * (heads / 16), max_seq_len, sms);
+  const size_t row = (size_t)kLatent * sizeof(float) + sizeof(float);
+  const size_t max_rows = (kScratchBytes - 256) / row;
+  const size_t per_split = (size_t)batch * heads;
+  if (splits > 1 && (size_t)splits * per_split > max_rows) splits = (int)(max_rows / per_split);
+  while (splits > 1 && scratch_bytes(batch, heads, splits) > kScratchBytes) --splits;
+  return splits < 1 ? 1 : splits;
+}
 
 }  // namespace
+
+extern "C" int afd_mla_decode_noalloc_pick_splits(int batch, int heads, int max_seq_len) {
+  if (batch <= 0 || heads <= 0 || heads % 16 != 0 || max_seq_len <= 0) return 1;
+  int dev = -1;
+  int sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 1;
+  return auto_splits(batch, heads, max_seq_len, sms);
+}
 
 extern "C" uint64_t afd_mla_decode_noalloc_scratch_bytes(int batch, int heads, int num_splits) {
   if (batch <= 0 || heads <= 0) return 0;
@@ -102,6 +124,9 @@ extern "C" int afd_mla_decode_noalloc(const void* q_lat, int64_t lat_sb, int64_t
                 table_stride, max_blocks_per_seq);
   if (!aligned16(q_lat) || !aligned16(q_pe) || lat_sb % 8 || lat_sh % 8 || pe_sb % 8 || pe_sh % 8)
     return fail(AFD_NOALLOC_EINVAL, "q rows must be 16-byte aligned");
+  if (!aligned16(cache)) return fail(AFD_NOALLOC_EINVAL, "cache base must be 16-byte aligned (TMA source)");
+  if (!aligned4(out) || out_sb % 2 || out_sh % 2)
+    return fail(AFD_NOALLOC_EINVAL, "out must be 4-byte aligned with even strides (bf16 pairs are stored)");
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(AFD_NOALLOC_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
@@ -109,7 +134,7 @@ extern "C" int afd_mla_decode_noalloc(const void* q_lat, int64_t lat_sb, int64_t
   if (int rc = setup_device(dev, slot)) return rc;
 
   int splits = num_splits;
-  if (splits <= 0) splits = mla_decode_num_splits(batch * (heads / 16), max_blocks_per_seq * block_size, slot->sms);
+  if (splits <= 0) splits = auto_splits(batch, heads, max_blocks_per_seq * block_size, slot->sms);
   const size_t need = scratch_bytes(batch, heads, splits);
   if (need > kScratchBytes)
     return fail(AFD_NOALLOC_ETOOBIG,
@@ -132,9 +157,9 @@ extern "C" int afd_mla_decode_noalloc(const void* q_lat, int64_t lat_sb, int64_t
   qo.out = static_cast<__nv_bfloat16*>(out);
   qo.out_sb = out_sb;
   qo.out_sh = out_sh;
-  launch_mla_decode(qo, cache, block_table, seq_lens, po, pl, status ? status : slot->status, batch, heads, kLatent,
-                    kRope, block_size, num_blocks, table_stride, splits, scale, static_cast<cudaStream_t>(stream));
-  e = cudaGetLastError();
+  e = launch_mla_decode(qo, cache, block_table, seq_lens, po, pl, status ? status : slot->status, batch, heads,
+                        kLatent, kRope, block_size, num_blocks, table_stride, splits, scale,
+                        static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(AFD_NOALLOC_ECUDA, "launch: %s", cudaGetErrorString(e));
   return AFD_NOALLOC_OK;
 }

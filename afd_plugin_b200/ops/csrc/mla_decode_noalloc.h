@@ -29,8 +29,11 @@
 //     step reads is written earlier in the same call.  The status word
 //     (`status`, or the internal one) must read zero before a call for a
 //     non-zero value afterwards to mean that this call timed out.
-//   * A request whose partials would not fit in the scratch is rejected with
-//     AFD_NOALLOC_ETOOBIG and nothing is launched.
+//   * With num_splits <= 0 the split count is picked automatically and always
+//     fits: the pick is lowered until the partials fit in the scratch (down to
+//     one split, which needs none).  afd_mla_decode_noalloc_pick_splits says
+//     which count a call will use.  An explicit num_splits whose partials would
+//     not fit is rejected with AFD_NOALLOC_ETOOBIG and nothing is launched.
 #pragma once
 
 #include <stdint.h>
@@ -50,11 +53,14 @@ enum {
 
 // q_lat [batch, heads, 512] and q_pe [batch, heads, 64]: bf16, last dimension
 // contiguous, row strides (in elements) multiples of 8, 16-byte aligned bases.
-// out: bf16, element (b, h, c) at out + b * out_sb + h * out_sh + c.
-// cache [num_blocks, block_size, 576] bf16 contiguous; block_table int32 with
+// out: bf16, element (b, h, c) at out + b * out_sb + h * out_sh + c; the base
+// 4-byte aligned and out_sb, out_sh even (pairs of bf16 are stored together).
+// cache [num_blocks, block_size, 576] bf16 contiguous, base 16-byte aligned
+// (the kernel reads it with TMA); block_table int32 with
 // `table_stride` elements between rows and `max_blocks_per_seq` used columns;
 // seq_lens int32 [batch].  heads % 16 == 0, block_size % 32 == 0.
-// num_splits <= 0 picks the split count from the batch and the SM count.
+// num_splits <= 0 picks the split count from the batch, the context length
+// and the SM count, capped so the partials fit in the scratch.
 // status: device int that records a pipeline wait timeout, or NULL for the
 // internal per-device word (read it with afd_mla_decode_noalloc_status).
 // stream: a cudaStream_t (NULL = legacy default stream).
@@ -63,6 +69,10 @@ int afd_mla_decode_noalloc(const void* q_lat, int64_t lat_sb, int64_t lat_sh, co
                            int block_size, const int32_t* block_table, int table_stride, int max_blocks_per_seq,
                            const int32_t* seq_lens, int batch, int heads, int num_splits, float scale, void* stream,
                            int* status);
+
+// The split count a call with num_splits <= 0 uses on the current device for
+// this batch, head count and longest context (max_blocks_per_seq * block_size).
+int afd_mla_decode_noalloc_pick_splits(int batch, int heads, int max_seq_len);
 
 // Scratch bytes a call with these sizes needs (0 when it runs unsplit).
 uint64_t afd_mla_decode_noalloc_scratch_bytes(int batch, int heads, int num_splits);

@@ -6,6 +6,7 @@
 // moe_gather  xs[row] = x[row_token[row]]  (expert-sorted activations)
 // moe_combine out[t] = sum_j w[t, j] * ys[row(t, j)] (+ shared[t]), fp32 sums.
 #include "common.cuh"
+#include "device_state.h"
 #include "launchers.h"
 
 namespace afd {
@@ -130,7 +131,8 @@ void launch_moe_gather(void* xs, const void* x, const int32_t* row_token, int ro
   AFD_DTYPE_SWITCH(dtype, T, {
     const size_t work = (size_t)rows_cap * hidden / Vec16<T>::N;
     int grid = (int)((work + 255) / 256);
-    grid = grid > 148 * 16 ? 148 * 16 : (grid < 1 ? 1 : grid);
+    const int cap = device_sm_count() * 16;
+    grid = grid > cap ? cap : (grid < 1 ? 1 : grid);
     moe_gather_kernel<T><<<grid, 256, 0, s>>>((T*)xs, (const T*)x, row_token, rows_cap, hidden, total_rows);
   });
 }

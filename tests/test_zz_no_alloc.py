@@ -1,9 +1,10 @@
-"""Allocation-free MLA decode C entry point vs the torch op on the same kernels.
+"""Allocation-free MLA decode C entry point vs the torch op and an fp32 reference.
 
 Calls ``afd_mla_decode_noalloc`` through its exported C symbol (ctypes on the
 in-tree extension) and compares two calls in a row against
-``torch.ops.afd_b200.mla_decode``.  Collected last on purpose (file name), and
-also passes on its own.
+``torch.ops.afd_b200.mla_decode`` (same kernels, per-call scratch) and against
+the plain fp32 PyTorch reference (``ops/reference.py::mla_decode``).
+Collected last on purpose (file name), and also passes on its own.
 """
 
 import ctypes
@@ -13,6 +14,7 @@ import pytest
 import torch
 
 from afd_plugin_b200.ops import _ext
+from afd_plugin_b200.ops import reference as ref
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -27,6 +29,8 @@ def _lib():
     f.argtypes = [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i32, i32, vp, i32, i32, vp, i32, i32, i32,
                   ctypes.c_float, vp, vp]
     f.restype = i32
+    lib.afd_mla_decode_noalloc_pick_splits.argtypes = [i32, i32, i32]
+    lib.afd_mla_decode_noalloc_pick_splits.restype = i32
     lib.afd_mla_decode_noalloc_scratch_bytes.argtypes = [i32, i32, i32]
     lib.afd_mla_decode_noalloc_scratch_bytes.restype = ctypes.c_uint64
     lib.afd_mla_decode_noalloc_status.argtypes = [ctypes.POINTER(i32), i32]
@@ -84,7 +88,61 @@ def test_noalloc_matches_torch_op_twice(splits):
     for i in (0, 1, 2):
         want = C.mla_decode(qs[i][..., :512], qs[i][..., 512:], cache, table, seq, scale, splits, False)
         torch.testing.assert_close(outs[i].float(), want.float(), atol=1e-2, rtol=1e-2)
+        gold = ref.mla_decode(qs[i].float(), cache.float(), table, seq, scale, 512)
+        torch.testing.assert_close(outs[i].float(), gold, atol=2e-2, rtol=2e-2)
     assert lib.afd_mla_decode_noalloc_status(ctypes.byref(st), 0) == 0 and st.value == 0
+
+
+def test_noalloc_auto_split_fits_long_context():
+    """Batch 1 at a 32k context: the automatic split count stays within the scratch."""
+    torch.manual_seed(11)
+    lib = _lib()
+    C = _ext.ops()
+    lens = [32 * 1024 - 5]
+    cache, table, seq = _paged(1, lens)
+    scale = 1 / math.sqrt(192)
+    max_len = table.shape[1] * cache.shape[1]
+    splits = lib.afd_mla_decode_noalloc_pick_splits(1, 16, max_len)
+    assert splits >= 1
+    assert lib.afd_mla_decode_noalloc_scratch_bytes(1, 16, splits) <= 16 << 20
+    q = torch.randn(1, 16, 576, device=DEV, dtype=torch.bfloat16)
+    outs = [torch.empty(1, 16, 512, device=DEV, dtype=torch.bfloat16) for _ in range(2)]
+    for o in outs:
+        assert _call(lib, q, cache, table, seq, o, scale, 0) == 0, lib.afd_mla_decode_noalloc_last_error()
+    torch.cuda.synchronize()
+    want = C.mla_decode(q[..., :512], q[..., 512:], cache, table, seq, scale, splits, False)
+    gold = ref.mla_decode(q.float(), cache.float(), table, seq, scale, 512)
+    for o in outs:
+        torch.testing.assert_close(o.float(), want.float(), atol=1e-2, rtol=1e-2)
+        torch.testing.assert_close(o.float(), gold, atol=2e-2, rtol=2e-2)
+
+
+def test_noalloc_rejects_misaligned_pointers():
+    lib = _lib()
+    lens = [64, 64]
+    cache, table, seq = _paged(len(lens), lens)
+    q = torch.randn(2, 16, 576, device=DEV, dtype=torch.bfloat16)
+    out = torch.zeros(2, 16, 512, device=DEV, dtype=torch.bfloat16)
+    flat = cache.view(-1)
+    odd_cache = flat[4 : 4 + (cache.numel() - 8)].view(-1)  # base 8 bytes past a 16-byte boundary
+    B, H = 2, 16
+    q_lat, q_pe = q[..., :512], q[..., 512:]
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.afd_mla_decode_noalloc(q_lat.data_ptr(), q_lat.stride(0), q_lat.stride(1), q_pe.data_ptr(),
+                                    q_pe.stride(0), q_pe.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+                                    odd_cache.data_ptr(), cache.shape[0] - 1, cache.shape[1], table.data_ptr(),
+                                    table.stride(0), table.shape[1], seq.data_ptr(), B, H, 1, 0.1, stream, None)
+    assert rc == 1 and b"16-byte" in lib.afd_mla_decode_noalloc_last_error()
+    # head rows 515 elements apart (an odd stride) cannot take bf16 pairs
+    out_odd = torch.zeros(2, 16, 515, device=DEV, dtype=torch.bfloat16)
+    rc = lib.afd_mla_decode_noalloc(q_lat.data_ptr(), q_lat.stride(0), q_lat.stride(1), q_pe.data_ptr(),
+                                    q_pe.stride(0), q_pe.stride(1), out_odd.data_ptr(), out_odd.stride(0),
+                                    out_odd.stride(1), cache.data_ptr(), cache.shape[0], cache.shape[1],
+                                    table.data_ptr(), table.stride(0), table.shape[1], seq.data_ptr(), B, H, 1, 0.1,
+                                    stream, None)
+    assert rc == 1 and b"even strides" in lib.afd_mla_decode_noalloc_last_error()
+    torch.cuda.synchronize()
+    assert int(out.abs().sum()) == 0 and int(out_odd.abs().sum()) == 0, "a rejected call must launch nothing"
 
 
 def test_noalloc_rejects_oversized_split_scratch():
