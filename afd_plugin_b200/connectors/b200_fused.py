@@ -402,13 +402,13 @@ class FusedFFNRunner:
     """FFN-side step: expand (after a bounded arrival wait), tcgen05 grouped GEMMs, combine-send."""
 
     def __init__(self, model, connector: B200FusedAFDConnector, engine_config):
-        from afd_plugin_b200.runtime.cuda_graph import validate_cuda_graph_mode
+        from afd_plugin_b200.runtime.cuda_graph import graph_settings
 
         self.model = model
         self.c = connector
         self.config = engine_config
         self.device = model.device
-        self.use_cuda_graph = validate_cuda_graph_mode(engine_config, role="ffn").enabled
+        self.use_cuda_graph = graph_settings(engine_config, role="ffn").enabled
         d = connector.dims
         dev = self.device
         S, A, H = d.stages, d.num_attn, d.hidden
@@ -550,19 +550,19 @@ class FusedFFNRunner:
                 self._layer(layer, s)
 
     def execute_model(self, payload) -> None:
-        from afd_plugin_b200.runtime.cuda_graph import AFDGraphRunMode, graph_run_mode, make_capacity_graph_key
+        from afd_plugin_b200.runtime.cuda_graph import RunMode, capacity_graph_key, pick_run_mode
 
         stages = tuple(sorted(payload.dp_metadata_list))
-        key = make_capacity_graph_key(stages, self.c.dims.t_cap)
+        key = capacity_graph_key(stages, self.c.dims.t_cap)
         entry = self._graphs.get(key)
-        mode = graph_run_mode(is_warmup=payload.is_warmup, is_graph_capturing=payload.is_graph_capturing,
-                              is_graph_replaying=payload.is_graph_replaying, graph_enabled=self.use_cuda_graph,
-                              graph_exists=entry is not None)
+        mode = pick_run_mode(warmup=payload.is_warmup, capturing=payload.is_graph_capturing,
+                             replaying=payload.is_graph_replaying, graphs_on=self.use_cuda_graph,
+                             have_graph=entry is not None)
         self.steps += 1
-        if mode is AFDGraphRunMode.REPLAY:
+        if mode is RunMode.REPLAY:
             entry.replay()
             return
-        if mode is AFDGraphRunMode.CAPTURE and self.use_cuda_graph:
+        if mode is RunMode.CAPTURE and self.use_cuda_graph:
             g = torch.cuda.CUDAGraph()
             if self._pool is None:
                 self._pool = torch.cuda.graph_pool_handle()
@@ -571,7 +571,7 @@ class FusedFFNRunner:
                 self._step(stages)
             self._graphs[key] = g
             return
-        if self.count_next_eager and mode is AFDGraphRunMode.EAGER:
+        if self.count_next_eager and mode is RunMode.EAGER:
             from afd_plugin_b200.utils.launch_count import count_afd_kernels
 
             self.count_next_eager = False

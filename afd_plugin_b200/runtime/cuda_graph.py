@@ -1,13 +1,24 @@
-"""CUDA-graph policy for AFD roles (importable without torch).
+"""When the AFD roles run a decode step as a CUDA graph, and which graph (torch-free).
 
-Rules match ``afd_plugin/v1/worker/cuda_graph.py:42-150``: only
-``FULL_DECODE_ONLY`` is accepted; ubatching (DBO) with graphs needs exactly
-two ubatches; the FFN graph key is ``((stage, per-FFN-rank token counts), ...)``
-and the FFN run mode comes from the control payload flags.
+A decode step of this framework is one CUDA graph per role and step shape:
 
-The fused B200 connector keeps token counts on the device, so its FFN graphs
-are keyed by the stage set and the padded capacity only
-(:func:`make_capacity_graph_key`): one capture serves any routing.
+* Attention ranks capture one graph per padded batch size
+  (:func:`pad_to_capture_size`).
+* FFN ranks capture one graph per *key*.  The fused connector keeps token
+  counts in device memory and sizes every buffer by capacity, so its key is
+  the stage set and the capacity (:func:`capacity_graph_key`): one capture
+  serves any routing and any batch up to the capacity.  The NCCL connector
+  moves tensors whose shapes are the token counts, so its key is what each
+  FFN rank receives per stage (:func:`count_graph_key`).  That key keeps the
+  layout ``((stage, per-FFN-rank counts), ...)`` of the reference's FFN runner
+  (``afd_plugin/v1/worker/cuda_graph.py:104-133``), so the two stacks capture
+  one graph per distinct traffic pattern alike.
+
+Only ``FULL_DECODE_ONLY`` is accepted (the reference states the same rule,
+``afd_plugin/v1/worker/cuda_graph.py:42-85``): prefill runs eagerly.  DBO
+with graphs needs exactly two ubatches, because the captured step
+interleaves two ubatch generators.  The run mode of an FFN step follows the
+control payload's flags (:func:`pick_run_mode`).
 """
 
 from __future__ import annotations
@@ -17,132 +28,115 @@ from dataclasses import dataclass
 from enum import Enum
 from typing import Any
 
-FULL_DECODE_ONLY = "FULL_DECODE_ONLY"
-_SUPPORTED = frozenset({FULL_DECODE_ONLY})
+from afd_plugin_b200.runtime.ffn_metadata import aggregate_ffn_token_counts
+
+GRAPH_MODE = "FULL_DECODE_ONLY"
 
 
-class AFDGraphRunMode(str, Enum):
-    EAGER = "eager"
-    WARMUP = "warmup"
-    CAPTURE = "capture"
-    REPLAY = "replay"
+class RunMode(str, Enum):
+    EAGER = "eager"  # run the step's kernels directly
+    WARMUP = "warmup"  # eager, to initialise lazily created state before a capture
+    CAPTURE = "capture"  # record the step into a new graph
+    REPLAY = "replay"  # launch the recorded graph
 
 
 @dataclass(frozen=True, slots=True)
-class AFDCUDAGraphPolicy:
-    enabled: bool
-    mode_name: str | None
-    allow_attention_full_decode_only: bool
-    enable_ffn_graph_cache: bool
-    allow_cuda_graph_with_ubatching: bool = False
+class GraphSettings:
+    """What the engine configuration allows for one role."""
+
+    enabled: bool  # graphs at all (False under enforce_eager)
+    mode: str | None  # the configured graph mode's name
+    attention_graphs: bool  # this role captures Attention decode steps
+    ffn_graphs: bool  # this role keeps a cache of FFN step graphs
+    two_ubatches: bool = False  # the captured step interleaves two DBO ubatches
 
 
-def cudagraph_mode_name(config: Any) -> str | None:
-    mode = getattr(getattr(config, "compilation_config", None), "cudagraph_mode", None)
-    if mode is None:
+def graph_mode_name(config: Any) -> str | None:
+    """Name of ``config.compilation_config.cudagraph_mode`` (an enum, its name or its str form)."""
+    raw = getattr(getattr(config, "compilation_config", None), "cudagraph_mode", None)
+    if raw is None:
         return None
-    name = getattr(mode, "name", None)
-    if isinstance(name, str):
-        return name
-    text = str(mode)
-    return (text.rsplit(".", 1)[-1] if "." in text else text) or None
+    name = getattr(raw, "name", None)
+    if not isinstance(name, str):
+        name = str(raw)
+    return name.split(".")[-1] or None
 
 
-def validate_cuda_graph_mode(config: Any, *, role: str | None = None) -> AFDCUDAGraphPolicy:
-    eager = bool(getattr(config.model_config, "enforce_eager", False))
-    mode = cudagraph_mode_name(config)
-    if eager:
-        return AFDCUDAGraphPolicy(False, mode, False, False)
-    if mode not in _SUPPORTED:
-        suffix = f" for {role}" if role else ""
-        raise RuntimeError(f"AFD only supports CUDA graph mode {FULL_DECODE_ONLY}{suffix}; got {mode!r}.")
+def graph_settings(config: Any, *, role: str | None = None) -> GraphSettings:
+    """Checks the graph configuration of ``role`` ("attention", "ffn" or None for both).
+
+    Raises ``RuntimeError`` for a mode other than ``FULL_DECODE_ONLY`` or for
+    DBO with a ubatch count other than two, unless ``enforce_eager`` is set.
+    """
+    mode = graph_mode_name(config)
+    if getattr(config.model_config, "enforce_eager", False):
+        return GraphSettings(False, mode, False, False)
+    who = f"the {role} role" if role else "AFD"
+    if mode != GRAPH_MODE:
+        raise RuntimeError(f"CUDA graphs for {who} run only as {GRAPH_MODE} (got {mode!r}); "
+                           "set enforce_eager to run without graphs.")
     par = getattr(config, "parallel_config", None)
-    ubatching = bool(getattr(par, "use_ubatching", False))
-    n_ub = getattr(par, "num_ubatches", None)
-    ub_ok = ubatching and int(n_ub or 0) == 2
-    if ubatching and not ub_ok:
-        raise RuntimeError(
-            f"AFD CUDA graph support currently supports ubatching only for {FULL_DECODE_ONLY} with exactly two "
-            f"ubatches; got num_ubatches={n_ub!r}."
-        )
-    return AFDCUDAGraphPolicy(
+    ubatched = bool(getattr(par, "use_ubatching", False))
+    if ubatched:
+        n = getattr(par, "num_ubatches", None)
+        if int(n or 0) != 2:
+            raise RuntimeError(f"a captured DBO step for {who} interleaves exactly two ubatches "
+                               f"({GRAPH_MODE}); got num_ubatches={n!r}.")
+    return GraphSettings(
         enabled=True,
-        mode_name=mode,
-        allow_attention_full_decode_only=role in (None, "attention"),
-        enable_ffn_graph_cache=role in (None, "ffn"),
-        allow_cuda_graph_with_ubatching=ub_ok,
+        mode=mode,
+        attention_graphs=role in (None, "attention"),
+        ffn_graphs=role in (None, "ffn"),
+        two_ubatches=ubatched,
     )
 
 
-def _values(values: Any) -> tuple[int, ...]:
-    tolist = getattr(values, "tolist", None)
-    if callable(tolist):
-        values = tolist()
-    elif hasattr(values, "item"):
-        values = [values.item()]
-    try:
-        return tuple(int(v) for v in values)
-    except TypeError:
-        return (int(values),)
+def _stage_counts(meta: Any) -> tuple[int, ...]:
+    """Per-Attention-rank (or per-DP-rank) token counts carried by a stage's metadata."""
+    raw = getattr(meta, "num_tokens_across_dp_cpu", meta)
+    if raw is None:
+        return ()
+    if hasattr(raw, "tolist"):
+        raw = raw.tolist()
+    if isinstance(raw, (int, float)):
+        return (int(raw),)
+    return tuple(int(v) for v in raw)
 
 
-def _aggregated_key_applies(attention_size: int | None, ffn_size: int | None) -> bool:
-    return (
-        attention_size is not None
-        and ffn_size is not None
-        and int(attention_size) >= int(ffn_size)
-        and int(attention_size) % int(ffn_size) == 0
-    )
+def count_graph_key(stage_meta: Mapping[int, Any], *, attention_size: int | None = None,
+                    ffn_size: int | None = None) -> tuple:
+    """FFN graph key of the NCCL connector: ``((stage, counts), ...)`` in stage order.
+
+    With both sizes given, the counts are what each FFN rank receives (its
+    Attention peers' counts, an empty peer sending one placeholder row;
+    :func:`aggregate_ffn_token_counts`); otherwise they are the raw counts.
+    """
+    key = []
+    fold = bool(attention_size) and bool(ffn_size)
+    for stage in sorted(stage_meta):
+        counts = _stage_counts(stage_meta[stage])
+        if fold:
+            counts = aggregate_ffn_token_counts(counts, attention_size=int(attention_size), ffn_size=int(ffn_size))
+        key.append((int(stage), counts))
+    return tuple(key)
 
 
-def _aggregate(values: tuple[int, ...], *, attention_size: int, ffn_size: int, fallback: int) -> tuple[int, ...]:
-    expanded = values
-    if len(values) < attention_size and values and attention_size % len(values) == 0:
-        tp = attention_size // len(values)
-        expanded = tuple(values[i // tp] for i in range(attention_size))
-    if len(expanded) < attention_size:
-        return tuple(max(1, int(fallback)) for _ in range(ffn_size))
-    g = attention_size // ffn_size
-    return tuple(max(1, sum(expanded[i * g : (i + 1) * g])) for i in range(ffn_size))
-
-
-def make_ffn_graph_key(
-    dp_metadata_list: Mapping[int, object],
-    *,
-    attention_size: int | None = None,
-    ffn_size: int | None = None,
-    fallback: int = 1,
-) -> tuple:
-    parts = []
-    agg = _aggregated_key_applies(attention_size, ffn_size)
-    for stage, meta in sorted(dp_metadata_list.items()):
-        raw = getattr(meta, "num_tokens_across_dp_cpu", None)
-        if raw is None:
-            vals = tuple(max(1, int(fallback)) for _ in range(int(ffn_size))) if agg else (repr(meta),)
-        else:
-            vals = _values(raw)
-            if agg:
-                vals = _aggregate(vals, attention_size=int(attention_size), ffn_size=int(ffn_size),
-                                  fallback=int(fallback))
-        parts.append((int(stage), vals))
-    return tuple(parts)
-
-
-def make_capacity_graph_key(stages: tuple[int, ...], capacity: int) -> tuple:
-    """Graph key of the fused connector: counts live on the device."""
+def capacity_graph_key(stages: tuple[int, ...], capacity: int) -> tuple:
+    """FFN graph key of the fused connector: the stage set and the per-rank token capacity."""
     return ("capacity", tuple(sorted(int(s) for s in stages)), int(capacity))
 
 
-def graph_run_mode(
-    *, is_warmup: bool, is_graph_capturing: bool, is_graph_replaying: bool, graph_enabled: bool, graph_exists: bool
-) -> AFDGraphRunMode:
-    if is_warmup:
-        return AFDGraphRunMode.WARMUP
-    if is_graph_capturing:
-        return AFDGraphRunMode.CAPTURE
-    if is_graph_replaying and graph_enabled and graph_exists:
-        return AFDGraphRunMode.REPLAY
-    return AFDGraphRunMode.EAGER
+def pick_run_mode(*, warmup: bool, capturing: bool, replaying: bool, graphs_on: bool, have_graph: bool) -> RunMode:
+    """Run mode of an FFN step from the control payload's flags.
+
+    A warm-up or capture request wins over replay; a replay request without
+    a recorded graph (or with graphs off) runs eagerly.
+    """
+    if warmup:
+        return RunMode.WARMUP
+    if capturing:
+        return RunMode.CAPTURE
+    return RunMode.REPLAY if (replaying and graphs_on and have_graph) else RunMode.EAGER
 
 
 def pad_to_capture_size(num_tokens: int, capture_sizes: list[int] | tuple[int, ...]) -> int | None:
@@ -152,13 +146,13 @@ def pad_to_capture_size(num_tokens: int, capture_sizes: list[int] | tuple[int, .
 
 
 __all__ = [
-    "AFDCUDAGraphPolicy",
-    "AFDGraphRunMode",
-    "FULL_DECODE_ONLY",
-    "cudagraph_mode_name",
-    "graph_run_mode",
-    "make_capacity_graph_key",
-    "make_ffn_graph_key",
+    "GRAPH_MODE",
+    "GraphSettings",
+    "RunMode",
+    "capacity_graph_key",
+    "count_graph_key",
+    "graph_mode_name",
+    "graph_settings",
     "pad_to_capture_size",
-    "validate_cuda_graph_mode",
+    "pick_run_mode",
 ]

@@ -36,7 +36,7 @@ import torch
 import torch.distributed as dist
 
 from afd_plugin_b200.engine_config import EngineConfig
-from afd_plugin_b200.runtime.cuda_graph import pad_to_capture_size, validate_cuda_graph_mode
+from afd_plugin_b200.runtime.cuda_graph import graph_settings, pad_to_capture_size
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor, LocalFFNExecutor
 from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache, block_hashes
 from afd_plugin_b200.runtime.model_runner import ModelRunner
@@ -142,7 +142,7 @@ class LLMEngine:
         # Prefix caching shares KV blocks between prompts; recurrent (Gated
         # DeltaNet) state is per request, so hybrid models never share.
         self.prefix_caching = bool(getattr(cc, "enable_prefix_caching", False)) and not self.runner.has_linear_state
-        policy = validate_cuda_graph_mode(engine_config, role="attention")
+        policy = graph_settings(engine_config, role="attention")
         self.use_graphs = (policy.enabled and self.device.type == "cuda"
                            and getattr(self.ffn, "supports_graph_capture", True))
         self.capture_sizes = sorted(engine_config.compilation_config.cudagraph_capture_sizes) if self.use_graphs else []

@@ -3,8 +3,8 @@
 Per control payload the runner walks ``layers x stages``:
 ``recv_attn_output -> compute -> send_ffn_output`` -- the structure of
 ``GPUFFNModelRunner._ffn_forward`` (``afd_plugin/v1/worker/ffn_model_runner.py:167-247``).
-Graphs are cached by :func:`make_ffn_graph_key` and replayed when the
-Attention side replays (:func:`graph_run_mode`).
+Graphs are cached by :func:`count_graph_key` and replayed when the
+Attention side replays (:func:`pick_run_mode`).
 
 With several FFN ranks the routed experts are sharded (expert parallelism):
 for MoE layers each FFN rank gathers its peers' tokens, applies its local
@@ -24,10 +24,10 @@ import torch.distributed as dist
 
 from afd_plugin_b200.connectors.metadata import AFDControlPayload
 from afd_plugin_b200.runtime.cuda_graph import (
-    AFDGraphRunMode,
-    graph_run_mode,
-    make_ffn_graph_key,
-    validate_cuda_graph_mode,
+    RunMode,
+    count_graph_key,
+    graph_settings,
+    pick_run_mode,
 )
 from afd_plugin_b200.runtime.ffn_metadata import aggregate_ffn_token_counts
 
@@ -43,7 +43,7 @@ class FFNModelRunner:
         self.ep_size = ep_size
         self.ep_rank = ep_rank
         self.device = model.device
-        policy = validate_cuda_graph_mode(engine_config, role="ffn")
+        policy = graph_settings(engine_config, role="ffn")
         self.use_cuda_graph = policy.enabled and self.device.type == "cuda" and self._graph_capable()
         self._graphs: dict[tuple, dict[str, Any]] = {}
         self._pool = None
@@ -59,24 +59,24 @@ class FFNModelRunner:
     # ----------------------------------------------------------- stepping
     def execute_model(self, payload: AFDControlPayload) -> None:
         dpl = payload.dp_metadata_list
-        key = make_ffn_graph_key(dpl, attention_size=self.connector.attn_size, ffn_size=self.connector.ffn_size)
+        key = count_graph_key(dpl, attention_size=self.connector.attn_size, ffn_size=self.connector.ffn_size)
         entry = self._graphs.get(key)
-        mode = graph_run_mode(
-            is_warmup=payload.is_warmup,
-            is_graph_capturing=payload.is_graph_capturing,
-            is_graph_replaying=payload.is_graph_replaying,
-            graph_enabled=self.use_cuda_graph,
-            graph_exists=entry is not None,
+        mode = pick_run_mode(
+            warmup=payload.is_warmup,
+            capturing=payload.is_graph_capturing,
+            replaying=payload.is_graph_replaying,
+            graphs_on=self.use_cuda_graph,
+            have_graph=entry is not None,
         )
         self.steps += 1
-        if mode is AFDGraphRunMode.REPLAY:
+        if mode is RunMode.REPLAY:
             self.connector.control_plane.update_state_from_dp_metadata(payload)
             entry["graph"].replay()
             return
-        if mode is AFDGraphRunMode.CAPTURE and self.use_cuda_graph:
+        if mode is RunMode.CAPTURE and self.use_cuda_graph:
             self._capture(payload, key)
             return
-        if self.count_next_eager and mode is AFDGraphRunMode.EAGER and self.device.type == "cuda":
+        if self.count_next_eager and mode is RunMode.EAGER and self.device.type == "cuda":
             from afd_plugin_b200.utils.launch_count import count_afd_kernels
 
             self.count_next_eager = False

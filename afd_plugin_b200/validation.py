@@ -13,7 +13,7 @@ from __future__ import annotations
 from typing import Any
 
 from afd_plugin_b200.config import AFD_ASYNC_CONNECTOR, AFDConfig
-from afd_plugin_b200.runtime.cuda_graph import validate_cuda_graph_mode
+from afd_plugin_b200.runtime.cuda_graph import graph_settings
 
 AFD_ATTENTION_WORKER_QUALNAME = "afd_plugin_b200.runtime.workers.AFDAttentionWorker"
 AFD_FFN_WORKER_QUALNAME = "afd_plugin_b200.runtime.workers.AFDFFNWorker"
@@ -51,7 +51,7 @@ def assert_compatible_afd_stack(engine_config: Any, afd: AFDConfig, *, worker_cl
         raise ValueError("AFD async DP (CAMAsyncAFDConnector) is Ascend-only and unavailable on B200")
     if bool(getattr(par, "use_ubatching", False)) and int(getattr(par, "num_ubatches", 0)) != 2:
         raise ValueError("AFD DBO requires exactly two ubatches")
-    validate_cuda_graph_mode(engine_config, role=afd.role)
+    graph_settings(engine_config, role=afd.role)
     arch = engine_config.model_config.hf_config
     if arch.architecture.startswith("Qwen3") and afd.compute_gate_on_attention:
         raise ValueError("Qwen3-MoE AFD supports compute_gate_on_attention=false only")

@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from afd_plugin_b200.connectors.metadata import AFDControlPayload, AFDDPMetadata, AFDExpertRoutingSpec
-from afd_plugin_b200.runtime.cuda_graph import make_ffn_graph_key
+from afd_plugin_b200.runtime.cuda_graph import count_graph_key
 from afd_plugin_b200.runtime.ffn_runner import FFNModelRunner
 
 H = 8
@@ -163,7 +163,7 @@ def test_replay_uses_cached_graph_without_touching_the_connector():
     runner = FFNModelRunner(model, conn, _cfg())
     runner.use_cuda_graph = True
     p = _payload(replaying=True)
-    key = make_ffn_graph_key(p.dp_metadata_list, attention_size=conn.attn_size, ffn_size=conn.ffn_size)
+    key = count_graph_key(p.dp_metadata_list, attention_size=conn.attn_size, ffn_size=conn.ffn_size)
     g = FakeGraph()
     runner._graphs[key] = {"graph": g}
     runner.execute_model(p)
@@ -178,7 +178,7 @@ def test_replay_without_graph_or_with_other_key_runs_eagerly():
     runner.use_cuda_graph = True
     g = FakeGraph()
     other = _payload(counts=(5, 5))
-    runner._graphs[make_ffn_graph_key(other.dp_metadata_list, attention_size=2, ffn_size=1)] = {"graph": g}
+    runner._graphs[count_graph_key(other.dp_metadata_list, attention_size=2, ffn_size=1)] = {"graph": g}
     runner.execute_model(_payload(replaying=True))
     assert g.replays == 0
     assert len([e for e in conn.events if e[0] == "recv"]) == 3

@@ -13,12 +13,12 @@ from afd_plugin_b200.connectors.metadata import (
     encode_control_payload,
 )
 from afd_plugin_b200.runtime.cuda_graph import (
-    AFDGraphRunMode,
-    graph_run_mode,
-    make_capacity_graph_key,
-    make_ffn_graph_key,
+    RunMode,
+    capacity_graph_key,
+    count_graph_key,
+    graph_settings,
     pad_to_capture_size,
-    validate_cuda_graph_mode,
+    pick_run_mode,
 )
 from afd_plugin_b200.runtime.ffn_metadata import aggregate_ffn_token_counts, project_ffn_token_counts_to_dp
 
@@ -77,14 +77,21 @@ def test_ffn_counts():
 
 def test_graph_key_and_modes():
     dpl = {1: AFDDPMetadata([1, 2, 3, 4]), 0: AFDDPMetadata([0, 0, 5, 5])}
-    assert make_ffn_graph_key(dpl) == ((0, (0, 0, 5, 5)), (1, (1, 2, 3, 4)))
-    assert make_ffn_graph_key(dpl, attention_size=4, ffn_size=2) == ((0, (1, 10)), (1, (3, 7)))
-    assert make_capacity_graph_key((1, 0), 64) == ("capacity", (0, 1), 64)
-    kw = dict(is_warmup=False, is_graph_capturing=False, is_graph_replaying=True, graph_enabled=True)
-    assert graph_run_mode(graph_exists=True, **kw) is AFDGraphRunMode.REPLAY
-    assert graph_run_mode(graph_exists=False, **kw) is AFDGraphRunMode.EAGER
-    assert graph_run_mode(is_warmup=True, is_graph_capturing=True, is_graph_replaying=True,
-                          graph_enabled=True, graph_exists=True) is AFDGraphRunMode.WARMUP
+    assert count_graph_key(dpl) == ((0, (0, 0, 5, 5)), (1, (1, 2, 3, 4)))
+    # each FFN rank receives its two peers' rows; an empty peer sends one placeholder row
+    assert count_graph_key(dpl, attention_size=4, ffn_size=2) == ((0, (2, 10)), (1, (3, 7)))
+    # counts given per DP rank are expanded over TP peers (DP 2 x TP 2 = 4 Attention ranks)
+    assert count_graph_key({0: AFDDPMetadata([3, 4])}, attention_size=4, ffn_size=2) == ((0, (6, 8)),)
+    assert capacity_graph_key((1, 0), 64) == ("capacity", (0, 1), 64)
+    kw = dict(warmup=False, capturing=False, replaying=True, graphs_on=True)
+    assert pick_run_mode(have_graph=True, **kw) is RunMode.REPLAY
+    assert pick_run_mode(have_graph=False, **kw) is RunMode.EAGER
+    assert pick_run_mode(warmup=False, capturing=False, replaying=True, graphs_on=False,
+                         have_graph=True) is RunMode.EAGER
+    assert pick_run_mode(warmup=True, capturing=True, replaying=True, graphs_on=True,
+                         have_graph=True) is RunMode.WARMUP
+    assert pick_run_mode(warmup=False, capturing=True, replaying=False, graphs_on=True,
+                         have_graph=False) is RunMode.CAPTURE
     assert pad_to_capture_size(5, [8, 4, 16]) == 8 and pad_to_capture_size(17, [8, 16]) is None
 
 
@@ -95,13 +102,13 @@ def _cfg(eager=False, mode="FULL_DECODE_ONLY", ub=False, n=1):
 
 
 def test_graph_policy():
-    assert not validate_cuda_graph_mode(_cfg(eager=True)).enabled
-    p = validate_cuda_graph_mode(_cfg(ub=True, n=2), role="ffn")
-    assert p.enabled and p.enable_ffn_graph_cache and not p.allow_attention_full_decode_only
-    assert p.allow_cuda_graph_with_ubatching
-    with pytest.raises(RuntimeError):
-        validate_cuda_graph_mode(_cfg(mode="PIECEWISE"))
-    with pytest.raises(RuntimeError):
-        validate_cuda_graph_mode(_cfg(ub=True, n=3))
+    assert not graph_settings(_cfg(eager=True)).enabled
+    p = graph_settings(_cfg(ub=True, n=2), role="ffn")
+    assert p.enabled and p.ffn_graphs and not p.attention_graphs and p.two_ubatches
+    with pytest.raises(RuntimeError, match="FULL_DECODE_ONLY"):
+        graph_settings(_cfg(mode="PIECEWISE"))
+    with pytest.raises(RuntimeError, match="two ubatches"):
+        graph_settings(_cfg(ub=True, n=3))
     enum_like = SimpleNamespace(name="FULL_DECODE_ONLY")
-    assert validate_cuda_graph_mode(_cfg(mode=enum_like)).mode_name == "FULL_DECODE_ONLY"
+    assert graph_settings(_cfg(mode=enum_like)).mode == "FULL_DECODE_ONLY"
+    assert graph_settings(_cfg(mode="CUDAGraphMode.FULL_DECODE_ONLY")).enabled
