@@ -69,29 +69,10 @@ def parse_args(argv=None):
 
 # ---------------------------------------------------------------- reference
 def reference_arm(args) -> None:
-    """Run the unmodified reference if its stack can run here, else say why."""
-    ref_dir = os.path.join(ROOT, "baseline", "_ref")
-    reason = None
-    if not os.path.isdir(os.path.join(ref_dir, "afd_plugin")):
-        reason = "reference not installed under baseline/_ref"
-    else:
-        try:
-            import vllm  # noqa: F401
-            import vllm.model_executor.models.deepseek_v2 as native
+    """The unmodified reference (``baseline/_ref``) on its stock path: ``bench_reference.py``."""
+    import bench_reference
 
-            ver = getattr(vllm, "__version__", "?")
-            if not hasattr(native, "_get_moe_router_dtype"):
-                reason = (f"reference pins vLLM 0.26.0 (afd_plugin/compat/vllm.py:12); installed vLLM {ver} lacks "
-                          "deepseek_v2._get_moe_router_dtype, which the reference's DeepSeek-V2 Attention role "
-                          "calls at construction (model_executor/models/deepseek_v2.py:261)")
-            elif not ver.startswith("0.26"):
-                reason = f"reference requires vLLM 0.26.0, found {ver}"
-        except Exception as exc:  # noqa: BLE001
-            reason = f"vLLM import failed: {type(exc).__name__}: {exc}"
-    if reason is None:
-        reason = "reference serving stack (vllm serve + AFD plugin, 8 processes) not wired into bench.py"
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": reason}))
+    bench_reference.main(args, METRIC, MODEL_DESC.get(args.model, args.model))
 
 
 # ------------------------------------------------------------------ helpers
