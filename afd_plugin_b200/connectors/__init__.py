@@ -7,11 +7,8 @@ from afd_plugin_b200.connectors.metadata import (
     AFDControlPayload,
     AFDDPMetadata,
     AFDExpertRoutingSpec,
-    AFDF2ATransferPayload,
-    AFDForwardContextMetadata,
     AFDTransferContext,
     AFDTransferMetadata,
-    AFDTransferState,
 )
 
 __all__ = [
@@ -22,10 +19,7 @@ __all__ = [
     "AFDControlPlane",
     "AFDDPMetadata",
     "AFDExpertRoutingSpec",
-    "AFDF2ATransferPayload",
-    "AFDForwardContextMetadata",
     "AFDTransferContext",
     "AFDTransferMetadata",
-    "AFDTransferState",
     "ConnectorExtraInfo",
 ]

@@ -3,11 +3,11 @@
 from types import SimpleNamespace
 
 import pytest
+import torch
 
 from afd_plugin_b200.connectors.metadata import (
     AFDControlPayload,
     AFDDPMetadata,
-    AFDForwardContextMetadata,
     AFDTransferMetadata,
     decode_control_payload,
     encode_control_payload,
@@ -40,14 +40,10 @@ def test_shutdown_flag_roundtrip():
     assert decode_control_payload(encode_control_payload(p)).is_shutdown
 
 
-def test_dp_metadata_sp_helpers():
+def test_dp_metadata_peak():
     m = AFDDPMetadata([5, 3])
-    with m.sp_local_sizes(2) as sizes:
-        assert sizes == [3, 3, 2, 2]
-    assert m.local_sizes is None
-    assert m.cu_tokens_across_sp(2).tolist() == [3, 6, 8, 10]
-    with m.chunked_sizes(2, 2, 1) as sizes:
-        assert sizes == [1, 1, 1, 1]
+    assert m.num_tokens_across_dp_cpu.dtype == torch.int32 and int(m.max_tokens_across_dp_cpu) == 5
+    assert int(AFDDPMetadata([]).max_tokens_across_dp_cpu) == 0
 
 
 def test_transfer_metadata():
@@ -57,13 +53,6 @@ def test_transfer_metadata():
         AFDTransferMetadata(0, 0, [])
     with pytest.raises(ValueError):
         AFDTransferMetadata(0, 0, [0])
-
-
-def test_forward_context_clone_is_deep_for_lists():
-    m = AFDForwardContextMetadata([0], [0], 0, connector=None, tokens_lens=[4], num_stages=1)
-    c = m.clone()
-    c.tokens_lens.append(1)
-    assert m.tokens_lens == [4]
 
 
 def test_ffn_counts():
