@@ -42,7 +42,8 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         with ClockSampler(local) as clk:
             n = w.run_ffn_server_loop()
         result.update(ms=0.0, per_step=[0.0], clocks=clk.summary(), steps_served=n,
-                      launches_local=w.model_runner.kernels_per_step * args.steps)
+                      launches_local=w.model_runner.kernels_per_step * args.steps,
+                      phases=getattr(getattr(w.model_runner, "timer", None), "summary", dict)())
         w.shutdown()
     else:
         from afd_plugin_b200.runtime.workers import AFDAttentionWorker
@@ -68,7 +69,7 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
                 e2e_ms, h2d, d2h = e2e_loop(eng, args.warmup, args.steps)
                 e2e = (e2e_ms, h2d, d2h)
         result.update(ms=ms, per_step=per_step, clocks=clk.summary(), e2e_raw=e2e, batch=batch,
-                      launches_local=per_step_kernels * args.steps)
+                      launches_local=per_step_kernels * args.steps, phases=eng.runner.timer.summary())
         log("timed loops done")
         if barrier is not None:
             barrier()
@@ -90,6 +91,11 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
         result["e2e"] = {"value": round(args.batch * args.steps / (float(mx[1]) / 1e3), 1), "unit": "tok/s",
                          "h2d_bytes_per_step": int(sm[1]), "d2h_bytes_per_step": int(sm[2])}
     result["launches"] = int(sm[0])
+    if args.phases:
+        every = [None] * dist.get_world_size()
+        dist.all_gather_object(every, {"rank": rank, "role": role, "role_rank": role_rank,
+                                       "phases": result.get("phases", {})})
+        result["phases"] = every
     dist.barrier()
     dist.destroy_process_group()
     return result

@@ -16,10 +16,13 @@ import os
 
 import torch
 
-# name: (local experts, hidden, intermediate, tokens per expert)
+# name: (local experts, hidden, intermediate, tokens per expert[, shared chunks, rows per shared chunk])
 SHAPES = {
     "dsv2-lite-f2": (32, 2048, 1408, 24),     # DeepSeek-V2-Lite, 6A2F: 256 tokens x top-6 over 64 experts
     "dsv2-lite-f1": (64, 2048, 1408, 24),     # DeepSeek-V2-Lite, one FFN rank holds every expert
+    # one GPU, 256-token decode batch: 64 routed experts plus the 2 shared-expert
+    # chunks (virtual experts of the routed width) that see every token
+    "dsv2-lite-colo": (64, 2048, 1408, 24, 2, 256),
     "qwen3-30b-f4": (32, 2048, 768, 32),      # Qwen3-30B-A3B, 4A4F: 512 tokens x top-8 over 128 experts
     "dsv3-f4": (64, 7168, 2048, 16),          # DeepSeek-V3 shapes, 4A4F: 512 tokens x top-8 over 256 experts
 }
@@ -67,18 +70,21 @@ def run(shape: str, reps: int, tokens_per_expert: int | None = None, fp8: bool =
     from afd_plugin_b200.ops import _ext
 
     C = _ext.ops()
-    E, H, I, tpe = SHAPES[shape]
+    E, H, I, tpe, *shared = SHAPES[shape]
     tpe = tokens_per_expert or tpe
     dev = "cuda"
-    rows = E * tpe
-    counts = torch.full((E,), tpe, dtype=torch.int32, device=dev)
-    offsets = (torch.arange(E, dtype=torch.int32, device=dev) * tpe).contiguous()
+    per = [tpe] * E + ([shared[1]] * shared[0] if shared else [])
+    E = len(per)
+    rows = sum(per)
+    counts = torch.tensor(per, dtype=torch.int32, device=dev)
+    offsets = torch.zeros(E, dtype=torch.int32, device=dev)
+    offsets[1:] = counts.cumsum(0)[:-1]
     a1 = (torch.randn(rows, H, device=dev) * 0.1).to(torch.bfloat16)
     w13 = (torch.randn(E, 2 * I, H, device=dev) * 0.02).to(torch.bfloat16)
     a2 = (torch.randn(rows, I, device=dev) * 0.1).to(torch.bfloat16)
     w2 = (torch.randn(E, H, I, device=dev) * 0.02).to(torch.bfloat16)
     peak, kind = _peak_gbs()
-    out = {"shape": shape, "experts": E, "hidden": H, "intermediate": I, "tokens_per_expert": tpe,
+    out = {"shape": shape, "experts": E, "hidden": H, "intermediate": I, "tokens_per_expert": tpe, "rows": rows,
            "weights": "fp8 e4m3, 128x128 block scales" if fp8 else "bf16"}
     if fp8:
         q13, s13 = _quant(w13)
@@ -89,9 +95,14 @@ def run(shape: str, reps: int, tokens_per_expert: int | None = None, fp8: bool =
             ("gemm2", lambda: C.grouped_gemm_w8(a2, q2, s2, offsets, counts, 0, E), q2.numel() + s2.numel() * 4),
         )
     else:
+        from afd_plugin_b200.ops.moe import moe_sync_buffer
+
+        sync = moe_sync_buffer(torch.device(dev), E)
         cases = (
             ("gemm1_swiglu", lambda: C.grouped_gemm_ex(a1, w13, offsets, counts, 1, -1), w13.numel() * 2),
             ("gemm2", lambda: C.grouped_gemm_ex(a2, w2, offsets, counts, 0, -1), w2.numel() * 2),
+            # both projections in one two-phase launch (what the MoE layers run)
+            ("moe_ffn", lambda: C.moe_ffn(a1, w13, w2, offsets, counts, sync), (w13.numel() + w2.numel()) * 2),
         )
     for name, fn, wbytes in cases:
         us = _time_us(fn, reps)

@@ -1,0 +1,72 @@
+"""Paged MLA decode kernel at decode-step shapes: device time and KV bandwidth.
+
+Decode attention reads every cached latent row once per step (576 bf16 = 1152
+bytes per token and layer); the figure of merit is those bytes per second
+against the measured HBM copy bandwidth (``MEASURED_PEAKS.json`` at the
+repository root, when present).  The cache is larger than L2 (126 MB), so
+consecutive launches read it from HBM.
+
+    python -m afd_plugin_b200.bench.mla_decode_bench [--shapes dsv2-lite-b256,...] [--reps 3]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from afd_plugin_b200.bench.grouped_gemm_bench import _peak_gbs
+
+# name: (batch, heads, context tokens)
+SHAPES = {
+    "dsv2-lite-b256": (256, 16, 1034),   # the 1-GPU decode step: 256 requests, ~1 K context
+    "dsv2-lite-b43": (43, 16, 1034),     # one Attention rank of 6A2F
+    "dsv3-b64": (64, 128, 2100),         # DeepSeek-V3 heads, one Attention rank of 4A4F
+}
+
+
+def run(shape: str, reps: int, bs: int = 64) -> dict:
+    from afd_plugin_b200.ops import _ext
+
+    C = _ext.ops()
+    B, H, ctx = SHAPES[shape]
+    dev = "cuda"
+    nblk = math.ceil(ctx / bs)
+    cache = torch.randn(B * nblk + 1, bs, 576, device=dev, dtype=torch.bfloat16)
+    table = (torch.randperm(B * nblk, device=dev).view(B, nblk) + 1).to(torch.int32)
+    seq = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(B, H, 576, device=dev, dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(192)
+    fn = lambda: C.mla_decode(q[..., :512], q[..., 512:], cache, table, seq, scale, 0, False)  # noqa: E731
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    ev[0].record()
+    for i in range(reps):
+        fn()
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    us = sorted(ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(reps))
+    med = us[len(us) // 2]
+    kv_bytes = B * ctx * 576 * 2
+    peak, kind = _peak_gbs()
+    gbs = kv_bytes / (med * 1e-6) / 1e9
+    return {"shape": shape, "batch": B, "heads": H, "context": ctx, "us_median": round(med, 2),
+            "kv_GBps": round(gbs, 1), f"frac_of_{kind}_hbm": round(gbs / peak, 3),
+            "status": int(C.read_status(torch.cuda.current_device()))}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--shapes", default=",".join(SHAPES))
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args(argv)
+    for shape in args.shapes.split(","):
+        print(json.dumps(run(shape, args.reps)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

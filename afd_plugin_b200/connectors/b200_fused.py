@@ -385,6 +385,10 @@ class FusedAttentionExecutor(FFNExecutor):
     def recv(self, layer_idx, handle, stage_idx):
         T, residual = handle
         c, d = self.c, self.c.dims
+        if self.timer.enabled:  # split the wait for the FFN ranks from the combine itself
+            torch.ops.afd_b200.afd_wait(c.comb_flag[stage_idx], layer_idx, c.epoch[stage_idx : stage_idx + 1],
+                                        d.num_ffn, c.timeout_ns)
+            self.timer.mark("ffn_wait")
         out = torch.ops.afd_b200.afd_combine(
             c.comb[stage_idx], c.fmask[stage_idx], T, c.comb_flag[stage_idx], layer_idx,
             c.epoch[stage_idx : stage_idx + 1], d.num_ffn, c.timeout_ns)
@@ -444,6 +448,9 @@ class FusedFFNRunner:
         self.meta_shared = torch.cat([((self.home_a0 + i) << 24) | (t << 8) | d.top_k for i in range(d.ratio)]).to(dev)
         self.rw_shared = torch.ones(d.ratio * d.t_cap, dtype=torch.float32, device=dev)
         self.no_flags = torch.zeros(1, dtype=torch.int64, device=dev)
+        from afd_plugin_b200.ops.moe import moe_sync_buffer
+
+        self.sync = moe_sync_buffer(dev, d.e_local + self.n_chunks)
         self._graphs: dict = {}
         self._pool = None
         self._prepare_weights()
@@ -451,6 +458,9 @@ class FusedFFNRunner:
         # Set by benchmarks: count the kernels of the next eager step.
         self.count_next_eager = False
         self.kernels_per_step = 0
+        from afd_plugin_b200.utils.phase_timer import NULL_TIMER, PhaseTimer, phase_timing_requested
+
+        self.timer = PhaseTimer(dev) if phase_timing_requested() else NULL_TIMER
 
     def _prepare_weights(self) -> None:
         """Per layer: routed (w13, w2) and the home-token weights (shared experts or dense MLP)."""
@@ -497,6 +507,10 @@ class FusedFFNRunner:
         merged = is_moe and self.n_chunks > 0
         counts = self.counts[s]
         n_chunks = self.n_chunks if merged else 0
+        timer = self.timer
+        if timer.enabled:  # split the wait for the Attention ranks from the expand copy
+            C.afd_wait(c.arrive[s], layer_idx, c.epoch[s : s + 1], A, c.timeout_ns)
+            timer.mark("arrive_wait")
         # expand waits (bounded) for every Attention rank's arrival first
         C.afd_expand(c.tok[s], c.rid[s], c.rwt[s], c.tcount[s], self.x[s], self.meta[s], self.rw[s], counts,
                      [A, d.t_cap, d.top_k, d.e_local, self.e_offset, d.cap, d.ratio, self.home_a0, int(is_moe),
@@ -518,8 +532,14 @@ class FusedFFNRunner:
             for ch in range(n_chunks):
                 lo = self.shared_base + ch * span
                 self.rw[s][lo : lo + span].copy_(g)
-        if merged:
-            # routed experts and shared-expert chunks in one GEMM per projection
+        if merged and w13.dtype == torch.bfloat16:
+            # routed experts and shared-expert chunks: gate_up -> SwiGLU -> down
+            # in one persistent launch whose epilogue scatters into staging
+            ne = d.e_local + n_chunks
+            total = int(C.moe_ffn_grid(ne, w13.shape[1], w2.shape[1]))
+            C.moe_ffn(self.x[s], w13, w2, self.off_all, counts[:ne], self.sync, -1, self.meta[s], self.rw[s],
+                      self.staging_ptrs[s], self.no_flags, c.done[s, 1:2], counts, [self.J, H, total, 0, layer_idx])
+        elif merged:
             ne = d.e_local + n_chunks
             h_r = C.grouped_gemm_ex(self.x[s], w13, self.off_all, counts[:ne], 1, ne)
             launches.append((h_r, w2, self.off_all, counts[:ne], ne, self.meta[s], self.rw[s], None))
@@ -530,21 +550,25 @@ class FusedFFNRunner:
             h_s = gemm1(home_rows, sw13, ss13, self.off_shared, counts[d.e_local : d.e_local + d.ratio], 1)
             launches.append((h_s, sw2, self.off_shared, counts[d.e_local : d.e_local + d.ratio], 1, self.meta_shared,
                              self.rw_shared, ss2))
+        timer.mark("expand")
         total = sum(int(C.grouped_gemm_grid((H // 128) * int(ln[3].numel()))) for ln in launches)
         for h, w, off, cnt, wexp, meta, rw, scale in launches:
             # Expert outputs land in local staging slots; the last CTA clears the counters.
             C.grouped_gemm_scatter(h, w, off, cnt, wexp, meta, rw, self.staging_ptrs[s], self.no_flags,
                                    c.done[s, 1:2], counts, [self.J, H, total, 0, layer_idx], scale)
+        timer.mark("experts")
         has_home = merged or sw13 is not None
         C.afd_combine_send(self.staging[s], c.rid[s], c.rwt[s], c.tcount[s], c.comb_ptrs[s], c.comb_flag_ptrs[s],
                            c.done[s, 2:3], H,
                            [A, d.t_cap, d.top_k, self.J, d.e_local, self.e_offset, d.ratio, self.home_a0,
                             int(is_moe), int(has_home), self.f_rank, d.num_ffn, layer_idx, 0,
                             n_chunks if merged else 1])
+        timer.mark("combine_send")
 
     def _step(self, stages) -> None:
         for s in stages:
             torch.ops.afd_b200.afd_epoch(self.c.epoch[s : s + 1])
+        self.timer.begin_step()
         for layer in range(self.model.num_layers):
             for s in stages:
                 self._layer(layer, s)

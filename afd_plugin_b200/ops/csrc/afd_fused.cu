@@ -191,6 +191,9 @@ AFD_DEVICE void unpack_e4m3x16(uint4 raw, float scale, Vec16<bf16>& a, Vec16<bf1
 
 __global__ void epoch_kernel(uint64_t* epoch) { *epoch += 1; }
 
+// Phase timing: the device clock when the stream reaches this point.
+__global__ void stamp_kernel(uint64_t* buf, int idx) { buf[idx] = globaltimer_ns(); }
+
 __global__ void wait_kernel(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns,
                             int* status) {
   if (threadIdx.x != 0) return;
@@ -621,6 +624,8 @@ bool pdl_enabled() {
 using namespace afd;
 
 void launch_afd_epoch(uint64_t* epoch, cudaStream_t s) { fused::epoch_kernel<<<1, 1, 0, s>>>(epoch); }
+
+void launch_afd_stamp(uint64_t* buf, int idx, cudaStream_t s) { fused::stamp_kernel<<<1, 1, 0, s>>>(buf, idx); }
 
 void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns, int* status,
                      cudaStream_t s) {

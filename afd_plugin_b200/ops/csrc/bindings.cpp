@@ -340,6 +340,79 @@ at::Tensor grouped_gemm(const at::Tensor& a, const at::Tensor& w, const at::Tens
   return d;
 }
 
+// An MoE layer's experts in one launch: h = SwiGLU(a x w13^T) per expert
+// segment, then y = h x w2^T (epilogue 0), or with a scatter config the
+// routing-weighted rows go to the Attention ranks' combine slots (epilogue 2).
+// sync: int32 [>= e_local + 1], zero before the first call and left zero by
+// every call ([0, e_local) per-expert tile counters, [e_local] CTA counter).
+// scatter (optional): meta, rw, dst_ptrs, flag_ptrs, done_ctr, counts_reset
+// and cfg [J, H, total_ctas, num_dst, layer] as in grouped_gemm_scatter.
+at::Tensor moe_ffn(const at::Tensor& a, const at::Tensor& w13, const at::Tensor& w2, const at::Tensor& offsets,
+                   const at::Tensor& counts, at::Tensor& sync, int64_t w_experts,
+                   const c10::optional<at::Tensor>& meta, const c10::optional<at::Tensor>& rw,
+                   const c10::optional<at::Tensor>& dst_ptrs, const c10::optional<at::Tensor>& flag_ptrs,
+                   const c10::optional<at::Tensor>& done_ctr, const c10::optional<at::Tensor>& counts_reset,
+                   c10::optional<std::vector<int64_t>> cfg) {
+  check_cuda(a, "a");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && w13.scalar_type() == at::kBFloat16 &&
+                  w2.scalar_type() == at::kBFloat16, "moe_ffn: bf16 activations and weights");
+  TORCH_CHECK(a.is_contiguous() && w13.is_contiguous() && w2.is_contiguous() && w13.dim() == 3 && w2.dim() == 3,
+              "moe_ffn: a [R, H], w13 [E, 2I, H], w2 [E, H, I] contiguous");
+  const int64_t R = a.size(0), H = a.size(1), N1 = w13.size(1), I = N1 / 2, N2 = w2.size(1);
+  const int e_local = (int)counts.numel();
+  TORCH_CHECK(w13.size(2) == H && H % 64 == 0 && N1 % 2 == 0 && I % 64 == 0, "moe_ffn: w13 shapes");
+  TORCH_CHECK(w2.size(2) == I && N2 % 128 == 0, "moe_ffn: w2 [E, N % 128 == 0, I]");
+  if (w_experts < 0) {
+    TORCH_CHECK(w13.size(0) == e_local && w2.size(0) == e_local, "moe_ffn: one weight set per expert segment");
+  } else {
+    TORCH_CHECK(w13.size(0) == w_experts && w2.size(0) == w_experts && (w_experts == 1 || w_experts == e_local),
+                "moe_ffn: w_experts must be 1 or the segment count");
+  }
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && counts.scalar_type() == at::kInt && offsets.numel() >= e_local,
+              "moe_ffn: int32 offsets / counts");
+  TORCH_CHECK(sync.scalar_type() == at::kInt && sync.is_contiguous() && sync.numel() >= e_local + 1 &&
+                  sync.device() == a.device(), "moe_ffn: int32 sync [>= e_local + 1] on the same device");
+  const bool scatter = meta.has_value() && meta->defined();
+  auto h = at::empty({R, I}, a.options());
+  at::Tensor y = scatter ? at::empty({0}, a.options()) : at::empty({R, N2}, a.options());
+  if (R == 0) return y;
+  const int we = (int)w_experts;
+  GemmSpec g0{h.data_ptr(), a.data_ptr(), w13.data_ptr(), offsets.data_ptr<int32_t>(), counts.data_ptr<int32_t>(),
+              e_local, (int)R, (int)N1, (int)H, 1, we};
+  GemmSpec g1{scatter ? nullptr : y.data_ptr(), h.data_ptr(), w2.data_ptr(), offsets.data_ptr<int32_t>(),
+              counts.data_ptr<int32_t>(), e_local, (int)R, (int)N2, (int)I, scatter ? 2 : 0, we};
+  ScatterParams sp{};
+  if (scatter) {
+    TORCH_CHECK(rw.has_value() && dst_ptrs.has_value() && flag_ptrs.has_value() && done_ctr.has_value() &&
+                    counts_reset.has_value() && cfg.has_value() && cfg->size() == 5,
+                "moe_ffn: a scatter needs meta, rw, dst_ptrs, flag_ptrs, done_ctr, counts_reset and cfg");
+    const auto& c = *cfg;
+    sp.meta = meta->data_ptr<int32_t>();
+    sp.rw = rw->data_ptr<float>();
+    sp.dst_ptrs = dst_ptrs->data_ptr<int64_t>();
+    sp.J = (int)c[0];
+    sp.H = (int)c[1];
+    sp.total_ctas = (int)c[2];
+    sp.num_dst = (int)c[3];
+    sp.layer = (int)c[4];
+    sp.flag_ptrs = flag_ptrs->data_ptr<int64_t>();
+    sp.done_ctr = reinterpret_cast<unsigned*>(done_ctr->data_ptr());
+    sp.counts_reset = counts_reset->data_ptr<int32_t>();
+    sp.n_reset = (int)counts_reset->numel();
+  }
+  int32_t* sy = sync.data_ptr<int32_t>();
+  c10::cuda::CUDAGuard guard(a.device());
+  const cudaError_t e = launch_grouped_gemm_phases(g0, &g1, sy, reinterpret_cast<unsigned*>(sy + e_local),
+                                                   status_ptr(a), scatter ? &sp : nullptr, stream());
+  TORCH_CHECK(e == cudaSuccess, "moe_ffn: launch failed: ", cudaGetErrorString(e));
+  return y;
+}
+
+// CTAs of one moe_ffn launch (both phases share the persistent grid).
+int64_t moe_ffn_grid(int64_t e_local, int64_t n1, int64_t n2) {
+  return grouped_gemm_grid((int)(e_local * ((n1 / 2) / 64 + n2 / 128)));
+}
+
 at::Tensor moe_combine(const at::Tensor& ys, const at::Tensor& topk_w, const at::Tensor& tsr,
                        const c10::optional<at::Tensor>& shared) {
   const int k_routed = (int)topk_w.size(1);
@@ -383,6 +456,13 @@ int64_t iptr(const at::Tensor& t) { return reinterpret_cast<int64_t>(t.data_ptr(
 void afd_epoch(at::Tensor& epoch) {
   c10::cuda::CUDAGuard g(epoch.device());
   launch_afd_epoch(reinterpret_cast<uint64_t*>(epoch.data_ptr()), stream());
+}
+
+void afd_stamp(at::Tensor& buf, int64_t idx) {
+  TORCH_CHECK(buf.scalar_type() == at::kLong && buf.is_contiguous() && idx >= 0 && idx < buf.numel(),
+              "afd_stamp: int64 buffer and an index inside it");
+  c10::cuda::CUDAGuard g(buf.device());
+  launch_afd_stamp(reinterpret_cast<uint64_t*>(buf.data_ptr()), (int)idx, stream());
 }
 
 void afd_wait(const at::Tensor& flag, int64_t index, const at::Tensor& epoch, int64_t arrivals, int64_t timeout_ns) {
@@ -797,6 +877,7 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("gdn_recurrent(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor A_log, Tensor dt_bias, Tensor norm_w, "
         "float eps, Tensor(a!) state, Tensor cu_seqlens, Tensor slots, Tensor? reset, int nk) -> Tensor");
   m.def("afd_epoch(Tensor(a!) epoch) -> ()");
+  m.def("afd_stamp(Tensor(a!) buf, int idx) -> ()");
   m.def("afd_wait(Tensor flag, int index, Tensor epoch, int arrivals, int timeout_ns) -> ()");
   m.def("afd_dispatch(Tensor attn_out, Tensor(a!) residual, Tensor norm_w, float eps, Tensor gate_w, Tensor? gate_bias, "
         "float scale, Tensor ptrs, Tensor(b!) fmask, Tensor(c!) done_ctr, int[] cfg, Tensor? hash_table=None, "
@@ -815,6 +896,10 @@ TORCH_LIBRARY(afd_b200, m) {
         "int w_experts) -> Tensor");
   m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
   m.def("grouped_gemm_grid(int n_items) -> int");
+  m.def("moe_ffn(Tensor a, Tensor w13, Tensor w2, Tensor offsets, Tensor counts, Tensor(a!) sync, "
+        "int w_experts=-1, Tensor? meta=None, Tensor? rw=None, Tensor? dst_ptrs=None, Tensor? flag_ptrs=None, "
+        "Tensor(b!)? done_ctr=None, Tensor(c!)? counts_reset=None, int[]? cfg=None) -> Tensor");
+  m.def("moe_ffn_grid(int e_local, int n1, int n2) -> int");
   m.def("read_status(int device) -> int");
   m.def("reset_status(int device) -> ()");
   m.def("status_word(int device) -> Tensor");
@@ -837,6 +922,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("moe_combine", &moe_combine);
   m.impl("decode_advance", &decode_advance);
   m.impl("afd_epoch", &afd_epoch);
+  m.impl("afd_stamp", &afd_stamp);
   m.impl("gdn_conv", &gdn_conv);
   m.impl("gdn_recurrent", &gdn_recurrent);
   m.impl("afd_wait", &afd_wait);
@@ -844,6 +930,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("afd_combine", &afd_combine);
   m.impl("grouped_gemm_scatter", &grouped_gemm_scatter);
   m.impl("grouped_gemm_ex", &grouped_gemm_ex);
+  m.impl("moe_ffn", &moe_ffn);
   m.impl("grouped_gemm_w8", &grouped_gemm_w8);
   m.impl("afd_expand", &afd_expand);
   m.impl("afd_combine_send", &afd_combine_send);
@@ -854,4 +941,5 @@ TORCH_LIBRARY_IMPL(afd_b200, CompositeExplicitAutograd, m) {
   m.impl("reset_status", &reset_status);
   m.impl("status_word", &status_word);
   m.impl("grouped_gemm_grid", &gg_grid);
+  m.impl("moe_ffn_grid", &moe_ffn_grid);
 }

@@ -36,21 +36,32 @@ namespace gg {
 constexpr int kBK = 64;            // K per stage (128 B of bf16)
 constexpr int kBM = 128;           // weight rows per CTA (MMA M)
 constexpr int kSub = 64;           // tokens per A sub-tile
-constexpr int kMaxSub = 4;         // tokens per pass <= 256 (MMA N)
-constexpr int kStages = 4;
 constexpr int kThreads = 6 * 32;
 constexpr int kWBytes = kBM * kBK * 2;          // 16 KB
 constexpr int kSubBytes = kSub * kBK * 2;       // 8 KB
-constexpr int kABytes = kMaxSub * kSubBytes;    // 32 KB
-constexpr uint32_t kAccCols = 256;   // one accumulator: 128 lanes x 256 fp32 columns
-constexpr uint32_t kTmemCols = 512;  // two accumulators
+
+// Pipeline: a ring of kWStages weight tiles (128 rows x 64 K, 16 KB each) and
+// a separate ring of kASlots activation sub-tiles (64 tokens x 64 K, 8 KB).
+// A stage takes one weight slot and 1-4 activation slots (the pass's tokens),
+// and each activation slot gets its own N = 64 MMA into its 64 accumulator
+// columns, so the slots of a stage need not be adjacent.  Weight bytes in
+// flight stay at 8 x 16 KB per SM whatever the token count (decode experts
+// see ~24 tokens, shared-expert chunks the whole batch), which is what a
+// weight-streaming GEMM needs to saturate HBM.
+constexpr int kWStages = 8;
+constexpr int kASlots = 10;
+constexpr int kMaxSub = 4;                      // tokens per pass <= 256
+constexpr int kPassRows = kMaxSub * kSub;
+constexpr uint32_t kAccCols = kPassRows;        // one accumulator: 128 lanes x 256 fp32 columns
+constexpr uint32_t kTmemCols = 2 * kAccCols;    // two accumulators
 
 struct Smem {
-  alignas(1024) uint8_t w[kStages][kWBytes];
-  alignas(1024) uint8_t a[kStages][kABytes];
+  alignas(1024) uint8_t w[kWStages][kWBytes];
+  alignas(1024) uint8_t a[kASlots][kSubBytes];
   float xchg[32 * 64];  // SwiGLU exchange: [col][row] for the 64 up rows
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kWStages];
+  uint64_t empty_w[kWStages];
+  uint64_t empty_a[kASlots];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
@@ -146,29 +157,85 @@ AFD_DEVICE bool next_item(int& idx, int n_items, int n_tiles, const int32_t* cou
   return false;
 }
 
+// AND of `pred` over the 128 epilogue threads (named barrier 1).
+AFD_DEVICE bool bar_red_and_epilogue(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(out)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return out != 0;
+}
+
+// Acquire load of a device-scope counter written by other CTAs of this grid.
+AFD_DEVICE int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Later async-proxy (TMA) reads of global memory see generic-proxy writes made
+// visible to this thread before the fence.
+AFD_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Work item of a (possibly two-phase) launch: phase, expert, weight tile.
+// Items are numbered phase-major, then expert-major, so the CTAs working on
+// one expert at the same time share its activation tiles in L2, and every
+// phase-1 item comes after all phase-0 items.
+struct PItem {
+  int ph, e, nt, cnt, seg;
+};
+
+AFD_DEVICE bool next_phase_item(int& idx, const GGArgs& g, int n0, int n_all, PItem& it) {
+  for (; idx < n_all; idx += gridDim.x) {
+    const int ph = idx < n0 ? 0 : 1;
+    const GGPhase& P = g.ph[ph];
+    const int j = ph ? idx - n0 : idx;
+    const int e = j / P.n_tiles;
+    const int c = P.counts[e];
+    if (c > 0) {
+      it.ph = ph;
+      it.e = e;
+      it.nt = j - e * P.n_tiles;
+      it.cnt = c;
+      it.seg = P.offsets[e];
+      idx += gridDim.x;
+      return true;
+    }
+  }
+  return false;
+}
+
 // Persistent grouped GEMM: one CTA per SM walks its work items; the TMA
 // producer runs ahead across item boundaries, the accumulator is double
-// buffered in TMEM (2 x 256 columns) so the epilogue of one item overlaps the
-// MMAs of the next.
-template <int EPI>
+// buffered in TMEM so the epilogue of one item overlaps the MMAs of the next.
+//
+// Two-phase launches (an MoE layer's gate_up -> SwiGLU -> down in one kernel):
+// phase 1 reads phase 0's output.  Every phase-0 item adds one to its
+// expert's counter once its rows are stored; a phase-1 item of expert e waits
+// (bounded) until all of e's phase-0 tiles are counted, then reads them with
+// TMA.  Items are handed out phase-major in a fixed order, so a waiting CTA
+// only waits for items that come earlier and never wait themselves: the wait
+// always ends.  One launch keeps the SMs busy across the phase boundary (no
+// kernel boundary, no tail of the first GEMM), and the intermediate rows stay
+// in L2.  The last CTA to finish clears the counters for the next launch.
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
-    const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap a_map,
-    __nv_bfloat16* __restrict__ d, const int32_t* __restrict__ offsets, const int32_t* __restrict__ counts, int n_w,
-    int w_stride_rows, int k_dim, int ld_d, int n_tiles, int n_experts, int* __restrict__ status,
-    const ScatterParams sp) {
+    const __grid_constant__ CUtensorMap w_map0, const __grid_constant__ CUtensorMap a_map0,
+    const __grid_constant__ CUtensorMap w_map1, const __grid_constant__ CUtensorMap a_map1,
+    const __grid_constant__ GGArgs g, const ScatterParams sp) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const int kb_total = k_dim / kBK;
-  const int n_items = n_tiles * n_experts;
-  constexpr int kPassRows = kMaxSub * kSub;
+  const int n0 = g.ph[0].n_tiles * g.ph[0].n_experts;
+  const int n_all = n0 + (g.n_phases > 1 ? g.ph[1].n_tiles * g.ph[1].n_experts : 0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kWStages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1);
+      mbar_init(&sm.empty_w[s], 1);
     }
+    for (int s = 0; s < kASlots; ++s) mbar_init(&sm.empty_a[s], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.acc_full[b], 1);
       mbar_init(&sm.acc_empty[b], 4);
@@ -188,12 +255,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   pdl_wait();
   pdl_launch_dependents();
 
-  auto w_rows = [&](const Item& it, int& r0, int& r1) {
-    if (EPI == 1) {
-      r0 = it.e * w_stride_rows + it.nt * 64;
-      r1 = it.e * w_stride_rows + n_w / 2 + it.nt * 64;
+  // Rows of the 128-row weight tile: [r0, r0 + 64) and [r1, r1 + 64).  SwiGLU
+  // tiles pair 64 gate rows with the matching 64 up rows.
+  auto w_rows = [&](const PItem& it, int& r0, int& r1) {
+    const GGPhase& P = g.ph[it.ph];
+    if (P.epi == 1) {
+      r0 = it.e * P.w_stride_rows + it.nt * 64;
+      r1 = it.e * P.w_stride_rows + P.n_w / 2 + it.nt * 64;
     } else {
-      r0 = it.e * w_stride_rows + it.nt * kBM;
+      r0 = it.e * P.w_stride_rows + it.nt * kBM;
       r1 = r0 + 64;
     }
   };
@@ -201,29 +271,62 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   if (warp == 0) {
     // ----------------------------------------------------------- producer
     if (lane == 0) {
-      prefetch_tensormap(&w_map);
-      prefetch_tensormap(&a_map);
-      int it_count = 0, idx = blockIdx.x;
-      Item it;
+      prefetch_tensormap(&w_map0);
+      prefetch_tensormap(&a_map0);
+      if (g.n_phases > 1) {
+        prefetch_tensormap(&w_map1);
+        prefetch_tensormap(&a_map1);
+      }
+      int w_count = 0, a_count = 0, idx = blockIdx.x;
+      PItem it;
       bool ok = true;
-      while (ok && next_item(idx, n_items, n_tiles, counts, offsets, it)) {
-        int r0, r1;
-        w_rows(it, r0, r1);
-        const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
-        for (int p = 0; p < n_pass && ok; ++p) {
-          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
-          for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
-            const int st = it_count % kStages;
-            if (!mbar_wait_bounded(&sm.empty[st], ((it_count / kStages) & 1) ^ 1)) {
-              atomicExch(status, kStatusWaitTimeout);
+      while (ok && next_phase_item(idx, g, n0, n_all, it)) {
+        const GGPhase& P = g.ph[it.ph];
+        const CUtensorMap* wm = it.ph ? &w_map1 : &w_map0;
+        const CUtensorMap* am = it.ph ? &a_map1 : &a_map0;
+        if (it.ph == 1 && g.ph[0].done != nullptr) {
+          // this expert's phase-0 rows: wait until every tile of them is stored
+          const int need = g.ph[0].n_tiles;
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire_gpu(g.ph[0].done + it.e) < need) {
+            if ((int64_t)(globaltimer_ns() - t0) > g.dep_timeout_ns) {
+              atomicExch(g.status, kStatusWaitTimeout);
               ok = false;
               break;
             }
+            __nanosleep(128);
+          }
+          if (!ok) break;
+          fence_proxy_async_global();
+        }
+        int r0, r1;
+        w_rows(it, r0, r1);
+        const int kb_total = P.k_dim / kBK;
+        const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
+        for (int p = 0; p < n_pass && ok; ++p) {
+          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          for (int kb = 0; kb < kb_total && ok; ++kb, ++w_count) {
+            const int st = w_count % kWStages;
+            if (!mbar_wait_bounded(&sm.empty_w[st], ((w_count / kWStages) & 1) ^ 1)) {
+              atomicExch(g.status, kStatusWaitTimeout);
+              ok = false;
+              break;
+            }
+            int slot[kMaxSub];
+            for (int s2 = 0; s2 < n_sub; ++s2, ++a_count) {
+              slot[s2] = a_count % kASlots;
+              if (!mbar_wait_bounded(&sm.empty_a[slot[s2]], ((a_count / kASlots) & 1) ^ 1)) {
+                atomicExch(g.status, kStatusWaitTimeout);
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) break;
             mbar_expect_tx(&sm.full[st], kWBytes + n_sub * kSubBytes);
-            tma_load_2d(sm.w[st], &w_map, &sm.full[st], kb * kBK, r0);
-            tma_load_2d(sm.w[st] + kWBytes / 2, &w_map, &sm.full[st], kb * kBK, r1);
+            tma_load_2d(sm.w[st], wm, &sm.full[st], kb * kBK, r0);
+            tma_load_2d(sm.w[st] + kWBytes / 2, wm, &sm.full[st], kb * kBK, r1);
             for (int s2 = 0; s2 < n_sub; ++s2)
-              tma_load_2d(sm.a[st] + s2 * kSubBytes, &a_map, &sm.full[st], kb * kBK, it.seg + p * kPassRows + s2 * kSub);
+              tma_load_2d(sm.a[slot[s2]], am, &sm.full[st], kb * kBK, it.seg + p * kPassRows + s2 * kSub);
           }
         }
       }
@@ -231,36 +334,40 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      int it_count = 0, acc_count = 0, idx = blockIdx.x;
-      Item it;
+      int w_count = 0, a_count = 0, acc_count = 0, idx = blockIdx.x;
+      PItem it;
       bool ok = true;
-      while (ok && next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+      const uint32_t idesc = make_idesc(kBM, kSub);  // one N = 64 MMA per activation slot
+      while (ok && next_phase_item(idx, g, n0, n_all, it)) {
+        const int kb_total = g.ph[it.ph].k_dim / kBK;
         const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
         for (int p = 0; p < n_pass && ok; ++p, ++acc_count) {
           const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
-          const uint32_t idesc = make_idesc(kBM, n_sub * kSub);
           const int ab = acc_count & 1;
           if (!mbar_wait_bounded(&sm.acc_empty[ab], ((acc_count >> 1) & 1) ^ 1)) {
-            atomicExch(status, kStatusWaitTimeout);
+            atomicExch(g.status, kStatusWaitTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t tacc = tmem + ab * kAccCols;
-          for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
-            const int st = it_count % kStages;
-            if (!mbar_wait_bounded(&sm.full[st], (it_count / kStages) & 1)) {
-              atomicExch(status, kStatusWaitTimeout);
+          for (int kb = 0; kb < kb_total; ++kb, ++w_count) {
+            const int st = w_count % kWStages;
+            if (!mbar_wait_bounded(&sm.full[st], (w_count / kWStages) & 1)) {
+              atomicExch(g.status, kStatusWaitTimeout);
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t wa = smem_u32(sm.w[st]);
-            const uint32_t aa = smem_u32(sm.a[st]);
+            for (int s2 = 0; s2 < n_sub; ++s2) {
+              const uint32_t aa = smem_u32(sm.a[(a_count + s2) % kASlots]);
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma(tacc, make_desc(wa + kk * 32), make_desc(aa + kk * 32), idesc, (kb | kk) != 0);
-            umma_commit(&sm.empty[st]);
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                umma(tacc + s2 * kSub, make_desc(wa + kk * 32), make_desc(aa + kk * 32), idesc, (kb | kk) != 0);
+            }
+            umma_commit(&sm.empty_w[st]);
+            for (int s2 = 0; s2 < n_sub; ++s2, ++a_count) umma_commit(&sm.empty_a[a_count % kASlots]);
           }
           if (ok) umma_commit(&sm.acc_full[ab]);
         }
@@ -271,15 +378,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     const int quarter = warp & 3;           // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;    // weight row within the tile
     int acc_count = 0, idx = blockIdx.x;
-    Item it;
+    PItem it;
     bool ok = true;
-    while (ok && next_item(idx, n_items, n_tiles, counts, offsets, it)) {
+    while (ok && next_phase_item(idx, g, n0, n_all, it)) {
+      const GGPhase& P = g.ph[it.ph];
+      const int epi = P.epi;
+      __nv_bfloat16* __restrict__ d = P.d;
+      const int ld_d = P.ld_d;
       const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
       for (int p = 0; p < n_pass; ++p, ++acc_count) {
         const int ab = acc_count & 1;
-        if (!mbar_wait_bounded(&sm.acc_full[ab], (acc_count >> 1) & 1)) {
-          atomicExch(status, kStatusWaitTimeout);
-          ok = false;
+        // The four epilogue warps agree on the outcome of the bounded wait, so
+        // the named barriers below are reached by all of them or by none.
+        ok = bar_red_and_epilogue(mbar_wait_bounded(&sm.acc_full[ab], (acc_count >> 1) & 1));
+        if (!ok) {
+          if (lane == 0) atomicExch(g.status, kStatusWaitTimeout);
           break;
         }
         tc_fence_after();
@@ -289,15 +402,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         for (int c0 = 0; c0 < n_cols; c0 += 32) {
           float v[32];
           tmem_ld32(tacc + c0, v);
-          if (EPI == 0) {
+          if (epi == 0) {
             const int col = it.nt * kBM + row;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (c0 + j < n_cols) d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(v[j]);
-          } else if (EPI == 2) {
-            // routing weight applied, row stored into the source rank's slot (peer memory)
+          } else if (epi == 2) {
+            // routing weight applied, row stored into the source rank's slot
             const int col = it.nt * kBM + row;
-#pragma unroll 4
+#pragma unroll
             for (int j = 0; j < 32; ++j) {
               if (c0 + j < n_cols) {
                 const int r = r_base + c0 + j;
@@ -318,9 +431,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 if (c0 + j < n_cols) {
-                  const float g = v[j];
+                  const float gt = v[j];
                   const float u = sm.xchg[j * 64 + row];
-                  d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
+                  d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(gt / (1.f + __expf(-gt)) * u);
                 }
               }
             }
@@ -330,10 +443,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         tc_fence_before();
         if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
       }
-    }
-    if (EPI == 2) {
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (warp == 2 && lane == 0) scatter_arrive(sp);
+      if (ok && P.done != nullptr) {
+        // this tile's rows are stored: count it for the expert's phase-1 items
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == 2 && lane == 0) atomicAdd(P.done + it.e, 1);
+      }
     }
   }
   tc_fence_before();
@@ -341,6 +456,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+  if (threadIdx.x == 0) {
+    // Every role of this CTA is done reading counts and storing rows.
+    if (g.ph[0].done != nullptr) {
+      __threadfence();
+      if (atomicAdd(g.finish_ctr, 1u) == gridDim.x - 1) {
+        for (int e = 0; e < g.ph[0].n_experts; ++e) g.ph[0].done[e] = 0;
+        *g.finish_ctr = 0u;
+        __threadfence();
+      }
+    }
+    if (g.ph[0].epi == 2 || (g.n_phases > 1 && g.ph[1].epi == 2)) scatter_arrive(sp);
   }
 }
 
@@ -675,34 +802,78 @@ int grouped_gemm_grid(int n_items) {
   return n_items < sms ? (n_items > 0 ? n_items : 1) : sms;
 }
 
+namespace {
+
+GGPhase make_phase(const GemmSpec& g, CUtensorMap* wmap, CUtensorMap* amap) {
+  const int w_experts = g.w_experts < 0 ? g.e_local : g.w_experts;
+  gg::encode_2d(wmap, g.w, (uint64_t)w_experts * g.n, g.k, 64);
+  gg::encode_2d(amap, g.a, g.rows_cap, g.k, gg::kSub);
+  GGPhase P{};
+  P.d = static_cast<__nv_bfloat16*>(g.d);
+  P.offsets = g.offsets;
+  P.counts = g.counts;
+  P.done = nullptr;
+  P.n_w = g.n;
+  P.w_stride_rows = (w_experts == 1) ? 0 : g.n;
+  P.k_dim = g.k;
+  P.n_experts = g.e_local;
+  P.epi = g.epilogue;
+  if (g.epilogue == 1) {
+    P.n_tiles = (g.n / 2) / 64;
+    P.ld_d = g.n / 2;
+  } else {
+    P.n_tiles = g.n / gg::kBM;
+    P.ld_d = g.n;
+  }
+  return P;
+}
+
+cudaError_t launch_kernel(const CUtensorMap& w0, const CUtensorMap& a0, const CUtensorMap& w1, const CUtensorMap& a1,
+                          const GGArgs& args, const ScatterParams& sp, int n_items, cudaStream_t s) {
+  const int smem = (int)sizeof(gg::Smem) + 1024;
+  static PerDeviceOnce attr;
+  cudaError_t e = attr.run([&] {
+    return cudaFuncSetAttribute(gg::grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  if (e != cudaSuccess) return e;
+  const int grid = grouped_gemm_grid(n_items);
+  return launch_pdl(gg::grouped_gemm_kernel, dim3(grid), dim3(gg::kThreads), (size_t)smem, s, w0, a0, w1, a1, args,
+                    sp);
+}
+
+}  // namespace
+
+int grouped_gemm_launch_grid(int n_items) { return grouped_gemm_grid(n_items); }
+
+cudaError_t launch_grouped_gemm_phases(const GemmSpec& g0, const GemmSpec* g1, int* done, unsigned* finish_ctr,
+                                       int* status, const ScatterParams* sp, cudaStream_t s) {
+  CUtensorMap w0, a0, w1, a1;
+  GGArgs args{};
+  args.ph[0] = make_phase(g0, &w0, &a0);
+  args.n_phases = 1;
+  if (g1 != nullptr) {
+    args.ph[1] = make_phase(*g1, &w1, &a1);
+    args.n_phases = 2;
+    args.ph[0].done = done;
+  } else {
+    w1 = w0;
+    a1 = a0;
+  }
+  args.status = status;
+  args.finish_ctr = finish_ctr;
+  args.dep_timeout_ns = 2000000000ll;  // 2 s: phase-0 tiles of an expert are minutes' worth of margin away
+  ScatterParams none{};
+  const ScatterParams& spv = sp ? *sp : none;
+  int n_items = args.ph[0].n_tiles * args.ph[0].n_experts;
+  if (g1 != nullptr) n_items += args.ph[1].n_tiles * args.ph[1].n_experts;
+  return launch_kernel(w0, a0, w1, a1, args, spv, n_items, s);
+}
+
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,
                          const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
                          int* status, cudaStream_t s, int w_experts, const ScatterParams* sp) {
-  if (w_experts < 0) w_experts = e_local;
-  CUtensorMap wmap, amap;
-  gg::encode_2d(&wmap, w, (uint64_t)w_experts * n, k, 64);
-  gg::encode_2d(&amap, a, rows_cap, k, gg::kSub);
-  const int smem = (int)sizeof(gg::Smem) + 1024;
-  const int w_stride = (w_experts == 1) ? 0 : n;
-  ScatterParams none{};
-  const ScatterParams& spv = sp ? *sp : none;
-  auto go = [&](auto epi_tag, int n_tiles, int ld) {
-    constexpr int EPI = decltype(epi_tag)::value;
-    static PerDeviceOnce attr;
-    attr.run([&] {
-      return cudaFuncSetAttribute(gg::grouped_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    });
-    const int grid = grouped_gemm_grid(n_tiles * e_local);
-    launch_pdl(gg::grouped_gemm_kernel<EPI>, dim3(grid), dim3(gg::kThreads), (size_t)smem, s, wmap, amap,
-               (__nv_bfloat16*)d, expert_offsets, expert_counts, n, w_stride, k, ld, n_tiles, e_local, status, spv);
-  };
-  if (epilogue == 1) {
-    go(std::integral_constant<int, 1>{}, (n / 2) / 64, n / 2);
-  } else if (epilogue == 2) {
-    go(std::integral_constant<int, 2>{}, n / gg::kBM, n);
-  } else {
-    go(std::integral_constant<int, 0>{}, n / gg::kBM, n);
-  }
+  GemmSpec g{d, a, w, expert_offsets, expert_counts, e_local, rows_cap, n, k, epilogue, w_experts};
+  launch_grouped_gemm_phases(g, nullptr, nullptr, nullptr, status, sp, s);
 }
 
 

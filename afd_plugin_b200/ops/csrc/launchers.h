@@ -163,6 +163,8 @@ struct CombineParams {
   int* status;
 };
 void launch_afd_epoch(uint64_t* epoch, cudaStream_t s);
+// buf[idx] = the device's global nanosecond timer once the stream gets there.
+void launch_afd_stamp(uint64_t* buf, int idx, cudaStream_t s);
 void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arrivals, int64_t timeout_ns, int* status,
                      cudaStream_t s);
 void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s);
@@ -199,9 +201,45 @@ void launch_grouped_gemm_w8(void* d, const void* a, const void* w, const float* 
                             int* status, cudaStream_t s, int w_experts, const ScatterParams* sp);
 // w_expert_rows: rows between consecutive experts in W (0 = one weight set
 // shared by every segment, e.g. shared experts / dense MLP over per-source segments).
+// A pass covers up to 256 rows of an expert; wider segments take several
+// passes over its weights.
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,
                          const int32_t* expert_counts, int e_local, int rows_cap, int n, int k, int epilogue,
                          int* status, cudaStream_t s, int w_experts = -1, const ScatterParams* sp = nullptr);
+
+// One grouped GEMM of a launch (bf16 weights).
+struct GemmSpec {
+  void* d;                 // output [rows_cap, N] (N / 2 for epilogue 1), unused for epilogue 2
+  const void* a;           // activations [rows_cap, K]
+  const void* w;           // weights [w_experts, N, K]
+  const int32_t* offsets;  // [e_local] first row of each expert's segment
+  const int32_t* counts;   // [e_local] rows of each expert
+  int e_local, rows_cap, n, k, epilogue;
+  int w_experts;           // -1: e_local; 1: one weight set for every segment
+};
+// Kernel-side description of a phase (filled by the launcher).
+struct GGPhase {
+  __nv_bfloat16* d;
+  const int32_t* offsets;
+  const int32_t* counts;
+  int* done;  // phase 0 of a two-phase launch: finished tiles per expert (zero between launches)
+  int n_w, w_stride_rows, k_dim, ld_d, n_tiles, n_experts, epi;
+};
+struct GGArgs {
+  GGPhase ph[2];
+  int n_phases;
+  int* status;
+  unsigned* finish_ctr;    // two-phase launches: CTAs done (zero between launches)
+  long long dep_timeout_ns;
+};
+// One launch of one or two grouped GEMMs.  With g1, phase 1 reads phase 0's
+// output (its `a` is g0's `d`, same row segments): an MoE layer's gate_up
+// (epilogue 1) and down projection (epilogue 0 or 2) in one persistent
+// kernel.  done: int32 [g0.e_local] and finish_ctr: one uint32, both zero
+// before the first launch and left zero by every launch.  Returns the launch
+// error, if any.
+cudaError_t launch_grouped_gemm_phases(const GemmSpec& g0, const GemmSpec* g1, int* done, unsigned* finish_ctr,
+                                       int* status, const ScatterParams* sp, cudaStream_t s);
 
 // ---- gdn.cu (Gated DeltaNet)
 struct GdnConvParams {

@@ -1,9 +1,11 @@
 """CUDA MoE expert path: align -> gather -> tcgen05 grouped GEMMs -> combine.
 
-The two GEMMs run on the 5th-generation tensor cores (``grouped_gemm``, or
-``grouped_gemm_w8`` for fp8 block-scaled weights): ``gate_up`` with the
-SwiGLU epilogue fused, then ``down``.  No step needs a
-host synchronisation, so the whole path captures into a CUDA graph.
+The two GEMMs run on the 5th-generation tensor cores.  With bf16 weights they
+are ONE persistent launch (``moe_ffn``): ``gate_up`` with the SwiGLU epilogue
+fused, then ``down``, the down tiles of an expert starting as soon as its
+gate_up tiles are stored.  fp8 block-scaled weights use two
+``grouped_gemm_w8`` launches.  No step needs a host synchronisation, so the
+whole path captures into a CUDA graph.
 """
 
 from __future__ import annotations
@@ -11,6 +13,26 @@ from __future__ import annotations
 import torch
 
 from afd_plugin_b200.ops._ext import ops as _cuda_ops
+
+# Per-device counters of the two-phase expert kernel (zero between launches).
+_SYNC: dict[torch.device, torch.Tensor] = {}
+_SYNC_LEN = 4096
+
+
+def moe_sync_buffer(device: torch.device, experts: int) -> torch.Tensor:
+    """The counters a ``moe_ffn`` launch over ``experts`` segments uses on ``device``.
+
+    Allocated once per device (first use comes from an eager step, before any
+    graph capture) and shared by every launch on that device's stream.
+    """
+    if experts + 1 > _SYNC_LEN:
+        raise ValueError(f"moe_ffn supports at most {_SYNC_LEN - 1} expert segments per launch, got {experts}")
+    device = torch.device(device)
+    buf = _SYNC.get(device)
+    if buf is None:
+        buf = torch.zeros(_SYNC_LEN, dtype=torch.int32, device=device)
+        _SYNC[device] = buf
+    return buf
 
 
 def moe_experts_cuda(
@@ -38,9 +60,8 @@ def moe_experts_cuda(
         h = C.grouped_gemm_w8(xs, w13, w13_scale, offsets, counts, 1, ne)
         y = C.grouped_gemm_w8(h, w2, w2_scale, offsets, counts, 0, ne)
     else:
-        h = C.grouped_gemm(xs, w13, offsets, counts, 1)
-        y = C.grouped_gemm(h, w2, offsets, counts, 0)
+        y = C.moe_ffn(xs, w13, w2, offsets, counts, moe_sync_buffer(x.device, w13.shape[0]))
     return C.moe_combine(y, topk_weights.float().contiguous(), tsr, shared_out)
 
 
-__all__ = ["moe_experts_cuda"]
+__all__ = ["moe_experts_cuda", "moe_sync_buffer"]

@@ -184,6 +184,12 @@ class LLMEngine:
         from afd_plugin_b200.utils.metrics import StepMetrics
 
         self.metrics = StepMetrics()
+        from afd_plugin_b200.utils.roofline import weight_bytes_per_step
+
+        # HBM bytes a decode step of this rank must move: its weights once, plus the KV
+        # rows of the running sequences (added per step from the staged lengths).
+        self._weight_bytes = weight_bytes_per_step(model)
+        self.last_hbm_bytes = 0
         self._last_phase = "decode"
         # noise for sampled requests without their own seed (same seed on every
         # tensor-parallel peer, so peers draw the same tokens)
@@ -480,7 +486,10 @@ class LLMEngine:
         out = self._step()
         self.metrics.record(phase=self._last_phase, batch=len(out), tokens=len(out),
                             ms=(time.perf_counter() - t0) * 1e3, h2d_bytes=self.last_h2d_bytes,
-                            d2h_bytes=self.last_d2h_bytes)
+                            d2h_bytes=self.last_d2h_bytes,
+                            hbm_bytes=self.last_hbm_bytes if self._last_phase == "decode" else 0)
+        if self.runner.timer.enabled and self._last_phase == "decode":
+            self.metrics.phases = self.runner.timer.summary()
         self.profiler.step()
         return out
 
@@ -709,6 +718,10 @@ class LLMEngine:
         b.seq_lens[:run_b].copy_(self._h_lens[:run_b], non_blocking=True)
         self.last_h2d_bytes = run_b * (4 + 8 + 8 + 4 + 4 * self.max_blocks_per_seq
                                        + (4 if self.runner.has_linear_state else 0))
+        from afd_plugin_b200.utils.roofline import kv_bytes_per_step
+
+        self.last_hbm_bytes = self._weight_bytes + kv_bytes_per_step(getattr(self.model, "cache_arch", self.model.arch), int(self._h_lens[:B].sum()),
+                                                                      elem_bytes=self.model.dtype.itemsize)
         flags = {}
         if len(votes) > 1:
             sp = ubatch_splits(run_b, self.runner.num_ubatches)

@@ -21,6 +21,7 @@ from typing import Any
 import torch
 import torch.distributed as dist
 
+from afd_plugin_b200.utils.phase_timer import NULL_TIMER
 from afd_plugin_b200.connectors.metadata import (
     AFDControlPayload,
     AFDDPMetadata,
@@ -37,6 +38,8 @@ class FFNExecutor:
     """
 
     supports_graph_capture = True
+    # Phase marks of the step (set by the model runner; a no-op timer by default).
+    timer = NULL_TIMER
 
     def begin_step(self, stage_tokens: dict[int, int], **flags: Any) -> None:
         """``flags``: is_warmup / is_graph_capturing / is_graph_replaying / tokens_across_attn."""

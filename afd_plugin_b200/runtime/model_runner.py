@@ -24,6 +24,7 @@ from afd_plugin_b200 import ops
 from afd_plugin_b200.models.layers import AttentionMetadata
 from afd_plugin_b200.runtime.ffn_executor import FFNExecutor
 from afd_plugin_b200.runtime.kv_cache import PAD_BLOCK, KVCache
+from afd_plugin_b200.utils.phase_timer import NULL_TIMER, PhaseTimer, phase_timing_requested
 
 
 @dataclass
@@ -100,17 +101,24 @@ class ModelRunner:
         self.sparse_decode = False
         # logits of the last prefill (one row per sequence) or decode step (one per row)
         self.last_logits: torch.Tensor | None = None
+        # Device-side phase marks of each step (off unless AFD_PHASE_TIMING=1).
+        self.timer = PhaseTimer(self.device) if phase_timing_requested() and self.device.type == "cuda" else NULL_TIMER
+        self.ffn.timer = self.timer
 
     # ------------------------------------------------------------ forward
     def _layers(self, h: torch.Tensor, meta: AttentionMetadata, stage: int):
         """Generator over one ubatch; yields after each layer's FFN send."""
         model = self.model
         residual = None
+        timer = self.timer
         for layer in range(model.num_layers):
             attn_out, residual = model.run_attention(layer, h, residual, meta, self.kv.layer(layer))
+            timer.mark("attn")
             handle = self.ffn.send(layer, attn_out, residual, stage)
+            timer.mark("ffn_send")
             yield None
             h, residual = self.ffn.recv(layer, handle, stage)
+            timer.mark("ffn_recv")
         yield (h, residual)
 
     def _run_stages(self, embeds: list[torch.Tensor], metas: list[AttentionMetadata]):
@@ -131,6 +139,7 @@ class ModelRunner:
         counts = {s: splits[s + 1] - splits[s] for s in range(len(splits) - 1)}
         self.ffn.begin_step(counts, **step_flags)
         self.ffn.step_prologue()
+        self.timer.begin_step()
         for s, m in enumerate(metas):
             m.input_ids = input_ids[splits[s] : splits[s + 1]]
         embeds = [self.model.embed(input_ids[splits[s] : splits[s + 1]]) for s in range(len(splits) - 1)]

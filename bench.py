@@ -17,6 +17,11 @@ e2e     the same metric through the public engine API (``LLMEngine.step``):
         memory, replays, and reads the sampled tokens back.
 Weights (~31 GB) and KV (~10 GB) are far larger than the 126 MB L2, so no L2
 flush is needed between steps.
+
+Diagnostics (not bench values): ``--phases`` adds per-role phase timing on the
+device; ``AFD_BENCH_NVTX=1`` wraps the timed loop in an NVTX range named
+"timed" (for a profiler's range filter); ``AFD_BENCH_VERBOSE=1`` logs each
+rank's progress to stderr.
 """
 
 from __future__ import annotations
@@ -62,8 +67,14 @@ def parse_args(argv=None):
                          "so a second ubatch re-reads every expert weight)")
     ap.add_argument("--no-dbo", action="store_true", help="force DBO off")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--layers", type=int, default=0, help="debug only: truncate layers (invalid as a bench)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="truncate the model to this many layers for quick checks; the line is marked invalid")
+    ap.add_argument("--no-launch-count", action="store_true",
+                    help="skip counting this package's kernels per step (the count runs one eager step under "
+                         "torch.profiler, which conflicts with an outside profiler such as ncu)")
     ap.add_argument("--topology", default="", help="override A,F split for N>1, e.g. 4,4 or 2,2")
+    ap.add_argument("--phases", action="store_true",
+                    help="diagnostic: per-role phase timing on the device (adds a stamp kernel per phase)")
     return ap.parse_args(argv)
 
 
@@ -181,14 +192,11 @@ def _log(msg: str) -> None:
 
 def main(argv=None) -> int:
     args = parse_args(argv)
-    trace_after = os.environ.get("AFD_BENCH_TRACE_AFTER")
-    if trace_after:
-        import faulthandler
-
-        faulthandler.dump_traceback_later(float(trace_after), exit=False)
     if args.impl == "reference":
         reference_arm(args)
         return 0
+    if args.phases:
+        os.environ["AFD_PHASE_TIMING"] = "1"
     from afd_plugin_b200.utils.clocks import ClockSampler
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -229,8 +237,7 @@ def main(argv=None) -> int:
             engine.capture_graphs()
         batch = len(engine.running)
         engine.load_decode_batch()
-        launches_per_step = (0 if os.environ.get("AFD_BENCH_NO_COUNT") == "1"
-                             else count_our_kernels(lambda: one_eager_step(engine, batch)))
+        launches_per_step = 0 if args.no_launch_count else count_our_kernels(lambda: one_eager_step(engine, batch))
         with ClockSampler(local) as clk:
             per_step, total_ms = device_loop(engine, batch, args.warmup, args.steps, args.isl, args.osl)
             e2e = None
@@ -239,13 +246,14 @@ def main(argv=None) -> int:
                 e2e = {"value": round(batch * args.steps / (e2e_ms / 1e3), 1), "unit": "tok/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
         result = dict(ms=total_ms, per_step=per_step, tokens=batch, e2e=e2e, clocks=clk.summary(),
-                      launches=launches_per_step * args.steps, parallelism="colocated-1gpu")
+                      launches=launches_per_step * args.steps, parallelism="colocated-1gpu",
+                      phases=[{"rank": 0, "role": "colocated", "phases": engine.runner.timer.summary()}])
         status = torch.ops.afd_b200.read_status(local)
         if status:
             raise RuntimeError(f"kernel status word {status} (a bounded wait expired)")
         engine.runner.release_graphs()
     else:
-        from afd_plugin_b200.runtime.afd_bench import run_afd_rank
+        from afd_plugin_b200.bench.afd_decode import run_afd_rank
 
         result = run_afd_rank(args, rank=rank, local=local, num_attn=num_attn, num_ffn=num_ffn, connector=connector,
                               build_config=build_config, prime_requests=prime_requests, device_loop=device_loop,
@@ -286,6 +294,11 @@ def main(argv=None) -> int:
             "e2e": result.get("e2e"),
             "gpu_launches": result.get("launches"),
         }
+        if args.layers:
+            line["invalid_as_bench"] = f"model truncated to {args.layers} layers"
+        if args.phases:
+            line["phases"] = result.get("phases")
+            line["note"] = "phase-timing run: stamp kernels inside the step; a diagnostic, not a bench value"
         print(json.dumps(line))
     return 0
 

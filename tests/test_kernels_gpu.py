@@ -262,3 +262,65 @@ def test_mla_decode_sparse_routing(monkeypatch):
     assert ops.sparse_kernel_enabled()
     got = ops.mla_decode_sparse(q, cache, table, seq, keep, 0.1, 512)
     _close(got, base, 2e-2, 2e-2)
+
+
+def _segments(counts_list):
+    counts = torch.tensor(counts_list, dtype=torch.int32, device=DEV)
+    offsets = torch.zeros(len(counts_list), dtype=torch.int32, device=DEV)
+    offsets[1:] = counts.cumsum(0)[:-1]
+    return counts, offsets, int(counts.sum())
+
+
+def _swiglu_ref(a, w13, w2=None):
+    y = a.float() @ w13.float().t()
+    i = y.shape[1] // 2
+    h = torch.nn.functional.silu(y[:, :i]) * y[:, i:]
+    return h if w2 is None else h.to(torch.bfloat16).float() @ w2.float().t()
+
+
+@pytest.mark.parametrize("counts_list", [[24, 0, 31, 256, 1, 64, 65, 130], [300, 3], [7] * 20])
+@pytest.mark.parametrize("epilogue", [0, 1])
+def test_grouped_gemm_activation_ring(counts_list, epilogue):
+    """Passes of 1-4 activation slots (and several passes for > 256 rows) vs fp32 per segment."""
+    torch.manual_seed(sum(counts_list) + epilogue)
+    C = _ext.ops()
+    counts, offsets, R = _segments(counts_list)
+    E, K, N = len(counts_list), 256, 384 if epilogue == 0 else 256
+    a = (torch.randn(R + 3, K, device=DEV) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(E, N, K, device=DEV) * 0.05).to(torch.bfloat16)
+    out = C.grouped_gemm(a, w, offsets, counts, epilogue)
+    torch.cuda.synchronize()
+    for e in range(E):
+        o, c = int(offsets[e]), int(counts[e])
+        if c == 0:
+            continue
+        y = _swiglu_ref(a[o : o + c], w[e]) if epilogue == 1 else a[o : o + c].float() @ w[e].float().t()
+        sc = y.abs().max().item() + 1e-6
+        _close(out[o : o + c] / sc, y / sc, 2e-2)
+
+
+@pytest.mark.parametrize("counts_list,H,I", [([24, 31, 0, 17, 256, 256], 512, 256), ([300, 5, 70], 256, 128),
+                                             ([3] * 66, 2048, 1408)])
+def test_moe_ffn_two_phase(counts_list, H, I):
+    """gate_up -> SwiGLU -> down in one launch vs fp32, twice in a row; the counters end at zero."""
+    from afd_plugin_b200.ops.moe import moe_sync_buffer
+
+    torch.manual_seed(len(counts_list) + H)
+    C = _ext.ops()
+    counts, offsets, R = _segments(counts_list)
+    E = len(counts_list)
+    w13 = (torch.randn(E, 2 * I, H, device=DEV) * 0.04).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, device=DEV) * 0.04).to(torch.bfloat16)
+    sync = moe_sync_buffer(torch.device(DEV), E)
+    for rep in range(2):
+        a = (torch.randn(R + 2, H, device=DEV) * 0.5).to(torch.bfloat16)
+        y = C.moe_ffn(a, w13, w2, offsets, counts, sync)
+        torch.cuda.synchronize()
+        assert int(sync.abs().sum()) == 0, "moe_ffn must leave its counters at zero"
+        for e in range(E):
+            o, c = int(offsets[e]), int(counts[e])
+            if c == 0:
+                continue
+            want = _swiglu_ref(a[o : o + c], w13[e], w2[e])
+            sc = want.abs().max().item() + 1e-6
+            _close(y[o : o + c] / sc, want / sc, 3e-2)
