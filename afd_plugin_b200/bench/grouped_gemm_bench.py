@@ -6,6 +6,10 @@ weight bytes moved per second against the measured HBM copy bandwidth
 (``MEASURED_PEAKS.json`` at the repository root, when present).
 
     python -m afd_plugin_b200.bench.grouped_gemm_bench [--shapes dsv2-lite-f2,...]
+    python -m afd_plugin_b200.bench.grouped_gemm_bench --dense [--shapes in_proj,...]
+
+``AFD_GG_PIPE=64|128|256`` selects the kernel's tokens per pass (and with it
+the pipeline depth: 8, 6 or 4 stages) for a comparison run.
 """
 
 from __future__ import annotations
@@ -102,7 +106,8 @@ def run(shape: str, reps: int, tokens_per_expert: int | None = None, fp8: bool =
             ("gemm1_swiglu", lambda: C.grouped_gemm_ex(a1, w13, offsets, counts, 1, -1), w13.numel() * 2),
             ("gemm2", lambda: C.grouped_gemm_ex(a2, w2, offsets, counts, 0, -1), w2.numel() * 2),
             # both projections in one two-phase launch (what the MoE layers run)
-            ("moe_ffn", lambda: C.moe_ffn(a1, w13, w2, offsets, counts, sync), (w13.numel() + w2.numel()) * 2),
+            ("moe_ffn", lambda: C.moe_ffn(a1, w13, w2, offsets, counts, sync, max(per)),
+             (w13.numel() + w2.numel()) * 2),
         )
     for name, fn, wbytes in cases:
         us = _time_us(fn, reps)
@@ -126,5 +131,65 @@ def main(argv=None) -> None:
         print(json.dumps(run(shape, args.reps, args.tokens_per_expert, fp8=args.fp8)), flush=True)
 
 
+
+
+# Dense decode-step GEMMs of DeepSeek-V2-Lite at 256 tokens: (tokens, N, K, batch)
+DENSE = {
+    "in_proj": (256, 3712, 2048, 0),       # q + kv_a projections in one weight (rows padded to 128)
+    "o_proj": (256, 2048, 2048, 0),
+    "lm_head": (256, 102400, 2048, 0),
+    "router": (256, 128, 2048, 0),         # 64 experts, rows padded to 128
+    "w_uk": (256, 512, 128, 16),           # per head: q_nope [128] -> latent [512]
+    "w_uv": (256, 128, 512, 16),           # per head: latent [512] -> v [128]
+    "in_proj_b43": (43, 3712, 2048, 0),    # one Attention rank of 6A2F
+    "o_proj_b43": (43, 2048, 2048, 0),
+}
+
+
+def run_dense(name: str, reps: int) -> dict:
+    """tcgen05 ``tc_gemm`` vs torch (cuBLAS) on one dense or per-head batched shape."""
+    from afd_plugin_b200.ops import _ext
+
+    from afd_plugin_b200.ops.moe import gemm_workspace
+
+    C = _ext.ops()
+    ws = gemm_workspace(torch.device("cuda"))
+    T, N, K, B = DENSE[name]
+    dev = "cuda"
+    if B:
+        a = (torch.randn(B, T, K, device=dev) * 0.1).to(torch.bfloat16)
+        w = (torch.randn(B, N, K, device=dev) * 0.02).to(torch.bfloat16)
+        ours = lambda: C.tc_gemm(a, w, 0, 0, False, *ws)  # noqa: E731
+        lib = lambda: torch.bmm(a, w.transpose(1, 2))  # noqa: E731
+    else:
+        a = (torch.randn(T, K, device=dev) * 0.1).to(torch.bfloat16)
+        w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+        ours = lambda: C.tc_gemm(a, w, 0, 0, False, *ws)  # noqa: E731
+        lib = lambda: torch.mm(a, w.t())  # noqa: E731
+    wbytes = w.numel() * 2
+    peak, kind = _peak_gbs()
+    out = {"dense": name, "tokens": T, "n": N, "k": K, "batch": B}
+    for tag, fn in (("tc_gemm", ours), ("cublas", lib)):
+        us = _time_us(fn, reps)
+        out[tag + "_us"] = round(us, 2)
+        out[tag + f"_frac_of_{kind}_hbm"] = round(wbytes / (us * 1e-6) / 1e9 / peak, 3)
+    return out
+
+
+def main_dense(argv=None) -> None:
+    ap = argparse.ArgumentParser(description="tcgen05 dense GEMMs vs cuBLAS at decode shapes")
+    ap.add_argument("--shapes", default=",".join(DENSE))
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args(argv)
+    for name in args.shapes.split(","):
+        print(json.dumps(run_dense(name, args.reps)), flush=True)
+
+
 if __name__ == "__main__":
-    main()
+    import sys
+
+    if "--dense" in sys.argv:
+        sys.argv.remove("--dense")
+        main_dense()
+    else:
+        main()

@@ -448,9 +448,11 @@ class FusedFFNRunner:
         self.meta_shared = torch.cat([((self.home_a0 + i) << 24) | (t << 8) | d.top_k for i in range(d.ratio)]).to(dev)
         self.rw_shared = torch.ones(d.ratio * d.t_cap, dtype=torch.float32, device=dev)
         self.no_flags = torch.zeros(1, dtype=torch.int64, device=dev)
-        from afd_plugin_b200.ops.moe import moe_sync_buffer
+        from afd_plugin_b200.ops.moe import moe_rows_hint, moe_sync_buffer
 
         self.sync = moe_sync_buffer(dev, d.e_local + self.n_chunks)
+        # routed rows per expert (all Attention ranks' tokens) and the home rows of a shared chunk
+        self.rows_hint = moe_rows_hint(A * d.t_cap, d.top_k, d.experts, self.n_chunks, d.ratio * d.t_cap)
         self._graphs: dict = {}
         self._pool = None
         self._prepare_weights()
@@ -537,8 +539,9 @@ class FusedFFNRunner:
             # in one persistent launch whose epilogue scatters into staging
             ne = d.e_local + n_chunks
             total = int(C.moe_ffn_grid(ne, w13.shape[1], w2.shape[1]))
-            C.moe_ffn(self.x[s], w13, w2, self.off_all, counts[:ne], self.sync, -1, self.meta[s], self.rw[s],
-                      self.staging_ptrs[s], self.no_flags, c.done[s, 1:2], counts, [self.J, H, total, 0, layer_idx])
+            C.moe_ffn(self.x[s], w13, w2, self.off_all, counts[:ne], self.sync, self.rows_hint, -1, self.meta[s],
+                      self.rw[s], self.staging_ptrs[s], self.no_flags, c.done[s, 1:2], counts,
+                      [self.J, H, total, 0, layer_idx])
         elif merged:
             ne = d.e_local + n_chunks
             h_r = C.grouped_gemm_ex(self.x[s], w13, self.off_all, counts[:ne], 1, ne)

@@ -201,7 +201,8 @@ class MLAAttention(nn.Module):
         # The two projections that read the layer input (q or q_a, and
         # kv_a_proj_with_mqa) share one weight so they run as one GEMM.
         self.n_q_in = arch.q_lora_rank if arch.q_lora_rank else nh * qk
-        self.in_proj = _param((self.n_q_in + self.kv_lora + self.qk_rope, H), dtype, device)
+        self.n_in = self.n_q_in + self.kv_lora + self.qk_rope
+        self.in_proj = _param((self.n_in, H), dtype, device)
         if arch.q_lora_rank:
             self.q_a_layernorm = RMSNorm(arch.q_lora_rank, arch.rms_norm_eps, dtype, device)
             self.q_b_proj = _param((nh * qk, arch.q_lora_rank), dtype, device)
@@ -220,7 +221,7 @@ class MLAAttention(nn.Module):
 
     @property
     def kv_a_proj_with_mqa(self) -> torch.Tensor:
-        return self.in_proj[self.n_q_in :]
+        return self.in_proj[self.n_q_in : self.n_in]
 
     def set_kv_b_proj(self, w: torch.Tensor) -> None:
         """Full checkpoint ``kv_b_proj [heads * (nope + v), kv_lora]``; keeps this rank's heads."""
@@ -232,7 +233,7 @@ class MLAAttention(nn.Module):
     def project(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
         """``(q [T, H, qk], kv_a [T, kv_lora + rope], q_latent [T, q_lora] | None)``; views may be strided."""
         y = ops.linear(h, self.in_proj)
-        kv_a = y[:, self.n_q_in :]
+        kv_a = y[:, self.n_q_in : self.n_in]
         q_latent = None
         if self.arch.q_lora_rank:
             q_latent = self.q_a_layernorm(y[:, : self.n_q_in].contiguous())

@@ -293,20 +293,55 @@ def moe_experts(
     )
 
 
+def _tc_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """Shapes the tcgen05 GEMM takes: bf16, N % 128 == 0, K % 64 == 0, 16-byte aligned rows."""
+    return (x.dtype == w.dtype == torch.bfloat16 and w.dim() == 2 and w.is_contiguous()
+            and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and x.dim() == 2 and x.stride(1) == 1
+            and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0)
+
+
 def dense_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
+    """SwiGLU MLP (a dense layer).  CUDA: cuBLAS GEMMs plus the SiLU-mul kernel
+    (``dense_ffn``, the one-launch tcgen05 version, is slower at 256-token
+    decode batches: its down projection has only H / 128 weight tiles)."""
     if _cuda(x):
         return torch.mm(silu_and_mul(torch.mm(x, w13.t())), w2.t())
     return ref.dense_mlp(x, w13, w2)
 
 
-def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """Plain ``x @ w.T`` (cuBLAS on CUDA, fp32-accumulating reference on CPU)."""
+def linear(x: torch.Tensor, w: torch.Tensor, *, n_valid: int = 0, out_f32: bool = False) -> torch.Tensor:
+    """``x @ w.T`` (cuBLAS on CUDA, fp32-accumulating reference on CPU).
+
+    ``n_valid`` keeps the first ``n_valid`` output columns (a weight padded with
+    zero rows); ``out_f32`` returns fp32 logits.  The dense decode projections
+    stay on cuBLAS: the tcgen05 kernel here streams weights with the tokens as
+    the MMA's N operand, which wins for expert segments of a few dozen tokens
+    (``moe_ffn``) but loses 4-5x to cuBLAS's token-tiled kernels at 256-token
+    dense projections (``tc_gemm``, measured in ``bench/grouped_gemm_bench.py
+    --dense``).
+    """
     if _cuda(x):
-        return torch.mm(x, w.t())
-    return (x.float() @ w.float().t()).to(x.dtype)
+        y = torch.mm(x, w.t(), out_dtype=torch.float32) if out_f32 else torch.mm(x, w.t())
+        return y[:, :n_valid] if n_valid else y
+    y = x.float() @ w.float().t()
+    y = y if out_f32 else y.to(x.dtype)
+    return y[:, :n_valid] if n_valid else y
+
+
+def head_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Per-head product ``x [E, T, K]`` x ``w [E, N, K]`` -> ``[T, E * N]`` token-major (cuBLAS on CUDA)."""
+    E, T, _ = x.shape
+    if x.is_cuda:
+        y = torch.bmm(x, w.transpose(1, 2))
+    else:
+        y = torch.bmm(x.float(), w.float().transpose(1, 2)).to(x.dtype)
+    return y.transpose(0, 1).reshape(T, E * w.shape[1])
 
 
 def argmax(logits: torch.Tensor) -> torch.Tensor:
+    """Greedy token per row (int32), lowest index on ties; reads bf16 logits in place on CUDA."""
+    if _cuda(logits) and logits.dim() == 2 and logits.stride(1) == 1:
+        return _cuda_ops().argmax_rows(logits)
     return torch.argmax(logits.float(), dim=-1).to(torch.int32)
 
 
@@ -316,6 +351,7 @@ __all__ = [
     "fused_add_rms_norm",
     "gqa_cache_write",
     "gqa_decode",
+    "head_linear",
     "linear",
     "mla_cache_write",
     "mla_decode",

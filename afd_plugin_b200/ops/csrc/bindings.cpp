@@ -87,6 +87,16 @@ at::Tensor silu_and_mul(const at::Tensor& x) {
   return out;
 }
 
+at::Tensor argmax_rows(const at::Tensor& x) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "argmax_rows: x [rows, n] with contiguous rows");
+  auto out = at::empty({x.size(0)}, x.options().dtype(at::kInt));
+  c10::cuda::CUDAGuard g(x.device());
+  launch_argmax_rows(x.data_ptr(), x.stride(0), (int)x.size(0), (int)x.size(1), dtype_code(x),
+                     out.data_ptr<int32_t>(), stream());
+  return out;
+}
+
 void rope_(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin, bool interleaved) {
   check_cuda(x, "x");
   TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "rope_: x must be [T, H, rot] with contiguous last dim");
@@ -345,10 +355,11 @@ at::Tensor grouped_gemm(const at::Tensor& a, const at::Tensor& w, const at::Tens
 // routing-weighted rows go to the Attention ranks' combine slots (epilogue 2).
 // sync: int32 [>= e_local + 1], zero before the first call and left zero by
 // every call ([0, e_local) per-expert tile counters, [e_local] CTA counter).
+// rows_hint: the largest segment expected (picks the pass width, not the result).
 // scatter (optional): meta, rw, dst_ptrs, flag_ptrs, done_ctr, counts_reset
 // and cfg [J, H, total_ctas, num_dst, layer] as in grouped_gemm_scatter.
 at::Tensor moe_ffn(const at::Tensor& a, const at::Tensor& w13, const at::Tensor& w2, const at::Tensor& offsets,
-                   const at::Tensor& counts, at::Tensor& sync, int64_t w_experts,
+                   const at::Tensor& counts, at::Tensor& sync, int64_t rows_hint, int64_t w_experts,
                    const c10::optional<at::Tensor>& meta, const c10::optional<at::Tensor>& rw,
                    const c10::optional<at::Tensor>& dst_ptrs, const c10::optional<at::Tensor>& flag_ptrs,
                    const c10::optional<at::Tensor>& done_ctr, const c10::optional<at::Tensor>& counts_reset,
@@ -403,8 +414,106 @@ at::Tensor moe_ffn(const at::Tensor& a, const at::Tensor& w13, const at::Tensor&
   int32_t* sy = sync.data_ptr<int32_t>();
   c10::cuda::CUDAGuard guard(a.device());
   const cudaError_t e = launch_grouped_gemm_phases(g0, &g1, sy, reinterpret_cast<unsigned*>(sy + e_local),
-                                                   status_ptr(a), scatter ? &sp : nullptr, stream());
+                                                   status_ptr(a), scatter ? &sp : nullptr, stream(), (int)rows_hint);
   TORCH_CHECK(e == cudaSuccess, "moe_ffn: launch failed: ", cudaGetErrorString(e));
+  return y;
+}
+
+// Dense or per-head-batched GEMM on the tcgen05 grouped kernel (no library GEMM).
+//   a [T, K] (rows any stride, 16-byte aligned), w [N, K] or [1, N, K]:
+//     out [T, N] (epilogue 0) or SiLU(gate) * up [T, N / 2] (epilogue 1).
+//   a [E, T, K] (any strides with a contiguous last dim, e.g. a per-head view
+//     of a projection), w [E, N, K]: out [T, E * N] with out[t, e * N + n] =
+//     a[e, t] . w[e, n] -- a batched product written token-major.
+// N % 128 == 0 (N / 2 % 64 == 0 for SwiGLU) and K % 64 == 0.  Dense epilogue 0
+// only: n_valid keeps the first n_valid output columns (weights padded to a
+// multiple of 128 rows), out_f32 stores fp32 (e.g. router logits).  With ws
+// (fp32, zero) and ctr (int32, zero) a GEMM with few output tiles splits K
+// over the SMs; both are left zero.
+at::Tensor tc_gemm(const at::Tensor& a, const at::Tensor& w, int64_t epilogue, int64_t n_valid, bool out_f32,
+                   const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& ctr) {
+  check_cuda(a, "a");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && w.is_contiguous(),
+              "tc_gemm: bf16, contiguous weights");
+  TORCH_CHECK(a.stride(-1) == 1 && reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0, "tc_gemm: 16-byte aligned a");
+  const bool batched = a.dim() == 3;
+  TORCH_CHECK(a.dim() == 2 || batched, "tc_gemm: a [T, K] or [E, T, K]");
+  const int64_t E = batched ? a.size(0) : 1, T = a.size(-2), K = a.size(-1);
+  const at::Tensor w3 = w.dim() == 2 ? w.unsqueeze(0) : w;
+  TORCH_CHECK(w3.dim() == 3 && w3.size(0) == E && w3.size(2) == K, "tc_gemm: w [E, N, K] matching a");
+  const int64_t N = w3.size(1);
+  TORCH_CHECK(K % 64 == 0, "tc_gemm: K must be a multiple of 64");
+  for (int d = 0; d + 1 < a.dim(); ++d)
+    TORCH_CHECK(a.stride(d) % 8 == 0, "tc_gemm: activation strides must be multiples of 16 bytes");
+  if (epilogue == 1) {
+    TORCH_CHECK(!batched && N % 128 == 0, "tc_gemm: SwiGLU for a dense [T, K] input with N % 128 == 0");
+  } else {
+    TORCH_CHECK(epilogue == 0 && N % 128 == 0, "tc_gemm: epilogue 0 or 1, N % 128 == 0");
+  }
+  const bool narrow = n_valid > 0 && n_valid < N;
+  TORCH_CHECK(!(narrow || out_f32) || (!batched && epilogue == 0), "tc_gemm: n_valid / out_f32 need a dense epilogue 0");
+  TORCH_CHECK(n_valid >= 0 && n_valid <= N, "tc_gemm: 0 <= n_valid <= N");
+  const int64_t n_out = epilogue == 1 ? N / 2 : (narrow ? n_valid : N * E);
+  auto d = at::empty({T, n_out}, a.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
+  if (T == 0) return d;
+  GemmSpec g{d.data_ptr(), a.data_ptr(), w3.data_ptr(), nullptr, nullptr, (int)E, (int)T, (int)N, (int)K,
+             batched ? 3 : (int)epilogue, -1};
+  g.fixed_count = (int)T;
+  g.out_f32 = out_f32 ? 1 : 0;
+  g.n_valid = narrow ? (int)n_valid : 0;
+  // Split K when the output tiles alone would leave SMs idle (few weight rows):
+  // one wave of items over the SMs, fp32 partials reduced in the workspace.
+  const int64_t tiles = E * (epilogue == 1 ? (N / 2) / 64 : N / 128);
+  const int sms = (int)grouped_gemm_grid(1 << 30);
+  if (epilogue == 0 && ws.has_value() && ctr.has_value() && tiles * 2 <= sms) {
+    TORCH_CHECK(ws->scalar_type() == at::kFloat && ctr->scalar_type() == at::kInt && ws->device() == a.device() &&
+                    ctr->device() == a.device(), "tc_gemm: fp32 workspace and int32 tile counters on a's device");
+    const int64_t cols = narrow ? n_valid : N * E;
+    if (T * cols <= ws->numel() && tiles <= ctr->numel()) {
+      g.k_splits = (int)std::min<int64_t>(K / 64, sms / tiles);
+      g.acc_ws = ws->data_ptr<float>();
+      g.tile_ctr = ctr->data_ptr<int32_t>();
+    }
+  }
+  g.a_ld = a.stride(-2);
+  g.a_plane = batched ? a.stride(0) : 0;
+  c10::cuda::CUDAGuard guard(a.device());
+  const cudaError_t e =
+      launch_grouped_gemm_phases(g, nullptr, nullptr, nullptr, status_ptr(a), nullptr, stream(), (int)T);
+  TORCH_CHECK(e == cudaSuccess, "tc_gemm: launch failed: ", cudaGetErrorString(e));
+  return d;
+}
+
+// Dense SwiGLU MLP in one launch: h = SiLU(x w_gate^T) * (x w_up^T), y = h w2^T,
+// as the two phases of the tcgen05 kernel over one segment of T rows.
+// x [T, H] (rows any 16-byte multiple apart), w13 [2I, H], w2 [H, I]; sync as in moe_ffn.
+at::Tensor dense_ffn(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& w2, at::Tensor& sync) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w13.scalar_type() == at::kBFloat16 &&
+                  w2.scalar_type() == at::kBFloat16 && w13.is_contiguous() && w2.is_contiguous(),
+              "dense_ffn: bf16, contiguous weights");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "dense_ffn: x [T, H], 16-byte aligned rows");
+  const int64_t T = x.size(0), H = x.size(1);
+  const at::Tensor a13 = w13.dim() == 3 ? w13[0] : w13, a2 = w2.dim() == 3 ? w2[0] : w2;
+  const int64_t N1 = a13.size(0), I = N1 / 2, N2 = a2.size(0);
+  TORCH_CHECK(a13.size(1) == H && H % 64 == 0 && N1 % 128 == 0 && I % 64 == 0, "dense_ffn: w13 [2I, H]");
+  TORCH_CHECK(a2.size(1) == I && N2 % 128 == 0, "dense_ffn: w2 [N % 128 == 0, I]");
+  TORCH_CHECK(sync.scalar_type() == at::kInt && sync.numel() >= 2 && sync.device() == x.device(),
+              "dense_ffn: int32 sync [>= 2]");
+  auto h = at::empty({T, I}, x.options());
+  auto y = at::empty({T, N2}, x.options());
+  if (T == 0) return y;
+  GemmSpec g0{h.data_ptr(), x.data_ptr(), a13.data_ptr(), nullptr, nullptr, 1, (int)T, (int)N1, (int)H, 1, 1};
+  g0.fixed_count = (int)T;
+  g0.a_ld = x.stride(0);
+  GemmSpec g1{y.data_ptr(), h.data_ptr(), a2.data_ptr(), nullptr, nullptr, 1, (int)T, (int)N2, (int)I, 0, 1};
+  g1.fixed_count = (int)T;
+  int32_t* sy = sync.data_ptr<int32_t>();
+  c10::cuda::CUDAGuard guard(x.device());
+  const cudaError_t e = launch_grouped_gemm_phases(g0, &g1, sy, reinterpret_cast<unsigned*>(sy + 1), status_ptr(x),
+                                                   nullptr, stream(), (int)T);
+  TORCH_CHECK(e == cudaSuccess, "dense_ffn: launch failed: ", cudaGetErrorString(e));
   return y;
 }
 
@@ -855,6 +964,7 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("rms_norm(Tensor x, Tensor w, float eps) -> Tensor");
   m.def("fused_add_rms_norm(Tensor x, Tensor(a!) residual, Tensor w, float eps) -> Tensor");
   m.def("silu_and_mul(Tensor x) -> Tensor");
+  m.def("argmax_rows(Tensor x) -> Tensor");
   m.def("rope_(Tensor(a!) x, Tensor positions, Tensor cos_sin, bool interleaved) -> ()");
   m.def("topk_route(Tensor logits, int k, int scoring, bool renorm, Tensor? bias, int n_group, int topk_group, "
         "float scale, Tensor? forced=None) -> (Tensor, Tensor)");
@@ -896,10 +1006,13 @@ TORCH_LIBRARY(afd_b200, m) {
         "int w_experts) -> Tensor");
   m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
   m.def("grouped_gemm_grid(int n_items) -> int");
-  m.def("moe_ffn(Tensor a, Tensor w13, Tensor w2, Tensor offsets, Tensor counts, Tensor(a!) sync, "
+  m.def("moe_ffn(Tensor a, Tensor w13, Tensor w2, Tensor offsets, Tensor counts, Tensor(a!) sync, int rows_hint, "
         "int w_experts=-1, Tensor? meta=None, Tensor? rw=None, Tensor? dst_ptrs=None, Tensor? flag_ptrs=None, "
         "Tensor(b!)? done_ctr=None, Tensor(c!)? counts_reset=None, int[]? cfg=None) -> Tensor");
   m.def("moe_ffn_grid(int e_local, int n1, int n2) -> int");
+  m.def("tc_gemm(Tensor a, Tensor w, int epilogue=0, int n_valid=0, bool out_f32=False, Tensor(a!)? ws=None, "
+        "Tensor(b!)? ctr=None) -> Tensor");
+  m.def("dense_ffn(Tensor x, Tensor w13, Tensor w2, Tensor(a!) sync) -> Tensor");
   m.def("read_status(int device) -> int");
   m.def("reset_status(int device) -> ()");
   m.def("status_word(int device) -> Tensor");
@@ -909,6 +1022,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
   m.impl("fused_add_rms_norm", &fused_add_rms_norm);
   m.impl("silu_and_mul", &silu_and_mul);
+  m.impl("argmax_rows", &argmax_rows);
   m.impl("rope_", &rope_);
   m.impl("topk_route", &topk_route);
   m.impl("mla_cache_write", &mla_cache_write);
@@ -931,6 +1045,8 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("grouped_gemm_scatter", &grouped_gemm_scatter);
   m.impl("grouped_gemm_ex", &grouped_gemm_ex);
   m.impl("moe_ffn", &moe_ffn);
+  m.impl("tc_gemm", &tc_gemm);
+  m.impl("dense_ffn", &dense_ffn);
   m.impl("grouped_gemm_w8", &grouped_gemm_w8);
   m.impl("afd_expand", &afd_expand);
   m.impl("afd_combine_send", &afd_combine_send);

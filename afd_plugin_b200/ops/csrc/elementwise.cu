@@ -297,9 +297,84 @@ __global__ void decode_advance_kernel(int32_t* __restrict__ input_ids, int64_t* 
   slots[b] = (int64_t)table[(size_t)b * table_stride + p / block_size] * block_size + p % block_size;
 }
 
+// ============================================================ row argmax
+// One CTA per row, 16-byte loads; ties go to the lowest index (torch.argmax).
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(512) argmax_rows_kernel(const T* __restrict__ x, int64_t ld, int n,
+                                                         int32_t* __restrict__ out) {
+  __shared__ float s_v[16];
+  __shared__ int s_i[16];
+  const T* row = x + (size_t)blockIdx.x * ld;
+  constexpr int V = 16 / sizeof(T);
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const int nv = kVec ? n / V : 0;
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+    const Vec16<T> c = load16(row + (size_t)v * V);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float f = to_f32(c.v[j]);
+      if (f > best) {
+        best = f;
+        bi = v * V + j;
+      }
+    }
+  }
+  for (int i = nv * V + threadIdx.x; i < n; i += blockDim.x) {
+    const float f = to_f32(row[i]);
+    if (f > best || (f == best && i < bi)) {
+      best = f;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    s_v[warp] = best;
+    s_i[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)blockDim.x / 32; ++w)
+      if (s_v[w] > best || (s_v[w] == best && s_i[w] < bi)) {
+        best = s_v[w];
+        bi = s_i[w];
+      }
+    out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
 void launch_decode_advance(int32_t* input_ids, int64_t* positions, int64_t* slots, int32_t* seq_lens,
                            const int32_t* next_tokens, const int32_t* table, int batch, int table_stride,
                            int block_size, int64_t wrap_at, int64_t wrap_to, cudaStream_t s) {
   decode_advance_kernel<<<(batch + 127) / 128, 128, 0, s>>>(input_ids, positions, slots, seq_lens, next_tokens,
                                                             table, batch, table_stride, block_size, wrap_at, wrap_to);
+}
+
+template <typename T>
+static void argmax_rows_go(const void* x, int64_t ld, int rows, int n, int32_t* out, cudaStream_t s) {
+  const T* p = static_cast<const T*>(x);
+  const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ld * (int64_t)sizeof(T)) % 16 == 0);
+  if (vec)
+    argmax_rows_kernel<T, true><<<rows, 512, 0, s>>>(p, ld, n, out);
+  else
+    argmax_rows_kernel<T, false><<<rows, 512, 0, s>>>(p, ld, n, out);
+}
+
+void launch_argmax_rows(const void* x, int64_t ld, int rows, int n, int dtype, int32_t* out, cudaStream_t s) {
+  if (rows <= 0) return;
+  if (dtype == kBF16)
+    argmax_rows_go<__nv_bfloat16>(x, ld, rows, n, out, s);
+  else if (dtype == kF16)
+    argmax_rows_go<__half>(x, ld, rows, n, out, s);
+  else
+    argmax_rows_go<float>(x, ld, rows, n, out, s);
 }

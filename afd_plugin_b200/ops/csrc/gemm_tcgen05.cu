@@ -20,6 +20,7 @@
 // winds down (TMEM is always released).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <type_traits>
 
 #include <cuda_fp8.h>
@@ -40,31 +41,26 @@ constexpr int kThreads = 6 * 32;
 constexpr int kWBytes = kBM * kBK * 2;          // 16 KB
 constexpr int kSubBytes = kSub * kBK * 2;       // 8 KB
 
-// Pipeline: a ring of kWStages weight tiles (128 rows x 64 K, 16 KB each) and
-// a separate ring of kASlots activation sub-tiles (64 tokens x 64 K, 8 KB).
-// A stage takes one weight slot and 1-4 activation slots (the pass's tokens),
-// and each activation slot gets its own N = 64 MMA into its 64 accumulator
-// columns, so the slots of a stage need not be adjacent.  Weight bytes in
-// flight stay at 8 x 16 KB per SM whatever the token count (decode experts
-// see ~24 tokens, shared-expert chunks the whole batch), which is what a
-// weight-streaming GEMM needs to saturate HBM.
-constexpr int kWStages = 8;
-constexpr int kASlots = 10;
-constexpr int kMaxSub = 4;                      // tokens per pass <= 256
-constexpr int kPassRows = kMaxSub * kSub;
-constexpr uint32_t kAccCols = kPassRows;        // one accumulator: 128 lanes x 256 fp32 columns
+// Pipeline: a ring of STAGES stages, each one weight tile (128 rows x 64 K,
+// 16 KB) plus SUB activation sub-tiles (64 tokens x 64 K, 8 KB each, adjacent
+// so one MMA of N = 64 * n_sub covers them).  A pass covers SUB * 64 tokens
+// of an expert; wider segments take several passes over its weights.  The
+// shapes instantiated trade pass width for weight bytes in flight per SM:
+// (4 stages, 256 tokens), (6, 128) and (8, 64).
+constexpr uint32_t kAccCols = 256;              // one accumulator: 128 lanes x up to 256 fp32 columns
 constexpr uint32_t kTmemCols = 2 * kAccCols;    // two accumulators
 
+template <int STAGES, int SUB>
 struct Smem {
-  alignas(1024) uint8_t w[kWStages][kWBytes];
-  alignas(1024) uint8_t a[kASlots][kSubBytes];
+  alignas(1024) uint8_t w[STAGES][kWBytes];
+  alignas(1024) uint8_t a[STAGES][SUB * kSubBytes];
   float xchg[32 * 64];  // SwiGLU exchange: [col][row] for the 64 up rows
-  uint64_t full[kWStages];
-  uint64_t empty_w[kWStages];
-  uint64_t empty_a[kASlots];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
+  int last_split;
 };
 
 // K-major, 128B-swizzled operand descriptor (8-row groups 1024 B apart).
@@ -183,7 +179,7 @@ AFD_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.glo
 // one expert at the same time share its activation tiles in L2, and every
 // phase-1 item comes after all phase-0 items.
 struct PItem {
-  int ph, e, nt, cnt, seg;
+  int ph, e, nt, cnt, seg, kb0, kb1;  // K blocks [kb0, kb1) of the weight rows
 };
 
 AFD_DEVICE bool next_phase_item(int& idx, const GGArgs& g, int n0, int n_all, PItem& it) {
@@ -191,14 +187,20 @@ AFD_DEVICE bool next_phase_item(int& idx, const GGArgs& g, int n0, int n_all, PI
     const int ph = idx < n0 ? 0 : 1;
     const GGPhase& P = g.ph[ph];
     const int j = ph ? idx - n0 : idx;
-    const int e = j / P.n_tiles;
-    const int c = P.counts[e];
+    const int per_e = P.n_tiles * P.k_splits;
+    const int e = j / per_e;
+    const int c = P.counts ? P.counts[e] : P.fixed_count;
     if (c > 0) {
+      const int rem = j - e * per_e;
+      const int ks = rem % P.k_splits;
+      const int kb_total = P.k_dim / kBK;
       it.ph = ph;
       it.e = e;
-      it.nt = j - e * P.n_tiles;
+      it.nt = rem / P.k_splits;
       it.cnt = c;
-      it.seg = P.offsets[e];
+      it.seg = P.offsets ? P.offsets[e] : 0;
+      it.kb0 = ks * P.kb_per;
+      it.kb1 = min(kb_total, it.kb0 + P.kb_per);
       idx += gridDim.x;
       return true;
     }
@@ -219,23 +221,25 @@ AFD_DEVICE bool next_phase_item(int& idx, const GGArgs& g, int n0, int n_all, PI
 // always ends.  One launch keeps the SMs busy across the phase boundary (no
 // kernel boundary, no tail of the first GEMM), and the intermediate rows stay
 // in L2.  The last CTA to finish clears the counters for the next launch.
+template <int STAGES, int SUB>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     const __grid_constant__ CUtensorMap w_map0, const __grid_constant__ CUtensorMap a_map0,
     const __grid_constant__ CUtensorMap w_map1, const __grid_constant__ CUtensorMap a_map1,
     const __grid_constant__ GGArgs g, const ScatterParams sp) {
+  constexpr int kPassRows = SUB * kSub;
   extern __shared__ uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using SmemT = Smem<STAGES, SUB>;
+  SmemT& sm = *reinterpret_cast<SmemT*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const int n0 = g.ph[0].n_tiles * g.ph[0].n_experts;
-  const int n_all = n0 + (g.n_phases > 1 ? g.ph[1].n_tiles * g.ph[1].n_experts : 0);
+  const int n0 = g.ph[0].n_tiles * g.ph[0].k_splits * g.ph[0].n_experts;
+  const int n_all = n0 + (g.n_phases > 1 ? g.ph[1].n_tiles * g.ph[1].k_splits * g.ph[1].n_experts : 0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kWStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty_w[s], 1);
+      mbar_init(&sm.empty[s], 1);
     }
-    for (int s = 0; s < kASlots; ++s) mbar_init(&sm.empty_a[s], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.acc_full[b], 1);
       mbar_init(&sm.acc_empty[b], 4);
@@ -277,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         prefetch_tensormap(&w_map1);
         prefetch_tensormap(&a_map1);
       }
-      int w_count = 0, a_count = 0, idx = blockIdx.x;
+      int it_count = 0, idx = blockIdx.x;
       PItem it;
       bool ok = true;
       while (ok && next_phase_item(idx, g, n0, n_all, it)) {
@@ -301,32 +305,26 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         }
         int r0, r1;
         w_rows(it, r0, r1);
-        const int kb_total = P.k_dim / kBK;
         const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
         for (int p = 0; p < n_pass && ok; ++p) {
-          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
-          for (int kb = 0; kb < kb_total && ok; ++kb, ++w_count) {
-            const int st = w_count % kWStages;
-            if (!mbar_wait_bounded(&sm.empty_w[st], ((w_count / kWStages) & 1) ^ 1)) {
+          const int n_sub = min(SUB, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          for (int kb = it.kb0; kb < it.kb1; ++kb, ++it_count) {
+            const int st = it_count % STAGES;
+            if (!mbar_wait_bounded(&sm.empty[st], ((it_count / STAGES) & 1) ^ 1)) {
               atomicExch(g.status, kStatusWaitTimeout);
               ok = false;
               break;
             }
-            int slot[kMaxSub];
-            for (int s2 = 0; s2 < n_sub; ++s2, ++a_count) {
-              slot[s2] = a_count % kASlots;
-              if (!mbar_wait_bounded(&sm.empty_a[slot[s2]], ((a_count / kASlots) & 1) ^ 1)) {
-                atomicExch(g.status, kStatusWaitTimeout);
-                ok = false;
-                break;
-              }
-            }
-            if (!ok) break;
             mbar_expect_tx(&sm.full[st], kWBytes + n_sub * kSubBytes);
             tma_load_2d(sm.w[st], wm, &sm.full[st], kb * kBK, r0);
             tma_load_2d(sm.w[st] + kWBytes / 2, wm, &sm.full[st], kb * kBK, r1);
-            for (int s2 = 0; s2 < n_sub; ++s2)
-              tma_load_2d(sm.a[slot[s2]], am, &sm.full[st], kb * kBK, it.seg + p * kPassRows + s2 * kSub);
+            for (int s2 = 0; s2 < n_sub; ++s2) {
+              const int arow = it.seg + p * kPassRows + s2 * kSub;
+              if (P.a3d)
+                tma_load_3d(sm.a[st] + s2 * kSubBytes, am, &sm.full[st], kb * kBK, arow, it.e);
+              else
+                tma_load_2d(sm.a[st] + s2 * kSubBytes, am, &sm.full[st], kb * kBK, arow);
+            }
           }
         }
       }
@@ -334,15 +332,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      int w_count = 0, a_count = 0, acc_count = 0, idx = blockIdx.x;
+      int it_count = 0, acc_count = 0, idx = blockIdx.x;
       PItem it;
       bool ok = true;
-      const uint32_t idesc = make_idesc(kBM, kSub);  // one N = 64 MMA per activation slot
       while (ok && next_phase_item(idx, g, n0, n_all, it)) {
-        const int kb_total = g.ph[it.ph].k_dim / kBK;
         const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
         for (int p = 0; p < n_pass && ok; ++p, ++acc_count) {
-          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          const int n_sub = min(SUB, (it.cnt - p * kPassRows + kSub - 1) / kSub);
+          const uint32_t idesc = make_idesc(kBM, n_sub * kSub);
           const int ab = acc_count & 1;
           if (!mbar_wait_bounded(&sm.acc_empty[ab], ((acc_count >> 1) & 1) ^ 1)) {
             atomicExch(g.status, kStatusWaitTimeout);
@@ -351,23 +348,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           }
           tc_fence_after();
           const uint32_t tacc = tmem + ab * kAccCols;
-          for (int kb = 0; kb < kb_total; ++kb, ++w_count) {
-            const int st = w_count % kWStages;
-            if (!mbar_wait_bounded(&sm.full[st], (w_count / kWStages) & 1)) {
+          for (int kb = it.kb0; kb < it.kb1; ++kb, ++it_count) {
+            const int st = it_count % STAGES;
+            if (!mbar_wait_bounded(&sm.full[st], (it_count / STAGES) & 1)) {
               atomicExch(g.status, kStatusWaitTimeout);
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t wa = smem_u32(sm.w[st]);
-            for (int s2 = 0; s2 < n_sub; ++s2) {
-              const uint32_t aa = smem_u32(sm.a[(a_count + s2) % kASlots]);
+            const uint32_t aa = smem_u32(sm.a[st]);
 #pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk)
-                umma(tacc + s2 * kSub, make_desc(wa + kk * 32), make_desc(aa + kk * 32), idesc, (kb | kk) != 0);
-            }
-            umma_commit(&sm.empty_w[st]);
-            for (int s2 = 0; s2 < n_sub; ++s2, ++a_count) umma_commit(&sm.empty_a[a_count % kASlots]);
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma(tacc, make_desc(wa + kk * 32), make_desc(aa + kk * 32), idesc, ((kb - it.kb0) | kk) != 0);
+            umma_commit(&sm.empty[st]);
           }
           if (ok) umma_commit(&sm.acc_full[ab]);
         }
@@ -402,11 +396,32 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         for (int c0 = 0; c0 < n_cols; c0 += 32) {
           float v[32];
           tmem_ld32(tacc + c0, v);
-          if (epi == 0) {
-            const int col = it.nt * kBM + row;
+          if (P.k_splits > 1) {
+            // partial sum of this K slice: fp32 atomics into the tile's workspace rows
+            const int col = it.nt * kBM + row + (epi == 3 ? it.e * P.n_w : 0);
+            const int rb = epi == 3 ? r_base - it.seg : r_base;
+            if (epi == 3 || col < P.n_valid) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (c0 + j < n_cols) d[(size_t)(r_base + c0 + j) * ld_d + col] = __float2bfloat16_rn(v[j]);
+              for (int j = 0; j < 32; ++j)
+                if (c0 + j < n_cols) atomicAdd(P.acc_ws + (size_t)(rb + c0 + j) * ld_d + col, v[j]);
+            }
+          } else if (epi == 0 && P.out_f32) {
+            const int col = it.nt * kBM + row;
+            float* df = reinterpret_cast<float*>(d);
+            if (col < P.n_valid) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (c0 + j < n_cols) df[(size_t)(r_base + c0 + j) * ld_d + col] = v[j];
+            }
+          } else if (epi == 0 || epi == 3) {
+            // epilogue 3: rows relative to the segment, columns in the expert's block
+            const int col = it.nt * kBM + row + (epi == 3 ? it.e * P.n_w : 0);
+            const int rb = epi == 3 ? r_base - it.seg : r_base;
+            if (epi == 3 || col < P.n_valid) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (c0 + j < n_cols) d[(size_t)(rb + c0 + j) * ld_d + col] = __float2bfloat16_rn(v[j]);
+            }
           } else if (epi == 2) {
             // routing weight applied, row stored into the source rank's slot
             const int col = it.nt * kBM + row;
@@ -442,6 +457,34 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         }
         tc_fence_before();
         if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
+      }
+      if (ok && P.k_splits > 1) {
+        // the last K slice of a tile to finish turns the fp32 sums into the output
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == 2 && lane == 0) {
+          int* ctr = P.tile_ctr + it.e * P.n_tiles + it.nt;
+          const int last = atomicAdd(ctr, 1) == P.k_splits - 1;
+          if (last) *ctr = 0;
+          sm.last_split = last;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (sm.last_split) {
+          __threadfence();
+          const int col = it.nt * kBM + row + (epi == 3 ? it.e * P.n_w : 0);
+          const int rb = epi == 3 ? 0 : it.seg;
+          if (epi == 3 || col < P.n_valid) {
+            for (int r = 0; r < it.cnt; ++r) {
+              float* src = P.acc_ws + (size_t)(rb + r) * ld_d + col;
+              const float x = __ldcg(src);
+              __stcg(src, 0.f);
+              if (P.out_f32)
+                reinterpret_cast<float*>(d)[(size_t)(rb + r) * ld_d + col] = x;
+              else
+                d[(size_t)(rb + r) * ld_d + col] = __float2bfloat16_rn(x);
+            }
+          }
+        }
       }
       if (ok && P.done != nullptr) {
         // this tile's rows are stored: count it for the expert's phase-1 items
@@ -804,11 +847,39 @@ int grouped_gemm_grid(int n_items) {
 
 namespace {
 
+// Activation map: rows of K elements a_ld apart, or (a_plane > 0) one plane
+// of rows_cap rows per expert, a_plane elements apart.
+void encode_activations(CUtensorMap* map, const GemmSpec& g) {
+  const uint64_t ld = g.a_ld > 0 ? (uint64_t)g.a_ld : (uint64_t)g.k;
+  if (g.a_plane <= 0 && ld == (uint64_t)g.k) {
+    gg::encode_2d(map, g.a, g.rows_cap, g.k, gg::kSub);
+    return;
+  }
+  const int rank = g.a_plane > 0 ? 3 : 2;
+  const cuuint64_t dims[3] = {(cuuint64_t)g.k, (cuuint64_t)g.rows_cap, (cuuint64_t)g.e_local};
+  const cuuint64_t strides[2] = {ld * 2, (cuuint64_t)(g.a_plane > 0 ? g.a_plane : 0) * 2};
+  const cuuint32_t box[3] = {gg::kBK, gg::kSub, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  get_tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(g.a), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
 GGPhase make_phase(const GemmSpec& g, CUtensorMap* wmap, CUtensorMap* amap) {
   const int w_experts = g.w_experts < 0 ? g.e_local : g.w_experts;
   gg::encode_2d(wmap, g.w, (uint64_t)w_experts * g.n, g.k, 64);
-  gg::encode_2d(amap, g.a, g.rows_cap, g.k, gg::kSub);
+  encode_activations(amap, g);
   GGPhase P{};
+  P.a3d = g.a_plane > 0 ? 1 : 0;
+  P.fixed_count = g.fixed_count;
+  P.out_f32 = g.out_f32;
+  P.n_valid = g.n_valid > 0 ? g.n_valid : g.n;
+  const int kb_total = g.k / gg::kBK;
+  P.k_splits = (g.k_splits > 1 && g.acc_ws && g.tile_ctr) ? min(g.k_splits, kb_total) : 1;
+  P.kb_per = (kb_total + P.k_splits - 1) / P.k_splits;
+  P.k_splits = (kb_total + P.kb_per - 1) / P.kb_per;  // no empty slices
+  P.acc_ws = g.acc_ws;
+  P.tile_ctr = g.tile_ctr;
   P.d = static_cast<__nv_bfloat16*>(g.d);
   P.offsets = g.offsets;
   P.counts = g.counts;
@@ -823,22 +894,42 @@ GGPhase make_phase(const GemmSpec& g, CUtensorMap* wmap, CUtensorMap* amap) {
     P.ld_d = g.n / 2;
   } else {
     P.n_tiles = g.n / gg::kBM;
-    P.ld_d = g.n;
+    P.ld_d = g.epilogue == 3 ? g.n * g.e_local : (g.n_valid > 0 ? g.n_valid : g.n);
   }
   return P;
 }
 
+template <int STAGES, int SUB>
 cudaError_t launch_kernel(const CUtensorMap& w0, const CUtensorMap& a0, const CUtensorMap& w1, const CUtensorMap& a1,
                           const GGArgs& args, const ScatterParams& sp, int n_items, cudaStream_t s) {
-  const int smem = (int)sizeof(gg::Smem) + 1024;
+  const int smem = (int)sizeof(gg::Smem<STAGES, SUB>) + 1024;
   static PerDeviceOnce attr;
   cudaError_t e = attr.run([&] {
-    return cudaFuncSetAttribute(gg::grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    return cudaFuncSetAttribute(gg::grouped_gemm_kernel<STAGES, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem);
   });
   if (e != cudaSuccess) return e;
   const int grid = grouped_gemm_grid(n_items);
-  return launch_pdl(gg::grouped_gemm_kernel, dim3(grid), dim3(gg::kThreads), (size_t)smem, s, w0, a0, w1, a1, args,
-                    sp);
+  return launch_pdl(gg::grouped_gemm_kernel<STAGES, SUB>, dim3(grid), dim3(gg::kThreads), (size_t)smem, s, w0, a0,
+                    w1, a1, args, sp);
+}
+
+// Tokens per pass for a launch whose segments are expected to need rows_hint
+// rows per pass.  Measured on B200 at decode shapes: 64-token passes (8
+// stages) stream routed experts fastest (0.92-0.99 of HBM); with a few
+// whole-batch segments among them (shared-expert chunks) 128-token passes (6
+// stages) win even though those segments take two passes (callers pass 128
+// then); 256-token passes (4 stages) suit dense GEMMs over a 256-row batch.
+// AFD_GG_PIPE=64|128|256 forces one shape for experiments.
+int pipe_rows(int rows_hint) {
+  static const int forced = [] {
+    const char* v = std::getenv("AFD_GG_PIPE");
+    const int r = v ? std::atoi(v) : 0;
+    return (r == 64 || r == 128 || r == 256) ? r : 0;
+  }();
+  if (forced) return forced;
+  if (rows_hint <= 64) return 64;
+  return rows_hint <= 128 ? 128 : 256;
 }
 
 }  // namespace
@@ -846,7 +937,7 @@ cudaError_t launch_kernel(const CUtensorMap& w0, const CUtensorMap& a0, const CU
 int grouped_gemm_launch_grid(int n_items) { return grouped_gemm_grid(n_items); }
 
 cudaError_t launch_grouped_gemm_phases(const GemmSpec& g0, const GemmSpec* g1, int* done, unsigned* finish_ctr,
-                                       int* status, const ScatterParams* sp, cudaStream_t s) {
+                                       int* status, const ScatterParams* sp, cudaStream_t s, int rows_hint) {
   CUtensorMap w0, a0, w1, a1;
   GGArgs args{};
   args.ph[0] = make_phase(g0, &w0, &a0);
@@ -864,9 +955,16 @@ cudaError_t launch_grouped_gemm_phases(const GemmSpec& g0, const GemmSpec* g1, i
   args.dep_timeout_ns = 2000000000ll;  // 2 s: phase-0 tiles of an expert are minutes' worth of margin away
   ScatterParams none{};
   const ScatterParams& spv = sp ? *sp : none;
-  int n_items = args.ph[0].n_tiles * args.ph[0].n_experts;
-  if (g1 != nullptr) n_items += args.ph[1].n_tiles * args.ph[1].n_experts;
-  return launch_kernel(w0, a0, w1, a1, args, spv, n_items, s);
+  int n_items = args.ph[0].n_tiles * args.ph[0].k_splits * args.ph[0].n_experts;
+  if (g1 != nullptr) n_items += args.ph[1].n_tiles * args.ph[1].k_splits * args.ph[1].n_experts;
+  switch (pipe_rows(rows_hint)) {
+    case 64:
+      return launch_kernel<8, 1>(w0, a0, w1, a1, args, spv, n_items, s);
+    case 128:
+      return launch_kernel<6, 2>(w0, a0, w1, a1, args, spv, n_items, s);
+    default:
+      return launch_kernel<4, 4>(w0, a0, w1, a1, args, spv, n_items, s);
+  }
 }
 
 void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* expert_offsets,

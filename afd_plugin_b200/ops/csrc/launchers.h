@@ -24,6 +24,9 @@ void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float 
 void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, const int64_t* slots, int tokens,
                             int row_elems, int64_t k_stride, int64_t v_stride, int dtype, cudaStream_t s);
 
+// out[r] = argmax over row r of x [rows, n] (row stride ld elements; lowest index on ties).
+void launch_argmax_rows(const void* x, int64_t ld, int rows, int n, int dtype, int32_t* out, cudaStream_t s);
+
 void launch_decode_advance(int32_t* input_ids, int64_t* positions, int64_t* slots, int32_t* seq_lens,
                            const int32_t* next_tokens, const int32_t* table, int batch, int table_stride,
                            int block_size, int64_t wrap_at, int64_t wrap_to, cudaStream_t s);
@@ -208,14 +211,29 @@ void launch_grouped_gemm(void* d, const void* a, const void* w, const int32_t* e
                          int* status, cudaStream_t s, int w_experts = -1, const ScatterParams* sp = nullptr);
 
 // One grouped GEMM of a launch (bf16 weights).
+//   epilogue 0: d[r, n] (row-major [rows_cap, N]); 1: SwiGLU over paired halves
+//   (d [rows_cap, N / 2]); 2: routing-weighted scatter (ScatterParams);
+//   3: expert-blocked columns, d[r - offsets[e], e * N + n] (d [rows, e_local * N]),
+//   e.g. a per-head batched product written token-major for the next GEMM.
 struct GemmSpec {
-  void* d;                 // output [rows_cap, N] (N / 2 for epilogue 1), unused for epilogue 2
-  const void* a;           // activations [rows_cap, K]
+  void* d;                 // output (see above); unused for epilogue 2
+  const void* a;           // activations: rows of K elements, a_ld apart
   const void* w;           // weights [w_experts, N, K]
   const int32_t* offsets;  // [e_local] first row of each expert's segment
   const int32_t* counts;   // [e_local] rows of each expert
   int e_local, rows_cap, n, k, epilogue;
   int w_experts;           // -1: e_local; 1: one weight set for every segment
+  int fixed_count = 0;     // with counts == nullptr: every segment has this many rows, starting at row 0
+  int k_splits = 1;        // > 1 (epilogue 0 / 3): K is split over that many items per tile; each adds its fp32
+                           // partial into acc_ws and the last one to finish a tile writes d and re-zeroes acc_ws
+  float* acc_ws = nullptr; // [rows_cap, output columns] fp32, zero between launches
+  int* tile_ctr = nullptr; // [e_local * n_tiles] int32, zero between launches
+  int out_f32 = 0;         // epilogue 0: d is float (fp32 results)
+  int n_valid = 0;         // epilogue 0: store only columns < n_valid (0: all N); the output's row stride is
+                           // then n_valid (weights padded to a multiple of 128 rows)
+  int64_t a_ld = 0;        // elements between activation rows (0: K)
+  int64_t a_plane = 0;     // > 0: expert e's rows start a_plane * e elements in (a 3-D view); offsets are then
+                           // rows within the expert's plane
 };
 // Kernel-side description of a phase (filled by the launcher).
 struct GGPhase {
@@ -224,6 +242,14 @@ struct GGPhase {
   const int32_t* counts;
   int* done;  // phase 0 of a two-phase launch: finished tiles per expert (zero between launches)
   int n_w, w_stride_rows, k_dim, ld_d, n_tiles, n_experts, epi;
+  int a3d;    // activation tiles from a 3-D tensor map (k, row, expert)
+  int fixed_count;  // counts == nullptr: rows per segment (segments start at row 0)
+  int out_f32;      // epilogue 0: fp32 output
+  int n_valid;      // epilogue 0: columns stored
+  int k_splits;     // items per tile along K
+  int kb_per;       // K blocks per split
+  float* acc_ws;    // split-K fp32 partial sums [rows, ld_d]
+  int* tile_ctr;    // split-K arrivals per (expert, tile)
 };
 struct GGArgs {
   GGPhase ph[2];
@@ -236,10 +262,11 @@ struct GGArgs {
 // output (its `a` is g0's `d`, same row segments): an MoE layer's gate_up
 // (epilogue 1) and down projection (epilogue 0 or 2) in one persistent
 // kernel.  done: int32 [g0.e_local] and finish_ctr: one uint32, both zero
-// before the first launch and left zero by every launch.  Returns the launch
-// error, if any.
+// before the first launch and left zero by every launch.  rows_hint: the
+// largest row count expected in one segment; it picks the tokens per pass
+// (and so the pipeline depth), never the result.  Returns the launch error.
 cudaError_t launch_grouped_gemm_phases(const GemmSpec& g0, const GemmSpec* g1, int* done, unsigned* finish_ctr,
-                                       int* status, const ScatterParams* sp, cudaStream_t s);
+                                       int* status, const ScatterParams* sp, cudaStream_t s, int rows_hint = 512);
 
 // ---- gdn.cu (Gated DeltaNet)
 struct GdnConvParams {

@@ -35,6 +35,31 @@ def moe_sync_buffer(device: torch.device, experts: int) -> torch.Tensor:
     return buf
 
 
+_WS: dict[torch.device, tuple[torch.Tensor, torch.Tensor]] = {}
+_WS_FLOATS = 4 << 20  # 16 MiB of fp32 partial sums
+
+
+def gemm_workspace(device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split-K workspace of the dense tcgen05 GEMM on ``device``: fp32 partial sums and
+    per-tile arrival counters, both zero between launches (every launch leaves them zero).
+    Allocated once per device on first use (an eager step, before any graph capture)."""
+    device = torch.device(device)
+    ws = _WS.get(device)
+    if ws is None:
+        ws = (torch.zeros(_WS_FLOATS, dtype=torch.float32, device=device),
+              torch.zeros(4096, dtype=torch.int32, device=device))
+        _WS[device] = ws
+    return ws
+
+
+def moe_rows_hint(tokens: int, top_k: int, experts: int, n_shared: int = 0, shared_rows: int | None = None) -> int:
+    """Largest expert segment a decode step expects: twice the mean routed load, or a shared chunk's rows."""
+    routed = 2 * (tokens * top_k + experts - 1) // max(1, experts)
+    shared = (tokens if shared_rows is None else shared_rows) if n_shared else 0
+    # a few whole-batch segments among many small ones: 128-token passes keep the pipeline deep
+    return max(1, routed, min(shared, 128))
+
+
 def moe_experts_cuda(
     x: torch.Tensor,
     w13: torch.Tensor,
@@ -60,8 +85,9 @@ def moe_experts_cuda(
         h = C.grouped_gemm_w8(xs, w13, w13_scale, offsets, counts, 1, ne)
         y = C.grouped_gemm_w8(h, w2, w2_scale, offsets, counts, 0, ne)
     else:
-        y = C.moe_ffn(xs, w13, w2, offsets, counts, moe_sync_buffer(x.device, w13.shape[0]))
+        y = C.moe_ffn(xs, w13, w2, offsets, counts, moe_sync_buffer(x.device, w13.shape[0]),
+                      moe_rows_hint(x.shape[0], topk_ids.shape[1], e_local, n_shared))
     return C.moe_combine(y, topk_weights.float().contiguous(), tsr, shared_out)
 
 
-__all__ = ["moe_experts_cuda", "moe_sync_buffer"]
+__all__ = ["gemm_workspace", "moe_experts_cuda", "moe_rows_hint", "moe_sync_buffer"]

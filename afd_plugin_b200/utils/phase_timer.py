@@ -37,6 +37,11 @@ class PhaseTimer:
         self.buf = torch.zeros(max_marks, dtype=torch.int64, device=device) if self.enabled else None
         self.names: list[str] = []
         self._pos = 0
+        self._ops = None
+        if self.enabled:
+            from afd_plugin_b200.ops._ext import ops
+
+            self._ops = ops()  # loads the extension (the stamp kernel lives there)
 
     def begin_step(self) -> None:
         """Starts the step's mark sequence (the first mark is the step's start)."""
@@ -54,7 +59,7 @@ class PhaseTimer:
             self.names[self._pos] = name
         else:
             self.names.append(name)
-        torch.ops.afd_b200.afd_stamp(self.buf, self._pos)
+        self._ops.afd_stamp(self.buf, self._pos)
         self._pos += 1
 
     def summary(self) -> dict:

@@ -314,7 +314,7 @@ def test_moe_ffn_two_phase(counts_list, H, I):
     sync = moe_sync_buffer(torch.device(DEV), E)
     for rep in range(2):
         a = (torch.randn(R + 2, H, device=DEV) * 0.5).to(torch.bfloat16)
-        y = C.moe_ffn(a, w13, w2, offsets, counts, sync)
+        y = C.moe_ffn(a, w13, w2, offsets, counts, sync, max(counts_list))
         torch.cuda.synchronize()
         assert int(sync.abs().sum()) == 0, "moe_ffn must leave its counters at zero"
         for e in range(E):
@@ -324,3 +324,94 @@ def test_moe_ffn_two_phase(counts_list, H, I):
             want = _swiglu_ref(a[o : o + c], w13[e], w2[e])
             sc = want.abs().max().item() + 1e-6
             _close(y[o : o + c] / sc, want / sc, 3e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("n", [102400, 1000, 37])
+def test_argmax_rows(dtype, n):
+    torch.manual_seed(n)
+    x = torch.randn(67, n, device=DEV).to(dtype)
+    x[3, :] = 0  # ties: the lowest index wins, as torch.argmax
+    x[5, n // 2] = x[5].max() + 1
+    x[5, n - 1] = x[5, n // 2]
+    got = _ext.ops().argmax_rows(x)
+    torch.cuda.synchronize()
+    assert torch.equal(got.cpu().long(), torch.argmax(x.float(), dim=-1).cpu())
+
+
+@pytest.mark.parametrize("T,N,K", [(256, 3712, 2048), (43, 2048, 2048), (1, 128, 64), (300, 102400 // 8, 2048)])
+def test_tc_gemm_dense(T, N, K):
+    torch.manual_seed(T + N)
+    x = (torch.randn(T, K, device=DEV) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) * 0.03).to(torch.bfloat16)
+    y = _ext.ops().tc_gemm(x, w, 0)
+    want = x.float() @ w.float().t()
+    sc = want.abs().max().item()
+    _close(y / sc, want / sc, 2e-2)
+
+
+def test_tc_gemm_strided_rows_and_swiglu():
+    torch.manual_seed(3)
+    big = (torch.randn(77, 3712, device=DEV) * 0.5).to(torch.bfloat16)
+    x = big[:, :2048]  # rows 3712 elements apart
+    w = (torch.randn(512, 2048, device=DEV) * 0.03).to(torch.bfloat16)
+    y = _ext.ops().tc_gemm(x, w, 1)
+    want = _swiglu_ref(x, w)
+    sc = want.abs().max().item()
+    _close(y / sc, want / sc, 2e-2)
+
+
+def test_tc_gemm_per_head_batched():
+    """MLA absorption shapes: q_nope heads read in place from the projection output, written token-major."""
+    torch.manual_seed(4)
+    T, nh = 37, 16
+    y = (torch.randn(T, 3712, device=DEV) * 0.5).to(torch.bfloat16)
+    q_nope = y[:, : nh * 192].view(T, nh, 192)[..., :128].transpose(0, 1)  # [16, T, 128], strided
+    w_uk_t = (torch.randn(nh, 512, 128, device=DEV) * 0.05).to(torch.bfloat16)
+    out = _ext.ops().tc_gemm(q_nope, w_uk_t)  # [T, 16 * 512]
+    want = torch.einsum("htk,hnk->thn", q_nope.float(), w_uk_t.float()).reshape(T, nh * 512)
+    sc = want.abs().max().item()
+    _close(out / sc, want / sc, 2e-2)
+    o_lat = (torch.randn(nh, T, 512, device=DEV) * 0.5).to(torch.bfloat16)  # head-major, contiguous
+    w_uv = (torch.randn(nh, 128, 512, device=DEV) * 0.05).to(torch.bfloat16)
+    o = _ext.ops().tc_gemm(o_lat, w_uv)  # [T, 16 * 128]
+    want = torch.einsum("htk,hnk->thn", o_lat.float(), w_uv.float()).reshape(T, nh * 128)
+    sc = want.abs().max().item()
+    _close(o / sc, want / sc, 2e-2)
+
+
+@pytest.mark.parametrize("T,N,K,n_valid,f32", [(256, 3712, 2048, 0, False), (43, 2048, 2048, 0, False),
+                                              (256, 128, 2048, 64, True), (7, 128, 512, 100, False)])
+def test_tc_gemm_split_k(T, N, K, n_valid, f32):
+    """Few output tiles: K split over the SMs with fp32 partial sums; the workspace is left zero."""
+    from afd_plugin_b200.ops.moe import gemm_workspace
+
+    torch.manual_seed(T * 3 + N)
+    ws, ctr = gemm_workspace(torch.device(DEV))
+    x = (torch.randn(T, K, device=DEV) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) * 0.03).to(torch.bfloat16)
+    for _ in range(2):
+        y = _ext.ops().tc_gemm(x, w, 0, n_valid, f32, ws, ctr)
+        torch.cuda.synchronize()
+        assert int(ctr.abs().sum()) == 0 and float(ws.abs().sum()) == 0.0
+    want = x.float() @ w.float().t()
+    if n_valid:
+        want = want[:, :n_valid]
+    assert y.dtype == (torch.float32 if f32 else torch.bfloat16) and tuple(y.shape) == tuple(want.shape)
+    sc = want.abs().max().item()
+    _close(y / sc, want / sc, 2e-2)
+
+
+def test_tc_gemm_split_k_per_head():
+    from afd_plugin_b200.ops.moe import gemm_workspace
+
+    torch.manual_seed(9)
+    ws, ctr = gemm_workspace(torch.device(DEV))
+    o_lat = (torch.randn(16, 64, 512, device=DEV) * 0.5).to(torch.bfloat16)
+    w_uv = (torch.randn(16, 128, 512, device=DEV) * 0.05).to(torch.bfloat16)
+    o = _ext.ops().tc_gemm(o_lat, w_uv, 0, 0, False, ws, ctr)
+    want = torch.einsum("htk,hnk->thn", o_lat.float(), w_uv.float()).reshape(64, 16 * 128)
+    sc = want.abs().max().item()
+    _close(o / sc, want / sc, 2e-2)
+    torch.cuda.synchronize()
+    assert int(ctr.abs().sum()) == 0 and float(ws.abs().sum()) == 0.0
