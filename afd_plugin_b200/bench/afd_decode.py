@@ -24,8 +24,6 @@ def run_afd_rank(args, *, rank, local, num_attn, num_ffn, connector, build_confi
     dist.init_process_group("nccl", timeout=timedelta(seconds=180))
     log("process group up")
     role, role_rank = role_of_world_rank(rank, attention_size=num_attn, ffn_size=num_ffn)
-    if connector == "P2pNcclAFDConnector":
-        args.eager = True  # NCCL p2p through torch.distributed is not captured into graphs here
     ec, per_rank = build_config(args, num_attn=num_attn, num_ffn=num_ffn, role=role, connector=connector)
     # Even split of the global batch over the Attention ranks.
     shares = [args.batch // num_attn + (1 if i < args.batch % num_attn else 0) for i in range(num_attn)]

@@ -14,10 +14,16 @@ transport of the CPU/gloo multi-rank tests.  Behaviour follows
 * a control plane carries per-stage DP token counts (JSON codec) from the
   first ``min(A, F)`` Attention ranks to the FFN ranks.
 
-Transport: ``torch.distributed`` point-to-point on the default (AFD world)
-group -- NCCL on GPUs, gloo on CPU.  The control payload travels over a gloo
-group on host tensors, so the FFN side never synchronises the device to read
-it (the reference stages it on the GPU and pays a ``.item()`` sync).
+Transport: on GPUs one NCCL communicator per subgroup (created from a unique
+id the FFN rank shares over a gloo group, as the reference builds a
+``PyNcclCommunicator`` per subgroup, ``p2p.py:269-286``), with ``ncclSend`` /
+``ncclRecv`` issued on the caller's current stream -- so a decode step
+through this connector captures into a CUDA graph on both roles, like the
+reference's graph-capturable custom ops (``p2p.py:905-992``).  On CPU,
+``torch.distributed`` point-to-point over gloo.  The control payload travels
+over a gloo group on host tensors, so the FFN side never synchronises the
+device to read it (the reference stages it on the GPU and pays a
+``.item()`` sync).
 """
 
 from __future__ import annotations
@@ -102,7 +108,13 @@ class P2pNcclAFDConnector(AFDConnectorBase):
         self.control_group = None
         # In-flight sends: (work, tensor kept alive until the work completes).
         self._pending: list[tuple[object, torch.Tensor]] = []
+        self._comm = 0  # NCCL communicator of this rank's subgroup (GPU transport)
         self.control_plane = P2pNcclAFDControlPlane(self)
+
+    @property
+    def supports_graph_capture(self) -> bool:
+        """Stream-ordered NCCL sends / receives capture into decode graphs."""
+        return bool(self._comm)
 
     def _use_cuda(self) -> bool:
         return dist.is_initialized() and dist.get_backend() == "nccl"
@@ -123,10 +135,40 @@ class P2pNcclAFDConnector(AFDConnectorBase):
         control_ranks = list(range(self.ffn_size + self.min_size))
         group = dist.new_group(ranks=control_ranks, backend="gloo")
         self.control_group = group if self.mapping.participates_in_dp_metadata_group else None
+        # Two ubatches keep torch.distributed's asynchronous sends: with stream-ordered
+        # sends, a rank's second send would queue ahead of its first receive.
+        ubatching = bool(getattr(getattr(self.engine_config, "parallel_config", None), "use_ubatching", False))
+        if self.device.type == "cuda" and self.group_size > 1 and not ubatching:
+            self._comm = self._init_subgroup_comm()
         self._initialized = True
+
+    def _init_subgroup_comm(self) -> int:
+        """One NCCL communicator per FFN subgroup; every world rank takes part in
+        creating every subgroup's gloo group (a collective), then joins its own."""
+        from afd_plugin_b200.ops._ext import ops
+
+        C = ops()
+        F, A, r = self.ffn_size, self.attn_size, self.ratio
+        mine = None
+        for k in range(F):
+            members = [k] + [F + k * r + j for j in range(r)]
+            g = dist.new_group(ranks=members, backend="gloo")
+            if k == self.mapping.subgroup_index:
+                mine = (g, members)
+        g, members = mine
+        box = [C.nccl_unique_id() if self.mapping.rank_in_subgroup == 0 else None]
+        dist.broadcast_object_list(box, src=members[0], group=g)
+        torch.cuda.set_device(self.device)
+        return int(C.nccl_comm_init(box[0], len(members), self.mapping.rank_in_subgroup))
 
     def close(self) -> None:
         self.flush()
+        if self._comm:
+            torch.cuda.synchronize(self.device)
+            from afd_plugin_b200.ops._ext import ops
+
+            ops().nccl_comm_destroy(self._comm)
+            self._comm = 0
         self.control_group = None
         self._recv_buffers.clear()
         self._ids_buffers.clear()
@@ -149,9 +191,14 @@ class P2pNcclAFDConnector(AFDConnectorBase):
             raise ValueError(f"invalid P2P destination rank {subgroup_dst}")
         if self.device.type == "cuda" and not t.is_cuda:
             raise ValueError("P2P hidden states must be on GPU")
+        t = t.contiguous()
+        if self._comm:
+            # stream-ordered: the buffer stays valid until the send completes (the
+            # caching allocator reuses it only behind this stream's later work)
+            torch.ops.afd_b200.nccl_send(t, subgroup_dst, self._comm)
+            return
         # Sends are posted without blocking so that, under DBO, a rank can post
         # its next ubatch's send before it receives the previous one's result.
-        t = t.contiguous()
         self._pending.append((dist.isend(t, dst=self._peer(subgroup_dst)), t))
 
     def flush(self) -> None:
@@ -175,7 +222,10 @@ class P2pNcclAFDConnector(AFDConnectorBase):
             out = ref_tensor
         else:
             out = torch.empty(size, dtype=spec.dtype, device=spec.device)
-        dist.recv(out, src=self._peer(subgroup_src))
+        if self._comm:
+            torch.ops.afd_b200.nccl_recv(out, subgroup_src, self._comm)
+        else:
+            dist.recv(out, src=self._peer(subgroup_src))
         return out
 
     # ---------------------------------------------------- attention side

@@ -389,7 +389,7 @@ int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
   // Splitting costs a partial-O round trip through HBM (and a combine launch),
   // so split only when the batch alone leaves SMs idle.
   if (batch * 2 >= 3 * num_sms) return 1;
-  const int target = 2 * num_sms * 2;  // two resident CTAs per SM, ~two waves
+  const int target = 2 * num_sms;  // one wave of two resident CTAs per SM
   int s = (target + batch - 1) / batch;
   s = s < 1 ? 1 : s;
   const int max_s = tiles / 2 > 0 ? tiles / 2 : 1;  // keep >= 2 tiles per split

@@ -86,12 +86,15 @@ class ConnectorFFNExecutor(FFNExecutor):
     metadata carries in the reference.
     """
 
+    @property
+    def supports_graph_capture(self) -> bool:
+        """Decode graphs need stream-ordered transfers (the NCCL connector's subgroup
+        communicator on GPUs); asked of the connector once it is initialised."""
+        return bool(getattr(self.connector, "supports_graph_capture", False))
+
     def __init__(self, model, connector, *, attn_dp_group=None, attn_size: int = 1, attn_rank: int = 0):
         self.model = model
         self.connector = connector
-        # Point-to-point sends through torch.distributed are not captured into
-        # graphs here; the FFN side of this connector runs eagerly as well.
-        self.supports_graph_capture = bool(getattr(connector, "supports_graph_capture", False))
         self.group = attn_dp_group
         self.attn_size = attn_size
         self.attn_rank = attn_rank

@@ -284,8 +284,7 @@ def main(argv=None) -> int:
                 "input_len": args.isl,
                 "output_len": args.osl,
                 "parallelism": result["parallelism"],
-                # the NCCL connector's point-to-point path is not captured: it always runs eager
-                "cuda_graphs": not args.eager and (args.gpus == 1 or connector == "B200FusedAFDConnector"),
+                "cuda_graphs": not args.eager,
                 "dbo": args.dbo,
                 "l2": "inputs larger than L2 (31 GB weights, ~10 GB KV per step); no flush",
             },

@@ -12,6 +12,20 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("afd_plugin_b200", "ops", "csrc")
+
+
+def _nccl_dirs():
+    """NCCL headers / library matching the one PyTorch loads (the nvidia-nccl wheel)."""
+    import importlib.util
+
+    spec = importlib.util.find_spec("nvidia.nccl")
+    if spec is not None and spec.submodule_search_locations:
+        base = list(spec.submodule_search_locations)[0]
+        return [os.path.join(base, "include")], [os.path.join(base, "lib")]
+    return [], []
+
+
+NCCL_INC, NCCL_LIB = _nccl_dirs()
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 DEBUG = os.environ.get("AFD_B200_KERNEL_DEBUG", "") in ("1", "true", "on")
 
@@ -31,7 +45,10 @@ setup(
         CUDAExtension(
             name="afd_plugin_b200._C",
             sources=sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp"))),
-            include_dirs=[os.path.join(ROOT, CSRC)],
+            include_dirs=[os.path.join(ROOT, CSRC)] + NCCL_INC,
+            library_dirs=NCCL_LIB,
+            # libnccl.so.2 is the library PyTorch itself loads (resolved by soname at load time)
+            extra_link_args=[f"-Wl,-rpath,{d}" for d in NCCL_LIB] + (["-l:libnccl.so.2"] if NCCL_LIB else ["-lnccl"]),
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc_flags},
         )
     ],

@@ -60,6 +60,15 @@ def test_nccl_connector_1a1f_exact():
     assert outs == ref
 
 
+def test_nccl_connector_1a1f_graphs_exact():
+    """Stream-ordered NCCL sends / receives captured into both roles' decode graphs."""
+    _need(2)
+    prompts = _prompts(4, 16)
+    ref = _colocated(prompts, 6)
+    outs = _run({"num_attention_ranks": 1, "num_ffn_ranks": 1}, prompts, 6, enforce_eager=False, capture_sizes=[4])
+    assert outs == ref
+
+
 @pytest.mark.parametrize("eager,dbo", [(True, False), (False, False), (False, True)])
 def test_fused_connector_1a1f(eager, dbo):
     _need(2)
