@@ -213,17 +213,8 @@ AFD_DEVICE void publish_dispatch(const DispatchParams& p) {
 // routing, which follows, tells each rank which rows it answers), the home
 // rank only for a dense layer.  A dense layer has no router step, so this
 // kernel also publishes the arrival.
-// kRoute: the MoE router runs in the same kernel (small gates, E x H <=
-// kFusedRouteElems): the CTA keeps its normalised row in shared memory,
-// each warp takes every 8th expert's dot product, one warp runs the top-k,
-// and the grid's last CTA publishes the arrival -- one launch and one
-// completion fence per layer instead of two kernels.
-constexpr int kFusedRouteElems = 128 * 2048;
-template <bool kRoute>
 __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams p) {
   __shared__ float s_red[kWarps];
-  __shared__ __align__(16) bf16 s_h[kRoute ? kThreads * kNormMaxVec * 8 : 8];
-  __shared__ float s_logit[kRoute ? kMaxRouteE : 1];
   pdl_wait();
   pdl_launch_dependents();
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -279,12 +270,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
       for (int j = 0; j < 8; ++j)
         y.v[j] = __float2bfloat16_rn(__bfloat162float(x[u].v[j]) * inv * __bfloat162float(w.v[j]));
     }
-    if (valid && p.moe) {
-      if constexpr (kRoute)
-        store16(s_h + v * 8, y);
-      else
-        store16(h + v * 8, y);
-    }
+    if (valid && p.moe) store16(h + v * 8, y);
     if (p.scale_ptrs != nullptr) {
       // e4m3 with one scale per 128 columns: the 16 vectors of a group sit in one half-warp
       float amax = 0.f;
@@ -312,44 +298,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_norm_kernel(DispatchParams 
     if (threadIdx.x == 0) p.fmask[t] = p.has_shared ? (int32_t)(1u << p.home_f) : 0;
     finish_grid(p.done_ctr, gridDim.x, [&] { publish_dispatch(p); });
   }
-  if constexpr (kRoute) {
-    if (!p.moe) return;
-    __syncthreads();
-    // logits: warp w takes experts w, w + 8, ...; lanes split the hidden dim
-    const bf16* gate = static_cast<const bf16*>(p.gate_w);
-    for (int e = warp; e < p.E; e += kWarps) {
-      const bf16* g = gate + (size_t)e * p.H;
-      float acc = 0.f;
-      for (int c = lane * 8; c < p.H; c += 32 * 8) {
-        const Vec16<bf16> gv = load16(g + c), hv = load16(s_h + c);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc += __bfloat162float(gv.v[j]) * __bfloat162float(hv.v[j]);
-      }
-      acc = warp_sum(acc);
-      if (lane == 0) s_logit[e] = acc;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      float w;
-      int id;
-      const int32_t* forced = p.hash_table ? p.hash_table + (size_t)p.input_ids[t] * p.k : nullptr;
-      warp_route(s_logit, p.gate_bias, p.E, p.k, p.scoring, p.renorm, p.n_group, p.topk_group, p.scale, w, id,
-                 forced);
-      const unsigned bit = lane < p.k ? (1u << (id / p.e_local)) : 0u;
-      const unsigned mask = __reduce_or_sync(0xffffffffu, bit) | (p.has_shared ? (1u << p.home_f) : 0u);
-      const size_t off = ((size_t)p.attn_rank * p.t_cap + t) * p.k;
-      if (lane < p.k) {
-        for (int f = 0; f < p.num_ffn; ++f) {
-          reinterpret_cast<int32_t*>(p.rid_ptrs[f])[off + lane] = id;
-          reinterpret_cast<float*>(p.rwt_ptrs[f])[off + lane] = w;
-        }
-      }
-      if (lane == 0) p.fmask[t] = (int32_t)mask;
-    }
-    finish_grid(p.done_ctr, gridDim.x, [&] { publish_dispatch(p); });
-  }
-  // Unfused MoE layers: the router kernel publishes; this kernel's stores are
-  // complete when it finishes, which precedes the router's release.
+  // MoE layers: the router kernel publishes; this kernel's stores are complete
+  // when it finishes, which precedes the router's release.
 }
 
 // ---- dispatch, step 2 (MoE layers): router logits on the tensor cores, top-k,
@@ -688,11 +638,7 @@ void launch_afd_wait(const uint64_t* flag, const uint64_t* epoch, uint64_t arriv
 void launch_afd_dispatch(const DispatchParams& p, cudaStream_t s) {
   using namespace fused;
   if (p.T <= 0) return;
-  if (p.moe && (int64_t)p.E * p.H <= kFusedRouteElems && p.E <= kMaxRouteE) {
-    launch_pdl(dispatch_norm_kernel<true>, dim3(p.T), dim3(kThreads), 0, s, p);
-    return;
-  }
-  launch_pdl(dispatch_norm_kernel<false>, dim3(p.T), dim3(kThreads), 0, s, p);
+  launch_pdl(dispatch_norm_kernel, dim3(p.T), dim3(kThreads), 0, s, p);
   if (!p.moe) return;
   const int mt = (p.T + kRouteTile - 1) / kRouteTile;
   const int target = device_sm_count() * 2;

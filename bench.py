@@ -6,8 +6,9 @@ Workload (BASELINE config #2): DeepSeek-V2-Lite architecture, bf16, random
 init; 256 concurrent requests, 1024-token prompts, 256 output tokens.
 Prompt KV is synthetic (filled at random, as the reference's decode-bench KV
 connector does), so only decode steps run.  N=1 is colocated; N>1 runs AFD
-with the FFN-first topology 1A1F (N=2), 3A1F (N=4), 6A2F (N=8).  The 256
-requests are split over the Attention ranks (fixed total work: strong scaling).
+with the FFN-first topology 1A1F (N=2), 2A2F (N=4), 4A4F (N=8)
+(``--topology A,F`` overrides, e.g. 6,2).  The 256 requests are split over
+the Attention ranks (fixed total work: strong scaling).
 
 value   output tokens/s of the whole job, CUDA-event timed over exactly K
         decode steps (device-resident loop: graph replay + on-device input
@@ -42,7 +43,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode output tok/s (8xB200, max over ranks) + p50 TPOT, AFD vs NCCL connector"
 BASELINE_VALUE = None  # the reference publishes no GPU number for this metric
-TOPOLOGY = {1: (0, 0), 2: (1, 1), 4: (2, 2), 8: (6, 2)}  # 4 GPUs: 2A2F halves each FFN rank's expert weights
+# (Attention ranks, FFN ranks) per GPU count.  With the batch fixed, a decode
+# step is a per-layer chain of the Attention ranks' attention and the FFN
+# ranks' expert GEMMs, and the FFN side is bound by streaming its experts'
+# weights: F = A halves that stream at 4 and 8 GPUs (2A2F, 4A4F), where 3A1F /
+# 6A2F would leave one or two FFN ranks reading 64 / 32 experts per layer.
+TOPOLOGY = {1: (0, 0), 2: (1, 1), 4: (2, 2), 8: (4, 4)}
 MODEL_DESC = {
     "deepseek-v2-lite": "DeepSeek-V2-Lite (27 layers, 64 experts top-6, MLA 16 heads)",
     "qwen3-30b-a3b": "Qwen3-30B-A3B (48 layers, 128 experts top-8, GQA 32q/4kv)",
