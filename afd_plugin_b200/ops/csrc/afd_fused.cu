@@ -155,6 +155,47 @@ AFD_DEVICE void warp_sum_rows(bf16* out, const bf16* src, size_t stride, unsigne
   }
 }
 
+// Column chunk `cc` (256 columns: one 16-byte vector per lane) of the sum of
+// the rows selected by `mask`; the rows' loads go out four at a time, so a
+// token's slots cost one or two memory round trips instead of one per slot.
+constexpr int kChunkCols = 256;
+template <bool kBypassL1>
+AFD_DEVICE void warp_sum_chunk(bf16* out, const bf16* src, size_t stride, unsigned mask, int H, int cc, int lane) {
+  const int col = cc * kChunkCols + lane * 8;
+  if (col >= H) return;
+  float acc[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+  while (mask) {
+    int r[4];
+    int n = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      r[u] = mask ? __ffs(mask) - 1 : -1;
+      if (mask) {
+        mask &= mask - 1;
+        ++n;
+      }
+    }
+    Vec16<bf16> x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (u < n) {
+        const bf16* row = src + (size_t)r[u] * stride + col;
+        x[u] = kBypassL1 ? load16_cg(row) : load16(row);
+      }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (u < n)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(x[u].v[q]);
+  }
+  Vec16<bf16> o;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) o.v[q] = __float2bfloat16_rn(acc[q]);
+  store16(out + col, o);
+}
+
 // e4m3 <-> bf16 helpers for rows that travel as fp8 with one scale per 128 columns.
 AFD_DEVICE uint2 pack_e4m3x8(const Vec16<bf16>& y, float inv) {
   uint32_t w[2];
@@ -544,7 +585,11 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
   if (threadIdx.x == 0) source_prefix(p.tcount, p.A, s_pre);
   __syncthreads();
   const int total = s_pre[p.A];
-  for (int q = blockIdx.x * kWarps + warp; q < total; q += gridDim.x * kWarps) {
+  // Expert-output sums go one (token, 256-column chunk) per warp; the
+  // transport-only echo mode keeps one warp per token.
+  const int nch = p.echo ? 1 : (p.H + kChunkCols - 1) / kChunkCols;
+  for (int item = blockIdx.x * kWarps + warp; item < total * nch; item += gridDim.x * kWarps) {
+    const int q = item / nch, cc = item - q * nch;
     const int a = source_of(s_pre, p.A, q);
     const int t = q - s_pre[a];
     const int pair = a * p.t_cap + t;
@@ -581,8 +626,8 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(CombineSendParam
       const float wsum = warp_sum(w);
       warp_sum_rows<true>(dst, static_cast<const bf16*>(p.staging) + (size_t)pair * p.H, 0, 1u, p.H, lane, wsum);
     } else {
-      warp_sum_rows<false>(dst, static_cast<const bf16*>(p.staging) + (size_t)pair * p.J * p.H, (size_t)p.H, used,
-                           p.H, lane);
+      warp_sum_chunk<false>(dst, static_cast<const bf16*>(p.staging) + (size_t)pair * p.J * p.H, (size_t)p.H, used,
+                            p.H, cc, lane);
     }
   }
   finish_grid(p.done_ctr, gridDim.x, [&] {
@@ -602,10 +647,12 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineParams p) {
     if (threadIdx.x == 0) atomicExch(p.status, kStatusWaitTimeout);
     return;
   }
-  for (int t = blockIdx.x * kWarps + warp; t < p.T; t += gridDim.x * kWarps) {
+  const int nch = (p.H + kChunkCols - 1) / kChunkCols;
+  for (int item = blockIdx.x * kWarps + warp; item < p.T * nch; item += gridDim.x * kWarps) {
+    const int t = item / nch, cc = item - t * nch;
     const unsigned mask = (unsigned)p.fmask[t];
-    warp_sum_rows<true>(static_cast<bf16*>(p.out) + (size_t)t * p.H,
-                        static_cast<const bf16*>(p.comb) + (size_t)t * p.F * p.H, (size_t)p.H, mask, p.H, lane);
+    warp_sum_chunk<true>(static_cast<bf16*>(p.out) + (size_t)t * p.H,
+                         static_cast<const bf16*>(p.comb) + (size_t)t * p.F * p.H, (size_t)p.H, mask, p.H, cc, lane);
   }
 }
 
@@ -659,9 +706,13 @@ void launch_afd_expand(const ExpandParams& p, cudaStream_t s) {
 }
 
 void launch_afd_combine_send(const CombineSendParams& p, cudaStream_t s) {
-  launch_pdl(fused::combine_send_kernel, dim3(warp_grid(p.A * p.t_cap, device_sm_count())), dim3(fused::kThreads), 0, s, p);
+  const int nch = p.echo ? 1 : (p.H + fused::kChunkCols - 1) / fused::kChunkCols;
+  launch_pdl(fused::combine_send_kernel, dim3(warp_grid(p.A * p.t_cap * nch, 2 * device_sm_count())),
+             dim3(fused::kThreads), 0, s, p);
 }
 
 void launch_afd_combine(const CombineParams& p, cudaStream_t s) {
-  launch_pdl(fused::combine_kernel, dim3(warp_grid(p.T, device_sm_count())), dim3(fused::kThreads), 0, s, p);
+  const int nch = (p.H + fused::kChunkCols - 1) / fused::kChunkCols;
+  launch_pdl(fused::combine_kernel, dim3(warp_grid(p.T * nch, 2 * device_sm_count())), dim3(fused::kThreads), 0, s,
+             p);
 }
