@@ -7,6 +7,11 @@ repository root, when present).  The cache is larger than L2 (126 MB), so
 consecutive launches read it from HBM.
 
     python -m afd_plugin_b200.bench.mla_decode_bench [--shapes dsv2-lite-b256,...] [--reps 3]
+    python -m afd_plugin_b200.bench.mla_decode_bench --sparse
+
+``--sparse`` compares DeepSeek-sparse-attention decode (the indexer's kept
+positions) on the sm_100a gather kernel against the gather + two batched
+GEMMs of ``ops/reference.py::mla_decode_sparse``.
 """
 
 from __future__ import annotations
@@ -59,11 +64,61 @@ def run(shape: str, reps: int, bs: int = 64) -> dict:
             "status": int(C.read_status(torch.cuda.current_device()))}
 
 
+# name: (batch, heads, context tokens, kept positions)
+SPARSE = {
+    "dsv32-b64-8k": (64, 128, 8192, 2048),   # DeepSeek-V3.2 heads and index_topk, one Attention rank
+    "dsv32-b16-32k": (16, 128, 32768, 2048),
+    "dsv32-b256-4k-h16": (256, 16, 4096, 2048),
+}
+
+
+def _median_us(fn, reps: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    ev[0].record()
+    for i in range(reps):
+        fn()
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    us = sorted(ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(reps))
+    return us[len(us) // 2]
+
+
+def run_sparse(shape: str, reps: int, bs: int = 64) -> dict:
+    from afd_plugin_b200.ops import _ext
+    from afd_plugin_b200.ops import reference as ref
+
+    C = _ext.ops()
+    B, H, ctx, K = SPARSE[shape]
+    dev = "cuda"
+    nblk = math.ceil(ctx / bs)
+    cache = torch.randn(B * nblk + 1, bs, 576, device=dev, dtype=torch.bfloat16)
+    table = (torch.randperm(B * nblk, device=dev).view(B, nblk) + 1).to(torch.int32)
+    seq = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    keep = torch.stack([torch.randperm(ctx, device=dev)[:K] for _ in range(B)]).to(torch.int32)
+    q = torch.randn(B, H, 576, device=dev, dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(192)
+    kern = lambda: C.mla_decode_sparse(q, cache, table, seq, keep, scale, 0)  # noqa: E731
+    gath = lambda: ref.mla_decode_sparse(q, cache, table, keep, scale, 512)  # noqa: E731
+    got, want = kern().float(), gath().float()
+    err = float((got - want).abs().max() / (want.abs().max() + 1e-6))
+    return {"shape": shape, "batch": B, "heads": H, "context": ctx, "kept": K,
+            "kernel_us": round(_median_us(kern, reps), 2), "gather_bmm_us": round(_median_us(gath, reps), 2),
+            "max_rel_diff": round(err, 4), "status": int(C.read_status(torch.cuda.current_device()))}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--shapes", default=",".join(SHAPES))
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--sparse", action="store_true", help="sparse (indexer-selected) decode: kernel vs gather + bmm")
     args = ap.parse_args(argv)
+    if args.sparse:
+        for shape in SPARSE:
+            print(json.dumps(run_sparse(shape, args.reps)), flush=True)
+        return
     for shape in args.shapes.split(","):
         print(json.dumps(run(shape, args.reps)), flush=True)
 

@@ -161,11 +161,13 @@ def mla_decode_sparse(
     """MLA decode over the positions a DeepSeek-sparse-attention indexer kept.
 
     ``keep_pos [B, K]`` lists each row's selected positions (-1 = unused).
-    With ``AFD_SPARSE_MLA_KERNEL=1`` on a GPU (DeepSeek's 512 + 64 latent,
-    heads a multiple of 16) the sm_100a sparse decode kernel gathers the
-    kept rows (``csrc/mla_decode.cu``, ``kSparse``); otherwise a gather plus
-    two small batched GEMMs.  The switch stays off by default until the
-    kernel's numerics test has passed on a B200.
+    On a GPU (DeepSeek's 512 + 64 latent, heads a multiple of 16) the sm_100a
+    sparse decode kernel gathers the kept rows (``csrc/mla_decode.cu``,
+    ``kSparse``) when the layer has at most 32 heads; with more heads its
+    16-head CTAs each gather the rows again and the gather plus two batched
+    GEMMs is faster (measured on B200: 16 heads 789 vs 1,983 us, 128 heads
+    1,248 vs 1,141 us; ``bench/mla_decode_bench.py --sparse``).
+    ``AFD_SPARSE_MLA_KERNEL=1`` / ``0`` forces one or the other.
     """
     if checks.enabled():
         checks.paged_attention("mla_decode_sparse", block_table, seq_lens, num_blocks=kv_cache.shape[0],
@@ -173,16 +175,22 @@ def mla_decode_sparse(
         bad = (keep_pos >= seq_lens.view(-1, 1).to(keep_pos.dtype)).any()
         if bool(bad):
             raise checks.KernelInputError("mla_decode_sparse: a kept position lies beyond its sequence")
-    if (_cuda(q) and sparse_kernel_enabled() and q.dtype == torch.bfloat16 and q.shape[-1] == 576
+    if (_cuda(q) and sparse_kernel_enabled(q.shape[1]) and q.dtype == torch.bfloat16 and q.shape[-1] == 576
             and kv_lora_rank == 512 and q.shape[1] % 16 == 0):
         return _cuda_ops().mla_decode_sparse(q, kv_cache, block_table, seq_lens.to(torch.int32),
                                              keep_pos.to(torch.int32).contiguous(), scale, num_splits)
     return ref.mla_decode_sparse(q, kv_cache, block_table, keep_pos, scale, kv_lora_rank)
 
 
-def sparse_kernel_enabled() -> bool:
-    """``AFD_SPARSE_MLA_KERNEL=1`` routes sparse MLA decode to the gather kernel."""
-    return os.environ.get("AFD_SPARSE_MLA_KERNEL", "") in ("1", "true", "on")
+def sparse_kernel_enabled(heads: int = 16) -> bool:
+    """Whether sparse MLA decode runs on the gather kernel for ``heads`` heads
+    (default: up to 32 heads; ``AFD_SPARSE_MLA_KERNEL=1`` / ``0`` forces it)."""
+    v = os.environ.get("AFD_SPARSE_MLA_KERNEL", "")
+    if v in ("1", "true", "on"):
+        return True
+    if v in ("0", "false", "off"):
+        return False
+    return heads <= 32
 
 
 def gqa_decode(

@@ -104,3 +104,16 @@ def test_indexer_weights_are_attention_role_and_load_by_name():
     assert weight_roles(name, arch, compute_gate_on_attention=False) == {"attention"}
     ffn = build_model(arch, role="ffn", dtype=torch.float32, seed=0)
     assert all("indexer" not in s.name for s in ffn.param_specs())
+
+
+def test_sparse_kernel_selection_by_head_count(monkeypatch):
+    """The gather kernel is the default up to 32 heads; the switch forces either path."""
+    from afd_plugin_b200 import ops
+
+    monkeypatch.delenv("AFD_SPARSE_MLA_KERNEL", raising=False)
+    assert ops.sparse_kernel_enabled(16) and ops.sparse_kernel_enabled(32)
+    assert not ops.sparse_kernel_enabled(128)
+    monkeypatch.setenv("AFD_SPARSE_MLA_KERNEL", "1")
+    assert ops.sparse_kernel_enabled(128)
+    monkeypatch.setenv("AFD_SPARSE_MLA_KERNEL", "0")
+    assert not ops.sparse_kernel_enabled(16)
