@@ -248,9 +248,11 @@ class MLAAttention(nn.Module):
             kv_cache, index_cache = kv_cache
         T = h.shape[0]
         q, kv_a, q_latent = self.project(h)
+        q_pe = q[..., self.qk_nope :]
+        # latent norm + key rope + cache store, and the query's rope (in place), in one launch
         ops.mla_cache_write(
             kv_cache, kv_a, self.kv_a_layernorm.weight, self.kv_a_layernorm.eps,
-            meta.positions, cos_sin, meta.slot_mapping, self.kv_lora,
+            meta.positions, cos_sin, meta.slot_mapping, self.kv_lora, q_pe=q_pe,
         )
         sparse = False
         if self.indexer is not None:
@@ -259,8 +261,6 @@ class MLAAttention(nn.Module):
             sparse = meta.sparse_decode or not meta.is_decode
             if sparse:
                 qi, wi = self.indexer.queries(h, q_latent, meta.positions, cos_sin)
-        q_pe = q[..., self.qk_nope :]
-        ops.rope_(q_pe, meta.positions, cos_sin, interleaved=True)
         q_nope = q[..., : self.qk_nope]
         if (h.is_cuda and meta.is_decode and not sparse and self.kv_lora == 512 and self.qk_rope == 64
                 and self.num_heads % 16 == 0):
@@ -268,8 +268,10 @@ class MLAAttention(nn.Module):
             q_lat = torch.bmm(q_nope.transpose(0, 1), self.w_uk)
             o_lat = ops.mla_decode_split(q_lat.transpose(0, 1), q_pe, kv_cache, meta.block_table, meta.seq_lens,
                                          self.scale, head_major_out=True)
-            o = torch.bmm(o_lat, self.w_uv_t).transpose(0, 1).reshape(T, self.num_heads * self.v_dim)
-            return self.tp.all_reduce(ops.linear(o, self.o_proj))
+            # [H,T,512]x[H,512,v] written straight into token-major rows (ldc = H*v) for o_proj
+            o = torch.empty(T, self.num_heads, self.v_dim, dtype=h.dtype, device=h.device)
+            torch.bmm(o_lat, self.w_uv_t, out=o.transpose(0, 1))
+            return self.tp.all_reduce(ops.linear(o.view(T, self.num_heads * self.v_dim), self.o_proj))
         # [H, T, nope] x [H, nope, kv_lora] -> [H, T, kv_lora]
         if h.is_cuda:
             q_lat = torch.bmm(q_nope.transpose(0, 1), self.w_uk)

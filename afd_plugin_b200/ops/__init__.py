@@ -24,6 +24,13 @@ def _cuda(t: torch.Tensor) -> bool:
     return t.is_cuda
 
 
+def _rows16(t: torch.Tensor) -> bool:
+    """Every row of ``t`` (last dim contiguous) starts on a 16-byte boundary and holds whole 16-byte vectors."""
+    vec = 16 // t.element_size()
+    return (t.stride(-1) == 1 and t.shape[-1] % vec == 0 and t.data_ptr() % 16 == 0
+            and all(st % vec == 0 for st in t.stride()[:-1]))
+
+
 # ----------------------------------------------------------------- norms
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     if _cuda(x):
@@ -237,16 +244,25 @@ def mla_cache_write(
     cos_sin: torch.Tensor,
     slot_mapping: torch.Tensor,
     kv_lora_rank: int,
+    q_pe: torch.Tensor | None = None,
 ) -> None:
     """Normalise the latent, rotate the shared rope key and store both in the cache.
 
-    ``kv_a [T, kv_lora + rope]`` is the ``kv_a_proj_with_mqa`` output.
+    ``kv_a [T, kv_lora + rope]`` is the ``kv_a_proj_with_mqa`` output.  With
+    ``q_pe [T, H, rope]`` the query's rope part is rotated in place as well
+    (interleaved pairs, like the key), in the same CUDA launch.
     """
     if checks.enabled():
         checks.cache_slots("mla_cache_write", slot_mapping, num_slots=kv_cache.shape[0] * kv_cache.shape[1])
     if _cuda(kv_a):
-        _cuda_ops().mla_cache_write(kv_cache, kv_a, norm_weight, eps, positions, cos_sin, slot_mapping, kv_lora_rank)
+        if q_pe is not None and not _rows16(q_pe):
+            rope_(q_pe, positions, cos_sin, interleaved=True)  # unaligned rows: the separate rope kernel
+            q_pe = None
+        _cuda_ops().mla_cache_write(kv_cache, kv_a, norm_weight, eps, positions, cos_sin, slot_mapping, kv_lora_rank,
+                                    q_pe)
         return
+    if q_pe is not None:
+        rope_(q_pe, positions, cos_sin, interleaved=True)
     latent = ref.rms_norm(kv_a[:, :kv_lora_rank], norm_weight, eps)
     k_pe = ref.apply_rope(kv_a[:, None, kv_lora_rank:], positions, cos_sin, interleaved=True)[:, 0]
     flat = kv_cache.view(-1, kv_cache.shape[-1])

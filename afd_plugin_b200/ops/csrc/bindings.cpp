@@ -1,6 +1,7 @@
 // torch.ops.afd_b200.* registrations for the sm_100a kernels.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGraphsC10Utils.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
@@ -47,6 +48,27 @@ at::Tensor& status_tensor(int device) {
 }
 
 int* status_ptr(const at::Tensor& like) { return status_tensor(like.get_device()).data_ptr<int>(); }
+
+// Per-device arrival counters for merging MLA split partials inside the decode
+// launch (zeroed once; every launch leaves them zero).  Decode launches on a
+// device are stream-ordered in this runtime, so one array serves them all.
+// Returns nullptr (the launch then runs the separate combine kernel) when the
+// array is too small or does not exist yet while a graph is being captured,
+// so that no allocation or memset is recorded into the graph.
+constexpr int64_t kMlaArrivals = 1 << 16;
+std::vector<at::Tensor> g_mla_arrivals;
+
+int* mla_arrivals(const at::Tensor& like, int64_t need) {
+  if (need > kMlaArrivals) return nullptr;
+  const int device = like.get_device();
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  if ((int)g_mla_arrivals.size() <= device) g_mla_arrivals.resize(device + 1);
+  if (!g_mla_arrivals[device].defined()) {
+    if (c10::cuda::currentStreamCaptureStatusMayInitCtx() != c10::cuda::CaptureStatus::None) return nullptr;
+    g_mla_arrivals[device] = at::zeros({kMlaArrivals}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
+  }
+  return g_mla_arrivals[device].data_ptr<int>();
+}
 
 // ------------------------------------------------------------------ norms
 at::Tensor rms_norm(const at::Tensor& x, const at::Tensor& w, double eps) {
@@ -140,18 +162,38 @@ std::tuple<at::Tensor, at::Tensor> topk_route(const at::Tensor& logits, int64_t 
 }
 
 // --------------------------------------------------------------- KV cache
+// With q_pe ([T, H, R], last dim contiguous), its interleaved RoPE runs in the
+// same launch (in place).
 void mla_cache_write(at::Tensor& cache, const at::Tensor& kv_a, const at::Tensor& w, double eps,
-                     const at::Tensor& positions, const at::Tensor& cos_sin, const at::Tensor& slots, int64_t L) {
+                     const at::Tensor& positions, const at::Tensor& cos_sin, const at::Tensor& slots, int64_t L,
+                     const c10::optional<at::Tensor>& q_pe) {
   check_cuda(kv_a, "kv_a");
   const int64_t D = cache.size(-1);
   const int R = (int)(D - L);
   TORCH_CHECK(kv_a.size(1) == D && kv_a.stride(1) == 1, "mla_cache_write: kv_a [T, L+R] row-major");
   TORCH_CHECK(cache.scalar_type() == kv_a.scalar_type() && cache.is_contiguous(), "mla_cache_write: cache");
   TORCH_CHECK(kv_a.stride(0) % (16 / kv_a.element_size()) == 0, "mla_cache_write: row stride alignment");
+  void* qp = nullptr;
+  int qh = 0;
+  int64_t qst = 0, qsh = 0;
+  if (q_pe.has_value() && q_pe->defined()) {
+    const at::Tensor& q = *q_pe;
+    const int64_t vec = 16 / q.element_size();
+    TORCH_CHECK(q.dim() == 3 && q.size(0) == kv_a.size(0) && q.size(2) == R && q.stride(2) == 1 &&
+                    q.scalar_type() == kv_a.scalar_type() && q.is_cuda(),
+                "mla_cache_write: q_pe [T, H, rope] with a contiguous last dim");
+    TORCH_CHECK(R % vec == 0 && q.stride(0) % vec == 0 && q.stride(1) % vec == 0 &&
+                    reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+                "mla_cache_write: q_pe rows must be 16-byte aligned");
+    qp = q.data_ptr();
+    qh = (int)q.size(1);
+    qst = q.stride(0);
+    qsh = q.stride(1);
+  }
   c10::cuda::CUDAGuard g(kv_a.device());
   launch_mla_cache_write(cache.data_ptr(), kv_a.data_ptr(), w.data_ptr(), (float)eps, positions.data_ptr<int64_t>(),
                          cos_sin.data_ptr<float>(), slots.data_ptr<int64_t>(), (int)kv_a.size(0), (int)L, R,
-                         kv_a.stride(0), dtype_code(kv_a), stream());
+                         kv_a.stride(0), dtype_code(kv_a), stream(), qp, qh, qst, qsh);
 }
 
 void gqa_cache_write(at::Tensor& kc, at::Tensor& vc, const at::Tensor& k, const at::Tensor& v,
@@ -215,7 +257,7 @@ at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at:
       launch_mla_decode(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
                         splits > 1 ? po.data_ptr<float>() : nullptr, splits > 1 ? pl.data_ptr<float>() : nullptr,
                         status_ptr(q_lat), B, H, 512, 64, bs, nblocks, (int)block_table.stride(0), splits,
-                        (float)scale, stream());
+                        (float)scale, stream(), splits > 1 ? mla_arrivals(q_lat, (int64_t)B * (H / 16)) : nullptr);
   TORCH_CHECK(e == cudaSuccess, "mla_decode: launch failed: ", cudaGetErrorString(e));
   return out;
 }
@@ -262,7 +304,8 @@ at::Tensor mla_decode_sparse(const at::Tensor& q, const at::Tensor& cache, const
   launch_mla_decode_sparse(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
                            keep_pos.data_ptr<int32_t>(), K, splits > 1 ? po.data_ptr<float>() : nullptr,
                            splits > 1 ? pl.data_ptr<float>() : nullptr, status_ptr(q), B, H, 512, (int)cache.size(1),
-                           (int)block_table.stride(0), splits, (float)scale, stream());
+                           (int)block_table.stride(0), splits, (float)scale, stream(),
+                           splits > 1 ? mla_arrivals(q, (int64_t)B * (H / 16)) : nullptr);
   return out;
 }
 
@@ -969,7 +1012,7 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("topk_route(Tensor logits, int k, int scoring, bool renorm, Tensor? bias, int n_group, int topk_group, "
         "float scale, Tensor? forced=None) -> (Tensor, Tensor)");
   m.def("mla_cache_write(Tensor(a!) cache, Tensor kv_a, Tensor w, float eps, Tensor positions, Tensor cos_sin, "
-        "Tensor slots, int L) -> ()");
+        "Tensor slots, int L, Tensor(b!)? q_pe=None) -> ()");
   m.def("gqa_cache_write(Tensor(a!) kc, Tensor(b!) vc, Tensor k, Tensor v, Tensor slots) -> ()");
   m.def("mla_decode(Tensor q_lat, Tensor q_pe, Tensor cache, Tensor block_table, Tensor seq_lens, float scale, "
         "int num_splits, bool head_major) -> Tensor");

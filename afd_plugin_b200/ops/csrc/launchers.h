@@ -18,9 +18,12 @@ void launch_rope(void* x, const int64_t* pos, const float* cos_sin, int tokens, 
 void launch_topk_route(const float* logits, const float* bias, float* w, int32_t* ids, int tokens, int E, int k,
                        int scoring, bool renorm, int n_group, int topk_group, float scale, const int32_t* forced,
                        cudaStream_t s);
+// q_pe (optional, [T, q_heads, R] with strides q_st / q_sh) is rotated in place
+// by the same launch.
 void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float eps, const int64_t* pos,
                             const float* cos_sin, const int64_t* slots, int tokens, int L, int R, int64_t kv_stride,
-                            int dtype, cudaStream_t s);
+                            int dtype, cudaStream_t s, void* q_pe = nullptr, int q_heads = 0, int64_t q_st = 0,
+                            int64_t q_sh = 0);
 void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, const int64_t* slots, int tokens,
                             int row_elems, int64_t k_stride, int64_t v_stride, int dtype, cudaStream_t s);
 
@@ -50,18 +53,21 @@ int mla_decode_num_splits(int batch, int max_seq_len, int num_sms);
 cudaError_t mla_decode_prepare_device();
 // Returns cudaSuccess after launching, or an error with nothing launched: the
 // cache base is not 16-byte aligned (a TMA rule), the shared-memory opt-in
-// failed, or the cache's tensor map could not be encoded.
+// failed, or the cache's tensor map could not be encoded.  With split
+// partials, `arrivals` (batch x heads/16 int32, all zero; left zero) lets the
+// last CTA of each group merge them in the same launch; nullptr launches the
+// separate combine kernel.  Launches sharing `arrivals` must be stream-ordered.
 cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
                               const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                               int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
-                              int num_splits, float scale, cudaStream_t s);
+                              int num_splits, float scale, cudaStream_t s, int* arrivals = nullptr);
 // Sparse (DeepSeek sparse attention) decode over keep_pos [B, num_keep] int32
 // (-1 or a position >= seq_lens[b] = unused entry); same outputs and scratch,
 // with splits over the kept entries.
 void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t* block_table, const int32_t* seq_lens,
                               const int32_t* keep_pos, int num_keep, float* partial_o, float* partial_lse, int* status,
                               int batch, int heads, int L, int block_size, int max_blocks_per_seq, int num_splits,
-                              float scale, cudaStream_t s);
+                              float scale, cudaStream_t s, int* arrivals = nullptr);
 
 // ---- gqa_decode.cu
 // q [B, hq, 128], caches [blocks, bs, hkv, 128], out [B, hq, 128] (bf16).

@@ -7,8 +7,10 @@
 // four math warps compute S = Q K^T (tokens split over warps), an online
 // softmax (exp2 domain) and O += P V (latent dims split over warps) with
 // tensor-core MMAs reading the swizzled tiles through ldmatrix.  With several
-// splits each CTA writes a normalised partial O plus its log-sum-exp and a
-// combine kernel merges them.
+// splits each CTA writes a normalised partial O plus its log-sum-exp; the last
+// CTA of a (request, head group) to finish merges them (a per-group arrival
+// counter that it resets), or, without counters, a combine kernel does.  The
+// producer warp starts streaming KV tiles while the math warps load the query.
 //
 // Memory-bound by design: per token per layer it reads 1152 B of cache and
 // does ~37 kFLOP for 16 heads, well under the tensor-core ceiling; the
@@ -55,6 +57,7 @@ struct Smem {
   float s[2][kHeads * kSStride];
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  int last;  // this CTA merges its group's split partials
 };
 
 // Byte offset of element (row, col) inside a 128B-swizzled tile made of
@@ -82,12 +85,72 @@ AFD_DEVICE bool sparse_entry_valid(const int32_t* __restrict__ keep_pos, int b, 
   return p >= 0 && p < seq_len;
 }
 
+// out[b, h, :] = sum_s w_s o_s / sum_s w_s with w_s = 2^(lse_s - max_s lse),
+// for the 16 heads of group hg, by the 128 math threads of the CTA that
+// arrived last.  Partials are read through L2 (other CTAs of this launch wrote
+// them).  The split log-sum-exps are staged in shared memory with independent
+// loads, turned into normalised weights per head, and then every thread owns
+// four latent columns of all 16 heads, so each split's rows arrive as eight
+// independent 16-byte loads per thread instead of a chain of dependent ones.
+constexpr int kMergeMaxSplits = (2 * kHeads * kSStride) / kHeads;  // the weights live in Smem::s
+
+AFD_DEVICE void merge_group(const MlaQO& qo, const float* part_o, const float* part_lse, int b, int hg, int heads,
+                            int num_splits, int tid, float* wsm) {
+  const float* pl = part_lse + (size_t)b * num_splits * heads + hg * kHeads;
+  for (int i = tid; i < num_splits * kHeads; i += kMathWarps * 32)
+    wsm[i] = __ldcg(pl + (size_t)(i / kHeads) * heads + (i % kHeads));
+  asm volatile("bar.sync 1, %0;" ::"n"(kMathWarps * 32));
+  if (tid < kHeads) {
+    float mx = -INFINITY;
+    for (int sp = 0; sp < num_splits; ++sp) mx = fmaxf(mx, wsm[sp * kHeads + tid]);
+    float wsum = 0.f;
+    for (int sp = 0; sp < num_splits; ++sp) {
+      const float v = wsm[sp * kHeads + tid];
+      const float w = (v == -INFINITY) ? 0.f : exp2f(v - mx);
+      wsm[sp * kHeads + tid] = w;
+      wsum += w;
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    for (int sp = 0; sp < num_splits; ++sp) wsm[sp * kHeads + tid] *= inv;
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kMathWarps * 32));
+  static_assert(kL / 4 == kMathWarps * 32, "one float4 column per math thread");
+  const int c = tid * 4;
+  const float* base = part_o + ((size_t)b * num_splits * heads + (size_t)hg * kHeads) * kL + c;
+#pragma unroll 1
+  for (int h0 = 0; h0 < kHeads; h0 += 8) {
+    float4 acc[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < num_splits; ++sp) {
+      const float* ps = base + ((size_t)sp * heads + h0) * kL;
+      float4 x[8];
+#pragma unroll
+      for (int h = 0; h < 8; ++h) x[h] = __ldcg(reinterpret_cast<const float4*>(ps + (size_t)h * kL));
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        const float w = wsm[sp * kHeads + h0 + h];
+        acc[h].x += w * x[h].x;
+        acc[h].y += w * x[h].y;
+        acc[h].z += w * x[h].z;
+        acc[h].w += w * x[h].w;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      __nv_bfloat16* ob = qo.out + (size_t)b * qo.out_sb + (size_t)(hg * kHeads + h0 + h) * qo.out_sh + c;
+      *reinterpret_cast<__nv_bfloat162*>(ob) = __floats2bfloat162_rn(acc[h].x, acc[h].y);
+      *reinterpret_cast<__nv_bfloat162*>(ob + 2) = __floats2bfloat162_rn(acc[h].z, acc[h].w);
+    }
+  }
+}
+
 template <bool kSparse>
-__global__ void __launch_bounds__(kThreads) mla_decode_kernel(
+__global__ void __launch_bounds__(kThreads, 2) mla_decode_kernel(
     const __grid_constant__ CUtensorMap kv_map, const MlaQO qo, const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
     float* __restrict__ part_lse, int* __restrict__ status, int heads, int block_size, int max_blocks,
     int num_splits, float scale_log2, const __nv_bfloat16* __restrict__ cache, const int32_t* __restrict__ keep_pos,
-    int num_keep) {
+    int num_keep, int* __restrict__ arrivals) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int b = blockIdx.x;
@@ -110,18 +173,23 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
     }
     fence_barrier_init();
   }
-  // Q tile (16 heads x 576) -> swizzled smem, all threads.  The latent part
-  // and the rope part come from separate (strided) tensors.
-  for (int c = threadIdx.x; c < kHeads * (kD / 8); c += kThreads) {
-    const int r = c / (kD / 8);
-    const int col = (c % (kD / 8)) * 8;
-    const int h = hg * kHeads + r;
-    const __nv_bfloat16* src =
-        (col < kL) ? qo.q_lat + (size_t)b * qo.lat_sb + (size_t)h * qo.lat_sh + col
-                   : qo.q_pe + (size_t)b * qo.pe_sb + (size_t)h * qo.pe_sh + (col - kL);
-    *reinterpret_cast<uint4*>(sm.q + swz(r, col, kQBoxBytes)) = *reinterpret_cast<const uint4*>(src);
-  }
   __syncthreads();
+
+  if (warp < kMathWarps) {
+    // Q tile (16 heads x 576) -> swizzled smem by the math warps while the
+    // producer's first tiles are in flight.  The latent part and the rope
+    // part come from separate (strided) tensors.
+    for (int c = threadIdx.x; c < kHeads * (kD / 8); c += kMathWarps * 32) {
+      const int r = c / (kD / 8);
+      const int col = (c % (kD / 8)) * 8;
+      const int h = hg * kHeads + r;
+      const __nv_bfloat16* src =
+          (col < kL) ? qo.q_lat + (size_t)b * qo.lat_sb + (size_t)h * qo.lat_sh + col
+                     : qo.q_pe + (size_t)b * qo.pe_sb + (size_t)h * qo.pe_sh + (col - kL);
+      *reinterpret_cast<uint4*>(sm.q + swz(r, col, kQBoxBytes)) = *reinterpret_cast<const uint4*>(src);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kMathWarps * 32));
+  }
 
   if (warp == kMathWarps) {
     // ------------------------------------------------------------ producer
@@ -331,6 +399,21 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(
       pl[h_lo] = l_run[0] > 0.f ? m_run[0] + log2f(l_run[0]) : -INFINITY;
       pl[h_lo + 8] = l_run[1] > 0.f ? m_run[1] + log2f(l_run[1]) : -INFINITY;
     }
+    if (arrivals != nullptr) {
+      // Release this CTA's partials, count it in; the last arrival merges.
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(kMathWarps * 32));
+      if (threadIdx.x == 0) {
+        int* ctr = arrivals + (size_t)b * gridDim.y + hg;
+        const int prev = atomicAdd(ctr, 1);
+        sm.last = prev == num_splits - 1;
+        if (sm.last) *ctr = 0;  // ready for the next launch (stream-ordered)
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kMathWarps * 32));
+      if (!sm.last) return;
+      __threadfence();
+      merge_group(qo, part_o, part_lse, b, hg, heads, num_splits, threadIdx.x, &sm.s[0][0]);
+    }
   }
 }
 
@@ -389,8 +472,10 @@ int mla_decode_num_splits(int batch, int max_seq_len, int num_sms) {
   // Splitting costs a partial-O round trip through HBM (and a combine launch),
   // so split only when the batch alone leaves SMs idle.
   if (batch * 2 >= 3 * num_sms) return 1;
-  const int target = 2 * num_sms;  // one wave of two resident CTAs per SM
-  int s = (target + batch - 1) / batch;
+  // One wave of two resident CTAs per SM: a split count that overfills it
+  // leaves a second, nearly empty wave that runs at a fraction of HBM.
+  const int slots = 2 * num_sms;
+  int s = slots / batch;
   s = s < 1 ? 1 : s;
   const int max_s = tiles / 2 > 0 ? tiles / 2 : 1;  // keep >= 2 tiles per split
   return s > max_s ? max_s : s;
@@ -411,7 +496,7 @@ cudaError_t mla_decode_prepare_device() {
 cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t* block_table,
                               const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                               int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
-                              int num_splits, float scale, cudaStream_t s) {
+                              int num_splits, float scale, cudaStream_t s, int* arrivals) {
   if ((reinterpret_cast<uintptr_t>(cache) & 15u) != 0) return cudaErrorMisalignedAddress;
   cudaError_t e = mla_decode_prepare_device();
   if (e != cudaSuccess) return e;
@@ -429,10 +514,12 @@ cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t*
   const int smem = (int)sizeof(mla::Smem) + 1024;
   dim3 grid(batch, heads / mla::kHeads, num_splits);
   const float scale_log2 = scale * 1.4426950408889634f;
+  if (num_splits == 1 || num_splits > mla::kMergeMaxSplits) arrivals = nullptr;
   mla::mla_decode_kernel<false><<<grid, mla::kThreads, smem, s>>>(map, qo, block_table, seq_lens, partial_o, partial_lse,
                                                                    status, heads, block_size, max_blocks_per_seq,
-                                                                   num_splits, scale_log2, nullptr, nullptr, 0);
-  if (num_splits > 1) {
+                                                                   num_splits, scale_log2, nullptr, nullptr, 0,
+                                                                   arrivals);
+  if (num_splits > 1 && arrivals == nullptr) {
     mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
   }
   return cudaGetLastError();
@@ -441,7 +528,7 @@ cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t*
 void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t* block_table, const int32_t* seq_lens,
                               const int32_t* keep_pos, int num_keep, float* partial_o, float* partial_lse, int* status,
                               int batch, int heads, int L, int block_size, int max_blocks_per_seq, int num_splits,
-                              float scale, cudaStream_t s) {
+                              float scale, cudaStream_t s, int* arrivals) {
   CUtensorMap unused;
   memset(&unused, 0, sizeof(unused));
   const int smem = (int)sizeof(mla::Smem) + 1024;
@@ -450,8 +537,9 @@ void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t*
   const float scale_log2 = scale * 1.4426950408889634f;
   mla::mla_decode_kernel<true><<<grid, mla::kThreads, smem, s>>>(
       unused, qo, block_table, seq_lens, partial_o, partial_lse, status, heads, block_size, max_blocks_per_seq,
-      num_splits, scale_log2, reinterpret_cast<const __nv_bfloat16*>(cache), keep_pos, num_keep);
-  if (num_splits > 1) {
+      num_splits, scale_log2, reinterpret_cast<const __nv_bfloat16*>(cache), keep_pos, num_keep,
+      num_splits > 1 && num_splits <= mla::kMergeMaxSplits ? arrivals : nullptr);
+  if (num_splits > 1 && arrivals == nullptr) {
     mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
   }
 }

@@ -415,3 +415,38 @@ def test_tc_gemm_split_k_per_head():
     _close(o / sc, want / sc, 2e-2)
     torch.cuda.synchronize()
     assert int(ctr.abs().sum()) == 0 and float(ws.abs().sum()) == 0.0
+
+
+def test_mla_decode_split_merge_repeats():
+    """Split partials merged inside the launch: the arrival counters reset, so
+    back-to-back launches (64 requests, one wave of splits) all match fp32."""
+    torch.manual_seed(11)
+    lens = torch.randint(300, 1100, (64,)).tolist()
+    cache, table, seq = _paged_cache(64, lens, 576)
+    scale = 1 / math.sqrt(192)
+    for rep in range(3):
+        q = torch.randn(64, 16, 576, device=DEV, dtype=torch.bfloat16)
+        out = ops.mla_decode(q, cache, table, seq, scale, 512)
+        expect = ref.mla_decode(q.float(), cache.float(), table, seq, scale, 512)
+        _close(out, expect, 2e-2, 2e-2)
+
+
+def test_mla_cache_write_rotates_query():
+    """The cache-write launch also applies the query's interleaved RoPE in place (strided q_pe view)."""
+    T, H, L, R = 13, 16, 512, 64
+    torch.manual_seed(5)
+    kv_a = torch.randn(T, L + R, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(L, device=DEV, dtype=torch.bfloat16)
+    cs = ref.rope_cos_sin_cache(R, 256, 10000.0, None, DEV)
+    pos = torch.randint(0, 256, (T,), device=DEV)
+    cache = torch.zeros(4, 64, L + R, device=DEV, dtype=torch.bfloat16)
+    slots = torch.randperm(256, device=DEV)[:T]
+    q = torch.randn(T, H, 192, device=DEV, dtype=torch.bfloat16)
+    q_pe = q[..., 128:]
+    expect_q = ref.apply_rope(q_pe.float(), pos, cs, interleaved=True)
+    nope_before = q[..., :128].clone()
+    ops.mla_cache_write(cache, kv_a, w, 1e-6, pos, cs, slots, L, q_pe=q_pe)
+    _close(q[..., 128:], expect_q, 3e-2, 2e-2)
+    assert torch.equal(q[..., :128], nope_before)
+    flat = cache.view(-1, L + R)[slots]
+    _close(flat[:, L:], ref.apply_rope(kv_a[:, None, L:].float(), pos, cs, interleaved=True)[:, 0], 3e-2, 2e-2)
