@@ -15,11 +15,15 @@ experts from N(0, 1) logits with softmax weights.
   rank each way (+ 8 bytes per routed expert of routing metadata).
 * ``nccl``: the reference wire protocol -- each Attention rank sends its
   ``[T, H]`` hidden states to its FFN rank and receives ``[T, H]`` back
-  (NCCL send/recv).  Bytes per token: one row each way.
+  (NCCL send/recv on the FFN subgroup's communicator, stream-ordered as the
+  NCCL connector issues them).  Bytes per token: one row each way.
 
-Every number is CUDA-event timed per rank; the max over ranks is reported,
-with the achieved GB/s (bytes one Attention rank moves out and in) and the
-fraction of the NVLink roofline (measured 770 GB/s per direction per GPU).
+Both paths are timed as the decode step runs them: ``--iters`` round trips
+captured into one CUDA graph per rank, replayed after a barrier, CUDA-event
+timed per rank; the max over ranks is reported (``--eager`` times plain
+launches instead), with the achieved GB/s (bytes one Attention rank moves out
+and in) and the fraction of the NVLink roofline (measured 770 GB/s per
+direction per GPU).
 """
 
 from __future__ import annotations
@@ -48,9 +52,46 @@ def _args(argv=None):
     ap.add_argument("--paths", default="fused,nccl")
     ap.add_argument("--out", default="")
     ap.add_argument("--fp8", action="store_true", help="rows travel as e4m3 with 1x128 scales (fused path)")
+    ap.add_argument("--eager", action="store_true", help="time plain launches instead of a CUDA graph replay")
     ap.add_argument("--breakdown", action="store_true",
                     help="time each kernel of single round trips (barrier between trips)")
     return ap.parse_args(argv)
+
+
+def _timed_us(fn, args) -> float:
+    """Device time per call of ``fn`` on this rank: ``args.iters`` calls
+    captured into one CUDA graph (or launched eagerly with ``--eager``),
+    every rank starting after a barrier."""
+    dist.barrier()
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.eager:
+        e0.record()
+        for _ in range(args.iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        return e0.elapsed_time(e1) * 1e3 / args.iters
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(args.iters):
+            fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    graph.replay()  # warm replay
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    del graph  # released before any communicator it recorded is destroyed
+    return e0.elapsed_time(e1) * 1e3 / args.iters
 
 
 def _max_over_ranks(x: float) -> float:
@@ -114,19 +155,7 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
         if args.breakdown:
             results.append(_breakdown(args, role, T, conn, x, res, norm_w, gate_w, role_rank, d, A, F, H))
             continue
-        dist.barrier()
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.iters):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        dist.barrier()
-        us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / args.iters)
+        us = _max_over_ranks(_timed_us(fn, args))
         status = int(C.read_status(torch.cuda.current_device()))
         # Rows this rank moved: one per (token, destination FFN rank) each way.
         if role == "attention":
@@ -199,49 +228,42 @@ def bench_nccl(args, rank: int, tokens: list[int]) -> list[dict]:
     from afd_plugin_b200.config import afd_config_from_mapping
     from afd_plugin_b200.parallel.topology import build_rank_mapping, role_of_world_rank
 
+    from afd_plugin_b200.connectors.p2p_nccl import init_subgroup_comm
+    from afd_plugin_b200.ops._ext import ops
+
     A, F = args.attn, args.ffn
     role, role_rank = role_of_world_rank(rank, attention_size=A, ffn_size=F)
     m = build_rank_mapping(afd_config_from_mapping({"role": role, "num_attention_ranks": A, "num_ffn_ranks": F}),
                            role_rank)
+    comm = init_subgroup_comm(m, attention_size=A, ffn_size=F, device=torch.device("cuda", torch.cuda.current_device()))
+    send, recv = torch.ops.afd_b200.nccl_send, torch.ops.afd_b200.nccl_recv
     H = args.hidden
     results = []
     for T in tokens:
-        if role == "attention":
+        if role == "attention":  # subgroup rank 0 is the FFN rank
             x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
             y = torch.empty_like(x)
 
             def fn():
-                dist.send(x, dst=m.subgroup_ranks[0])
-                dist.recv(y, src=m.subgroup_ranks[0])
-        else:
-            peers = list(m.subgroup_ranks[1:])
-            bufs = [torch.empty(T, H, device="cuda", dtype=torch.bfloat16) for _ in peers]
+                send(x, 0, comm)
+                recv(y, 0, comm)
+        else:  # subgroup ranks 1..A/F are this FFN rank's Attention ranks
+            bufs = [torch.empty(T, H, device="cuda", dtype=torch.bfloat16) for _ in range(A // F)]
 
             def fn():
-                for p, b in zip(peers, bufs):
-                    dist.recv(b, src=p)
-                cat = torch.cat(bufs) if len(bufs) > 1 else bufs[0]
-                for i, p in enumerate(peers):
-                    dist.send(cat[i * T : (i + 1) * T].contiguous(), dst=p)
+                for j, b in enumerate(bufs):
+                    recv(b, j + 1, comm)
+                for j, b in enumerate(bufs):
+                    send(b, j + 1, comm)
 
-        dist.barrier()
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.iters):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        dist.barrier()
-        us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / args.iters)
+        us = _max_over_ranks(_timed_us(fn, args))
         bytes_per_attn = 2 * T * H * 2
         gbps = bytes_per_attn / (us * 1e-6) / 1e9
         ideal_us = (T * H * 2 * (A // F)) / (NVLINK_GBPS * 1e9) * 1e6  # the FFN rank serves A/F peers
         results.append({"path": "nccl", "tokens": T, "us": round(us, 2), "GBps": round(gbps, 1),
                         "roofline_frac": round(ideal_us / us, 3)})
+    torch.cuda.synchronize()
+    ops().nccl_comm_destroy(comm)
     return results
 
 

@@ -57,6 +57,29 @@ class _WireSpec(NamedTuple):
     size: torch.Size
 
 
+def init_subgroup_comm(mapping, *, attention_size: int, ffn_size: int, device) -> int:
+    """One NCCL communicator per FFN subgroup (the FFN rank first, then its
+    Attention ranks); returns this rank's communicator handle.  Every world
+    rank takes part in creating every subgroup's gloo group (a collective),
+    then joins its own communicator; its send/recv run on the caller's
+    current stream, so they can be captured into a CUDA graph."""
+    from afd_plugin_b200.ops._ext import ops
+
+    C = ops()
+    F, r = ffn_size, attention_size // ffn_size
+    mine = None
+    for k in range(F):
+        members = [k] + [F + k * r + j for j in range(r)]
+        g = dist.new_group(ranks=members, backend="gloo")
+        if k == mapping.subgroup_index:
+            mine = (g, members)
+    g, members = mine
+    box = [C.nccl_unique_id() if mapping.rank_in_subgroup == 0 else None]
+    dist.broadcast_object_list(box, src=members[0], group=g)
+    torch.cuda.set_device(device)
+    return int(C.nccl_comm_init(box[0], len(members), mapping.rank_in_subgroup))
+
+
 def num_tokens_for_attention_rank(dp_metadata: AFDDPMetadata, *, attention_rank: int, attention_size: int,
                                   fallback: int = 1) -> int:
     """Tokens one Attention rank puts on the wire for a stage (never below one)."""
@@ -143,23 +166,8 @@ class P2pNcclAFDConnector(AFDConnectorBase):
         self._initialized = True
 
     def _init_subgroup_comm(self) -> int:
-        """One NCCL communicator per FFN subgroup; every world rank takes part in
-        creating every subgroup's gloo group (a collective), then joins its own."""
-        from afd_plugin_b200.ops._ext import ops
-
-        C = ops()
-        F, A, r = self.ffn_size, self.attn_size, self.ratio
-        mine = None
-        for k in range(F):
-            members = [k] + [F + k * r + j for j in range(r)]
-            g = dist.new_group(ranks=members, backend="gloo")
-            if k == self.mapping.subgroup_index:
-                mine = (g, members)
-        g, members = mine
-        box = [C.nccl_unique_id() if self.mapping.rank_in_subgroup == 0 else None]
-        dist.broadcast_object_list(box, src=members[0], group=g)
-        torch.cuda.set_device(self.device)
-        return int(C.nccl_comm_init(box[0], len(members), self.mapping.rank_in_subgroup))
+        return init_subgroup_comm(self.mapping, attention_size=self.attn_size, ffn_size=self.ffn_size,
+                                  device=self.device)
 
     def close(self) -> None:
         self.flush()
@@ -359,4 +367,4 @@ class P2pNcclAFDControlPlane(AFDControlPlane):
         return recv_control_payload(src=c.mapping.control_source(), group=c.control_group, device=torch.device("cpu"))
 
 
-__all__ = ["P2pNcclAFDConnector", "P2pNcclAFDControlPlane", "num_tokens_for_attention_rank"]
+__all__ = ["P2pNcclAFDConnector", "P2pNcclAFDControlPlane", "init_subgroup_comm", "num_tokens_for_attention_rank"]

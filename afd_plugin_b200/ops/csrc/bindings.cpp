@@ -5,7 +5,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "launchers.h"
@@ -56,6 +58,16 @@ int* status_ptr(const at::Tensor& like) { return status_tensor(like.get_device()
 // array is too small or does not exist yet while a graph is being captured,
 // so that no allocation or memset is recorded into the graph.
 constexpr int64_t kMlaArrivals = 1 << 16;
+
+// AFD_MLA_KERNEL=mma selects the mma.sync MLA decode kernel (A/B comparisons);
+// the default is the tcgen05 kernel for the shapes it takes.
+bool mla_tc_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("AFD_MLA_KERNEL");
+    return !(v != nullptr && std::string(v) == "mma");
+  }();
+  return on;
+}
 std::vector<at::Tensor> g_mla_arrivals;
 
 int* mla_arrivals(const at::Tensor& like, int64_t need) {
@@ -232,10 +244,15 @@ at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at:
   const int maxb = (int)block_table.size(1);
   at::Tensor out = head_major ? at::empty({H, B, 512}, q_lat.options()) : at::empty({B, H, 512}, q_lat.options());
   if (B == 0) return out;
+  const int dev_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  // The tcgen05 kernel for the head counts it is faster at (64+ heads), unless
+  // AFD_MLA_KERNEL=mma asks for the mma.sync one; other shapes take mma.sync.
+  const int tc_hg = mla_tc_enabled() ? mla_decode_tc_heads_per_cta(H) : 0;
+  const bool use_tc = tc_hg > 0 && bs % 64 == 0;  // every tile shape divides a 64-token block
   int splits = (int)num_splits;
   if (splits <= 0) {
-    int dev_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-    splits = mla_decode_num_splits(B * (H / 16), maxb * bs, dev_sms);
+    splits = use_tc ? mla_decode_tc_num_splits(B, H, maxb * bs, dev_sms)
+                    : mla_decode_num_splits(B * (H / 16), maxb * bs, dev_sms);
   }
   at::Tensor po, pl;
   if (splits > 1) {
@@ -253,11 +270,31 @@ at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at:
   qo.out_sb = head_major ? 512 : (int64_t)H * 512;
   qo.out_sh = head_major ? (int64_t)B * 512 : 512;
   c10::cuda::CUDAGuard g(q_lat.device());
-  const cudaError_t e =
-      launch_mla_decode(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
-                        splits > 1 ? po.data_ptr<float>() : nullptr, splits > 1 ? pl.data_ptr<float>() : nullptr,
-                        status_ptr(q_lat), B, H, 512, 64, bs, nblocks, (int)block_table.stride(0), splits,
-                        (float)scale, stream(), splits > 1 ? mla_arrivals(q_lat, (int64_t)B * (H / 16)) : nullptr);
+  float* po_ptr = splits > 1 ? po.data_ptr<float>() : nullptr;
+  float* pl_ptr = splits > 1 ? pl.data_ptr<float>() : nullptr;
+  cudaError_t e = cudaErrorNotSupported;
+  if (use_tc) {
+    int* arr = splits > 1 ? mla_arrivals(q_lat, (int64_t)B * (H / tc_hg)) : nullptr;
+    if (splits == 1 || (arr != nullptr && splits <= mla_decode_tc_max_splits(tc_hg)))
+      e = launch_mla_decode_tc(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                               po_ptr, pl_ptr, status_ptr(q_lat), B, H, bs, nblocks, (int)block_table.stride(0), splits,
+                               (float)scale, stream(), arr);
+  }
+  if (e == cudaErrorNotSupported) {  // nothing launched: the mma.sync kernel takes the shape
+    if (use_tc && splits > 1 && num_splits <= 0) {
+      // the split count was picked for the other kernel's geometry: pick again
+      splits = mla_decode_num_splits(B * (H / 16), maxb * bs, dev_sms);
+      if (splits > 1 && po.size(1) < splits) {
+        po = at::empty({B, splits, H, 512}, q_lat.options().dtype(at::kFloat));
+        pl = at::empty({B, splits, H}, q_lat.options().dtype(at::kFloat));
+      }
+      po_ptr = splits > 1 ? po.data_ptr<float>() : nullptr;
+      pl_ptr = splits > 1 ? pl.data_ptr<float>() : nullptr;
+    }
+    e = launch_mla_decode(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), po_ptr,
+                          pl_ptr, status_ptr(q_lat), B, H, 512, 64, bs, nblocks, (int)block_table.stride(0), splits,
+                          (float)scale, stream(), splits > 1 ? mla_arrivals(q_lat, (int64_t)B * (H / 16)) : nullptr);
+  }
   TORCH_CHECK(e == cudaSuccess, "mla_decode: launch failed: ", cudaGetErrorString(e));
   return out;
 }

@@ -156,21 +156,45 @@ __global__ void topk_route_kernel(const float* __restrict__ logits, const float*
 
 // ============================================================ MLA cache write
 // kv_a [T, L + R]: latent (RMSNorm) || k_pe (interleaved RoPE) -> cache[slot].
-// With q_pe, the same warp also rotates the token's query rope part in place
-// (q_pe [T, q_heads, R] strided; same position, same interleaved pairing), so
-// decode needs no separate query-rope launch.
+// With q_pe, the token's query rope part is rotated in place by the same
+// launch (q_pe [T, q_heads, R] strided; same position, same interleaved
+// pairing), so decode needs no separate query-rope launch.  One CTA per
+// token: warp 0 writes the cache row, the other warps (kQWarps) rotate the
+// query in 16-byte vectors whose loads are all in flight together.
+constexpr int kQWarps = 3;
+
 template <typename T>
 __global__ void mla_cache_write_kernel(T* __restrict__ cache, const T* __restrict__ kv_a, const T* __restrict__ w,
                                        float eps, const int64_t* __restrict__ pos, const float* __restrict__ cos_sin,
                                        const int64_t* __restrict__ slots, int tokens, int L, int R,
                                        int64_t kv_stride, T* __restrict__ q_pe, int q_heads, int64_t q_st,
                                        int64_t q_sh) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (warp >= tokens) return;
   constexpr int VN = Vec16<T>::N;
-  const T* src = kv_a + (size_t)warp * kv_stride;
-  T* dst = cache + slots[warp] * (int64_t)(L + R);
+  const float* cs = cos_sin + pos[t] * R;
+  if (warp > 0) {
+    T* qt = q_pe + (size_t)t * q_st;
+    const int per_head = R / VN;
+    for (int i = threadIdx.x - 32; i < q_heads * per_head; i += kQWarps * 32) {
+      const int h = i / per_head, c0 = (i % per_head) * VN;
+      T* x = qt + (size_t)h * q_sh + c0;
+      Vec16<T> v = load16(x);
+#pragma unroll
+      for (int j = 0; j < VN / 2; ++j) {
+        const int p = c0 / 2 + j;
+        const float c = cs[p], s = cs[R / 2 + p];
+        const float a = to_f32(v.v[2 * j]), b = to_f32(v.v[2 * j + 1]);
+        v.v[2 * j] = from_f32<T>(a * c - b * s);
+        v.v[2 * j + 1] = from_f32<T>(b * c + a * s);
+      }
+      store16(x, v);
+    }
+    return;
+  }
+  const T* src = kv_a + (size_t)t * kv_stride;
+  T* dst = cache + slots[t] * (int64_t)(L + R);
   float ss = 0.f;
   for (int v = lane; v < L / VN; v += 32) {
     Vec16<T> a = load16(src + v * VN);
@@ -186,32 +210,11 @@ __global__ void mla_cache_write_kernel(T* __restrict__ cache, const T* __restric
     for (int i = 0; i < VN; ++i) a.v[i] = from_f32<T>(to_f32(a.v[i]) * inv * to_f32(ww.v[i]));
     store16(dst + v * VN, a);
   }
-  const float* cs = cos_sin + pos[warp] * R;
   for (int p = lane; p < R / 2; p += 32) {
     const float c = cs[p], s = cs[R / 2 + p];
     const float a = to_f32(src[L + 2 * p]), b = to_f32(src[L + 2 * p + 1]);
     dst[L + 2 * p] = from_f32<T>(a * c - b * s);
     dst[L + 2 * p + 1] = from_f32<T>(b * c + a * s);
-  }
-  if (q_pe != nullptr) {
-    // 16-byte vectors (VN / 2 interleaved pairs each); every lane's vectors
-    // are independent, so their loads are in flight together.
-    T* qt = q_pe + (size_t)warp * q_st;
-    const int per_head = R / VN;
-    for (int i = lane; i < q_heads * per_head; i += 32) {
-      const int h = i / per_head, c0 = (i % per_head) * VN;
-      T* x = qt + (size_t)h * q_sh + c0;
-      Vec16<T> v = load16(x);
-#pragma unroll
-      for (int j = 0; j < VN / 2; ++j) {
-        const int p = c0 / 2 + j;
-        const float c = cs[p], s = cs[R / 2 + p];
-        const float a = to_f32(v.v[2 * j]), b = to_f32(v.v[2 * j + 1]);
-        v.v[2 * j] = from_f32<T>(a * c - b * s);
-        v.v[2 * j + 1] = from_f32<T>(b * c + a * s);
-      }
-      store16(x, v);
-    }
   }
 }
 
@@ -286,10 +289,11 @@ void launch_topk_route(const float* logits, const float* bias, float* w, int32_t
 void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float eps, const int64_t* pos,
                             const float* cos_sin, const int64_t* slots, int tokens, int L, int R, int64_t kv_stride,
                             int dtype, cudaStream_t s, void* q_pe, int q_heads, int64_t q_st, int64_t q_sh) {
+  if (tokens == 0) return;
   AFD_DTYPE_SWITCH(dtype, T, {
-    dim3 grid((tokens + 3) / 4);
-    mla_cache_write_kernel<T><<<grid, 128, 0, s>>>((T*)cache, (const T*)kv_a, (const T*)w, eps, pos, cos_sin, slots,
-                                                   tokens, L, R, kv_stride, (T*)q_pe, q_heads, q_st, q_sh);
+    const int threads = q_pe != nullptr ? 32 * (1 + kQWarps) : 32;
+    mla_cache_write_kernel<T><<<tokens, threads, 0, s>>>((T*)cache, (const T*)kv_a, (const T*)w, eps, pos, cos_sin,
+                                                         slots, tokens, L, R, kv_stride, (T*)q_pe, q_heads, q_st, q_sh);
   });
 }
 

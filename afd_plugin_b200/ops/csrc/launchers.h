@@ -61,6 +61,19 @@ cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t*
                               const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                               int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
                               int num_splits, float scale, cudaStream_t s, int* arrivals = nullptr);
+// ---- mla_decode_tc.cu (tcgen05 version of the same decode; DeepSeek 512 + 64
+// latent, block sizes that are multiples of 64, heads a multiple of 16).
+// Heads per CTA for `heads` (0 = unsupported), the split count for a batch,
+// and the largest split count its in-launch merge takes.  Returns cudaErrorNotSupported
+// (nothing launched) for a shape it does not take; split partials need
+// `arrivals` as in launch_mla_decode.
+int mla_decode_tc_heads_per_cta(int heads);
+int mla_decode_tc_num_splits(int batch, int heads, int max_seq_len, int num_sms);
+int mla_decode_tc_max_splits(int heads_per_cta);
+cudaError_t launch_mla_decode_tc(const MlaQO& qo, const void* cache, const int32_t* block_table,
+                                 const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
+                                 int heads, int block_size, int num_blocks, int max_blocks_per_seq, int num_splits,
+                                 float scale, cudaStream_t s, int* arrivals);
 // Sparse (DeepSeek sparse attention) decode over keep_pos [B, num_keep] int32
 // (-1 or a position >= seq_lens[b] = unused entry); same outputs and scratch,
 // with splits over the kept entries.

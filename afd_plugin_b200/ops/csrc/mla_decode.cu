@@ -218,21 +218,34 @@ __global__ void __launch_bounds__(kThreads, 2) mla_decode_kernel(
         cp_async_mbar_arrive_noinc(&sm.full[st]);
       }
       cp_async_wait_all();
-    } else if (lane == 0) {
-      prefetch_tensormap(&kv_map);
+    } else {
+      // The cache rows of 32 tiles at a time are looked up by the warp's
+      // lanes together (one block-table load each), so no global load sits
+      // between a stage's release and its next TMA.
+      if (lane == 0) prefetch_tensormap(&kv_map);
+      int my_row = 0;
       for (int i = 0; i < n_tiles; ++i) {
         const int st = i % kStages;
-        if (i >= kStages && !mbar_wait_bounded(&sm.empty[st], ((i / kStages) - 1) & 1)) {
-          atomicExch(status, kStatusWaitTimeout);
+        if ((i & 31) == 0) {
+          const int ti = i + lane;
+          if (ti < n_tiles) {
+            const int t0 = (tile_begin + ti) * kTile;
+            my_row = block_table[(size_t)b * max_blocks + t0 / block_size] * block_size + (t0 % block_size);
+          }
+        }
+        const int row = __shfl_sync(0xffffffffu, my_row, i & 31);
+        int ok = 1;
+        if (lane == 0 && i >= kStages) ok = mbar_wait_bounded(&sm.empty[st], ((i / kStages) - 1) & 1);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {  // the whole warp leaves together
+          if (lane == 0) atomicExch(status, kStatusWaitTimeout);
           break;
         }
-        const int t0 = (tile_begin + i) * kTile;
-        const int blk = block_table[(size_t)b * max_blocks + t0 / block_size];
-        const int row = blk * block_size + (t0 % block_size);
-        mbar_expect_tx(&sm.full[st], kTileBytes);
+        if (lane == 0) {
+          mbar_expect_tx(&sm.full[st], kTileBytes);
 #pragma unroll
-        for (int bx = 0; bx < kBoxes; ++bx)
-          tma_load_2d(sm.kv[st] + bx * kBoxBytes, &kv_map, &sm.full[st], bx * kBoxCols, row);
+          for (int bx = 0; bx < kBoxes; ++bx)
+            tma_load_2d(sm.kv[st] + bx * kBoxBytes, &kv_map, &sm.full[st], bx * kBoxCols, row);
+        }
       }
     }
     return;

@@ -110,9 +110,10 @@ def _paged_cache(B, lens, width, bs=64, dtype=torch.bfloat16, extra_blocks=3):
     return cache, table.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV)
 
 
-@pytest.mark.parametrize("heads", [16, 32])
+@pytest.mark.parametrize("heads", [16, 32, 128])
 @pytest.mark.parametrize("splits", [1, 0, 3])
 def test_mla_decode(heads, splits):
+    """MLA decode (tcgen05 kernel: 16 heads per CTA, 32 from 64 heads up) vs fp32."""
     torch.manual_seed(heads + splits)
     lens = [1, 31, 32, 33, 64, 200, 1029]
     B = len(lens)
@@ -450,3 +451,39 @@ def test_mla_cache_write_rotates_query():
     assert torch.equal(q[..., :128], nope_before)
     flat = cache.view(-1, L + R)[slots]
     _close(flat[:, L:], ref.apply_rope(kv_a[:, None, L:].float(), pos, cs, interleaved=True)[:, 0], 3e-2, 2e-2)
+
+
+@pytest.mark.parametrize("shape", ["32,2", "32,4", "64,2"])
+def test_mla_decode_tc_shapes_16_heads(shape):
+    """The tcgen05 MLA kernel's 16-heads-per-CTA shapes (selected only through
+    AFD_MLA_TC_SHAPE, read once per process, hence the child process) vs fp32."""
+    import os
+    import subprocess
+    import sys
+
+    code = (
+        "import math, torch\n"
+        "from afd_plugin_b200 import ops\n"
+        "from afd_plugin_b200.ops import reference as ref\n"
+        "torch.manual_seed(0)\n"
+        "lens=[1,33,64,200,1029]\n"
+        "bs=64\n"
+        "nb=[math.ceil(n/bs) for n in lens]\n"
+        "cache=torch.randn(sum(nb)+2,bs,576,device='cuda',dtype=torch.bfloat16)\n"
+        "table=torch.zeros(len(lens),max(nb),dtype=torch.int32)\n"
+        "o=1\n"
+        "for b,k in enumerate(nb):\n"
+        "    table[b,:k]=torch.arange(o,o+k,dtype=torch.int32); o+=k\n"
+        "table=table.cuda(); seq=torch.tensor(lens,dtype=torch.int32,device='cuda')\n"
+        "for heads in (16, 32):\n"
+        "    for splits in (1, 0, 3):\n"
+        "        q=torch.randn(len(lens),heads,576,device='cuda',dtype=torch.bfloat16)\n"
+        "        out=ops.mla_decode(q,cache,table,seq,0.07,512,num_splits=splits).float()\n"
+        "        exp=ref.mla_decode(q.float(),cache.float(),table,seq,0.07,512)\n"
+        "        err=((out-exp).abs().max()/(exp.abs().max()+1e-6)).item()\n"
+        "        assert err < 2e-2, (heads, splits, err)\n"
+        "print('ok')\n"
+    )
+    env = dict(os.environ, AFD_MLA_TC_SHAPE=shape)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
