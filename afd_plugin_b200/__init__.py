@@ -75,10 +75,13 @@ def _force_spawn_multiprocessing_if_requested() -> None:
 def register_afd() -> dict[str, str]:
     """Plugin hook (``vllm.general_plugins: afd = afd_plugin_b200:register_afd``).
 
-    Registers every ``AFD<Arch>`` alias in this package's model registry and,
-    when vLLM is importable, in vLLM's ``ModelRegistry`` as a lazy
-    ``module:Class`` string pointing at the standalone wrappers.  Idempotent;
-    returns the alias map.
+    Registers every ``AFD<Arch>`` alias in this package's model registry; the
+    models run on this package's own engine (``LLMEngine``, the Attention /
+    FFN workers, ``python -m afd_plugin_b200.serving``), not inside a vLLM
+    worker.  vLLM cannot instantiate these standalone modules, so its
+    ``ModelRegistry`` receives the aliases (as lazy ``module:Class`` strings)
+    only when ``AFD_PUBLISH_VLLM_ALIASES=1`` asks for it, e.g. for tooling that
+    resolves architecture names.  Idempotent; returns the alias map.
     """
     global _REGISTERED
     _force_spawn_multiprocessing_if_requested()
@@ -88,7 +91,10 @@ def register_afd() -> dict[str, str]:
 
     for arch, alias in MODEL_ALIASES.items():
         MODEL_REGISTRY.setdefault(alias, MODEL_REGISTRY[arch])
-    try:  # optional: publish into vLLM when present
+    if os.environ.get("AFD_PUBLISH_VLLM_ALIASES", "").lower() not in ("1", "true", "yes", "on"):
+        _REGISTERED = True
+        return dict(MODEL_ALIASES)
+    try:  # opt-in: publish the names into vLLM when present
         from vllm import ModelRegistry  # type: ignore
 
         supported = set(ModelRegistry.get_supported_archs())

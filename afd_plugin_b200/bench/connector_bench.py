@@ -53,6 +53,8 @@ def _args(argv=None):
     ap.add_argument("--out", default="")
     ap.add_argument("--fp8", action="store_true", help="rows travel as e4m3 with 1x128 scales (fused path)")
     ap.add_argument("--eager", action="store_true", help="time plain launches instead of a CUDA graph replay")
+    ap.add_argument("--wait-timeout-ms", type=int, default=2000,
+                    help="bound of every in-kernel wait of the fused path (a missed flag ends the wait with an error)")
     ap.add_argument("--breakdown", action="store_true",
                     help="time each kernel of single round trips (barrier between trips)")
     return ap.parse_args(argv)
@@ -117,7 +119,7 @@ def bench_fused(args, rank: int, tokens: list[int]) -> list[dict]:
         "role": role, "connector": "B200FusedAFDConnector", "num_attention_ranks": A, "num_ffn_ranks": F,
         "connector_extra_config": {"max_tokens_per_rank": t_cap, "expert_capacity_factor": 4.0,
                                    "fp8_dispatch": bool(args.fp8),
-                                   "wait_timeout_ms": 20000}})
+                                   "wait_timeout_ms": args.wait_timeout_ms}})
     ec = EngineConfig(ModelConfig(arch, dtype=torch.bfloat16), additional_config={"afd": {}}, max_num_seqs=t_cap)
     conn = B200FusedAFDConnector(rank, rank, ec, afd, role_rank)
     conn.init_afd_connector()

@@ -76,7 +76,16 @@ class _FakeRegistry:
         self.registered[name] = target
 
 
+def test_vllm_registry_untouched_by_default(monkeypatch, fresh_registration):
+    reg = _FakeRegistry(["DeepseekV2ForCausalLM"])
+    monkeypatch.setitem(sys.modules, "vllm", types.SimpleNamespace(ModelRegistry=reg))
+    monkeypatch.delenv("AFD_PUBLISH_VLLM_ALIASES", raising=False)
+    assert pkg.register_afd() == pkg.MODEL_ALIASES
+    assert reg.registered == {}
+
+
 def test_register_publishes_lazy_targets_into_vllm(monkeypatch, fresh_registration):
+    monkeypatch.setenv("AFD_PUBLISH_VLLM_ALIASES", "1")
     reg = _FakeRegistry(["DeepseekV2ForCausalLM", "AFDQwen3MoeForCausalLM"])
     monkeypatch.setitem(sys.modules, "vllm", types.SimpleNamespace(ModelRegistry=reg))
     pkg.register_afd()
@@ -95,6 +104,8 @@ def test_register_publishes_lazy_targets_into_vllm(monkeypatch, fresh_registrati
 
 
 def test_registry_failure_is_not_fatal(monkeypatch, fresh_registration):
+    monkeypatch.setenv("AFD_PUBLISH_VLLM_ALIASES", "1")
+
     class Broken:
         def get_supported_archs(self):
             raise RuntimeError("registry unavailable")
