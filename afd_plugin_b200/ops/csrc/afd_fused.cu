@@ -379,7 +379,47 @@ __global__ void __launch_bounds__(kRouterThreads, 1) dispatch_router_kernel(Disp
   float acc[NT][4];
 #pragma unroll
   for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-  const int ksteps = p.H / 16;
+  if (p.H % 64 == 0) {
+    // 64-column chunks, split over the warps.  K is permuted inside a chunk
+    // (the same way for both operands, so the dot products are unchanged):
+    // lane q = lane % 4 owns columns [16q, 16q + 16) and reads them with two
+    // 16-byte loads per row; MMA step j takes its pairs 16q + 4j + {0,1} and
+    // + {2,3}.  A quad of lanes reads 128 contiguous bytes of each row.
+    const int q = lane & 3;
+    const bf16* hr0 = h + (size_t)(t0 + (ok0 ? g : 0)) * p.H + 16 * q;
+    const bf16* hr1 = h + (size_t)(t0 + (ok1 ? g + 8 : 0)) * p.H + 16 * q;
+    const bf16* gr[NT];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) gr[n] = gate + (size_t)(okE[n] ? e0 + n * 8 + g : 0) * p.H + 16 * q;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    const int kchunks = p.H / 64;
+#pragma unroll(NT >= 4 ? 1 : 2)
+    for (int kc = warp; kc < kchunks; kc += kRouterWarps) {
+      const int k = kc * 64;
+      uint4 a0[2], a1[2], bv[NT][2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        a0[hh] = ok0 ? __ldg(reinterpret_cast<const uint4*>(hr0 + k + 8 * hh)) : z;
+        a1[hh] = ok1 ? __ldg(reinterpret_cast<const uint4*>(hr1 + k + 8 * hh)) : z;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) bv[n][hh] = okE[n] ? __ldg(reinterpret_cast<const uint4*>(gr[n] + k + 8 * hh)) : z;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int hh = j >> 1;
+        const bool hi = j & 1;  // words 0,1 or 2,3 of the 16-byte vector
+        uint32_t a[4];
+        a[0] = hi ? a0[hh].z : a0[hh].x;
+        a[1] = hi ? a1[hh].z : a1[hh].x;
+        a[2] = hi ? a0[hh].w : a0[hh].y;
+        a[3] = hi ? a1[hh].w : a1[hh].y;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+          mma_bf16_16816(acc[n], a, hi ? bv[n][hh].z : bv[n][hh].x, hi ? bv[n][hh].w : bv[n][hh].y);
+      }
+    }
+  }
+  const int ksteps = p.H % 64 == 0 ? 0 : p.H / 16;
 #pragma unroll 4
   for (int ks = warp; ks < ksteps; ks += kRouterWarps) {
     const int k = ks * 16;

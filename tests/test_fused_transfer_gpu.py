@@ -239,3 +239,34 @@ def test_dispatch_fp8_rows_then_expand():
         m = meta[le * cap : le * cap + n].long()
         tt = (m >> 8) & 0xFFFF
         torch.testing.assert_close(xs[le * cap : le * cap + n].float(), deq[tt], atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("H,E,k,T", [(7168, 256, 8, 1), (7168, 256, 8, 64), (7168, 256, 8, 300), (2048, 64, 6, 129),
+                                     (272, 64, 6, 40)])
+def test_dispatch_router_shapes(H, E, k, T):
+    """Router logits + top-k of the dispatch at DeepSeek-V3 / V2-Lite widths
+    (the 64-column vector path, every expert-tile width) and at a width that is
+    not a multiple of 64 (the 16-column path): ids and weights match the fp32
+    top-k of the kernel's own normalised rows."""
+    torch.manual_seed(H + T)
+    F, t_cap = 4, max(T, 16)
+    lb = _Loopback(F, t_cap, H, E, k)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    res = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    norm_w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    gate = (torch.randn(E, H, device=DEV) / H**0.5).to(torch.bfloat16)
+    _dispatch(lb, x, res, norm_w, gate, None, 1.0, 0, 1, 1, 1)
+    torch.cuda.synchronize()
+    h_k = lb.tok[0][0, :T]
+    logits = h_k.float() @ gate.float().t()
+    w_ref, id_ref = ref.topk_route(logits, k, scoring="softmax", renormalize=True)
+    ids = lb.rid[0][0, :T].long()
+    srt, order = ids.sort(dim=-1)
+    rsrt, rorder = id_ref.long().sort(dim=-1)
+    # near-ties between the k-th and (k+1)-th logit may order differently under
+    # a different summation order; everything else must agree
+    agree = (srt == rsrt).all(-1).float().mean().item()
+    assert agree >= 0.98, agree
+    same = (srt == rsrt).all(-1)
+    torch.testing.assert_close(lb.rwt[0][0, :T].gather(1, order)[same], w_ref.gather(1, rorder)[same],
+                               atol=2e-3, rtol=1e-2)
