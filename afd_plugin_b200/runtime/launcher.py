@@ -44,6 +44,8 @@ class LocalAFDSpec:
     tp: int = 1
     # HF checkpoint directory: architecture from its config.json, role-filtered weights
     checkpoint: str | None = None
+    # Attention ranks return the logits of their first N engine steps (fp32, CPU)
+    record_logits_steps: int = 0
 
 
 def free_port() -> int:
@@ -123,6 +125,7 @@ def _rank_main(world_rank: int, world_size: int, rendezvous: str, spec: LocalAFD
                 w.engine.capture_graphs()
             group = w.groups.attention_group
             step = 0
+            logits = []
             while True:
                 flag = torch.tensor([int(w.engine.has_unfinished())])
                 if A > 1:
@@ -134,12 +137,16 @@ def _rank_main(world_rank: int, world_size: int, rendezvous: str, spec: LocalAFD
                         raise RuntimeError("injected fault")
                     os._exit(3)
                 w.engine.step()
+                if step < spec.record_logits_steps and w.engine.runner.last_logits is not None:
+                    # numpy pickles by value (a tensor would travel as a shared-memory handle
+                    # that dies with this process)
+                    logits.append(w.engine.runner.last_logits[: len(ids)].float().cpu().numpy())
                 step += 1
             outs = [w.engine.finished[i].output for i in ids] if role_rank % spec.tp == 0 else []
             if A > 1:
                 dist.barrier(group=group)
             w.shutdown()
-            results.put((world_rank, {"role": role, "outputs": outs, "steps": step}))
+            results.put((world_rank, {"role": role, "outputs": outs, "steps": step, "logits": logits}))
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as exc:  # noqa: BLE001 - reported to the parent

@@ -43,6 +43,28 @@ def test_config1_1a1f_matches_colocated():
     assert res[0]["role"] == "ffn" and res[0]["steps"] == res[1]["steps"]
 
 
+def test_config1_1a1f_logits_match_colocated():
+    """The Attention rank's logits of the prefill and first decode step equal the
+    colocated model's (fp32, same ops on both sides)."""
+    prompts = _prompts()
+    arch = get_preset("tiny-dsv2")
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=128), max_num_seqs=8)
+    eng = LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, device="cpu", seed=0,
+                                    max_positions=128))
+    for p in prompts:
+        eng.add_request(p, 4)
+    ref = []
+    for _ in range(2):
+        eng.step()
+        ref.append(eng.runner.last_logits[: len(prompts)].float())
+    _, res = _run("tiny-dsv2", {"num_attention_ranks": 1, "num_ffn_ranks": 1}, prompts, max_tokens=4,
+                  record_logits_steps=2)
+    got = [torch.from_numpy(a) for a in res[1]["logits"]]
+    assert len(got) == 2
+    for g, r in zip(got, ref):
+        torch.testing.assert_close(g, r, atol=1e-5, rtol=1e-5)
+
+
 @pytest.mark.parametrize("A,F,gate", [(2, 1, False), (2, 2, False), (2, 1, True)])
 def test_topologies_match_colocated(A, F, gate):
     prompts = _prompts(n=5)
