@@ -29,6 +29,8 @@ SHAPES = {
     "dsv2-lite-colo": (64, 2048, 1408, 24, 2, 256),
     "qwen3-30b-f4": (32, 2048, 768, 32),      # Qwen3-30B-A3B, 4A4F: 512 tokens x top-8 over 128 experts
     "dsv3-f4": (64, 7168, 2048, 16),          # DeepSeek-V3 shapes, 4A4F: 512 tokens x top-8 over 256 experts
+    "dsv3-e8": (8, 7168, 2048, 16),           # the same experts, 8 of them (profiling-sized, still > L2)
+    "dsv3-e24": (24, 7168, 2048, 16),         # 24 of them: about five waves of (expert, tile) items
 }
 
 

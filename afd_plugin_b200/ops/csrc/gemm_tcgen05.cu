@@ -516,10 +516,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
 
 // ===================================================================== fp8 weights
 // Block-scaled fp8 (e4m3) weights with bf16 activations ("W8A16"): TMA streams
-// 128-row x 128-K fp8 weight tiles (half the HBM bytes of bf16), four
+// 128-row x 128-K fp8 weight tiles (half the HBM bytes of bf16), twelve
 // converter warps dequantise each tile with its 128 x 128 block scale into two
 // 128B-swizzled bf16 tiles in shared memory, and the tcgen05 MMA reads those.
-// Warp roles: 0 TMA producer, 1 TMEM + MMA issuer, 2-5 epilogue, 6-13 converter.
+// Warp roles: 0 TMA producer, 1 TMEM + MMA issuer, 2-5 epilogue, 6-17 converter.
 // Decode gives a few tokens per expert, so a pass takes 64 tokens and the
 // shared memory goes to pipeline depth (4 TMA stages) and to the converted ring.
 namespace gg8 {
@@ -530,7 +530,7 @@ constexpr int kSub = 64;
 constexpr int kMaxSub = 1;                     // tokens per pass <= 64
 constexpr int kStages = 4;
 constexpr int kCvt = 2;
-constexpr int kCvtWarps = 8;
+constexpr int kCvtWarps = 12;
 constexpr int kCvtThreads = kCvtWarps * 32;
 constexpr int kThreads = (6 + kCvtWarps) * 32;
 constexpr int kWBytes = kBM * kBK;             // 16 KB fp8
@@ -554,20 +554,31 @@ struct Smem {
   uint32_t tmem_base;
 };
 
+// Two fp32 products in one packed multiply (sm_100 mul.f32x2).
+AFD_DEVICE float2 mul_f32x2(float2 a, float s) {
+  uint64_t x = ((uint64_t)__float_as_uint(a.y) << 32) | __float_as_uint(a.x);
+  const uint64_t ss = ((uint64_t)__float_as_uint(s) << 32) | __float_as_uint(s);
+  uint64_t y;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(y) : "l"(x), "l"(ss));
+  return make_float2(__uint_as_float((uint32_t)y), __uint_as_float((uint32_t)(y >> 32)));
+}
+
 AFD_DEVICE uint4 cvt16(uint4 raw, float scale, uint4& hi) {
   // 16 e4m3 values -> 16 bf16 (scaled); returns the first 8, `hi` the last 8.
+  // Per pair: e4m3x2 -> f16x2 (exact), f16 -> f32 (exact), one packed fp32
+  // multiply by the block scale, one rounding to bf16x2.
   const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
   uint32_t out[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((in[i] >> (16 * h)) & 0xFFFFu);
+      const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)(h ? (in[i] >> 16) : (in[i] & 0xFFFFu));
       const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
       __half2 h2;
       *reinterpret_cast<__half2_raw*>(&h2) = hr;
-      const float2 f = __half22float2(h2);
-      out[i * 2 + h] = pack_bf16(f.x * scale, f.y * scale);
+      const float2 f = mul_f32x2(__half22float2(h2), scale);
+      out[i * 2 + h] = pack_bf16(f.x, f.y);
     }
   }
   hi = make_uint4(out[4], out[5], out[6], out[7]);
@@ -674,16 +685,19 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
       const float* sc_hi = w_scale + ((size_t)ew * nblk_n + r1 / 128) * kb_total;
       const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
       for (int p = 0; p < n_pass && ok; ++p) {
+        // the block scales of the next K block load while this one converts
+        float s_lo = sc_lo[0], s_hi = sc_hi[0];
         for (int kb = 0; kb < kb_total; ++kb, ++it_count) {
           const int st = it_count % kStages;
           const int cs = it_count % kCvt;
+          const int kn = kb + 1 < kb_total ? kb + 1 : kb;
+          const float s_lo_next = sc_lo[kn], s_hi_next = sc_hi[kn];
           if (!mbar_wait_bounded(&sm.full[st], (it_count / kStages) & 1) ||
               !mbar_wait_bounded(&sm.cempty[cs], ((it_count / kCvt) & 1) ^ 1)) {
             atomicExch(status, kStatusWaitTimeout);
             ok = false;
             break;
           }
-          const float s_lo = sc_lo[kb], s_hi = sc_hi[kb];
           const uint8_t* src = sm.w[st];
           uint8_t* dst = sm.wc[cs];
 #pragma unroll
@@ -693,10 +707,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
             uint4 hi;
             const uint4 lo = cvt16(raw, r < 64 ? s_lo : s_hi, hi);
             uint8_t* tile = dst + (c >> 2) * kWcHalf + r * 128;
+            // Chunks 0-3 of a source row go to the first K half, 4-7 to the
+            // second (16 KB apart, the same banks): the second half stores its
+            // odd chunk first, so each store instruction writes eight distinct
+            // 16-byte bank groups per row.
             const int d0 = (c & 3) * 2;
-            *reinterpret_cast<uint4*>(tile + ((d0 ^ (r & 7)) << 4)) = lo;
-            *reinterpret_cast<uint4*>(tile + (((d0 + 1) ^ (r & 7)) << 4)) = hi;
+            const bool h1 = c >= 4;
+            *reinterpret_cast<uint4*>(tile + (((h1 ? d0 + 1 : d0) ^ (r & 7)) << 4)) = h1 ? hi : lo;
+            *reinterpret_cast<uint4*>(tile + (((h1 ? d0 : d0 + 1) ^ (r & 7)) << 4)) = h1 ? lo : hi;
           }
+          s_lo = s_lo_next;
+          s_hi = s_hi_next;
           fence_proxy_async();
           mbar_arrive(&sm.cfull[cs]);
         }
@@ -711,8 +732,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
       while (ok && gg::next_item(idx, n_items, n_tiles, counts, offsets, it)) {
         const int n_pass = (it.cnt + kPassRows - 1) / kPassRows;
         for (int p = 0; p < n_pass && ok; ++p, ++acc_count) {
-          const int n_sub = min(kMaxSub, (it.cnt - p * kPassRows + kSub - 1) / kSub);
-          const uint32_t idesc = gg::make_idesc(kBM, n_sub * kSub);
+          // N = this pass's tokens rounded up to 16 (the MMA reads the first
+          // N rows of the 64-row activation tile)
+          const int n_tok = min(kPassRows, it.cnt - p * kPassRows);
+          const uint32_t idesc = gg::make_idesc(kBM, (n_tok + 15) / 16 * 16);
           const int ab = acc_count & 1;
           if (!mbar_wait_bounded(&sm.acc_empty[ab], ((acc_count >> 1) & 1) ^ 1)) {
             atomicExch(status, kStatusWaitTimeout);

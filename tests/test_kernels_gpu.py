@@ -188,10 +188,11 @@ def _quant_experts(w):
     return q, s.contiguous(), deq
 
 
-@pytest.mark.parametrize("counts_list", [[3, 0, 130, 64], [1, 1, 1, 1, 1, 1, 1, 1], [200]])
+@pytest.mark.parametrize("counts_list", [[3, 0, 130, 64], [1, 1, 1, 1, 1, 1, 1, 1], [200], [16, 17, 33, 5]])
 @pytest.mark.parametrize("epilogue", [0, 1])
 def test_grouped_gemm_w8_matches_dequantised_reference(counts_list, epilogue):
-    """fp8 block-scaled weights (tiles dequantised in shared memory) vs fp32 math on the dequantised weights."""
+    """fp8 block-scaled weights (tiles dequantised in shared memory) vs fp32 math on the
+    dequantised weights (segments of 1-200 tokens: N rounded to 16, several passes)."""
     torch.manual_seed(len(counts_list) * 10 + epilogue)
     C = _ext.ops()
     E, K, N = len(counts_list), 512, 384 if epilogue == 0 else 512
