@@ -76,6 +76,8 @@ class TPInfo:
     rank: int = 0
     size: int = 1
     group: object | None = None
+    # a peer-memory all-reduce over ``group`` (``parallel/tp_allreduce.py``); NCCL when absent
+    peer_ar: object | None = None
 
     def shard(self, n: int, what: str) -> tuple[int, int]:
         """(first index, count) of this rank's share of ``n`` items."""
@@ -86,6 +88,8 @@ class TPInfo:
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.size > 1:
+            if self.peer_ar is not None and x.is_cuda:
+                return self.peer_ar(x)
             import torch.distributed as dist
 
             dist.all_reduce(x, group=self.group)

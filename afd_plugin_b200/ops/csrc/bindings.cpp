@@ -131,6 +131,22 @@ at::Tensor argmax_rows(const at::Tensor& x) {
   return out;
 }
 
+// out (fp32, at least copies * span entries): out[c * span + r] = sigmoid(x[r] . w).
+void gate_sigmoid_rows(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, int64_t copies, int64_t span) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.dim() == 2 &&
+                  x.is_contiguous() && w.is_contiguous() && w.numel() == x.size(1),
+              "gate_sigmoid_rows: x [rows, H] and w [H] bf16, contiguous");
+  check_vec16(x, x.size(1), "x");
+  check_vec16(w, w.numel(), "w");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && span >= x.size(0) &&
+                  out.numel() >= (copies - 1) * span + x.size(0),
+              "gate_sigmoid_rows: out fp32 with copies x span entries");
+  c10::cuda::CUDAGuard g(x.device());
+  launch_gate_sigmoid_rows(x.data_ptr(), w.data_ptr(), (int)x.size(0), (int)x.size(1), out.data_ptr<float>(),
+                           (int)copies, (int)span, stream());
+}
+
 void rope_(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin, bool interleaved) {
   check_cuda(x, "x");
   TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "rope_: x must be [T, H, rot] with contiguous last dim");
@@ -940,6 +956,40 @@ at::Tensor grouped_gemm_w8(const at::Tensor& a, const at::Tensor& w, const at::T
   return d;
 }
 
+// Tensor-parallel all-reduce of x [rows, H] bf16 in place over the symmetric
+// heap (see tp_allreduce.cu); `max_ctas` is the flag table's CTA capacity.
+void tp_allreduce_(at::Tensor& x, const at::Tensor& slot_ptrs, const at::Tensor& flag_ptrs,
+                   const at::Tensor& local_slots, const at::Tensor& local_flags, at::Tensor& epoch, at::Tensor& done,
+                   int64_t rank, int64_t world, int64_t slot_elems, int64_t max_ctas, int64_t timeout_ns) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "tp_allreduce: x [rows, H] bf16");
+  TORCH_CHECK(x.size(1) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "tp_allreduce: 16-byte rows");
+  TORCH_CHECK(x.numel() <= slot_elems, "tp_allreduce: ", x.numel(), " elements exceed the slot size ", slot_elems);
+  TORCH_CHECK(slot_ptrs.numel() == world && flag_ptrs.numel() == world && world >= 1 && world <= 16 && rank < world,
+              "tp_allreduce: pointer tables");
+  TORCH_CHECK(epoch.scalar_type() == at::kLong && done.scalar_type() == at::kInt, "tp_allreduce: epoch int64, done int32");
+  TPAllReduceParams p{};
+  p.x = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  p.rows = (int)x.size(0);
+  p.H = (int)x.size(1);
+  p.rows_per_cta = tp_allreduce_rows_per_cta(p.rows, (int)max_ctas);
+  p.world = (int)world;
+  p.rank = (int)rank;
+  p.slot_elems = slot_elems;
+  p.slot_ptrs = slot_ptrs.data_ptr<int64_t>();
+  p.flag_ptrs = flag_ptrs.data_ptr<int64_t>();
+  p.local_slots = reinterpret_cast<const __nv_bfloat16*>(local_slots.data_ptr());
+  p.local_flags = reinterpret_cast<const uint64_t*>(local_flags.data_ptr());
+  p.epoch = reinterpret_cast<uint64_t*>(epoch.data_ptr());
+  p.done_ctr = reinterpret_cast<unsigned*>(done.data_ptr());
+  p.status = status_ptr(x);
+  p.timeout_ns = timeout_ns;
+  c10::cuda::CUDAGuard g(x.device());
+  const cudaError_t e = launch_tp_allreduce(p, stream());
+  TORCH_CHECK(e == cudaSuccess, "tp_allreduce: launch failed: ", cudaGetErrorString(e));
+}
+
 at::Tensor grouped_gemm_ex(const at::Tensor& a, const at::Tensor& w, const at::Tensor& offsets,
                            const at::Tensor& counts, int64_t epilogue, int64_t w_experts) {
   check_cuda(a, "a");
@@ -1085,6 +1135,9 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("grouped_gemm_w8(Tensor a, Tensor w, Tensor w_scale, Tensor offsets, Tensor counts, int epilogue, "
         "int w_experts) -> Tensor");
   m.def("grouped_gemm_ex(Tensor a, Tensor w, Tensor offsets, Tensor counts, int epilogue, int w_experts) -> Tensor");
+  m.def("gate_sigmoid_rows(Tensor x, Tensor w, Tensor(a!) out, int copies, int span) -> ()");
+  m.def("tp_allreduce_(Tensor(a!) x, Tensor slot_ptrs, Tensor flag_ptrs, Tensor local_slots, Tensor local_flags, "
+        "Tensor(b!) epoch, Tensor(c!) done, int rank, int world, int slot_elems, int max_ctas, int timeout_ns) -> ()");
   m.def("grouped_gemm_grid(int n_items) -> int");
   m.def("moe_ffn(Tensor a, Tensor w13, Tensor w2, Tensor offsets, Tensor counts, Tensor(a!) sync, int rows_hint, "
         "int w_experts=-1, Tensor? meta=None, Tensor? rw=None, Tensor? dst_ptrs=None, Tensor? flag_ptrs=None, "
@@ -1103,6 +1156,8 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("fused_add_rms_norm", &fused_add_rms_norm);
   m.impl("silu_and_mul", &silu_and_mul);
   m.impl("argmax_rows", &argmax_rows);
+  m.impl("gate_sigmoid_rows", &gate_sigmoid_rows);
+  m.impl("tp_allreduce_", &tp_allreduce_);
   m.impl("rope_", &rope_);
   m.impl("topk_route", &topk_route);
   m.impl("mla_cache_write", &mla_cache_write);

@@ -397,6 +397,36 @@ static void argmax_rows_go(const void* x, int64_t ld, int rows, int n, int32_t* 
     argmax_rows_kernel<T, false><<<rows, 512, 0, s>>>(p, ld, n, out);
 }
 
+// ============================================================ gated shared expert
+// out[c * span + r] = sigmoid(x[r] . w) for every copy c < copies: one warp
+// per row, 16-byte loads, fp32 dot product (Qwen3.5's shared-expert gate,
+// written into the routing weights of each shared-expert chunk's rows).
+__global__ void gate_sigmoid_rows_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                        int rows, int H, float* __restrict__ out, int copies, int span) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int VN = Vec16<__nv_bfloat16>::N;
+  const __nv_bfloat16* xr = x + (size_t)row * H;
+  float acc = 0.f;
+  for (int v = lane; v < H / VN; v += 32) {
+    const Vec16<__nv_bfloat16> a = load16(xr + v * VN), b = load16(w + v * VN);
+#pragma unroll
+    for (int i = 0; i < VN; ++i) acc += to_f32(a.v[i]) * to_f32(b.v[i]);
+  }
+  acc = warp_sum(acc);
+  const float g = 1.f / (1.f + expf(-acc));
+  for (int c = lane; c < copies; c += 32) out[(size_t)c * span + row] = g;
+}
+
+void launch_gate_sigmoid_rows(const void* x, const void* w, int rows, int H, float* out, int copies, int span,
+                              cudaStream_t s) {
+  if (rows <= 0) return;
+  const int warps = 4;
+  gate_sigmoid_rows_kernel<<<(rows + warps - 1) / warps, 32 * warps, 0, s>>>(
+      (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rows, H, out, copies, span);
+}
+
 void launch_argmax_rows(const void* x, int64_t ld, int rows, int n, int dtype, int32_t* out, cudaStream_t s) {
   if (rows <= 0) return;
   if (dtype == kBF16)

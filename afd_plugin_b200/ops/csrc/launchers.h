@@ -29,6 +29,9 @@ void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, co
 
 // out[r] = argmax over row r of x [rows, n] (row stride ld elements; lowest index on ties).
 void launch_argmax_rows(const void* x, int64_t ld, int rows, int n, int dtype, int32_t* out, cudaStream_t s);
+// out[c * span + r] = sigmoid(x[r] . w), x [rows, H] bf16 (H % 8 == 0), w [H] bf16, c < copies.
+void launch_gate_sigmoid_rows(const void* x, const void* w, int rows, int H, float* out, int copies, int span,
+                              cudaStream_t s);
 
 void launch_decode_advance(int32_t* input_ids, int64_t* positions, int64_t* slots, int32_t* seq_lens,
                            const int32_t* next_tokens, const int32_t* table, int batch, int table_stride,
@@ -81,6 +84,26 @@ void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t*
                               const int32_t* keep_pos, int num_keep, float* partial_o, float* partial_lse, int* status,
                               int batch, int heads, int L, int block_size, int max_blocks_per_seq, int num_splits,
                               float scale, cudaStream_t s, int* arrivals = nullptr);
+
+// ---- tp_allreduce.cu: one-shot all-reduce of x [rows, H] bf16 (in place)
+// over peer memory.  slot_ptrs / flag_ptrs: device int64 arrays of every
+// rank's slots base ([2][world][slot_elems] bf16) and flags base
+// ([max_ctas][world] uint64) in the symmetric heap; local_* are this rank's.
+struct TPAllReduceParams {
+  __nv_bfloat16* x;
+  int rows, H, rows_per_cta, world, rank;
+  int64_t slot_elems;
+  const int64_t* slot_ptrs;
+  const int64_t* flag_ptrs;
+  const __nv_bfloat16* local_slots;
+  const uint64_t* local_flags;
+  uint64_t* epoch;
+  unsigned* done_ctr;
+  int* status;
+  int64_t timeout_ns;
+};
+int tp_allreduce_rows_per_cta(int rows, int max_ctas);
+cudaError_t launch_tp_allreduce(const TPAllReduceParams& p, cudaStream_t s);
 
 // ---- gqa_decode.cu
 // q [B, hq, 128], caches [blocks, bs, hkv, 128], out [B, hq, 128] (bf16).

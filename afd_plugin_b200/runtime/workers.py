@@ -131,7 +131,14 @@ class AFDAttentionWorker(_WorkerBase):
         from afd_plugin_b200.models.layers import TPInfo
 
         mc = engine_config.model_config
-        tp = TPInfo(self.role_rank % self.tp_size, self.tp_size, self.groups.tp_group)
+        self.peer_ar = None
+        if self.tp_size > 1 and self.device.type == "cuda" and mc.dtype == torch.bfloat16:
+            # the row-parallel o_proj's partial sums go over peer memory (NCCL for larger tensors)
+            from afd_plugin_b200.parallel.tp_allreduce import PeerAllReduce
+
+            self.peer_ar = PeerAllReduce(self.groups.tp_group, max_rows=max(256, engine_config.max_num_seqs),
+                                         hidden=mc.arch.hidden_size, device=self.device.index)
+        tp = TPInfo(self.role_rank % self.tp_size, self.tp_size, self.groups.tp_group, self.peer_ar)
         self.model = build_model(
             mc.arch, role="attention", dtype=mc.dtype, device=self.device,
             compute_gate_on_attention=self.afd.compute_gate_on_attention,
@@ -163,6 +170,10 @@ class AFDAttentionWorker(_WorkerBase):
         if callable(stop):
             stop()
         self.connector.close()
+        if self.peer_ar is not None:
+            torch.cuda.synchronize(self.device)
+            self.peer_ar.close()
+            self.peer_ar = None
 
 
 class AFDFFNWorker(_WorkerBase):

@@ -488,3 +488,17 @@ def test_mla_decode_tc_shapes_16_heads(shape):
     env = dict(os.environ, AFD_MLA_TC_SHAPE=shape)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+def test_gate_sigmoid_rows():
+    """Qwen3.5 shared-expert gate: sigmoid(x . w) per row, written into each chunk's routing weights."""
+    torch.manual_seed(4)
+    R, H, copies, span = 37, 2048, 3, 40
+    x = torch.randn(R, H, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(H, device=DEV) * 0.02).to(torch.bfloat16)
+    out = torch.full((copies * span,), -1.0, device=DEV)
+    _ext.ops().gate_sigmoid_rows(x, w, out, copies, span)
+    expect = torch.sigmoid(x.float() @ w.float())
+    for c in range(copies):
+        _close(out[c * span : c * span + R], expect, 1e-4, 1e-4)
+        assert bool((out[c * span + R : (c + 1) * span] == -1.0).all())
