@@ -40,4 +40,10 @@ class PerDeviceOnce {
   std::mutex mutex_;
 };
 
+// L2 eviction hints of the streaming loads (bit 0: grouped GEMM weight
+// tiles, bit 1: MLA decode KV rows).  AFD_L2_HINTS=0 / gemm / mla / all
+// (default all) selects them, for A/B measurements on one machine.
+constexpr int kL2HintGemm = 1, kL2HintMla = 2;
+int l2_hint_mask();
+
 }  // namespace afd

@@ -284,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       int it_count = 0, idx = blockIdx.x;
       PItem it;
       bool ok = true;
+      const uint64_t pol_keep = l2_policy_evict_last(), pol_stream = l2_policy_evict_first();
       while (ok && next_phase_item(idx, g, n0, n_all, it)) {
         const GGPhase& P = g.ph[it.ph];
         const CUtensorMap* wm = it.ph ? &w_map1 : &w_map0;
@@ -316,8 +317,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
               break;
             }
             mbar_expect_tx(&sm.full[st], kWBytes + n_sub * kSubBytes);
-            tma_load_2d(sm.w[st], wm, &sm.full[st], kb * kBK, r0);
-            tma_load_2d(sm.w[st] + kWBytes / 2, wm, &sm.full[st], kb * kBK, r1);
+            // A weight tile read by several passes (a segment wider than a pass,
+            // e.g. a shared-expert chunk that sees every token) stays in L2 for
+            // the next pass; one read once is the first to leave.
+            if (g.l2_hints) {
+              const uint64_t pol = n_pass > 1 ? pol_keep : pol_stream;
+              tma_load_2d_hint(sm.w[st], wm, &sm.full[st], kb * kBK, r0, pol);
+              tma_load_2d_hint(sm.w[st] + kWBytes / 2, wm, &sm.full[st], kb * kBK, r1, pol);
+            } else {
+              tma_load_2d(sm.w[st], wm, &sm.full[st], kb * kBK, r0);
+              tma_load_2d(sm.w[st] + kWBytes / 2, wm, &sm.full[st], kb * kBK, r1);
+            }
             for (int s2 = 0; s2 < n_sub; ++s2) {
               const int arow = it.seg + p * kPassRows + s2 * kSub;
               if (P.a3d)
@@ -590,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap a_map,
     const float* __restrict__ w_scale, __nv_bfloat16* __restrict__ d, const int32_t* __restrict__ offsets,
     const int32_t* __restrict__ counts, int n_w, int w_stride_rows, int k_dim, int ld_d, int n_tiles, int n_experts,
-    int w_experts, int* __restrict__ status, const ScatterParams sp) {
+    int w_experts, int* __restrict__ status, const ScatterParams sp, int l2_hints) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
@@ -646,6 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
       int it_count = 0, idx = blockIdx.x;
       gg::Item it;
       bool ok = true;
+      const uint64_t pol_keep = l2_policy_evict_last(), pol_stream = l2_policy_evict_first();
       while (ok && gg::next_item(idx, n_items, n_tiles, counts, offsets, it)) {
         int r0, r1;
         w_rows(it, r0, r1);
@@ -661,8 +672,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
               break;
             }
             mbar_expect_tx(&sm.full[st], kWBytes + 2 * n_sub * kSubBytes);
-            tma_load_2d(sm.w[st], &w_map, &sm.full[st], kb * kBK, wb + r0);
-            tma_load_2d(sm.w[st] + kWBytes / 2, &w_map, &sm.full[st], kb * kBK, wb + r1);
+            // as in the bf16 kernel: weight tiles of a single pass leave L2 first
+            if (l2_hints) {
+              const uint64_t pol = n_pass > 1 ? pol_keep : pol_stream;
+              tma_load_2d_hint(sm.w[st], &w_map, &sm.full[st], kb * kBK, wb + r0, pol);
+              tma_load_2d_hint(sm.w[st] + kWBytes / 2, &w_map, &sm.full[st], kb * kBK, wb + r1, pol);
+            } else {
+              tma_load_2d(sm.w[st], &w_map, &sm.full[st], kb * kBK, wb + r0);
+              tma_load_2d(sm.w[st] + kWBytes / 2, &w_map, &sm.full[st], kb * kBK, wb + r1);
+            }
             for (int h = 0; h < 2; ++h)
               for (int s2 = 0; s2 < n_sub; ++s2)
                 tma_load_2d(sm.a[st] + h * kAHalf + s2 * kSubBytes, &a_map, &sm.full[st], kb * kBK + h * 64,
@@ -976,6 +994,7 @@ cudaError_t launch_grouped_gemm_phases(const GemmSpec& g0, const GemmSpec* g1, i
   args.status = status;
   args.finish_ctr = finish_ctr;
   args.dep_timeout_ns = 2000000000ll;  // 2 s: phase-0 tiles of an expert are minutes' worth of margin away
+  args.l2_hints = (l2_hint_mask() & kL2HintGemm) ? 1 : 0;
   ScatterParams none{};
   const ScatterParams& spv = sp ? *sp : none;
   int n_items = args.ph[0].n_tiles * args.ph[0].k_splits * args.ph[0].n_experts;
@@ -1027,7 +1046,7 @@ void launch_grouped_gemm_w8(void* d, const void* a, const void* w, const float* 
     const int grid = grouped_gemm_grid(n_tiles * e_local);
     launch_pdl(gg::gg8::grouped_gemm_w8_kernel<EPI>, dim3(grid), dim3(gg::gg8::kThreads), (size_t)smem, s, wmap, amap, w_scale,
                (__nv_bfloat16*)d, expert_offsets, expert_counts, n, w_stride, k, ld, n_tiles, e_local, w_experts,
-               status, spv);
+               status, spv, (l2_hint_mask() & kL2HintGemm) ? 1 : 0);
   };
   if (epilogue == 1) {
     go(std::integral_constant<int, 1>{}, (n / 2) / 64, n / 2);

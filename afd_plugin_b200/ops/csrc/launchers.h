@@ -299,6 +299,7 @@ struct GGArgs {
   int* status;
   unsigned* finish_ctr;    // two-phase launches: CTAs done (zero between launches)
   long long dep_timeout_ns;
+  int l2_hints;            // L2 eviction policies on the weight stream (0 = plain loads)
 };
 // One launch of one or two grouped GEMMs.  With g1, phase 1 reads phase 0's
 // output (its `a` is g0's `d`, same row segments): an MoE layer's gate_up

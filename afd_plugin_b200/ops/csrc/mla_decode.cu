@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 2) mla_decode_kernel(
     const __grid_constant__ CUtensorMap kv_map, const MlaQO qo, const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
     float* __restrict__ part_lse, int* __restrict__ status, int heads, int block_size, int max_blocks,
     int num_splits, float scale_log2, const __nv_bfloat16* __restrict__ cache, const int32_t* __restrict__ keep_pos,
-    int num_keep, int* __restrict__ arrivals) {
+    int num_keep, int* __restrict__ arrivals, int l2_stream) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int b = blockIdx.x;
@@ -223,6 +223,10 @@ __global__ void __launch_bounds__(kThreads, 2) mla_decode_kernel(
       // lanes together (one block-table load each), so no global load sits
       // between a stage's release and its next TMA.
       if (lane == 0) prefetch_tensormap(&kv_map);
+      // With one head group the KV rows are read once per step: they are the
+      // first to leave L2 (weights and activations of the next kernels stay).
+      const bool stream_kv = l2_stream && gridDim.y == 1;
+      const uint64_t pol = l2_policy_evict_first();
       int my_row = 0;
       for (int i = 0; i < n_tiles; ++i) {
         const int st = i % kStages;
@@ -243,8 +247,12 @@ __global__ void __launch_bounds__(kThreads, 2) mla_decode_kernel(
         if (lane == 0) {
           mbar_expect_tx(&sm.full[st], kTileBytes);
 #pragma unroll
-          for (int bx = 0; bx < kBoxes; ++bx)
-            tma_load_2d(sm.kv[st] + bx * kBoxBytes, &kv_map, &sm.full[st], bx * kBoxCols, row);
+          for (int bx = 0; bx < kBoxes; ++bx) {
+            if (stream_kv)
+              tma_load_2d_hint(sm.kv[st] + bx * kBoxBytes, &kv_map, &sm.full[st], bx * kBoxCols, row, pol);
+            else
+              tma_load_2d(sm.kv[st] + bx * kBoxBytes, &kv_map, &sm.full[st], bx * kBoxCols, row);
+          }
         }
       }
     }
@@ -531,7 +539,7 @@ cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t*
   mla::mla_decode_kernel<false><<<grid, mla::kThreads, smem, s>>>(map, qo, block_table, seq_lens, partial_o, partial_lse,
                                                                    status, heads, block_size, max_blocks_per_seq,
                                                                    num_splits, scale_log2, nullptr, nullptr, 0,
-                                                                   arrivals);
+                                                                   arrivals, (l2_hint_mask() & kL2HintMla) ? 1 : 0);
   if (num_splits > 1 && arrivals == nullptr) {
     mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
   }
@@ -551,7 +559,7 @@ void launch_mla_decode_sparse(const MlaQO& qo, const void* cache, const int32_t*
   mla::mla_decode_kernel<true><<<grid, mla::kThreads, smem, s>>>(
       unused, qo, block_table, seq_lens, partial_o, partial_lse, status, heads, block_size, max_blocks_per_seq,
       num_splits, scale_log2, reinterpret_cast<const __nv_bfloat16*>(cache), keep_pos, num_keep,
-      num_splits > 1 && num_splits <= mla::kMergeMaxSplits ? arrivals : nullptr);
+      num_splits > 1 && num_splits <= mla::kMergeMaxSplits ? arrivals : nullptr, 0);
   if (num_splits > 1 && arrivals == nullptr) {
     mla::mla_combine_kernel<<<dim3(batch, heads), 128, 0, s>>>(qo, partial_o, partial_lse, heads, num_splits, L);
   }
