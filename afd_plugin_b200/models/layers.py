@@ -330,6 +330,15 @@ class GQAAttention(nn.Module):
     def forward(self, h: torch.Tensor, meta: AttentionMetadata, kv_cache: tuple[torch.Tensor, torch.Tensor], cos_sin):
         T = h.shape[0]
         qkv = ops.linear(h, self.qkv_proj)
+        k_cache, v_cache = kv_cache
+        if h.is_cuda and cos_sin.shape[-1] == self.d and self.d in (32, 64, 128, 256):
+            # QK-norm, RoPE and the cache write of k / v in one kernel
+            q = ops.gqa_prologue(qkv, self.nq, self.nkv, self.d,
+                                 self.q_norm.weight if self.qk_norm else None,
+                                 self.k_norm.weight if self.qk_norm else None,
+                                 self.q_norm.eps if self.qk_norm else 1e-6,
+                                 meta.positions, cos_sin, k_cache, v_cache, meta.slot_mapping)
+            return self._attend(q, meta, k_cache, v_cache, T)
         q, k, v = qkv.split([self.nq * self.d, self.nkv * self.d, self.nkv * self.d], dim=-1)
         if self.qk_norm:
             q = self.q_norm(q.reshape(T * self.nq, self.d)).view(T, self.nq, self.d)
@@ -340,8 +349,10 @@ class GQAAttention(nn.Module):
         v = v.reshape(T, self.nkv, self.d)
         ops.rope_(q, meta.positions, cos_sin, interleaved=False)
         ops.rope_(k, meta.positions, cos_sin, interleaved=False)
-        k_cache, v_cache = kv_cache
         ops.gqa_cache_write(k_cache, v_cache, k, v, meta.slot_mapping)
+        return self._attend(q, meta, k_cache, v_cache, T)
+
+    def _attend(self, q, meta, k_cache, v_cache, T):
         if meta.is_decode:
             o = ops.gqa_decode(q, k_cache, v_cache, meta.block_table, meta.seq_lens, self.scale)
         else:

@@ -283,6 +283,46 @@ def gqa_cache_write(
     vf[slot_mapping.long()] = v.to(v_cache.dtype)
 
 
+def gqa_prologue(
+    qkv: torch.Tensor,
+    nq: int,
+    nkv: int,
+    head_dim: int,
+    q_norm_w: torch.Tensor | None,
+    k_norm_w: torch.Tensor | None,
+    eps: float,
+    positions: torch.Tensor,
+    cos_sin: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+) -> torch.Tensor:
+    """GQA attention prologue: optional per-head q / k RMSNorm, NeoX RoPE on
+    whole heads, k / v into the paged caches; returns q ``[T, nq, head_dim]``.
+
+    ``qkv [T, (nq + 2 nkv) * head_dim]`` is the fused projection's output.  On
+    a GPU one kernel does all of it (one CTA per token); on CPU the same steps
+    run one by one.
+    """
+    if checks.enabled():
+        checks.cache_slots("gqa_prologue", slot_mapping, num_slots=k_cache.shape[0] * k_cache.shape[1])
+    if _cuda(qkv):
+        return _cuda_ops().gqa_prologue(qkv, nq, nkv, head_dim, q_norm_w, k_norm_w, eps, positions, cos_sin, k_cache,
+                                        v_cache, slot_mapping)
+    T = qkv.shape[0]
+    q, k, v = qkv.split([nq * head_dim, nkv * head_dim, nkv * head_dim], dim=-1)
+    q = q.reshape(T, nq, head_dim)
+    k = k.reshape(T, nkv, head_dim)
+    if q_norm_w is not None:
+        q = ref.rms_norm(q, q_norm_w, eps).to(qkv.dtype)
+    if k_norm_w is not None:
+        k = ref.rms_norm(k, k_norm_w, eps).to(qkv.dtype)
+    q = ref.apply_rope(q, positions, cos_sin, interleaved=False).to(qkv.dtype)
+    k = ref.apply_rope(k, positions, cos_sin, interleaved=False).to(qkv.dtype)
+    gqa_cache_write(k_cache, v_cache, k, v.reshape(T, nkv, head_dim), slot_mapping)
+    return q
+
+
 # -------------------------------------------------------------------- MoE
 def moe_experts(
     x: torch.Tensor,

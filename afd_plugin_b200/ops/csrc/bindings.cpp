@@ -224,6 +224,35 @@ void mla_cache_write(at::Tensor& cache, const at::Tensor& kv_a, const at::Tensor
                          kv_a.stride(0), dtype_code(kv_a), stream(), qp, qh, qst, qsh);
 }
 
+// qkv [T, (nq + 2 nkv) * d] (rows may be strided) -> q [T, nq, d]; k, v into
+// the caches [blocks, bs, nkv, d] at slot_mapping; optional per-head norms.
+at::Tensor gqa_prologue(const at::Tensor& qkv, int64_t nq, int64_t nkv, int64_t d, const c10::optional<at::Tensor>& qw,
+                        const c10::optional<at::Tensor>& kw, double eps, const at::Tensor& positions,
+                        const at::Tensor& cos_sin, at::Tensor& kc, at::Tensor& vc, const at::Tensor& slots) {
+  check_cuda(qkv, "qkv");
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (nq + 2 * nkv) * d, "gqa_prologue: qkv rows");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == d, "gqa_prologue: rope over the whole head");
+  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous() && kc.size(-1) == d && kc.size(-2) == nkv &&
+                  kc.scalar_type() == qkv.scalar_type() && vc.scalar_type() == qkv.scalar_type(),
+              "gqa_prologue: caches [blocks, bs, nkv, d]");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong, "gqa_prologue: int64 meta");
+  auto check_w = [&](const c10::optional<at::Tensor>& w) -> const void* {
+    if (!w.has_value() || !w->defined()) return nullptr;
+    TORCH_CHECK(w->numel() == d && w->is_contiguous() && w->scalar_type() == qkv.scalar_type(), "gqa_prologue: norm w");
+    return w->data_ptr();
+  };
+  const void* qwp = check_w(qw);
+  const void* kwp = check_w(kw);
+  auto q = at::empty({qkv.size(0), nq, d}, qkv.options());
+  c10::cuda::CUDAGuard g(qkv.device());
+  const bool ok = launch_gqa_prologue(qkv.data_ptr(), qkv.stride(0), (int)qkv.size(0), (int)nq, (int)nkv, (int)d, qwp,
+                                      kwp, (float)eps, positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
+                                      q.data_ptr(), kc.data_ptr(), vc.data_ptr(), slots.data_ptr<int64_t>(),
+                                      dtype_code(qkv), stream());
+  TORCH_CHECK(ok, "gqa_prologue: head size ", d, " not supported (32 / 64 / 128 / 256)");
+  return q;
+}
+
 void gqa_cache_write(at::Tensor& kc, at::Tensor& vc, const at::Tensor& k, const at::Tensor& v,
                      const at::Tensor& slots) {
   check_cuda(k, "k");
@@ -1101,6 +1130,8 @@ TORCH_LIBRARY(afd_b200, m) {
   m.def("mla_cache_write(Tensor(a!) cache, Tensor kv_a, Tensor w, float eps, Tensor positions, Tensor cos_sin, "
         "Tensor slots, int L, Tensor(b!)? q_pe=None) -> ()");
   m.def("gqa_cache_write(Tensor(a!) kc, Tensor(b!) vc, Tensor k, Tensor v, Tensor slots) -> ()");
+  m.def("gqa_prologue(Tensor qkv, int nq, int nkv, int d, Tensor? qw, Tensor? kw, float eps, Tensor positions, "
+        "Tensor cos_sin, Tensor(a!) kc, Tensor(b!) vc, Tensor slots) -> Tensor");
   m.def("mla_decode(Tensor q_lat, Tensor q_pe, Tensor cache, Tensor block_table, Tensor seq_lens, float scale, "
         "int num_splits, bool head_major) -> Tensor");
   m.def("mla_decode_sparse(Tensor q, Tensor cache, Tensor block_table, Tensor seq_lens, Tensor keep_pos, float scale, "
@@ -1158,6 +1189,7 @@ TORCH_LIBRARY_IMPL(afd_b200, CUDA, m) {
   m.impl("argmax_rows", &argmax_rows);
   m.impl("gate_sigmoid_rows", &gate_sigmoid_rows);
   m.impl("tp_allreduce_", &tp_allreduce_);
+  m.impl("gqa_prologue", &gqa_prologue);
   m.impl("rope_", &rope_);
   m.impl("topk_route", &topk_route);
   m.impl("mla_cache_write", &mla_cache_write);

@@ -1,6 +1,9 @@
 // Memory-bound kernels: RMSNorm (+fused residual add), SiLU-and-mul, RoPE,
-// routing top-k, KV-cache writes.  Every kernel moves 16-byte vectors and
-// computes in fp32.
+// routing top-k, KV-cache writes (the MLA one with the query's RoPE, the GQA
+// attention prologue with QK-norm and RoPE).  Every kernel computes in fp32.
+#include <algorithm>
+#include <type_traits>
+
 #include "common.cuh"
 #include "device_state.h"
 #include "launchers.h"
@@ -235,6 +238,59 @@ __global__ void gqa_cache_write_kernel(T* __restrict__ kc, T* __restrict__ vc, c
   }
 }
 
+// GQA attention prologue, one CTA per token, one warp per head of the qkv
+// projection row [q heads | k heads | v heads] x D: optional per-head RMSNorm
+// of q and k (Qwen3 QK-norm; rounded to the storage type as the separate
+// norm kernel does), NeoX RoPE on the whole head (pairs c, c + D/2, i.e.
+// lanes l and l ^ 16 with D/32 elements per lane), q into q_out [T, nq, D],
+// k and v into the paged caches at the token's slot.
+template <typename T, int E>
+__global__ void gqa_prologue_kernel(const T* __restrict__ qkv, int64_t qkv_stride, int nq, int nkv,
+                                    const T* __restrict__ qw, const T* __restrict__ kw, float eps,
+                                    const int64_t* __restrict__ pos, const float* __restrict__ cos_sin,
+                                    T* __restrict__ q_out, T* __restrict__ kc, T* __restrict__ vc,
+                                    const int64_t* __restrict__ slots) {
+  constexpr int D = 32 * E, half = D / 2;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x / 32;
+  const T* row = qkv + (size_t)t * qkv_stride;
+  const float* cs = cos_sin + pos[t] * D;
+  const int64_t slot = slots[t];
+  for (int h = warp; h < nq + 2 * nkv; h += nwarps) {
+    const T* src = row + (size_t)h * D + lane * E;
+    float x[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) x[i] = to_f32(src[i]);
+    if (h >= nq + nkv) {  // v head: straight into the cache
+      T* dst = vc + ((size_t)slot * nkv + (h - nq - nkv)) * D + lane * E;
+#pragma unroll
+      for (int i = 0; i < E; ++i) dst[i] = from_f32<T>(x[i]);
+      continue;
+    }
+    const bool is_q = h < nq;
+    const T* nw = is_q ? qw : kw;
+    if (nw != nullptr) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) ss += x[i] * x[i];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+      for (int i = 0; i < E; ++i) x[i] = to_f32(from_f32<T>(x[i] * inv * to_f32(nw[lane * E + i])));
+    }
+    T* dst = is_q ? q_out + ((size_t)t * nq + h) * D + lane * E : kc + ((size_t)slot * nkv + (h - nq)) * D + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[i], 16);
+      const int c = lane * E + i;
+      const int p = c < half ? c : c - half;
+      const float cv = cs[p], sv = cs[half + p];
+      dst[i] = from_f32<T>(c < half ? x[i] * cv - other * sv : x[i] * cv + other * sv);
+    }
+  }
+}
+
 static int grid_for(size_t work, int block) {
   size_t g = (work + block - 1) / block;
   const size_t cap = (size_t)device_sm_count() * 32;
@@ -295,6 +351,37 @@ void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float 
     mla_cache_write_kernel<T><<<tokens, threads, 0, s>>>((T*)cache, (const T*)kv_a, (const T*)w, eps, pos, cos_sin,
                                                          slots, tokens, L, R, kv_stride, (T*)q_pe, q_heads, q_st, q_sh);
   });
+}
+
+template <typename T>
+static void gqa_prologue_typed(const void* qkv, int64_t qkv_stride, int tokens, int nq, int nkv, int e,
+                               const void* qw, const void* kw, float eps, const int64_t* pos, const float* cos_sin,
+                               void* q_out, void* kc, void* vc, const int64_t* slots, cudaStream_t s) {
+  const int threads = 32 * std::min(8, nq + 2 * nkv);
+  auto go = [&](auto ec) {
+    constexpr int E = decltype(ec)::value;
+    gqa_prologue_kernel<T, E><<<tokens, threads, 0, s>>>((const T*)qkv, qkv_stride, nq, nkv, (const T*)qw,
+                                                         (const T*)kw, eps, pos, cos_sin, (T*)q_out, (T*)kc, (T*)vc,
+                                                         slots);
+  };
+  switch (e) {
+    case 1: go(std::integral_constant<int, 1>{}); break;
+    case 2: go(std::integral_constant<int, 2>{}); break;
+    case 4: go(std::integral_constant<int, 4>{}); break;
+    default: go(std::integral_constant<int, 8>{}); break;
+  }
+}
+
+bool launch_gqa_prologue(const void* qkv, int64_t qkv_stride, int tokens, int nq, int nkv, int d, const void* qw,
+                         const void* kw, float eps, const int64_t* pos, const float* cos_sin, void* q_out, void* kc,
+                         void* vc, const int64_t* slots, int dtype, cudaStream_t s) {
+  const int e = d / 32;
+  if (d % 32 != 0 || d > 256 || (e & (e - 1))) return false;
+  if (tokens <= 0) return true;
+  AFD_DTYPE_SWITCH(dtype, T, {
+    gqa_prologue_typed<T>(qkv, qkv_stride, tokens, nq, nkv, e, qw, kw, eps, pos, cos_sin, q_out, kc, vc, slots, s);
+  });
+  return true;
 }
 
 void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, const int64_t* slots, int tokens,

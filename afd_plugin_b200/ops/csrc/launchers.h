@@ -24,6 +24,13 @@ void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float 
                             const float* cos_sin, const int64_t* slots, int tokens, int L, int R, int64_t kv_stride,
                             int dtype, cudaStream_t s, void* q_pe = nullptr, int q_heads = 0, int64_t q_st = 0,
                             int64_t q_sh = 0);
+// GQA prologue (see elementwise.cu): q / k RMSNorm when qw / kw are given,
+// NeoX RoPE on whole heads, q -> q_out [T, nq, d], k / v -> caches [slots,
+// nkv, d].  Returns false (nothing launched) for a head size it does not take
+// (d = 32, 64, 128 or 256).
+bool launch_gqa_prologue(const void* qkv, int64_t qkv_stride, int tokens, int nq, int nkv, int d, const void* qw,
+                         const void* kw, float eps, const int64_t* pos, const float* cos_sin, void* q_out, void* kc,
+                         void* vc, const int64_t* slots, int dtype, cudaStream_t s);
 void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, const int64_t* slots, int tokens,
                             int row_elems, int64_t k_stride, int64_t v_stride, int dtype, cudaStream_t s);
 

@@ -502,3 +502,31 @@ def test_gate_sigmoid_rows():
     for c in range(copies):
         _close(out[c * span : c * span + R], expect, 1e-4, 1e-4)
         assert bool((out[c * span + R : (c + 1) * span] == -1.0).all())
+
+
+@pytest.mark.parametrize("nq,nkv,d,norm", [(32, 4, 128, True), (8, 8, 128, False), (4, 2, 64, True), (6, 2, 32, True)])
+def test_gqa_prologue_matches_unfused(nq, nkv, d, norm):
+    """q / k RMSNorm + NeoX RoPE + k / v cache write in one kernel vs the
+    separate norm, rope and cache-write ops (fp32 reference math)."""
+    torch.manual_seed(nq + d)
+    T, bs = 9, 16
+    qkv_full = torch.randn(T, (nq + 2 * nkv) * d + 8, device=DEV).to(torch.bfloat16)
+    qkv = qkv_full[:, 8:]  # strided rows
+    qw = (1 + 0.1 * torch.randn(d, device=DEV)).to(torch.bfloat16) if norm else None
+    kw = (1 + 0.1 * torch.randn(d, device=DEV)).to(torch.bfloat16) if norm else None
+    cs = ref.rope_cos_sin_cache(d, 512, 10000.0, None, DEV)
+    pos = torch.randint(0, 512, (T,), device=DEV)
+    slots = torch.randperm(4 * bs, device=DEV)[:T]
+    kc = torch.zeros(4, bs, nkv, d, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q = ops.gqa_prologue(qkv, nq, nkv, d, qw, kw, 1e-6, pos, cs, kc, vc, slots)
+    qf, kf, vf = qkv.float().split([nq * d, nkv * d, nkv * d], dim=-1)
+    qf, kf = qf.reshape(T, nq, d), kf.reshape(T, nkv, d)
+    if norm:
+        qf = ref.rms_norm(qf, qw.float(), 1e-6)
+        kf = ref.rms_norm(kf, kw.float(), 1e-6)
+    qf = ref.apply_rope(qf, pos, cs, interleaved=False)
+    kf = ref.apply_rope(kf, pos, cs, interleaved=False)
+    _close(q.float(), qf, 3e-2, 2e-2)
+    _close(kc.view(-1, nkv, d)[slots].float(), kf, 3e-2, 2e-2)
+    assert torch.equal(vc.view(-1, nkv, d)[slots], qkv[:, (nq + nkv) * d :].reshape(T, nkv, d))
