@@ -263,7 +263,9 @@ using namespace afd;
 int gqa_decode_num_splits(int batch, int hkv, int max_seq_len, int num_sms) {
   const int tiles = (max_seq_len + gqa::kTile - 1) / gqa::kTile;
   const int ctas = batch * hkv;
-  int s = (2 * num_sms * 2 + ctas - 1) / ctas;
+  // One wave of the four resident CTAs per SM (shared memory allows four): a
+  // split count that overfills it leaves a nearly empty second wave.
+  int s = (4 * num_sms) / ctas;
   s = s < 1 ? 1 : s;
   const int max_s = tiles / 2 > 0 ? tiles / 2 : 1;
   return s > max_s ? max_s : s;
