@@ -16,6 +16,8 @@ namespace afd {
 template <typename T, int TPR, bool kAddResidual>
 __global__ void rms_norm_kernel(T* __restrict__ out, const T* __restrict__ x, T* __restrict__ residual,
                                 const T* __restrict__ w, int rows, int hidden, float eps) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   constexpr int VN = Vec16<T>::N;
   constexpr int kRowsPerBlock = (TPR >= 256) ? 1 : 256 / TPR;
   const int sub = threadIdx.x / TPR;
@@ -82,8 +84,8 @@ static void rms_norm_dispatch(void* out, const void* x, void* res, const void* w
     constexpr int TPR = decltype(tpr_tag)::value;
     constexpr int RPB = (TPR >= 256) ? 1 : 256 / TPR;
     dim3 grid((rows + RPB - 1) / RPB);
-    rms_norm_kernel<T, TPR, kAdd><<<grid, RPB * TPR, 0, s>>>((T*)out, (const T*)x, (T*)res, (const T*)w, rows,
-                                                             hidden, eps);
+    launch_pdl(rms_norm_kernel<T, TPR, kAdd>, dim3(grid), dim3(RPB * TPR), 0, s, (T*)out, (const T*)x, (T*)res, (const T*)w,
+               rows, hidden, eps);
   };
   if (nvec <= 8) go(std::integral_constant<int, 8>{});
   else if (nvec <= 16) go(std::integral_constant<int, 16>{});
@@ -96,6 +98,8 @@ static void rms_norm_dispatch(void* out, const void* x, void* res, const void* w
 // ============================================================ SiLU * up
 template <typename T>
 __global__ void silu_and_mul_kernel(T* __restrict__ out, const T* __restrict__ in, int rows, int d) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   constexpr int VN = Vec16<T>::N;
   const int nvec = d / VN;
   const size_t total = (size_t)rows * nvec;
@@ -120,6 +124,8 @@ __global__ void silu_and_mul_kernel(T* __restrict__ out, const T* __restrict__ i
 template <typename T>
 __global__ void rope_kernel(T* __restrict__ x, const int64_t* __restrict__ pos, const float* __restrict__ cos_sin,
                             int tokens, int heads, int rot, int64_t st, int64_t sh, bool interleaved) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   const int half = rot / 2;
   const size_t total = (size_t)tokens * heads * half;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -144,6 +150,8 @@ __global__ void topk_route_kernel(const float* __restrict__ logits, const float*
                                   float* __restrict__ out_w, int32_t* __restrict__ out_id, int tokens, int E, int k,
                                   int scoring, bool renorm, int n_group, int topk_group, float scale,
                                   const int32_t* __restrict__ forced) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (warp >= tokens) return;
@@ -172,6 +180,8 @@ __global__ void mla_cache_write_kernel(T* __restrict__ cache, const T* __restric
                                        const int64_t* __restrict__ slots, int tokens, int L, int R,
                                        int64_t kv_stride, T* __restrict__ q_pe, int q_heads, int64_t q_st,
                                        int64_t q_sh) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   const int t = blockIdx.x;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -226,6 +236,8 @@ template <typename T>
 __global__ void gqa_cache_write_kernel(T* __restrict__ kc, T* __restrict__ vc, const T* __restrict__ k,
                                        const T* __restrict__ v, const int64_t* __restrict__ slots, int tokens,
                                        int row_elems, int64_t k_stride, int64_t v_stride) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   constexpr int VN = Vec16<T>::N;
   const int nv = row_elems / VN;
   const size_t total = (size_t)tokens * nv;
@@ -250,6 +262,8 @@ __global__ void gqa_prologue_kernel(const T* __restrict__ qkv, int64_t qkv_strid
                                     const int64_t* __restrict__ pos, const float* __restrict__ cos_sin,
                                     T* __restrict__ q_out, T* __restrict__ kc, T* __restrict__ vc,
                                     const int64_t* __restrict__ slots) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   constexpr int D = 32 * E, half = D / 2;
   const int t = blockIdx.x;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -321,7 +335,7 @@ void launch_fused_add_rms_norm(void* out, const void* x, void* residual, const v
 void launch_silu_and_mul(void* out, const void* in, int rows, int d, int dtype, cudaStream_t s) {
   AFD_DTYPE_SWITCH(dtype, T, {
     const size_t work = (size_t)rows * d / Vec16<T>::N;
-    silu_and_mul_kernel<T><<<grid_for(work, 256), 256, 0, s>>>((T*)out, (const T*)in, rows, d);
+    launch_pdl(silu_and_mul_kernel<T>, dim3(grid_for(work, 256)), dim3(256), 0, s, (T*)out, (const T*)in, rows, d);
   });
 }
 
@@ -329,7 +343,8 @@ void launch_rope(void* x, const int64_t* pos, const float* cos_sin, int tokens, 
                  int64_t sh, bool interleaved, int dtype, cudaStream_t s) {
   AFD_DTYPE_SWITCH(dtype, T, {
     const size_t work = (size_t)tokens * heads * rot / 2;
-    rope_kernel<T><<<grid_for(work, 256), 256, 0, s>>>((T*)x, pos, cos_sin, tokens, heads, rot, st, sh, interleaved);
+    launch_pdl(rope_kernel<T>, dim3(grid_for(work, 256)), dim3(256), 0, s, (T*)x, pos, cos_sin, tokens, heads, rot, st, sh,
+               interleaved);
   });
 }
 
@@ -338,8 +353,8 @@ void launch_topk_route(const float* logits, const float* bias, float* w, int32_t
                        cudaStream_t s) {
   const int warps_per_block = 4;
   dim3 grid((tokens + warps_per_block - 1) / warps_per_block);
-  topk_route_kernel<<<grid, 32 * warps_per_block, 0, s>>>(logits, bias, w, ids, tokens, E, k, scoring, renorm,
-                                                          n_group, topk_group, scale, forced);
+  launch_pdl(topk_route_kernel, dim3(grid), dim3(32 * warps_per_block), 0, s, logits, bias, w, ids, tokens, E, k, scoring,
+             renorm, n_group, topk_group, scale, forced);
 }
 
 void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float eps, const int64_t* pos,
@@ -348,8 +363,8 @@ void launch_mla_cache_write(void* cache, const void* kv_a, const void* w, float 
   if (tokens == 0) return;
   AFD_DTYPE_SWITCH(dtype, T, {
     const int threads = q_pe != nullptr ? 32 * (1 + kQWarps) : 32;
-    mla_cache_write_kernel<T><<<tokens, threads, 0, s>>>((T*)cache, (const T*)kv_a, (const T*)w, eps, pos, cos_sin,
-                                                         slots, tokens, L, R, kv_stride, (T*)q_pe, q_heads, q_st, q_sh);
+    launch_pdl(mla_cache_write_kernel<T>, dim3(tokens), dim3(threads), 0, s, (T*)cache, (const T*)kv_a, (const T*)w, eps, pos,
+               cos_sin, slots, tokens, L, R, kv_stride, (T*)q_pe, q_heads, q_st, q_sh);
   });
 }
 
@@ -360,9 +375,8 @@ static void gqa_prologue_typed(const void* qkv, int64_t qkv_stride, int tokens, 
   const int threads = 32 * std::min(8, nq + 2 * nkv);
   auto go = [&](auto ec) {
     constexpr int E = decltype(ec)::value;
-    gqa_prologue_kernel<T, E><<<tokens, threads, 0, s>>>((const T*)qkv, qkv_stride, nq, nkv, (const T*)qw,
-                                                         (const T*)kw, eps, pos, cos_sin, (T*)q_out, (T*)kc, (T*)vc,
-                                                         slots);
+    launch_pdl(gqa_prologue_kernel<T, E>, dim3(tokens), dim3(threads), 0, s, (const T*)qkv, qkv_stride, nq, nkv, (const T*)qw,
+               (const T*)kw, eps, pos, cos_sin, (T*)q_out, (T*)kc, (T*)vc, slots);
   };
   switch (e) {
     case 1: go(std::integral_constant<int, 1>{}); break;
@@ -388,8 +402,8 @@ void launch_gqa_cache_write(void* kc, void* vc, const void* k, const void* v, co
                             int row_elems, int64_t k_stride, int64_t v_stride, int dtype, cudaStream_t s) {
   AFD_DTYPE_SWITCH(dtype, T, {
     const size_t work = (size_t)tokens * row_elems / Vec16<T>::N;
-    gqa_cache_write_kernel<T><<<grid_for(work, 256), 256, 0, s>>>((T*)kc, (T*)vc, (const T*)k, (const T*)v, slots,
-                                                                 tokens, row_elems, k_stride, v_stride);
+    launch_pdl(gqa_cache_write_kernel<T>, dim3(grid_for(work, 256)), dim3(256), 0, s, (T*)kc, (T*)vc, (const T*)k, (const T*)v,
+               slots, tokens, row_elems, k_stride, v_stride);
   });
 }
 
@@ -417,6 +431,8 @@ __global__ void decode_advance_kernel(int32_t* __restrict__ input_ids, int64_t* 
 template <typename T, bool kVec>
 __global__ void __launch_bounds__(512) argmax_rows_kernel(const T* __restrict__ x, int64_t ld, int n,
                                                          int32_t* __restrict__ out) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   __shared__ float s_v[16];
   __shared__ int s_i[16];
   const T* row = x + (size_t)blockIdx.x * ld;
@@ -479,9 +495,9 @@ static void argmax_rows_go(const void* x, int64_t ld, int rows, int n, int32_t* 
   const T* p = static_cast<const T*>(x);
   const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ld * (int64_t)sizeof(T)) % 16 == 0);
   if (vec)
-    argmax_rows_kernel<T, true><<<rows, 512, 0, s>>>(p, ld, n, out);
+    launch_pdl(argmax_rows_kernel<T, true>, dim3(rows), dim3(512), 0, s, p, ld, n, out);
   else
-    argmax_rows_kernel<T, false><<<rows, 512, 0, s>>>(p, ld, n, out);
+    launch_pdl(argmax_rows_kernel<T, false>, dim3(rows), dim3(512), 0, s, p, ld, n, out);
 }
 
 // ============================================================ gated shared expert
@@ -490,6 +506,8 @@ static void argmax_rows_go(const void* x, int64_t ld, int rows, int n, int32_t* 
 // written into the routing weights of each shared-expert chunk's rows).
 __global__ void gate_sigmoid_rows_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                         int rows, int H, float* __restrict__ out, int copies, int span) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -510,8 +528,8 @@ void launch_gate_sigmoid_rows(const void* x, const void* w, int rows, int H, flo
                               cudaStream_t s) {
   if (rows <= 0) return;
   const int warps = 4;
-  gate_sigmoid_rows_kernel<<<(rows + warps - 1) / warps, 32 * warps, 0, s>>>(
-      (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rows, H, out, copies, span);
+  launch_pdl(gate_sigmoid_rows_kernel, dim3((rows + warps - 1) / warps), dim3(32 * warps), 0, s, (const __nv_bfloat16*)x,
+             (const __nv_bfloat16*)w, rows, H, out, copies, span);
 }
 
 void launch_argmax_rows(const void* x, int64_t ld, int rows, int n, int dtype, int32_t* out, cudaStream_t s) {

@@ -21,6 +21,8 @@ __global__ void moe_align_kernel(const int32_t* __restrict__ ids, int tokens, in
                                  int offset, int32_t* __restrict__ counts_out, int32_t* __restrict__ offsets_out,
                                  int32_t* __restrict__ row_token, int32_t* __restrict__ row_slot,
                                  int32_t* __restrict__ token_slot_row, int* __restrict__ total_rows) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   __shared__ int cnt[kMaxLocalExperts];
   __shared__ int cur[kMaxLocalExperts];
   const int ks = k + n_shared;
@@ -64,6 +66,8 @@ __global__ void moe_align_kernel(const int32_t* __restrict__ ids, int tokens, in
 template <typename T>
 __global__ void moe_gather_kernel(T* __restrict__ xs, const T* __restrict__ x, const int32_t* __restrict__ row_token,
                                   int rows_cap, int hidden, const int* __restrict__ total_rows) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   constexpr int VN = Vec16<T>::N;
   const int nv = hidden / VN;
   const int total = *total_rows;
@@ -82,6 +86,8 @@ template <typename T>
 __global__ void moe_combine_kernel(T* __restrict__ out, const T* __restrict__ ys, const float* __restrict__ w,
                                    const int32_t* __restrict__ tsr, int k, int k_routed, int hidden,
                                    const T* __restrict__ shared) {
+  pdl_wait();  // launched with PDL: nothing global is touched before the predecessor completes
+  pdl_launch_dependents();
   constexpr int VN = Vec16<T>::N;
   const int t = blockIdx.x;
   for (int c = threadIdx.x; c < hidden / VN; c += blockDim.x) {
@@ -122,8 +128,8 @@ using namespace afd;
 void launch_moe_align(const int32_t* topk_ids, int tokens, int k, int n_shared, int e_local, int offset,
                       int32_t* expert_counts, int32_t* expert_offsets, int32_t* row_token, int32_t* row_slot,
                       int32_t* token_slot_row, int* total_rows, cudaStream_t s) {
-  moe_align_kernel<<<1, 1024, 0, s>>>(topk_ids, tokens, k, n_shared, e_local, offset, expert_counts, expert_offsets,
-                                      row_token, row_slot, token_slot_row, total_rows);
+  launch_pdl(moe_align_kernel, dim3(1), dim3(1024), 0, s, topk_ids, tokens, k, n_shared, e_local, offset, expert_counts,
+             expert_offsets, row_token, row_slot, token_slot_row, total_rows);
 }
 
 void launch_moe_gather(void* xs, const void* x, const int32_t* row_token, int rows_cap, int hidden,
@@ -133,7 +139,7 @@ void launch_moe_gather(void* xs, const void* x, const int32_t* row_token, int ro
     int grid = (int)((work + 255) / 256);
     const int cap = device_sm_count() * 16;
     grid = grid > cap ? cap : (grid < 1 ? 1 : grid);
-    moe_gather_kernel<T><<<grid, 256, 0, s>>>((T*)xs, (const T*)x, row_token, rows_cap, hidden, total_rows);
+    launch_pdl(moe_gather_kernel<T>, dim3(grid), dim3(256), 0, s, (T*)xs, (const T*)x, row_token, rows_cap, hidden, total_rows);
   });
 }
 
@@ -141,7 +147,7 @@ void launch_moe_combine(void* out, const void* ys, const float* topk_w, const in
                         int k, int k_routed, int hidden, const void* shared_out, int dtype, cudaStream_t s) {
   AFD_DTYPE_SWITCH(dtype, T, {
     const int threads = hidden / Vec16<T>::N < 256 ? hidden / Vec16<T>::N : 256;
-    moe_combine_kernel<T><<<tokens, threads, 0, s>>>((T*)out, (const T*)ys, topk_w, token_slot_row, k, k_routed,
-                                                     hidden, (const T*)shared_out);
+    launch_pdl(moe_combine_kernel<T>, dim3(tokens), dim3(threads), 0, s, (T*)out, (const T*)ys, topk_w, token_slot_row, k,
+               k_routed, hidden, (const T*)shared_out);
   });
 }
