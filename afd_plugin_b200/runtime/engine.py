@@ -19,6 +19,15 @@ the KV blocks of common prompt prefixes; ``hold_kv`` / ``export_kv`` /
 ``add_prefilled_request`` hand a request's cache rows to another engine
 (``runtime/kv_transfer.py``); ``abort`` ends a request early.
 
+With ``EngineConfig.async_scheduling`` a steady greedy decode (no request
+waiting, on every Attention rank) launches step t+1 before it reads step t's tokens:
+the next input ids are gathered on the device from step t's output, the host
+stages positions and block tables one token ahead, and the bookkeeping of
+step t (appending tokens, ending requests) runs while step t+1 is on the GPU.
+A ``step()`` then returns the previous step's tokens; a request that stopped
+on step t has already been decoded once more on step t+1, and that token is
+dropped.  Any other step first drains the step in flight.
+
 On AFD Attention ranks several engines (one per rank, data parallel) step in
 lockstep: a per-step exchange over the Attention group agrees on eager vs
 graph mode and the padded size, the same agreement vLLM's DP metadata provides
@@ -93,6 +102,25 @@ class Request:
         return "abort" if self.aborted else ("stop" if self.stopped else "length")
 
 
+@dataclass
+class _InFlight:
+    """A launched decode step whose tokens the host has not read yet (async scheduling)."""
+
+    reqs: list[Request]  # the step's rows, in order
+    host: torch.Tensor  # pinned int32 tokens, filled by the step's device->host copy
+    done: torch.cuda.Event  # recorded after that copy
+
+
+class _HostEvent:
+    """Stands in for a CUDA event on a CPU engine, whose copies and steps complete in order on the host."""
+
+    def record(self) -> None:
+        pass
+
+    def synchronize(self) -> None:
+        pass
+
+
 class AttentionCoordinator:
     """Per-step agreement among Attention (DP) ranks; trivial for one rank."""
 
@@ -109,6 +137,15 @@ class AttentionCoordinator:
         dist.all_gather(out, mine, group=self.group)
         self.any_sparse = any(bool(t[2]) for t in out)
         return [(int(t[0]), bool(t[1])) for t in out]
+
+    def agree_pipelined(self, num_tokens: int) -> list[int]:
+        """Async scheduling: every rank's launch size for a pipelined decode step (-1: it cannot)."""
+        if self.group is None or self.size == 1:
+            return [num_tokens]
+        mine = torch.tensor([num_tokens], dtype=torch.int64)
+        out = [torch.empty_like(mine) for _ in range(self.size)]
+        dist.all_gather(out, mine, group=self.group)
+        return [int(t) for t in out]
 
 
 class LLMEngine:
@@ -168,6 +205,19 @@ class LLMEngine:
         self._h_table = mk(self.max_batch, self.max_blocks_per_seq, dt=torch.int32)
         self._h_lens = mk(self.max_batch, dt=torch.int32)
         self._h_next = mk(self.max_batch, dt=torch.int32)
+        # async scheduling: the decode step whose tokens have not been read yet,
+        # a second pinned token buffer (two steps' tokens can be on their way)
+        # and the gather index for survivors of a step that ended requests
+        self.async_scheduling = bool(getattr(engine_config, "async_scheduling", False))
+        self._inflight: _InFlight | None = None
+        self._next_bufs = [self._h_next] + ([mk(self.max_batch, dt=torch.int32)] if self.async_scheduling else [])
+        self._flip = 0
+        self.num_async_steps = 0  # decode steps launched ahead of their predecessor's read-back
+        self._h_idx = mk(self.max_batch, dt=torch.int64)
+        self._d_idx = torch.zeros(self.max_batch, dtype=torch.int64, device=self.device)
+        event = torch.cuda.Event if self.device.type == "cuda" else _HostEvent
+        self._events = [event() for _ in range(2)]
+        self._staged = event()
         self._h_state = mk(self.max_batch, dt=torch.int32)
         # numpy views of the pinned staging tensors: a decode step fills them
         # with a few vectorised writes instead of per-element tensor indexing
@@ -457,7 +507,8 @@ class LLMEngine:
         return n
 
     def has_unfinished(self) -> bool:
-        return bool(self.waiting or self.running or self._kv_waiting or self.prefilling)
+        return bool(self.waiting or self.running or self._kv_waiting or self.prefilling
+                    or self._inflight is not None)
 
     def _ensure_blocks(self, req: Request, upto_tokens: int) -> None:
         need = math.ceil(upto_tokens / self.block_size) - len(req.blocks)
@@ -503,6 +554,11 @@ class LLMEngine:
         self.metrics.close()
 
     def _step(self) -> dict[int, int]:
+        if self.async_scheduling:
+            out = self._step_async()
+            if out is not None:
+                self._last_phase = "decode"
+                return out
         if self._kv_waiting:
             self._admit_prefilled()
             if not (self.waiting or self.running or self.prefilling) and self.coordinator.size == 1:
@@ -661,15 +717,21 @@ class LLMEngine:
         # Ranks that are not prefilling join with one placeholder row.
         return {"tokens_across_attn": {0: tuple(max(1, n) if p else 1 for n, p in votes)}}
 
-    def _stage_decode_inputs(self, reqs: list[Request], run_b: int) -> None:
-        """Fill the pinned staging rows ``[0, run_b)`` for a decode step (padding rows after the requests)."""
+    def _stage_decode_inputs(self, reqs: list[Request], run_b: int, lag: int = 0) -> None:
+        """Fill the pinned staging rows ``[0, run_b)`` for a decode step (padding rows after the requests).
+
+        ``lag`` = 1 stages the position after the one of the step in flight
+        (async scheduling); the input ids then come from that step's output
+        on the device and are not staged.
+        """
         bs = self.block_size
         B = len(reqs)
-        pos = [r.num_tokens - 1 for r in reqs]
+        pos = [r.num_tokens - 1 + lag for r in reqs]
         for r, p in zip(reqs, pos):
             if len(r.blocks) * bs <= p:
                 self._ensure_blocks(r, p + 1)
-        self._n_ids[:B] = [r.output[-1] if r.output else r.prompt[-1] for r in reqs]
+        if not lag:
+            self._n_ids[:B] = [r.output[-1] if r.output else r.prompt[-1] for r in reqs]
         self._n_pos[:B] = pos
         self._n_slot[:B] = [r.blocks[p // bs] * bs + p % bs for r, p in zip(reqs, pos)]
         self._n_lens[:B] = self._n_pos[:B] + 1
@@ -744,6 +806,132 @@ class LLMEngine:
             (self._finish(r) if r.finished else still.append(r))
         self.running = still
         return out
+
+    # ------------------------------------------------------ async scheduling
+    def _step_async(self) -> dict[int, int] | None:
+        """A pipelined decode step, a drain of the step in flight, or None (the step runs synchronously).
+
+        Attention ranks agree first (one exchange of launch sizes): they
+        pipeline only when every rank can, at the largest rank's batch, so
+        their FFN stages line up.
+        """
+        launch = self._pipeline_batch()
+        sizes = self.coordinator.agree_pipelined(-1 if launch is None else len(launch))
+        if min(sizes) > 0:
+            with torch.profiler.record_function("afd_decode_step"):
+                return self._decode_step_async(launch, max(sizes), len(sizes))
+        if self._inflight is not None:
+            return self._drain()
+        return None
+
+    def _pipeline_batch(self) -> list[Request] | None:
+        """The requests the next step decodes if it may launch before the previous step's tokens are
+        read (a greedy decode with no prompt or imported request waiting and enough free KV blocks)."""
+        if (not self.running or self.waiting or self.prefilling or self._kv_waiting
+                or getattr(self.model.arch, "index_topk", 0)):
+            return None
+        for r in self.running:
+            sp = r.sampling
+            if not sp.greedy or sp.logprobs is not None or sp.penalized or sp.min_tokens:
+                return None
+        lag = 0 if self._inflight is None else 1
+        # a request whose token in flight is its last one is not decoded again
+        launch = [r for r in self.running if len(r.output) + 1 < r.max_tokens] if lag else self.running
+        if not launch:
+            return None
+        bs = self.block_size
+        need = 0
+        for r in launch:
+            need += max(0, (r.num_tokens - 1 + lag) // bs + 1 - len(r.blocks))
+        return launch if need <= self.kv.allocator.num_free else None
+
+    def _decode_step_async(self, launch: list[Request], top: int, nranks: int) -> dict[int, int]:
+        """Launch a decode step of ``launch`` (padded to ``top`` rows, the largest Attention rank's batch)
+        from staged positions and the device-resident tokens of the step in flight, then read that step's
+        tokens."""
+        from afd_plugin_b200.runtime.model_runner import ubatch_splits
+
+        prev = self._inflight
+        lag = 0 if prev is None else 1
+        B = len(launch)
+        padded = pad_to_capture_size(top, self.capture_sizes) if self.use_graphs else None
+        use_graph = padded is not None and padded in self.runner.graphs
+        run_b = padded if use_graph else top
+        flags = {}
+        if nranks > 1:
+            sp = ubatch_splits(run_b, self.runner.num_ubatches)
+            flags["tokens_across_attn"] = {s: (sp[s + 1] - sp[s],) * nranks for s in range(len(sp) - 1)}
+        self.runner.sparse_decode = False
+        # the pinned staging rows are rewritten below: the previous step's
+        # host->device copies of them must have run
+        self._staged.synchronize()
+        self._stage_decode_inputs(launch, run_b, lag=lag)
+        b = self.runner.buf
+        h2d = run_b * (8 + 8 + 4 + 4 * self.max_blocks_per_seq)
+        if self.runner.has_linear_state:
+            b.state_slots[:run_b].copy_(self._h_state[:run_b], non_blocking=True)
+            h2d += run_b * 4
+        if not lag:
+            b.input_ids[:run_b].copy_(self._h_ids[:run_b], non_blocking=True)
+            h2d += run_b * 4
+        else:
+            if run_b > B:  # padding rows
+                b.input_ids[B:run_b].copy_(self._h_ids[B:run_b], non_blocking=True)
+                h2d += (run_b - B) * 4
+            if B == len(prev.reqs):  # no request ended: the rows line up
+                b.input_ids[:B].copy_(b.next_tokens[:B])
+            else:
+                row = {id(r): i for i, r in enumerate(prev.reqs)}
+                self._h_idx.numpy()[:B] = [row[id(r)] for r in launch]
+                self._d_idx[:B].copy_(self._h_idx[:B], non_blocking=True)
+                b.input_ids[:B].copy_(b.next_tokens.index_select(0, self._d_idx[:B]))
+                h2d += B * 8
+        b.positions[:run_b].copy_(self._h_pos[:run_b], non_blocking=True)
+        b.slot_mapping[:run_b].copy_(self._h_slot[:run_b], non_blocking=True)
+        b.block_table[:run_b].copy_(self._h_table[:run_b], non_blocking=True)
+        b.seq_lens[:run_b].copy_(self._h_lens[:run_b], non_blocking=True)
+        self._staged.record()
+        self.last_h2d_bytes = h2d
+        from afd_plugin_b200.utils.roofline import kv_bytes_per_step
+
+        self.last_hbm_bytes = self._weight_bytes + kv_bytes_per_step(getattr(self.model, "cache_arch", self.model.arch),
+                                                                      int(self._h_lens[:B].sum()),
+                                                                      elem_bytes=self.model.dtype.itemsize)
+        nxt = self.runner.decode_step(run_b, use_graph=use_graph, **flags)
+        host = self._next_bufs[self._flip]
+        host[:run_b].copy_(nxt, non_blocking=True)
+        done = self._events[self._flip]
+        done.record()
+        self._flip ^= 1
+        self.num_async_steps += 1
+        self.last_d2h_bytes = run_b * 4
+        self._inflight = _InFlight(launch, host, done)
+        return self._consume(prev) if prev is not None else {}
+
+    def _consume(self, fl: _InFlight) -> dict[int, int]:
+        """Read a launched step's tokens and append them; requests that ended before it drop theirs."""
+        fl.done.synchronize()
+        check = getattr(self.ffn, "check_device_status", None)
+        if check is not None:
+            check()
+        out = {}
+        ended = False
+        for r, t in zip(fl.reqs, fl.host.numpy()[: len(fl.reqs)].tolist()):
+            if r.aborted or r.finished:
+                continue
+            r.output.append(t)
+            out[r.req_id] = t
+            if r.finished:
+                self._finish(r)
+                ended = True
+        if ended:
+            self.running = [r for r in self.running if not (r.finished or r.aborted)]
+        return out
+
+    def _drain(self) -> dict[int, int]:
+        """Read the step in flight without launching another (before any step that is not pipelined)."""
+        fl, self._inflight = self._inflight, None
+        return self._consume(fl)
 
     def generate(self, prompts: list[list[int]], max_tokens: int,
                  sampling: SamplingParams | None = None) -> list[list[int]]:

@@ -46,6 +46,8 @@ class LocalAFDSpec:
     checkpoint: str | None = None
     # Attention ranks return the logits of their first N engine steps (fp32, CPU)
     record_logits_steps: int = 0
+    # EngineConfig.async_scheduling on the Attention ranks
+    async_scheduling: bool = False
 
 
 def free_port() -> int:
@@ -74,6 +76,7 @@ def build_engine_config(spec: LocalAFDSpec):
         compilation_config=CompilationConfig(cudagraph_capture_sizes=list(spec.capture_sizes)),
         additional_config={"afd": dict(spec.afd)},
         max_num_seqs=spec.max_num_seqs,
+        async_scheduling=spec.async_scheduling,
     )
 
 
@@ -146,7 +149,8 @@ def _rank_main(world_rank: int, world_size: int, rendezvous: str, spec: LocalAFD
             if A > 1:
                 dist.barrier(group=group)
             w.shutdown()
-            results.put((world_rank, {"role": role, "outputs": outs, "steps": step, "logits": logits}))
+            results.put((world_rank, {"role": role, "outputs": outs, "steps": step, "logits": logits,
+                                      "async_steps": w.engine.num_async_steps}))
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as exc:  # noqa: BLE001 - reported to the parent

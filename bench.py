@@ -73,6 +73,9 @@ def parse_args(argv=None):
                          "so a second ubatch re-reads every expert weight)")
     ap.add_argument("--no-dbo", action="store_true", help="force DBO off")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sync-scheduling", action="store_true",
+                    help="end-to-end loop: read each step's tokens before launching the next (the default "
+                         "launches step t+1 before reading step t back, EngineConfig.async_scheduling)")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the model to this many layers for quick checks; the line is marked invalid")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -114,6 +117,7 @@ def build_config(args, *, num_attn: int, num_ffn: int, role: str | None, connect
         cache_config=CacheConfig(block_size=64),
         additional_config=additional,
         max_num_seqs=per_rank,
+        async_scheduling=not args.sync_scheduling,
     ), per_rank
 
 
@@ -292,6 +296,7 @@ def main(argv=None) -> int:
                 "parallelism": result["parallelism"],
                 "cuda_graphs": not args.eager,
                 "dbo": args.dbo,
+                "e2e_scheduling": "sync" if args.sync_scheduling else "async",
                 "l2": "inputs larger than L2 (31 GB weights, ~10 GB KV per step); no flush",
             },
             "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"),

@@ -189,3 +189,15 @@ def test_afd_from_an_hf_checkpoint(tmp_path):
     for r in sorted(res):
         outs += res[r].get("outputs", [])
     assert outs == ref
+
+
+@pytest.mark.parametrize("A,F,tp", [(1, 1, 1), (2, 1, 1), (2, 2, 1), (2, 1, 2)])
+def test_async_scheduling_matches_colocated(A, F, tp):
+    """Decode steps launched before the previous step's tokens are read (uneven DP shares pad to the
+    largest rank's batch) give the colocated tokens."""
+    prompts = _prompts(n=5, length=12)
+    ref = _colocated("tiny-dsv2", prompts, 7)
+    outs, res = _run("tiny-dsv2", {"num_attention_ranks": A, "num_ffn_ranks": F}, prompts, max_tokens=7, tp=tp,
+                     async_scheduling=True)
+    assert outs == ref
+    assert all(v["async_steps"] >= 4 for v in res.values() if v["role"] == "attention")

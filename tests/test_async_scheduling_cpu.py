@@ -1,0 +1,89 @@
+"""Async scheduling: decode step t+1 launches before step t's tokens are read; outputs equal the sync engine's."""
+
+from __future__ import annotations
+
+import torch
+
+from afd_plugin_b200.engine_config import CacheConfig, EngineConfig, ModelConfig
+from afd_plugin_b200.models import build_model, get_preset
+from afd_plugin_b200.runtime.engine import LLMEngine
+from afd_plugin_b200.runtime.sampling import SamplingParams
+
+
+def _engine(async_scheduling: bool, block_size: int = 4, num_blocks: int | None = None) -> LLMEngine:
+    arch = get_preset("tiny-dsv2")
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96),
+                      cache_config=CacheConfig(block_size=block_size, num_blocks=num_blocks), max_num_seqs=8,
+                      async_scheduling=async_scheduling)
+    return LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=96))
+
+
+PROMPTS = [[3, 9, 4], [7, 1, 2, 8, 5, 6], [11, 12], [5, 5, 5, 5], [2, 30, 17, 9, 1]]
+MAX_TOKENS = [9, 4, 13, 7, 11]
+
+
+def _run(eng: LLMEngine, stop: dict[int, int] | None = None) -> tuple[list[list[int]], int]:
+    ids = []
+    for i, (p, m) in enumerate(zip(PROMPTS, MAX_TOKENS)):
+        sp = SamplingParams(stop_token_ids=[stop[i]]) if stop and i in stop else None
+        ids.append(eng.add_request(p, m, sampling=sp))
+    while eng.has_unfinished():
+        eng.step()
+    return [eng.finished[i].output for i in ids], eng.num_async_steps
+
+
+def test_async_equals_sync_with_lengths_and_stop_tokens():
+    ref, _ = _run(_engine(False))
+    # stop request 0 at its 4th token and request 3 at its 2nd: rows end between steps both ways
+    stop = {0: ref[0][3], 3: ref[3][1]}
+    want, _ = _run(_engine(False), stop)
+    got, pipelined = _run(_engine(True), stop)
+    assert got == want
+    assert pipelined > 5  # most decode steps launched ahead of their predecessor's read-back
+    assert len(want[0]) <= 4 and len(want[3]) <= 2
+
+
+def test_async_step_returns_previous_tokens_and_drains_for_new_work():
+    eng = _engine(True)
+    a = eng.add_request(PROMPTS[0], 12)
+    first = eng.step()  # prefill: synchronous, returns the first token
+    assert list(first) == [a]
+    assert eng.step() == {}  # the first pipelined decode launches; nothing read back yet
+    got = eng.step()  # launches the next step and returns the previous one's token
+    assert list(got) == [a] and eng._inflight is not None
+    b = eng.add_request(PROMPTS[1], 5)
+    drained = eng.step()  # a prompt is waiting: read the step in flight, launch nothing
+    assert list(drained) == [a] and eng._inflight is None
+    while eng.has_unfinished():
+        eng.step()
+    ref = _engine(False)
+    ra = ref.add_request(PROMPTS[0], 12)
+    rb = ref.add_request(PROMPTS[1], 5)
+    while ref.has_unfinished():
+        ref.step()
+    assert eng.finished[a].output == ref.finished[ra].output
+    assert eng.finished[b].output == ref.finished[rb].output
+
+
+def test_async_abort_drops_the_token_in_flight():
+    eng = _engine(True)
+    ids = [eng.add_request(p, m) for p, m in zip(PROMPTS[:3], (10, 10, 10))]
+    eng.step()
+    for _ in range(3):
+        eng.step()
+    n = len(eng.running[1].output)
+    assert eng.abort(ids[1])
+    while eng.has_unfinished():
+        eng.step()
+    assert len(eng.finished[ids[1]].output) == n and eng.finished[ids[1]].aborted
+    assert all(len(eng.finished[i].output) == 10 for i in (ids[0], ids[2]))
+    assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks - 1  # every block back (block 0 pads)
+
+
+def test_async_falls_back_when_blocks_run_short():
+    """With too few free KV blocks for the next positions, the engine drains and the sync path preempts."""
+    ref, eng = _engine(False, block_size=2, num_blocks=16), _engine(True, block_size=2, num_blocks=16)
+    want, _ = _run(ref)
+    got, pipelined = _run(eng)
+    assert got == want
+    assert ref.num_preemptions > 0 and eng.num_preemptions > 0 and pipelined > 0

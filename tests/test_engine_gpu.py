@@ -10,10 +10,12 @@ from afd_plugin_b200.runtime.engine import LLMEngine
 pytestmark = pytest.mark.gpu
 
 
-def _engine(preset, *, eager, sizes=(8,), device="cuda", dtype=torch.bfloat16, max_len=256, seqs=8, init_on=None):
+def _engine(preset, *, eager, sizes=(8,), device="cuda", dtype=torch.bfloat16, max_len=256, seqs=8, init_on=None,
+            async_scheduling=False):
     arch = get_preset(preset)
     ec = EngineConfig(ModelConfig(arch, dtype=dtype, enforce_eager=eager, max_model_len=max_len),
-                      compilation_config=CompilationConfig(cudagraph_capture_sizes=list(sizes)), max_num_seqs=seqs)
+                      compilation_config=CompilationConfig(cudagraph_capture_sizes=list(sizes)), max_num_seqs=seqs,
+                      async_scheduling=async_scheduling)
     m = build_model(arch, role="colocated", dtype=dtype, device=device, seed=0, max_positions=max_len,
                     init_on=init_on)
     return LLMEngine(ec, m)
@@ -33,6 +35,29 @@ def test_graph_decode_matches_eager(preset):
     eng.capture_graphs()
     assert 8 in eng.runner.graphs
     assert eng.generate(prompts, 8) == eager
+
+
+@pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-qwen3.5"])
+def test_async_scheduling_graph_decode_matches_sync(preset):
+    """Graph replays launched before the previous step's tokens are read (input ids gathered on the
+    device, requests of different lengths ending between steps) give the sync engine's tokens."""
+    from afd_plugin_b200.runtime.sampling import SamplingParams
+
+    prompts = _prompts(6, 20, 1024)
+    lens = [5, 9, 12, 7, 12, 3]
+
+    def run(async_scheduling):
+        eng = _engine(preset, eager=False, async_scheduling=async_scheduling)
+        eng.capture_graphs()
+        ids = [eng.add_request(p, n, sampling=SamplingParams()) for p, n in zip(prompts, lens)]
+        while eng.has_unfinished():
+            eng.step()
+        return [eng.finished[i].output for i in ids], eng.num_async_steps
+
+    want, _ = run(False)
+    got, n_async = run(True)
+    assert got == want
+    assert n_async >= 8
 
 
 def test_dsa_dense_steps_replay_graphs_then_sparse_steps_run_eagerly():
