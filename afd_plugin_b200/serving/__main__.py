@@ -56,6 +56,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--max-num-batched-tokens", type=int, default=None,
                     help="prompt tokens per prefill step (chunked prefill; default: whole prompts)")
     ap.add_argument("--eager", "--enforce-eager", dest="eager", action="store_true")
+    ap.add_argument("--async-scheduling", action="store_true",
+                    help="launch each greedy decode step before the previous step's tokens are read back")
     ap.add_argument("--capture-sizes", default="", help="comma-separated decode graph batch sizes "
                     "(default: --max-num-seqs)")
     ap.add_argument("--compilation-config", default="", help="JSON with cudagraph_mode / cudagraph_capture_sizes")
@@ -124,7 +126,8 @@ def main(argv=None) -> None:
                                       checkpoint=args.checkpoint, seed=args.seed),
                           compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
                           cache_config=CacheConfig(enable_prefix_caching=args.enable_prefix_caching),
-                          max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens)
+                          max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
+                          async_scheduling=args.async_scheduling)
         engine = LLMEngine.colocated(ec, device="cuda" if torch.cuda.is_available() else "cpu")
         if not args.eager and engine.device.type == "cuda":
             engine.capture_graphs()
@@ -174,7 +177,7 @@ def main(argv=None) -> None:
                       compilation_config=CompilationConfig(cudagraph_capture_sizes=sizes),
                       cache_config=CacheConfig(enable_prefix_caching=args.enable_prefix_caching),
                       additional_config={"afd": dict(afd, role=role)}, max_num_seqs=args.max_num_seqs,
-                      max_num_batched_tokens=args.max_num_batched_tokens)
+                      max_num_batched_tokens=args.max_num_batched_tokens, async_scheduling=args.async_scheduling)
     if role == "ffn":
         w = AFDFFNWorker(ec, local_rank=local)
         if per_role and role_rank == 0:

@@ -17,17 +17,27 @@ from afd_plugin_b200.runtime.launcher import free_port
 from afd_plugin_b200.serving import EngineLoop, build_app, byte_detokenize, byte_tokenize
 
 
-def _engine():
+def _engine(async_scheduling=False):
     arch = get_preset("tiny-dsv2")
-    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96), max_num_seqs=4)
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96), max_num_seqs=4,
+                      async_scheduling=async_scheduling)
     return LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=96))
+
+
+@pytest.fixture(params=[False, True], ids=["sync", "async"])
+def any_server(request):
+    yield from _serve_engine(request.param)
 
 
 @pytest.fixture
 def server():
+    yield from _serve_engine(False)
+
+
+def _serve_engine(async_scheduling):
     import uvicorn
 
-    loop = EngineLoop(_engine()).start()
+    loop = EngineLoop(_engine(async_scheduling)).start()
     port = free_port()
     srv = uvicorn.Server(uvicorn.Config(build_app(loop), host="127.0.0.1", port=port, log_level="warning"))
     t = threading.Thread(target=srv.run, daemon=True)
@@ -45,8 +55,8 @@ def server():
     loop.stop()
 
 
-def test_completions_match_engine_generate(server):
-    url, loop = server
+def test_completions_match_engine_generate(any_server):
+    url, loop = any_server
     prompts = [[5, 9, 100, 7, 3, 1], [42] * 10, [1, 2, 3], [900, 800, 700, 600]]
     want = _engine().generate(prompts, 6)
     with ThreadPoolExecutor(4) as ex:  # concurrent requests are batched by the engine loop
@@ -63,6 +73,7 @@ def test_completions_match_engine_generate(server):
     assert models["data"][0]["id"] == "afd-b200" and models["data"][0]["max_model_len"] == 96
     assert m["ttft_count"] == 4 and m["tpot_count"] == 4
     assert 0 < m["mean_ttft_s"] < 60 and 0 < m["mean_tpot_s"] < 60
+    assert (loop.engine.num_async_steps > 0) == loop.engine.async_scheduling
 
 
 def test_text_prompt_and_validation(server):
@@ -244,8 +255,8 @@ def _stream_tokens(url, body):
     return toks, usage, events
 
 
-def test_streaming_completions(server):
-    url, _ = server
+def test_streaming_completions(any_server):
+    url, _ = any_server
     prompt = [5, 9, 100, 7, 3, 1]
     want = _engine().generate([prompt], 6)[0]
     toks, usage, events = _stream_tokens(url, {"prompt": prompt, "max_tokens": 6})
@@ -568,8 +579,8 @@ def test_server_cli_accepts_reference_recipe_flags():
         parse_args(["--afd", "{}", "--additional-config", '{"afd": {}}'])
 
 
-def test_text_stop_sequences(server):
-    url, loop = server
+def test_text_stop_sequences(any_server):
+    url, loop = any_server
     prompt = [5, 9, 100, 7, 3, 1]
     full = _engine().generate([prompt], 12)[0]
     text = byte_detokenize(full)
