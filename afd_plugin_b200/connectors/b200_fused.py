@@ -344,10 +344,17 @@ class FusedAttentionExecutor(FFNExecutor):
         for s in getattr(self, "_stages", (0,)):
             torch.ops.afd_b200.afd_epoch(self.c.epoch[s : s + 1])
 
-    def check_device_status(self) -> None:
-        st = self.c.read_status()
+    def check_device_status(self, status: int | None = None) -> None:
+        """Raise if a bounded device wait expired; ``status`` is a value already read from
+        ``device_status_word()`` (reading the word here synchronises with the current stream)."""
+        st = self.c.read_status() if status is None else int(status)
         if st:
             raise RuntimeError(f"Attention step failed on the device (status {st}: a peer wait timed out)")
+
+    def device_status_word(self) -> torch.Tensor:
+        """The device's status word (int32 [1]); an async-scheduled engine copies it to the host behind
+        each step instead of reading it synchronously."""
+        return torch.ops.afd_b200.status_word(self.c.local_rank)
 
     def send(self, layer_idx, attn_out, residual, stage_idx):
         c, d, a = self.c, self.c.dims, self.arch

@@ -109,6 +109,7 @@ class _InFlight:
     reqs: list[Request]  # the step's rows, in order
     host: torch.Tensor  # pinned int32 tokens, filled by the step's device->host copy
     done: torch.cuda.Event  # recorded after that copy
+    status: torch.Tensor | None = None  # pinned copy of the device status word behind the step
 
 
 class _HostEvent:
@@ -217,6 +218,7 @@ class LLMEngine:
         self._d_idx = torch.zeros(self.max_batch, dtype=torch.int64, device=self.device)
         event = torch.cuda.Event if self.device.type == "cuda" else _HostEvent
         self._events = [event() for _ in range(2)]
+        self._h_status = [mk(1, dt=torch.int32) for _ in range(2)]
         self._staged = event()
         self._h_state = mk(self.max_batch, dt=torch.int32)
         # numpy views of the pinned staging tensors: a decode step fills them
@@ -900,12 +902,17 @@ class LLMEngine:
         nxt = self.runner.decode_step(run_b, use_graph=use_graph, **flags)
         host = self._next_bufs[self._flip]
         host[:run_b].copy_(nxt, non_blocking=True)
+        status = None
+        word_of = getattr(self.ffn, "device_status_word", None)
+        if word_of is not None:  # read after the step's event instead of a blocking read
+            status = self._h_status[self._flip]
+            status.copy_(word_of(), non_blocking=True)
         done = self._events[self._flip]
         done.record()
         self._flip ^= 1
         self.num_async_steps += 1
-        self.last_d2h_bytes = run_b * 4
-        self._inflight = _InFlight(launch, host, done)
+        self.last_d2h_bytes = run_b * 4 + (4 if status is not None else 0)
+        self._inflight = _InFlight(launch, host, done, status)
         return self._consume(prev) if prev is not None else {}
 
     def _consume(self, fl: _InFlight) -> dict[int, int]:
@@ -913,7 +920,10 @@ class LLMEngine:
         fl.done.synchronize()
         check = getattr(self.ffn, "check_device_status", None)
         if check is not None:
-            check()
+            if fl.status is not None:
+                check(int(fl.status[0]))
+            else:
+                check()
         out = {}
         ended = False
         for r, t in zip(fl.reqs, fl.host.numpy()[: len(fl.reqs)].tolist()):

@@ -2,6 +2,7 @@
 
 from __future__ import annotations
 
+import pytest
 import torch
 
 from afd_plugin_b200.engine_config import CacheConfig, EngineConfig, ModelConfig
@@ -87,3 +88,37 @@ def test_async_falls_back_when_blocks_run_short():
     got, pipelined = _run(eng)
     assert got == want
     assert ref.num_preemptions > 0 and eng.num_preemptions > 0 and pipelined > 0
+
+
+def test_async_reads_the_device_status_behind_each_step():
+    """An executor with a device status word: the async engine copies the word behind every step and
+    checks the copy after the step's event (no blocking read of the live word), and a set word raises."""
+    from afd_plugin_b200.runtime.ffn_executor import LocalFFNExecutor
+
+    class Watched(LocalFFNExecutor):
+        def __init__(self, model):
+            super().__init__(model)
+            self.word = torch.zeros(1, dtype=torch.int32)
+            self.seen = []
+
+        def device_status_word(self):
+            return self.word
+
+        def check_device_status(self, status=None):
+            assert status is not None  # the engine passes the copy it read behind the step
+            self.seen.append(status)
+            if status:
+                raise RuntimeError(f"status {status}")
+
+    eng = _engine(True)
+    eng.ffn = eng.runner.ffn = Watched(eng.model)
+    eng.add_request(PROMPTS[0], 12)
+    eng.step()  # prefill (sync path: the executor's own check runs with no argument only there)
+    eng.ffn.seen.clear()
+    for _ in range(3):
+        eng.step()
+    assert eng.ffn.seen == [0, 0] and eng.num_async_steps == 3
+    eng.ffn.word[0] = 7  # a bounded wait expired during the next launched step
+    eng.step()  # reads the step launched before the word was set: still clean
+    with pytest.raises(RuntimeError, match="status 7"):
+        eng.step()
