@@ -94,6 +94,11 @@ def register_afd() -> dict[str, str]:
     if os.environ.get("AFD_PUBLISH_VLLM_ALIASES", "").lower() not in ("1", "true", "yes", "on"):
         _REGISTERED = True
         return dict(MODEL_ALIASES)
+    from afd_plugin_b200.compat import can_publish_aliases
+
+    if not can_publish_aliases():
+        _REGISTERED = True
+        return dict(MODEL_ALIASES)
     try:  # opt-in: publish the names into vLLM when present
         from vllm import ModelRegistry  # type: ignore
 

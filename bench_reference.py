@@ -326,12 +326,9 @@ def _healthy(port: int) -> bool:
 
 
 def _vllm_version() -> str:
-    try:
-        from importlib.metadata import version
+    from afd_plugin_b200.compat import installed_vllm_version
 
-        return f"vLLM {version('vllm')}"
-    except Exception:  # noqa: BLE001
-        return "vLLM ?"
+    return f"vLLM {installed_vllm_version() or '(not installed)'}"
 
 
 def main(args, metric: str, model_desc: str) -> None:
@@ -349,6 +346,10 @@ def main(args, metric: str, model_desc: str) -> None:
             import traceback
 
             tb = traceback.format_exc().strip().splitlines()
-            _unavailable(f"reference baseline run failed: {type(exc).__name__}: {exc} | " + " | ".join(tb[-4:]))
+            from afd_plugin_b200.compat import reference_vllm_mismatch
+
+            why = reference_vllm_mismatch()
+            _unavailable(f"reference baseline run failed: {type(exc).__name__}: {exc} | " + " | ".join(tb[-4:])
+                         + (f" | note: {why}" if why else ""))
         return
     run_afd(args, metric, model_desc)
