@@ -3,7 +3,7 @@
     torchrun --nproc-per-node A+F -m afd_plugin_b200.bench.connector_bench \
         --attn A --ffn F [--tokens 1,2,4,...,1024] [--hidden 7168 --experts 256 --topk 8]
 
-Payload (BASELINE config #4): hidden-7168 bf16 rows, top-8 routing over 256
+Payload (the reference's connector sweep: DeepSeek-V3 width): hidden-7168 bf16 rows, top-8 routing over 256
 experts from N(0, 1) logits with softmax weights.
 
 * ``fused``: Attention ranks run the fused dispatch kernel (norm, router,

@@ -2,7 +2,7 @@
 
     python bench.py --gpus N --steps K --warmup W [--impl reference]
 
-Workload (BASELINE config #2): DeepSeek-V2-Lite architecture, bf16, random
+Workload (the reference's DeepSeek-V2-Lite decode recipes): DeepSeek-V2-Lite architecture, bf16, random
 init; 256 concurrent requests, 1024-token prompts, 256 output tokens.
 Prompt KV is synthetic (filled at random, as the reference's decode-bench KV
 connector does), so only decode steps run.  N=1 is colocated; N>1 runs AFD

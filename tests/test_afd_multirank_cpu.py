@@ -1,6 +1,6 @@
 """AFD over real processes (gloo on CPU): split roles reproduce colocated tokens.
 
-BASELINE config #1: tiny DeepSeek-V2-style MoE, fp32, seed 0, 1 Attention +
+Correctness oracle: tiny DeepSeek-V2-style MoE, fp32, seed 0, 1 Attention +
 1 FFN rank, 4 prompts x 32 uniform ids, 16 greedy tokens -> identical output.
 """
 
