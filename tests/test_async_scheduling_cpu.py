@@ -122,3 +122,37 @@ def test_async_reads_the_device_status_behind_each_step():
     eng.step()  # reads the step launched before the word was set: still clean
     with pytest.raises(RuntimeError, match="status 7"):
         eng.step()
+
+
+def _engine_with(async_scheduling: bool, **cfg) -> LLMEngine:
+    arch = get_preset("tiny-dsv2")
+    cache = CacheConfig(block_size=4, enable_prefix_caching=cfg.pop("prefix", False))
+    ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96),
+                      cache_config=cache, max_num_seqs=8, async_scheduling=async_scheduling, **cfg)
+    return LLMEngine(ec, build_model(arch, role="colocated", dtype=torch.float32, seed=0, max_positions=96))
+
+
+@pytest.mark.parametrize("cfg", [{"max_num_batched_tokens": 5}, {"prefix": True}], ids=["chunked", "prefix"])
+def test_async_with_staggered_arrivals(cfg):
+    """Requests arrive while others decode (chunked prefill or prefix-cache hits in between): every
+    request's tokens equal the sync engine's under the same arrival schedule (arrivals keyed to the
+    number of tokens the first request has produced)."""
+    shared = [8, 8, 1, 2, 3, 4, 5, 6]  # two full 4-token blocks shared by the later prompts
+    arrivals = {0: [shared + [9]], 3: [shared + [7, 7], [4, 5]], 6: [shared + [1]]}
+
+    def run(async_scheduling):
+        eng = _engine_with(async_scheduling, **dict(cfg))
+        first = eng.add_request(PROMPTS[1], 14)
+        ids, done = [first], set()
+        while eng.has_unfinished():
+            n = len(eng.request(first).output) if first not in eng.finished else 99
+            for at, prompts in arrivals.items():
+                if n >= at and at not in done:
+                    done.add(at)
+                    ids += [eng.add_request(p, 8) for p in prompts]
+            eng.step()
+        return [eng.finished[i].output for i in ids], eng.num_async_steps
+
+    want, _ = run(False)
+    got, n_async = run(True)
+    assert got == want and n_async > 0
