@@ -74,8 +74,9 @@ class EngineConfig:
     max_num_seqs: int = 256
     # Prompt tokens one prefill step may compute (chunked prefill); None = whole prompts.
     max_num_batched_tokens: int | None = None
-    # Launch decode step t+1 before reading step t's tokens back (greedy decode
-    # with no request waiting); a step() then returns the previous step's tokens.
+    # Launch decode step t+1 before reading step t's tokens back (decode steps
+    # without penalties / logprobs / min_tokens and with no request waiting);
+    # a step() then returns the previous step's tokens.
     async_scheduling: bool = False
 
 

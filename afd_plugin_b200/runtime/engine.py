@@ -19,8 +19,9 @@ the KV blocks of common prompt prefixes; ``hold_kv`` / ``export_kv`` /
 ``add_prefilled_request`` hand a request's cache rows to another engine
 (``runtime/kv_transfer.py``); ``abort`` ends a request early.
 
-With ``EngineConfig.async_scheduling`` a steady greedy decode (no request
-waiting, on every Attention rank) launches step t+1 before it reads step t's tokens:
+With ``EngineConfig.async_scheduling`` a steady decode (no request waiting,
+on every Attention rank; greedy or sampled on the device, no penalties or
+logprobs) launches step t+1 before it reads step t's tokens:
 the next input ids are gathered on the device from step t's output, the host
 stages positions and block tables one token ahead, and the bookkeeping of
 step t (appending tokens, ending requests) runs while step t+1 is on the GPU.
@@ -828,13 +829,15 @@ class LLMEngine:
 
     def _pipeline_batch(self) -> list[Request] | None:
         """The requests the next step decodes if it may launch before the previous step's tokens are
-        read (a greedy decode with no prompt or imported request waiting and enough free KV blocks)."""
+        read (a decode without penalties, logprobs or min_tokens, with no prompt or imported request
+        waiting and enough free KV blocks)."""
         if (not self.running or self.waiting or self.prefilling or self._kv_waiting
                 or getattr(self.model.arch, "index_topk", 0)):
             return None
+        # penalties, logprobs and min_tokens read the generated tokens on the host (one behind here)
         for r in self.running:
             sp = r.sampling
-            if not sp.greedy or sp.logprobs is not None or sp.penalized or sp.min_tokens:
+            if sp.logprobs is not None or sp.penalized or sp.min_tokens:
                 return None
         lag = 0 if self._inflight is None else 1
         # a request whose token in flight is its last one is not decoded again
@@ -900,6 +903,9 @@ class LLMEngine:
                                                                       int(self._h_lens[:B].sum()),
                                                                       elem_bytes=self.model.dtype.itemsize)
         nxt = self.runner.decode_step(run_b, use_graph=use_graph, **flags)
+        if any(not r.sampling.greedy for r in launch):
+            # drawn on the device from this step's logits, before the next replay overwrites them
+            nxt = self._sample(launch, nxt)
         host = self._next_bufs[self._flip]
         host[:run_b].copy_(nxt, non_blocking=True)
         status = None

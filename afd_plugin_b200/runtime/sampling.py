@@ -132,11 +132,19 @@ def mask_tokens(logits: torch.Tensor, banned: list[list[int]]) -> torch.Tensor:
     return logits
 
 
+def _on_device(values: list, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A small host list as a device tensor without a stream synchronisation: a copy from pageable
+    memory waits for the stream's queued work, one from pinned memory is only ordered after it."""
+    t = torch.tensor(values, dtype=dtype, pin_memory=device.type == "cuda")
+    return t.to(device, non_blocking=True)
+
+
 def filtered_probs(logits: torch.Tensor, params: list[SamplingParams]) -> torch.Tensor:
-    """Row-wise probabilities after temperature, top-k and top-p; ``logits [n, V]``."""
+    """Row-wise probabilities after temperature, top-k and top-p; ``logits [n, V]``.  Enqueues device
+    work only (no host read-back), so a step launched ahead of its predecessor's read-back can sample."""
     x = logits.float()
     dev = x.device
-    temp = torch.tensor([max(p.temperature, 1e-6) for p in params], device=dev).unsqueeze(1)
+    temp = _on_device([max(p.temperature, 1e-6) for p in params], torch.float32, dev).unsqueeze(1)
     x = x / temp
     V = x.shape[1]
     ks = [p.top_k if 0 < p.top_k < V else 0 for p in params]
@@ -144,12 +152,12 @@ def filtered_probs(logits: torch.Tensor, params: list[SamplingParams]) -> torch.
     if need_sort:
         sorted_x, _ = x.sort(dim=-1, descending=True)
         if any(ks):
-            kk = torch.tensor([k if k else V for k in ks], device=dev)
+            kk = _on_device([k if k else V for k in ks], torch.int64, dev)
             kth = sorted_x.gather(1, (kk - 1).unsqueeze(1))
             x = x.masked_fill(x < kth, float("-inf"))
             sorted_x = sorted_x.masked_fill(torch.arange(V, device=dev)[None, :] >= kk[:, None], float("-inf"))
-        top_p = torch.tensor([p.top_p for p in params], device=dev).unsqueeze(1)
-        if bool((top_p < 1.0).any()):
+        top_p = _on_device([p.top_p for p in params], torch.float32, dev).unsqueeze(1)
+        if any(p.top_p < 1.0 for p in params):
             sp = torch.softmax(sorted_x, dim=-1)
             # keep the smallest prefix whose mass reaches top_p (the first token always stays)
             before = sp.cumsum(dim=-1) - sp
@@ -167,12 +175,12 @@ def sample(logits: torch.Tensor, params: list[SamplingParams], generators: list[
     rows = [i for i, p in enumerate(params) if not p.greedy]
     if not rows:
         return out
-    idx = torch.tensor(rows, device=logits.device)
+    idx = _on_device(rows, torch.int64, logits.device)
     probs = filtered_probs(logits.index_select(0, idx), [params[i] for i in rows])
     noise = torch.empty_like(probs)
     shared = [j for j, i in enumerate(rows) if generators[i] is None]
     if shared:
-        sel = torch.tensor(shared, device=logits.device)
+        sel = _on_device(shared, torch.int64, logits.device)
         noise[sel] = torch.empty(len(shared), probs.shape[1], device=probs.device).exponential_(
             generator=default_generator)
     for j, i in enumerate(rows):

@@ -156,3 +156,27 @@ def test_async_with_staggered_arrivals(cfg):
     want, _ = run(False)
     got, n_async = run(True)
     assert got == want and n_async > 0
+
+
+def test_async_sampled_requests_match_sync():
+    """Seeded temperature / top-k / top-p requests (each its own generator) pipelined: tokens equal the
+    sync engine's; a penalised request drains and runs synchronously."""
+    sps = [SamplingParams(temperature=0.8, seed=11), SamplingParams(temperature=1.2, top_k=20, seed=5),
+           SamplingParams(temperature=0.7, top_p=0.9, seed=3), SamplingParams()]
+
+    def run(async_scheduling, extra=None):
+        eng = _engine(async_scheduling)
+        ids = [eng.add_request(p, m, sampling=sp) for p, m, sp in zip(PROMPTS, MAX_TOKENS, sps)]
+        if extra is not None:
+            ids.append(eng.add_request(PROMPTS[4], 6, sampling=extra))
+        while eng.has_unfinished():
+            eng.step()
+        return [eng.finished[i].output for i in ids], eng.num_async_steps
+
+    want, _ = run(False)
+    got, n_async = run(True)
+    assert got == want and n_async >= 8
+    pen = SamplingParams(temperature=0.9, seed=2, presence_penalty=0.5)
+    want, _ = run(False, pen)
+    got, n_async = run(True, pen)
+    assert got == want and n_async >= 4  # pipelined again once the penalised request ends

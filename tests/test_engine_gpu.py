@@ -40,16 +40,21 @@ def test_graph_decode_matches_eager(preset):
 @pytest.mark.parametrize("preset", ["tiny-dsv2", "tiny-qwen3.5"])
 def test_async_scheduling_graph_decode_matches_sync(preset):
     """Graph replays launched before the previous step's tokens are read (input ids gathered on the
-    device, requests of different lengths ending between steps) give the sync engine's tokens."""
+    device, requests of different lengths ending between steps, seeded sampling on the device) give
+    the sync engine's tokens."""
     from afd_plugin_b200.runtime.sampling import SamplingParams
 
     prompts = _prompts(6, 20, 1024)
     lens = [5, 9, 12, 7, 12, 3]
+    # greedy rows plus seeded sampled rows (drawn on the device after each replay)
+    sps = [SamplingParams(), SamplingParams(temperature=0.8, seed=7), SamplingParams(),
+           SamplingParams(temperature=1.1, top_k=40, seed=3), SamplingParams(temperature=0.7, top_p=0.9, seed=9),
+           SamplingParams()]
 
     def run(async_scheduling):
         eng = _engine(preset, eager=False, async_scheduling=async_scheduling)
         eng.capture_graphs()
-        ids = [eng.add_request(p, n, sampling=SamplingParams()) for p, n in zip(prompts, lens)]
+        ids = [eng.add_request(p, n, sampling=sp) for p, n, sp in zip(prompts, lens, sps)]
         while eng.has_unfinished():
             eng.step()
         return [eng.finished[i].output for i in ids], eng.num_async_steps
