@@ -618,23 +618,30 @@ class FusedFFNRunner:
 
         Steps are launched without waiting for the previous one: the captured
         step itself waits (bounded) for the Attention side's arrivals, so the
-        host can queue the next step while the device runs.  The device status
-        is checked every ``check_every`` steps and at the end.
+        host can queue the next step while the device runs.  Behind every step
+        the device status word is copied into pinned memory (stream-ordered,
+        no host wait); the host checks the latest landed copy before each
+        launch, reads the live word every ``check_every`` steps and at the end.
         """
         from afd_plugin_b200.utils.profiler import RoleProfiler
 
         cp = self.c.control_plane
         prof = RoleProfiler("ffn")
+        word = torch.ops.afd_b200.status_word(self.c.local_rank)
+        seen = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         n = 0
         try:
             while (max_steps is None or n < max_steps) and not (stop is not None and stop.is_set()):
                 check = getattr(self, "health_check", None)
                 if check is not None:
                     check()  # a peer stopped heartbeating: fail before waiting on it
+                if int(seen[0]):
+                    self._check()
                 payload = cp.recv_dp_metadata_list()
                 if payload.is_shutdown:
                     break
                 self.execute_model(payload)
+                seen.copy_(word, non_blocking=True)
                 n += 1
                 prof.step()
                 if n % check_every == 0:
