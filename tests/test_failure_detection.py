@@ -130,3 +130,16 @@ def test_heartbeat_quiet_on_clean_runs(monkeypatch):
                         timeout_s=30)
     res = launch_local(spec, join_timeout_s=90)
     assert not any("error" in v for v in res.values()), res
+
+
+@pytest.mark.parametrize("A", [1, 2])
+def test_attention_rank_exception_with_async_scheduling(A):
+    """A step launched ahead of its predecessor's read-back is in flight when the Attention rank raises:
+    the error still surfaces on every rank within the process-group timeout (no hang)."""
+    spec = LocalAFDSpec(afd={"num_attention_ranks": A, "num_ffn_ranks": 1}, prompts=_prompts(n=4), max_tokens=8,
+                        timeout_s=8, fault={"rank": 1, "kind": "raise", "at_step": 3}, async_scheduling=True)
+    t0 = time.time()
+    res = launch_local(spec, join_timeout_s=60)
+    assert time.time() - t0 < 60
+    assert "injected fault" in res[1]["error"]
+    assert all("error" in v for v in res.values())
