@@ -343,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       int it_count = 0, acc_count = 0, idx = blockIdx.x;
+      int fail_ab = 0, fail_par = 0;  // the accumulator barrier whose phase a timeout leaves open
       PItem it;
       bool ok = true;
       while (ok && next_phase_item(idx, g, n0, n_all, it)) {
@@ -351,6 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           const int n_sub = min(SUB, (it.cnt - p * kPassRows + kSub - 1) / kSub);
           const uint32_t idesc = make_idesc(kBM, n_sub * kSub);
           const int ab = acc_count & 1;
+          fail_ab = ab;
+          fail_par = (acc_count >> 1) & 1;
           if (!mbar_wait_bounded(&sm.acc_empty[ab], ((acc_count >> 1) & 1) ^ 1)) {
             atomicExch(g.status, kStatusWaitTimeout);
             ok = false;
@@ -375,6 +378,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           }
           if (ok) umma_commit(&sm.acc_full[ab]);
         }
+      }
+      if (!ok) {
+        // a commit's arrival marks every MMA issued before it complete: wait (bounded)
+        // for it so that no MMA still writes TMEM when the CTA deallocates it
+        umma_commit(&sm.acc_full[fail_ab]);
+        mbar_wait_bounded(&sm.acc_full[fail_ab], fail_par);
       }
     }
   } else {
@@ -745,6 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       int it_count = 0, acc_count = 0, idx = blockIdx.x;
+      int fail_ab = 0, fail_par = 0;  // the accumulator barrier whose phase a timeout leaves open
       gg::Item it;
       bool ok = true;
       while (ok && gg::next_item(idx, n_items, n_tiles, counts, offsets, it)) {
@@ -755,6 +765,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
           const int n_tok = min(kPassRows, it.cnt - p * kPassRows);
           const uint32_t idesc = gg::make_idesc(kBM, (n_tok + 15) / 16 * 16);
           const int ab = acc_count & 1;
+          fail_ab = ab;
+          fail_par = (acc_count >> 1) & 1;
           if (!mbar_wait_bounded(&sm.acc_empty[ab], ((acc_count >> 1) & 1) ^ 1)) {
             atomicExch(status, kStatusWaitTimeout);
             ok = false;
@@ -785,6 +797,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_w8_kernel(
           }
           if (ok) gg::umma_commit(&sm.acc_full[ab]);
         }
+      }
+      if (!ok) {
+        // drain the issued MMAs before the CTA deallocates TMEM (see the bf16 kernel)
+        gg::umma_commit(&sm.acc_full[fail_ab]);
+        mbar_wait_bounded(&sm.acc_full[fail_ab], fail_par);
       }
     }
   } else {

@@ -428,8 +428,14 @@ __global__ void __launch_bounds__(kThreads, MIN_CTAS) mla_decode_tc_kernel(
           ok = false;
         }
       }
-      if (ok) commit(&sm.o_last);
-      if (!ok) atomicExch(status, kStatusWaitTimeout);
+      // The commit's arrival also marks every MMA issued so far complete: after
+      // a timeout this thread waits (bounded) for it, so no MMA still writes
+      // TMEM when the CTA deallocates it.
+      commit(&sm.o_last);
+      if (!ok) {
+        atomicExch(status, kStatusWaitTimeout);
+        wait(&sm.o_last, 0);
+      }
     }
   } else {
     // ----------------------------------------- softmax / correction / epilogue
