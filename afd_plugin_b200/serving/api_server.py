@@ -636,6 +636,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
             out["prefix_cache_hit_rate"] = round(alloc.hits / alloc.queries, 4) if alloc.queries else None
         out["kv_blocks_free"] = alloc.num_free
         out["preemptions"] = getattr(loop.engine, "num_preemptions", 0)
+        out["async_steps"] = getattr(loop.engine, "num_async_steps", 0)
         return out
 
     @app.get("/metrics/prometheus")
@@ -645,7 +646,7 @@ def build_app(loop: EngineLoop, *, model_name: str = "afd-b200", request_timeout
 
         m = metrics()
         kinds = {"requests": "counter", "completed": "counter", "aborted": "counter", "generated_tokens": "counter",
-                 "steps": "counter", "preemptions": "counter", "decode_tokens": "counter"}
+                 "steps": "counter", "preemptions": "counter", "decode_tokens": "counter", "async_steps": "counter"}
         lines = []
         for key, value in sorted(m.items()):
             if not isinstance(value, (int, float)) or isinstance(value, bool):

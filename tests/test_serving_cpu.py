@@ -74,6 +74,7 @@ def test_completions_match_engine_generate(any_server):
     assert m["ttft_count"] == 4 and m["tpot_count"] == 4
     assert 0 < m["mean_ttft_s"] < 60 and 0 < m["mean_tpot_s"] < 60
     assert (loop.engine.num_async_steps > 0) == loop.engine.async_scheduling
+    assert 0 < m["async_steps"] <= loop.engine.num_async_steps if loop.engine.async_scheduling else m["async_steps"] == 0
 
 
 def test_text_prompt_and_validation(server):
