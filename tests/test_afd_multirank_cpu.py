@@ -81,11 +81,12 @@ def test_qwen3_moe_2a2f():
     assert outs == ref
 
 
-def test_dbo_two_ubatches_matches():
+@pytest.mark.parametrize("async_scheduling", [False, True], ids=["sync", "async"])
+def test_dbo_two_ubatches_matches(async_scheduling):
     prompts = _prompts(n=4, length=16)
     ref = _colocated("tiny-dsv2", prompts, 6)
     outs, _ = _run("tiny-dsv2", {"num_attention_ranks": 1, "num_ffn_ranks": 1}, prompts, max_tokens=6,
-                   use_ubatching=True)
+                   use_ubatching=True, async_scheduling=async_scheduling)
     assert outs == ref
 
 
