@@ -11,8 +11,9 @@ from afd_plugin_b200.runtime.engine import LLMEngine
 from afd_plugin_b200.runtime.sampling import SamplingParams
 
 
-def _engine(async_scheduling: bool, block_size: int = 4, num_blocks: int | None = None) -> LLMEngine:
-    arch = get_preset("tiny-dsv2")
+def _engine(async_scheduling: bool, block_size: int = 4, num_blocks: int | None = None,
+            preset: str = "tiny-dsv2") -> LLMEngine:
+    arch = get_preset(preset)
     ec = EngineConfig(ModelConfig(arch, dtype=torch.float32, enforce_eager=True, max_model_len=96),
                       cache_config=CacheConfig(block_size=block_size, num_blocks=num_blocks), max_num_seqs=8,
                       async_scheduling=async_scheduling)
@@ -180,3 +181,12 @@ def test_async_sampled_requests_match_sync():
     want, _ = run(False, pen)
     got, n_async = run(True, pen)
     assert got == want and n_async >= 4  # pipelined again once the penalised request ends
+
+
+@pytest.mark.parametrize("preset", ["tiny-qwen3-moe", "tiny-qwen3.5", "tiny-dsv4", "tiny-dsv1"])
+def test_async_equals_sync_across_model_families(preset):
+    """GQA + QK-norm, Gated DeltaNet state rows, mHC streams with hash routing (the router reads the
+    device-gathered input ids) and DeepSeek V1: pipelined tokens equal the sync engine's."""
+    want, _ = _run(_engine(False, preset=preset))
+    got, n_async = _run(_engine(True, preset=preset))
+    assert got == want and n_async >= 8
