@@ -140,14 +140,17 @@ class AttentionCoordinator:
         self.any_sparse = any(bool(t[2]) for t in out)
         return [(int(t[0]), bool(t[1])) for t in out]
 
-    def agree_pipelined(self, num_tokens: int) -> list[int]:
-        """Async scheduling: every rank's launch size for a pipelined decode step (-1: it cannot)."""
+    def agree_pipelined(self, num_tokens: int, *, sparse: bool = False) -> list[int]:
+        """Async scheduling: every rank's launch size for a pipelined decode step (-1: it cannot);
+        ``any_sparse`` afterwards says whether some rank's step selects sparse positions."""
         if self.group is None or self.size == 1:
+            self.any_sparse = sparse
             return [num_tokens]
-        mine = torch.tensor([num_tokens], dtype=torch.int64)
+        mine = torch.tensor([num_tokens, int(sparse)], dtype=torch.int64)
         out = [torch.empty_like(mine) for _ in range(self.size)]
         dist.all_gather(out, mine, group=self.group)
-        return [int(t) for t in out]
+        self.any_sparse = any(bool(t[1]) for t in out)
+        return [int(t[0]) for t in out]
 
 
 class LLMEngine:
@@ -570,8 +573,7 @@ class LLMEngine:
         plan = self._plan_prefill()
         is_prefill = bool(plan)
         ntok = sum(take for _, take in plan) if is_prefill else len(self.running)
-        topk = getattr(self.model.arch, "index_topk", 0)
-        sparse = bool(topk) and any(r.num_tokens > topk for r in self.running)
+        sparse = self._needs_sparse(self.running)
         votes = self.coordinator.exchange(ntok, is_prefill, sparse=sparse)
         if any(p for _, p in votes):
             self._last_phase = "prefill"
@@ -819,10 +821,11 @@ class LLMEngine:
         their FFN stages line up.
         """
         launch = self._pipeline_batch()
-        sizes = self.coordinator.agree_pipelined(-1 if launch is None else len(launch))
+        sparse = self._needs_sparse(launch, lag=0 if self._inflight is None else 1) if launch else False
+        sizes = self.coordinator.agree_pipelined(-1 if launch is None else len(launch), sparse=sparse)
         if min(sizes) > 0:
             with torch.profiler.record_function("afd_decode_step"):
-                return self._decode_step_async(launch, max(sizes), len(sizes))
+                return self._decode_step_async(launch, max(sizes), len(sizes), self.coordinator.any_sparse)
         if self._inflight is not None:
             return self._drain()
         return None
@@ -831,8 +834,7 @@ class LLMEngine:
         """The requests the next step decodes if it may launch before the previous step's tokens are
         read (a decode without penalties, logprobs or min_tokens, with no prompt or imported request
         waiting and enough free KV blocks)."""
-        if (not self.running or self.waiting or self.prefilling or self._kv_waiting
-                or getattr(self.model.arch, "index_topk", 0)):
+        if not self.running or self.waiting or self.prefilling or self._kv_waiting:
             return None
         # penalties, logprobs and min_tokens read the generated tokens on the host (one behind here)
         for r in self.running:
@@ -850,7 +852,14 @@ class LLMEngine:
             need += max(0, (r.num_tokens - 1 + lag) // bs + 1 - len(r.blocks))
         return launch if need <= self.kv.allocator.num_free else None
 
-    def _decode_step_async(self, launch: list[Request], top: int, nranks: int) -> dict[int, int]:
+    def _needs_sparse(self, reqs: list[Request], lag: int = 0) -> bool:
+        """DeepSeek sparse attention: some request's context (with ``lag`` tokens still in flight)
+        is past ``index_topk``, so the step selects positions (eagerly) instead of replaying a graph."""
+        topk = getattr(self.model.arch, "index_topk", 0)
+        return bool(topk) and any(r.num_tokens + lag > topk for r in reqs)
+
+    def _decode_step_async(self, launch: list[Request], top: int, nranks: int,
+                           sparse: bool = False) -> dict[int, int]:
         """Launch a decode step of ``launch`` (padded to ``top`` rows, the largest Attention rank's batch)
         from staged positions and the device-resident tokens of the step in flight, then read that step's
         tokens."""
@@ -860,13 +869,13 @@ class LLMEngine:
         lag = 0 if prev is None else 1
         B = len(launch)
         padded = pad_to_capture_size(top, self.capture_sizes) if self.use_graphs else None
-        use_graph = padded is not None and padded in self.runner.graphs
+        use_graph = padded is not None and padded in self.runner.graphs and not sparse
         run_b = padded if use_graph else top
         flags = {}
         if nranks > 1:
             sp = ubatch_splits(run_b, self.runner.num_ubatches)
             flags["tokens_across_attn"] = {s: (sp[s + 1] - sp[s],) * nranks for s in range(len(sp) - 1)}
-        self.runner.sparse_decode = False
+        self.runner.sparse_decode = sparse
         # the pinned staging rows are rewritten below: the previous step's
         # host->device copies of them must have run
         self._staged.synchronize()

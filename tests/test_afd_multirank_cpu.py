@@ -122,12 +122,17 @@ def test_attention_tp2_matches_colocated(preset):
     assert outs == ref
 
 
-def test_dsv32_sparse_attention_2a2f():
-    """DeepSeek sparse attention (indexer on the Attention side, prompts past index_topk) across 2A2F."""
+@pytest.mark.parametrize("async_scheduling", [False, True], ids=["sync", "async"])
+def test_dsv32_sparse_attention_2a2f(async_scheduling):
+    """DeepSeek sparse attention (indexer on the Attention side, prompts past index_topk) across 2A2F;
+    with async scheduling the ranks agree on the sparse mode in the same exchange as the launch sizes."""
     prompts = _prompts(n=4, length=20)
     ref = _colocated("tiny-dsv32", prompts, 6)
-    outs, _ = _run("tiny-dsv32", {"num_attention_ranks": 2, "num_ffn_ranks": 2}, prompts, max_tokens=6)
+    outs, res = _run("tiny-dsv32", {"num_attention_ranks": 2, "num_ffn_ranks": 2}, prompts, max_tokens=6,
+                     async_scheduling=async_scheduling)
     assert outs == ref
+    if async_scheduling:
+        assert all(v["async_steps"] >= 3 for v in res.values() if v["role"] == "attention")
 
 
 def test_dsv32_attention_tp2():

@@ -183,10 +183,34 @@ def test_async_sampled_requests_match_sync():
     assert got == want and n_async >= 4  # pipelined again once the penalised request ends
 
 
-@pytest.mark.parametrize("preset", ["tiny-qwen3-moe", "tiny-qwen3.5", "tiny-dsv4", "tiny-dsv1"])
+@pytest.mark.parametrize("preset", ["tiny-qwen3-moe", "tiny-qwen3.5", "tiny-dsv4", "tiny-dsv1", "tiny-dsv32"])
 def test_async_equals_sync_across_model_families(preset):
     """GQA + QK-norm, Gated DeltaNet state rows, mHC streams with hash routing (the router reads the
-    device-gathered input ids) and DeepSeek V1: pipelined tokens equal the sync engine's."""
+    device-gathered input ids), DeepSeek V1, and DeepSeek sparse attention (contexts cross index_topk
+    while steps are in flight: the sparse decision counts the token in flight): pipelined tokens equal
+    the sync engine's."""
     want, _ = _run(_engine(False, preset=preset))
     got, n_async = _run(_engine(True, preset=preset))
     assert got == want and n_async >= 8
+
+
+@pytest.mark.parametrize("async_scheduling", [False, True], ids=["sync", "async"])
+def test_sparse_attention_decision_counts_the_token_in_flight(async_scheduling):
+    """DeepSeek sparse attention selects positions exactly on the steps whose longest context exceeds
+    index_topk; with a step in flight the staged context is one token longer than the host's view."""
+    eng = _engine(async_scheduling, preset="tiny-dsv32")
+    topk = eng.model.arch.index_topk
+    seen = []
+    inner = eng.runner.decode_step
+
+    def spy(batch, **kw):
+        seen.append((bool(eng.runner.sparse_decode), int(eng._n_lens[:batch].max())))
+        return inner(batch, **kw)
+
+    eng.runner.decode_step = spy
+    for p, m in zip(PROMPTS, MAX_TOKENS):
+        eng.add_request(p, m)
+    while eng.has_unfinished():
+        eng.step()
+    assert any(s for s, _ in seen) and not all(s for s, _ in seen)
+    assert all(s == (longest > topk) for s, longest in seen)

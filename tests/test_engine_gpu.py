@@ -65,15 +65,18 @@ def test_async_scheduling_graph_decode_matches_sync(preset):
     assert n_async >= 8
 
 
-def test_dsa_dense_steps_replay_graphs_then_sparse_steps_run_eagerly():
+@pytest.mark.parametrize("async_scheduling", [False, True], ids=["sync", "async"])
+def test_dsa_dense_steps_replay_graphs_then_sparse_steps_run_eagerly(async_scheduling):
     """DeepSeek sparse attention: within index_topk the captured dense graph replays; past it the
-    engine selects positions eagerly.  Tokens equal an all-eager engine's."""
+    engine selects positions eagerly (also with steps launched ahead of their predecessor's
+    read-back).  Tokens equal an all-eager engine's."""
     prompts = _prompts(4, 5, 1024)  # index_topk 8: decode steps 1-3 dense, later ones sparse
     eager = _engine("tiny-dsv32", eager=True).generate(prompts, 8)
-    eng = _engine("tiny-dsv32", eager=False)
+    eng = _engine("tiny-dsv32", eager=False, async_scheduling=async_scheduling)
     eng.capture_graphs()
     assert 8 in eng.runner.graphs
     assert eng.generate(prompts, 8) == eager
+    assert (eng.num_async_steps > 0) == async_scheduling
 
 
 def test_gpu_prefill_logits_track_fp32_reference():
