@@ -208,6 +208,8 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--tp", type=int, default=1, help="attention tensor parallelism")
     ap.add_argument("--dbo", action="store_true", help="two-ubatch overlap")
     ap.add_argument("--graphs", action="store_true", help="capture decode CUDA graphs (nccl backend)")
+    ap.add_argument("--async-scheduling", action="store_true",
+                    help="launch each decode step before the previous step's tokens are read back")
     args = ap.parse_args(argv)
     afd = json.loads(args.additional_config)["afd"]
     from afd_plugin_b200.models.configs import get_preset
@@ -222,7 +224,8 @@ def main(argv: list[str] | None = None) -> int:
     prompts = torch.randint(0, vocab, (args.num_prompts, args.prompt_len), generator=g).tolist()
     spec = LocalAFDSpec(preset=args.preset, afd=afd, prompts=prompts, max_tokens=args.max_tokens,
                         backend=args.backend, dtype=args.dtype, checkpoint=args.checkpoint, tp=args.tp,
-                        use_ubatching=args.dbo, enforce_eager=not args.graphs)
+                        use_ubatching=args.dbo, enforce_eager=not args.graphs,
+                        async_scheduling=args.async_scheduling)
     res = launch_local(spec)
     print(json.dumps({str(k): v for k, v in sorted(res.items())}))
     return 0 if all("error" not in v for v in res.values()) else 1
