@@ -29,6 +29,8 @@ class Scenario:
     # Prefill/decode disaggregation: this scenario's server decodes behind the
     # proxy, and a server of the ``prefill`` scenario runs the prompts.
     prefill: "Scenario | None" = None
+    # the server launches each decode step before the previous one's tokens are read back
+    async_scheduling: bool = False
 
     @property
     def world_size(self) -> int:
@@ -53,8 +55,8 @@ class Scenario:
         return cfg
 
 
-def _s(name, baseline, graph, dbo, a, f, connector=NCCL, tp=1) -> tuple[str, Scenario]:
-    return name, Scenario(name, baseline, graph, dbo, a, f, connector, tp)
+def _s(name, baseline, graph, dbo, a, f, connector=NCCL, tp=1, async_scheduling=False) -> tuple[str, Scenario]:
+    return name, Scenario(name, baseline, graph, dbo, a, f, connector, tp, async_scheduling=async_scheduling)
 
 
 def _pd(name, decode: str, prefill: str) -> tuple[str, Scenario]:
@@ -79,6 +81,10 @@ _BASE: dict[str, Scenario] = dict([
     _s("afd-fused-graph-2a2f", False, True, False, 2, 2, FUSED),
     _s("afd-fused-graph-dbo-2a2f", False, True, True, 2, 2, FUSED),
     _s("afd-fused-graph-6a2f", False, True, False, 6, 2, FUSED),
+    # async scheduling: greedy tokens must equal the synchronous rows'
+    _s("baseline-graph-async", True, True, False, 1, 0, async_scheduling=True),
+    _s("afd-graph-2a2f-async", False, True, False, 2, 2, async_scheduling=True),
+    _s("afd-fused-graph-2a2f-async", False, True, False, 2, 2, FUSED, async_scheduling=True),
 ])
 
 # Prefill on a colocated server, decode on an AFD deployment, the proxy in front.
@@ -107,6 +113,8 @@ def server_command(scn: Scenario, *, python: str, preset: str, port: int, master
         serve += ["--dbo"]
     if scn.tp > 1:
         serve += ["--tp", str(scn.tp)]
+    if scn.async_scheduling:
+        serve += ["--async-scheduling"]
     if scn.baseline:
         return [python, *serve]
     serve += ["--afd", json.dumps(scn.afd_config(connector_extra), separators=(",", ":"))]

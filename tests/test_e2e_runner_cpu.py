@@ -239,3 +239,12 @@ def test_roles_launched_separately_join_one_afd_world(tmp_path):
     finally:
         stop_server(attn)
         stop_server(ffn)
+
+
+def test_async_scheduling_scenarios():
+    """The async-scheduling rows pass the server flag; the others do not."""
+    for name in ("baseline-graph-async", "afd-graph-2a2f-async", "afd-fused-graph-2a2f-async"):
+        cmd = server_command(SCENARIOS[name], python="py", preset="p", port=9, master_port=10)
+        assert "--async-scheduling" in cmd and SCENARIOS[name].async_scheduling
+    plain = server_command(SCENARIOS["afd-graph-2a2f"], python="py", preset="p", port=9, master_port=10)
+    assert "--async-scheduling" not in plain
