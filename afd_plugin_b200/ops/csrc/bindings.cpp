@@ -68,6 +68,16 @@ bool mla_tc_enabled() {
   }();
   return on;
 }
+// AFD_MLA_BALANCED=1 runs the work-balanced MLA decode kernel (the KV tiles of
+// all requests split evenly over one wave of CTAs) for the shapes the split
+// kernel would take; off by default.
+bool mla_balanced_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("AFD_MLA_BALANCED");
+    return v != nullptr && std::string(v) == "1";
+  }();
+  return on;
+}
 std::vector<at::Tensor> g_mla_arrivals;
 
 int* mla_arrivals(const at::Tensor& like, int64_t need) {
@@ -324,6 +334,19 @@ at::Tensor mla_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at:
       e = launch_mla_decode_tc(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
                                po_ptr, pl_ptr, status_ptr(q_lat), B, H, bs, nblocks, (int)block_table.stride(0), splits,
                                (float)scale, stream(), arr);
+  }
+  if (e == cudaErrorNotSupported && mla_balanced_enabled() && num_splits <= 0 &&
+      B <= mla_decode_balanced_max_batch()) {
+    int* arr = mla_arrivals(q_lat, (int64_t)B * (H / 16));
+    if (arr != nullptr) {
+      const int ctas = mla_decode_balanced_ctas(H, dev_sms);
+      at::Tensor bpo = at::empty({2 * ctas, H, 512}, q_lat.options().dtype(at::kFloat));
+      at::Tensor bpl = at::empty({2 * ctas, H}, q_lat.options().dtype(at::kFloat));
+      e = launch_mla_decode_balanced(qo, cache.data_ptr(), block_table.data_ptr<int32_t>(),
+                                     seq_lens.data_ptr<int32_t>(), bpo.data_ptr<float>(), bpl.data_ptr<float>(),
+                                     status_ptr(q_lat), arr, B, H, bs, nblocks, (int)block_table.stride(0), ctas,
+                                     (float)scale, stream());
+    }
   }
   if (e == cudaErrorNotSupported) {  // nothing launched: the mma.sync kernel takes the shape
     if (use_tc && splits > 1 && num_splits <= 0) {

@@ -71,6 +71,17 @@ cudaError_t launch_mla_decode(const MlaQO& qo, const void* cache, const int32_t*
                               const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status, int batch,
                               int heads, int L, int R, int block_size, int num_blocks, int max_blocks_per_seq,
                               int num_splits, float scale, cudaStream_t s, int* arrivals = nullptr);
+// Work-balanced variant: `ctas` CTAs per 16-head group split the concatenated
+// KV tiles of all requests evenly; partial_o [2 * ctas, heads, 512] and
+// partial_lse [2 * ctas, heads] fp32; arrivals: >= batch * heads / 16 zeroed
+// ints (left zero).  batch <= mla_decode_balanced_max_batch().  Returns
+// cudaErrorNotSupported (nothing launched) for shapes it does not take.
+int mla_decode_balanced_ctas(int heads, int num_sms);
+int mla_decode_balanced_max_batch();
+cudaError_t launch_mla_decode_balanced(const MlaQO& qo, const void* cache, const int32_t* block_table,
+                                       const int32_t* seq_lens, float* partial_o, float* partial_lse, int* status,
+                                       int* arrivals, int batch, int heads, int block_size, int num_blocks,
+                                       int max_blocks_per_seq, int ctas, float scale, cudaStream_t s);
 // ---- mla_decode_tc.cu (tcgen05 version of the same decode; DeepSeek 512 + 64
 // latent, block sizes that are multiples of 64, heads a multiple of 16).
 // Heads per CTA for `heads` (0 = unsupported), the split count for a batch,

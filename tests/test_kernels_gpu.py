@@ -2,6 +2,8 @@
 
 import math
 
+import os
+
 import pytest
 import torch
 
@@ -486,6 +488,44 @@ def test_mla_decode_tc_shapes_16_heads(shape):
         "print('ok')\n"
     )
     env = dict(os.environ, AFD_MLA_TC_SHAPE=shape)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+@pytest.mark.skipif(os.environ.get("AFD_RUN_UNVERIFIED_KERNELS") != "1",
+                    reason="the work-balanced MLA kernel has not run on a GPU yet; AFD_RUN_UNVERIFIED_KERNELS=1 runs it")
+def test_mla_decode_balanced_vs_fp32():
+    """The work-balanced MLA decode kernel (AFD_MLA_BALANCED=1, read once per process, hence the child
+    process) vs fp32: mixed lengths, one request over many CTAs, more CTAs than tiles, 16 and 128 heads,
+    and repeated launches (the per-request arrival counters must be left at zero)."""
+    import subprocess
+    import sys
+
+    code = (
+        "import math, torch\n"
+        "from afd_plugin_b200 import ops\n"
+        "from afd_plugin_b200.ops import reference as ref\n"
+        "torch.manual_seed(0)\n"
+        "bs=64\n"
+        "for lens, heads in (([1,33,64,200,1029], 16), ([20000], 16), ([1034]*300, 16), ([5,700,64,1], 128),\n"
+        "                    ([2,3], 16)):\n"
+        "    nb=[math.ceil(n/bs) for n in lens]\n"
+        "    cache=torch.randn(sum(nb)+2,bs,576,device='cuda',dtype=torch.bfloat16)\n"
+        "    table=torch.zeros(len(lens),max(nb),dtype=torch.int32)\n"
+        "    o=1\n"
+        "    for b,k in enumerate(nb):\n"
+        "        table[b,:k]=torch.arange(o,o+k,dtype=torch.int32); o+=k\n"
+        "    table=table.cuda(); seq=torch.tensor(lens,dtype=torch.int32,device='cuda')\n"
+        "    for rep in range(3):\n"
+        "        q=torch.randn(len(lens),heads,576,device='cuda',dtype=torch.bfloat16)\n"
+        "        out=ops.mla_decode(q,cache,table,seq,0.07,512).float()\n"
+        "        exp=ref.mla_decode(q.float(),cache.float(),table,seq,0.07,512)\n"
+        "        err=((out-exp).abs().max()/(exp.abs().max()+1e-6)).item()\n"
+        "        assert err < 2e-2, (len(lens), heads, rep, err)\n"
+        "assert torch.ops.afd_b200.read_status(0) == 0\n"
+        "print('ok')\n"
+    )
+    env = dict(os.environ, AFD_MLA_BALANCED="1", AFD_MLA_KERNEL="mma")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
 
