@@ -11,7 +11,10 @@ that evicts L2 (126 MB), so the cache is read from HBM at every shape.
 
 ``--sparse`` compares DeepSeek-sparse-attention decode (the indexer's kept
 positions) on the sm_100a gather kernel against the gather + two batched
-GEMMs of ``ops/reference.py::mla_decode_sparse``.
+GEMMs of ``ops/reference.py::mla_decode_sparse``.  The kernel is chosen per
+process by the environment: ``AFD_MLA_KERNEL=mma`` (the mma.sync split
+kernel at every head count), ``AFD_MLA_BALANCED=1`` (the work-balanced
+kernel for 16-head groups), ``AFD_MLA_TC_SHAPE`` (a tcgen05 shape).
 """
 
 from __future__ import annotations
