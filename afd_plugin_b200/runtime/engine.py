@@ -555,7 +555,10 @@ class LLMEngine:
         self.model.reload_weights(checkpoint, seed=seed)
 
     def close(self) -> None:
-        """Flush an active profiler trace and the metrics stream."""
+        """Read back a decode step still in flight (its tokens are appended), then flush an active
+        profiler trace and the metrics stream."""
+        if self._inflight is not None:
+            self._drain()
         self.profiler.close()
         self.metrics.close()
 

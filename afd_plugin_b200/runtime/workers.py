@@ -165,6 +165,10 @@ class AFDAttentionWorker(_WorkerBase):
     def shutdown(self) -> None:
         """Stop the FFN loops (control senders only) and release graphs."""
         self._stop_watchdog()
+        if self.engine.device.type == "cuda":
+            # an async-scheduled decode step may still run: finish it before its graph and the
+            # connector's peer memory go away
+            torch.cuda.synchronize(self.engine.device)
         self.engine.runner.release_graphs()
         stop = getattr(self.executor, "shutdown_remote", None)
         if callable(stop):

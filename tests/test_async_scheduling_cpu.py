@@ -214,3 +214,14 @@ def test_sparse_attention_decision_counts_the_token_in_flight(async_scheduling):
         eng.step()
     assert any(s for s, _ in seen) and not all(s for s, _ in seen)
     assert all(s == (longest > topk) for s, longest in seen)
+
+
+def test_close_reads_back_the_step_in_flight():
+    eng = _engine(True)
+    rid = eng.add_request(PROMPTS[0], 12)
+    for _ in range(4):
+        eng.step()
+    assert eng._inflight is not None
+    n = len(eng.request(rid).output)
+    eng.close()
+    assert eng._inflight is None and len(eng.request(rid).output) == n + 1
